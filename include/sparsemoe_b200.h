@@ -1,0 +1,94 @@
+// C ABI of the B200 capacity-routed MoE layer (libsparsemoe_b200.so).
+//
+// Plain pointers, sizes and a cudaStream_t only.  Each entry point names the
+// reference interface it replaces (paths are within MattJBorowski1991/SparseMoE).
+#pragma once
+
+#include <stddef.h>
+#include <stdint.h>
+#include "moe_args.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+// ---- status codes (moe_solve_v2 and friends) ------------------------------
+#define MOE_OK                 0
+#define MOE_ERR_INVALID_ARG   -1   // null pointer / bad shape
+#define MOE_ERR_UNSUPPORTED   -2   // shape or dtype this build has no kernel for
+#define MOE_ERR_CUDA          -3   // a CUDA runtime/driver call failed
+#define MOE_ERR_TIMEOUT       -4   // a device-side bounded wait gave up
+#define MOE_ERR_NO_KERNEL     -5   // the sm_100a kernels cannot run on this device
+
+// ---- activation / weight formats ------------------------------------------
+#define MOE_DTYPE_F16   0   // fp16 weights/activations (reference kernels/capacity.cu)
+#define MOE_DTYPE_BF16  1   // bf16 bit patterns in the same `half*` fields
+
+// ---- router formats --------------------------------------------------------
+#define MOE_ROUTER_SAME 0   // router_weights have the activation dtype
+#define MOE_ROUTER_F32  1   // router_weights point to f32 [d, E]
+
+// Runtime shape of one layer call.  The reference fixes these at compile time
+// (include/config.h:6-38); here they travel with the call.
+typedef struct MoeDims {
+    int   num_batches;      // B: independent routing groups (blockIdx.z in the reference)
+    int   tokens;           // N: tokens per batch
+    int   d_model;          // d  (multiple of 256)
+    int   d_ff;             // f  (multiple of 128)
+    int   num_experts;      // E  (multiple of 8, <= 256)
+    int   top_k;            // k  (1..32, <= E)
+    float capacity_factor;  // cf
+    int   cap;              // >0: use this CAP;  0: CAP = moe_capacity(N,k,E,cf);  -1: no drop (CAP = N)
+    int   dtype;            // MOE_DTYPE_*
+    int   router_dtype;     // MOE_ROUTER_*
+    const float* router_bias;  // optional device [E] f32 added to every logit (Zipf popularity bias)
+    void* output_16;        // optional device [B, N, d] copy of the output in the 16-bit dtype
+} MoeDims;
+
+// Reference: kernels/launcher.h:21 `extern "C" void solve(MoEArgs args)`.
+// Runs the whole layer for the dims set by moe_set_solve_dims (defaults: the
+// reference's include/config.h), synchronises the device, prints
+// "Total duration via cudaEventRecord: %.3f ms" and exits(1) on any error,
+// exactly as the reference launcher does.  The format path is chosen from the
+// non-null weight fields (fp16 weights -> the `capacity` semantics).
+void solve(struct MoEArgs args);
+
+// Status-returning, stream-ordered form of solve() with runtime dims.
+// Asynchronous: returns once the layer is enqueued on `stream`.
+int moe_solve_v2(const struct MoEArgs* args, const MoeDims* dims, cudaStream_t stream);
+
+// Synchronises `stream` and reports a device-side failure (MOE_ERR_TIMEOUT) of
+// the last moe_solve_v2 on this device, MOE_OK otherwise.
+int moe_check_device_status(cudaStream_t stream);
+
+// Dims used by solve() and by the input builder (inputs/data.h functions).
+int moe_set_solve_dims(const MoeDims* dims);
+int moe_get_solve_dims(MoeDims* dims);
+
+// Reference: inputs/data.cu:392-398 and kernels/capacity.cu:502-503:
+// CAP = round_up((int)ceilf((float)N*(float)k/(float)E*cf), 16).
+int moe_capacity(int tokens, int top_k, int num_experts, float capacity_factor);
+
+// Bytes of device scratch the library keeps for a call with these dims
+// (routing tables; the caller's MoEArgs buffers hold everything else).
+size_t moe_workspace_bytes(const MoeDims* dims);
+
+// Frees the library's cached device scratch on the current device.
+void moe_release(void);
+
+// Text of the last error recorded on this host thread ("" if none).
+const char* moe_last_error(void);
+
+// ---- seeded input generator (the reference has none: inputs/data.cu:164-177
+//      zero-fills everything).  Counter-based, thread-count independent:
+//      value i of (seed, stream) depends only on (seed, stream, i). ----------
+// Normal(0, std) values written as fp16 (bf16 != 0: bf16) bit patterns.
+void moe_fill_normal_16(uint16_t* dst, size_t n, uint64_t seed, uint64_t stream, float std, int bf16);
+void moe_fill_normal_f32(float* dst, size_t n, uint64_t seed, uint64_t stream, float std);
+// Zipf(s) expert-popularity bias: bias[e] = -scale * s * ln(1 + rank(e)),
+// rank a seeded permutation of 0..E-1 (seed 0 = identity).
+void moe_zipf_bias(float* dst, int num_experts, float s, float scale, uint64_t seed);
+
+#ifdef __cplusplus
+}
+#endif

@@ -1,0 +1,281 @@
+// CPU oracle for the capacity-routed MoE layer.  TEST INFRASTRUCTURE ONLY:
+// used by tests/, __graft_entry__.smoke() and bench.py's cpu_baseline /
+// `--impl reference` arm as the checker and the timed CPU baseline.  The
+// product library never links or calls it.
+//
+// It restates, serially, the five stages of the reference fp16 kernel
+// (MattJBorowski1991/SparseMoE kernels/capacity.cu) with each stage finishing
+// before the next and routes processed in route-id order -- the semantics the
+// reference's fused kernel intends but does not guarantee (its stages are
+// separated only by block-local __syncthreads, and slot order follows
+// atomicAdd arrival order):
+//   router logits      capacity.cu:13-142 (wmma_db<false>), call :484
+//   top-k + softmax    capacity.cu:171-238
+//   slots / drop / clamp  capacity.cu:245-309, CAP from inputs/data.cu:392-398
+//   gather             capacity.cu:312-377
+//   up/gate, SwiGLU    capacity.cu:144-168, :505-508 (h rounded to 16-bit)
+//   down               capacity.cu:511
+//   combine            capacity.cu:380-423 (no renormalisation after drops)
+// The router's fp32 reduction order is fixed (the reference's WMMA order is
+// unspecified): logit[t,e] = fmaf-chain over j = 0..d-1 starting at 0.0f,
+// then + bias[e].  The GPU router uses the same order, so logits, expert
+// indices, slots and drops compare bit-exactly.
+//
+// Parity pinning: the reference has no tests, golden vectors or CPU code; its
+// only workload is all-zero data, whose known answer (experts 0..k-1, weights
+// 1/k, counts min(N,CAP) for e<k, zero output) is checked in tests/.
+#include <immintrin.h>
+#include <atomic>
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <thread>
+#include <vector>
+#include <algorithm>
+
+namespace {
+
+inline float bf16_to_f32(uint16_t v) {
+    uint32_t u = (uint32_t)v << 16;
+    float f;
+    std::memcpy(&f, &u, 4);
+    return f;
+}
+inline uint16_t f32_to_bf16_rn(float f) {
+    uint32_t u;
+    std::memcpy(&u, &f, 4);
+    if ((u & 0x7fffffffu) > 0x7f800000u) return (uint16_t)((u >> 16) | 0x40);  // quiet NaN
+    u += 0x7fffu + ((u >> 16) & 1u);
+    return (uint16_t)(u >> 16);
+}
+inline float f16_to_f32(uint16_t v) { return _cvtsh_ss(v); }
+inline uint16_t f32_to_f16_rn(float f) { return _cvtss_sh(f, _MM_FROUND_TO_NEAREST_INT); }
+
+inline float to_f32(uint16_t v, int bf16) { return bf16 ? bf16_to_f32(v) : f16_to_f32(v); }
+inline float round16(float f, int bf16) {
+    return bf16 ? bf16_to_f32(f32_to_bf16_rn(f)) : f16_to_f32(f32_to_f16_rn(f));
+}
+
+// Converts n 16-bit values to f32 (n multiple of 8).
+inline void cvt_row(const uint16_t* src, float* dst, int n, int bf16) {
+    if (bf16) {
+        for (int i = 0; i < n; i += 8) {
+            __m128i h = _mm_loadu_si128((const __m128i*)(src + i));
+            __m256i w = _mm256_slli_epi32(_mm256_cvtepu16_epi32(h), 16);
+            _mm256_storeu_ps(dst + i, _mm256_castsi256_ps(w));
+        }
+    } else {
+        for (int i = 0; i < n; i += 8) {
+            __m128i h = _mm_loadu_si128((const __m128i*)(src + i));
+            _mm256_storeu_ps(dst + i, _mm256_cvtph_ps(h));
+        }
+    }
+}
+
+template <class F>
+void parallel_for(int64_t n, int nthreads, F&& fn) {
+    if (nthreads <= 1 || n <= 1) {
+        for (int64_t i = 0; i < n; ++i) fn(i);
+        return;
+    }
+    std::atomic<int64_t> next{0};
+    std::vector<std::thread> pool;
+    int nt = (int)std::min<int64_t>(nthreads, n);
+    for (int t = 0; t < nt; ++t)
+        pool.emplace_back([&]() {
+            for (;;) {
+                int64_t i = next.fetch_add(1);
+                if (i >= n) break;
+                fn(i);
+            }
+        });
+    for (auto& th : pool) th.join();
+}
+
+}  // namespace
+
+extern "C" {
+
+// inputs/data.cu:392-398 (same float expression, rounded up to 16).
+int oracle_capacity(int tokens, int top_k, int num_experts, float cf) {
+    volatile float a = (float)tokens * (float)top_k;
+    volatile float b = a / (float)num_experts;
+    volatile float c = b * cf;
+    int raw = (int)ceilf(c);
+    return ((raw + 15) / 16) * 16;
+}
+
+// Stages 1-3: router logits, top-k + gated softmax, capacity slots.
+//   x        [B*N, d] 16-bit          wr  [d, E] 16-bit (router_f32: f32)
+//   bias     [E] f32 or null
+//   logits   [B*N, E]   idx/w [B*N, k]   counts [B, E]
+//   token_ids / token_weights [B, E, cap]   route_slot [B*N*k] (-1 = dropped/none)
+void oracle_route(const uint16_t* x, const void* wr, int router_f32, const float* bias,
+                  int B, int N, int d, int E, int k, int cap, int bf16,
+                  float* logits, int* idx, float* w, int* counts, int* token_ids,
+                  float* token_weights, int* route_slot, int nthreads) {
+    const int64_t T = (int64_t)B * N;
+    std::vector<float> wrf((size_t)d * E);
+    if (router_f32) {
+        std::memcpy(wrf.data(), wr, sizeof(float) * (size_t)d * E);
+    } else {
+        const uint16_t* w16 = (const uint16_t*)wr;
+        for (size_t i = 0; i < (size_t)d * E; ++i) wrf[i] = to_f32(w16[i], bf16);
+    }
+    // capacity.cu:13-142 (router GEMM), fixed sequential fmaf order.
+    parallel_for((T + 63) / 64, nthreads, [&](int64_t blk) {
+        std::vector<float> xr(d), acc(E);
+        for (int64_t t = blk * 64; t < std::min<int64_t>(T, blk * 64 + 64); ++t) {
+            for (int j = 0; j < d; ++j) xr[j] = to_f32(x[t * d + j], bf16);
+            for (int e = 0; e < E; ++e) acc[e] = 0.0f;
+            for (int j = 0; j < d; ++j) {
+                const float xj = xr[j];
+                const float* wrow = &wrf[(size_t)j * E];
+                for (int e = 0; e < E; ++e) acc[e] = fmaf(xj, wrow[e], acc[e]);
+            }
+            for (int e = 0; e < E; ++e) logits[t * E + e] = bias ? acc[e] + bias[e] : acc[e];
+        }
+    });
+    // capacity.cu:171-238: insertion top-k with strict '>' (ties keep the lower
+    // index), sentinel (-1e20, -1), softmax over the k kept values.
+    parallel_for(T, nthreads, [&](int64_t t) {
+        float vals[32];
+        int ids[32];
+        for (int i = 0; i < k; ++i) { vals[i] = -1e20f; ids[i] = -1; }
+        for (int e = 0; e < E; ++e) {
+            float v = logits[t * E + e];
+            if (v > vals[k - 1]) {
+                vals[k - 1] = v;
+                ids[k - 1] = e;
+                for (int i = k - 1; i > 0 && vals[i] > vals[i - 1]; --i) {
+                    std::swap(vals[i], vals[i - 1]);
+                    std::swap(ids[i], ids[i - 1]);
+                }
+            }
+        }
+        float mx = vals[0], sum = 0.0f;
+        for (int l = 0; l < k; ++l) sum += expf(vals[l] - mx);
+        for (int l = 0; l < k; ++l) {
+            idx[t * k + l] = ids[l];
+            w[t * k + l] = expf(vals[l] - mx) / (sum + 1e-10f);
+        }
+    });
+    // capacity.cu:245-309 serialised in route-id order: slot = number of
+    // earlier routes of this batch to the same expert; kept iff slot < cap.
+    std::vector<int> cnt(E);
+    for (int b = 0; b < B; ++b) {
+        std::fill(cnt.begin(), cnt.end(), 0);
+        for (int64_t r = 0; r < (int64_t)N * k; ++r) {
+            const int64_t gr = (int64_t)b * N * k + r;
+            const int e = idx[gr];
+            route_slot[gr] = -1;
+            if (e < 0 || e >= E) continue;
+            const int slot = cnt[e]++;
+            if (slot < cap) {
+                const size_t o = ((size_t)b * E + e) * cap + slot;
+                token_ids[o] = (int)(r / k);
+                token_weights[o] = w[gr];
+                route_slot[gr] = slot;
+            }
+        }
+        for (int e = 0; e < E; ++e) counts[b * E + e] = std::min(cnt[e], cap);
+    }
+}
+
+// Stages 4-5 for the tokens [t_begin, t_end) of the flattened [B*N] range:
+// gather, up/gate GEMMs, SwiGLU (h rounded to the 16-bit type, capacity.cu:166),
+// down GEMM, then combine (capacity.cu:380-423) summing kept routes in
+// l = 0..k-1 order:  out = ((0 + w0*y0) + w1*y1) + ...
+// `out` is [B*N, d]; only rows t_begin..t_end-1 are written.
+void oracle_ffn_combine(const uint16_t* x, const uint16_t* wg, const uint16_t* wu,
+                        const uint16_t* wd, int B, int N, int d, int f, int E, int k,
+                        int bf16, const int* idx, const float* w, const int* route_slot,
+                        int64_t t_begin, int64_t t_end, float* out, int nthreads) {
+    (void)B; (void)N;
+    // Group the kept routes of the token range by expert.
+    std::vector<std::vector<int64_t>> routes(E);
+    for (int64_t t = t_begin; t < t_end; ++t)
+        for (int l = 0; l < k; ++l) {
+            const int64_t r = t * k + l;
+            if (route_slot[r] >= 0) routes[idx[r]].push_back(r);
+        }
+    std::vector<float> y;  // [t_end-t_begin, k, d] per-route outputs
+    y.assign((size_t)(t_end - t_begin) * k * d, 0.0f);
+    constexpr int RB = 32, CT = 512;
+    struct Item { int e; int r0; };
+    std::vector<Item> items;
+    for (int e = 0; e < E; ++e)
+        for (int r0 = 0; r0 < (int)routes[e].size(); r0 += RB) items.push_back({e, r0});
+    parallel_for((int64_t)items.size(), nthreads, [&](int64_t it) {
+        const int e = items[it].e, r0 = items[it].r0;
+        const int nr = std::min<int>(RB, (int)routes[e].size() - r0);
+        std::vector<float> a((size_t)RB * d), hbuf((size_t)RB * f);
+        std::vector<float> accg((size_t)RB * CT), accu((size_t)RB * CT), wrow_g(CT), wrow_u(CT);
+        for (int r = 0; r < nr; ++r) {
+            const int64_t tok = routes[e][r0 + r] / k;
+            cvt_row(x + tok * d, &a[(size_t)r * d], d, bf16);
+        }
+        const uint16_t* Wg = wg + (size_t)e * d * f;
+        const uint16_t* Wu = wu + (size_t)e * d * f;
+        const uint16_t* Wd = wd + (size_t)e * f * d;
+        for (int c0 = 0; c0 < f; c0 += CT) {
+            const int nc = std::min(CT, f - c0);
+            std::fill(accg.begin(), accg.end(), 0.0f);
+            std::fill(accu.begin(), accu.end(), 0.0f);
+            for (int j = 0; j < d; ++j) {
+                cvt_row(Wg + (size_t)j * f + c0, wrow_g.data(), nc, bf16);
+                cvt_row(Wu + (size_t)j * f + c0, wrow_u.data(), nc, bf16);
+                for (int r = 0; r < nr; ++r) {
+                    const float av = a[(size_t)r * d + j];
+                    float* pg = &accg[(size_t)r * CT];
+                    float* pu = &accu[(size_t)r * CT];
+                    for (int c = 0; c < nc; ++c) {
+                        pg[c] += av * wrow_g[c];
+                        pu[c] += av * wrow_u[c];
+                    }
+                }
+            }
+            for (int r = 0; r < nr; ++r)
+                for (int c = 0; c < nc; ++c) {
+                    const float g = accg[(size_t)r * CT + c], u = accu[(size_t)r * CT + c];
+                    const float silu = g / (1.0f + expf(-g));
+                    hbuf[(size_t)r * f + c0 + c] = round16(u * silu, bf16);
+                }
+        }
+        std::vector<float> accy((size_t)RB * CT), wrow_d(CT);
+        for (int c0 = 0; c0 < d; c0 += CT) {
+            const int nc = std::min(CT, d - c0);
+            std::fill(accy.begin(), accy.end(), 0.0f);
+            for (int j = 0; j < f; ++j) {
+                cvt_row(Wd + (size_t)j * d + c0, wrow_d.data(), nc, bf16);
+                for (int r = 0; r < nr; ++r) {
+                    const float hv = hbuf[(size_t)r * f + j];
+                    float* py = &accy[(size_t)r * CT];
+                    for (int c = 0; c < nc; ++c) py[c] += hv * wrow_d[c];
+                }
+            }
+            for (int r = 0; r < nr; ++r) {
+                const int64_t route = routes[e][r0 + r];
+                float* dst = &y[((size_t)(route - t_begin * k)) * d + c0];
+                std::memcpy(dst, &accy[(size_t)r * CT], sizeof(float) * nc);
+            }
+        }
+    });
+    parallel_for(t_end - t_begin, nthreads, [&](int64_t i) {
+        const int64_t t = t_begin + i;
+        float* o = out + t * d;
+        for (int c = 0; c < d; ++c) o[c] = 0.0f;
+        for (int l = 0; l < k; ++l) {
+            const int64_t r = t * k + l;
+            if (route_slot[r] < 0) continue;
+            const float wl = w[r];
+            const float* yr = &y[((size_t)(r - t_begin * k)) * d];
+            for (int c = 0; c < d; ++c) {
+                volatile float p = wl * yr[c];
+                o[c] = o[c] + p;
+            }
+        }
+    });
+}
+
+}  // extern "C"

@@ -1,0 +1,103 @@
+"""ctypes binding of the CPU oracle (oracle/moe_oracle.cpp).
+
+TEST INFRASTRUCTURE ONLY: imported by tests/, __graft_entry__.smoke() and
+bench.py's CPU-baseline arm as the checker; the product never calls it.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+import time
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+LIB = HERE / "_build" / "libmoe_oracle.so"
+
+
+def build() -> Path:
+    src = HERE / "moe_oracle.cpp"
+    if not LIB.exists() or LIB.stat().st_mtime < src.stat().st_mtime:
+        subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
+    return LIB
+
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        if not LIB.exists():
+            build()
+        L = ctypes.CDLL(str(LIB))
+        P = ctypes.c_void_p
+        I = ctypes.c_int
+        L.oracle_capacity.restype = I
+        L.oracle_capacity.argtypes = [I, I, I, ctypes.c_float]
+        L.oracle_route.restype = None
+        L.oracle_route.argtypes = [P, P, I, P, I, I, I, I, I, I, I, P, P, P, P, P, P, P, I]
+        L.oracle_ffn_combine.restype = None
+        L.oracle_ffn_combine.argtypes = [P, P, P, P, I, I, I, I, I, I, I, P, P, P, ctypes.c_int64,
+                                         ctypes.c_int64, P, I]
+        _lib = L
+    return _lib
+
+
+def _ptr(a):
+    return None if a is None else a.ctypes.data
+
+
+def threads() -> int:
+    return int(os.environ.get("ORACLE_THREADS", os.cpu_count() or 1))
+
+
+def capacity(tokens: int, top_k: int, num_experts: int, cf: float) -> int:
+    return lib().oracle_capacity(tokens, top_k, num_experts, ctypes.c_float(cf))
+
+
+def route(x, wr, bias, B, N, d, E, k, cap, bf16, router_f32=False, nthreads=None):
+    """Stages 1-3.  Returns dict(logits, idx, w, counts, token_ids, token_weights, route_slot)."""
+    T = B * N
+    x = np.ascontiguousarray(x, dtype=np.uint16)
+    wr = np.ascontiguousarray(wr, dtype=np.float32 if router_f32 else np.uint16)
+    out = {
+        "logits": np.empty((T, E), np.float32), "idx": np.empty((T, k), np.int32),
+        "w": np.empty((T, k), np.float32), "counts": np.empty((B, E), np.int32),
+        "token_ids": np.full((B, E, max(cap, 0)), -1, np.int32),
+        "token_weights": np.zeros((B, E, max(cap, 0)), np.float32),
+        "route_slot": np.empty((T * k,), np.int32),
+    }
+    b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
+    lib().oracle_route(_ptr(x), _ptr(wr), int(router_f32), _ptr(b), B, N, d, E, k, cap, int(bf16),
+                       _ptr(out["logits"]), _ptr(out["idx"]), _ptr(out["w"]), _ptr(out["counts"]),
+                       _ptr(out["token_ids"]), _ptr(out["token_weights"]), _ptr(out["route_slot"]),
+                       nthreads or threads())
+    return out
+
+
+def ffn_combine(x, wg, wu, wd, B, N, d, f, E, k, bf16, idx, w, route_slot, t_begin=0, t_end=None,
+                nthreads=None):
+    """Stages 4-5 for tokens [t_begin, t_end); returns the [t_end - t_begin, d] f32 output rows."""
+    T = B * N
+    t_end = T if t_end is None else t_end
+    out = np.zeros((T, d), np.float32) if t_end - t_begin == T else np.zeros((T, d), np.float32)
+    args = [np.ascontiguousarray(a, dtype=np.uint16) for a in (x, wg, wu, wd)]
+    lib().oracle_ffn_combine(*(_ptr(a) for a in args), B, N, d, f, E, k, int(bf16),
+                             _ptr(np.ascontiguousarray(idx, np.int32)), _ptr(np.ascontiguousarray(w, np.float32)),
+                             _ptr(np.ascontiguousarray(route_slot, np.int32)), t_begin, t_end, _ptr(out),
+                             nthreads or threads())
+    return out[t_begin:t_end]
+
+
+def forward(inputs: dict, cfg, t_begin=0, t_end=None, nthreads=None):
+    """Whole layer on the CPU for a sparsemoe_b200.LayerConfig and make_inputs() dict."""
+    cap = cfg.capacity()
+    r = route(inputs["x"], inputs["wr"], inputs.get("bias"), cfg.num_batches, cfg.tokens, cfg.d_model,
+              cfg.num_experts, cfg.top_k, cap, cfg.bf16, cfg.router_f32, nthreads)
+    r["out"] = ffn_combine(inputs["x"], inputs["wg"], inputs["wu"], inputs["wd"], cfg.num_batches, cfg.tokens,
+                           cfg.d_model, cfg.d_ff, cfg.num_experts, cfg.top_k, cfg.bf16, r["idx"], r["w"],
+                           r["route_slot"], t_begin, t_end, nthreads)
+    return r

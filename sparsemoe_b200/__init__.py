@@ -1,0 +1,205 @@
+"""Host-side mirror of the B200 MoE layer's C ABI (include/sparsemoe_b200.h).
+
+The product is libsparsemoe_b200.so: hand-written sm_100a CUDA behind the
+reference's C++ host API (`MoEArgs`, `solve()`, the input builder of
+MattJBorowski1991/SparseMoE).  This module binds that library with ctypes and
+uses PyTorch only for device memory and streams.  There is no CPU fallback:
+importing the module fails if the library is missing.
+"""
+from __future__ import annotations
+
+import ctypes
+import dataclasses
+import os
+from pathlib import Path
+
+import numpy as np
+
+_PKG = Path(__file__).resolve().parent
+LIB_PATH = _PKG / "libsparsemoe_b200.so"
+
+MOE_OK = 0
+MOE_ERR_INVALID_ARG = -1
+MOE_ERR_UNSUPPORTED = -2
+MOE_ERR_CUDA = -3
+MOE_ERR_TIMEOUT = -4
+MOE_ERR_NO_KERNEL = -5
+
+DTYPE_F16 = 0
+DTYPE_BF16 = 1
+ROUTER_SAME = 0
+ROUTER_F32 = 1
+
+
+class MoeError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"moe error {code}: {msg}")
+        self.code = code
+
+
+_p = ctypes.c_void_p
+
+
+class MoEArgs(ctypes.Structure):
+    """ctypes image of `struct MoEArgs` (include/moe_args.h; reference include/moe_args.h:8-55)."""
+
+    _fields_ = [
+        ("input", _p), ("router_weights", _p),
+        ("expert_up_proj_weights", _p), ("expert_gate_proj_weights", _p), ("expert_down_proj_weights", _p),
+        ("expert_up_proj_weights_int8", _p), ("expert_gate_proj_weights_int8", _p),
+        ("expert_down_proj_weights_int8", _p),
+        ("expert_up_proj_weights_int4", _p), ("expert_gate_proj_weights_int4", _p),
+        ("expert_down_proj_weights_int4", _p),
+        ("expert_up_proj_weights_fp8", _p), ("expert_gate_proj_weights_fp8", _p),
+        ("expert_down_proj_weights_fp8", _p),
+        ("scale_up_w", ctypes.c_float), ("scale_gate_w", ctypes.c_float), ("scale_down_w", ctypes.c_float),
+        ("scale_input_act", ctypes.c_float), ("scale_mid_act", ctypes.c_float),
+        ("expert_logits", _p), ("selected_expert_indices", _p), ("selected_expert_weights", _p),
+        ("expert_counts", _p), ("expert_token_ids", _p), ("expert_token_weights", _p),
+        ("per_expert_wmma_inputs", _p), ("per_expert_wmma_inputs_int8", _p),
+        ("per_expert_wmma_inputs_int4", _p), ("per_expert_wmma_inputs_fp8", _p),
+        ("hidden_mlp_layer_1_out", _p), ("hidden_mlp_gate_out", _p), ("hidden_mlp_layer_1_out_fp16", _p),
+        ("hidden_mlp_layer_1_out_int8", _p), ("hidden_mlp_layer_1_out_int4", _p),
+        ("hidden_mlp_layer_1_out_fp8", _p), ("hidden_mlp_layer_2_out", _p),
+        ("final_output", _p),
+        ("num_batches", ctypes.c_int), ("use_capacity", ctypes.c_bool), ("cap", ctypes.c_int),
+    ]
+
+
+class MoeDims(ctypes.Structure):
+    """ctypes image of `MoeDims` (include/sparsemoe_b200.h)."""
+
+    _fields_ = [
+        ("num_batches", ctypes.c_int), ("tokens", ctypes.c_int), ("d_model", ctypes.c_int),
+        ("d_ff", ctypes.c_int), ("num_experts", ctypes.c_int), ("top_k", ctypes.c_int),
+        ("capacity_factor", ctypes.c_float), ("cap", ctypes.c_int), ("dtype", ctypes.c_int),
+        ("router_dtype", ctypes.c_int), ("router_bias", _p), ("output_16", _p),
+    ]
+
+
+def _load() -> ctypes.CDLL:
+    if not LIB_PATH.exists():
+        raise ImportError(
+            f"{LIB_PATH} is missing: build it with `python -m sparsemoe_b200.build` "
+            "(there is no CPU fallback)")
+    lib = ctypes.CDLL(str(LIB_PATH), mode=os.RTLD_NOW | os.RTLD_GLOBAL)
+    sig = {
+        "solve": (None, [MoEArgs]),
+        "moe_solve_v2": (ctypes.c_int, [ctypes.POINTER(MoEArgs), ctypes.POINTER(MoeDims), _p]),
+        "moe_check_device_status": (ctypes.c_int, [_p]),
+        "moe_set_solve_dims": (ctypes.c_int, [ctypes.POINTER(MoeDims)]),
+        "moe_get_solve_dims": (ctypes.c_int, [ctypes.POINTER(MoeDims)]),
+        "moe_capacity": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float]),
+        "moe_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(MoeDims)]),
+        "moe_release": (None, []),
+        "moe_last_error": (ctypes.c_char_p, []),
+        "moe_fill_normal_16": (None, [_p, ctypes.c_size_t, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_float,
+                                      ctypes.c_int]),
+        "moe_fill_normal_f32": (None, [_p, ctypes.c_size_t, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_float]),
+        "moe_zipf_bias": (None, [_p, ctypes.c_int, ctypes.c_float, ctypes.c_float, ctypes.c_uint64]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    return lib
+
+
+lib = _load()
+
+
+def last_error() -> str:
+    return lib.moe_last_error().decode()
+
+
+def check(rc: int) -> None:
+    if rc != MOE_OK:
+        raise MoeError(rc, last_error())
+
+
+def capacity(tokens: int, top_k: int, num_experts: int, cf: float) -> int:
+    """CAP = round_up(ceilf(N*k/E*cf), 16) (reference inputs/data.cu:392-398)."""
+    return lib.moe_capacity(tokens, top_k, num_experts, ctypes.c_float(cf))
+
+
+# ---- seeded generator -------------------------------------------------------
+def normal16(n: int, seed: int, stream: int, std: float, bf16: bool) -> np.ndarray:
+    out = np.empty(n, dtype=np.uint16)
+    lib.moe_fill_normal_16(out.ctypes.data, n, seed, stream, ctypes.c_float(std), int(bf16))
+    return out
+
+
+def normal_f32(n: int, seed: int, stream: int, std: float) -> np.ndarray:
+    out = np.empty(n, dtype=np.float32)
+    lib.moe_fill_normal_f32(out.ctypes.data, n, seed, stream, ctypes.c_float(std))
+    return out
+
+
+def zipf_bias(num_experts: int, s: float, scale: float = 1.0, seed: int = 0) -> np.ndarray:
+    out = np.empty(num_experts, dtype=np.float32)
+    lib.moe_zipf_bias(out.ctypes.data, num_experts, ctypes.c_float(s), ctypes.c_float(scale), seed)
+    return out
+
+
+@dataclasses.dataclass(frozen=True)
+class LayerConfig:
+    """One layer shape.  `tokens` is per batch (routing and CAP are per batch)."""
+
+    num_batches: int
+    tokens: int
+    d_model: int
+    d_ff: int
+    num_experts: int
+    top_k: int
+    capacity_factor: float
+    dtype: int = DTYPE_F16
+    router_f32: bool = False
+    zipf_s: float = 0.0          # > 0: add a Zipf(s) popularity bias to the logits
+    cap: int = 0                 # 0: computed; > 0: override; -1: no drop
+
+    @property
+    def T(self) -> int:
+        return self.num_batches * self.tokens
+
+    @property
+    def bf16(self) -> bool:
+        return self.dtype == DTYPE_BF16
+
+    def capacity(self) -> int:
+        if self.cap > 0:
+            return self.cap
+        if self.cap < 0:
+            return self.tokens
+        return capacity(self.tokens, self.top_k, self.num_experts, self.capacity_factor)
+
+    def dims(self, router_bias_ptr: int | None = None, out16_ptr: int | None = None) -> MoeDims:
+        return MoeDims(self.num_batches, self.tokens, self.d_model, self.d_ff, self.num_experts, self.top_k,
+                       self.capacity_factor, self.cap, self.dtype, ROUTER_F32 if self.router_f32 else ROUTER_SAME,
+                       router_bias_ptr, out16_ptr)
+
+
+def make_inputs(cfg: LayerConfig, seed: int = 0) -> dict:
+    """Seeded host inputs (streams: x 0, router 1, gate 2, up 3, down 4).
+
+    x ~ N(0,1); router ~ N(0,0.02); gate/up ~ N(0,1/sqrt(d)); down ~ N(0,1/sqrt(f)).
+    16-bit tensors are returned as uint16 bit patterns.
+    """
+    d, f, E = cfg.d_model, cfg.d_ff, cfg.num_experts
+    out = {
+        "x": normal16(cfg.T * d, seed, 0, 1.0, cfg.bf16).reshape(cfg.T, d),
+        "wg": normal16(E * d * f, seed, 2, 1.0 / np.sqrt(d), cfg.bf16).reshape(E, d, f),
+        "wu": normal16(E * d * f, seed, 3, 1.0 / np.sqrt(d), cfg.bf16).reshape(E, d, f),
+        "wd": normal16(E * f * d, seed, 4, 1.0 / np.sqrt(f), cfg.bf16).reshape(E, f, d),
+    }
+    if cfg.router_f32:
+        out["wr"] = normal_f32(d * E, seed, 1, 0.02).reshape(d, E)
+    else:
+        out["wr"] = normal16(d * E, seed, 1, 0.02, cfg.bf16).reshape(d, E)
+    out["bias"] = zipf_bias(E, cfg.zipf_s) if cfg.zipf_s > 0 else None
+    return out
+
+
+from .layer import MoeLayer  # noqa: E402  (needs `lib` above)
+
+__all__ = ["MoEArgs", "MoeDims", "LayerConfig", "MoeLayer", "make_inputs", "capacity", "lib", "check",
+           "MoeError", "normal16", "normal_f32", "zipf_bias", "DTYPE_F16", "DTYPE_BF16"]

@@ -1,0 +1,265 @@
+// Host input builder: the reference's inputs/data.h API (inputs/data.cu:13-640
+// of MattJBorowski1991/SparseMoE), rewritten, with shapes taken from the
+// runtime solve() dims instead of config.h constants, plus a seeded variant.
+//
+// Buffer sizes follow the reference (inputs/data.cu:400-521): every
+// intermediate is [B, E, CAP, .]-sized, CAP = moe_capacity(...) when
+// use_capacity else N; only the buffers of the chosen weight format are
+// allocated; unused pointers stay null (memset 0, inputs/data.cu:211).
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <vector>
+#include <cuda_fp8.h>
+
+#include "../../include/data.h"
+#include "../../include/sparsemoe_b200.h"
+
+namespace {
+
+#define BUILDER_CHECK(call)                                                                   \
+    do {                                                                                      \
+        cudaError_t err_ = (call);                                                            \
+        if (err_ != cudaSuccess) {                                                            \
+            fprintf(stderr, "CUDA Error at: %s: %d: %s \n", __FILE__, __LINE__,              \
+                    cudaGetErrorString(err_));                                                \
+            exit(1);                                                                          \
+        }                                                                                     \
+    } while (0)
+
+struct BuilderState {
+    bool seeded = false;
+    uint64_t seed = 0;
+};
+BuilderState g_builder;
+
+float h2f(half v) { return __half2float(v); }
+
+float max_abs(const std::vector<half>& v) {
+    float m = 0.0f;
+    for (const half& x : v) m = std::fmax(m, std::fabs(h2f(x)));
+    return m;
+}
+
+// inputs/data.cu:13-34 / 36-57: per-tensor symmetric, scale = max|x| / qmax,
+// q = nearbyint(clamp(x / scale, -qmax, qmax)).
+float quant_symmetric(const std::vector<half>& src, std::vector<int8_t>& dst, float qmax) {
+    const float m = max_abs(src);
+    const float scale = m > 0.0f ? m / qmax : 1.0f;
+    dst.resize(src.size());
+    for (size_t i = 0; i < src.size(); ++i) {
+        const float c = std::fmin(qmax, std::fmax(-qmax, h2f(src[i]) / scale));
+        dst[i] = (int8_t)(int)nearbyintf(c);
+    }
+    return scale;
+}
+
+// inputs/data.cu:59-87: int4 values, two per byte, even index in the low nibble.
+void pack_int4(const std::vector<int8_t>& q, std::vector<uint8_t>& out) {
+    out.assign((q.size() + 1) / 2, 0);
+    for (size_t i = 0; i < q.size(); ++i) {
+        const uint8_t nib = (uint8_t)(q[i] & 0xF);
+        out[i >> 1] |= (i & 1) ? (uint8_t)(nib << 4) : nib;
+    }
+}
+
+// inputs/data.cu:89-140: per expert, [K, Ncols] -> bytes [Ncols/2][K]; byte
+// (n/2, kk) holds columns n (low nibble, even) and n+1 (high nibble).
+void pack_int4_transposed(const std::vector<int8_t>& q, std::vector<uint8_t>& out, int experts, int K,
+                          int Ncols) {
+    const size_t per = (size_t)K * Ncols;
+    const size_t bytes_per = (size_t)(Ncols / 2) * K;
+    out.assign((size_t)experts * bytes_per, 0);
+    for (int e = 0; e < experts; ++e)
+        for (int kk = 0; kk < K; ++kk)
+            for (int n = 0; n < Ncols; ++n) {
+                const uint8_t nib = (uint8_t)(q[(size_t)e * per + (size_t)kk * Ncols + n] & 0xF);
+                uint8_t& b = out[(size_t)e * bytes_per + (size_t)(n / 2) * K + kk];
+                b |= (n & 1) ? (uint8_t)(nib << 4) : nib;
+            }
+}
+
+template <class T>
+T* upload(const T* host, size_t count) {
+    T* d = nullptr;
+    BUILDER_CHECK(cudaMalloc(&d, count * sizeof(T)));
+    BUILDER_CHECK(cudaMemcpy(d, host, count * sizeof(T), cudaMemcpyHostToDevice));
+    return d;
+}
+template <class T>
+T* alloc(size_t count) {
+    T* d = nullptr;
+    BUILDER_CHECK(cudaMalloc(&d, count * sizeof(T)));
+    return d;
+}
+
+enum class Fmt { F16, INT8, INT4, INT4_PTX, FP8 };
+
+MoEArgs build(const std::vector<half>& x, const std::vector<half>& wu, const std::vector<half>& wg,
+              const std::vector<half>& wd, bool use_capacity, Fmt fmt) {
+    MoeDims dims;
+    moe_get_solve_dims(&dims);
+    const int B = dims.num_batches, Nt = dims.tokens, d = dims.d_model, f = dims.d_ff, E = dims.num_experts,
+              kk = dims.top_k;
+    MoEArgs a;
+    std::memset(&a, 0, sizeof(a));
+    a.num_batches = B;
+    a.use_capacity = use_capacity;
+    a.input = upload(x.data(), (size_t)B * Nt * d);
+    // Router weights: zero (reference inputs/data.cu:237-243) or seeded N(0, 0.02).
+    {
+        const size_t n = (size_t)d * E;
+        half* r = alloc<half>(n);
+        if (g_builder.seeded) {
+            std::vector<uint16_t> h(n);
+            moe_fill_normal_16(h.data(), n, g_builder.seed, 1, 0.02f, 0);
+            BUILDER_CHECK(cudaMemcpy(r, h.data(), n * 2, cudaMemcpyHostToDevice));
+        } else {
+            BUILDER_CHECK(cudaMemset(r, 0, n * 2));
+        }
+        a.router_weights = r;
+    }
+    const size_t nw = (size_t)E * d * f;
+    if (fmt == Fmt::F16) {
+        a.expert_up_proj_weights = upload(wu.data(), nw);
+        a.expert_gate_proj_weights = upload(wg.data(), nw);
+        a.expert_down_proj_weights = upload(wd.data(), nw);
+    } else if (fmt == Fmt::INT8 || fmt == Fmt::INT4 || fmt == Fmt::INT4_PTX) {
+        const float qmax = fmt == Fmt::INT8 ? 127.0f : 7.0f;
+        std::vector<int8_t> qu, qg, qd;
+        a.scale_up_w = quant_symmetric(wu, qu, qmax);
+        a.scale_gate_w = quant_symmetric(wg, qg, qmax);
+        a.scale_down_w = quant_symmetric(wd, qd, qmax);
+        a.scale_input_act = 1.0f;  // placeholder activation scales (inputs/data.cu:320-322)
+        a.scale_mid_act = 1.0f;
+        a.expert_up_proj_weights_int8 = upload(qu.data(), qu.size());
+        a.expert_gate_proj_weights_int8 = upload(qg.data(), qg.size());
+        a.expert_down_proj_weights_int8 = upload(qd.data(), qd.size());
+        if (fmt != Fmt::INT8) {
+            std::vector<uint8_t> pu, pg, pd;
+            if (fmt == Fmt::INT4_PTX) {
+                pack_int4_transposed(qu, pu, E, d, f);
+                pack_int4_transposed(qg, pg, E, d, f);
+                pack_int4_transposed(qd, pd, E, f, d);
+            } else {
+                pack_int4(qu, pu);
+                pack_int4(qg, pg);
+                pack_int4(qd, pd);
+            }
+            a.expert_up_proj_weights_int4 = upload(pu.data(), pu.size());
+            a.expert_gate_proj_weights_int4 = upload(pg.data(), pg.size());
+            a.expert_down_proj_weights_int4 = upload(pd.data(), pd.size());
+        }
+    } else {  // FP8: direct e4m3 cast, unit scales (inputs/data.cu:142-150, 359-390)
+        auto cast = [&](const std::vector<half>& src) {
+            std::vector<__nv_fp8_e4m3> q(src.size());
+            for (size_t i = 0; i < src.size(); ++i) q[i] = __nv_fp8_e4m3(h2f(src[i]));
+            return upload(q.data(), q.size());
+        };
+        a.expert_up_proj_weights_fp8 = cast(wu);
+        a.expert_gate_proj_weights_fp8 = cast(wg);
+        a.expert_down_proj_weights_fp8 = cast(wd);
+        a.scale_up_w = a.scale_gate_w = a.scale_down_w = a.scale_input_act = a.scale_mid_act = 1.0f;
+    }
+    const int cap = use_capacity ? moe_capacity(Nt, kk, E, dims.capacity_factor) : Nt;
+    a.cap = cap;
+    const size_t rows = (size_t)B * E * cap;
+    a.expert_logits = alloc<float>((size_t)B * Nt * E);
+    a.selected_expert_indices = alloc<int>((size_t)B * Nt * kk);
+    a.selected_expert_weights = alloc<float>((size_t)B * Nt * kk);
+    a.expert_counts = alloc<int>((size_t)B * E);
+    a.expert_token_ids = alloc<int>(rows);
+    a.expert_token_weights = alloc<float>(rows);
+    if (fmt == Fmt::F16) a.per_expert_wmma_inputs = alloc<half>(rows * d);
+    if (fmt == Fmt::INT8 || fmt == Fmt::INT4 || fmt == Fmt::INT4_PTX)
+        a.per_expert_wmma_inputs_int8 = alloc<int8_t>(rows * d);
+    if (fmt == Fmt::INT4 || fmt == Fmt::INT4_PTX) a.per_expert_wmma_inputs_int4 = alloc<uint8_t>(rows * d / 2);
+    if (fmt == Fmt::FP8) a.per_expert_wmma_inputs_fp8 = alloc<__nv_fp8_e4m3>(rows * d);
+    a.hidden_mlp_layer_1_out = alloc<float>(rows * f);
+    a.hidden_mlp_gate_out = alloc<float>(rows * f);
+    if (fmt == Fmt::F16) a.hidden_mlp_layer_1_out_fp16 = alloc<half>(rows * f);
+    if (fmt == Fmt::INT8 || fmt == Fmt::INT4 || fmt == Fmt::INT4_PTX)
+        a.hidden_mlp_layer_1_out_int8 = alloc<int8_t>(rows * f);
+    if (fmt == Fmt::INT4 || fmt == Fmt::INT4_PTX) a.hidden_mlp_layer_1_out_int4 = alloc<uint8_t>(rows * f / 2);
+    if (fmt == Fmt::FP8) a.hidden_mlp_layer_1_out_fp8 = alloc<__nv_fp8_e4m3>(rows * f);
+    a.hidden_mlp_layer_2_out = alloc<float>(rows * d);
+    a.final_output = alloc<float>((size_t)B * Nt * d);
+    return a;
+}
+
+}  // namespace
+
+void initialize_host_data(std::vector<half>& h_input, std::vector<float>& h_final_output,
+                          std::vector<half>& h_expert_up_proj_weights,
+                          std::vector<half>& h_expert_gate_proj_weights,
+                          std::vector<half>& h_expert_down_proj_weights) {
+    g_builder.seeded = false;
+    const half z = __float2half(0.0f);
+    std::fill(h_input.begin(), h_input.end(), z);
+    std::fill(h_final_output.begin(), h_final_output.end(), 0.0f);
+    std::fill(h_expert_up_proj_weights.begin(), h_expert_up_proj_weights.end(), z);
+    std::fill(h_expert_gate_proj_weights.begin(), h_expert_gate_proj_weights.end(), z);
+    std::fill(h_expert_down_proj_weights.begin(), h_expert_down_proj_weights.end(), z);
+}
+
+void initialize_host_data_seeded(std::vector<half>& h_input, std::vector<float>& h_final_output,
+                                 std::vector<half>& h_expert_up_proj_weights,
+                                 std::vector<half>& h_expert_gate_proj_weights,
+                                 std::vector<half>& h_expert_down_proj_weights, uint64_t seed) {
+    MoeDims dims;
+    moe_get_solve_dims(&dims);
+    g_builder.seeded = true;
+    g_builder.seed = seed;
+    auto fill = [&](std::vector<half>& v, uint64_t stream, float stdv) {
+        moe_fill_normal_16(reinterpret_cast<uint16_t*>(v.data()), v.size(), seed, stream, stdv, 0);
+    };
+    fill(h_input, 0, 1.0f);
+    fill(h_expert_gate_proj_weights, 2, 1.0f / std::sqrt((float)dims.d_model));
+    fill(h_expert_up_proj_weights, 3, 1.0f / std::sqrt((float)dims.d_model));
+    fill(h_expert_down_proj_weights, 4, 1.0f / std::sqrt((float)dims.d_ff));
+    std::fill(h_final_output.begin(), h_final_output.end(), 0.0f);
+}
+
+MoEArgs allocate_and_copy_to_device(const std::vector<half>& x, const std::vector<half>& wu,
+                                    const std::vector<half>& wg, const std::vector<half>& wd, bool use_capacity) {
+    return build(x, wu, wg, wd, use_capacity, Fmt::F16);
+}
+MoEArgs allocate_and_copy_to_device_int8(const std::vector<half>& x, const std::vector<half>& wu,
+                                         const std::vector<half>& wg, const std::vector<half>& wd,
+                                         bool use_capacity) {
+    return build(x, wu, wg, wd, use_capacity, Fmt::INT8);
+}
+MoEArgs allocate_and_copy_to_device_int4(const std::vector<half>& x, const std::vector<half>& wu,
+                                         const std::vector<half>& wg, const std::vector<half>& wd,
+                                         bool use_capacity) {
+    return build(x, wu, wg, wd, use_capacity, Fmt::INT4);
+}
+MoEArgs allocate_and_copy_to_device_int4_ptx(const std::vector<half>& x, const std::vector<half>& wu,
+                                             const std::vector<half>& wg, const std::vector<half>& wd,
+                                             bool use_capacity) {
+    return build(x, wu, wg, wd, use_capacity, Fmt::INT4_PTX);
+}
+MoEArgs allocate_and_copy_to_device_fp8(const std::vector<half>& x, const std::vector<half>& wu,
+                                        const std::vector<half>& wg, const std::vector<half>& wd,
+                                        bool use_capacity) {
+    return build(x, wu, wg, wd, use_capacity, Fmt::FP8);
+}
+
+void cleanup_device_data(MoEArgs& a) {
+    const void* ptrs[] = {a.input, a.router_weights, a.expert_up_proj_weights, a.expert_gate_proj_weights,
+                          a.expert_down_proj_weights, a.expert_up_proj_weights_int8,
+                          a.expert_gate_proj_weights_int8, a.expert_down_proj_weights_int8,
+                          a.expert_up_proj_weights_int4, a.expert_gate_proj_weights_int4,
+                          a.expert_down_proj_weights_int4, a.expert_up_proj_weights_fp8,
+                          a.expert_gate_proj_weights_fp8, a.expert_down_proj_weights_fp8, a.expert_logits,
+                          a.selected_expert_indices, a.selected_expert_weights, a.expert_counts,
+                          a.expert_token_ids, a.expert_token_weights, a.per_expert_wmma_inputs,
+                          a.per_expert_wmma_inputs_int8, a.per_expert_wmma_inputs_int4,
+                          a.per_expert_wmma_inputs_fp8, a.hidden_mlp_layer_1_out, a.hidden_mlp_gate_out,
+                          a.hidden_mlp_layer_1_out_fp16, a.hidden_mlp_layer_1_out_int8,
+                          a.hidden_mlp_layer_1_out_int4, a.hidden_mlp_layer_1_out_fp8,
+                          a.hidden_mlp_layer_2_out, a.final_output};
+    for (const void* p : ptrs)
+        if (p) BUILDER_CHECK(cudaFree(const_cast<void*>(p)));
+}

@@ -1,0 +1,359 @@
+// Stage 4: the expert SwiGLU FFN as two grouped GEMMs on tcgen05 tensor cores.
+//
+// Reference semantics: kernels/capacity.cu:505-511 -- U = A_e Wup_e and
+// G = A_e Wgate_e in f32, h = U * G / (1 + exp(-G)) rounded to the 16-bit type
+// (capacity.cu:144-168), then Y = h_e Wdown_e in f32.
+//
+// Design (one persistent CTA per SM, warp-specialised, 192 threads):
+//   warp 0      TMA producer: A tile 128 x 64 (K-major, 128B swizzle) and the
+//               B tile 64 x 256 straight from the reference's row-major
+//               [K, N] weights (N-contiguous = MN-major, 128B swizzle), into a
+//               4-stage smem ring guarded by full/empty mbarriers.
+//   warp 1      MMA issuer: one thread issues tcgen05.mma M=128 N=256 K=16
+//               (4 per 64-wide K block) into a double-buffered TMEM
+//               accumulator (2 x 256 f32 columns), commits to the ring's
+//               empty barrier and, per tile, to the accumulator-full barrier.
+//   warps 2-5   epilogue: tcgen05.ld rows out of TMEM, releases the buffer,
+//               then
+//                 up/gate mode: columns [0,128) = gate, [128,256) = up of the
+//                 same 128 output features (the B tile holds Wgate | Wup), so
+//                 SwiGLU is applied in registers and only h is written;
+//                 down mode: writes the f32 rows of Y.
+// Tiles: expert e owns ceil(rows_e / 128) M-tiles (rows_e = kept routes of e,
+// from the dispatch stage, read on the device -- empty capacity slots cost no
+// MMA work); tile order is expert-major, then N-tile, then M-tile, so the CTAs
+// in flight share one expert's weights and activations in L2.
+#include "moe_internal.h"
+#include "common.cuh"
+#include "sm100.cuh"
+
+#include <cudaTypedefs.h>
+#include <cuda.h>
+#include <mutex>
+
+namespace moe {
+namespace {
+
+using namespace sm100;
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;
+constexpr int kUmmaN = 256;
+constexpr int kStages = 4;
+constexpr int kThreads = 192;
+constexpr int kABytes = kBM * kBK * 2;              // 16 KB
+constexpr int kBChunkBytes = kBK * 64 * 2;          // 8 KB: 64 K-rows x 64 N (one 128B swizzle span)
+constexpr int kBBytes = kUmmaN / 64 * kBChunkBytes; // 32 KB
+constexpr int kStageBytes = kABytes + kBBytes;
+constexpr int kAccCols = kUmmaN;
+constexpr int kTmemCols = 2 * kAccCols;
+constexpr int kMaxExperts = 256;
+constexpr size_t kSmemBytes = 1024 + (size_t)kStages * kStageBytes + 256;
+
+struct GemmParams {
+    const int* expert_rows;  // [E] kept rows per expert
+    int E;
+    int rows_per_expert;     // row stride of one expert in A and in the output (B*CAP)
+    int K;                   // reduction length (d for up/gate, f for down)
+    int n_tiles;             // output tiles along N per expert
+    int out_ld;              // output row length in elements (f or d)
+    void* out;               // 16-bit h rows (up/gate) or f32 y rows (down)
+    int* status;
+    uint32_t idesc;
+};
+
+__device__ __forceinline__ void decode_tile(int t, const int* pre, const int* mt, int E, int& e,
+                                            int& m, int& n) {
+    int lo = 0, hi = E - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (pre[mid] <= t) lo = mid; else hi = mid - 1;
+    }
+    e = lo;
+    const int local = t - pre[e];
+    n = local / mt[e];
+    m = local - n * mt[e];
+}
+
+template <int kMode, typename T16>  // kMode 0: up/gate + SwiGLU -> h;  1: down -> f32 y
+__global__ void __launch_bounds__(kThreads, 1)
+    expert_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB0,
+                       const __grid_constant__ CUtensorMap tmB1, const GemmParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ int s_pre[kMaxExperts + 1];
+    __shared__ int s_mt[kMaxExperts];
+    __shared__ int s_rows[kMaxExperts];
+
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + kStages * kABytes;
+    uint64_t* full = reinterpret_cast<uint64_t*>(sB + kStages * kBBytes);
+    uint64_t* empty = full + kStages;
+    uint64_t* tfull = empty + kStages;
+    uint64_t* tempty = tfull + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+        for (int a = 0; a < 2; ++a) { mbar_init(&tfull[a], 1); mbar_init(&tempty[a], 128); }
+        fence_mbar_init();
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB0);
+        if (kMode == 0) tma_prefetch_desc(&tmB1);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, kTmemCols);
+        tmem_relinquish();
+    }
+    for (int e = threadIdx.x; e < p.E; e += kThreads) {
+        const int r = p.expert_rows[e];
+        s_rows[e] = r;
+        s_mt[e] = (r + kBM - 1) / kBM;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int acc = 0;
+        for (int e = 0; e < p.E; ++e) { s_pre[e] = acc; acc += s_mt[e] * p.n_tiles; }
+        s_pre[p.E] = acc;
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const int total = s_pre[p.E];
+    const int kblocks = p.K / kBK;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------- TMA producer ----------------
+            int s = 0;
+            uint32_t ph = 0;
+            for (int t = blockIdx.x; t < total; t += gridDim.x) {
+                int e, m, n;
+                decode_tile(t, s_pre, s_mt, p.E, e, m, n);
+                const int a_row = e * p.rows_per_expert + m * kBM;
+                const int b_row = e * p.K;
+                for (int kb = 0; kb < kblocks; ++kb) {
+                    if (!mbar_wait(&empty[s], ph ^ 1u, p.status, kDevErrTimeout)) goto producer_done;
+                    mbar_arrive_expect_tx(&full[s], kStageBytes);
+                    uint8_t* a_dst = sA + s * kABytes;
+                    uint8_t* b_dst = sB + s * kBBytes;
+                    tma_load_2d(a_dst, &tmA, &full[s], kb * kBK, a_row);
+                    if (kMode == 0) {
+                        const int n0 = n * 128;
+                        tma_load_2d(b_dst + 0 * kBChunkBytes, &tmB0, &full[s], n0, b_row + kb * kBK);
+                        tma_load_2d(b_dst + 1 * kBChunkBytes, &tmB0, &full[s], n0 + 64, b_row + kb * kBK);
+                        tma_load_2d(b_dst + 2 * kBChunkBytes, &tmB1, &full[s], n0, b_row + kb * kBK);
+                        tma_load_2d(b_dst + 3 * kBChunkBytes, &tmB1, &full[s], n0 + 64, b_row + kb * kBK);
+                    } else {
+                        const int n0 = n * 256;
+#pragma unroll
+                        for (int j = 0; j < 4; ++j)
+                            tma_load_2d(b_dst + j * kBChunkBytes, &tmB0, &full[s], n0 + 64 * j, b_row + kb * kBK);
+                    }
+                    if (++s == kStages) { s = 0; ph ^= 1u; }
+                }
+            }
+        producer_done:;
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---------------- MMA issuer ----------------
+            int s = 0;
+            uint32_t ph = 0;
+            int acc = 0;
+            uint32_t aph = 0;
+            for (int t = blockIdx.x; t < total; t += gridDim.x) {
+                if (!mbar_wait(&tempty[acc], aph ^ 1u, p.status, kDevErrTimeout)) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + acc * kAccCols;
+                bool ok = true;
+                for (int kb = 0; kb < kblocks; ++kb) {
+                    if (!mbar_wait(&full[s], ph, p.status, kDevErrTimeout)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t a_base = smem_u32(sA + s * kABytes);
+                    const uint32_t b_base = smem_u32(sB + s * kBBytes);
+#pragma unroll
+                    for (int kk = 0; kk < kBK / 16; ++kk) {
+                        // A: K-major SW128, 8-row groups 1024 B apart; K step = 32 B.
+                        const uint64_t adesc = smem_desc_sw128(a_base + kk * 32, 16, 1024);
+                        // B: MN-major SW128; 64-wide N chunks kBChunkBytes apart (LBO),
+                        // 8-row K groups 1024 B apart (SBO); K step = 16 rows = 2048 B.
+                        const uint64_t bdesc = smem_desc_sw128(b_base + kk * 2048, kBChunkBytes, 1024);
+                        mma_f16_ss(d_tmem, adesc, bdesc, p.idesc, (kb | kk) != 0 ? 1u : 0u);
+                    }
+                    mma_commit(&empty[s]);
+                    if (++s == kStages) { s = 0; ph ^= 1u; }
+                }
+                if (!ok) break;
+                mma_commit(&tfull[acc]);
+                acc ^= 1;
+                if (acc == 0) aph ^= 1u;
+            }
+        }
+    } else {
+        // ---------------- epilogue (warps 2..5) ----------------
+        const int q = warp & 3;                // TMEM lane quarter this warp may access
+        const int row_in_tile = q * 32 + lane;
+        int acc = 0;
+        uint32_t aph = 0;
+        for (int t = blockIdx.x; t < total; t += gridDim.x) {
+            int e, m, n;
+            decode_tile(t, s_pre, s_mt, p.E, e, m, n);
+            if (!mbar_wait(&tfull[acc], aph, p.status, kDevErrTimeout)) break;
+            tc_fence_after();
+            const int row_local = m * kBM + row_in_tile;
+            const bool valid = row_local < s_rows[e];
+            const int64_t out_row = (int64_t)e * p.rows_per_expert + row_local;
+            const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + acc * kAccCols;
+            if (kMode == 0) {
+                T16* h = reinterpret_cast<T16*>(p.out) + out_row * p.out_ld + n * 128;
+#pragma unroll 1
+                for (int c = 0; c < 128; c += 32) {
+                    uint32_t g[32], u[32];
+                    tmem_ld_32x32b_x32(taddr + c, g);
+                    tmem_ld_32x32b_x32(taddr + 128 + c, u);
+                    tmem_wait_ld();
+                    if (c == 96) { tc_fence_before(); mbar_arrive(&tempty[acc]); }
+                    uint32_t packed[16];
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        float hv[2];
+#pragma unroll
+                        for (int j = 0; j < 2; ++j) {
+                            const float gv = __uint_as_float(g[2 * i + j]);
+                            const float uv = __uint_as_float(u[2 * i + j]);
+                            const float silu = gv / (1.0f + __expf(-gv));
+                            hv[j] = uv * silu;
+                        }
+                        packed[i] = F16Traits<T16>::pack2(hv[0], hv[1]);
+                    }
+                    if (valid) {
+                        uint4* dst = reinterpret_cast<uint4*>(h + c);
+#pragma unroll
+                        for (int v = 0; v < 4; ++v)
+                            dst[v] = make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
+                    }
+                }
+            } else {
+                float* y = reinterpret_cast<float*>(p.out) + out_row * p.out_ld + n * 256;
+#pragma unroll 1
+                for (int c = 0; c < 256; c += 32) {
+                    uint32_t r[32];
+                    tmem_ld_32x32b_x32(taddr + c, r);
+                    tmem_wait_ld();
+                    if (c == 224) { tc_fence_before(); mbar_arrive(&tempty[acc]); }
+                    if (valid) {
+                        uint4* dst = reinterpret_cast<uint4*>(y + c);
+#pragma unroll
+                        for (int v = 0; v < 8; ++v)
+                            dst[v] = make_uint4(r[4 * v], r[4 * v + 1], r[4 * v + 2], r[4 * v + 3]);
+                    }
+                }
+            }
+            acc ^= 1;
+            if (acc == 0) aph ^= 1u;
+        }
+    }
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, kTmemCols);
+    }
+}
+
+// ---- host side ----------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, []() {
+        cudaDriverEntryPointQueryResult q;
+        void* ptr = nullptr;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    });
+    return fn;
+}
+
+// 2-D row-major tensor [outer, inner] of 16-bit elements, 128B-swizzled boxes.
+bool make_map_16(CUtensorMap* map, const void* base, bool bf16, uint64_t inner, uint64_t outer,
+                 uint32_t box_inner, uint32_t box_outer) {
+    auto fn = encode_fn();
+    if (!fn) { set_error("cuTensorMapEncodeTiled unavailable"); return false; }
+    cuuint64_t dims[2] = {inner, outer};
+    cuuint64_t strides[1] = {inner * 2};
+    cuuint32_t box[2] = {box_inner, box_outer};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                    const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        set_error("cuTensorMapEncodeTiled failed (%d) for [%llu, %llu] box [%u, %u]", (int)r,
+                  (unsigned long long)outer, (unsigned long long)inner, box_outer, box_inner);
+        return false;
+    }
+    return true;
+}
+
+template <int kMode, typename T16>
+cudaError_t launch_gemm(const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& b1,
+                        const GemmParams& p, cudaStream_t st, int num_sms) {
+    auto kern = expert_gemm_kernel<kMode, T16>;
+    cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+    if (err != cudaSuccess) return err;
+    kern<<<num_sms, kThreads, kSmemBytes, st>>>(a, b0, b1, p);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_expert_up_gate(const void* a_rows, const void* w_gate, const void* w_up, const Shape& s,
+                                  const Workspace& ws, void* h_rows, cudaStream_t st, int num_sms) {
+    const bool bf = s.dtype == MOE_DTYPE_BF16;
+    const uint64_t rows = (uint64_t)s.E * s.rows_per_expert();
+    CUtensorMap ta, tg, tu;
+    if (!make_map_16(&ta, a_rows, bf, s.d, rows, kBK, kBM) ||
+        !make_map_16(&tg, w_gate, bf, s.f, (uint64_t)s.E * s.d, 64, kBK) ||
+        !make_map_16(&tu, w_up, bf, s.f, (uint64_t)s.E * s.d, 64, kBK))
+        return cudaErrorInvalidValue;
+    GemmParams p;
+    p.expert_rows = ws.expert_rows;
+    p.E = s.E;
+    p.rows_per_expert = (int)s.rows_per_expert();
+    p.K = s.d;
+    p.n_tiles = s.f / 128;
+    p.out_ld = s.f;
+    p.out = h_rows;
+    p.status = ws.status;
+    p.idesc = idesc_f16(bf, kBM, kUmmaN, false, true);
+    return bf ? launch_gemm<0, __nv_bfloat16>(ta, tg, tu, p, st, num_sms)
+              : launch_gemm<0, __half>(ta, tg, tu, p, st, num_sms);
+}
+
+cudaError_t launch_expert_down(const void* h_rows, const void* w_down, const Shape& s, const Workspace& ws,
+                               float* y_rows, cudaStream_t st, int num_sms) {
+    const bool bf = s.dtype == MOE_DTYPE_BF16;
+    const uint64_t rows = (uint64_t)s.E * s.rows_per_expert();
+    CUtensorMap th, td;
+    if (!make_map_16(&th, h_rows, bf, s.f, rows, kBK, kBM) ||
+        !make_map_16(&td, w_down, bf, s.d, (uint64_t)s.E * s.f, 64, kBK))
+        return cudaErrorInvalidValue;
+    GemmParams p;
+    p.expert_rows = ws.expert_rows;
+    p.E = s.E;
+    p.rows_per_expert = (int)s.rows_per_expert();
+    p.K = s.f;
+    p.n_tiles = s.d / 256;
+    p.out_ld = s.d;
+    p.out = y_rows;
+    p.status = ws.status;
+    p.idesc = idesc_f16(bf, kBM, kUmmaN, false, true);
+    return bf ? launch_gemm<1, __nv_bfloat16>(th, td, td, p, st, num_sms)
+              : launch_gemm<1, __half>(th, td, td, p, st, num_sms);
+}
+
+}  // namespace moe

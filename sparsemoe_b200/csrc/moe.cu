@@ -1,0 +1,328 @@
+// Orchestration of one MoE layer call and the C ABI (include/sparsemoe_b200.h).
+//
+// Stage order on the caller's stream (all asynchronous):
+//   router_topk -> dispatch (count, scan, assign+gather) -> up/gate GEMM with
+//   fused SwiGLU -> down GEMM -> combine.
+// The library owns one small device scratch block per device (routing tables,
+// status word), grown on demand and freed by moe_release(); every large
+// buffer comes from the caller's MoEArgs, as in the reference
+// (inputs/data.cu:199-524 allocates, kernels/launcher.h:21 only launches).
+#include "moe_internal.h"
+#include "../../include/config.h"
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <mutex>
+#include <string>
+
+namespace moe {
+
+namespace {
+thread_local std::string g_error;
+std::mutex g_mu;
+constexpr int kMaxDevices = 64;
+struct DeviceState {
+    void* ws = nullptr;
+    size_t ws_bytes = 0;
+    int* status = nullptr;  // status word of the last call (inside ws)
+    int num_sms = 0;
+    int cc_major = -1;
+};
+DeviceState g_dev[kMaxDevices];
+
+MoeDims default_dims() {
+    MoeDims d{};
+    d.num_batches = num_batches;
+    d.tokens = N;
+    d.d_model = d_model;
+    d.d_ff = up_proj_dim * d_model;
+    d.num_experts = num_experts;
+    d.top_k = k;
+    d.capacity_factor = capacity_factor;
+    d.cap = 0;
+    d.dtype = MOE_DTYPE_F16;
+    d.router_dtype = MOE_ROUTER_SAME;
+    d.router_bias = nullptr;
+    d.output_16 = nullptr;
+    return d;
+}
+MoeDims g_solve_dims = default_dims();
+
+size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+}  // namespace
+
+void set_error(const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_error = buf;
+}
+
+size_t workspace_bytes(const Shape& s) {
+    const size_t routes = (size_t)s.T() * s.k;
+    const size_t chunk_tab = (size_t)s.B * s.chunks() * s.E;
+    return align256(sizeof(int) * routes) + 2 * align256(sizeof(int) * chunk_tab) +
+           align256(sizeof(int) * (size_t)s.B * s.E) + align256(sizeof(int) * s.E) + 256;
+}
+
+void carve_workspace(void* base, const Shape& s, Workspace* ws) {
+    uint8_t* p = static_cast<uint8_t*>(base);
+    const size_t routes = (size_t)s.T() * s.k;
+    const size_t chunk_tab = (size_t)s.B * s.chunks() * s.E;
+    ws->route_slot = reinterpret_cast<int*>(p);  p += align256(sizeof(int) * routes);
+    ws->chunk_count = reinterpret_cast<int*>(p); p += align256(sizeof(int) * chunk_tab);
+    ws->chunk_base = reinterpret_cast<int*>(p);  p += align256(sizeof(int) * chunk_tab);
+    ws->row_base = reinterpret_cast<int*>(p);    p += align256(sizeof(int) * (size_t)s.B * s.E);
+    ws->expert_rows = reinterpret_cast<int*>(p); p += align256(sizeof(int) * s.E);
+    ws->status = reinterpret_cast<int*>(p);
+}
+
+namespace {
+
+int cuda_fail(cudaError_t e, const char* what) {
+    set_error("%s: %s", what, cudaGetErrorString(e));
+    return MOE_ERR_CUDA;
+}
+
+// Shape checks shared by every entry point.
+int make_shape(const MoeDims* d, Shape* s) {
+    if (!d) { set_error("dims is null"); return MOE_ERR_INVALID_ARG; }
+    if (d->num_batches < 0 || d->tokens < 0 || d->d_model <= 0 || d->d_ff <= 0 || d->num_experts <= 0 ||
+        d->top_k <= 0) {
+        set_error("non-positive dimension");
+        return MOE_ERR_INVALID_ARG;
+    }
+    if (d->top_k > 32 || d->top_k > d->num_experts) {
+        set_error("top_k=%d must be <= 32 and <= num_experts=%d", d->top_k, d->num_experts);
+        return MOE_ERR_INVALID_ARG;
+    }
+    if (d->num_experts % 8 != 0 || d->num_experts > 256) {
+        set_error("num_experts=%d: this build needs a multiple of 8, <= 256", d->num_experts);
+        return MOE_ERR_UNSUPPORTED;
+    }
+    if (d->d_model % 256 != 0 || d->d_ff % 128 != 0) {
+        set_error("d_model=%d must be a multiple of 256 and d_ff=%d of 128", d->d_model, d->d_ff);
+        return MOE_ERR_UNSUPPORTED;
+    }
+    if (d->dtype != MOE_DTYPE_F16 && d->dtype != MOE_DTYPE_BF16) {
+        set_error("dtype %d not supported by this entry point", d->dtype);
+        return MOE_ERR_UNSUPPORTED;
+    }
+    if (d->router_dtype != MOE_ROUTER_SAME && d->router_dtype != MOE_ROUTER_F32) {
+        set_error("router_dtype %d unknown", d->router_dtype);
+        return MOE_ERR_INVALID_ARG;
+    }
+    s->B = d->num_batches;
+    s->N = d->tokens;
+    s->d = d->d_model;
+    s->f = d->d_ff;
+    s->E = d->num_experts;
+    s->k = d->top_k;
+    s->dtype = d->dtype;
+    s->router_dtype = d->router_dtype;
+    if (d->cap > 0) s->cap = d->cap;
+    else if (d->cap == 0) s->cap = moe_capacity(d->tokens, d->top_k, d->num_experts, d->capacity_factor);
+    else s->cap = d->tokens;  // no-drop ("baseline") policy
+    if (s->cap < 0) { set_error("negative capacity"); return MOE_ERR_INVALID_ARG; }
+    const int64_t rows = (int64_t)s->E * s->B * s->cap;
+    if (rows >= (int64_t)1 << 31 || (int64_t)s->E * s->f >= (int64_t)1 << 31 ||
+        (int64_t)s->E * s->d >= (int64_t)1 << 31) {
+        set_error("problem too large for 32-bit tile coordinates");
+        return MOE_ERR_UNSUPPORTED;
+    }
+    return MOE_OK;
+}
+
+int device_state(DeviceState** out, int* dev_out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    if (dev >= kMaxDevices) { set_error("device ordinal %d too large", dev); return MOE_ERR_INVALID_ARG; }
+    DeviceState& st = g_dev[dev];
+    if (st.cc_major < 0) {
+        int major = 0, sms = 0;
+        e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
+        e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
+        st.cc_major = major;
+        st.num_sms = sms;
+    }
+    if (st.cc_major != 10) {
+        set_error("device %d has compute capability %d.x; the kernels are built for sm_100a only", dev,
+                  st.cc_major);
+        return MOE_ERR_NO_KERNEL;
+    }
+    *out = &st;
+    *dev_out = dev;
+    return MOE_OK;
+}
+
+int get_workspace(DeviceState& st, const Shape& s, Workspace* ws) {
+    const size_t need = workspace_bytes(s);
+    if (st.ws_bytes < need) {
+        if (st.ws) {
+            cudaError_t e = cudaFree(st.ws);
+            st.ws = nullptr;
+            st.ws_bytes = 0;
+            if (e != cudaSuccess) return cuda_fail(e, "cudaFree(workspace)");
+        }
+        const size_t bytes = need + need / 4;
+        cudaError_t e = cudaMalloc(&st.ws, bytes);
+        if (e != cudaSuccess) { st.ws = nullptr; return cuda_fail(e, "cudaMalloc(workspace)"); }
+        st.ws_bytes = bytes;
+    }
+    carve_workspace(st.ws, s, ws);
+    st.status = ws->status;
+    return MOE_OK;
+}
+
+}  // namespace
+}  // namespace moe
+
+using namespace moe;
+
+extern "C" int moe_capacity(int tokens, int top_k, int num_experts, float cf) {
+    // inputs/data.cu:392-398: (int)ceilf((float)N * (float)k / (float)E * cf), rounded up to 16.
+    volatile float a = (float)tokens * (float)top_k;
+    volatile float b = a / (float)num_experts;
+    volatile float c = b * cf;
+    const int raw = (int)ceilf(c);
+    return ((raw + 15) / 16) * 16;
+}
+
+extern "C" size_t moe_workspace_bytes(const MoeDims* dims) {
+    Shape s;
+    if (make_shape(dims, &s) != MOE_OK) return 0;
+    return workspace_bytes(s);
+}
+
+extern "C" const char* moe_last_error(void) { return g_error.c_str(); }
+
+extern "C" int moe_set_solve_dims(const MoeDims* dims) {
+    Shape s;
+    const int rc = make_shape(dims, &s);
+    if (rc != MOE_OK) return rc;
+    std::lock_guard<std::mutex> lk(g_mu);
+    g_solve_dims = *dims;
+    return MOE_OK;
+}
+
+extern "C" int moe_get_solve_dims(MoeDims* dims) {
+    if (!dims) return MOE_ERR_INVALID_ARG;
+    std::lock_guard<std::mutex> lk(g_mu);
+    *dims = g_solve_dims;
+    return MOE_OK;
+}
+
+extern "C" int moe_solve_v2(const MoEArgs* a, const MoeDims* dims, cudaStream_t stream) {
+    Shape s;
+    int rc = make_shape(dims, &s);
+    if (rc != MOE_OK) return rc;
+    if (!a) { set_error("args is null"); return MOE_ERR_INVALID_ARG; }
+    if (!a->input || !a->router_weights || !a->expert_up_proj_weights || !a->expert_gate_proj_weights ||
+        !a->expert_down_proj_weights || !a->selected_expert_indices || !a->selected_expert_weights ||
+        !a->expert_counts || !a->expert_token_ids || !a->expert_token_weights || !a->per_expert_wmma_inputs ||
+        !a->hidden_mlp_layer_1_out_fp16 || !a->hidden_mlp_layer_2_out || !a->final_output) {
+        set_error("a 16-bit path buffer of MoEArgs is null");
+        return MOE_ERR_INVALID_ARG;
+    }
+    DeviceState* st = nullptr;
+    int dev = 0;
+    rc = device_state(&st, &dev);
+    if (rc != MOE_OK) return rc;
+    Workspace ws;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        rc = get_workspace(*st, s, &ws);
+    }
+    if (rc != MOE_OK) return rc;
+    cudaError_t e = cudaMemsetAsync(ws.status, 0, sizeof(int), stream);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(status)");
+
+    e = launch_router_topk(a->input, a->router_weights, dims->router_bias, s, a->expert_logits,
+                           a->selected_expert_indices, a->selected_expert_weights, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "router_topk");
+    e = launch_dispatch(a->input, a->selected_expert_indices, a->selected_expert_weights, s, ws,
+                        a->expert_counts, a->expert_token_ids, a->expert_token_weights,
+                        a->per_expert_wmma_inputs, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "dispatch");
+    if (s.T() > 0 && s.cap > 0) {
+        e = launch_expert_up_gate(a->per_expert_wmma_inputs, a->expert_gate_proj_weights,
+                                  a->expert_up_proj_weights, s, ws, a->hidden_mlp_layer_1_out_fp16, stream,
+                                  st->num_sms);
+        if (e != cudaSuccess) return cuda_fail(e, "expert up/gate GEMM");
+        e = launch_expert_down(a->hidden_mlp_layer_1_out_fp16, a->expert_down_proj_weights, s, ws,
+                               a->hidden_mlp_layer_2_out, stream, st->num_sms);
+        if (e != cudaSuccess) return cuda_fail(e, "expert down GEMM");
+    }
+    e = launch_combine(a->hidden_mlp_layer_2_out, a->selected_expert_indices, a->selected_expert_weights, s,
+                       ws, a->final_output, dims->output_16, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "combine");
+    return MOE_OK;
+}
+
+extern "C" int moe_check_device_status(cudaStream_t stream) {
+    cudaError_t e = cudaStreamSynchronize(stream);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
+    int dev = 0;
+    e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    if (dev >= kMaxDevices || !g_dev[dev].status) return MOE_OK;
+    int host = 0;
+    e = cudaMemcpy(&host, g_dev[dev].status, sizeof(int), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpy(status)");
+    if (host != 0) {
+        set_error("device-side wait timed out (status %d)", host);
+        return MOE_ERR_TIMEOUT;
+    }
+    return MOE_OK;
+}
+
+extern "C" void moe_release(void) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev >= kMaxDevices) return;
+    std::lock_guard<std::mutex> lk(g_mu);
+    DeviceState& st = g_dev[dev];
+    if (st.ws) cudaFree(st.ws);
+    st.ws = nullptr;
+    st.ws_bytes = 0;
+    st.status = nullptr;
+}
+
+// kernels/launcher.h:21-48: launch, synchronise, time with events, print the
+// duration line, exit(1) on any error.
+extern "C" void solve(MoEArgs args) {
+    MoeDims dims;
+    moe_get_solve_dims(&dims);
+    dims.num_batches = args.num_batches;
+    dims.cap = args.use_capacity ? (args.cap > 0 ? args.cap : 0) : -1;
+    auto die = [](const char* what) {
+        fprintf(stderr, "CUDA Error at: %s: %s \n", what, moe_last_error());
+        exit(1);
+    };
+    if (!args.expert_up_proj_weights) {
+        set_error("only the 16-bit (capacity) weight format is implemented by solve()");
+        die("solve");
+    }
+    cudaEvent_t start, stop;
+    if (cudaEventCreate(&start) != cudaSuccess || cudaEventCreate(&stop) != cudaSuccess) {
+        set_error("cudaEventCreate failed");
+        die("solve");
+    }
+    cudaEventRecord(start);
+    if (moe_solve_v2(&args, &dims, 0) != MOE_OK) die("moe_solve_v2");
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) { set_error("%s", cudaGetErrorString(e)); die("cudaDeviceSynchronize"); }
+    if (moe_check_device_status(0) != MOE_OK) die("moe_check_device_status");
+    cudaEventRecord(stop);
+    cudaEventSynchronize(stop);
+    float ms = 0.0f;
+    cudaEventElapsedTime(&ms, start, stop);
+    printf("Total duration via cudaEventRecord: %.3f ms\n", ms);
+    cudaEventDestroy(start);
+    cudaEventDestroy(stop);
+}

@@ -1,0 +1,57 @@
+// Internal interfaces between the orchestration (moe.cu) and the kernels.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+#include "../../include/sparsemoe_b200.h"
+
+namespace moe {
+
+// Routes per dispatch chunk: the unit of the deterministic slot scan.
+constexpr int kChunkRoutes = 1024;
+
+// Error codes the kernels write to the device status word.
+constexpr int kDevErrTimeout = 1;
+
+struct Shape {
+    int B, N, d, f, E, k, cap;
+    int dtype;         // MOE_DTYPE_*
+    int router_dtype;  // MOE_ROUTER_*
+    int64_t T() const { return (int64_t)B * N; }
+    int chunks() const { return (int)(((int64_t)N * k + kChunkRoutes - 1) / kChunkRoutes); }
+    int64_t rows_per_expert() const { return (int64_t)B * cap; }  // row stride of one expert
+};
+
+// Device scratch owned by the library (one block per device, grown on demand).
+struct Workspace {
+    int* route_slot;    // [B*N*k]   slot of each route, -1 if dropped / no expert
+    int* chunk_count;   // [B, chunks, E] routes per (batch, chunk, expert)
+    int* chunk_base;    // [B, chunks, E] exclusive prefix over chunks
+    int* row_base;      // [B, E]    first row of (b, e) inside expert e's compact block
+    int* expert_rows;   // [E]       kept rows of expert e over all batches
+    int* status;        // [1]       device error word (kDevErrTimeout, ...)
+};
+size_t workspace_bytes(const Shape& s);
+void carve_workspace(void* base, const Shape& s, Workspace* ws);
+
+// router.cu: logits (+bias), warp-shuffle top-k, softmax.
+cudaError_t launch_router_topk(const void* x, const void* wr, const float* bias, const Shape& s,
+                               float* logits, int* idx, float* w, cudaStream_t st);
+// dispatch.cu: deterministic capacity slots + 16-byte row gather.
+cudaError_t launch_dispatch(const void* x, const int* idx, const float* w, const Shape& s,
+                            const Workspace& ws, int* counts, int* token_ids,
+                            float* token_weights, void* a_rows, cudaStream_t st);
+// expert_gemm.cu: grouped tcgen05 GEMMs.
+cudaError_t launch_expert_up_gate(const void* a_rows, const void* w_gate, const void* w_up,
+                                  const Shape& s, const Workspace& ws, void* h_rows,
+                                  cudaStream_t st, int num_sms);
+cudaError_t launch_expert_down(const void* h_rows, const void* w_down, const Shape& s,
+                               const Workspace& ws, float* y_rows, cudaStream_t st, int num_sms);
+// combine.cu: gate-weighted gather-sum into [B, N, d].
+cudaError_t launch_combine(const float* y_rows, const int* idx, const float* w, const Shape& s,
+                           const Workspace& ws, float* out, void* out16, cudaStream_t st);
+
+void set_error(const char* fmt, ...);
+
+}  // namespace moe

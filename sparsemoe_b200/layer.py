@@ -1,0 +1,114 @@
+"""MoeLayer: device buffers for one layer shape plus the call into the C ABI.
+
+PyTorch allocates the device memory (the reference's allocator role,
+inputs/data.cu:199-524); every computation runs in libsparsemoe_b200.so.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import torch
+
+from . import LayerConfig, MoEArgs, check, lib
+
+
+def _t16(cfg: LayerConfig):
+    return torch.bfloat16 if cfg.bf16 else torch.float16
+
+
+class MoeLayer:
+    def __init__(self, cfg: LayerConfig, device: str | torch.device = "cuda", want_logits: bool = True,
+                 want_out16: bool = True):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        B, N, d, f, E, k = cfg.num_batches, cfg.tokens, cfg.d_model, cfg.d_ff, cfg.num_experts, cfg.top_k
+        cap = cfg.capacity()
+        self.cap = cap
+        t16 = _t16(cfg)
+        dev = self.device
+        rows = max(B * E * cap, 1)
+        T = cfg.T
+        z = lambda *s, dt: torch.empty(*s, dtype=dt, device=dev)  # noqa: E731
+        self.x = z(max(T, 1), d, dt=t16)
+        self.wr = z(d, E, dt=torch.float32 if cfg.router_f32 else t16)
+        self.wg = z(E, d, f, dt=t16)
+        self.wu = z(E, d, f, dt=t16)
+        self.wd = z(E, f, d, dt=t16)
+        self.bias = None
+        self.logits = z(max(T, 1), E, dt=torch.float32) if want_logits else None
+        self.idx = z(max(T, 1), k, dt=torch.int32)
+        self.w = z(max(T, 1), k, dt=torch.float32)
+        self.counts = z(max(B, 1), E, dt=torch.int32)
+        self.token_ids = z(rows, dt=torch.int32)
+        self.token_weights = z(rows, dt=torch.float32)
+        self.a_rows = z(rows, d, dt=t16)
+        self.h_rows = z(rows, f, dt=t16)
+        self.y_rows = z(rows, d, dt=torch.float32)
+        self.out = z(max(T, 1), d, dt=torch.float32)
+        self.out16 = z(max(T, 1), d, dt=t16) if want_out16 else None
+
+    # -- inputs ---------------------------------------------------------------
+    def load(self, inputs: dict) -> "MoeLayer":
+        """Copies host inputs from make_inputs() (uint16 bit patterns) to the device."""
+        def put(dst: torch.Tensor, arr: np.ndarray):
+            arr = np.ascontiguousarray(arr)
+            if arr.dtype == np.uint16:
+                src = torch.from_numpy(arr.view(np.int16)).view(dst.dtype)
+            else:
+                src = torch.from_numpy(arr)
+            dst.copy_(src.reshape(dst.shape), non_blocking=False)
+        if self.cfg.T > 0:
+            put(self.x, inputs["x"])
+        put(self.wr, inputs["wr"])
+        put(self.wg, inputs["wg"])
+        put(self.wu, inputs["wu"])
+        put(self.wd, inputs["wd"])
+        if inputs.get("bias") is not None:
+            self.bias = torch.from_numpy(inputs["bias"]).to(self.device)
+        return self
+
+    # -- call -----------------------------------------------------------------
+    def args(self) -> MoEArgs:
+        a = MoEArgs()
+        p = lambda t: None if t is None else t.data_ptr()  # noqa: E731
+        a.input = p(self.x)
+        a.router_weights = p(self.wr)
+        a.expert_up_proj_weights = p(self.wu)
+        a.expert_gate_proj_weights = p(self.wg)
+        a.expert_down_proj_weights = p(self.wd)
+        a.expert_logits = p(self.logits)
+        a.selected_expert_indices = p(self.idx)
+        a.selected_expert_weights = p(self.w)
+        a.expert_counts = p(self.counts)
+        a.expert_token_ids = p(self.token_ids)
+        a.expert_token_weights = p(self.token_weights)
+        a.per_expert_wmma_inputs = p(self.a_rows)
+        a.hidden_mlp_layer_1_out_fp16 = p(self.h_rows)
+        a.hidden_mlp_layer_2_out = p(self.y_rows)
+        a.final_output = p(self.out)
+        a.num_batches = self.cfg.num_batches
+        a.use_capacity = self.cfg.cap >= 0
+        a.cap = self.cap
+        return a
+
+    def dims(self):
+        return self.cfg.dims(None if self.bias is None else self.bias.data_ptr(),
+                             None if self.out16 is None else self.out16.data_ptr())
+
+    def forward(self, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+        """Enqueues one layer call on `stream` (default: torch's current stream)."""
+        s = stream if stream is not None else torch.cuda.current_stream(self.device)
+        a, dm = self.args(), self.dims()
+        self._keep = (a, dm)
+        check(lib.moe_solve_v2(ctypes.byref(a), ctypes.byref(dm), ctypes.c_void_p(s.cuda_stream)))
+        return self.out
+
+    def sync_check(self, stream: torch.cuda.Stream | None = None) -> None:
+        s = stream if stream is not None else torch.cuda.current_stream(self.device)
+        check(lib.moe_check_device_status(ctypes.c_void_p(s.cuda_stream)))
+
+    # -- views --------------------------------------------------------------
+    def expert_rows(self) -> np.ndarray:
+        """Kept rows per expert (sum over batches of counts)."""
+        return self.counts.cpu().numpy().sum(axis=0)
