@@ -1,0 +1,359 @@
+#!/usr/bin/env python
+"""Benchmark of the capacity-routed MoE layer (BASELINE metric: MoE-layer tokens/s).
+
+Default workload (fits one B200): Mixtral-8x7B-shape layer
+in bf16, num_batches=8 x N=2048 tokens (T=16384), d_model=4096, d_ff=14336,
+E=8, top-2, capacity_factor=1.25 (CAP=640 per batch).  One step = one full
+layer call (router, top-k, dispatch, up/gate GEMM + SwiGLU, down GEMM,
+combine) over the T tokens.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N>1 runs under torchrun: every rank runs its own replica of the layer on its
+own tokens (no collective on the data path), value = all tokens / max-over-
+ranks time.  `--impl reference` times the CPU transcription of the reference's
+five stages (oracle/, rank 0 only) on a bounded token sample.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+STAGES = ["router_topk", "dispatch", "expert_up_gate_gemm", "expert_down_gemm", "combine"]
+KERNELS_PER_STEP = 7   # router_topk, dispatch x3 (count, scan, assign), up/gate GEMM, down GEMM, combine
+
+
+def workload(name: str):
+    import sparsemoe_b200 as sm
+    table = {
+        "mixtral_bf16": sm.LayerConfig(8, 2048, 4096, 14336, 8, 2, 1.25, dtype=sm.DTYPE_BF16),
+        "mixtral_fp16": sm.LayerConfig(8, 2048, 4096, 14336, 8, 2, 1.25, dtype=sm.DTYPE_F16),
+        "small_fp16": sm.LayerConfig(1, 512, 1024, 2048, 8, 2, 1.25, dtype=sm.DTYPE_F16),
+        # Mixtral weights with one 2048-token batch: the small case for ncu captures.
+        "mixtral_t2048": sm.LayerConfig(1, 2048, 4096, 14336, 8, 2, 1.25, dtype=sm.DTYPE_BF16),
+    }
+    return table[name]
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d, "measured"
+    return FALLBACK_PEAKS, "fallback"
+
+
+def cfg_json(name, cfg, cap):
+    return {"workload": name, "num_batches": cfg.num_batches, "tokens_per_batch": cfg.tokens,
+            "tokens": cfg.T, "d_model": cfg.d_model, "d_ff": cfg.d_ff, "experts": cfg.num_experts,
+            "top_k": cfg.top_k, "capacity_factor": cfg.capacity_factor, "cap": cap,
+            "l2": "inputs larger than L2 (x 134 MB, weights 2.8 GB; no flush needed)"}
+
+
+# ---------------------------------------------------------------------------
+def init_dist():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if ws > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl" if os.environ.get("BENCH_BACKEND", "nccl") == "nccl" else "gloo")
+    return ws, rank, local
+
+
+def barrier(ws):
+    if ws > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(v: float, ws: int, device) -> float:
+    if ws == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.f = None
+
+    def __enter__(self):
+        try:
+            self.f = tempfile.TemporaryFile(mode="w+")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.idx), "-lms", "200"], stdout=self.f,
+                                         stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if self.proc is None or self.f is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.f.seek(0)
+        rows = [r.split(", ") for r in self.f.read().strip().splitlines() if r.strip()]
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                mx = float(r[2])
+                for n, v in zip(names, r[5:9]):
+                    if v.strip() == "Active":
+                        reasons.add(n)
+            except (ValueError, IndexError):
+                continue
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+def device_inputs(layer, seed: int):
+    """Seeded synthetic inputs generated on the device (x ~ N(0,1), router
+    ~ N(0,0.02), gate/up ~ N(0,1/sqrt(d)), down ~ N(0,1/sqrt(f)))."""
+    import torch
+    cfg = layer.cfg
+    g = torch.Generator(device=layer.device)
+    g.manual_seed(seed)
+    for t, std in ((layer.x, 1.0), (layer.wr, 0.02), (layer.wg, cfg.d_model ** -0.5),
+                   (layer.wu, cfg.d_model ** -0.5), (layer.wd, cfg.d_ff ** -0.5)):
+        t.normal_(0.0, std, generator=g)
+
+
+def cpu_measure(layer, sample_tokens: int, nthreads: int):
+    """The oracle (CPU transcription of the reference's five stages) on a
+    bounded sample: routing of all T tokens, expert FFN + combine of the first
+    `sample_tokens` tokens.  tokens/s = S / (t_ffn(S) + t_route(T) * S / T)."""
+    import numpy as np
+    import torch
+    from oracle import oracle as O
+    cfg = layer.cfg
+    u16 = lambda t: t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)  # noqa: E731
+    x, wg, wu, wd = u16(layer.x), u16(layer.wg), u16(layer.wu), u16(layer.wd)
+    wr = layer.wr.cpu().numpy() if cfg.router_f32 else u16(layer.wr)
+    cap = layer.cap
+    t0 = time.perf_counter()
+    r = O.route(x, wr, None, cfg.num_batches, cfg.tokens, cfg.d_model, cfg.num_experts, cfg.top_k, cap,
+                cfg.bf16, cfg.router_f32, nthreads)
+    t_route = time.perf_counter() - t0
+    S = min(sample_tokens, cfg.T)
+    t0 = time.perf_counter()
+    O.ffn_combine(x, wg, wu, wd, cfg.num_batches, cfg.tokens, cfg.d_model, cfg.d_ff, cfg.num_experts,
+                  cfg.top_k, cfg.bf16, r["idx"], r["w"], r["route_slot"], 0, S, nthreads)
+    t_ffn = time.perf_counter() - t0
+    return S / (t_ffn + t_route * S / cfg.T), t_route, t_ffn, S
+
+
+def run_reference_arm(args, ws, rank, local):
+    """`--impl reference`: the reference has no CPU implementation and its GPU
+    kernels are not this arm; the CPU transcription of its five stages (oracle/)
+    is timed on the host cores, rank 0 only."""
+    if rank != 0:
+        return
+    import torch
+    import sparsemoe_b200 as sm
+    cfg = workload(args.config)
+    nthreads = os.cpu_count() or 1
+    layer = sm.MoeLayer(cfg, f"cuda:{local}" if torch.cuda.is_available() else "cpu", want_logits=False,
+                        want_out16=False) if torch.cuda.is_available() else None
+    if layer is None:
+        print(json.dumps({"impl": "reference", "unavailable": "no GPU to hold the synthetic workload"}))
+        return
+    device_inputs(layer, 0)
+    torch.cuda.synchronize()
+    for _ in range(args.warmup):
+        cpu_measure(layer, args.ref_sample_tokens, nthreads)
+    vals = []
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        v, _, _, S = cpu_measure(layer, args.ref_sample_tokens, nthreads)
+        vals.append(v)
+    wall = time.perf_counter() - t0
+    value = statistics.mean(vals)
+    sample = (f"routing of all {cfg.T} tokens + expert FFN/combine of {S} tokens per step, "
+              f"scaled to tokens/s")
+    print(json.dumps({
+        "impl": "reference", "metric": f"MoE-layer tokens/s ({args.config})", "value": value,
+        "unit": "tokens/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1000.0 * wall / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16" if cfg.bf16 else "f16", "data": "synthetic",
+        "config": cfg_json(args.config, cfg, layer.cap),
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": nthreads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }))
+
+
+# ---------------------------------------------------------------------------
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="mixtral_bf16")
+    ap.add_argument("--cpu-sample-tokens", type=int, default=1024)
+    ap.add_argument("--ref-sample-tokens", type=int, default=128)
+    ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline measurement")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    ws, rank, local = init_dist()
+    if args.impl == "reference":
+        run_reference_arm(args, ws, rank, local)
+        return
+
+    import torch
+    import sparsemoe_b200 as sm
+    torch.cuda.set_device(local)
+    dev = torch.device(f"cuda:{local}")
+    cfg = workload(args.config)
+    layer = sm.MoeLayer(cfg, dev, want_logits=True, want_out16=True)
+    device_inputs(layer, seed=1000 + rank)
+    stream = torch.cuda.current_stream(dev)
+
+    # warm-up (also checks the device status word once)
+    for _ in range(args.warmup):
+        layer.forward(stream)
+    layer.sync_check(stream)
+    kept = int(layer.counts.sum().item())
+
+    # ---- device-resident timing with per-stage events ----------------------
+    K = args.steps
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(6)] for _ in range(K)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for row in evs:            # torch creates the CUDA event on its first record
+        for e in row:
+            e.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier(ws)
+    torch.cuda.synchronize(dev)
+    with ClockSampler(local) as clocks:
+        start.record(stream)
+        for i in range(K):
+            arr = (ctypes.c_void_p * 6)(*[e.cuda_event for e in evs[i]])
+            sm.lib.moe_set_stage_events(arr, 6)
+            layer.forward(stream)
+        end.record(stream)
+        sm.lib.moe_set_stage_events(None, 0)
+        torch.cuda.synchronize(dev)
+    barrier(ws)
+    ms_local = start.elapsed_time(end) / K
+    ms = max_over_ranks(ms_local, ws, dev)
+    stage_ms = {name: statistics.mean(evs[i][j].elapsed_time(evs[i][j + 1]) for i in range(K))
+                for j, name in enumerate(STAGES)}
+    layer.sync_check(stream)
+
+    # ---- end-to-end through the public API with host buffers ---------------
+    x_host = torch.empty_like(layer.x, device="cpu").pin_memory()
+    x_host.copy_(layer.x)
+    out_host = torch.empty_like(layer.out16, device="cpu").pin_memory()
+    h2d = x_host.numel() * x_host.element_size()
+    d2h = out_host.numel() * out_host.element_size()
+    for _ in range(args.warmup):
+        layer.x.copy_(x_host, non_blocking=True)
+        layer.forward(stream)
+        out_host.copy_(layer.out16, non_blocking=True)
+    torch.cuda.synchronize(dev)
+    barrier(ws)
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(K):
+        layer.x.copy_(x_host, non_blocking=True)
+        layer.forward(stream)
+        out_host.copy_(layer.out16, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier(ws)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / K, ws, dev)
+
+    # ---- roofline of the dominant kernel (up/gate GEMM with fused SwiGLU) --
+    peaks, peak_src = load_peaks()
+    peak_tf = float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
+    d, f = cfg.d_model, cfg.d_ff
+    flop_up = 4.0 * d * f * kept            # gate + up, kept routes only
+    flop_down = 2.0 * d * f * kept
+    flop_router = 2.0 * cfg.T * d * cfg.num_experts
+    ach_up = flop_up / (stage_ms["expert_up_gate_gemm"] * 1e-3) / 1e12
+    ach_down = flop_down / (stage_ms["expert_down_gemm"] * 1e-3) / 1e12
+    traffic = None
+    tf = ROOT / "profiles" / "traffic.json"
+    if tf.exists():
+        try:
+            t = json.loads(tf.read_text()).get(args.config, {}).get("expert_up_gate_gemm")
+            traffic = None if t is None else float(t)
+        except Exception:
+            traffic = None
+
+    result = {
+        "metric": f"MoE-layer tokens/s ({args.config})", "value": ws * cfg.T / (ms * 1e-3),
+        "unit": "tokens/s", "n_gpus": ws, "steps": K, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16" if cfg.bf16 else "f16",
+        "data": "synthetic (seeded torch normal: x N(0,1), router N(0,0.02), W N(0,1/sqrt(fan_in)))",
+        "config": {**cfg_json(args.config, cfg, layer.cap),
+                   "parallelism": "single GPU" if ws == 1 else f"{ws} independent replicas (no data-path collective)"},
+        "roofline": {"bound": "tensor", "achieved": ach_up, "peak": peak_tf, "unit": "TFLOP/s",
+                     "frac": ach_up / peak_tf, "traffic": traffic,
+                     "kernel": "expert_up_gate_gemm (tcgen05, fused SwiGLU)",
+                     "peak_source": f"{peak_src} bf16_tflops_sustained (cuBLAS bf16, power-capped loop)"},
+        "stages_ms": stage_ms,
+        "stage_tflops": {"expert_up_gate_gemm": ach_up, "expert_down_gemm": ach_down,
+                         "layer_alg": (flop_up + flop_down + flop_router) / (ms * 1e-3) / 1e12},
+        "kept_routes": kept,
+        "e2e": {"value": ws * cfg.T / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
+                "path": "MoeLayer.forward -> moe_solve_v2, pinned host x in, 16-bit output out"},
+        "gpu_launches": KERNELS_PER_STEP * K,
+        "clocks": clocks.summary(),
+    }
+    if rank == 0 and ws == 1 and not args.no_cpu:
+        nthreads = os.cpu_count() or 1
+        v, t_route, t_ffn, S = cpu_measure(layer, args.cpu_sample_tokens, nthreads)
+        result["cpu_baseline"] = {
+            "value": v, "unit": "tokens/s", "cores": nthreads, "kind": "port",
+            "sample": f"oracle: routing of all {cfg.T} tokens ({t_route:.2f} s, scaled by S/T) + expert "
+                      f"FFN/combine of S={S} tokens ({t_ffn:.2f} s)"}
+    if rank == 0:
+        print(json.dumps(result))
+    if ws > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

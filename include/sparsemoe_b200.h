@@ -73,6 +73,13 @@ int moe_capacity(int tokens, int top_k, int num_experts, float capacity_factor);
 // (routing tables; the caller's MoEArgs buffers hold everything else).
 size_t moe_workspace_bytes(const MoeDims* dims);
 
+// Instrumentation (no reference counterpart; the reference times the whole
+// launch only, kernels/launcher.h:23-45).  With 6 cudaEvent_t handles set,
+// each later moe_solve_v2 on this host thread records events[i] on its stream
+// before stage i (0 router+top-k, 1 dispatch, 2 up/gate GEMM, 3 down GEMM,
+// 4 combine) and events[5] after the last one.  count = 0 turns it off.
+int moe_set_stage_events(void* const* events, int count);
+
 // Frees the library's cached device scratch on the current device.
 void moe_release(void);
 

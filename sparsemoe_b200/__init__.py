@@ -80,7 +80,7 @@ class MoeDims(ctypes.Structure):
 def _load() -> ctypes.CDLL:
     if not LIB_PATH.exists():
         raise ImportError(
-            f"{LIB_PATH} is missing: build it with `python -m sparsemoe_b200.build` "
+            f"{LIB_PATH} is missing: build it with `python sparsemoe_b200/build.py` "
             "(there is no CPU fallback)")
     lib = ctypes.CDLL(str(LIB_PATH), mode=os.RTLD_NOW | os.RTLD_GLOBAL)
     sig = {
@@ -92,6 +92,7 @@ def _load() -> ctypes.CDLL:
         "moe_capacity": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float]),
         "moe_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(MoeDims)]),
         "moe_release": (None, []),
+        "moe_set_stage_events": (ctypes.c_int, [ctypes.POINTER(ctypes.c_void_p), ctypes.c_int]),
         "moe_last_error": (ctypes.c_char_p, []),
         "moe_fill_normal_16": (None, [_p, ctypes.c_size_t, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_float,
                                       ctypes.c_int]),

@@ -1,6 +1,6 @@
 """Builds libsparsemoe_b200.so (the C-ABI library) in-tree with nvcc for sm_100a.
 
-Usage: python -m sparsemoe_b200.build   (or sparsemoe_b200.build.build())
+Usage: python sparsemoe_b200/build.py   (loaded by path: the package import needs the built library)
 """
 from __future__ import annotations
 

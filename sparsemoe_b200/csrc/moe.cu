@@ -20,6 +20,10 @@ namespace moe {
 
 namespace {
 thread_local std::string g_error;
+// Optional per-stage timing events (moe_set_stage_events), per host thread.
+constexpr int kStageEvents = 6;
+thread_local cudaEvent_t g_stage_ev[kStageEvents] = {};
+thread_local bool g_stage_on = false;
 std::mutex g_mu;
 constexpr int kMaxDevices = 64;
 struct DeviceState {
@@ -242,26 +246,48 @@ extern "C" int moe_solve_v2(const MoEArgs* a, const MoeDims* dims, cudaStream_t 
     if (rc != MOE_OK) return rc;
     cudaError_t e = cudaMemsetAsync(ws.status, 0, sizeof(int), stream);
     if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(status)");
+    auto mark = [&](int i) -> cudaError_t {
+        return g_stage_on ? cudaEventRecord(g_stage_ev[i], stream) : cudaSuccess;
+    };
+    if ((e = mark(0)) != cudaSuccess) return cuda_fail(e, "cudaEventRecord(stage event)");
 
     e = launch_router_topk(a->input, a->router_weights, dims->router_bias, s, a->expert_logits,
                            a->selected_expert_indices, a->selected_expert_weights, stream);
     if (e != cudaSuccess) return cuda_fail(e, "router_topk");
+    if ((e = mark(1)) != cudaSuccess) return cuda_fail(e, "cudaEventRecord(stage event)");
     e = launch_dispatch(a->input, a->selected_expert_indices, a->selected_expert_weights, s, ws,
                         a->expert_counts, a->expert_token_ids, a->expert_token_weights,
                         a->per_expert_wmma_inputs, stream);
     if (e != cudaSuccess) return cuda_fail(e, "dispatch");
+    if ((e = mark(2)) != cudaSuccess) return cuda_fail(e, "cudaEventRecord(stage event)");
     if (s.T() > 0 && s.cap > 0) {
         e = launch_expert_up_gate(a->per_expert_wmma_inputs, a->expert_gate_proj_weights,
                                   a->expert_up_proj_weights, s, ws, a->hidden_mlp_layer_1_out_fp16, stream,
                                   st->num_sms);
         if (e != cudaSuccess) return cuda_fail(e, "expert up/gate GEMM");
+        if ((e = mark(3)) != cudaSuccess) return cuda_fail(e, "cudaEventRecord(stage event)");
         e = launch_expert_down(a->hidden_mlp_layer_1_out_fp16, a->expert_down_proj_weights, s, ws,
                                a->hidden_mlp_layer_2_out, stream, st->num_sms);
         if (e != cudaSuccess) return cuda_fail(e, "expert down GEMM");
+    } else {
+        if ((e = mark(3)) != cudaSuccess) return cuda_fail(e, "cudaEventRecord(stage event)");
     }
+    if ((e = mark(4)) != cudaSuccess) return cuda_fail(e, "cudaEventRecord(stage event)");
     e = launch_combine(a->hidden_mlp_layer_2_out, a->selected_expert_indices, a->selected_expert_weights, s,
                        ws, a->final_output, dims->output_16, stream);
     if (e != cudaSuccess) return cuda_fail(e, "combine");
+    if ((e = mark(5)) != cudaSuccess) return cuda_fail(e, "cudaEventRecord(stage event)");
+    return MOE_OK;
+}
+
+extern "C" int moe_set_stage_events(void* const* events, int count) {
+    if (count == 0) { g_stage_on = false; return MOE_OK; }
+    if (!events || count != kStageEvents) {
+        set_error("moe_set_stage_events needs %d events (or count 0)", kStageEvents);
+        return MOE_ERR_INVALID_ARG;
+    }
+    for (int i = 0; i < kStageEvents; ++i) g_stage_ev[i] = static_cast<cudaEvent_t>(events[i]);
+    g_stage_on = true;
     return MOE_OK;
 }
 
