@@ -32,7 +32,7 @@ sys.path.insert(0, str(ROOT))
 
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 STAGES = ["router_topk", "dispatch", "expert_up_gate_gemm", "expert_down_gemm", "combine"]
-KERNELS_PER_STEP = 7   # router_topk, dispatch x3 (count, scan, assign), up/gate GEMM, down GEMM, combine
+KERNELS_PER_STEP = 8   # router_topk, dispatch x4 (count, scan, assign, gather), up/gate GEMM, down GEMM, combine
 
 
 def workload(name: str):

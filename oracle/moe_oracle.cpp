@@ -17,8 +17,9 @@
 //   down               capacity.cu:511
 //   combine            capacity.cu:380-423 (no renormalisation after drops)
 // The router's fp32 reduction order is fixed (the reference's WMMA order is
-// unspecified): logit[t,e] = fmaf-chain over j = 0..d-1 starting at 0.0f,
-// then + bias[e].  The GPU router uses the same order, so logits, expert
+// unspecified): 32 lane partials over interleaved 8-element chunks, each an
+// fmaf chain in ascending j, combined by an xor butterfly, then + bias[e]
+// (see oracle_route).  The GPU router uses the same order, so logits, expert
 // indices, slots and drops compare bit-exactly.
 //
 // Parity pinning: the reference has no tests, golden vectors or CPU code; its
@@ -122,18 +123,32 @@ void oracle_route(const uint16_t* x, const void* wr, int router_f32, const float
         const uint16_t* w16 = (const uint16_t*)wr;
         for (size_t i = 0; i < (size_t)d * E; ++i) wrf[i] = to_f32(w16[i], bf16);
     }
-    // capacity.cu:13-142 (router GEMM), fixed sequential fmaf order.
+    // capacity.cu:13-142 (router GEMM) in the fixed order the GPU router uses:
+    // lane l (0..31) accumulates, with fmaf from 0.0f, the 8-element chunks
+    // c = l, l+32, ... (elements 8c..8c+7) in ascending j; the 32 partials
+    // are combined by the xor butterfly p[l] = p[l] + p[l^off], off = 16..1;
+    // logit = p[0], then + bias[e].
     parallel_for((T + 63) / 64, nthreads, [&](int64_t blk) {
-        std::vector<float> xr(d), acc(E);
+        std::vector<float> xr(d);
+        float p[32], q[32];
         for (int64_t t = blk * 64; t < std::min<int64_t>(T, blk * 64 + 64); ++t) {
             for (int j = 0; j < d; ++j) xr[j] = to_f32(x[t * d + j], bf16);
-            for (int e = 0; e < E; ++e) acc[e] = 0.0f;
-            for (int j = 0; j < d; ++j) {
-                const float xj = xr[j];
-                const float* wrow = &wrf[(size_t)j * E];
-                for (int e = 0; e < E; ++e) acc[e] = fmaf(xj, wrow[e], acc[e]);
+            for (int e = 0; e < E; ++e) {
+                for (int l = 0; l < 32; ++l) {
+                    float acc = 0.0f;
+                    for (int c = l; c < d / 8; c += 32)
+                        for (int jj = 0; jj < 8; ++jj) {
+                            const int j = 8 * c + jj;
+                            acc = fmaf(xr[j], wrf[(size_t)j * E + e], acc);
+                        }
+                    p[l] = acc;
+                }
+                for (int off = 16; off > 0; off >>= 1) {
+                    for (int l = 0; l < 32; ++l) q[l] = p[l] + p[l ^ off];
+                    for (int l = 0; l < 32; ++l) p[l] = q[l];
+                }
+                logits[t * E + e] = bias ? p[0] + bias[e] : p[0];
             }
-            for (int e = 0; e < E; ++e) logits[t * E + e] = bias ? acc[e] + bias[e] : acc[e];
         }
     });
     // capacity.cu:171-238: insertion top-k with strict '>' (ties keep the lower

@@ -7,15 +7,17 @@
 // reference loop.  Kept iff slot < CAP; no renormalisation of the kept
 // weights; counts[b,e] = min(routes, CAP).
 //
-// Three launches:
+// Four launches:
 //   count   grid (chunks, B): per-(chunk, expert) route histogram
 //   scan    1 CTA:            exclusive prefix over chunks; counts; per-expert
 //                             row bases of the compact expert-major layout
 //   assign  grid (chunks, B): warp-aggregated ranking (__match_any_sync +
 //                             popc), in-order prefix across warps, writes the
-//                             slot tables, then each warp copies its kept token
-//                             rows into the expert's compact block with 16-byte
-//                             vector loads/stores.
+//                             slot tables (token ids / weights / route slots)
+//   gather  one warp per capacity slot: copies the slot's token row into the
+//                             expert's compact block with 16-byte vector
+//                             loads/stores (HBM-bound: R_kept*d*2 B read and
+//                             written).
 // Rows of expert e: [e*B*CAP + row_base[b,e], + counts[b,e]) for batch b.
 #include "moe_internal.h"
 #include <cstdint>
@@ -72,12 +74,10 @@ __global__ void __launch_bounds__(256) dispatch_scan_kernel(const int* __restric
     expert_rows[e] = rows;
 }
 
-template <typename TVec>
 __global__ void __launch_bounds__(kThreads) dispatch_assign_kernel(
-    const TVec* __restrict__ x, const int* __restrict__ idx, const float* __restrict__ w, int N,
-    int k, int E, int B, int cap, int chunks, int vec_per_row, const int* __restrict__ chunk_base,
-    const int* __restrict__ row_base, int* __restrict__ token_ids, float* __restrict__ token_weights,
-    int* __restrict__ route_slot, TVec* __restrict__ a_rows) {
+    const int* __restrict__ idx, const float* __restrict__ w, int N, int k, int E, int cap, int chunks,
+    const int* __restrict__ chunk_base, int* __restrict__ token_ids, float* __restrict__ token_weights,
+    int* __restrict__ route_slot) {
     __shared__ int base[256];
     __shared__ int wcnt[kWarps][256];
     const int c = blockIdx.x, b = blockIdx.y;
@@ -90,7 +90,6 @@ __global__ void __launch_bounds__(kThreads) dispatch_assign_kernel(
     __syncthreads();
     const int64_t routes = (int64_t)N * k;
     const int64_t rb = (int64_t)b * routes;
-    const int64_t rows_per_expert = (int64_t)B * cap;
     const unsigned lt_mask = (1u << lane) - 1u;
     for (int i = 0; i < kRounds; ++i) {
         const int64_t r = (int64_t)c * kChunkRoutes + i * kThreads + threadIdx.x;
@@ -118,31 +117,44 @@ __global__ void __launch_bounds__(kThreads) dispatch_assign_kernel(
         }
         // Slot tables.
         const bool kept = e >= 0 && slot < cap;
-        int64_t dst_row = -1;
-        int64_t tok = 0;
         if (r < routes) {
             route_slot[rb + r] = kept ? slot : -1;
             if (kept) {
-                tok = r / k;
                 const int64_t o = ((int64_t)b * E + e) * cap + slot;
-                token_ids[o] = (int)tok;
+                token_ids[o] = (int)(r / k);
                 token_weights[o] = w[rb + r];
-                dst_row = (int64_t)e * rows_per_expert + row_base[b * E + e] + slot;
             }
-        }
-        // Row gather: the warp copies each kept route's token row in turn.
-        unsigned todo = __ballot_sync(0xffffffffu, dst_row >= 0);
-        while (todo) {
-            const int src_lane = __ffs(todo) - 1;
-            todo &= todo - 1;
-            const int64_t drow = __shfl_sync(0xffffffffu, dst_row, src_lane);
-            const int64_t t = __shfl_sync(0xffffffffu, tok, src_lane);
-            const TVec* src = x + ((int64_t)b * N + t) * vec_per_row;
-            TVec* dst = a_rows + drow * vec_per_row;
-            for (int v = lane; v < vec_per_row; v += 32) dst[v] = __ldg(src + v);
         }
         __syncthreads();
     }
+}
+
+// One warp per capacity slot (b, e, s) in [B, E, CAP] order; slots past the
+// expert's count are skipped.
+__global__ void __launch_bounds__(kThreads) dispatch_gather_kernel(
+    const uint4* __restrict__ x, const int* __restrict__ counts, const int* __restrict__ token_ids,
+    const int* __restrict__ row_base, int N, int E, int B, int cap, int vec_per_row,
+    uint4* __restrict__ a_rows) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t slot_lin = (int64_t)blockIdx.x * kWarps + warp;
+    if (slot_lin >= (int64_t)B * E * cap) return;
+    const int be = (int)(slot_lin / cap);
+    const int s = (int)(slot_lin - (int64_t)be * cap);
+    if (s >= counts[be]) return;
+    const int b = be / E, e = be - b * E;
+    const int64_t t = token_ids[slot_lin];
+    const uint4* src = x + ((int64_t)b * N + t) * vec_per_row;
+    uint4* dst = a_rows + ((int64_t)e * B * cap + row_base[be] + s) * vec_per_row;
+    int v = lane;
+    for (; v + 96 < vec_per_row; v += 128) {
+        const uint4 a0 = __ldg(src + v), a1 = __ldg(src + v + 32), a2 = __ldg(src + v + 64),
+                    a3 = __ldg(src + v + 96);
+        dst[v] = a0;
+        dst[v + 32] = a1;
+        dst[v + 64] = a2;
+        dst[v + 96] = a3;
+    }
+    for (; v < vec_per_row; v += 32) dst[v] = __ldg(src + v);
 }
 
 }  // namespace
@@ -159,10 +171,13 @@ cudaError_t launch_dispatch(const void* x, const int* idx, const float* w, const
     dispatch_count_kernel<<<grid, kThreads, 0, st>>>(idx, s.N, s.k, s.E, s.chunks(), ws.chunk_count);
     dispatch_scan_kernel<<<1, 256, 0, st>>>(ws.chunk_count, s.B, s.E, s.chunks(), s.cap,
                                             ws.chunk_base, counts, ws.row_base, ws.expert_rows);
+    dispatch_assign_kernel<<<grid, kThreads, 0, st>>>(idx, w, s.N, s.k, s.E, s.cap, s.chunks(), ws.chunk_base,
+                                                      token_ids, token_weights, ws.route_slot);
     // 16-bit activations: rows of d elements = d/8 16-byte vectors.
-    dispatch_assign_kernel<uint4><<<grid, kThreads, 0, st>>>(
-        (const uint4*)x, idx, w, s.N, s.k, s.E, s.B, s.cap, s.chunks(), s.d / 8, ws.chunk_base,
-        ws.row_base, token_ids, token_weights, ws.route_slot, (uint4*)a_rows);
+    const int64_t slots = (int64_t)s.B * s.E * s.cap;
+    if (slots > 0)
+        dispatch_gather_kernel<<<(unsigned)((slots + kWarps - 1) / kWarps), kThreads, 0, st>>>(
+            (const uint4*)x, counts, token_ids, ws.row_base, s.N, s.E, s.B, s.cap, s.d / 8, (uint4*)a_rows);
     return cudaGetLastError();
 }
 

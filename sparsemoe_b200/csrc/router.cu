@@ -2,19 +2,24 @@
 //
 // Reference semantics: kernels/capacity.cu:13-142 (router GEMM, fp32 result)
 // and :171-238 (top_k_gating).  Differences by design:
-//  * logits use a fixed fp32 order -- for each (token, expert) a sequential
-//    fmaf chain over j = 0..d-1 starting at 0.0f, then + bias[e] -- so the CPU
-//    oracle reproduces them bit for bit (the reference's WMMA order is
-//    unspecified);
+//  * logits use a fixed fp32 order (the reference's WMMA order is
+//    unspecified) that the CPU oracle reproduces bit for bit:
+//      lane l (0..31) owns the 8-element chunks c = l, l+32, l+64, ... of the
+//      d-dimension (elements 8c..8c+7) and accumulates them in ascending j
+//      with fmaf, starting at 0.0f;  the 32 partial sums are then combined by
+//      an xor butterfly  p[l] = p[l] + p[l ^ off]  for off = 16, 8, 4, 2, 1;
+//      logit = p[0] (+ bias[e], one rounded add);
 //  * top-k is a k-round warp argmax over (value desc, index asc), the same
 //    selection as the reference's insertion sort with strict '>' (ties go to
 //    the lower expert index; values <= -1e20 and NaN are never selected;
 //    unfilled slots keep (-1e20, -1)).
 //
-// Layout: one CTA = 32*TPT tokens x all E experts.  Warp g owns experts
-// [8g, 8g+8); lane l owns tokens l, l+32, ... of the tile.  x and Wr are
-// staged through shared memory in K-chunks (x transposed so lanes read
-// consecutive words).  The kernel is HBM-bound on reading x once.
+// Layout: 8 warps per CTA, each warp owns TT consecutive tokens and walks the
+// experts in groups of 8.  Lanes read x as 16-byte vectors (one 512-byte
+// coalesced segment per warp load) and the matching 8 router rows x 8
+// experts; all lanes end the butterfly with the same sums.  Logits go to
+// shared memory, then the same warp runs the top-k for its tokens.  The
+// kernel reads x once from HBM (the router weights stay in L1/L2).
 #include "moe_internal.h"
 #include "common.cuh"
 #include <algorithm>
@@ -22,97 +27,100 @@
 namespace moe {
 namespace {
 
-constexpr int kTPT = 2;               // tokens per thread
-constexpr int kTM = 32 * kTPT;        // tokens per CTA
-constexpr int kKC = 64;               // K chunk staged in shared memory
+constexpr int kWarps = 8;
+constexpr int kTT = 4;  // tokens per warp
+
+template <typename TW>
+__device__ __forceinline__ void load_wr8(const TW* __restrict__ p, float (&w)[8]) {
+    if constexpr (sizeof(TW) == 4) {
+        const float4 a = *reinterpret_cast<const float4*>(p);
+        const float4 b = *reinterpret_cast<const float4*>(p + 4);
+        w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w; w[4] = b.x; w[5] = b.y; w[6] = b.z; w[7] = b.w;
+    } else {
+        const uint4 raw = __ldg(reinterpret_cast<const uint4*>(p));
+        const uint32_t* u = reinterpret_cast<const uint32_t*>(&raw);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const float2 f = F16Traits<TW>::unpack2(u[q]);
+            w[2 * q] = f.x;
+            w[2 * q + 1] = f.y;
+        }
+    }
+}
 
 template <typename TX, typename TW>
-__global__ void __launch_bounds__(1024) router_topk_kernel(
+__global__ void __launch_bounds__(kWarps * 32) router_topk_kernel(
     const TX* __restrict__ x, const TW* __restrict__ wr, const float* __restrict__ bias,
     int64_t T, int d, int E, int k, float* __restrict__ logits, int* __restrict__ idx,
     float* __restrict__ wts) {
-    extern __shared__ float smem[];
-    float* xs = smem;                   // [kKC][kTM]
-    float* ws = xs + kKC * kTM;         // [kKC][E]
-    float* lg = ws;                     // reused after the K loop: [kTM][E]
-    const int G = E / 8;
+    extern __shared__ float lg_all[];  // [kWarps][kTT][E]
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nthr = blockDim.x;
-    const int64_t t0 = (int64_t)blockIdx.x * kTM;
+    const int64_t t0 = ((int64_t)blockIdx.x * kWarps + warp) * kTT;
+    float* lg = lg_all + warp * kTT * E;
+    const int nchunks = d / 256;
 
-    float acc[kTPT][8];
+    for (int g = 0; g < E / 8; ++g) {
+        float acc[kTT][8];
 #pragma unroll
-    for (int i = 0; i < kTPT; ++i)
+        for (int tt = 0; tt < kTT; ++tt)
 #pragma unroll
-        for (int e = 0; e < 8; ++e) acc[i][e] = 0.0f;
-
-    for (int j0 = 0; j0 < d; j0 += kKC) {
-        // x tile: kTM tokens x kKC columns as 16-byte vectors, stored transposed.
-        for (int v = threadIdx.x; v < kTM * (kKC / 8); v += nthr) {
-            const int tt = v / (kKC / 8), jv = v % (kKC / 8);
-            const int64_t t = t0 + tt;
-            float f8[8];
-            if (t < T) {
-                const uint4 raw = *reinterpret_cast<const uint4*>(x + t * d + j0 + jv * 8);
-                const uint32_t* u = reinterpret_cast<const uint32_t*>(&raw);
+            for (int e = 0; e < 8; ++e) acc[tt][e] = 0.0f;
+        for (int i = 0; i < nchunks; ++i) {
+            const int j0 = 8 * (lane + 32 * i);
+            float xv[kTT][8];
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    float2 p = F16Traits<TX>::unpack2(u[q]);
-                    f8[2 * q] = p.x;
-                    f8[2 * q + 1] = p.y;
+            for (int tt = 0; tt < kTT; ++tt) {
+                const int64_t t = t0 + tt;
+                if (t < T) {
+                    const uint4 raw = __ldg(reinterpret_cast<const uint4*>(x + t * d + j0));
+                    const uint32_t* u = reinterpret_cast<const uint32_t*>(&raw);
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const float2 f = F16Traits<TX>::unpack2(u[q]);
+                        xv[tt][2 * q] = f.x;
+                        xv[tt][2 * q + 1] = f.y;
+                    }
+                } else {
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) xv[tt][q] = 0.0f;
                 }
-            } else {
-#pragma unroll
-                for (int q = 0; q < 8; ++q) f8[q] = 0.0f;
             }
 #pragma unroll
-            for (int q = 0; q < 8; ++q) xs[(jv * 8 + q) * kTM + tt] = f8[q];
-        }
-        // Wr rows j0..j0+kKC, all experts.
-        for (int v = threadIdx.x; v < kKC * E; v += nthr) {
-            const int jj = v / E, e = v % E;
-            if constexpr (sizeof(TW) == 4) {
-                ws[v] = wr[(int64_t)(j0 + jj) * E + e];
-            } else {
-                ws[v] = F16Traits<TW>::to_f32(wr[(int64_t)(j0 + jj) * E + e]);
+            for (int jj = 0; jj < 8; ++jj) {
+                float wv[8];
+                load_wr8(wr + (int64_t)(j0 + jj) * E + 8 * g, wv);
+#pragma unroll
+                for (int tt = 0; tt < kTT; ++tt)
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) acc[tt][e] = fmaf(xv[tt][jj], wv[e], acc[tt][e]);
             }
         }
-        __syncthreads();
-#pragma unroll 4
-        for (int jj = 0; jj < kKC; ++jj) {
-            const float4 w0 = *reinterpret_cast<const float4*>(&ws[jj * E + warp * 8]);
-            const float4 w1 = *reinterpret_cast<const float4*>(&ws[jj * E + warp * 8 + 4]);
-            const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
-            for (int i = 0; i < kTPT; ++i) {
-                const float xv = xs[jj * kTM + i * 32 + lane];
+        for (int tt = 0; tt < kTT; ++tt)
 #pragma unroll
-                for (int e = 0; e < 8; ++e) acc[i][e] = fmaf(xv, wv[e], acc[i][e]);
-            }
-        }
-        __syncthreads();
-    }
-
-    // Logits (+bias) to shared memory and (optionally) global.
+            for (int e = 0; e < 8; ++e)
 #pragma unroll
-    for (int i = 0; i < kTPT; ++i) {
-        const int tt = i * 32 + lane;
-        const int64_t t = t0 + tt;
+                for (int off = 16; off > 0; off >>= 1)
+                    acc[tt][e] = acc[tt][e] + __shfl_xor_sync(0xffffffffu, acc[tt][e], off);
+        if (lane == 0) {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-            const int ee = warp * 8 + e;
-            const float v = bias ? __fadd_rn(acc[i][e], bias[ee]) : acc[i][e];
-            lg[tt * E + ee] = v;
-            if (logits != nullptr && t < T) logits[t * E + ee] = v;
+            for (int tt = 0; tt < kTT; ++tt)
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    const int ee = 8 * g + e;
+                    lg[tt * E + ee] = bias ? __fadd_rn(acc[tt][e], bias[ee]) : acc[tt][e];
+                }
         }
     }
-    __syncthreads();
+    __syncwarp();
 
-    // Top-k: warp g handles tokens g, g+G, ...  Lane l owns experts l, l+32, ...
     const int per_lane = (E + 31) / 32;  // <= 8
-    for (int tt = warp; tt < kTM; tt += G) {
+    for (int tt = 0; tt < kTT; ++tt) {
         const int64_t t = t0 + tt;
         if (t >= T) break;
+        const float* row = lg + tt * E;
+        if (logits != nullptr)
+            for (int e = lane; e < E; e += 32) logits[t * E + e] = row[e];
         uint32_t taken = 0;
         float my_v = -1e20f;
         int my_i = -1;
@@ -122,7 +130,7 @@ __global__ void __launch_bounds__(1024) router_topk_kernel(
             for (int q = 0; q < per_lane; ++q) {
                 const int e = lane + 32 * q;
                 if (e < E && !(taken & (1u << q))) {
-                    const float v = lg[tt * E + e];
+                    const float v = row[e];
                     if (v > -1e20f && (bi < 0 || v > bv)) { bv = v; bi = e; }
                 }
             }
@@ -132,7 +140,7 @@ __global__ void __launch_bounds__(1024) router_topk_kernel(
                 const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
                 if (oi >= 0 && (bi < 0 || ov > bv || (ov == bv && oi < bi))) { bv = ov; bi = oi; }
             }
-            if (bi < 0) break;  // fewer than k selectable experts: rest keep the sentinel
+            if (bi < 0) break;  // fewer than k selectable experts: the rest keep the sentinel
             if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
             if (lane == l) { my_v = bv; my_i = bi; }
         }
@@ -151,12 +159,13 @@ __global__ void __launch_bounds__(1024) router_topk_kernel(
 template <typename TX, typename TW>
 cudaError_t launch_typed(const void* x, const void* wr, const float* bias, const Shape& s,
                          float* logits, int* idx, float* w, cudaStream_t st) {
-    const int threads = 32 * (s.E / 8);
-    const size_t smem = sizeof(float) * ((size_t)kKC * kTM + (size_t)std::max(kKC, kTM) * s.E);
+    const int threads = kWarps * 32;
+    const size_t smem = sizeof(float) * (size_t)kWarps * kTT * s.E;
     auto kern = router_topk_kernel<TX, TW>;
     cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (err != cudaSuccess) return err;
-    const int64_t blocks = (s.T() + kTM - 1) / kTM;
+    const int64_t per_cta = (int64_t)kWarps * kTT;
+    const int64_t blocks = (s.T() + per_cta - 1) / per_cta;
     kern<<<(unsigned)blocks, threads, smem, st>>>((const TX*)x, (const TW*)wr, bias, s.T(), s.d, s.E,
                                                   s.k, logits, idx, w);
     return cudaGetLastError();
