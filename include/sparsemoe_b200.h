@@ -57,6 +57,19 @@ void solve(struct MoEArgs args);
 // Asynchronous: returns once the layer is enqueued on `stream`.
 int moe_solve_v2(const struct MoEArgs* args, const MoeDims* dims, cudaStream_t stream);
 
+// No reference counterpart.  Same as moe_solve_v2, but the library allocates
+// nothing: its scratch lives in a static device array of
+// moe_noalloc_scratch_bytes() (4 MiB) per GPU, held until process exit.  For
+// callers that cannot let the library call cudaMalloc (engines that own all
+// device memory through a pre-planned pool; serving loops that cannot take
+// the device synchronisation of cudaMalloc/cudaFree).  Calls needing more
+// scratch than the array (moe_workspace_bytes) fail with MOE_ERR_UNSUPPORTED.
+// All calls on a device share the array: calls that overlap on the GPU race.
+// The first call on a device resolves the array's address (cudaGetSymbolAddress);
+// make it before any stream capture.
+int moe_solve_v2_noalloc(const struct MoEArgs* args, const MoeDims* dims, cudaStream_t stream);
+size_t moe_noalloc_scratch_bytes(void);
+
 // Synchronises `stream` and reports a device-side failure (MOE_ERR_TIMEOUT) of
 // the last moe_solve_v2 on this device, MOE_OK otherwise.
 int moe_check_device_status(cudaStream_t stream);

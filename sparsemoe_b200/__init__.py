@@ -92,6 +92,8 @@ def _load() -> ctypes.CDLL:
         "moe_capacity": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float]),
         "moe_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(MoeDims)]),
         "moe_release": (None, []),
+        "moe_solve_v2_noalloc": (ctypes.c_int, [ctypes.POINTER(MoEArgs), ctypes.POINTER(MoeDims), _p]),
+        "moe_noalloc_scratch_bytes": (ctypes.c_size_t, []),
         "moe_set_stage_events": (ctypes.c_int, [ctypes.POINTER(ctypes.c_void_p), ctypes.c_int]),
         "moe_last_error": (ctypes.c_char_p, []),
         "moe_fill_normal_16": (None, [_p, ctypes.c_size_t, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_float,

@@ -222,10 +222,11 @@ extern "C" int moe_get_solve_dims(MoeDims* dims) {
     return MOE_OK;
 }
 
-extern "C" int moe_solve_v2(const MoEArgs* a, const MoeDims* dims, cudaStream_t stream) {
-    Shape s;
-    int rc = make_shape(dims, &s);
-    if (rc != MOE_OK) return rc;
+namespace moe {
+
+int make_shape_checked(const MoeDims* dims, Shape* s) { return make_shape(dims, s); }
+
+int check_args_16(const MoEArgs* a) {
     if (!a) { set_error("args is null"); return MOE_ERR_INVALID_ARG; }
     if (!a->input || !a->router_weights || !a->expert_up_proj_weights || !a->expert_gate_proj_weights ||
         !a->expert_down_proj_weights || !a->selected_expert_indices || !a->selected_expert_weights ||
@@ -234,16 +235,24 @@ extern "C" int moe_solve_v2(const MoEArgs* a, const MoeDims* dims, cudaStream_t 
         set_error("a 16-bit path buffer of MoEArgs is null");
         return MOE_ERR_INVALID_ARG;
     }
+    return MOE_OK;
+}
+
+int current_device(int* dev, int* num_sms) {
     DeviceState* st = nullptr;
-    int dev = 0;
-    rc = device_state(&st, &dev);
-    if (rc != MOE_OK) return rc;
-    Workspace ws;
-    {
-        std::lock_guard<std::mutex> lk(g_mu);
-        rc = get_workspace(*st, s, &ws);
-    }
-    if (rc != MOE_OK) return rc;
+    const int rc = device_state(&st, dev);
+    if (rc == MOE_OK) *num_sms = st->num_sms;
+    return rc;
+}
+
+void note_status_word(int dev, int* status) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (dev >= 0 && dev < kMaxDevices) g_dev[dev].status = status;
+}
+
+// The stage sequence of one layer call on `stream`, given its scratch.
+int enqueue_layer(const MoEArgs* a, const MoeDims* dims, const Shape& s, const Workspace& ws, int num_sms,
+                  cudaStream_t stream) {
     cudaError_t e = cudaMemsetAsync(ws.status, 0, sizeof(int), stream);
     if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(status)");
     auto mark = [&](int i) -> cudaError_t {
@@ -263,11 +272,11 @@ extern "C" int moe_solve_v2(const MoEArgs* a, const MoeDims* dims, cudaStream_t 
     if (s.T() > 0 && s.cap > 0) {
         e = launch_expert_up_gate(a->per_expert_wmma_inputs, a->expert_gate_proj_weights,
                                   a->expert_up_proj_weights, s, ws, a->hidden_mlp_layer_1_out_fp16, stream,
-                                  st->num_sms);
+                                  num_sms);
         if (e != cudaSuccess) return cuda_fail(e, "expert up/gate GEMM");
         if ((e = mark(3)) != cudaSuccess) return cuda_fail(e, "cudaEventRecord(stage event)");
         e = launch_expert_down(a->hidden_mlp_layer_1_out_fp16, a->expert_down_proj_weights, s, ws,
-                               a->hidden_mlp_layer_2_out, stream, st->num_sms);
+                               a->hidden_mlp_layer_2_out, stream, num_sms);
         if (e != cudaSuccess) return cuda_fail(e, "expert down GEMM");
     } else {
         if ((e = mark(3)) != cudaSuccess) return cuda_fail(e, "cudaEventRecord(stage event)");
@@ -278,6 +287,27 @@ extern "C" int moe_solve_v2(const MoEArgs* a, const MoeDims* dims, cudaStream_t 
     if (e != cudaSuccess) return cuda_fail(e, "combine");
     if ((e = mark(5)) != cudaSuccess) return cuda_fail(e, "cudaEventRecord(stage event)");
     return MOE_OK;
+}
+
+}  // namespace moe
+
+extern "C" int moe_solve_v2(const MoEArgs* a, const MoeDims* dims, cudaStream_t stream) {
+    Shape s;
+    int rc = make_shape(dims, &s);
+    if (rc != MOE_OK) return rc;
+    rc = check_args_16(a);
+    if (rc != MOE_OK) return rc;
+    DeviceState* st = nullptr;
+    int dev = 0;
+    rc = device_state(&st, &dev);
+    if (rc != MOE_OK) return rc;
+    Workspace ws;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        rc = get_workspace(*st, s, &ws);
+    }
+    if (rc != MOE_OK) return rc;
+    return enqueue_layer(a, dims, s, ws, st->num_sms, stream);
 }
 
 extern "C" int moe_set_stage_events(void* const* events, int count) {

@@ -54,4 +54,12 @@ cudaError_t launch_combine(const float* y_rows, const int* idx, const float* w, 
 
 void set_error(const char* fmt, ...);
 
+// moe.cu: shared pieces of the layer entry points.
+int make_shape_checked(const MoeDims* dims, Shape* s);
+int check_args_16(const MoEArgs* a);
+int current_device(int* dev, int* num_sms);           // sm_100 check, cached SM count
+void note_status_word(int dev, int* status);            // read by moe_check_device_status
+int enqueue_layer(const MoEArgs* a, const MoeDims* dims, const Shape& s, const Workspace& ws, int num_sms,
+                  cudaStream_t stream);
+
 }  // namespace moe
