@@ -213,3 +213,28 @@ def test_stage_buffers_against_torch(gpu):
         y = L.y_rows[base:base + n]
         err_y = float((y - y_ref).abs().max() / y_ref.abs().max())
         assert err_y < 1e-3, f"expert {e} down GEMM max-abs-rel {err_y}"
+
+
+@pytest.mark.parametrize("name", ["k2", "k4"])
+def test_matches_reference_gpu_golden(gpu, name):
+    """Our layer vs the reference's own kernels/unfused.cu output on the same
+    seeded inputs (tests/golden/ref_unfused_*.npz, no capacity drop)."""
+    from pathlib import Path
+    from oracle.make_golden import layer_config
+    g = np.load(Path(__file__).parent / "golden" / f"ref_unfused_{name}.npz")
+    cfg, seed, _ = layer_config(name)
+    L = run(cfg, sm.make_inputs(cfg, seed), gpu)
+    assert np.array_equal(L.idx.cpu().numpy()[: cfg.T], g["idx"])
+    assert np.array_equal(L.counts.cpu().numpy(), g["counts"])
+    out = L.out.cpu().numpy()[: cfg.T][g["out_rows"]]
+    assert max_abs_rel(out, g["out"]) < TOL_16
+
+
+def test_nan_token_selects_nothing(gpu):
+    cfg = sm.LayerConfig(1, 64, 256, 128, 8, 2, 2.0)
+    inp = sm.make_inputs(cfg, 0)
+    inp["x"] = inp["x"].copy()
+    inp["x"][5, 3] = 0x7E00
+    L, ref, _ = full_check(cfg, gpu, inputs=inp)
+    assert (L.idx.cpu().numpy()[5] == -1).all()
+    assert float(L.out[5].abs().max()) == 0.0
