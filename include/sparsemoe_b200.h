@@ -23,6 +23,8 @@ extern "C" {
 // ---- activation / weight formats ------------------------------------------
 #define MOE_DTYPE_F16   0   // fp16 weights/activations (reference kernels/capacity.cu)
 #define MOE_DTYPE_BF16  1   // bf16 bit patterns in the same `half*` fields
+#define MOE_DTYPE_INT8  2   // per-tensor int8 weights/activations, s32 accumulate, f16 x and router
+                            // (reference kernels/capacity_int8_ptx.cu; MoEArgs *_int8 fields + scales)
 
 // ---- router formats --------------------------------------------------------
 #define MOE_ROUTER_SAME 0   // router_weights have the activation dtype
@@ -98,6 +100,11 @@ void moe_release(void);
 
 // Text of the last error recorded on this host thread ("" if none).
 const char* moe_last_error(void);
+
+// Reference inputs/data.cu:13-57: per-tensor symmetric quantiser of n fp16
+// values, scale = max|x| / qmax (1 if all zero), q = nearbyint(clamp(x/scale,
+// -qmax, qmax)).  qmax = 127 (int8) or 7 (int4 values).  Returns the scale.
+float moe_quantize_per_tensor(const uint16_t* src_f16, size_t n, int8_t* dst, float qmax);
 
 // ---- seeded input generator (the reference has none: inputs/data.cu:164-177
 //      zero-fills everything).  Counter-based, thread-count independent:

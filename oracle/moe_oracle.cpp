@@ -293,4 +293,102 @@ void oracle_ffn_combine(const uint16_t* x, const uint16_t* wg, const uint16_t* w
     });
 }
 
+// int8 path (reference kernels/capacity_int8_ptx.cu): per-tensor quantised
+// operands, exact integer GEMMs, the reference's dequant / SiLU / requant
+// arithmetic in f32.
+//   a = rn(clamp(x / s_in, -128, 127))                        :391-432
+//   U, G = s32 GEMMs; uf = U*(s_in*s_up), gf = G*(s_in*s_gate)
+//   h = rn(clamp(uf * gf/(1+exp(-gf)) * (1/s_mid), -128, 127))  :445-476
+//   Y = s32 GEMM; y = (float)Y * (s_mid*s_down)                :578-619
+//   out = sum_l w_l * y_l in route order                        (combine)
+void oracle_ffn_combine_int8(const uint16_t* x, const int8_t* wg, const int8_t* wu, const int8_t* wd,
+                             float s_in, float s_gate, float s_up, float s_mid, float s_down, int d, int f,
+                             int E, int k, const int* idx, const float* w, const int* route_slot,
+                             int64_t t_begin, int64_t t_end, float* out, int nthreads) {
+    std::vector<std::vector<int64_t>> routes(E);
+    for (int64_t t = t_begin; t < t_end; ++t)
+        for (int l = 0; l < k; ++l) {
+            const int64_t r = t * k + l;
+            if (route_slot[r] >= 0) routes[idx[r]].push_back(r);
+        }
+    const float deq_up = s_in * s_up, deq_gate = s_in * s_gate, inv_mid = 1.0f / s_mid,
+                deq_down = s_mid * s_down;
+    std::vector<float> y((size_t)(t_end - t_begin) * k * d, 0.0f);
+    constexpr int RB = 16;
+    struct Item { int e; int r0; };
+    std::vector<Item> items;
+    for (int e = 0; e < E; ++e)
+        for (int r0 = 0; r0 < (int)routes[e].size(); r0 += RB) items.push_back({e, r0});
+    parallel_for((int64_t)items.size(), nthreads, [&](int64_t it) {
+        const int e = items[it].e, r0 = items[it].r0;
+        const int nr = std::min<int>(RB, (int)routes[e].size() - r0);
+        std::vector<int32_t> a((size_t)RB * d), accg((size_t)RB * f), accu((size_t)RB * f), accy((size_t)RB * d);
+        std::vector<int32_t> h((size_t)RB * f);
+        for (int r = 0; r < nr; ++r) {
+            const int64_t tok = routes[e][r0 + r] / k;
+            for (int j = 0; j < d; ++j) {
+                const float v = f16_to_f32(x[tok * d + j]) / s_in;
+                a[(size_t)r * d + j] = (int32_t)nearbyintf(fminf(fmaxf(v, -128.f), 127.f));
+            }
+        }
+        std::fill(accg.begin(), accg.end(), 0);
+        std::fill(accu.begin(), accu.end(), 0);
+        const int8_t* Wg = wg + (size_t)e * d * f;
+        const int8_t* Wu = wu + (size_t)e * d * f;
+        const int8_t* Wd = wd + (size_t)e * f * d;
+        for (int j = 0; j < d; ++j) {
+            const int8_t* gr = Wg + (size_t)j * f;
+            const int8_t* ur = Wu + (size_t)j * f;
+            for (int r = 0; r < nr; ++r) {
+                const int32_t av = a[(size_t)r * d + j];
+                if (av == 0) continue;
+                int32_t* pg = &accg[(size_t)r * f];
+                int32_t* pu = &accu[(size_t)r * f];
+                for (int c = 0; c < f; ++c) {
+                    pg[c] += av * gr[c];
+                    pu[c] += av * ur[c];
+                }
+            }
+        }
+        for (int r = 0; r < nr; ++r)
+            for (int c = 0; c < f; ++c) {
+                const float uf = (float)accu[(size_t)r * f + c] * deq_up;
+                const float gf = (float)accg[(size_t)r * f + c] * deq_gate;
+                const float silu = gf / (1.0f + expf(-gf));
+                const float fused = uf * silu;
+                h[(size_t)r * f + c] = (int32_t)nearbyintf(fminf(fmaxf(fused * inv_mid, -128.f), 127.f));
+            }
+        std::fill(accy.begin(), accy.end(), 0);
+        for (int j = 0; j < f; ++j) {
+            const int8_t* dr = Wd + (size_t)j * d;
+            for (int r = 0; r < nr; ++r) {
+                const int32_t hv = h[(size_t)r * f + j];
+                if (hv == 0) continue;
+                int32_t* py = &accy[(size_t)r * d];
+                for (int c = 0; c < d; ++c) py[c] += hv * dr[c];
+            }
+        }
+        for (int r = 0; r < nr; ++r) {
+            const int64_t route = routes[e][r0 + r];
+            float* dst = &y[((size_t)(route - t_begin * k)) * d];
+            for (int c = 0; c < d; ++c) dst[c] = (float)accy[(size_t)r * d + c] * deq_down;
+        }
+    });
+    parallel_for(t_end - t_begin, nthreads, [&](int64_t i) {
+        const int64_t t = t_begin + i;
+        float* o = out + t * d;
+        for (int c = 0; c < d; ++c) o[c] = 0.0f;
+        for (int l = 0; l < k; ++l) {
+            const int64_t r = t * k + l;
+            if (route_slot[r] < 0) continue;
+            const float wl = w[r];
+            const float* yr = &y[((size_t)(r - t_begin * k)) * d];
+            for (int c = 0; c < d; ++c) {
+                volatile float p = wl * yr[c];
+                o[c] = o[c] + p;
+            }
+        }
+    });
+}
+
 }  // extern "C"

@@ -42,6 +42,10 @@ def lib() -> ctypes.CDLL:
         L.oracle_ffn_combine.restype = None
         L.oracle_ffn_combine.argtypes = [P, P, P, P, I, I, I, I, I, I, I, P, P, P, ctypes.c_int64,
                                          ctypes.c_int64, P, I]
+        L.oracle_ffn_combine_int8.restype = None
+        F = ctypes.c_float
+        L.oracle_ffn_combine_int8.argtypes = [P, P, P, P, F, F, F, F, F, I, I, I, I, P, P, P, ctypes.c_int64,
+                                              ctypes.c_int64, P, I]
         _lib = L
     return _lib
 
@@ -92,12 +96,32 @@ def ffn_combine(x, wg, wu, wd, B, N, d, f, E, k, bf16, idx, w, route_slot, t_beg
     return out[t_begin:t_end]
 
 
+def ffn_combine_int8(x, q, cfg, idx, w, route_slot, t_begin=0, t_end=None, nthreads=None):
+    """int8 path (reference capacity_int8_ptx.cu) for tokens [t_begin, t_end).
+    `q` holds wg_q/wu_q/wd_q (int8) and the scales s_in, s_gate, s_up, s_mid, s_down."""
+    T = cfg.T
+    t_end = T if t_end is None else t_end
+    out = np.zeros((T, cfg.d_model), np.float32)
+    ws = [np.ascontiguousarray(q[n], np.int8) for n in ("wg_q", "wu_q", "wd_q")]
+    lib().oracle_ffn_combine_int8(_ptr(np.ascontiguousarray(x, np.uint16)), *(_ptr(a) for a in ws),
+                                  q["s_in"], q["s_gate"], q["s_up"], q["s_mid"], q["s_down"], cfg.d_model,
+                                  cfg.d_ff, cfg.num_experts, cfg.top_k,
+                                  _ptr(np.ascontiguousarray(idx, np.int32)), _ptr(np.ascontiguousarray(w, np.float32)),
+                                  _ptr(np.ascontiguousarray(route_slot, np.int32)), t_begin, t_end, _ptr(out),
+                                  nthreads or threads())
+    return out[t_begin:t_end]
+
+
 def forward(inputs: dict, cfg, t_begin=0, t_end=None, nthreads=None):
     """Whole layer on the CPU for a sparsemoe_b200.LayerConfig and make_inputs() dict."""
     cap = cfg.capacity()
     r = route(inputs["x"], inputs["wr"], inputs.get("bias"), cfg.num_batches, cfg.tokens, cfg.d_model,
               cfg.num_experts, cfg.top_k, cap, cfg.bf16, cfg.router_f32, nthreads)
-    r["out"] = ffn_combine(inputs["x"], inputs["wg"], inputs["wu"], inputs["wd"], cfg.num_batches, cfg.tokens,
-                           cfg.d_model, cfg.d_ff, cfg.num_experts, cfg.top_k, cfg.bf16, r["idx"], r["w"],
-                           r["route_slot"], t_begin, t_end, nthreads)
+    if getattr(cfg, "int8", False):
+        r["out"] = ffn_combine_int8(inputs["x"], inputs, cfg, r["idx"], r["w"], r["route_slot"], t_begin, t_end,
+                                    nthreads)
+    else:
+        r["out"] = ffn_combine(inputs["x"], inputs["wg"], inputs["wu"], inputs["wd"], cfg.num_batches, cfg.tokens,
+                               cfg.d_model, cfg.d_ff, cfg.num_experts, cfg.top_k, cfg.bf16, r["idx"], r["w"],
+                               r["route_slot"], t_begin, t_end, nthreads)
     return r

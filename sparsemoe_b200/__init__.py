@@ -27,6 +27,7 @@ MOE_ERR_NO_KERNEL = -5
 
 DTYPE_F16 = 0
 DTYPE_BF16 = 1
+DTYPE_INT8 = 2
 ROUTER_SAME = 0
 ROUTER_F32 = 1
 
@@ -98,6 +99,7 @@ def _load() -> ctypes.CDLL:
         "moe_last_error": (ctypes.c_char_p, []),
         "moe_fill_normal_16": (None, [_p, ctypes.c_size_t, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_float,
                                       ctypes.c_int]),
+        "moe_quantize_per_tensor": (ctypes.c_float, [_p, ctypes.c_size_t, _p, ctypes.c_float]),
         "moe_fill_normal_f32": (None, [_p, ctypes.c_size_t, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_float]),
         "moe_zipf_bias": (None, [_p, ctypes.c_int, ctypes.c_float, ctypes.c_float, ctypes.c_uint64]),
     }
@@ -159,6 +161,8 @@ class LayerConfig:
     router_f32: bool = False
     zipf_s: float = 0.0          # > 0: add a Zipf(s) popularity bias to the logits
     cap: int = 0                 # 0: computed; > 0: override; -1: no drop
+    act_scale: float = 1.0       # int8 path: s_in (the reference's placeholder is 1.0)
+    mid_scale: float = 1.0       # int8 path: s_mid
 
     @property
     def T(self) -> int:
@@ -167,6 +171,10 @@ class LayerConfig:
     @property
     def bf16(self) -> bool:
         return self.dtype == DTYPE_BF16
+
+    @property
+    def int8(self) -> bool:
+        return self.dtype == DTYPE_INT8
 
     def capacity(self) -> int:
         if self.cap > 0:
@@ -199,10 +207,28 @@ def make_inputs(cfg: LayerConfig, seed: int = 0) -> dict:
     else:
         out["wr"] = normal16(d * E, seed, 1, 0.02, cfg.bf16).reshape(d, E)
     out["bias"] = zipf_bias(E, cfg.zipf_s) if cfg.zipf_s > 0 else None
+    if cfg.int8:
+        # reference inputs/data.cu:315-322: per-tensor int8 weights, placeholder activation scales
+        for n in ("wg", "wu", "wd"):
+            q = np.empty(out[n].size, np.int8)
+            scale = lib.moe_quantize_per_tensor(out[n].ctypes.data, out[n].size, q.ctypes.data, 127.0)
+            out[n + "_q"] = q.reshape(out[n].shape)
+            out["s_" + {"wg": "gate", "wu": "up", "wd": "down"}[n]] = float(scale)
+        out["s_in"] = float(np.float32(cfg.act_scale))
+        out["s_mid"] = float(np.float32(cfg.mid_scale))
     return out
+
+
+def quantize_per_tensor(w16: np.ndarray, qmax: float = 127.0):
+    """Reference inputs/data.cu:13-57 per-tensor quantiser; returns (int8 values, scale)."""
+    w16 = np.ascontiguousarray(w16, np.uint16)
+    q = np.empty(w16.size, np.int8)
+    scale = lib.moe_quantize_per_tensor(w16.ctypes.data, w16.size, q.ctypes.data, ctypes.c_float(qmax))
+    return q.reshape(w16.shape), float(scale)
 
 
 from .layer import MoeLayer  # noqa: E402  (needs `lib` above)
 
 __all__ = ["MoEArgs", "MoeDims", "LayerConfig", "MoeLayer", "make_inputs", "capacity", "lib", "check",
-           "MoeError", "normal16", "normal_f32", "zipf_bias", "DTYPE_F16", "DTYPE_BF16"]
+           "MoeError", "normal16", "normal_f32", "zipf_bias", "quantize_per_tensor", "DTYPE_F16", "DTYPE_BF16",
+           "DTYPE_INT8"]

@@ -65,7 +65,7 @@ __global__ void __launch_bounds__(kThreads) combine_kernel(
 cudaError_t launch_combine(const float* y_rows, const int* idx, const float* w, const Shape& s,
                            const Workspace& ws, float* out, void* out16, cudaStream_t st) {
     if (s.T() == 0) return cudaSuccess;
-    if (s.dtype == MOE_DTYPE_BF16)
+    if (s.act_bf16)
         combine_kernel<__nv_bfloat16><<<(unsigned)s.T(), kThreads, 0, st>>>(
             y_rows, idx, w, ws.route_slot, ws.row_base, s.N, s.d, s.E, s.k, s.rows_per_expert(), out,
             (__nv_bfloat16*)out16);

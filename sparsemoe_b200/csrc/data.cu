@@ -36,23 +36,34 @@ BuilderState g_builder;
 
 float h2f(half v) { return __half2float(v); }
 
-float max_abs(const std::vector<half>& v) {
-    float m = 0.0f;
-    for (const half& x : v) m = std::fmax(m, std::fabs(h2f(x)));
-    return m;
-}
-
 // inputs/data.cu:13-34 / 36-57: per-tensor symmetric, scale = max|x| / qmax,
 // q = nearbyint(clamp(x / scale, -qmax, qmax)).
-float quant_symmetric(const std::vector<half>& src, std::vector<int8_t>& dst, float qmax) {
-    const float m = max_abs(src);
+float quant_symmetric(const std::vector<half>& src, std::vector<int8_t>& dst, float qmax);
+
+}  // namespace
+
+extern "C" float moe_quantize_per_tensor(const uint16_t* src, size_t n, int8_t* dst, float qmax) {
+    float m = 0.0f;
+    for (size_t i = 0; i < n; ++i) {
+        half h;
+        std::memcpy(&h, &src[i], 2);
+        m = std::fmax(m, std::fabs(__half2float(h)));
+    }
     const float scale = m > 0.0f ? m / qmax : 1.0f;
-    dst.resize(src.size());
-    for (size_t i = 0; i < src.size(); ++i) {
-        const float c = std::fmin(qmax, std::fmax(-qmax, h2f(src[i]) / scale));
+    for (size_t i = 0; i < n; ++i) {
+        half h;
+        std::memcpy(&h, &src[i], 2);
+        const float c = std::fmin(qmax, std::fmax(-qmax, __half2float(h) / scale));
         dst[i] = (int8_t)(int)nearbyintf(c);
     }
     return scale;
+}
+
+namespace {
+
+float quant_symmetric(const std::vector<half>& src, std::vector<int8_t>& dst, float qmax) {
+    dst.resize(src.size());
+    return moe_quantize_per_tensor(reinterpret_cast<const uint16_t*>(src.data()), src.size(), dst.data(), qmax);
 }
 
 // inputs/data.cu:59-87: int4 values, two per byte, even index in the low nibble.

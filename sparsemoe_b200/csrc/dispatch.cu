@@ -21,6 +21,7 @@
 // Rows of expert e: [e*B*CAP + row_base[b,e], + counts[b,e]) for batch b.
 #include "moe_internal.h"
 #include <cstdint>
+#include <cuda_fp16.h>
 
 namespace moe {
 namespace {
@@ -157,11 +158,42 @@ __global__ void __launch_bounds__(kThreads) dispatch_gather_kernel(
     for (; v < vec_per_row; v += 32) dst[v] = __ldg(src + v);
 }
 
+// int8 path (reference capacity_int8_ptx.cu:391-432): the slot's f16 token row
+// quantised as rn(clamp(x / s_in, -128, 127)), 8 values per 16-byte load.
+__global__ void __launch_bounds__(kThreads) dispatch_gather_q8_kernel(
+    const uint4* __restrict__ x, const int* __restrict__ counts, const int* __restrict__ token_ids,
+    const int* __restrict__ row_base, int N, int E, int B, int cap, int vec_per_row, float s_in,
+    uint2* __restrict__ a_rows) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t slot_lin = (int64_t)blockIdx.x * kWarps + warp;
+    if (slot_lin >= (int64_t)B * E * cap) return;
+    const int be = (int)(slot_lin / cap);
+    const int s = (int)(slot_lin - (int64_t)be * cap);
+    if (s >= counts[be]) return;
+    const int b = be / E, e = be - b * E;
+    const int64_t t = token_ids[slot_lin];
+    const uint4* src = x + ((int64_t)b * N + t) * vec_per_row;
+    uint2* dst = a_rows + ((int64_t)e * B * cap + row_base[be] + s) * vec_per_row;
+    for (int v = lane; v < vec_per_row; v += 32) {
+        const uint4 raw = __ldg(src + v);
+        const __half2* h2 = reinterpret_cast<const __half2*>(&raw);
+        uint32_t w[2] = {0u, 0u};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const float2 f = __half22float2(h2[q]);
+            const int q0 = __float2int_rn(fminf(fmaxf(f.x / s_in, -128.f), 127.f));
+            const int q1 = __float2int_rn(fminf(fmaxf(f.y / s_in, -128.f), 127.f));
+            w[q >> 1] |= ((uint32_t)(q0 & 0xFF) | ((uint32_t)(q1 & 0xFF) << 8)) << (16 * (q & 1));
+        }
+        dst[v] = make_uint2(w[0], w[1]);
+    }
+}
+
 }  // namespace
 
 cudaError_t launch_dispatch(const void* x, const int* idx, const float* w, const Shape& s,
-                            const Workspace& ws, int* counts, int* token_ids, float* token_weights,
-                            void* a_rows, cudaStream_t st) {
+                            const Workspace& ws, const GemmScales& sc, int* counts, int* token_ids,
+                            float* token_weights, void* a_rows, cudaStream_t st) {
     if (s.T() == 0) {
         cudaError_t e = cudaMemsetAsync(ws.expert_rows, 0, sizeof(int) * s.E, st);
         if (e == cudaSuccess && s.B > 0) e = cudaMemsetAsync(counts, 0, sizeof(int) * s.B * s.E, st);
@@ -175,9 +207,14 @@ cudaError_t launch_dispatch(const void* x, const int* idx, const float* w, const
                                                       token_ids, token_weights, ws.route_slot);
     // 16-bit activations: rows of d elements = d/8 16-byte vectors.
     const int64_t slots = (int64_t)s.B * s.E * s.cap;
-    if (slots > 0)
-        dispatch_gather_kernel<<<(unsigned)((slots + kWarps - 1) / kWarps), kThreads, 0, st>>>(
-            (const uint4*)x, counts, token_ids, ws.row_base, s.N, s.E, s.B, s.cap, s.d / 8, (uint4*)a_rows);
+    const unsigned gblocks = (unsigned)((slots + kWarps - 1) / kWarps);
+    if (slots > 0 && s.dtype == MOE_DTYPE_INT8)
+        dispatch_gather_q8_kernel<<<gblocks, kThreads, 0, st>>>((const uint4*)x, counts, token_ids, ws.row_base,
+                                                                s.N, s.E, s.B, s.cap, s.d / 8, sc.s_in,
+                                                                (uint2*)a_rows);
+    else if (slots > 0)
+        dispatch_gather_kernel<<<gblocks, kThreads, 0, st>>>((const uint4*)x, counts, token_ids, ws.row_base,
+                                                             s.N, s.E, s.B, s.cap, s.d / 8, (uint4*)a_rows);
     return cudaGetLastError();
 }
 

@@ -1,24 +1,34 @@
 // Stage 4: the expert SwiGLU FFN as two grouped GEMMs on tcgen05 tensor cores.
 //
-// Reference semantics: kernels/capacity.cu:505-511 -- U = A_e Wup_e and
-// G = A_e Wgate_e in f32, h = U * G / (1 + exp(-G)) rounded to the 16-bit type
-// (capacity.cu:144-168), then Y = h_e Wdown_e in f32.
+// Reference semantics:
+//   16-bit  kernels/capacity.cu:505-511 -- U = A_e Wup_e, G = A_e Wgate_e in
+//           f32, h = U * G / (1 + exp(-G)) rounded to the 16-bit type
+//           (capacity.cu:144-168), then Y = h_e Wdown_e in f32.
+//   int8    kernels/capacity_int8_ptx.cu:445-476 and :578-619 -- s32 GEMMs on
+//           per-tensor quantised operands; U*s_in*s_up, G*s_in*s_gate, SiLU*mul,
+//           requantised h = rn(clamp(x / s_mid, -128, 127)); the down GEMM's
+//           s32 result is dequantised by s_mid*s_down.
 //
 // Design (one persistent CTA per SM, warp-specialised, 192 threads):
-//   warp 0      TMA producer: A tile 128 x 64 (K-major, 128B swizzle) and the
-//               B tile 64 x 256 straight from the reference's row-major
-//               [K, N] weights (N-contiguous = MN-major, 128B swizzle), into a
-//               4-stage smem ring guarded by full/empty mbarriers.
-//   warp 1      MMA issuer: one thread issues tcgen05.mma M=128 N=256 K=16
-//               (4 per 64-wide K block) into a double-buffered TMEM
-//               accumulator (2 x 256 f32 columns), commits to the ring's
-//               empty barrier and, per tile, to the accumulator-full barrier.
+//   warp 0      TMA producer: A tile 128 rows x 128 bytes of K (K-major, 128B
+//               swizzle) and the B tile of 128 bytes of K rows x 256 columns
+//               straight from the reference's row-major [K, N] weights
+//               (N-contiguous = MN-major, 128B swizzle), into a 4-stage smem
+//               ring guarded by full/empty mbarriers.
+//   warp 1      MMA issuer: one thread issues tcgen05.mma M=128 N=256 (4 per
+//               K block) into a double-buffered TMEM accumulator (2 x 256
+//               columns), commits to the ring's empty barrier and, per tile,
+//               to the accumulator-full barrier.
 //   warps 2-5   epilogue: tcgen05.ld rows out of TMEM, releases the buffer,
 //               then
 //                 up/gate mode: columns [0,128) = gate, [128,256) = up of the
 //                 same 128 output features (the B tile holds Wgate | Wup), so
-//                 SwiGLU is applied in registers and only h is written;
-//                 down mode: writes the f32 rows of Y.
+//                 SwiGLU (and the int8 requantisation) happens in registers
+//                 and only h is written;
+//                 down mode: writes the f32 rows of Y (int8: dequantised).
+// The operand format is a trait (Fmt16 / FmtI8): both keep 128-byte swizzle
+// rows, so only the K block (64 vs 128 elements), the B chunk width (64 vs
+// 128 columns), the MMA kind and the epilogue arithmetic differ.
 // Tiles: expert e owns ceil(rows_e / 128) M-tiles (rows_e = kept routes of e,
 // from the dispatch stage, read on the device -- empty capacity slots cost no
 // MMA work); tile order is expert-major, then N-tile, then M-tile, so the CTAs
@@ -37,13 +47,11 @@ namespace {
 using namespace sm100;
 
 constexpr int kBM = 128;
-constexpr int kBK = 64;
 constexpr int kUmmaN = 256;
 constexpr int kStages = 4;
 constexpr int kThreads = 192;
-constexpr int kABytes = kBM * kBK * 2;              // 16 KB
-constexpr int kBChunkBytes = kBK * 64 * 2;          // 8 KB: 64 K-rows x 64 N (one 128B swizzle span)
-constexpr int kBBytes = kUmmaN / 64 * kBChunkBytes; // 32 KB
+constexpr int kABytes = kBM * 128;                  // 16 KB: 128 rows x 128 bytes of K
+constexpr int kBBytes = 128 * kUmmaN;               // 32 KB: 128 bytes of K rows x 256 columns
 constexpr int kStageBytes = kABytes + kBBytes;
 constexpr int kAccCols = kUmmaN;
 constexpr int kTmemCols = 2 * kAccCols;
@@ -57,9 +65,86 @@ struct GemmParams {
     int K;                   // reduction length (d for up/gate, f for down)
     int n_tiles;             // output tiles along N per expert
     int out_ld;              // output row length in elements (f or d)
-    void* out;               // 16-bit h rows (up/gate) or f32 y rows (down)
+    void* out;               // h rows (up/gate) or f32 y rows (down)
     int* status;
     uint32_t idesc;
+    // int8 per-tensor scales (capacity_int8_ptx.cu:455-457, 596)
+    float deq_gate, deq_up;  // s_in*s_gate, s_in*s_up
+    float inv_mid;           // 1 / s_mid
+    float deq_down;          // s_mid*s_down
+};
+
+// ---- operand formats -----------------------------------------------------------
+template <typename T16>
+struct Fmt16 {
+    static constexpr int kElemBytes = 2;
+    static constexpr int kBK = 64;           // K elements per stage (128 bytes)
+    static constexpr int kChunkN = 64;       // B columns per 128-byte swizzle span
+    static constexpr int kUmmaK = 16;
+    static __device__ __forceinline__ void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t id, uint32_t acc) {
+        mma_f16_ss(d, a, b, id, acc);
+    }
+    // 32 columns of gate/up accumulators -> 32 h values (16-bit) at dst.
+    static __device__ __forceinline__ void swiglu_store(const uint32_t (&g)[32], const uint32_t (&u)[32],
+                                                        const GemmParams&, void* dst, bool valid) {
+        uint32_t packed[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            float hv[2];
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                const float gv = __uint_as_float(g[2 * i + j]);
+                const float uv = __uint_as_float(u[2 * i + j]);
+                hv[j] = uv * (gv / (1.0f + __expf(-gv)));
+            }
+            packed[i] = F16Traits<T16>::pack2(hv[0], hv[1]);
+        }
+        if (valid) {
+            uint4* o = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+            for (int v = 0; v < 4; ++v)
+                o[v] = make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
+        }
+    }
+    static __device__ __forceinline__ float down_value(uint32_t r, const GemmParams&) { return __uint_as_float(r); }
+};
+
+struct FmtI8 {
+    static constexpr int kElemBytes = 1;
+    static constexpr int kBK = 128;
+    static constexpr int kChunkN = 128;
+    static constexpr int kUmmaK = 32;
+    static __device__ __forceinline__ void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t id, uint32_t acc) {
+        mma_i8_ss(d, a, b, id, acc);
+    }
+    // capacity_int8_ptx.cu:465-474: dequant, SiLU(gate)*up, requant to int8.
+    static __device__ __forceinline__ void swiglu_store(const uint32_t (&g)[32], const uint32_t (&u)[32],
+                                                        const GemmParams& p, void* dst, bool valid) {
+        uint32_t packed[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            uint32_t word = 0;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float uf = (float)(int)u[4 * i + j] * p.deq_up;
+                const float gf = (float)(int)g[4 * i + j] * p.deq_gate;
+                const float silu = gf / (1.0f + __expf(-gf));
+                const float fused = uf * silu;
+                const int q = __float2int_rn(fminf(fmaxf(fused * p.inv_mid, -128.f), 127.f));
+                word |= (uint32_t)(q & 0xFF) << (8 * j);
+            }
+            packed[i] = word;
+        }
+        if (valid) {
+            uint4* o = reinterpret_cast<uint4*>(dst);
+            o[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+            o[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+        }
+    }
+    // capacity_int8_ptx.cu:615: (float)int32 * (s_mid * s_down)
+    static __device__ __forceinline__ float down_value(uint32_t r, const GemmParams& p) {
+        return (float)(int)r * p.deq_down;
+    }
 };
 
 __device__ __forceinline__ void decode_tile(int t, const int* pre, const int* mt, int E, int& e,
@@ -75,10 +160,16 @@ __device__ __forceinline__ void decode_tile(int t, const int* pre, const int* mt
     m = local - n * mt[e];
 }
 
-template <int kMode, typename T16>  // kMode 0: up/gate + SwiGLU -> h;  1: down -> f32 y
+template <int kMode, class Fmt>  // kMode 0: up/gate + SwiGLU -> h;  1: down -> f32 y
 __global__ void __launch_bounds__(kThreads, 1)
     expert_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB0,
                        const __grid_constant__ CUtensorMap tmB1, const GemmParams p) {
+    constexpr int kBK = Fmt::kBK;
+    constexpr int kChunkN = Fmt::kChunkN;
+    constexpr int kChunkBytes = kBK * 128;            // K rows x 128 bytes
+    constexpr int kChunks = kUmmaN / kChunkN;         // B chunks per stage
+    constexpr int kKSteps = kBK / Fmt::kUmmaK;        // MMAs per stage
+    constexpr int kOutN = kMode == 0 ? 128 : 256;     // output columns per tile
     extern __shared__ uint8_t smem_raw[];
     __shared__ int s_pre[kMaxExperts + 1];
     __shared__ int s_mt[kMaxExperts];
@@ -140,18 +231,22 @@ __global__ void __launch_bounds__(kThreads, 1)
                     mbar_arrive_expect_tx(&full[s], kStageBytes);
                     uint8_t* a_dst = sA + s * kABytes;
                     uint8_t* b_dst = sB + s * kBBytes;
-                    tma_load_2d(a_dst, &tmA, &full[s], kb * kBK, a_row);
+                    const int k0 = kb * kBK;
+                    tma_load_2d(a_dst, &tmA, &full[s], k0, a_row);
                     if (kMode == 0) {
+                        // [Wgate cols n0..n0+127 | Wup cols n0..n0+127]
                         const int n0 = n * 128;
-                        tma_load_2d(b_dst + 0 * kBChunkBytes, &tmB0, &full[s], n0, b_row + kb * kBK);
-                        tma_load_2d(b_dst + 1 * kBChunkBytes, &tmB0, &full[s], n0 + 64, b_row + kb * kBK);
-                        tma_load_2d(b_dst + 2 * kBChunkBytes, &tmB1, &full[s], n0, b_row + kb * kBK);
-                        tma_load_2d(b_dst + 3 * kBChunkBytes, &tmB1, &full[s], n0 + 64, b_row + kb * kBK);
+#pragma unroll
+                        for (int j = 0; j < kChunks / 2; ++j) {
+                            tma_load_2d(b_dst + j * kChunkBytes, &tmB0, &full[s], n0 + j * kChunkN, b_row + k0);
+                            tma_load_2d(b_dst + (kChunks / 2 + j) * kChunkBytes, &tmB1, &full[s], n0 + j * kChunkN,
+                                        b_row + k0);
+                        }
                     } else {
                         const int n0 = n * 256;
 #pragma unroll
-                        for (int j = 0; j < 4; ++j)
-                            tma_load_2d(b_dst + j * kBChunkBytes, &tmB0, &full[s], n0 + 64 * j, b_row + kb * kBK);
+                        for (int j = 0; j < kChunks; ++j)
+                            tma_load_2d(b_dst + j * kChunkBytes, &tmB0, &full[s], n0 + j * kChunkN, b_row + k0);
                     }
                     if (++s == kStages) { s = 0; ph ^= 1u; }
                 }
@@ -176,13 +271,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint32_t a_base = smem_u32(sA + s * kABytes);
                     const uint32_t b_base = smem_u32(sB + s * kBBytes);
 #pragma unroll
-                    for (int kk = 0; kk < kBK / 16; ++kk) {
-                        // A: K-major SW128, 8-row groups 1024 B apart; K step = 32 B.
+                    for (int kk = 0; kk < kKSteps; ++kk) {
+                        // A: K-major SW128, 8-row groups 1024 B apart; K step = 32 bytes.
                         const uint64_t adesc = smem_desc_sw128(a_base + kk * 32, 16, 1024);
-                        // B: MN-major SW128; 64-wide N chunks kBChunkBytes apart (LBO),
-                        // 8-row K groups 1024 B apart (SBO); K step = 16 rows = 2048 B.
-                        const uint64_t bdesc = smem_desc_sw128(b_base + kk * 2048, kBChunkBytes, 1024);
-                        mma_f16_ss(d_tmem, adesc, bdesc, p.idesc, (kb | kk) != 0 ? 1u : 0u);
+                        // B: MN-major SW128; column chunks kChunkBytes apart (LBO), 8-row K
+                        // groups 1024 B apart (SBO); K step = kUmmaK rows of 128 bytes.
+                        const uint64_t bdesc =
+                            smem_desc_sw128(b_base + kk * Fmt::kUmmaK * 128, kChunkBytes, 1024);
+                        Fmt::mma(d_tmem, adesc, bdesc, p.idesc, (kb | kk) != 0 ? 1u : 0u);
                     }
                     mma_commit(&empty[s]);
                     if (++s == kStages) { s = 0; ph ^= 1u; }
@@ -209,7 +305,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int64_t out_row = (int64_t)e * p.rows_per_expert + row_local;
             const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + acc * kAccCols;
             if (kMode == 0) {
-                T16* h = reinterpret_cast<T16*>(p.out) + out_row * p.out_ld + n * 128;
+                uint8_t* h = reinterpret_cast<uint8_t*>(p.out) +
+                             (out_row * p.out_ld + (int64_t)n * kOutN) * Fmt::kElemBytes;
 #pragma unroll 1
                 for (int c = 0; c < 128; c += 32) {
                     uint32_t g[32], u[32];
@@ -217,28 +314,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tmem_ld_32x32b_x32(taddr + 128 + c, u);
                     tmem_wait_ld();
                     if (c == 96) { tc_fence_before(); mbar_arrive(&tempty[acc]); }
-                    uint32_t packed[16];
-#pragma unroll
-                    for (int i = 0; i < 16; ++i) {
-                        float hv[2];
-#pragma unroll
-                        for (int j = 0; j < 2; ++j) {
-                            const float gv = __uint_as_float(g[2 * i + j]);
-                            const float uv = __uint_as_float(u[2 * i + j]);
-                            const float silu = gv / (1.0f + __expf(-gv));
-                            hv[j] = uv * silu;
-                        }
-                        packed[i] = F16Traits<T16>::pack2(hv[0], hv[1]);
-                    }
-                    if (valid) {
-                        uint4* dst = reinterpret_cast<uint4*>(h + c);
-#pragma unroll
-                        for (int v = 0; v < 4; ++v)
-                            dst[v] = make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
-                    }
+                    Fmt::swiglu_store(g, u, p, h + c * Fmt::kElemBytes, valid);
                 }
             } else {
-                float* y = reinterpret_cast<float*>(p.out) + out_row * p.out_ld + n * 256;
+                float* y = reinterpret_cast<float*>(p.out) + out_row * p.out_ld + n * kOutN;
 #pragma unroll 1
                 for (int c = 0; c < 256; c += 32) {
                     uint32_t r[32];
@@ -246,10 +325,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tmem_wait_ld();
                     if (c == 224) { tc_fence_before(); mbar_arrive(&tempty[acc]); }
                     if (valid) {
-                        uint4* dst = reinterpret_cast<uint4*>(y + c);
+                        float4* dst = reinterpret_cast<float4*>(y + c);
 #pragma unroll
                         for (int v = 0; v < 8; ++v)
-                            dst[v] = make_uint4(r[4 * v], r[4 * v + 1], r[4 * v + 2], r[4 * v + 3]);
+                            dst[v] = make_float4(Fmt::down_value(r[4 * v], p), Fmt::down_value(r[4 * v + 1], p),
+                                                 Fmt::down_value(r[4 * v + 2], p), Fmt::down_value(r[4 * v + 3], p));
                     }
                 }
             }
@@ -278,82 +358,117 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
-// 2-D row-major tensor [outer, inner] of 16-bit elements, 128B-swizzled boxes.
-bool make_map_16(CUtensorMap* map, const void* base, bool bf16, uint64_t inner, uint64_t outer,
-                 uint32_t box_inner, uint32_t box_outer) {
+// 2-D row-major tensor [outer, inner] of `elem_bytes`-byte elements, boxes of
+// 128 bytes x box_outer rows with the 128-byte swizzle.
+bool make_map(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes, uint64_t inner,
+              uint64_t outer, uint32_t box_outer) {
     auto fn = encode_fn();
     if (!fn) { set_error("cuTensorMapEncodeTiled unavailable"); return false; }
     cuuint64_t dims[2] = {inner, outer};
-    cuuint64_t strides[1] = {inner * 2};
-    cuuint32_t box[2] = {box_inner, box_outer};
+    cuuint64_t strides[1] = {inner * (uint64_t)elem_bytes};
+    cuuint32_t box[2] = {(cuuint32_t)(128 / elem_bytes), box_outer};
     cuuint32_t estr[2] = {1, 1};
-    CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
-                    const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    CUresult r = fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
         set_error("cuTensorMapEncodeTiled failed (%d) for [%llu, %llu] box [%u, %u]", (int)r,
-                  (unsigned long long)outer, (unsigned long long)inner, box_outer, box_inner);
+                  (unsigned long long)outer, (unsigned long long)inner, box_outer, box[0]);
         return false;
     }
     return true;
 }
 
-template <int kMode, typename T16>
+template <int kMode, class Fmt>
 cudaError_t launch_gemm(const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& b1,
                         const GemmParams& p, cudaStream_t st, int num_sms) {
-    auto kern = expert_gemm_kernel<kMode, T16>;
+    auto kern = expert_gemm_kernel<kMode, Fmt>;
     cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
     if (err != cudaSuccess) return err;
     kern<<<num_sms, kThreads, kSmemBytes, st>>>(a, b0, b1, p);
     return cudaGetLastError();
 }
 
-}  // namespace
+struct FmtDesc {
+    CUtensorMapDataType dt;
+    int elem_bytes;
+    int bk;
+    int chunk_n;
+};
+FmtDesc fmt_desc(int dtype) {
+    switch (dtype) {
+        case MOE_DTYPE_BF16: return {CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 64, 64};
+        case MOE_DTYPE_INT8: return {CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, 128, 128};
+        default: return {CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, 64, 64};
+    }
+}
 
-cudaError_t launch_expert_up_gate(const void* a_rows, const void* w_gate, const void* w_up, const Shape& s,
-                                  const Workspace& ws, void* h_rows, cudaStream_t st, int num_sms) {
-    const bool bf = s.dtype == MOE_DTYPE_BF16;
-    const uint64_t rows = (uint64_t)s.E * s.rows_per_expert();
-    CUtensorMap ta, tg, tu;
-    if (!make_map_16(&ta, a_rows, bf, s.d, rows, kBK, kBM) ||
-        !make_map_16(&tg, w_gate, bf, s.f, (uint64_t)s.E * s.d, 64, kBK) ||
-        !make_map_16(&tu, w_up, bf, s.f, (uint64_t)s.E * s.d, 64, kBK))
-        return cudaErrorInvalidValue;
-    GemmParams p;
+GemmParams base_params(const Shape& s, const Workspace& ws, const GemmScales& sc) {
+    GemmParams p{};
     p.expert_rows = ws.expert_rows;
     p.E = s.E;
     p.rows_per_expert = (int)s.rows_per_expert();
+    p.status = ws.status;
+    p.deq_gate = sc.s_in * sc.s_gate;
+    p.deq_up = sc.s_in * sc.s_up;
+    p.inv_mid = 1.0f / sc.s_mid;
+    p.deq_down = sc.s_mid * sc.s_down;
+    return p;
+}
+
+}  // namespace
+
+cudaError_t launch_expert_up_gate(const void* a_rows, const void* w_gate, const void* w_up, const Shape& s,
+                                  const Workspace& ws, const GemmScales& sc, void* h_rows, cudaStream_t st,
+                                  int num_sms) {
+    const FmtDesc fd = fmt_desc(s.dtype);
+    const uint64_t rows = (uint64_t)s.E * s.rows_per_expert();
+    CUtensorMap ta, tg, tu;
+    if (!make_map(&ta, a_rows, fd.dt, fd.elem_bytes, s.d, rows, kBM) ||
+        !make_map(&tg, w_gate, fd.dt, fd.elem_bytes, s.f, (uint64_t)s.E * s.d, fd.bk) ||
+        !make_map(&tu, w_up, fd.dt, fd.elem_bytes, s.f, (uint64_t)s.E * s.d, fd.bk))
+        return cudaErrorInvalidValue;
+    GemmParams p = base_params(s, ws, sc);
     p.K = s.d;
     p.n_tiles = s.f / 128;
     p.out_ld = s.f;
     p.out = h_rows;
-    p.status = ws.status;
-    p.idesc = idesc_f16(bf, kBM, kUmmaN, false, true);
-    return bf ? launch_gemm<0, __nv_bfloat16>(ta, tg, tu, p, st, num_sms)
-              : launch_gemm<0, __half>(ta, tg, tu, p, st, num_sms);
+    switch (s.dtype) {
+        case MOE_DTYPE_INT8:
+            p.idesc = idesc_i8(kBM, kUmmaN, true);
+            return launch_gemm<0, FmtI8>(ta, tg, tu, p, st, num_sms);
+        case MOE_DTYPE_BF16:
+            p.idesc = idesc_f16(true, kBM, kUmmaN, false, true);
+            return launch_gemm<0, Fmt16<__nv_bfloat16>>(ta, tg, tu, p, st, num_sms);
+        default:
+            p.idesc = idesc_f16(false, kBM, kUmmaN, false, true);
+            return launch_gemm<0, Fmt16<__half>>(ta, tg, tu, p, st, num_sms);
+    }
 }
 
 cudaError_t launch_expert_down(const void* h_rows, const void* w_down, const Shape& s, const Workspace& ws,
-                               float* y_rows, cudaStream_t st, int num_sms) {
-    const bool bf = s.dtype == MOE_DTYPE_BF16;
+                               const GemmScales& sc, float* y_rows, cudaStream_t st, int num_sms) {
+    const FmtDesc fd = fmt_desc(s.dtype);
     const uint64_t rows = (uint64_t)s.E * s.rows_per_expert();
     CUtensorMap th, td;
-    if (!make_map_16(&th, h_rows, bf, s.f, rows, kBK, kBM) ||
-        !make_map_16(&td, w_down, bf, s.d, (uint64_t)s.E * s.f, 64, kBK))
+    if (!make_map(&th, h_rows, fd.dt, fd.elem_bytes, s.f, rows, kBM) ||
+        !make_map(&td, w_down, fd.dt, fd.elem_bytes, s.d, (uint64_t)s.E * s.f, fd.bk))
         return cudaErrorInvalidValue;
-    GemmParams p;
-    p.expert_rows = ws.expert_rows;
-    p.E = s.E;
-    p.rows_per_expert = (int)s.rows_per_expert();
+    GemmParams p = base_params(s, ws, sc);
     p.K = s.f;
     p.n_tiles = s.d / 256;
     p.out_ld = s.d;
     p.out = y_rows;
-    p.status = ws.status;
-    p.idesc = idesc_f16(bf, kBM, kUmmaN, false, true);
-    return bf ? launch_gemm<1, __nv_bfloat16>(th, td, td, p, st, num_sms)
-              : launch_gemm<1, __half>(th, td, td, p, st, num_sms);
+    switch (s.dtype) {
+        case MOE_DTYPE_INT8:
+            p.idesc = idesc_i8(kBM, kUmmaN, true);
+            return launch_gemm<1, FmtI8>(th, td, td, p, st, num_sms);
+        case MOE_DTYPE_BF16:
+            p.idesc = idesc_f16(true, kBM, kUmmaN, false, true);
+            return launch_gemm<1, Fmt16<__nv_bfloat16>>(th, td, td, p, st, num_sms);
+        default:
+            p.idesc = idesc_f16(false, kBM, kUmmaN, false, true);
+            return launch_gemm<1, Fmt16<__half>>(th, td, td, p, st, num_sms);
+    }
 }
 
 }  // namespace moe

@@ -111,7 +111,7 @@ int make_shape(const MoeDims* d, Shape* s) {
         set_error("d_model=%d must be a multiple of 256 and d_ff=%d of 128", d->d_model, d->d_ff);
         return MOE_ERR_UNSUPPORTED;
     }
-    if (d->dtype != MOE_DTYPE_F16 && d->dtype != MOE_DTYPE_BF16) {
+    if (d->dtype != MOE_DTYPE_F16 && d->dtype != MOE_DTYPE_BF16 && d->dtype != MOE_DTYPE_INT8) {
         set_error("dtype %d not supported by this entry point", d->dtype);
         return MOE_ERR_UNSUPPORTED;
     }
@@ -127,6 +127,7 @@ int make_shape(const MoeDims* d, Shape* s) {
     s->k = d->top_k;
     s->dtype = d->dtype;
     s->router_dtype = d->router_dtype;
+    s->act_bf16 = d->dtype == MOE_DTYPE_BF16;
     if (d->cap > 0) s->cap = d->cap;
     else if (d->cap == 0) s->cap = moe_capacity(d->tokens, d->top_k, d->num_experts, d->capacity_factor);
     else s->cap = d->tokens;  // no-drop ("baseline") policy
@@ -226,13 +227,26 @@ namespace moe {
 
 int make_shape_checked(const MoeDims* dims, Shape* s) { return make_shape(dims, s); }
 
-int check_args_16(const MoEArgs* a) {
+int check_args_16(const MoEArgs* a) { return check_args(a, MOE_DTYPE_F16); }
+
+int check_args(const MoEArgs* a, int dtype) {
     if (!a) { set_error("args is null"); return MOE_ERR_INVALID_ARG; }
-    if (!a->input || !a->router_weights || !a->expert_up_proj_weights || !a->expert_gate_proj_weights ||
-        !a->expert_down_proj_weights || !a->selected_expert_indices || !a->selected_expert_weights ||
-        !a->expert_counts || !a->expert_token_ids || !a->expert_token_weights || !a->per_expert_wmma_inputs ||
-        !a->hidden_mlp_layer_1_out_fp16 || !a->hidden_mlp_layer_2_out || !a->final_output) {
-        set_error("a 16-bit path buffer of MoEArgs is null");
+    const bool common = a->input && a->router_weights && a->selected_expert_indices && a->selected_expert_weights &&
+                        a->expert_counts && a->expert_token_ids && a->expert_token_weights &&
+                        a->hidden_mlp_layer_2_out && a->final_output;
+    bool fmt = false;
+    if (dtype == MOE_DTYPE_INT8)
+        fmt = a->expert_up_proj_weights_int8 && a->expert_gate_proj_weights_int8 &&
+              a->expert_down_proj_weights_int8 && a->per_expert_wmma_inputs_int8 && a->hidden_mlp_layer_1_out_int8;
+    else
+        fmt = a->expert_up_proj_weights && a->expert_gate_proj_weights && a->expert_down_proj_weights &&
+              a->per_expert_wmma_inputs && a->hidden_mlp_layer_1_out_fp16;
+    if (!common || !fmt) {
+        set_error("a MoEArgs buffer needed by the %s path is null", dtype == MOE_DTYPE_INT8 ? "int8" : "16-bit");
+        return MOE_ERR_INVALID_ARG;
+    }
+    if (dtype == MOE_DTYPE_INT8 && !(a->scale_input_act > 0.0f && a->scale_mid_act > 0.0f)) {
+        set_error("int8 path needs positive scale_input_act and scale_mid_act");
         return MOE_ERR_INVALID_ARG;
     }
     return MOE_OK;
@@ -264,19 +278,29 @@ int enqueue_layer(const MoEArgs* a, const MoeDims* dims, const Shape& s, const W
                            a->selected_expert_indices, a->selected_expert_weights, stream);
     if (e != cudaSuccess) return cuda_fail(e, "router_topk");
     if ((e = mark(1)) != cudaSuccess) return cuda_fail(e, "cudaEventRecord(stage event)");
-    e = launch_dispatch(a->input, a->selected_expert_indices, a->selected_expert_weights, s, ws,
-                        a->expert_counts, a->expert_token_ids, a->expert_token_weights,
-                        a->per_expert_wmma_inputs, stream);
+    const bool i8 = s.dtype == MOE_DTYPE_INT8;
+    GemmScales sc;
+    if (i8) {
+        sc.s_in = a->scale_input_act;
+        sc.s_gate = a->scale_gate_w;
+        sc.s_up = a->scale_up_w;
+        sc.s_mid = a->scale_mid_act;
+        sc.s_down = a->scale_down_w;
+    }
+    void* a_rows = i8 ? (void*)a->per_expert_wmma_inputs_int8 : (void*)a->per_expert_wmma_inputs;
+    void* h_rows = i8 ? (void*)a->hidden_mlp_layer_1_out_int8 : (void*)a->hidden_mlp_layer_1_out_fp16;
+    const void* wg = i8 ? (const void*)a->expert_gate_proj_weights_int8 : (const void*)a->expert_gate_proj_weights;
+    const void* wu = i8 ? (const void*)a->expert_up_proj_weights_int8 : (const void*)a->expert_up_proj_weights;
+    const void* wd = i8 ? (const void*)a->expert_down_proj_weights_int8 : (const void*)a->expert_down_proj_weights;
+    e = launch_dispatch(a->input, a->selected_expert_indices, a->selected_expert_weights, s, ws, sc,
+                        a->expert_counts, a->expert_token_ids, a->expert_token_weights, a_rows, stream);
     if (e != cudaSuccess) return cuda_fail(e, "dispatch");
     if ((e = mark(2)) != cudaSuccess) return cuda_fail(e, "cudaEventRecord(stage event)");
     if (s.T() > 0 && s.cap > 0) {
-        e = launch_expert_up_gate(a->per_expert_wmma_inputs, a->expert_gate_proj_weights,
-                                  a->expert_up_proj_weights, s, ws, a->hidden_mlp_layer_1_out_fp16, stream,
-                                  num_sms);
+        e = launch_expert_up_gate(a_rows, wg, wu, s, ws, sc, h_rows, stream, num_sms);
         if (e != cudaSuccess) return cuda_fail(e, "expert up/gate GEMM");
         if ((e = mark(3)) != cudaSuccess) return cuda_fail(e, "cudaEventRecord(stage event)");
-        e = launch_expert_down(a->hidden_mlp_layer_1_out_fp16, a->expert_down_proj_weights, s, ws,
-                               a->hidden_mlp_layer_2_out, stream, num_sms);
+        e = launch_expert_down(h_rows, wd, s, ws, sc, a->hidden_mlp_layer_2_out, stream, num_sms);
         if (e != cudaSuccess) return cuda_fail(e, "expert down GEMM");
     } else {
         if ((e = mark(3)) != cudaSuccess) return cuda_fail(e, "cudaEventRecord(stage event)");
@@ -295,7 +319,7 @@ extern "C" int moe_solve_v2(const MoEArgs* a, const MoeDims* dims, cudaStream_t 
     Shape s;
     int rc = make_shape(dims, &s);
     if (rc != MOE_OK) return rc;
-    rc = check_args_16(a);
+    rc = check_args(a, s.dtype);
     if (rc != MOE_OK) return rc;
     DeviceState* st = nullptr;
     int dev = 0;
@@ -360,8 +384,14 @@ extern "C" void solve(MoEArgs args) {
         fprintf(stderr, "CUDA Error at: %s: %s \n", what, moe_last_error());
         exit(1);
     };
-    if (!args.expert_up_proj_weights) {
-        set_error("only the 16-bit (capacity) weight format is implemented by solve()");
+    // The reference picks the kernel at build time (Makefile KERNEL=); here the
+    // weight format the builder filled in picks the path.
+    if (args.expert_up_proj_weights) {
+        if (dims.dtype == MOE_DTYPE_INT8) dims.dtype = MOE_DTYPE_F16;
+    } else if (args.expert_up_proj_weights_int8 && !args.expert_up_proj_weights_int4) {
+        dims.dtype = MOE_DTYPE_INT8;
+    } else {
+        set_error("solve(): no kernel for this weight format (int4 / fp8 MoEArgs fields)");
         die("solve");
     }
     cudaEvent_t start, stop;

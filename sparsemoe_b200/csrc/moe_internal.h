@@ -18,6 +18,7 @@ struct Shape {
     int B, N, d, f, E, k, cap;
     int dtype;         // MOE_DTYPE_*
     int router_dtype;  // MOE_ROUTER_*
+    bool act_bf16;     // x (and the 16-bit output copy) are bf16 rather than f16
     int64_t T() const { return (int64_t)B * N; }
     int chunks() const { return (int)(((int64_t)N * k + kChunkRoutes - 1) / kChunkRoutes); }
     int64_t rows_per_expert() const { return (int64_t)B * cap; }  // row stride of one expert
@@ -35,19 +36,26 @@ struct Workspace {
 size_t workspace_bytes(const Shape& s);
 void carve_workspace(void* base, const Shape& s, Workspace* ws);
 
+// Per-tensor scales of the int8 path (MoEArgs scale_* fields).
+struct GemmScales {
+    float s_in = 1.0f, s_gate = 1.0f, s_up = 1.0f, s_mid = 1.0f, s_down = 1.0f;
+};
+
 // router.cu: logits (+bias), warp-shuffle top-k, softmax.
 cudaError_t launch_router_topk(const void* x, const void* wr, const float* bias, const Shape& s,
                                float* logits, int* idx, float* w, cudaStream_t st);
 // dispatch.cu: deterministic capacity slots + 16-byte row gather.
+// a_rows receives 16-bit rows, or int8 rows quantised with 1/s_in (int8 path).
 cudaError_t launch_dispatch(const void* x, const int* idx, const float* w, const Shape& s,
-                            const Workspace& ws, int* counts, int* token_ids,
+                            const Workspace& ws, const GemmScales& sc, int* counts, int* token_ids,
                             float* token_weights, void* a_rows, cudaStream_t st);
 // expert_gemm.cu: grouped tcgen05 GEMMs.
 cudaError_t launch_expert_up_gate(const void* a_rows, const void* w_gate, const void* w_up,
-                                  const Shape& s, const Workspace& ws, void* h_rows,
-                                  cudaStream_t st, int num_sms);
+                                  const Shape& s, const Workspace& ws, const GemmScales& sc,
+                                  void* h_rows, cudaStream_t st, int num_sms);
 cudaError_t launch_expert_down(const void* h_rows, const void* w_down, const Shape& s,
-                               const Workspace& ws, float* y_rows, cudaStream_t st, int num_sms);
+                               const Workspace& ws, const GemmScales& sc, float* y_rows,
+                               cudaStream_t st, int num_sms);
 // combine.cu: gate-weighted gather-sum into [B, N, d].
 cudaError_t launch_combine(const float* y_rows, const int* idx, const float* w, const Shape& s,
                            const Workspace& ws, float* out, void* out16, cudaStream_t st);
@@ -57,6 +65,7 @@ void set_error(const char* fmt, ...);
 // moe.cu: shared pieces of the layer entry points.
 int make_shape_checked(const MoeDims* dims, Shape* s);
 int check_args_16(const MoEArgs* a);
+int check_args(const MoEArgs* a, int dtype);
 int current_device(int* dev, int* num_sms);           // sm_100 check, cached SM count
 void note_status_word(int dev, int* status);            // read by moe_check_device_status
 int enqueue_layer(const MoEArgs* a, const MoeDims* dims, const Shape& s, const Workspace& ws, int num_sms,

@@ -67,7 +67,7 @@ extern "C" int moe_solve_v2_noalloc(const MoEArgs* a, const MoeDims* dims, cudaS
     Shape s;
     int rc = make_shape_checked(dims, &s);
     if (rc != MOE_OK) return rc;
-    rc = check_args_16(a);
+    rc = check_args(a, s.dtype);
     if (rc != MOE_OK) return rc;
     const size_t need = workspace_bytes(s);
     if (need > kNoAllocScratchBytes) {

@@ -176,7 +176,7 @@ cudaError_t launch_typed(const void* x, const void* wr, const float* bias, const
 cudaError_t launch_router_topk(const void* x, const void* wr, const float* bias, const Shape& s,
                                float* logits, int* idx, float* w, cudaStream_t st) {
     if (s.T() == 0) return cudaSuccess;
-    const bool bf = s.dtype == MOE_DTYPE_BF16;
+    const bool bf = s.act_bf16;
     if (s.router_dtype == MOE_ROUTER_F32) {
         return bf ? launch_typed<__nv_bfloat16, float>(x, wr, bias, s, logits, idx, w, st)
                   : launch_typed<__half, float>(x, wr, bias, s, logits, idx, w, st);

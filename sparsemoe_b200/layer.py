@@ -32,9 +32,11 @@ class MoeLayer:
         z = lambda *s, dt: torch.empty(*s, dtype=dt, device=dev)  # noqa: E731
         self.x = z(max(T, 1), d, dt=t16)
         self.wr = z(d, E, dt=torch.float32 if cfg.router_f32 else t16)
-        self.wg = z(E, d, f, dt=t16)
-        self.wu = z(E, d, f, dt=t16)
-        self.wd = z(E, f, d, dt=t16)
+        wt = torch.int8 if cfg.int8 else t16
+        self.wg = z(E, d, f, dt=wt)
+        self.wu = z(E, d, f, dt=wt)
+        self.wd = z(E, f, d, dt=wt)
+        self.scales = {}
         self.bias = None
         self.logits = z(max(T, 1), E, dt=torch.float32) if want_logits else None
         self.idx = z(max(T, 1), k, dt=torch.int32)
@@ -42,8 +44,8 @@ class MoeLayer:
         self.counts = z(max(B, 1), E, dt=torch.int32)
         self.token_ids = z(rows, dt=torch.int32)
         self.token_weights = z(rows, dt=torch.float32)
-        self.a_rows = z(rows, d, dt=t16)
-        self.h_rows = z(rows, f, dt=t16)
+        self.a_rows = z(rows, d, dt=wt)
+        self.h_rows = z(rows, f, dt=wt)
         self.y_rows = z(rows, d, dt=torch.float32)
         self.out = z(max(T, 1), d, dt=torch.float32)
         self.out16 = z(max(T, 1), d, dt=t16) if want_out16 else None
@@ -61,9 +63,12 @@ class MoeLayer:
         if self.cfg.T > 0:
             put(self.x, inputs["x"])
         put(self.wr, inputs["wr"])
-        put(self.wg, inputs["wg"])
-        put(self.wu, inputs["wu"])
-        put(self.wd, inputs["wd"])
+        sfx = "_q" if self.cfg.int8 else ""
+        put(self.wg, inputs["wg" + sfx])
+        put(self.wu, inputs["wu" + sfx])
+        put(self.wd, inputs["wd" + sfx])
+        if self.cfg.int8:
+            self.scales = {k: inputs[k] for k in ("s_in", "s_gate", "s_up", "s_mid", "s_down")}
         if inputs.get("bias") is not None:
             self.bias = torch.from_numpy(inputs["bias"]).to(self.device)
         return self
@@ -74,17 +79,27 @@ class MoeLayer:
         p = lambda t: None if t is None else t.data_ptr()  # noqa: E731
         a.input = p(self.x)
         a.router_weights = p(self.wr)
-        a.expert_up_proj_weights = p(self.wu)
-        a.expert_gate_proj_weights = p(self.wg)
-        a.expert_down_proj_weights = p(self.wd)
+        if self.cfg.int8:
+            a.expert_up_proj_weights_int8 = p(self.wu)
+            a.expert_gate_proj_weights_int8 = p(self.wg)
+            a.expert_down_proj_weights_int8 = p(self.wd)
+            a.per_expert_wmma_inputs_int8 = p(self.a_rows)
+            a.hidden_mlp_layer_1_out_int8 = p(self.h_rows)
+            sc = self.scales
+            a.scale_input_act, a.scale_gate_w, a.scale_up_w = sc["s_in"], sc["s_gate"], sc["s_up"]
+            a.scale_mid_act, a.scale_down_w = sc["s_mid"], sc["s_down"]
+        else:
+            a.expert_up_proj_weights = p(self.wu)
+            a.expert_gate_proj_weights = p(self.wg)
+            a.expert_down_proj_weights = p(self.wd)
+            a.per_expert_wmma_inputs = p(self.a_rows)
+            a.hidden_mlp_layer_1_out_fp16 = p(self.h_rows)
         a.expert_logits = p(self.logits)
         a.selected_expert_indices = p(self.idx)
         a.selected_expert_weights = p(self.w)
         a.expert_counts = p(self.counts)
         a.expert_token_ids = p(self.token_ids)
         a.expert_token_weights = p(self.token_weights)
-        a.per_expert_wmma_inputs = p(self.a_rows)
-        a.hidden_mlp_layer_1_out_fp16 = p(self.h_rows)
         a.hidden_mlp_layer_2_out = p(self.y_rows)
         a.final_output = p(self.out)
         a.num_batches = self.cfg.num_batches
