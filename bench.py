@@ -218,6 +218,93 @@ def run_reference_arm(args, ws, rank, local):
 
 
 # ---------------------------------------------------------------------------
+def run_ep(args, cfg, ws, rank, local, dev):
+    """Expert parallelism: every rank holds E/P experts and routes its own T
+    tokens (weak scaling); rows cross NVLink twice per layer (NCCL all-to-all)."""
+    import torch
+    import torch.distributed as dist
+    from sparsemoe_b200.ep import ExpertParallelLayer
+    layer = ExpertParallelLayer(cfg, dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(1000 + rank)
+    layer.x.normal_(0.0, 1.0, generator=g)
+    g.manual_seed(7)                                   # router replicated on every rank
+    layer.wr.normal_(0.0, 0.02, generator=g)
+    g.manual_seed(2000 + rank)                         # this rank's experts
+    for t, std in ((layer.wg, cfg.d_model ** -0.5), (layer.wu, cfg.d_model ** -0.5), (layer.wd, cfg.d_ff ** -0.5)):
+        t.normal_(0.0, std, generator=g)
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(args.warmup):
+        layer.forward(stream)
+    layer.sync_check(stream)
+    K = args.steps
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(6)] for _ in range(K)]
+    owner_rows = []
+    torch.cuda.synchronize(dev)
+    barrier(ws)
+    torch.cuda.synchronize(dev)
+    with ClockSampler(local) as clocks:
+        for i in range(K):
+            layer.forward(stream, events=evs[i])
+            owner_rows.append(layer.last_plan["owner_rows"])
+        torch.cuda.synchronize(dev)
+    barrier(ws)
+    ms_local = statistics.mean(evs[i][0].elapsed_time(evs[i][5]) for i in range(K))
+    ms = max_over_ranks(ms_local, ws, dev)
+    phase_ms = {name: statistics.mean(evs[i][j].elapsed_time(evs[i][j + 1]) for i in range(K))
+                for j, name in enumerate(layer.PHASES)}
+    layer.sync_check(stream)
+    # end-to-end: host x in, 16-bit output out, per step
+    x_host = torch.empty_like(layer.x, device="cpu").pin_memory()
+    x_host.copy_(layer.x)
+    out_host = torch.empty_like(layer.out16, device="cpu").pin_memory()
+    for _ in range(args.warmup):
+        layer.x.copy_(x_host, non_blocking=True)
+        layer.forward(stream)
+        out_host.copy_(layer.out16, non_blocking=True)
+    torch.cuda.synchronize(dev)
+    barrier(ws)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(K):
+        layer.x.copy_(x_host, non_blocking=True)
+        layer.forward(stream)
+        out_host.copy_(layer.out16, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier(ws)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / K, ws, dev)
+    peaks, peak_src = load_peaks()
+    peak_tf = float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
+    flop_ffn = 6.0 * cfg.d_model * cfg.d_ff * statistics.mean(owner_rows)
+    ach = flop_ffn / (phase_ms["expert_ffn"] * 1e-3) / 1e12
+    ach_min = max_over_ranks(-ach, ws, dev) * -1.0      # slowest rank
+    h2d = x_host.numel() * x_host.element_size()
+    d2h = out_host.numel() * out_host.element_size()
+    result = {
+        "metric": f"MoE-layer tokens/s ({args.config})", "value": ws * cfg.T / (ms * 1e-3), "unit": "tokens/s",
+        "n_gpus": ws, "steps": K, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16" if cfg.bf16 else ("int8" if cfg.int8 else "f16"),
+        "data": "synthetic (seeded torch normal: x N(0,1), router N(0,0.02), W N(0,1/sqrt(fan_in)))",
+        "config": {**cfg_json(args.config, cfg, layer.cap),
+                   "parallelism": f"ep{ws} (expert parallel, {cfg.num_experts // ws} experts per GPU, "
+                                  f"NCCL all-to-all dispatch/return; {cfg.T} tokens per GPU)"},
+        "roofline": {"bound": "tensor", "achieved": ach_min, "peak": peak_tf, "unit": "TFLOP/s",
+                     "frac": ach_min / peak_tf, "traffic": None,
+                     "kernel": "expert_ffn phase (up/gate + down tcgen05 GEMMs), slowest rank",
+                     "peak_source": f"{peak_src} bf16_tflops_sustained"},
+        "phases_ms": phase_ms,
+        "e2e": {"value": ws * cfg.T / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
+                "path": "ExpertParallelLayer.forward (moe_stage_route / moe_stage_expert_ffn / moe_stage_combine)"},
+        "gpu_launches": KERNELS_PER_STEP * K,
+        "clocks": clocks.summary(),
+    }
+    if rank == 0:
+        print(json.dumps(result))
+    dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -228,6 +315,8 @@ def main():
     ap.add_argument("--cpu-sample-tokens", type=int, default=1024)
     ap.add_argument("--ref-sample-tokens", type=int, default=128)
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline measurement")
+    ap.add_argument("--parallel", default="auto", choices=["auto", "ep", "replicas"],
+                    help="N>1: expert parallelism over NCCL (default) or independent replicas")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -241,6 +330,10 @@ def main():
     torch.cuda.set_device(local)
     dev = torch.device(f"cuda:{local}")
     cfg = workload(args.config)
+    mode = args.parallel if args.parallel != "auto" else ("ep" if ws > 1 else "single")
+    if ws > 1 and mode == "ep":
+        run_ep(args, cfg, ws, rank, local, dev)
+        return
     layer = sm.MoeLayer(cfg, dev, want_logits=True, want_out16=True)
     device_inputs(layer, seed=1000 + rank)
     stream = torch.cuda.current_stream(dev)

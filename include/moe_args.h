@@ -17,14 +17,15 @@
 //   expert_counts                 [B, E]                    i32, min(routes, CAP)
 //   expert_token_ids              [B, E, CAP]               i32
 //   expert_token_weights          [B, E, CAP]               f32
-//   per_expert_wmma_inputs        [E, B*CAP, d]  expert-major, compacted rows
-//   hidden_mlp_layer_1_out_fp16   [E, B*CAP, f]  SwiGLU output (same layout)
-//   hidden_mlp_layer_2_out        [E, B*CAP, d]  f32 down-projection output
+//   per_expert_wmma_inputs        [B*E*CAP, d]  kept rows, dense expert-major
+//   hidden_mlp_layer_1_out_fp16   [B*E*CAP, f]  SwiGLU output (same rows)
+//   hidden_mlp_layer_2_out        [B*E*CAP, d]  f32 down-projection output
 //   final_output                  [B, N, d]                 f32
 // The three per-expert scratch buffers have the reference's byte size
-// (B*E*CAP rows) but hold the kept rows of expert e contiguously starting at
-// row e*B*CAP (batch 0's kept slots, then batch 1's, ...), so one expert is
-// one contiguous GEMM operand.  hidden_mlp_layer_1_out / hidden_mlp_gate_out
+// (B*E*CAP rows) but hold only the kept rows, expert by expert: expert e's
+// rows start after all kept rows of experts < e, batch 0's slots first, so
+// one expert is one contiguous GEMM operand (the int8 path uses the *_int8
+// fields the same way).  hidden_mlp_layer_1_out / hidden_mlp_gate_out
 // (f32 up/gate) are not used: SwiGLU is fused into the up/gate GEMM epilogue.
 #pragma once
 

@@ -72,6 +72,28 @@ int moe_solve_v2(const struct MoEArgs* args, const MoeDims* dims, cudaStream_t s
 int moe_solve_v2_noalloc(const struct MoEArgs* args, const MoeDims* dims, cudaStream_t stream);
 size_t moe_noalloc_scratch_bytes(void);
 
+// ---- expert-parallel building blocks (no reference counterpart: the reference
+//      is single-GPU).  One layer call = moe_stage_route -> (exchange rows) ->
+//      moe_stage_expert_ffn on the owner -> (exchange rows back) ->
+//      moe_stage_combine, with the same dims for route and combine, on one
+//      device and host thread.
+// Router, top-k, capacity slots (kept iff slot < CAP, route-id order within a
+// batch) and the gather of the kept token rows into per_expert_wmma_inputs in
+// the dense expert-major layout: expert e's rows start at
+// sum_{e'<e} sum_b expert_counts[b, e'], batch 0's slots first.
+int moe_stage_route(const struct MoEArgs* args, const MoeDims* dims, cudaStream_t stream);
+// SwiGLU FFN over row groups: group g has group_rows[g] rows starting at row
+// group_start[g] of per_expert_wmma_inputs (A), hidden_mlp_layer_1_out_fp16
+// (H) and hidden_mlp_layer_2_out (Y, f32), all with rows_capacity rows, and
+// uses expert group_expert[g] (NULL: g) of the dims.num_experts experts whose
+// weights args holds.  The three arrays are host memory (copied on `stream`).
+int moe_stage_expert_ffn(const struct MoEArgs* args, const MoeDims* dims, const int* group_rows,
+                         const int* group_start, const int* group_expert, int num_groups,
+                         int64_t rows_capacity, cudaStream_t stream);
+// Combine: final_output[t] = sum over kept routes in route order of
+// w * Y[row], Y = hidden_mlp_layer_2_out in the layout moe_stage_route made.
+int moe_stage_combine(const struct MoEArgs* args, const MoeDims* dims, cudaStream_t stream);
+
 // Synchronises `stream` and reports a device-side failure (MOE_ERR_TIMEOUT) of
 // the last moe_solve_v2 on this device, MOE_OK otherwise.
 int moe_check_device_status(cudaStream_t stream);

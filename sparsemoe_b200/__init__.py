@@ -93,6 +93,10 @@ def _load() -> ctypes.CDLL:
         "moe_capacity": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float]),
         "moe_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(MoeDims)]),
         "moe_release": (None, []),
+        "moe_stage_route": (ctypes.c_int, [ctypes.POINTER(MoEArgs), ctypes.POINTER(MoeDims), _p]),
+        "moe_stage_expert_ffn": (ctypes.c_int, [ctypes.POINTER(MoEArgs), ctypes.POINTER(MoeDims), _p, _p, _p,
+                                                ctypes.c_int, ctypes.c_int64, _p]),
+        "moe_stage_combine": (ctypes.c_int, [ctypes.POINTER(MoEArgs), ctypes.POINTER(MoeDims), _p]),
         "moe_solve_v2_noalloc": (ctypes.c_int, [ctypes.POINTER(MoEArgs), ctypes.POINTER(MoeDims), _p]),
         "moe_noalloc_scratch_bytes": (ctypes.c_size_t, []),
         "moe_set_stage_events": (ctypes.c_int, [ctypes.POINTER(ctypes.c_void_p), ctypes.c_int]),

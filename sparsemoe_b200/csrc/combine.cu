@@ -19,8 +19,8 @@ constexpr int kThreads = 256;
 template <typename T16>
 __global__ void __launch_bounds__(kThreads) combine_kernel(
     const float* __restrict__ y_rows, const int* __restrict__ idx, const float* __restrict__ w,
-    const int* __restrict__ route_slot, const int* __restrict__ row_base, int N, int d, int E, int k,
-    int64_t rows_per_expert, float* __restrict__ out, T16* __restrict__ out16) {
+    const int* __restrict__ route_slot, const int* __restrict__ row_base, const int* __restrict__ expert_start,
+    int N, int d, int E, int k, float* __restrict__ out, T16* __restrict__ out16) {
     __shared__ int64_t s_row[32];
     __shared__ float s_w[32];
     const int64_t t = blockIdx.x;  // flattened token b*N + n
@@ -31,7 +31,7 @@ __global__ void __launch_bounds__(kThreads) combine_kernel(
         int64_t row = -1;
         if (slot >= 0) {
             const int e = idx[r];
-            row = (int64_t)e * rows_per_expert + row_base[b * E + e] + slot;
+            row = (int64_t)expert_start[e] + row_base[b * E + e] + slot;
         }
         s_row[threadIdx.x] = row;
         s_w[threadIdx.x] = w[r];
@@ -67,11 +67,11 @@ cudaError_t launch_combine(const float* y_rows, const int* idx, const float* w, 
     if (s.T() == 0) return cudaSuccess;
     if (s.act_bf16)
         combine_kernel<__nv_bfloat16><<<(unsigned)s.T(), kThreads, 0, st>>>(
-            y_rows, idx, w, ws.route_slot, ws.row_base, s.N, s.d, s.E, s.k, s.rows_per_expert(), out,
+            y_rows, idx, w, ws.route_slot, ws.row_base, ws.expert_start, s.N, s.d, s.E, s.k, out,
             (__nv_bfloat16*)out16);
     else
         combine_kernel<__half><<<(unsigned)s.T(), kThreads, 0, st>>>(
-            y_rows, idx, w, ws.route_slot, ws.row_base, s.N, s.d, s.E, s.k, s.rows_per_expert(), out,
+            y_rows, idx, w, ws.route_slot, ws.row_base, ws.expert_start, s.N, s.d, s.E, s.k, out,
             (__half*)out16);
     return cudaGetLastError();
 }

@@ -18,7 +18,10 @@
 //                             expert's compact block with 16-byte vector
 //                             loads/stores (HBM-bound: R_kept*d*2 B read and
 //                             written).
-// Rows of expert e: [e*B*CAP + row_base[b,e], + counts[b,e]) for batch b.
+// Dense expert-major row layout: expert e's kept rows start at
+// expert_start[e] = sum of the kept rows of experts < e; within it batch b's
+// slots start at row_base[b,e].  Row of (b, e, slot) = expert_start[e] +
+// row_base[b,e] + slot.
 #include "moe_internal.h"
 #include <cstdint>
 #include <cuda_fp16.h>
@@ -56,10 +59,12 @@ __global__ void __launch_bounds__(256) dispatch_scan_kernel(const int* __restric
                                                             int* __restrict__ chunk_base,
                                                             int* __restrict__ counts,
                                                             int* __restrict__ row_base,
-                                                            int* __restrict__ expert_rows) {
+                                                            int* __restrict__ expert_rows,
+                                                            int* __restrict__ expert_start) {
+    __shared__ int s_rows[256];
     const int e = threadIdx.x;
-    if (e >= E) return;
     int rows = 0;
+    if (e < E) {
     for (int b = 0; b < B; ++b) {
         int run = 0;
         for (int c = 0; c < chunks; ++c) {
@@ -73,6 +78,13 @@ __global__ void __launch_bounds__(256) dispatch_scan_kernel(const int* __restric
         rows += kept;
     }
     expert_rows[e] = rows;
+    s_rows[e] = rows;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int acc = 0;
+        for (int q = 0; q < E; ++q) { expert_start[q] = acc; acc += s_rows[q]; }
+    }
 }
 
 __global__ void __launch_bounds__(kThreads) dispatch_assign_kernel(
@@ -134,8 +146,8 @@ __global__ void __launch_bounds__(kThreads) dispatch_assign_kernel(
 // expert's count are skipped.
 __global__ void __launch_bounds__(kThreads) dispatch_gather_kernel(
     const uint4* __restrict__ x, const int* __restrict__ counts, const int* __restrict__ token_ids,
-    const int* __restrict__ row_base, int N, int E, int B, int cap, int vec_per_row,
-    uint4* __restrict__ a_rows) {
+    const int* __restrict__ row_base, const int* __restrict__ expert_start, int N, int E, int B, int cap,
+    int vec_per_row, uint4* __restrict__ a_rows) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t slot_lin = (int64_t)blockIdx.x * kWarps + warp;
     if (slot_lin >= (int64_t)B * E * cap) return;
@@ -145,7 +157,7 @@ __global__ void __launch_bounds__(kThreads) dispatch_gather_kernel(
     const int b = be / E, e = be - b * E;
     const int64_t t = token_ids[slot_lin];
     const uint4* src = x + ((int64_t)b * N + t) * vec_per_row;
-    uint4* dst = a_rows + ((int64_t)e * B * cap + row_base[be] + s) * vec_per_row;
+    uint4* dst = a_rows + ((int64_t)expert_start[e] + row_base[be] + s) * vec_per_row;
     int v = lane;
     for (; v + 96 < vec_per_row; v += 128) {
         const uint4 a0 = __ldg(src + v), a1 = __ldg(src + v + 32), a2 = __ldg(src + v + 64),
@@ -162,8 +174,8 @@ __global__ void __launch_bounds__(kThreads) dispatch_gather_kernel(
 // quantised as rn(clamp(x / s_in, -128, 127)), 8 values per 16-byte load.
 __global__ void __launch_bounds__(kThreads) dispatch_gather_q8_kernel(
     const uint4* __restrict__ x, const int* __restrict__ counts, const int* __restrict__ token_ids,
-    const int* __restrict__ row_base, int N, int E, int B, int cap, int vec_per_row, float s_in,
-    uint2* __restrict__ a_rows) {
+    const int* __restrict__ row_base, const int* __restrict__ expert_start, int N, int E, int B, int cap,
+    int vec_per_row, float s_in, uint2* __restrict__ a_rows) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t slot_lin = (int64_t)blockIdx.x * kWarps + warp;
     if (slot_lin >= (int64_t)B * E * cap) return;
@@ -173,7 +185,7 @@ __global__ void __launch_bounds__(kThreads) dispatch_gather_q8_kernel(
     const int b = be / E, e = be - b * E;
     const int64_t t = token_ids[slot_lin];
     const uint4* src = x + ((int64_t)b * N + t) * vec_per_row;
-    uint2* dst = a_rows + ((int64_t)e * B * cap + row_base[be] + s) * vec_per_row;
+    uint2* dst = a_rows + ((int64_t)expert_start[e] + row_base[be] + s) * vec_per_row;
     for (int v = lane; v < vec_per_row; v += 32) {
         const uint4 raw = __ldg(src + v);
         const __half2* h2 = reinterpret_cast<const __half2*>(&raw);
@@ -196,13 +208,14 @@ cudaError_t launch_dispatch(const void* x, const int* idx, const float* w, const
                             float* token_weights, void* a_rows, cudaStream_t st) {
     if (s.T() == 0) {
         cudaError_t e = cudaMemsetAsync(ws.expert_rows, 0, sizeof(int) * s.E, st);
+        if (e == cudaSuccess) e = cudaMemsetAsync(ws.expert_start, 0, sizeof(int) * s.E, st);
         if (e == cudaSuccess && s.B > 0) e = cudaMemsetAsync(counts, 0, sizeof(int) * s.B * s.E, st);
         return e;
     }
     const dim3 grid(s.chunks(), s.B);
     dispatch_count_kernel<<<grid, kThreads, 0, st>>>(idx, s.N, s.k, s.E, s.chunks(), ws.chunk_count);
     dispatch_scan_kernel<<<1, 256, 0, st>>>(ws.chunk_count, s.B, s.E, s.chunks(), s.cap,
-                                            ws.chunk_base, counts, ws.row_base, ws.expert_rows);
+                                            ws.chunk_base, counts, ws.row_base, ws.expert_rows, ws.expert_start);
     dispatch_assign_kernel<<<grid, kThreads, 0, st>>>(idx, w, s.N, s.k, s.E, s.cap, s.chunks(), ws.chunk_base,
                                                       token_ids, token_weights, ws.route_slot);
     // 16-bit activations: rows of d elements = d/8 16-byte vectors.
@@ -210,11 +223,12 @@ cudaError_t launch_dispatch(const void* x, const int* idx, const float* w, const
     const unsigned gblocks = (unsigned)((slots + kWarps - 1) / kWarps);
     if (slots > 0 && s.dtype == MOE_DTYPE_INT8)
         dispatch_gather_q8_kernel<<<gblocks, kThreads, 0, st>>>((const uint4*)x, counts, token_ids, ws.row_base,
-                                                                s.N, s.E, s.B, s.cap, s.d / 8, sc.s_in,
-                                                                (uint2*)a_rows);
+                                                                ws.expert_start, s.N, s.E, s.B, s.cap, s.d / 8,
+                                                                sc.s_in, (uint2*)a_rows);
     else if (slots > 0)
         dispatch_gather_kernel<<<gblocks, kThreads, 0, st>>>((const uint4*)x, counts, token_ids, ws.row_base,
-                                                             s.N, s.E, s.B, s.cap, s.d / 8, (uint4*)a_rows);
+                                                             ws.expert_start, s.N, s.E, s.B, s.cap, s.d / 8,
+                                                             (uint4*)a_rows);
     return cudaGetLastError();
 }
 

@@ -29,10 +29,11 @@
 // The operand format is a trait (Fmt16 / FmtI8): both keep 128-byte swizzle
 // rows, so only the K block (64 vs 128 elements), the B chunk width (64 vs
 // 128 columns), the MMA kind and the epilogue arithmetic differ.
-// Tiles: expert e owns ceil(rows_e / 128) M-tiles (rows_e = kept routes of e,
-// from the dispatch stage, read on the device -- empty capacity slots cost no
-// MMA work); tile order is expert-major, then N-tile, then M-tile, so the CTAs
-// in flight share one expert's weights and activations in L2.
+// Tiles: a row group (an expert's kept rows on one GPU; a (sender, expert)
+// block under expert parallelism) owns ceil(rows / 128) M-tiles, with the row
+// counts read on the device -- empty capacity slots cost no MMA work.  Tile
+// order is group-major, then N-tile, then M-tile, so the CTAs in flight share
+// one expert's weights and activations in L2.
 #include "moe_internal.h"
 #include "common.cuh"
 #include "sm100.cuh"
@@ -55,13 +56,13 @@ constexpr int kBBytes = 128 * kUmmaN;               // 32 KB: 128 bytes of K row
 constexpr int kStageBytes = kABytes + kBBytes;
 constexpr int kAccCols = kUmmaN;
 constexpr int kTmemCols = 2 * kAccCols;
-constexpr int kMaxExperts = 256;
 constexpr size_t kSmemBytes = 1024 + (size_t)kStages * kStageBytes + 256;
 
 struct GemmParams {
-    const int* expert_rows;  // [E] kept rows per expert
-    int E;
-    int rows_per_expert;     // row stride of one expert in A and in the output (B*CAP)
+    const int* g_rows;       // [G] rows of each group
+    const int* g_start;      // [G] first row of each group in A and in the output
+    const int* g_weight;     // [G] expert weight index of each group (null: g)
+    int G;
     int K;                   // reduction length (d for up/gate, f for down)
     int n_tiles;             // output tiles along N per expert
     int out_ld;              // output row length in elements (f or d)
@@ -147,9 +148,9 @@ struct FmtI8 {
     }
 };
 
-__device__ __forceinline__ void decode_tile(int t, const int* pre, const int* mt, int E, int& e,
+__device__ __forceinline__ void decode_tile(int t, const int* pre, const int* mt, int G, int& e,
                                             int& m, int& n) {
-    int lo = 0, hi = E - 1;
+    int lo = 0, hi = G - 1;
     while (lo < hi) {
         const int mid = (lo + hi + 1) >> 1;
         if (pre[mid] <= t) lo = mid; else hi = mid - 1;
@@ -171,9 +172,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr int kKSteps = kBK / Fmt::kUmmaK;        // MMAs per stage
     constexpr int kOutN = kMode == 0 ? 128 : 256;     // output columns per tile
     extern __shared__ uint8_t smem_raw[];
-    __shared__ int s_pre[kMaxExperts + 1];
-    __shared__ int s_mt[kMaxExperts];
-    __shared__ int s_rows[kMaxExperts];
+    __shared__ int s_pre[kMaxGroups + 1];
+    __shared__ int s_mt[kMaxGroups];
+    __shared__ int s_rows[kMaxGroups];
+    __shared__ int s_start[kMaxGroups];
+    __shared__ int s_wt[kMaxGroups];
 
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sA = smem;
@@ -198,22 +201,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_alloc(tmem_slot, kTmemCols);
         tmem_relinquish();
     }
-    for (int e = threadIdx.x; e < p.E; e += kThreads) {
-        const int r = p.expert_rows[e];
-        s_rows[e] = r;
-        s_mt[e] = (r + kBM - 1) / kBM;
+    for (int g = threadIdx.x; g < p.G; g += kThreads) {
+        const int r = p.g_rows[g];
+        s_rows[g] = r;
+        s_mt[g] = (r + kBM - 1) / kBM;
+        s_start[g] = p.g_start[g];
+        s_wt[g] = p.g_weight ? p.g_weight[g] : g;
     }
     __syncthreads();
     if (threadIdx.x == 0) {
         int acc = 0;
-        for (int e = 0; e < p.E; ++e) { s_pre[e] = acc; acc += s_mt[e] * p.n_tiles; }
-        s_pre[p.E] = acc;
+        for (int g = 0; g < p.G; ++g) { s_pre[g] = acc; acc += s_mt[g] * p.n_tiles; }
+        s_pre[p.G] = acc;
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
-    const int total = s_pre[p.E];
+    const int total = s_pre[p.G];
     const int kblocks = p.K / kBK;
 
     if (warp == 0) {
@@ -223,9 +228,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t ph = 0;
             for (int t = blockIdx.x; t < total; t += gridDim.x) {
                 int e, m, n;
-                decode_tile(t, s_pre, s_mt, p.E, e, m, n);
-                const int a_row = e * p.rows_per_expert + m * kBM;
-                const int b_row = e * p.K;
+                decode_tile(t, s_pre, s_mt, p.G, e, m, n);
+                const int a_row = s_start[e] + m * kBM;
+                const int b_row = s_wt[e] * p.K;
                 for (int kb = 0; kb < kblocks; ++kb) {
                     if (!mbar_wait(&empty[s], ph ^ 1u, p.status, kDevErrTimeout)) goto producer_done;
                     mbar_arrive_expect_tx(&full[s], kStageBytes);
@@ -297,12 +302,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t aph = 0;
         for (int t = blockIdx.x; t < total; t += gridDim.x) {
             int e, m, n;
-            decode_tile(t, s_pre, s_mt, p.E, e, m, n);
+            decode_tile(t, s_pre, s_mt, p.G, e, m, n);
             if (!mbar_wait(&tfull[acc], aph, p.status, kDevErrTimeout)) break;
             tc_fence_after();
             const int row_local = m * kBM + row_in_tile;
             const bool valid = row_local < s_rows[e];
-            const int64_t out_row = (int64_t)e * p.rows_per_expert + row_local;
+            const int64_t out_row = (int64_t)s_start[e] + row_local;
             const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + acc * kAccCols;
             if (kMode == 0) {
                 uint8_t* h = reinterpret_cast<uint8_t*>(p.out) +
@@ -402,12 +407,13 @@ FmtDesc fmt_desc(int dtype) {
     }
 }
 
-GemmParams base_params(const Shape& s, const Workspace& ws, const GemmScales& sc) {
+GemmParams base_params(const GroupTable& gt, int* status, const GemmScales& sc) {
     GemmParams p{};
-    p.expert_rows = ws.expert_rows;
-    p.E = s.E;
-    p.rows_per_expert = (int)s.rows_per_expert();
-    p.status = ws.status;
+    p.g_rows = gt.rows;
+    p.g_start = gt.start;
+    p.g_weight = gt.weight;
+    p.G = gt.G;
+    p.status = status;
     p.deq_gate = sc.s_in * sc.s_gate;
     p.deq_up = sc.s_in * sc.s_up;
     p.inv_mid = 1.0f / sc.s_mid;
@@ -418,16 +424,17 @@ GemmParams base_params(const Shape& s, const Workspace& ws, const GemmScales& sc
 }  // namespace
 
 cudaError_t launch_expert_up_gate(const void* a_rows, const void* w_gate, const void* w_up, const Shape& s,
-                                  const Workspace& ws, const GemmScales& sc, void* h_rows, cudaStream_t st,
-                                  int num_sms) {
+                                  const GroupTable& gt, int* status, const GemmScales& sc, void* h_rows,
+                                  cudaStream_t st, int num_sms) {
+    if (gt.G <= 0 || gt.rows_capacity <= 0) return cudaSuccess;
     const FmtDesc fd = fmt_desc(s.dtype);
-    const uint64_t rows = (uint64_t)s.E * s.rows_per_expert();
+    const uint64_t rows = (uint64_t)gt.rows_capacity;
     CUtensorMap ta, tg, tu;
     if (!make_map(&ta, a_rows, fd.dt, fd.elem_bytes, s.d, rows, kBM) ||
         !make_map(&tg, w_gate, fd.dt, fd.elem_bytes, s.f, (uint64_t)s.E * s.d, fd.bk) ||
         !make_map(&tu, w_up, fd.dt, fd.elem_bytes, s.f, (uint64_t)s.E * s.d, fd.bk))
         return cudaErrorInvalidValue;
-    GemmParams p = base_params(s, ws, sc);
+    GemmParams p = base_params(gt, status, sc);
     p.K = s.d;
     p.n_tiles = s.f / 128;
     p.out_ld = s.f;
@@ -445,15 +452,16 @@ cudaError_t launch_expert_up_gate(const void* a_rows, const void* w_gate, const 
     }
 }
 
-cudaError_t launch_expert_down(const void* h_rows, const void* w_down, const Shape& s, const Workspace& ws,
-                               const GemmScales& sc, float* y_rows, cudaStream_t st, int num_sms) {
+cudaError_t launch_expert_down(const void* h_rows, const void* w_down, const Shape& s, const GroupTable& gt,
+                               int* status, const GemmScales& sc, float* y_rows, cudaStream_t st, int num_sms) {
+    if (gt.G <= 0 || gt.rows_capacity <= 0) return cudaSuccess;
     const FmtDesc fd = fmt_desc(s.dtype);
-    const uint64_t rows = (uint64_t)s.E * s.rows_per_expert();
+    const uint64_t rows = (uint64_t)gt.rows_capacity;
     CUtensorMap th, td;
     if (!make_map(&th, h_rows, fd.dt, fd.elem_bytes, s.f, rows, kBM) ||
         !make_map(&td, w_down, fd.dt, fd.elem_bytes, s.d, (uint64_t)s.E * s.f, fd.bk))
         return cudaErrorInvalidValue;
-    GemmParams p = base_params(s, ws, sc);
+    GemmParams p = base_params(gt, status, sc);
     p.K = s.f;
     p.n_tiles = s.d / 256;
     p.out_ld = s.d;

@@ -65,23 +65,29 @@ void set_error(const char* fmt, ...) {
     g_error = buf;
 }
 
+size_t workspace_header_bytes() { return 256 + 3 * align256(sizeof(int) * kMaxGroups); }
+
 size_t workspace_bytes(const Shape& s) {
     const size_t routes = (size_t)s.T() * s.k;
     const size_t chunk_tab = (size_t)s.B * s.chunks() * s.E;
-    return align256(sizeof(int) * routes) + 2 * align256(sizeof(int) * chunk_tab) +
-           align256(sizeof(int) * (size_t)s.B * s.E) + align256(sizeof(int) * s.E) + 256;
+    return workspace_header_bytes() + align256(sizeof(int) * routes) + 2 * align256(sizeof(int) * chunk_tab) +
+           align256(sizeof(int) * (size_t)s.B * s.E) + 2 * align256(sizeof(int) * s.E);
 }
 
 void carve_workspace(void* base, const Shape& s, Workspace* ws) {
     uint8_t* p = static_cast<uint8_t*>(base);
     const size_t routes = (size_t)s.T() * s.k;
     const size_t chunk_tab = (size_t)s.B * s.chunks() * s.E;
-    ws->route_slot = reinterpret_cast<int*>(p);  p += align256(sizeof(int) * routes);
-    ws->chunk_count = reinterpret_cast<int*>(p); p += align256(sizeof(int) * chunk_tab);
-    ws->chunk_base = reinterpret_cast<int*>(p);  p += align256(sizeof(int) * chunk_tab);
-    ws->row_base = reinterpret_cast<int*>(p);    p += align256(sizeof(int) * (size_t)s.B * s.E);
-    ws->expert_rows = reinterpret_cast<int*>(p); p += align256(sizeof(int) * s.E);
-    ws->status = reinterpret_cast<int*>(p);
+    ws->status = reinterpret_cast<int*>(p);       p += 256;
+    ws->grp_rows = reinterpret_cast<int*>(p);     p += align256(sizeof(int) * kMaxGroups);
+    ws->grp_start = reinterpret_cast<int*>(p);    p += align256(sizeof(int) * kMaxGroups);
+    ws->grp_weight = reinterpret_cast<int*>(p);   p += align256(sizeof(int) * kMaxGroups);
+    ws->route_slot = reinterpret_cast<int*>(p);   p += align256(sizeof(int) * routes);
+    ws->chunk_count = reinterpret_cast<int*>(p);  p += align256(sizeof(int) * chunk_tab);
+    ws->chunk_base = reinterpret_cast<int*>(p);   p += align256(sizeof(int) * chunk_tab);
+    ws->row_base = reinterpret_cast<int*>(p);     p += align256(sizeof(int) * (size_t)s.B * s.E);
+    ws->expert_rows = reinterpret_cast<int*>(p);  p += align256(sizeof(int) * s.E);
+    ws->expert_start = reinterpret_cast<int*>(p);
 }
 
 namespace {
@@ -166,8 +172,8 @@ int device_state(DeviceState** out, int* dev_out) {
     return MOE_OK;
 }
 
-int get_workspace(DeviceState& st, const Shape& s, Workspace* ws) {
-    const size_t need = workspace_bytes(s);
+int get_workspace(DeviceState& st, const Shape& s, Workspace* ws, bool header_only = false) {
+    const size_t need = header_only ? workspace_header_bytes() : workspace_bytes(s);
     if (st.ws_bytes < need) {
         if (st.ws) {
             cudaError_t e = cudaFree(st.ws);
@@ -264,52 +270,90 @@ void note_status_word(int dev, int* status) {
     if (dev >= 0 && dev < kMaxDevices) g_dev[dev].status = status;
 }
 
-// The stage sequence of one layer call on `stream`, given its scratch.
-int enqueue_layer(const MoEArgs* a, const MoeDims* dims, const Shape& s, const Workspace& ws, int num_sms,
-                  cudaStream_t stream) {
-    cudaError_t e = cudaMemsetAsync(ws.status, 0, sizeof(int), stream);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(status)");
-    auto mark = [&](int i) -> cudaError_t {
-        return g_stage_on ? cudaEventRecord(g_stage_ev[i], stream) : cudaSuccess;
-    };
-    if ((e = mark(0)) != cudaSuccess) return cuda_fail(e, "cudaEventRecord(stage event)");
-
-    e = launch_router_topk(a->input, a->router_weights, dims->router_bias, s, a->expert_logits,
-                           a->selected_expert_indices, a->selected_expert_weights, stream);
-    if (e != cudaSuccess) return cuda_fail(e, "router_topk");
-    if ((e = mark(1)) != cudaSuccess) return cuda_fail(e, "cudaEventRecord(stage event)");
-    const bool i8 = s.dtype == MOE_DTYPE_INT8;
+GemmScales scales_of(const MoEArgs* a, const Shape& s) {
     GemmScales sc;
-    if (i8) {
+    if (s.dtype == MOE_DTYPE_INT8) {
         sc.s_in = a->scale_input_act;
         sc.s_gate = a->scale_gate_w;
         sc.s_up = a->scale_up_w;
         sc.s_mid = a->scale_mid_act;
         sc.s_down = a->scale_down_w;
     }
-    void* a_rows = i8 ? (void*)a->per_expert_wmma_inputs_int8 : (void*)a->per_expert_wmma_inputs;
-    void* h_rows = i8 ? (void*)a->hidden_mlp_layer_1_out_int8 : (void*)a->hidden_mlp_layer_1_out_fp16;
-    const void* wg = i8 ? (const void*)a->expert_gate_proj_weights_int8 : (const void*)a->expert_gate_proj_weights;
-    const void* wu = i8 ? (const void*)a->expert_up_proj_weights_int8 : (const void*)a->expert_up_proj_weights;
-    const void* wd = i8 ? (const void*)a->expert_down_proj_weights_int8 : (const void*)a->expert_down_proj_weights;
-    e = launch_dispatch(a->input, a->selected_expert_indices, a->selected_expert_weights, s, ws, sc,
-                        a->expert_counts, a->expert_token_ids, a->expert_token_weights, a_rows, stream);
-    if (e != cudaSuccess) return cuda_fail(e, "dispatch");
-    if ((e = mark(2)) != cudaSuccess) return cuda_fail(e, "cudaEventRecord(stage event)");
+    return sc;
+}
+
+struct FfnBuffers {
+    void* a_rows;
+    void* h_rows;
+    const void *wg, *wu, *wd;
+};
+FfnBuffers ffn_buffers(const MoEArgs* a, const Shape& s) {
+    const bool i8 = s.dtype == MOE_DTYPE_INT8;
+    FfnBuffers b;
+    b.a_rows = i8 ? (void*)a->per_expert_wmma_inputs_int8 : (void*)a->per_expert_wmma_inputs;
+    b.h_rows = i8 ? (void*)a->hidden_mlp_layer_1_out_int8 : (void*)a->hidden_mlp_layer_1_out_fp16;
+    b.wg = i8 ? (const void*)a->expert_gate_proj_weights_int8 : (const void*)a->expert_gate_proj_weights;
+    b.wu = i8 ? (const void*)a->expert_up_proj_weights_int8 : (const void*)a->expert_up_proj_weights;
+    b.wd = i8 ? (const void*)a->expert_down_proj_weights_int8 : (const void*)a->expert_down_proj_weights;
+    return b;
+}
+
+#define MOE_TRY(expr, what)                                \
+    do {                                                   \
+        cudaError_t e_ = (expr);                           \
+        if (e_ != cudaSuccess) return cuda_fail(e_, what); \
+    } while (0)
+
+cudaError_t mark_stage(int i, cudaStream_t stream) {
+    return g_stage_on ? cudaEventRecord(g_stage_ev[i], stream) : cudaSuccess;
+}
+
+// Stages 1-3: router + top-k, slots, gather into the dense expert-major rows.
+int enqueue_route(const MoEArgs* a, const MoeDims* dims, const Shape& s, const Workspace& ws, cudaStream_t stream) {
+    MOE_TRY(launch_router_topk(a->input, a->router_weights, dims->router_bias, s, a->expert_logits,
+                               a->selected_expert_indices, a->selected_expert_weights, stream),
+            "router_topk");
+    MOE_TRY(mark_stage(1, stream), "cudaEventRecord(stage event)");
+    const FfnBuffers fb = ffn_buffers(a, s);
+    MOE_TRY(launch_dispatch(a->input, a->selected_expert_indices, a->selected_expert_weights, s, ws, scales_of(a, s),
+                            a->expert_counts, a->expert_token_ids, a->expert_token_weights, fb.a_rows, stream),
+            "dispatch");
+    return MOE_OK;
+}
+
+// Stage 4: the two grouped GEMMs over the row groups `gt`.
+int enqueue_ffn(const MoEArgs* a, const Shape& s, const GroupTable& gt, int* status, int num_sms,
+                cudaStream_t stream) {
+    const FfnBuffers fb = ffn_buffers(a, s);
+    const GemmScales sc = scales_of(a, s);
+    MOE_TRY(launch_expert_up_gate(fb.a_rows, fb.wg, fb.wu, s, gt, status, sc, fb.h_rows, stream, num_sms),
+            "expert up/gate GEMM");
+    MOE_TRY(mark_stage(3, stream), "cudaEventRecord(stage event)");
+    MOE_TRY(launch_expert_down(fb.h_rows, fb.wd, s, gt, status, sc, a->hidden_mlp_layer_2_out, stream, num_sms),
+            "expert down GEMM");
+    return MOE_OK;
+}
+
+// The stage sequence of one layer call on `stream`, given its scratch.
+int enqueue_layer(const MoEArgs* a, const MoeDims* dims, const Shape& s, const Workspace& ws, int num_sms,
+                  cudaStream_t stream) {
+    MOE_TRY(cudaMemsetAsync(ws.status, 0, sizeof(int), stream), "cudaMemsetAsync(status)");
+    MOE_TRY(mark_stage(0, stream), "cudaEventRecord(stage event)");
+    int rc = enqueue_route(a, dims, s, ws, stream);
+    if (rc != MOE_OK) return rc;
+    MOE_TRY(mark_stage(2, stream), "cudaEventRecord(stage event)");
     if (s.T() > 0 && s.cap > 0) {
-        e = launch_expert_up_gate(a_rows, wg, wu, s, ws, sc, h_rows, stream, num_sms);
-        if (e != cudaSuccess) return cuda_fail(e, "expert up/gate GEMM");
-        if ((e = mark(3)) != cudaSuccess) return cuda_fail(e, "cudaEventRecord(stage event)");
-        e = launch_expert_down(h_rows, wd, s, ws, sc, a->hidden_mlp_layer_2_out, stream, num_sms);
-        if (e != cudaSuccess) return cuda_fail(e, "expert down GEMM");
+        const GroupTable gt{ws.expert_rows, ws.expert_start, nullptr, s.E, s.rows_capacity()};
+        rc = enqueue_ffn(a, s, gt, ws.status, num_sms, stream);
+        if (rc != MOE_OK) return rc;
     } else {
-        if ((e = mark(3)) != cudaSuccess) return cuda_fail(e, "cudaEventRecord(stage event)");
+        MOE_TRY(mark_stage(3, stream), "cudaEventRecord(stage event)");
     }
-    if ((e = mark(4)) != cudaSuccess) return cuda_fail(e, "cudaEventRecord(stage event)");
-    e = launch_combine(a->hidden_mlp_layer_2_out, a->selected_expert_indices, a->selected_expert_weights, s,
-                       ws, a->final_output, dims->output_16, stream);
-    if (e != cudaSuccess) return cuda_fail(e, "combine");
-    if ((e = mark(5)) != cudaSuccess) return cuda_fail(e, "cudaEventRecord(stage event)");
+    MOE_TRY(mark_stage(4, stream), "cudaEventRecord(stage event)");
+    MOE_TRY(launch_combine(a->hidden_mlp_layer_2_out, a->selected_expert_indices, a->selected_expert_weights, s, ws,
+                           a->final_output, dims->output_16, stream),
+            "combine");
+    MOE_TRY(mark_stage(5, stream), "cudaEventRecord(stage event)");
     return MOE_OK;
 }
 
@@ -332,6 +376,119 @@ extern "C" int moe_solve_v2(const MoEArgs* a, const MoeDims* dims, cudaStream_t 
     }
     if (rc != MOE_OK) return rc;
     return enqueue_layer(a, dims, s, ws, st->num_sms, stream);
+}
+
+// ---- expert-parallel building blocks ---------------------------------------
+extern "C" int moe_stage_route(const MoEArgs* a, const MoeDims* dims, cudaStream_t stream) {
+    Shape s;
+    int rc = make_shape(dims, &s);
+    if (rc != MOE_OK) return rc;
+    const bool i8 = s.dtype == MOE_DTYPE_INT8;
+    if (!a || !a->input || !a->router_weights || !a->selected_expert_indices || !a->selected_expert_weights ||
+        !a->expert_counts || !a->expert_token_ids || !a->expert_token_weights ||
+        !(i8 ? (const void*)a->per_expert_wmma_inputs_int8 : (const void*)a->per_expert_wmma_inputs)) {
+        set_error("moe_stage_route: a routing buffer of MoEArgs is null");
+        return MOE_ERR_INVALID_ARG;
+    }
+    DeviceState* st = nullptr;
+    int dev = 0;
+    rc = device_state(&st, &dev);
+    if (rc != MOE_OK) return rc;
+    Workspace ws;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        rc = get_workspace(*st, s, &ws);
+    }
+    if (rc != MOE_OK) return rc;
+    MOE_TRY(cudaMemsetAsync(ws.status, 0, sizeof(int), stream), "cudaMemsetAsync(status)");
+    return enqueue_route(a, dims, s, ws, stream);
+}
+
+extern "C" int moe_stage_expert_ffn(const MoEArgs* a, const MoeDims* dims, const int* group_rows,
+                                    const int* group_start, const int* group_expert, int num_groups,
+                                    int64_t rows_capacity, cudaStream_t stream) {
+    // Only the FFN shape matters here: an owner may hold a single expert.
+    if (!dims) { set_error("dims is null"); return MOE_ERR_INVALID_ARG; }
+    MoeDims fd = *dims;
+    fd.num_experts = 8;
+    fd.top_k = 1;
+    fd.num_batches = 0;
+    Shape s;
+    int rc = make_shape(&fd, &s);
+    if (rc != MOE_OK) return rc;
+    s.E = dims->num_experts;
+    if (s.E < 1) { set_error("moe_stage_expert_ffn: num_experts %d", s.E); return MOE_ERR_INVALID_ARG; }
+    if (!a) { set_error("args is null"); return MOE_ERR_INVALID_ARG; }
+    {
+        const FfnBuffers fb = ffn_buffers(a, s);
+        if (!fb.a_rows || !fb.h_rows || !fb.wg || !fb.wu || !fb.wd || !a->hidden_mlp_layer_2_out) {
+            set_error("moe_stage_expert_ffn: a weight or row buffer of MoEArgs is null");
+            return MOE_ERR_INVALID_ARG;
+        }
+    }
+    if (!group_rows || !group_start || num_groups < 0 || num_groups > kMaxGroups || rows_capacity < 0 ||
+        rows_capacity >= ((int64_t)1 << 31)) {
+        set_error("moe_stage_expert_ffn: bad group table (num_groups %d, max %d)", num_groups, kMaxGroups);
+        return MOE_ERR_INVALID_ARG;
+    }
+    for (int g = 0; g < num_groups; ++g) {
+        const int w = group_expert ? group_expert[g] : g;
+        if (group_rows[g] < 0 || group_start[g] < 0 || (int64_t)group_start[g] + group_rows[g] > rows_capacity ||
+            w < 0 || w >= s.E) {
+            set_error("moe_stage_expert_ffn: group %d out of range", g);
+            return MOE_ERR_INVALID_ARG;
+        }
+    }
+    DeviceState* st = nullptr;
+    int dev = 0;
+    rc = device_state(&st, &dev);
+    if (rc != MOE_OK) return rc;
+    Workspace ws;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        rc = get_workspace(*st, s, &ws, /*header_only=*/true);
+    }
+    if (rc != MOE_OK) return rc;
+    if (num_groups == 0 || rows_capacity == 0) return MOE_OK;
+    MOE_TRY(cudaMemcpyAsync(ws.grp_rows, group_rows, sizeof(int) * num_groups, cudaMemcpyHostToDevice, stream),
+            "cudaMemcpyAsync(group rows)");
+    MOE_TRY(cudaMemcpyAsync(ws.grp_start, group_start, sizeof(int) * num_groups, cudaMemcpyHostToDevice, stream),
+            "cudaMemcpyAsync(group starts)");
+    if (group_expert)
+        MOE_TRY(cudaMemcpyAsync(ws.grp_weight, group_expert, sizeof(int) * num_groups, cudaMemcpyHostToDevice,
+                                stream),
+                "cudaMemcpyAsync(group experts)");
+    const GroupTable gt{ws.grp_rows, ws.grp_start, group_expert ? ws.grp_weight : nullptr, num_groups,
+                        rows_capacity};
+    return enqueue_ffn(a, s, gt, ws.status, st->num_sms, stream);
+}
+
+extern "C" int moe_stage_combine(const MoEArgs* a, const MoeDims* dims, cudaStream_t stream) {
+    Shape s;
+    int rc = make_shape(dims, &s);
+    if (rc != MOE_OK) return rc;
+    if (!a || !a->hidden_mlp_layer_2_out || !a->final_output || !a->selected_expert_indices ||
+        !a->selected_expert_weights) {
+        set_error("moe_stage_combine: null buffer");
+        return MOE_ERR_INVALID_ARG;
+    }
+    DeviceState* st = nullptr;
+    int dev = 0;
+    rc = device_state(&st, &dev);
+    if (rc != MOE_OK) return rc;
+    Workspace ws;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        if (st->ws_bytes < workspace_bytes(s)) {
+            set_error("moe_stage_combine: no routing tables for these dims (run moe_stage_route first)");
+            return MOE_ERR_INVALID_ARG;
+        }
+        carve_workspace(st->ws, s, &ws);
+    }
+    MOE_TRY(launch_combine(a->hidden_mlp_layer_2_out, a->selected_expert_indices, a->selected_expert_weights, s, ws,
+                           a->final_output, dims->output_16, stream),
+            "combine");
+    return MOE_OK;
 }
 
 extern "C" int moe_set_stage_events(void* const* events, int count) {

@@ -21,17 +21,39 @@ struct Shape {
     bool act_bf16;     // x (and the 16-bit output copy) are bf16 rather than f16
     int64_t T() const { return (int64_t)B * N; }
     int chunks() const { return (int)(((int64_t)N * k + kChunkRoutes - 1) / kChunkRoutes); }
-    int64_t rows_per_expert() const { return (int64_t)B * cap; }  // row stride of one expert
+    int64_t rows_capacity() const { return (int64_t)E * B * cap; }  // rows of the per-expert buffers
 };
 
+// Most row groups one grouped-GEMM launch takes (experts, or (sender, expert)
+// blocks under expert parallelism).
+constexpr int kMaxGroups = 1024;
+
 // Device scratch owned by the library (one block per device, grown on demand).
+// A fixed-size header (status word, GEMM group table) comes first, so calls
+// with different shapes never move it; the routing tables follow.
 struct Workspace {
+    int* status;        // [1]       device error word (kDevErrTimeout, ...)
+    int* grp_rows;      // [kMaxGroups] rows of each GEMM group (expert-parallel calls)
+    int* grp_start;     // [kMaxGroups] first row of each group
+    int* grp_weight;    // [kMaxGroups] expert weight index of each group
     int* route_slot;    // [B*N*k]   slot of each route, -1 if dropped / no expert
     int* chunk_count;   // [B, chunks, E] routes per (batch, chunk, expert)
     int* chunk_base;    // [B, chunks, E] exclusive prefix over chunks
-    int* row_base;      // [B, E]    first row of (b, e) inside expert e's compact block
+    int* row_base;      // [B, E]    first row of (b, e) inside expert e's block
     int* expert_rows;   // [E]       kept rows of expert e over all batches
-    int* status;        // [1]       device error word (kDevErrTimeout, ...)
+    int* expert_start;  // [E]       first row of expert e: exclusive prefix of expert_rows
+};
+size_t workspace_header_bytes();
+
+// Row groups of one grouped GEMM: group g has rows[g] rows starting at row
+// start[g] of the A/H/Y buffers (capacity rows_capacity) and multiplies expert
+// weight[g] (weight == nullptr: group g uses expert g).  Device arrays.
+struct GroupTable {
+    const int* rows;
+    const int* start;
+    const int* weight;
+    int G;
+    int64_t rows_capacity;
 };
 size_t workspace_bytes(const Shape& s);
 void carve_workspace(void* base, const Shape& s, Workspace* ws);
@@ -51,10 +73,10 @@ cudaError_t launch_dispatch(const void* x, const int* idx, const float* w, const
                             float* token_weights, void* a_rows, cudaStream_t st);
 // expert_gemm.cu: grouped tcgen05 GEMMs.
 cudaError_t launch_expert_up_gate(const void* a_rows, const void* w_gate, const void* w_up,
-                                  const Shape& s, const Workspace& ws, const GemmScales& sc,
+                                  const Shape& s, const GroupTable& gt, int* status, const GemmScales& sc,
                                   void* h_rows, cudaStream_t st, int num_sms);
 cudaError_t launch_expert_down(const void* h_rows, const void* w_down, const Shape& s,
-                               const Workspace& ws, const GemmScales& sc, float* y_rows,
+                               const GroupTable& gt, int* status, const GemmScales& sc, float* y_rows,
                                cudaStream_t st, int num_sms);
 // combine.cu: gate-weighted gather-sum into [B, N, d].
 cudaError_t launch_combine(const float* y_rows, const int* idx, const float* w, const Shape& s,

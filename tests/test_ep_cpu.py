@@ -1,0 +1,116 @@
+"""Expert-parallel host logic on CPU: the planner (pure functions of
+sparsemoe_b200.ep) and the full exchange pattern over a world-size-2 gloo
+group, with the oracle's routing and an f32 host FFN standing in for the GPU
+stages.  The exchanged result must equal the single-process layer."""
+import os
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+import sparsemoe_b200 as sm
+from sparsemoe_b200.ep import recv_plan, send_splits
+from oracle import oracle as O
+
+
+def test_send_splits_and_recv_plan():
+    table = np.array([[3, 0, 5, 1], [2, 4, 0, 6]], np.int32)      # P=2 senders, E=4
+    assert send_splits(table[0], 2) == [3, 6]
+    assert send_splits(table[1], 2) == [6, 6]
+    rsplit, (rows, start, exp) = recv_plan(table, 0)              # owner 0: experts 0, 1
+    assert rsplit == [3, 6]
+    # groups ordered (local expert, sender); receive buffer = [s0: e0 e1][s1: e0 e1]
+    assert rows.tolist() == [3, 2, 0, 4]
+    assert start.tolist() == [0, 3, 3, 5]
+    assert exp.tolist() == [0, 0, 1, 1]
+    rsplit, (rows, start, exp) = recv_plan(table, 1)              # owner 1: experts 2, 3
+    assert rsplit == [6, 6] and rows.tolist() == [5, 0, 1, 6] and start.tolist() == [0, 6, 5, 6]
+
+
+def _to_f32(u16):
+    return u16.view(np.float16).astype(np.float32)
+
+
+def _dense_rows(r, cfg, cap):
+    """The dense expert-major row order of moe_stage_route: for each expert e,
+    batches in order, slots in order -> (token index, route index)."""
+    B, N, E, k = cfg.num_batches, cfg.tokens, cfg.num_experts, cfg.top_k
+    order = []
+    for e in range(E):
+        for b in range(B):
+            for s in range(int(r["counts"][b, e])):
+                t = int(r["token_ids"][b, e, s])
+                order.append(b * N + t)
+    return order
+
+
+def _ffn_rows(a16, wg, wu, wd):
+    a = _to_f32(a16)
+    g = a @ _to_f32(wg)
+    u = a @ _to_f32(wu)
+    h = (u * (g / (1 + np.exp(-g)))).astype(np.float16).astype(np.float32)
+    return (h @ _to_f32(wd)).astype(np.float32)
+
+
+def _rank_main(rank, world, port, cfg_args, results):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    cfg = sm.LayerConfig(*cfg_args)
+    full = sm.make_inputs(cfg, 5)                      # same weights everywhere
+    mine = sm.make_inputs(cfg, 100 + rank)             # this rank's own tokens
+    cap = cfg.capacity()
+    r = O.route(mine["x"], full["wr"], None, cfg.num_batches, cfg.tokens, cfg.d_model, cfg.num_experts,
+                cfg.top_k, cap, False)
+    order = _dense_rows(r, cfg, cap)
+    send_x = mine["x"][order] if order else np.zeros((0, cfg.d_model), np.uint16)
+    rows_e = r["counts"].sum(axis=0).astype(np.int32)
+    table = [torch.zeros(cfg.num_experts, dtype=torch.int32) for _ in range(world)]
+    dist.all_gather(table, torch.from_numpy(rows_e))
+    table = torch.stack(table).numpy()
+    ss = send_splits(table[rank], world)
+    rs, (g_rows, g_start, g_exp) = recv_plan(table, rank)
+    # 16-bit rows travel as int32 pairs (gloo has no 16-bit all-to-all)
+    recv = torch.empty(sum(rs), cfg.d_model // 2, dtype=torch.int32)
+    dist.all_to_all_single(recv, torch.from_numpy(np.ascontiguousarray(send_x).view(np.int32)), rs, ss)
+    recv = recv.numpy().view(np.uint16)
+    e_loc = cfg.num_experts // world
+    y = np.zeros((recv.shape[0], cfg.d_model), np.float32)
+    for n, st, j in zip(g_rows, g_start, g_exp):
+        e = rank * e_loc + j
+        if n:
+            y[st:st + n] = _ffn_rows(recv[st:st + n], full["wg"][e], full["wu"][e], full["wd"][e])
+    back = torch.empty(sum(ss), cfg.d_model, dtype=torch.float32)
+    dist.all_to_all_single(back, torch.from_numpy(y), ss, rs)
+    back = back.numpy()
+    # combine: route -> its row in the dense layout
+    start = np.concatenate([[0], np.cumsum(rows_e)])
+    rowbase = np.zeros((cfg.num_batches, cfg.num_experts), np.int64)
+    for e in range(cfg.num_experts):
+        acc = 0
+        for b in range(cfg.num_batches):
+            rowbase[b, e] = acc
+            acc += r["counts"][b, e]
+    out = np.zeros((cfg.T, cfg.d_model), np.float32)
+    for t in range(cfg.T):
+        b = t // cfg.tokens
+        for l in range(cfg.top_k):
+            ri = t * cfg.top_k + l
+            if r["route_slot"][ri] >= 0:
+                e = r["idx"][t, l]
+                out[t] += r["w"][t, l] * back[start[e] + rowbase[b, e] + r["route_slot"][ri]]
+    ref = O.forward({**full, "x": mine["x"]}, cfg)["out"]
+    results[rank] = float(np.abs(out - ref).max() / np.abs(ref).max())
+    dist.destroy_process_group()
+
+
+def test_ep_exchange_gloo_world2():
+    cfg_args = (2, 96, 256, 128, 8, 2, 1.0)
+    port = 29500 + (os.getpid() % 2000)
+    with mp.Manager() as m:
+        results = m.dict()
+        mp.spawn(_rank_main, args=(2, port, cfg_args, results), nprocs=2, join=True)
+        errs = dict(results)
+    assert set(errs) == {0, 1}
+    assert max(errs.values()) < 1e-2, errs
