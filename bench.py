@@ -224,7 +224,7 @@ def run_ep(args, cfg, ws, rank, local, dev):
     import torch
     import torch.distributed as dist
     from sparsemoe_b200.ep import ExpertParallelLayer
-    layer = ExpertParallelLayer(cfg, dev)
+    layer = ExpertParallelLayer(cfg, dev, chunks=args.ep_chunks)
     g = torch.Generator(device=dev)
     g.manual_seed(1000 + rank)
     layer.x.normal_(0.0, 1.0, generator=g)
@@ -238,21 +238,28 @@ def run_ep(args, cfg, ws, rank, local, dev):
         layer.forward(stream)
     layer.sync_check(stream)
     K = args.steps
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(6)] for _ in range(K)]
+    timings = [dict() for _ in range(K)]
     owner_rows = []
     torch.cuda.synchronize(dev)
     barrier(ws)
     torch.cuda.synchronize(dev)
     with ClockSampler(local) as clocks:
         for i in range(K):
-            layer.forward(stream, events=evs[i])
+            layer.forward(stream, timing=timings[i])
             owner_rows.append(layer.last_plan["owner_rows"])
         torch.cuda.synchronize(dev)
     barrier(ws)
-    ms_local = statistics.mean(evs[i][0].elapsed_time(evs[i][5]) for i in range(K))
+
+    def span(tm, a, b):
+        return tm[a][0].elapsed_time(tm[b][0])
+    ms_local = statistics.mean(span(tm, "start", "end") for tm in timings)
     ms = max_over_ranks(ms_local, ws, dev)
-    phase_ms = {name: statistics.mean(evs[i][j].elapsed_time(evs[i][j + 1]) for i in range(K))
-                for j, name in enumerate(layer.PHASES)}
+    ffn_ms = statistics.mean(sum(tm["ffn"][2 * j].elapsed_time(tm["ffn"][2 * j + 1])
+                                 for j in range(len(tm["ffn"]) // 2)) for tm in timings)
+    phase_ms = {"route": statistics.mean(span(tm, "start", "routed") for tm in timings),
+                "expert_ffn_compute": ffn_ms,
+                "combine_tail": statistics.mean(tm["combine"][-1].elapsed_time(tm["end"][0]) for tm in timings)}
+    phase_ms["exposed_exchange"] = ms_local - phase_ms["route"] - ffn_ms - phase_ms["combine_tail"]
     layer.sync_check(stream)
     # end-to-end: host x in, 16-bit output out, per step
     x_host = torch.empty_like(layer.x, device="cpu").pin_memory()
@@ -277,7 +284,7 @@ def run_ep(args, cfg, ws, rank, local, dev):
     peaks, peak_src = load_peaks()
     peak_tf = float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
     flop_ffn = 6.0 * cfg.d_model * cfg.d_ff * statistics.mean(owner_rows)
-    ach = flop_ffn / (phase_ms["expert_ffn"] * 1e-3) / 1e12
+    ach = flop_ffn / (phase_ms["expert_ffn_compute"] * 1e-3) / 1e12
     ach_min = max_over_ranks(-ach, ws, dev) * -1.0      # slowest rank
     h2d = x_host.numel() * x_host.element_size()
     d2h = out_host.numel() * out_host.element_size()
@@ -288,7 +295,8 @@ def run_ep(args, cfg, ws, rank, local, dev):
         "data": "synthetic (seeded torch normal: x N(0,1), router N(0,0.02), W N(0,1/sqrt(fan_in)))",
         "config": {**cfg_json(args.config, cfg, layer.cap),
                    "parallelism": f"ep{ws} (expert parallel, {cfg.num_experts // ws} experts per GPU, "
-                                  f"NCCL all-to-all dispatch/return; {cfg.T} tokens per GPU)"},
+                                  f"NCCL all-to-all dispatch/return on a second stream, {layer.n_chunks} "
+                                  f"pipelined batch chunks; {cfg.T} tokens per GPU)"},
         "roofline": {"bound": "tensor", "achieved": ach_min, "peak": peak_tf, "unit": "TFLOP/s",
                      "frac": ach_min / peak_tf, "traffic": None,
                      "kernel": "expert_ffn phase (up/gate + down tcgen05 GEMMs), slowest rank",
@@ -317,6 +325,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline measurement")
     ap.add_argument("--parallel", default="auto", choices=["auto", "ep", "replicas"],
                     help="N>1: expert parallelism over NCCL (default) or independent replicas")
+    ap.add_argument("--ep-chunks", type=int, default=1, help="pipelined batch chunks in EP mode")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 

@@ -45,6 +45,8 @@ typedef struct MoeDims {
     int   router_dtype;     // MOE_ROUTER_*
     const float* router_bias;  // optional device [E] f32 added to every logit (Zipf popularity bias)
     void* output_16;        // optional device [B, N, d] copy of the output in the 16-bit dtype
+    void* scratch;          // optional caller device memory for the library's routing tables
+    size_t scratch_bytes;   //   (>= moe_workspace_bytes(dims)); NULL: the library's own block
 } MoeDims;
 
 // Reference: kernels/launcher.h:21 `extern "C" void solve(MoEArgs args)`.

@@ -75,6 +75,7 @@ class MoeDims(ctypes.Structure):
         ("d_ff", ctypes.c_int), ("num_experts", ctypes.c_int), ("top_k", ctypes.c_int),
         ("capacity_factor", ctypes.c_float), ("cap", ctypes.c_int), ("dtype", ctypes.c_int),
         ("router_dtype", ctypes.c_int), ("router_bias", _p), ("output_16", _p),
+        ("scratch", _p), ("scratch_bytes", ctypes.c_size_t),
     ]
 
 
@@ -187,10 +188,11 @@ class LayerConfig:
             return self.tokens
         return capacity(self.tokens, self.top_k, self.num_experts, self.capacity_factor)
 
-    def dims(self, router_bias_ptr: int | None = None, out16_ptr: int | None = None) -> MoeDims:
+    def dims(self, router_bias_ptr: int | None = None, out16_ptr: int | None = None,
+             scratch_ptr: int | None = None, scratch_bytes: int = 0) -> MoeDims:
         return MoeDims(self.num_batches, self.tokens, self.d_model, self.d_ff, self.num_experts, self.top_k,
                        self.capacity_factor, self.cap, self.dtype, ROUTER_F32 if self.router_f32 else ROUTER_SAME,
-                       router_bias_ptr, out16_ptr)
+                       router_bias_ptr, out16_ptr, scratch_ptr, scratch_bytes)
 
 
 def make_inputs(cfg: LayerConfig, seed: int = 0) -> dict:

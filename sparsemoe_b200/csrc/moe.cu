@@ -191,6 +191,28 @@ int get_workspace(DeviceState& st, const Shape& s, Workspace* ws, bool header_on
     return MOE_OK;
 }
 
+// Workspace for a call: the caller's scratch (dims->scratch) when given, else
+// the library's per-device block.
+int resolve_workspace(DeviceState& st, int dev, const MoeDims* dims, const Shape& s, Workspace* ws,
+                      bool header_only = false) {
+    if (dims->scratch) {
+        const size_t need = header_only ? workspace_header_bytes() : workspace_bytes(s);
+        if (dims->scratch_bytes < need) {
+            set_error("scratch of %zu bytes is smaller than the %zu this call needs", dims->scratch_bytes, need);
+            return MOE_ERR_INVALID_ARG;
+        }
+        if (reinterpret_cast<uintptr_t>(dims->scratch) % 256 != 0) {
+            set_error("scratch must be 256-byte aligned");
+            return MOE_ERR_INVALID_ARG;
+        }
+        carve_workspace(dims->scratch, s, ws);
+        note_status_word(dev, ws->status);
+        return MOE_OK;
+    }
+    std::lock_guard<std::mutex> lk(g_mu);
+    return get_workspace(st, s, ws, header_only);
+}
+
 }  // namespace
 }  // namespace moe
 
@@ -370,10 +392,7 @@ extern "C" int moe_solve_v2(const MoEArgs* a, const MoeDims* dims, cudaStream_t 
     rc = device_state(&st, &dev);
     if (rc != MOE_OK) return rc;
     Workspace ws;
-    {
-        std::lock_guard<std::mutex> lk(g_mu);
-        rc = get_workspace(*st, s, &ws);
-    }
+    rc = resolve_workspace(*st, dev, dims, s, &ws);
     if (rc != MOE_OK) return rc;
     return enqueue_layer(a, dims, s, ws, st->num_sms, stream);
 }
@@ -395,10 +414,7 @@ extern "C" int moe_stage_route(const MoEArgs* a, const MoeDims* dims, cudaStream
     rc = device_state(&st, &dev);
     if (rc != MOE_OK) return rc;
     Workspace ws;
-    {
-        std::lock_guard<std::mutex> lk(g_mu);
-        rc = get_workspace(*st, s, &ws);
-    }
+    rc = resolve_workspace(*st, dev, dims, s, &ws);
     if (rc != MOE_OK) return rc;
     MOE_TRY(cudaMemsetAsync(ws.status, 0, sizeof(int), stream), "cudaMemsetAsync(status)");
     return enqueue_route(a, dims, s, ws, stream);
@@ -444,10 +460,7 @@ extern "C" int moe_stage_expert_ffn(const MoEArgs* a, const MoeDims* dims, const
     rc = device_state(&st, &dev);
     if (rc != MOE_OK) return rc;
     Workspace ws;
-    {
-        std::lock_guard<std::mutex> lk(g_mu);
-        rc = get_workspace(*st, s, &ws, /*header_only=*/true);
-    }
+    rc = resolve_workspace(*st, dev, dims, s, &ws, /*header_only=*/true);
     if (rc != MOE_OK) return rc;
     if (num_groups == 0 || rows_capacity == 0) return MOE_OK;
     MOE_TRY(cudaMemcpyAsync(ws.grp_rows, group_rows, sizeof(int) * num_groups, cudaMemcpyHostToDevice, stream),
@@ -477,7 +490,10 @@ extern "C" int moe_stage_combine(const MoEArgs* a, const MoeDims* dims, cudaStre
     rc = device_state(&st, &dev);
     if (rc != MOE_OK) return rc;
     Workspace ws;
-    {
+    if (dims->scratch) {
+        rc = resolve_workspace(*st, dev, dims, s, &ws);
+        if (rc != MOE_OK) return rc;
+    } else {
         std::lock_guard<std::mutex> lk(g_mu);
         if (st->ws_bytes < workspace_bytes(s)) {
             set_error("moe_stage_combine: no routing tables for these dims (run moe_stage_route first)");

@@ -24,7 +24,7 @@ def _worker(rank, world, port, cfg_args, results):
     full = sm.make_inputs(cfg, 5)
     mine = sm.make_inputs(cfg, 100 + rank)
     inputs = {**full, "x": mine["x"]}
-    ep = ExpertParallelLayer(cfg, f"cuda:{rank}").load(inputs)
+    ep = ExpertParallelLayer(cfg, f"cuda:{rank}", chunks=cfg_args[9] if len(cfg_args) > 9 else 1).load(inputs)
     ep.forward()
     ep.sync_check()
     ep.forward()          # second call: reuses buffers and the library scratch
@@ -43,6 +43,7 @@ def _worker(rank, world, port, cfg_args, results):
     (2, 256, 512, 512, 8, 2, 1.25, 1, 0.0),     # bf16, Mixtral-like routing
     (1, 384, 256, 256, 16, 4, 1.0, 0, 1.1),     # fp16, Zipf bias -> drops
     (2, 128, 512, 256, 8, 2, 1.25, 2, 0.0),     # int8 path
+    (4, 128, 256, 256, 8, 2, 1.25, 1, 0.0, 2),  # two pipelined batch chunks
 ])
 def test_ep_matches_single_gpu(gpu, cfg_args):
     import torch
