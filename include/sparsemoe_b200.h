@@ -25,6 +25,9 @@ extern "C" {
 #define MOE_DTYPE_BF16  1   // bf16 bit patterns in the same `half*` fields
 #define MOE_DTYPE_INT8  2   // per-tensor int8 weights/activations, s32 accumulate, f16 x and router
                             // (reference kernels/capacity_int8_ptx.cu; MoEArgs *_int8 fields + scales)
+#define MOE_DTYPE_FP8_BLOCK 3  // e4m3 weights with f32 scales per 128x128 block (MoeDims.w_scale_*),
+                               // activations and h quantised on the fly per 1x128 block, bf16 x and
+                               // router, f32 accumulate; MoEArgs *_fp8 fields
 
 // ---- router formats --------------------------------------------------------
 #define MOE_ROUTER_SAME 0   // router_weights have the activation dtype
@@ -47,6 +50,10 @@ typedef struct MoeDims {
     void* output_16;        // optional device [B, N, d] copy of the output in the 16-bit dtype
     void* scratch;          // optional caller device memory for the library's routing tables
     size_t scratch_bytes;   //   (>= moe_workspace_bytes(dims)); NULL: the library's own block
+    // MOE_DTYPE_FP8_BLOCK weight scales (device f32): gate/up [E, d/128, f/128], down [E, f/128, d/128]
+    const float* w_scale_gate;
+    const float* w_scale_up;
+    const float* w_scale_down;
 } MoeDims;
 
 // Reference: kernels/launcher.h:21 `extern "C" void solve(MoEArgs args)`.
@@ -129,6 +136,12 @@ const char* moe_last_error(void);
 // values, scale = max|x| / qmax (1 if all zero), q = nearbyint(clamp(x/scale,
 // -qmax, qmax)).  qmax = 127 (int8) or 7 (int4 values).  Returns the scale.
 float moe_quantize_per_tensor(const uint16_t* src_f16, size_t n, int8_t* dst, float qmax);
+
+// FP8 block quantiser for weights [E, K, N] (16-bit, bf16 != 0: bf16):
+// per expert and 128x128 block, s = amax / 448 (1 if the block is zero),
+// q = e4m3(x / s) rounded to nearest even, saturating at +-448.
+// Writes q [E, K, N] (e4m3 bytes) and scales [E, K/128, N/128].
+void moe_quantize_fp8_blocks(const uint16_t* src, int E, int K, int N, int bf16, uint8_t* q, float* scales);
 
 // ---- seeded input generator (the reference has none: inputs/data.cu:164-177
 //      zero-fills everything).  Counter-based, thread-count independent:

@@ -93,9 +93,41 @@ void parallel_for(int64_t n, int nthreads, F&& fn) {
     for (auto& th : pool) th.join();
 }
 
+// e4m3 (1-4-3, bias 7, no infinities, max 448): decode and nearest-even encode
+// with saturation to +-448 (the "satfinite" conversion), restated from the
+// format definition.
+inline float e4m3_to_f32(uint8_t v) {
+    const int sgn = v >> 7, ex = (v >> 3) & 15, man = v & 7;
+    float mag;
+    if (ex == 15 && man == 7) mag = NAN;
+    else if (ex == 0) mag = ldexpf((float)man, -9);
+    else mag = ldexpf(1.0f + man / 8.0f, ex - 7);
+    return sgn ? -mag : mag;
+}
+inline uint8_t f32_to_e4m3(float x) {
+    if (std::isnan(x)) return 0x7F;
+    const uint8_t sgn = std::signbit(x) ? 0x80 : 0;
+    double a = std::fabs((double)x);
+    if (a >= 448.0) return sgn | 0x7E;
+    if (a < ldexp(1.0, -6)) {                           // subnormal range: multiples of 2^-9
+        const int q = (int)std::nearbyint(a * 512.0);   // 0..8 (8 = smallest normal)
+        return sgn | (uint8_t)q;
+    }
+    int e;
+    std::frexp(a, &e);                                  // a = f * 2^e, f in [0.5, 1)
+    e -= 1;                                             // a = (1+m) * 2^e
+    int mq = (int)std::nearbyint((a / std::ldexp(1.0, e) - 1.0) * 8.0);
+    if (mq == 8) { mq = 0; e += 1; }
+    if (e > 8 || (e == 8 && mq == 7)) return sgn | 0x7E;
+    return sgn | (uint8_t)(((e + 7) << 3) | mq);
+}
+
 }  // namespace
 
 extern "C" {
+
+uint8_t oracle_e4m3(float x) { return f32_to_e4m3(x); }
+float oracle_e4m3_decode(uint8_t v) { return e4m3_to_f32(v); }
 
 // inputs/data.cu:392-398 (same float expression, rounded up to 16).
 int oracle_capacity(int tokens, int top_k, int num_experts, float cf) {
@@ -386,6 +418,99 @@ void oracle_ffn_combine_int8(const uint16_t* x, const int8_t* wg, const int8_t* 
             for (int c = 0; c < d; ++c) {
                 volatile float p = wl * yr[c];
                 o[c] = o[c] + p;
+            }
+        }
+    });
+}
+
+// FP8 block-scaled path: x (bf16) quantised per 1x128
+// block (s = amax/448, 1 if zero), weights e4m3 with scales per 128x128 block;
+// per K block: P = sum of e4m3 products (f32), acc = fmaf(P, s_a*s_w, acc);
+// h = u * g/(1+exp(-g)), quantised per 1x128 block of f the same way; the down
+// GEMM likewise with the h scales; then the route-order combine.
+//   wq: [E, K, N] e4m3 codes; ws: [E, K/128, N/128] f32 scales.
+void oracle_ffn_combine_fp8(const uint16_t* x, const uint8_t* wg, const uint8_t* wu, const uint8_t* wd,
+                            const float* sg, const float* su, const float* sd, int d, int f, int E, int k,
+                            const int* idx, const float* w, const int* route_slot, int64_t t_begin, int64_t t_end,
+                            float* out, int nthreads) {
+    std::vector<std::vector<int64_t>> routes(E);
+    for (int64_t t = t_begin; t < t_end; ++t)
+        for (int l = 0; l < k; ++l) {
+            const int64_t r = t * k + l;
+            if (route_slot[r] >= 0) routes[idx[r]].push_back(r);
+        }
+    std::vector<float> dec(256);
+    for (int i = 0; i < 256; ++i) dec[i] = e4m3_to_f32((uint8_t)i);
+    std::vector<float> y((size_t)(t_end - t_begin) * k * d, 0.0f);
+    const int dk = d / 128, fk = f / 128;
+    struct Item { int e; int r; };
+    std::vector<Item> items;
+    for (int e = 0; e < E; ++e)
+        for (int r = 0; r < (int)routes[e].size(); ++r) items.push_back({e, r});
+    auto quant_row = [&](const float* v, int n, float* qv, float* sc) {
+        for (int b = 0; b < n / 128; ++b) {
+            float m = 0.0f;
+            for (int i = 0; i < 128; ++i) m = fmaxf(m, fabsf(v[b * 128 + i]));
+            const float s = m > 0.0f ? m / 448.0f : 1.0f;
+            sc[b] = s;
+            for (int i = 0; i < 128; ++i) qv[b * 128 + i] = dec[f32_to_e4m3(v[b * 128 + i] / s)];
+        }
+    };
+    parallel_for((int64_t)items.size(), nthreads, [&](int64_t it) {
+        const int e = items[it].e;
+        const int64_t route = routes[e][items[it].r];
+        const int64_t tok = route / k;
+        std::vector<float> xv(d), qa(d), sa(dk), g(f, 0.0f), u(f, 0.0f), p(f), pu(f), h(f), qh(f), sh(fk),
+            acc(d, 0.0f), pd(d);
+        for (int j = 0; j < d; ++j) xv[j] = bf16_to_f32(x[tok * d + j]);
+        quant_row(xv.data(), d, qa.data(), sa.data());
+        const uint8_t* Wg = wg + (size_t)e * d * f;
+        const uint8_t* Wu = wu + (size_t)e * d * f;
+        const uint8_t* Wd = wd + (size_t)e * f * d;
+        for (int kb = 0; kb < dk; ++kb) {
+            std::fill(p.begin(), p.end(), 0.0f);
+            std::fill(pu.begin(), pu.end(), 0.0f);
+            for (int j = kb * 128; j < kb * 128 + 128; ++j) {
+                const float av = qa[j];
+                const uint8_t* gr = Wg + (size_t)j * f;
+                const uint8_t* ur = Wu + (size_t)j * f;
+                for (int c = 0; c < f; ++c) {
+                    p[c] += av * dec[gr[c]];
+                    pu[c] += av * dec[ur[c]];
+                }
+            }
+            for (int c = 0; c < f; ++c) {
+                const size_t si = ((size_t)e * dk + kb) * fk + c / 128;
+                g[c] = fmaf(p[c], sa[kb] * sg[si], g[c]);
+                u[c] = fmaf(pu[c], sa[kb] * su[si], u[c]);
+            }
+        }
+        for (int c = 0; c < f; ++c) h[c] = u[c] * (g[c] / (1.0f + expf(-g[c])));
+        quant_row(h.data(), f, qh.data(), sh.data());
+        for (int kb = 0; kb < fk; ++kb) {
+            std::fill(pd.begin(), pd.end(), 0.0f);
+            for (int j = kb * 128; j < kb * 128 + 128; ++j) {
+                const float hv = qh[j];
+                const uint8_t* dr = Wd + (size_t)j * d;
+                for (int c = 0; c < d; ++c) pd[c] += hv * dec[dr[c]];
+            }
+            for (int c = 0; c < d; ++c)
+                acc[c] = fmaf(pd[c], sh[kb] * sd[((size_t)e * fk + kb) * dk + c / 128], acc[c]);
+        }
+        std::memcpy(&y[((size_t)(route - t_begin * k)) * d], acc.data(), sizeof(float) * d);
+    });
+    parallel_for(t_end - t_begin, nthreads, [&](int64_t i) {
+        const int64_t t = t_begin + i;
+        float* o = out + t * d;
+        for (int c = 0; c < d; ++c) o[c] = 0.0f;
+        for (int l = 0; l < k; ++l) {
+            const int64_t r = t * k + l;
+            if (route_slot[r] < 0) continue;
+            const float wl = w[r];
+            const float* yr = &y[((size_t)(r - t_begin * k)) * d];
+            for (int c = 0; c < d; ++c) {
+                volatile float pp = wl * yr[c];
+                o[c] = o[c] + pp;
             }
         }
     });

@@ -46,6 +46,13 @@ def lib() -> ctypes.CDLL:
         F = ctypes.c_float
         L.oracle_ffn_combine_int8.argtypes = [P, P, P, P, F, F, F, F, F, I, I, I, I, P, P, P, ctypes.c_int64,
                                               ctypes.c_int64, P, I]
+        L.oracle_ffn_combine_fp8.restype = None
+        L.oracle_ffn_combine_fp8.argtypes = [P, P, P, P, P, P, P, I, I, I, I, P, P, P, ctypes.c_int64,
+                                             ctypes.c_int64, P, I]
+        L.oracle_e4m3.restype = ctypes.c_uint8
+        L.oracle_e4m3.argtypes = [ctypes.c_float]
+        L.oracle_e4m3_decode.restype = ctypes.c_float
+        L.oracle_e4m3_decode.argtypes = [ctypes.c_uint8]
         _lib = L
     return _lib
 
@@ -112,12 +119,32 @@ def ffn_combine_int8(x, q, cfg, idx, w, route_slot, t_begin=0, t_end=None, nthre
     return out[t_begin:t_end]
 
 
+def ffn_combine_fp8(x, q, cfg, idx, w, route_slot, t_begin=0, t_end=None, nthreads=None):
+    """FP8 block-scaled path for tokens [t_begin, t_end); q holds wg_q/wu_q/wd_q
+    (e4m3 bytes) and sg/su/sd (block scales)."""
+    T = cfg.T
+    t_end = T if t_end is None else t_end
+    out = np.zeros((T, cfg.d_model), np.float32)
+    ws = [np.ascontiguousarray(q[n], np.uint8) for n in ("wg_q", "wu_q", "wd_q")]
+    ss = [np.ascontiguousarray(q[n], np.float32) for n in ("sg", "su", "sd")]
+    lib().oracle_ffn_combine_fp8(_ptr(np.ascontiguousarray(x, np.uint16)), *(_ptr(a) for a in ws),
+                                 *(_ptr(a) for a in ss), cfg.d_model, cfg.d_ff, cfg.num_experts, cfg.top_k,
+                                 _ptr(np.ascontiguousarray(idx, np.int32)), _ptr(np.ascontiguousarray(w, np.float32)),
+                                 _ptr(np.ascontiguousarray(route_slot, np.int32)), t_begin, t_end, _ptr(out),
+                                 nthreads or threads())
+    return out[t_begin:t_end]
+
+
 def forward(inputs: dict, cfg, t_begin=0, t_end=None, nthreads=None):
     """Whole layer on the CPU for a sparsemoe_b200.LayerConfig and make_inputs() dict."""
     cap = cfg.capacity()
+    act_bf16 = cfg.bf16 or getattr(cfg, "fp8", False)
     r = route(inputs["x"], inputs["wr"], inputs.get("bias"), cfg.num_batches, cfg.tokens, cfg.d_model,
-              cfg.num_experts, cfg.top_k, cap, cfg.bf16, cfg.router_f32, nthreads)
-    if getattr(cfg, "int8", False):
+              cfg.num_experts, cfg.top_k, cap, act_bf16, cfg.router_f32, nthreads)
+    if getattr(cfg, "fp8", False):
+        r["out"] = ffn_combine_fp8(inputs["x"], inputs, cfg, r["idx"], r["w"], r["route_slot"], t_begin, t_end,
+                                   nthreads)
+    elif getattr(cfg, "int8", False):
         r["out"] = ffn_combine_int8(inputs["x"], inputs, cfg, r["idx"], r["w"], r["route_slot"], t_begin, t_end,
                                     nthreads)
     else:

@@ -28,6 +28,7 @@ MOE_ERR_NO_KERNEL = -5
 DTYPE_F16 = 0
 DTYPE_BF16 = 1
 DTYPE_INT8 = 2
+DTYPE_FP8_BLOCK = 3
 ROUTER_SAME = 0
 ROUTER_F32 = 1
 
@@ -76,6 +77,7 @@ class MoeDims(ctypes.Structure):
         ("capacity_factor", ctypes.c_float), ("cap", ctypes.c_int), ("dtype", ctypes.c_int),
         ("router_dtype", ctypes.c_int), ("router_bias", _p), ("output_16", _p),
         ("scratch", _p), ("scratch_bytes", ctypes.c_size_t),
+        ("w_scale_gate", _p), ("w_scale_up", _p), ("w_scale_down", _p),
     ]
 
 
@@ -105,6 +107,7 @@ def _load() -> ctypes.CDLL:
         "moe_fill_normal_16": (None, [_p, ctypes.c_size_t, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_float,
                                       ctypes.c_int]),
         "moe_quantize_per_tensor": (ctypes.c_float, [_p, ctypes.c_size_t, _p, ctypes.c_float]),
+        "moe_quantize_fp8_blocks": (None, [_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _p, _p]),
         "moe_fill_normal_f32": (None, [_p, ctypes.c_size_t, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_float]),
         "moe_zipf_bias": (None, [_p, ctypes.c_int, ctypes.c_float, ctypes.c_float, ctypes.c_uint64]),
     }
@@ -178,6 +181,15 @@ class LayerConfig:
         return self.dtype == DTYPE_BF16
 
     @property
+    def fp8(self) -> bool:
+        return self.dtype == DTYPE_FP8_BLOCK
+
+    @property
+    def act_bf16(self) -> bool:
+        """Activations (x, router, 16-bit output) are bf16."""
+        return self.dtype in (DTYPE_BF16, DTYPE_FP8_BLOCK)
+
+    @property
     def int8(self) -> bool:
         return self.dtype == DTYPE_INT8
 
@@ -189,10 +201,10 @@ class LayerConfig:
         return capacity(self.tokens, self.top_k, self.num_experts, self.capacity_factor)
 
     def dims(self, router_bias_ptr: int | None = None, out16_ptr: int | None = None,
-             scratch_ptr: int | None = None, scratch_bytes: int = 0) -> MoeDims:
+             scratch_ptr: int | None = None, scratch_bytes: int = 0, w_scales=(None, None, None)) -> MoeDims:
         return MoeDims(self.num_batches, self.tokens, self.d_model, self.d_ff, self.num_experts, self.top_k,
                        self.capacity_factor, self.cap, self.dtype, ROUTER_F32 if self.router_f32 else ROUTER_SAME,
-                       router_bias_ptr, out16_ptr, scratch_ptr, scratch_bytes)
+                       router_bias_ptr, out16_ptr, scratch_ptr, scratch_bytes, *w_scales)
 
 
 def make_inputs(cfg: LayerConfig, seed: int = 0) -> dict:
@@ -202,16 +214,21 @@ def make_inputs(cfg: LayerConfig, seed: int = 0) -> dict:
     16-bit tensors are returned as uint16 bit patterns.
     """
     d, f, E = cfg.d_model, cfg.d_ff, cfg.num_experts
+    b16 = cfg.act_bf16
     out = {
-        "x": normal16(cfg.T * d, seed, 0, 1.0, cfg.bf16).reshape(cfg.T, d),
-        "wg": normal16(E * d * f, seed, 2, 1.0 / np.sqrt(d), cfg.bf16).reshape(E, d, f),
-        "wu": normal16(E * d * f, seed, 3, 1.0 / np.sqrt(d), cfg.bf16).reshape(E, d, f),
-        "wd": normal16(E * f * d, seed, 4, 1.0 / np.sqrt(f), cfg.bf16).reshape(E, f, d),
+        "x": normal16(cfg.T * d, seed, 0, 1.0, b16).reshape(cfg.T, d),
+        "wg": normal16(E * d * f, seed, 2, 1.0 / np.sqrt(d), b16).reshape(E, d, f),
+        "wu": normal16(E * d * f, seed, 3, 1.0 / np.sqrt(d), b16).reshape(E, d, f),
+        "wd": normal16(E * f * d, seed, 4, 1.0 / np.sqrt(f), b16).reshape(E, f, d),
     }
     if cfg.router_f32:
         out["wr"] = normal_f32(d * E, seed, 1, 0.02).reshape(d, E)
     else:
-        out["wr"] = normal16(d * E, seed, 1, 0.02, cfg.bf16).reshape(d, E)
+        out["wr"] = normal16(d * E, seed, 1, 0.02, b16).reshape(d, E)
+    if cfg.fp8:
+        for n, key in (("wg", "sg"), ("wu", "su"), ("wd", "sd")):
+            q, sc = quantize_fp8_blocks(out[n], bf16=True)
+            out[n + "_q"], out[key] = q, sc
     out["bias"] = zipf_bias(E, cfg.zipf_s) if cfg.zipf_s > 0 else None
     if cfg.int8:
         # reference inputs/data.cu:315-322: per-tensor int8 weights, placeholder activation scales
@@ -223,6 +240,17 @@ def make_inputs(cfg: LayerConfig, seed: int = 0) -> dict:
         out["s_in"] = float(np.float32(cfg.act_scale))
         out["s_mid"] = float(np.float32(cfg.mid_scale))
     return out
+
+
+def quantize_fp8_blocks(w16: np.ndarray, bf16: bool = True):
+    """e4m3 weights with f32 scales per 128x128 block of each [K, N] expert
+    matrix (s = amax/448).  w16: [E, K, N] 16-bit bit patterns."""
+    E, K, N = w16.shape
+    w16 = np.ascontiguousarray(w16, np.uint16)
+    q = np.empty((E, K, N), np.uint8)
+    sc = np.empty((E, K // 128, N // 128), np.float32)
+    lib.moe_quantize_fp8_blocks(w16.ctypes.data, E, K, N, int(bf16), q.ctypes.data, sc.ctypes.data)
+    return q, sc
 
 
 def quantize_per_tensor(w16: np.ndarray, qmax: float = 127.0):
@@ -237,4 +265,4 @@ from .layer import MoeLayer  # noqa: E402  (needs `lib` above)
 
 __all__ = ["MoEArgs", "MoeDims", "LayerConfig", "MoeLayer", "make_inputs", "capacity", "lib", "check",
            "MoeError", "normal16", "normal_f32", "zipf_bias", "quantize_per_tensor", "DTYPE_F16", "DTYPE_BF16",
-           "DTYPE_INT8"]
+           "DTYPE_INT8", "DTYPE_FP8_BLOCK", "quantize_fp8_blocks"]

@@ -59,6 +59,37 @@ extern "C" float moe_quantize_per_tensor(const uint16_t* src, size_t n, int8_t* 
     return scale;
 }
 
+extern "C" void moe_quantize_fp8_blocks(const uint16_t* src, int E, int K, int N, int bf16, uint8_t* q,
+                                        float* scales) {
+    auto val = [&](size_t i) -> float {
+        if (bf16) {
+            uint32_t u = (uint32_t)src[i] << 16;
+            float f;
+            std::memcpy(&f, &u, 4);
+            return f;
+        }
+        half h;
+        std::memcpy(&h, &src[i], 2);
+        return __half2float(h);
+    };
+    const int kb = K / 128, nb = N / 128;
+    for (int e = 0; e < E; ++e)
+        for (int bk = 0; bk < kb; ++bk)
+            for (int bn = 0; bn < nb; ++bn) {
+                float m = 0.0f;
+                for (int i = 0; i < 128; ++i)
+                    for (int j = 0; j < 128; ++j)
+                        m = std::fmax(m, std::fabs(val(((size_t)e * K + bk * 128 + i) * N + bn * 128 + j)));
+                const float sc = m > 0.0f ? m / 448.0f : 1.0f;
+                scales[((size_t)e * kb + bk) * nb + bn] = sc;
+                for (int i = 0; i < 128; ++i)
+                    for (int j = 0; j < 128; ++j) {
+                        const size_t idx = ((size_t)e * K + bk * 128 + i) * N + bn * 128 + j;
+                        q[idx] = (uint8_t)__nv_cvt_float_to_fp8(val(idx) / sc, __NV_SATFINITE, __NV_E4M3);
+                    }
+            }
+}
+
 namespace {
 
 float quant_symmetric(const std::vector<half>& src, std::vector<int8_t>& dst, float qmax) {

@@ -25,6 +25,8 @@
 #include "moe_internal.h"
 #include <cstdint>
 #include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <cuda_fp8.h>
 
 namespace moe {
 namespace {
@@ -201,6 +203,40 @@ __global__ void __launch_bounds__(kThreads) dispatch_gather_q8_kernel(
     }
 }
 
+// FP8 block path: the slot's bf16 token row quantised per 1x128 block,
+// s = amax / 448 (1 for an all-zero block), q = e4m3(x / s) (nearest even,
+// saturating); lane l handles elements 4l..4l+3 of each block.
+__global__ void __launch_bounds__(kThreads) dispatch_gather_fp8_kernel(
+    const __nv_bfloat16* __restrict__ x, const int* __restrict__ counts, const int* __restrict__ token_ids,
+    const int* __restrict__ row_base, const int* __restrict__ expert_start, int N, int E, int B, int cap, int d,
+    uint8_t* __restrict__ a_rows, float* __restrict__ a_scale) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t slot_lin = (int64_t)blockIdx.x * kWarps + warp;
+    if (slot_lin >= (int64_t)B * E * cap) return;
+    const int be = (int)(slot_lin / cap);
+    const int s = (int)(slot_lin - (int64_t)be * cap);
+    if (s >= counts[be]) return;
+    const int b = be / E, e = be - b * E;
+    const int64_t t = token_ids[slot_lin];
+    const __nv_bfloat16* src = x + ((int64_t)b * N + t) * d;
+    const int64_t row = (int64_t)expert_start[e] + row_base[be] + s;
+    uint8_t* dst = a_rows + row * d;
+    const int nblk = d / 128;
+    for (int blk = 0; blk < nblk; ++blk) {
+        const uint2 raw = __ldg(reinterpret_cast<const uint2*>(src + blk * 128) + lane);
+        const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+        const float2 v0 = __bfloat1622float2(h2[0]), v1 = __bfloat1622float2(h2[1]);
+        float amax = fmaxf(fmaxf(fabsf(v0.x), fabsf(v0.y)), fmaxf(fabsf(v1.x), fabsf(v1.y)));
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+        const float sc = amax > 0.0f ? amax / 448.0f : 1.0f;
+        const uint32_t lo = __nv_cvt_float2_to_fp8x2(make_float2(v0.x / sc, v0.y / sc), __NV_SATFINITE, __NV_E4M3);
+        const uint32_t hi = __nv_cvt_float2_to_fp8x2(make_float2(v1.x / sc, v1.y / sc), __NV_SATFINITE, __NV_E4M3);
+        reinterpret_cast<uint32_t*>(dst + blk * 128)[lane] = lo | (hi << 16);
+        if (lane == 0) a_scale[row * nblk + blk] = sc;
+    }
+}
+
 }  // namespace
 
 cudaError_t launch_dispatch(const void* x, const int* idx, const float* w, const Shape& s,
@@ -221,7 +257,11 @@ cudaError_t launch_dispatch(const void* x, const int* idx, const float* w, const
     // 16-bit activations: rows of d elements = d/8 16-byte vectors.
     const int64_t slots = (int64_t)s.B * s.E * s.cap;
     const unsigned gblocks = (unsigned)((slots + kWarps - 1) / kWarps);
-    if (slots > 0 && s.dtype == MOE_DTYPE_INT8)
+    if (slots > 0 && s.dtype == MOE_DTYPE_FP8_BLOCK)
+        dispatch_gather_fp8_kernel<<<gblocks, kThreads, 0, st>>>(
+            (const __nv_bfloat16*)x, counts, token_ids, ws.row_base, ws.expert_start, s.N, s.E, s.B, s.cap, s.d,
+            (uint8_t*)a_rows, ws.a_scale);
+    else if (slots > 0 && s.dtype == MOE_DTYPE_INT8)
         dispatch_gather_q8_kernel<<<gblocks, kThreads, 0, st>>>((const uint4*)x, counts, token_ids, ws.row_base,
                                                                 ws.expert_start, s.N, s.E, s.B, s.cap, s.d / 8,
                                                                 sc.s_in, (uint2*)a_rows);

@@ -423,6 +423,10 @@ GemmParams base_params(const GroupTable& gt, int* status, const GemmScales& sc) 
 
 }  // namespace
 
+bool make_map_u8(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint32_t box_outer) {
+    return make_map(map, base, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, inner, outer, box_outer);
+}
+
 cudaError_t launch_expert_up_gate(const void* a_rows, const void* w_gate, const void* w_up, const Shape& s,
                                   const GroupTable& gt, int* status, const GemmScales& sc, void* h_rows,
                                   cudaStream_t st, int num_sms) {

@@ -1,0 +1,375 @@
+// Stage 4, FP8 block-scaled form: e4m3 operands with f32 scales per 1x128
+// activation block and per 128x128 weight block (amax / 448), f32 accumulate.
+//
+//   U[r, n] = sum_kb  s_a[r, kb] * s_w[kb, n/128] * sum_{k in kb} qa[r, k] qw[k, n]
+//
+// The scales are arbitrary f32 (not powers of two), so the tensor core's MX
+// block scaling cannot apply them.  Each 128-wide K block is instead MMA'd
+// into its own TMEM partial (double-buffered, 2 x 256 columns) and promoted by
+// the epilogue warps into register accumulators with one packed f32x2 FMA per
+// two columns: acc += P_kb * (s_a * s_w).
+//
+// Warp roles (320 threads, one persistent CTA per SM):
+//   warp 0      TMA producer: A 128 rows x 128 B (one K block, K-major, 128B
+//               swizzle) + B 128 K-rows x 256 columns from the row-major
+//               [K, N] e4m3 weights (MN-major, 128B swizzle); 4-stage ring.
+//   warp 1      MMA issuer: per K block 4 x tcgen05.mma kind::f8f6f4 M128
+//               N256 K32 into TMEM partial P[kb & 1].
+//   warps 2-9   promotion + epilogue: warp w reads TMEM lanes 32*(w%4).. and
+//               half (w-2)/4 of the columns:
+//                 up/gate: gate cols [64h, 64h+64) and up cols 128+[64h, ..)
+//                 of the same 64 output features, so SwiGLU is local; the h
+//                 row block of 128 features (the tile) gets its 1x128 scale
+//                 from the two halves' amax (exchanged through shared
+//                 memory) and is written as e4m3 plus its f32 scale;
+//                 down: cols [128h, 128h+128), written as f32 rows of Y.
+// Quantisation (host weights, device activations and h) rounds x / s to the
+// nearest e4m3, saturating at +-448.
+#include "moe_internal.h"
+#include "common.cuh"
+#include "sm100.cuh"
+
+#include <cuda.h>
+#include <cuda_fp8.h>
+#include <cudaTypedefs.h>
+
+namespace moe {
+
+bool make_map_u8(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint32_t box_outer);
+
+namespace {
+
+using namespace sm100;
+
+constexpr int kBM = 128;
+constexpr int kStages = 4;
+constexpr int kThreads = 320;
+constexpr int kPromoWarps = 8;
+constexpr int kABytes = kBM * 128;
+constexpr int kBBytes = 128 * 256;
+constexpr int kStageBytes = kABytes + kBBytes;
+constexpr int kChunkBytes = 128 * 128;   // 128 K-rows x 128 columns (one swizzle span)
+constexpr int kTmemCols = 512;
+constexpr size_t kSmemBytes = 1024 + (size_t)kStages * kStageBytes + 1024;
+
+struct Fp8Params {
+    const int* g_rows;
+    const int* g_start;
+    const int* g_weight;
+    int G;
+    int K;               // reduction length
+    int n_tiles;         // output tiles per group
+    int out_ld;          // output row length (f or d)
+    void* out;           // e4m3 h rows (up/gate) or f32 y rows (down)
+    float* out_scale;    // up/gate: [rows, f/128] h block scales
+    const float* a_scale;    // [rows, K/128] activation block scales
+    const float* w_scale0;   // up/gate: gate [Ew, K/128, f/128]; down: [Ew, f/128, d/128]
+    const float* w_scale1;   // up/gate: up scales
+    int* status;
+    uint32_t idesc;
+};
+
+__device__ __forceinline__ void decode_tile(int t, const int* pre, const int* mt, int G, int& g, int& m, int& n) {
+    int lo = 0, hi = G - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (pre[mid] <= t) lo = mid; else hi = mid - 1;
+    }
+    g = lo;
+    const int local = t - pre[g];
+    n = local / mt[g];
+    m = local - n * mt[g];
+}
+
+__device__ __forceinline__ void ffma2(float& a0, float& a1, float p0, float p1, float s) {
+    unsigned long long acc, pp, ss;
+    float2 av = make_float2(a0, a1), pv = make_float2(p0, p1), sv = make_float2(s, s);
+    acc = *reinterpret_cast<unsigned long long*>(&av);
+    pp = *reinterpret_cast<unsigned long long*>(&pv);
+    ss = *reinterpret_cast<unsigned long long*>(&sv);
+    asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc) : "l"(pp), "l"(ss));
+    const float2 r = *reinterpret_cast<float2*>(&acc);
+    a0 = r.x;
+    a1 = r.y;
+}
+
+__device__ __forceinline__ uint32_t e4m3x4(float a, float b, float c, float d) {
+    const uint32_t lo = __nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3);
+    const uint32_t hi = __nv_cvt_float2_to_fp8x2(make_float2(c, d), __NV_SATFINITE, __NV_E4M3);
+    return lo | (hi << 16);
+}
+
+template <int kMode>  // 0: up/gate + SwiGLU -> e4m3 h + scales;  1: down -> f32 y
+__global__ void __launch_bounds__(kThreads, 1)
+    fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB0,
+                    const __grid_constant__ CUtensorMap tmB1, const Fp8Params p) {
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ int s_pre[kMaxGroups + 1];
+    __shared__ int s_mt[kMaxGroups];
+    __shared__ int s_rows[kMaxGroups];
+    __shared__ int s_start[kMaxGroups];
+    __shared__ int s_wt[kMaxGroups];
+    __shared__ float s_amax[2][kBM];
+
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + kStages * kABytes;
+    uint64_t* full = reinterpret_cast<uint64_t*>(sB + kStages * kBBytes);
+    uint64_t* empty = full + kStages;
+    uint64_t* pfull = empty + kStages;
+    uint64_t* pempty = pfull + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pempty + 2);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+        for (int a = 0; a < 2; ++a) { mbar_init(&pfull[a], 1); mbar_init(&pempty[a], kPromoWarps * 32); }
+        fence_mbar_init();
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB0);
+        if (kMode == 0) tma_prefetch_desc(&tmB1);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, kTmemCols);
+        tmem_relinquish();
+    }
+    for (int g = threadIdx.x; g < p.G; g += kThreads) {
+        const int r = p.g_rows[g];
+        s_rows[g] = r;
+        s_mt[g] = (r + kBM - 1) / kBM;
+        s_start[g] = p.g_start[g];
+        s_wt[g] = p.g_weight ? p.g_weight[g] : g;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int acc = 0;
+        for (int g = 0; g < p.G; ++g) { s_pre[g] = acc; acc += s_mt[g] * p.n_tiles; }
+        s_pre[p.G] = acc;
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const int total = s_pre[p.G];
+    const int kblocks = p.K / 128;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int s = 0;
+            uint32_t ph = 0;
+            for (int t = blockIdx.x; t < total; t += gridDim.x) {
+                int g, m, n;
+                decode_tile(t, s_pre, s_mt, p.G, g, m, n);
+                const int a_row = s_start[g] + m * kBM;
+                const int b_row = s_wt[g] * p.K;
+                for (int kb = 0; kb < kblocks; ++kb) {
+                    if (!mbar_wait(&empty[s], ph ^ 1u, p.status, kDevErrTimeout)) goto producer_done;
+                    mbar_arrive_expect_tx(&full[s], kStageBytes);
+                    uint8_t* a_dst = sA + s * kABytes;
+                    uint8_t* b_dst = sB + s * kBBytes;
+                    tma_load_2d(a_dst, &tmA, &full[s], kb * 128, a_row);
+                    if (kMode == 0) {
+                        tma_load_2d(b_dst, &tmB0, &full[s], n * 128, b_row + kb * 128);
+                        tma_load_2d(b_dst + kChunkBytes, &tmB1, &full[s], n * 128, b_row + kb * 128);
+                    } else {
+                        tma_load_2d(b_dst, &tmB0, &full[s], n * 256, b_row + kb * 128);
+                        tma_load_2d(b_dst + kChunkBytes, &tmB0, &full[s], n * 256 + 128, b_row + kb * 128);
+                    }
+                    if (++s == kStages) { s = 0; ph ^= 1u; }
+                }
+            }
+        producer_done:;
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            int s = 0, pb = 0;
+            uint32_t ph = 0, pph = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+                for (int kb = 0; kb < kblocks; ++kb) {
+                    if (!mbar_wait(&pempty[pb], pph ^ 1u, p.status, kDevErrTimeout) ||
+                        !mbar_wait(&full[s], ph, p.status, kDevErrTimeout)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_base = smem_u32(sA + s * kABytes);
+                    const uint32_t b_base = smem_u32(sB + s * kBBytes);
+                    const uint32_t d_tmem = tmem_base + pb * 256;
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk) {
+                        const uint64_t adesc = smem_desc_sw128(a_base + kk * 32, 16, 1024);
+                        const uint64_t bdesc = smem_desc_sw128(b_base + kk * 32 * 128, kChunkBytes, 1024);
+                        mma_f8_ss(d_tmem, adesc, bdesc, p.idesc, kk != 0 ? 1u : 0u);
+                    }
+                    mma_commit(&empty[s]);
+                    mma_commit(&pfull[pb]);
+                    if (++s == kStages) { s = 0; ph ^= 1u; }
+                    pb ^= 1;
+                    if (pb == 0) pph ^= 1u;
+                }
+            }
+        }
+    } else {
+        // ---------------- promotion + epilogue (warps 2..9) ----------------
+        const int q = warp & 3;
+        const int half = (warp - 2) >> 2;
+        const int row_in_tile = q * 32 + lane;
+        const int nkb = kblocks;
+        const int nblk = p.out_ld / 128;
+        int pb = 0;
+        uint32_t pph = 0;
+        for (int t = blockIdx.x; t < total; t += gridDim.x) {
+            int g, m, n;
+            decode_tile(t, s_pre, s_mt, p.G, g, m, n);
+            const int row_local = m * kBM + row_in_tile;
+            const bool valid = row_local < s_rows[g];
+            const int64_t row = (int64_t)s_start[g] + row_local;
+            // rows past the group's end read the group's first row's (finite) scales; never stored
+            const float* arow = p.a_scale + (valid ? row : (int64_t)s_start[g]) * nkb;
+            const int wexp = s_wt[g];
+            float acc[128];
+#pragma unroll
+            for (int i = 0; i < 128; ++i) acc[i] = 0.0f;
+            bool ok = true;
+            for (int kb = 0; kb < nkb; ++kb) {
+                const float sa = arow[kb];
+                float sw0, sw1;
+                if (kMode == 0) {
+                    sw0 = p.w_scale0[((int64_t)wexp * nkb + kb) * nblk + n];
+                    sw1 = p.w_scale1[((int64_t)wexp * nkb + kb) * nblk + n];
+                } else {
+                    sw0 = p.w_scale0[((int64_t)wexp * nkb + kb) * nblk + 2 * n + half];
+                    sw1 = sw0;
+                }
+                if (!mbar_wait(&pfull[pb], pph, p.status, kDevErrTimeout)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + pb * 256;
+                const float sc0 = sa * sw0, sc1 = sa * sw1;
+#pragma unroll
+                for (int piece = 0; piece < 4; ++piece) {
+                    uint32_t r[32];
+                    const int col = kMode == 0 ? (piece < 2 ? 64 * half + 32 * piece : 128 + 64 * half + 32 * (piece - 2))
+                                               : 128 * half + 32 * piece;
+                    tmem_ld_32x32b_x32(tbase + col, r);
+                    tmem_wait_ld();
+                    if (piece == 3) { tc_fence_before(); mbar_arrive(&pempty[pb]); }
+                    const float sc = (kMode == 0 && piece >= 2) ? sc1 : sc0;
+#pragma unroll
+                    for (int i = 0; i < 32; i += 2)
+                        ffma2(acc[32 * piece + i], acc[32 * piece + i + 1], __uint_as_float(r[i]),
+                              __uint_as_float(r[i + 1]), sc);
+                }
+                pb ^= 1;
+                if (pb == 0) pph ^= 1u;
+            }
+            if (!ok) break;
+            if (kMode == 0) {
+                float amax = 0.0f;
+#pragma unroll
+                for (int i = 0; i < 64; ++i) {
+                    const float gv = acc[i], uv = acc[64 + i];
+                    const float h = uv * (gv / (1.0f + __expf(-gv)));
+                    acc[i] = h;
+                    amax = fmaxf(amax, fabsf(h));
+                }
+                // the 1x128 block of h = both halves of this row
+                asm volatile("bar.sync %0, 64;" ::"r"(1 + q) : "memory");
+                s_amax[half][row_in_tile] = amax;
+                asm volatile("bar.sync %0, 64;" ::"r"(1 + q) : "memory");
+                const float bmax = fmaxf(s_amax[0][row_in_tile], s_amax[1][row_in_tile]);
+                const float sh = bmax > 0.0f ? bmax / 448.0f : 1.0f;
+                if (valid) {
+                    uint8_t* h8 = reinterpret_cast<uint8_t*>(p.out) + row * p.out_ld + n * 128 + 64 * half;
+                    uint4* o = reinterpret_cast<uint4*>(h8);
+#pragma unroll
+                    for (int v = 0; v < 4; ++v) {
+                        uint32_t w4[4];
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            const int i = 16 * v + 4 * j;
+                            w4[j] = e4m3x4(acc[i] / sh, acc[i + 1] / sh, acc[i + 2] / sh, acc[i + 3] / sh);
+                        }
+                        o[v] = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+                    }
+                    if (half == 0) p.out_scale[row * nblk + n] = sh;
+                }
+            } else if (valid) {
+                float4* y = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + row * p.out_ld + n * 256 +
+                                                      128 * half);
+#pragma unroll
+                for (int v = 0; v < 32; ++v) y[v] = make_float4(acc[4 * v], acc[4 * v + 1], acc[4 * v + 2], acc[4 * v + 3]);
+            }
+        }
+    }
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, kTmemCols);
+    }
+}
+
+template <int kMode>
+cudaError_t launch(const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& b1, const Fp8Params& p,
+                   cudaStream_t st, int num_sms) {
+    auto kern = fp8_gemm_kernel<kMode>;
+    cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+    if (err != cudaSuccess) return err;
+    kern<<<num_sms, kThreads, kSmemBytes, st>>>(a, b0, b1, p);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_fp8_up_gate(const void* a_rows, const float* a_scale, const void* w_gate, const void* w_up,
+                               const float* s_gate, const float* s_up, const Shape& s, const GroupTable& gt,
+                               int* status, void* h_rows, float* h_scale, cudaStream_t st, int num_sms) {
+    if (gt.G <= 0 || gt.rows_capacity <= 0) return cudaSuccess;
+    CUtensorMap ta, tg, tu;
+    if (!make_map_u8(&ta, a_rows, s.d, gt.rows_capacity, kBM) ||
+        !make_map_u8(&tg, w_gate, s.f, (uint64_t)s.E * s.d, 128) ||
+        !make_map_u8(&tu, w_up, s.f, (uint64_t)s.E * s.d, 128))
+        return cudaErrorInvalidValue;
+    Fp8Params p{};
+    p.g_rows = gt.rows;
+    p.g_start = gt.start;
+    p.g_weight = gt.weight;
+    p.G = gt.G;
+    p.K = s.d;
+    p.n_tiles = s.f / 128;
+    p.out_ld = s.f;
+    p.out = h_rows;
+    p.out_scale = h_scale;
+    p.a_scale = a_scale;
+    p.w_scale0 = s_gate;
+    p.w_scale1 = s_up;
+    p.status = status;
+    p.idesc = idesc_e4m3(kBM, 256, true);
+    return launch<0>(ta, tg, tu, p, st, num_sms);
+}
+
+cudaError_t launch_fp8_down(const void* h_rows, const float* h_scale, const void* w_down, const float* s_down,
+                            const Shape& s, const GroupTable& gt, int* status, float* y_rows, cudaStream_t st,
+                            int num_sms) {
+    if (gt.G <= 0 || gt.rows_capacity <= 0) return cudaSuccess;
+    CUtensorMap th, td;
+    if (!make_map_u8(&th, h_rows, s.f, gt.rows_capacity, kBM) ||
+        !make_map_u8(&td, w_down, s.d, (uint64_t)s.E * s.f, 128))
+        return cudaErrorInvalidValue;
+    Fp8Params p{};
+    p.g_rows = gt.rows;
+    p.g_start = gt.start;
+    p.g_weight = gt.weight;
+    p.G = gt.G;
+    p.K = s.f;
+    p.n_tiles = s.d / 256;
+    p.out_ld = s.d;
+    p.out = y_rows;
+    p.a_scale = h_scale;
+    p.w_scale0 = s_down;
+    p.status = status;
+    p.idesc = idesc_e4m3(kBM, 256, true);
+    return launch<1>(th, td, td, p, st, num_sms);
+}
+
+}  // namespace moe

@@ -67,11 +67,16 @@ void set_error(const char* fmt, ...) {
 
 size_t workspace_header_bytes() { return 256 + 3 * align256(sizeof(int) * kMaxGroups); }
 
+size_t scale_bytes(const Shape& s, int dim) {
+    return s.dtype == MOE_DTYPE_FP8_BLOCK ? align256(sizeof(float) * (size_t)s.rows_capacity() * (dim / 128)) : 0;
+}
+
 size_t workspace_bytes(const Shape& s) {
     const size_t routes = (size_t)s.T() * s.k;
     const size_t chunk_tab = (size_t)s.B * s.chunks() * s.E;
     return workspace_header_bytes() + align256(sizeof(int) * routes) + 2 * align256(sizeof(int) * chunk_tab) +
-           align256(sizeof(int) * (size_t)s.B * s.E) + 2 * align256(sizeof(int) * s.E);
+           align256(sizeof(int) * (size_t)s.B * s.E) + 2 * align256(sizeof(int) * s.E) + scale_bytes(s, s.d) +
+           scale_bytes(s, s.f);
 }
 
 void carve_workspace(void* base, const Shape& s, Workspace* ws) {
@@ -87,7 +92,10 @@ void carve_workspace(void* base, const Shape& s, Workspace* ws) {
     ws->chunk_base = reinterpret_cast<int*>(p);   p += align256(sizeof(int) * chunk_tab);
     ws->row_base = reinterpret_cast<int*>(p);     p += align256(sizeof(int) * (size_t)s.B * s.E);
     ws->expert_rows = reinterpret_cast<int*>(p);  p += align256(sizeof(int) * s.E);
-    ws->expert_start = reinterpret_cast<int*>(p);
+    ws->expert_start = reinterpret_cast<int*>(p); p += align256(sizeof(int) * s.E);
+    ws->a_scale = scale_bytes(s, s.d) ? reinterpret_cast<float*>(p) : nullptr;
+    p += scale_bytes(s, s.d);
+    ws->h_scale = scale_bytes(s, s.f) ? reinterpret_cast<float*>(p) : nullptr;
 }
 
 namespace {
@@ -117,7 +125,8 @@ int make_shape(const MoeDims* d, Shape* s) {
         set_error("d_model=%d must be a multiple of 256 and d_ff=%d of 128", d->d_model, d->d_ff);
         return MOE_ERR_UNSUPPORTED;
     }
-    if (d->dtype != MOE_DTYPE_F16 && d->dtype != MOE_DTYPE_BF16 && d->dtype != MOE_DTYPE_INT8) {
+    if (d->dtype != MOE_DTYPE_F16 && d->dtype != MOE_DTYPE_BF16 && d->dtype != MOE_DTYPE_INT8 &&
+        d->dtype != MOE_DTYPE_FP8_BLOCK) {
         set_error("dtype %d not supported by this entry point", d->dtype);
         return MOE_ERR_UNSUPPORTED;
     }
@@ -133,7 +142,11 @@ int make_shape(const MoeDims* d, Shape* s) {
     s->k = d->top_k;
     s->dtype = d->dtype;
     s->router_dtype = d->router_dtype;
-    s->act_bf16 = d->dtype == MOE_DTYPE_BF16;
+    s->act_bf16 = d->dtype == MOE_DTYPE_BF16 || d->dtype == MOE_DTYPE_FP8_BLOCK;
+    if (d->dtype == MOE_DTYPE_FP8_BLOCK && (!d->w_scale_gate || !d->w_scale_up || !d->w_scale_down)) {
+        set_error("MOE_DTYPE_FP8_BLOCK needs MoeDims.w_scale_gate / w_scale_up / w_scale_down");
+        return MOE_ERR_INVALID_ARG;
+    }
     if (d->cap > 0) s->cap = d->cap;
     else if (d->cap == 0) s->cap = moe_capacity(d->tokens, d->top_k, d->num_experts, d->capacity_factor);
     else s->cap = d->tokens;  // no-drop ("baseline") policy
@@ -263,14 +276,18 @@ int check_args(const MoEArgs* a, int dtype) {
                         a->expert_counts && a->expert_token_ids && a->expert_token_weights &&
                         a->hidden_mlp_layer_2_out && a->final_output;
     bool fmt = false;
-    if (dtype == MOE_DTYPE_INT8)
+    if (dtype == MOE_DTYPE_FP8_BLOCK)
+        fmt = a->expert_up_proj_weights_fp8 && a->expert_gate_proj_weights_fp8 && a->expert_down_proj_weights_fp8 &&
+              a->per_expert_wmma_inputs_fp8 && a->hidden_mlp_layer_1_out_fp8;
+    else if (dtype == MOE_DTYPE_INT8)
         fmt = a->expert_up_proj_weights_int8 && a->expert_gate_proj_weights_int8 &&
               a->expert_down_proj_weights_int8 && a->per_expert_wmma_inputs_int8 && a->hidden_mlp_layer_1_out_int8;
     else
         fmt = a->expert_up_proj_weights && a->expert_gate_proj_weights && a->expert_down_proj_weights &&
               a->per_expert_wmma_inputs && a->hidden_mlp_layer_1_out_fp16;
     if (!common || !fmt) {
-        set_error("a MoEArgs buffer needed by the %s path is null", dtype == MOE_DTYPE_INT8 ? "int8" : "16-bit");
+        set_error("a MoEArgs buffer needed by the %s path is null",
+                  dtype == MOE_DTYPE_INT8 ? "int8" : dtype == MOE_DTYPE_FP8_BLOCK ? "fp8" : "16-bit");
         return MOE_ERR_INVALID_ARG;
     }
     if (dtype == MOE_DTYPE_INT8 && !(a->scale_input_act > 0.0f && a->scale_mid_act > 0.0f)) {
@@ -312,6 +329,14 @@ struct FfnBuffers {
 FfnBuffers ffn_buffers(const MoEArgs* a, const Shape& s) {
     const bool i8 = s.dtype == MOE_DTYPE_INT8;
     FfnBuffers b;
+    if (s.dtype == MOE_DTYPE_FP8_BLOCK) {
+        b.a_rows = (void*)a->per_expert_wmma_inputs_fp8;
+        b.h_rows = (void*)a->hidden_mlp_layer_1_out_fp8;
+        b.wg = a->expert_gate_proj_weights_fp8;
+        b.wu = a->expert_up_proj_weights_fp8;
+        b.wd = a->expert_down_proj_weights_fp8;
+        return b;
+    }
     b.a_rows = i8 ? (void*)a->per_expert_wmma_inputs_int8 : (void*)a->per_expert_wmma_inputs;
     b.h_rows = i8 ? (void*)a->hidden_mlp_layer_1_out_int8 : (void*)a->hidden_mlp_layer_1_out_fp16;
     b.wg = i8 ? (const void*)a->expert_gate_proj_weights_int8 : (const void*)a->expert_gate_proj_weights;
@@ -344,9 +369,19 @@ int enqueue_route(const MoEArgs* a, const MoeDims* dims, const Shape& s, const W
 }
 
 // Stage 4: the two grouped GEMMs over the row groups `gt`.
-int enqueue_ffn(const MoEArgs* a, const Shape& s, const GroupTable& gt, int* status, int num_sms,
-                cudaStream_t stream) {
+int enqueue_ffn(const MoEArgs* a, const MoeDims* dims, const Shape& s, const GroupTable& gt, int* status,
+                float* a_scale, float* h_scale, int num_sms, cudaStream_t stream) {
     const FfnBuffers fb = ffn_buffers(a, s);
+    if (s.dtype == MOE_DTYPE_FP8_BLOCK) {
+        MOE_TRY(launch_fp8_up_gate(fb.a_rows, a_scale, fb.wg, fb.wu, dims->w_scale_gate, dims->w_scale_up, s, gt,
+                                   status, fb.h_rows, h_scale, stream, num_sms),
+                "fp8 up/gate GEMM");
+        MOE_TRY(mark_stage(3, stream), "cudaEventRecord(stage event)");
+        MOE_TRY(launch_fp8_down(fb.h_rows, h_scale, fb.wd, dims->w_scale_down, s, gt, status,
+                                a->hidden_mlp_layer_2_out, stream, num_sms),
+                "fp8 down GEMM");
+        return MOE_OK;
+    }
     const GemmScales sc = scales_of(a, s);
     MOE_TRY(launch_expert_up_gate(fb.a_rows, fb.wg, fb.wu, s, gt, status, sc, fb.h_rows, stream, num_sms),
             "expert up/gate GEMM");
@@ -366,7 +401,7 @@ int enqueue_layer(const MoEArgs* a, const MoeDims* dims, const Shape& s, const W
     MOE_TRY(mark_stage(2, stream), "cudaEventRecord(stage event)");
     if (s.T() > 0 && s.cap > 0) {
         const GroupTable gt{ws.expert_rows, ws.expert_start, nullptr, s.E, s.rows_capacity()};
-        rc = enqueue_ffn(a, s, gt, ws.status, num_sms, stream);
+        rc = enqueue_ffn(a, dims, s, gt, ws.status, ws.a_scale, ws.h_scale, num_sms, stream);
         if (rc != MOE_OK) return rc;
     } else {
         MOE_TRY(mark_stage(3, stream), "cudaEventRecord(stage event)");
@@ -473,7 +508,11 @@ extern "C" int moe_stage_expert_ffn(const MoEArgs* a, const MoeDims* dims, const
                 "cudaMemcpyAsync(group experts)");
     const GroupTable gt{ws.grp_rows, ws.grp_start, group_expert ? ws.grp_weight : nullptr, num_groups,
                         rows_capacity};
-    return enqueue_ffn(a, s, gt, ws.status, st->num_sms, stream);
+    if (s.dtype == MOE_DTYPE_FP8_BLOCK) {
+        set_error("moe_stage_expert_ffn: the FP8 block path runs through moe_solve_v2 only in this build");
+        return MOE_ERR_UNSUPPORTED;
+    }
+    return enqueue_ffn(a, dims, s, gt, ws.status, nullptr, nullptr, st->num_sms, stream);
 }
 
 extern "C" int moe_stage_combine(const MoEArgs* a, const MoeDims* dims, cudaStream_t stream) {

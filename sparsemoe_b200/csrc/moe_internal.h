@@ -42,6 +42,8 @@ struct Workspace {
     int* row_base;      // [B, E]    first row of (b, e) inside expert e's block
     int* expert_rows;   // [E]       kept rows of expert e over all batches
     int* expert_start;  // [E]       first row of expert e: exclusive prefix of expert_rows
+    float* a_scale;     // FP8 path: [E*B*CAP, d/128] activation block scales
+    float* h_scale;     // FP8 path: [E*B*CAP, f/128] h block scales
 };
 size_t workspace_header_bytes();
 
@@ -78,6 +80,14 @@ cudaError_t launch_expert_up_gate(const void* a_rows, const void* w_gate, const 
 cudaError_t launch_expert_down(const void* h_rows, const void* w_down, const Shape& s,
                                const GroupTable& gt, int* status, const GemmScales& sc, float* y_rows,
                                cudaStream_t st, int num_sms);
+// expert_gemm_fp8.cu: block-scaled e4m3 GEMMs.
+cudaError_t launch_fp8_up_gate(const void* a_rows, const float* a_scale, const void* w_gate, const void* w_up,
+                               const float* s_gate, const float* s_up, const Shape& s, const GroupTable& gt,
+                               int* status, void* h_rows, float* h_scale, cudaStream_t st, int num_sms);
+cudaError_t launch_fp8_down(const void* h_rows, const float* h_scale, const void* w_down, const float* s_down,
+                            const Shape& s, const GroupTable& gt, int* status, float* y_rows, cudaStream_t st,
+                            int num_sms);
+
 // combine.cu: gate-weighted gather-sum into [B, N, d].
 cudaError_t launch_combine(const float* y_rows, const int* idx, const float* w, const Shape& s,
                            const Workspace& ws, float* out, void* out16, cudaStream_t st);

@@ -14,7 +14,7 @@ from . import LayerConfig, MoEArgs, check, lib
 
 
 def _t16(cfg: LayerConfig):
-    return torch.bfloat16 if cfg.bf16 else torch.float16
+    return torch.bfloat16 if cfg.act_bf16 else torch.float16
 
 
 class MoeLayer:
@@ -32,7 +32,7 @@ class MoeLayer:
         z = lambda *s, dt: torch.empty(*s, dtype=dt, device=dev)  # noqa: E731
         self.x = z(max(T, 1), d, dt=t16)
         self.wr = z(d, E, dt=torch.float32 if cfg.router_f32 else t16)
-        wt = torch.int8 if cfg.int8 else t16
+        wt = torch.int8 if cfg.int8 else (torch.uint8 if cfg.fp8 else t16)
         self.wg = z(E, d, f, dt=wt)
         self.wu = z(E, d, f, dt=wt)
         self.wd = z(E, f, d, dt=wt)
@@ -63,12 +63,15 @@ class MoeLayer:
         if self.cfg.T > 0:
             put(self.x, inputs["x"])
         put(self.wr, inputs["wr"])
-        sfx = "_q" if self.cfg.int8 else ""
+        sfx = "_q" if (self.cfg.int8 or self.cfg.fp8) else ""
         put(self.wg, inputs["wg" + sfx])
         put(self.wu, inputs["wu" + sfx])
         put(self.wd, inputs["wd" + sfx])
         if self.cfg.int8:
             self.scales = {k: inputs[k] for k in ("s_in", "s_gate", "s_up", "s_mid", "s_down")}
+        if self.cfg.fp8:
+            self.wscale = [torch.from_numpy(np.ascontiguousarray(inputs[k])).to(self.device)
+                           for k in ("sg", "su", "sd")]
         if inputs.get("bias") is not None:
             self.bias = torch.from_numpy(inputs["bias"]).to(self.device)
         return self
@@ -79,7 +82,13 @@ class MoeLayer:
         p = lambda t: None if t is None else t.data_ptr()  # noqa: E731
         a.input = p(self.x)
         a.router_weights = p(self.wr)
-        if self.cfg.int8:
+        if self.cfg.fp8:
+            a.expert_up_proj_weights_fp8 = p(self.wu)
+            a.expert_gate_proj_weights_fp8 = p(self.wg)
+            a.expert_down_proj_weights_fp8 = p(self.wd)
+            a.per_expert_wmma_inputs_fp8 = p(self.a_rows)
+            a.hidden_mlp_layer_1_out_fp8 = p(self.h_rows)
+        elif self.cfg.int8:
             a.expert_up_proj_weights_int8 = p(self.wu)
             a.expert_gate_proj_weights_int8 = p(self.wg)
             a.expert_down_proj_weights_int8 = p(self.wd)
@@ -108,8 +117,9 @@ class MoeLayer:
         return a
 
     def dims(self):
+        ws = tuple(t.data_ptr() for t in self.wscale) if self.cfg.fp8 else (None, None, None)
         return self.cfg.dims(None if self.bias is None else self.bias.data_ptr(),
-                             None if self.out16 is None else self.out16.data_ptr())
+                             None if self.out16 is None else self.out16.data_ptr(), w_scales=ws)
 
     def forward(self, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
         """Enqueues one layer call on `stream` (default: torch's current stream)."""

@@ -120,3 +120,24 @@ def test_nan_and_tie_semantics():
     for t in (0, 2, 3):
         if 6 in r["idx"][t]:
             assert 3 in r["idx"][t] and list(r["idx"][t]).index(3) < list(r["idx"][t]).index(6)
+
+
+def test_e4m3_encoder_matches_product_quantiser():
+    """The oracle's e4m3 rounding (restated from the format) agrees with the
+    library's block quantiser on random blocks, including saturation at 448
+    and subnormals."""
+    rng = np.random.default_rng(1)
+    w = (rng.standard_normal((2, 256, 128)) * np.array([1e-4, 1.0])[:, None, None]).astype(np.float32)
+    w[0, 0, 0] = 0.0
+    w[1, 5, 7] = -3.0e4
+    b16 = (w.view(np.uint32) >> 16).astype(np.uint16)       # truncate to bf16 bit patterns
+    q, sc = sm.quantize_fp8_blocks(b16, bf16=True)
+    vals = (b16.astype(np.uint32) << 16).view(np.float32)
+    L = O.lib()
+    for e in range(2):
+        for kb in range(2):
+            blk = vals[e, kb * 128:(kb + 1) * 128, :] / sc[e, kb, 0]
+            enc = np.array([L.oracle_e4m3(float(v)) for v in blk.reshape(-1)], np.uint8)
+            assert np.array_equal(enc, q[e, kb * 128:(kb + 1) * 128, :].reshape(-1))
+    assert L.oracle_e4m3(1000.0) == 0x7E and L.oracle_e4m3(-1000.0) == 0xFE
+    assert L.oracle_e4m3_decode(0x7E) == 448.0 and L.oracle_e4m3_decode(0x01) == 2.0 ** -9
