@@ -43,6 +43,11 @@ def workload(name: str):
         "small_fp16": sm.LayerConfig(1, 512, 1024, 2048, 8, 2, 1.25, dtype=sm.DTYPE_F16),
         # Mixtral weights with one 2048-token batch: the small case for ncu captures.
         "mixtral_t2048": sm.LayerConfig(1, 2048, 4096, 14336, 8, 2, 1.25, dtype=sm.DTYPE_BF16),
+        # BASELINE configs[2] shape in the reference's int8 format (per-tensor int8 weights and
+        # activations, kernels/capacity_int8_ptx.cu), Zipf(1.1) router bias so hot experts drop routes.
+        "int8_cfg3": sm.LayerConfig(1, 16384, 2048, 1408, 64, 6, 1.0, dtype=sm.DTYPE_INT8, zipf_s=1.1),
+        # FP8 e4m3, 128x128 weight / 1x128 activation block scales.
+        "fp8_cfg4": sm.LayerConfig(1, 32768, 2048, 768, 128, 8, 1.25, dtype=sm.DTYPE_FP8_BLOCK),
     }
     return table[name]
 
@@ -55,11 +60,18 @@ def load_peaks():
     return FALLBACK_PEAKS, "fallback"
 
 
+def dtype_name(cfg):
+    return "int8" if cfg.int8 else ("fp8_e4m3_block" if cfg.fp8 else ("bf16" if cfg.bf16 else "f16"))
+
+
 def cfg_json(name, cfg, cap):
+    wb = 1 if (cfg.int8 or cfg.fp8) else 2
+    xb = cfg.T * cfg.d_model * 2 / 1e6
+    wmb = 3 * cfg.num_experts * cfg.d_model * cfg.d_ff * wb / 1e9
     return {"workload": name, "num_batches": cfg.num_batches, "tokens_per_batch": cfg.tokens,
             "tokens": cfg.T, "d_model": cfg.d_model, "d_ff": cfg.d_ff, "experts": cfg.num_experts,
-            "top_k": cfg.top_k, "capacity_factor": cfg.capacity_factor, "cap": cap,
-            "l2": "inputs larger than L2 (x 134 MB, weights 2.8 GB; no flush needed)"}
+            "top_k": cfg.top_k, "capacity_factor": cfg.capacity_factor, "cap": cap, "zipf_s": cfg.zipf_s,
+            "l2": f"inputs larger than L2 (x {xb:.0f} MB, weights {wmb:.2f} GB; no flush needed)"}
 
 
 # ---------------------------------------------------------------------------
@@ -146,6 +158,12 @@ def device_inputs(layer, seed: int):
     ~ N(0,0.02), gate/up ~ N(0,1/sqrt(d)), down ~ N(0,1/sqrt(f)))."""
     import torch
     cfg = layer.cfg
+    if cfg.int8 or cfg.fp8 or cfg.zipf_s > 0:
+        # quantised formats: seeded host generator + the library's host quantisers
+        import sparsemoe_b200 as sm
+        layer.host_inputs = sm.make_inputs(cfg, seed)
+        layer.load(layer.host_inputs)
+        return
     g = torch.Generator(device=layer.device)
     g.manual_seed(seed)
     for t, std in ((layer.x, 1.0), (layer.wr, 0.02), (layer.wg, cfg.d_model ** -0.5),
@@ -161,6 +179,23 @@ def cpu_measure(layer, sample_tokens: int, nthreads: int):
     import torch
     from oracle import oracle as O
     cfg = layer.cfg
+    if getattr(layer, "host_inputs", None) is not None:
+        inp = layer.host_inputs
+        t0 = time.perf_counter()
+        r = O.route(inp["x"], inp["wr"], inp["bias"], cfg.num_batches, cfg.tokens, cfg.d_model, cfg.num_experts,
+                    cfg.top_k, layer.cap, cfg.act_bf16, cfg.router_f32, nthreads)
+        t_route = time.perf_counter() - t0
+        S = min(sample_tokens, cfg.T)
+        fn = O.ffn_combine_fp8 if cfg.fp8 else (O.ffn_combine_int8 if cfg.int8 else None)
+        t0 = time.perf_counter()
+        if fn is not None:
+            fn(inp["x"], inp, cfg, r["idx"], r["w"], r["route_slot"], 0, S, nthreads)
+        else:
+            O.ffn_combine(inp["x"], inp["wg"], inp["wu"], inp["wd"], cfg.num_batches, cfg.tokens, cfg.d_model,
+                          cfg.d_ff, cfg.num_experts, cfg.top_k, cfg.bf16, r["idx"], r["w"], r["route_slot"], 0, S,
+                          nthreads)
+        t_ffn = time.perf_counter() - t0
+        return S / (t_ffn + t_route * S / cfg.T), t_route, t_ffn, S
     u16 = lambda t: t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)  # noqa: E731
     x, wg, wu, wd = u16(layer.x), u16(layer.wg), u16(layer.wu), u16(layer.wd)
     wr = layer.wr.cpu().numpy() if cfg.router_f32 else u16(layer.wr)
@@ -209,7 +244,7 @@ def run_reference_arm(args, ws, rank, local):
         "impl": "reference", "metric": f"MoE-layer tokens/s ({args.config})", "value": value,
         "unit": "tokens/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1000.0 * wall / args.steps, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "bf16" if cfg.bf16 else "f16", "data": "synthetic",
+        "vs_baseline": None, "dtype": dtype_name(cfg), "data": "synthetic",
         "config": cfg_json(args.config, cfg, layer.cap),
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": nthreads, "kind": "port",
                          "sample": sample},
@@ -406,6 +441,10 @@ def main():
     # ---- roofline of the dominant kernel (up/gate GEMM with fused SwiGLU) --
     peaks, peak_src = load_peaks()
     peak_tf = float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
+    peak_note = f"{peak_src} bf16_tflops_sustained (cuBLAS bf16, power-capped loop)"
+    if cfg.int8 or cfg.fp8:
+        peak_tf *= 2.0   # dense int8 / fp8 tensor rate is twice bf16 on B200
+        peak_note = f"2 x {peak_src} bf16_tflops_sustained (dense 8-bit rate = 2x bf16; no 8-bit peak measured)"
     d, f = cfg.d_model, cfg.d_ff
     flop_up = 4.0 * d * f * kept            # gate + up, kept routes only
     flop_down = 2.0 * d * f * kept
@@ -425,14 +464,14 @@ def main():
         "metric": f"MoE-layer tokens/s ({args.config})", "value": ws * cfg.T / (ms * 1e-3),
         "unit": "tokens/s", "n_gpus": ws, "steps": K, "warmup": args.warmup, "ms_per_step": ms,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "bf16" if cfg.bf16 else "f16",
-        "data": "synthetic (seeded torch normal: x N(0,1), router N(0,0.02), W N(0,1/sqrt(fan_in)))",
+        "dtype": dtype_name(cfg),
+        "data": "synthetic (seeded normal: x N(0,1), router N(0,0.02), W N(0,1/sqrt(fan_in)))",
         "config": {**cfg_json(args.config, cfg, layer.cap),
                    "parallelism": "single GPU" if ws == 1 else f"{ws} independent replicas (no data-path collective)"},
         "roofline": {"bound": "tensor", "achieved": ach_up, "peak": peak_tf, "unit": "TFLOP/s",
                      "frac": ach_up / peak_tf, "traffic": traffic,
                      "kernel": "expert_up_gate_gemm (tcgen05, fused SwiGLU)",
-                     "peak_source": f"{peak_src} bf16_tflops_sustained (cuBLAS bf16, power-capped loop)"},
+                     "peak_source": peak_note},
         "stages_ms": stage_ms,
         "stage_tflops": {"expert_up_gate_gemm": ach_up, "expert_down_gemm": ach_down,
                          "layer_alg": (flop_up + flop_down + flop_router) / (ms * 1e-3) / 1e12},

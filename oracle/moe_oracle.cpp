@@ -155,7 +155,9 @@ void oracle_route(const uint16_t* x, const void* wr, int router_f32, const float
         const uint16_t* w16 = (const uint16_t*)wr;
         for (size_t i = 0; i < (size_t)d * E; ++i) wrf[i] = to_f32(w16[i], bf16);
     }
-    // capacity.cu:13-142 (router GEMM) in the fixed order the GPU router uses:
+    // capacity.cu:13-142 (router GEMM) in the fixed order the GPU router uses.
+    // E >= 64: per (token, expert) a sequential fmaf chain over j from 0.0f.
+    // E < 64:
     // lane l (0..31) accumulates, with fmaf from 0.0f, the 8-element chunks
     // c = l, l+32, ... (elements 8c..8c+7) in ascending j; the 32 partials
     // are combined by the xor butterfly p[l] = p[l] + p[l^off], off = 16..1;
@@ -166,6 +168,12 @@ void oracle_route(const uint16_t* x, const void* wr, int router_f32, const float
         for (int64_t t = blk * 64; t < std::min<int64_t>(T, blk * 64 + 64); ++t) {
             for (int j = 0; j < d; ++j) xr[j] = to_f32(x[t * d + j], bf16);
             for (int e = 0; e < E; ++e) {
+                if (E >= 64) {   // many experts: one sequential fmaf chain (GPU router_tiled_kernel)
+                    float acc = 0.0f;
+                    for (int j = 0; j < d; ++j) acc = fmaf(xr[j], wrf[(size_t)j * E + e], acc);
+                    logits[t * E + e] = bias ? acc + bias[e] : acc;
+                    continue;
+                }
                 for (int l = 0; l < 32; ++l) {
                     float acc = 0.0f;
                     for (int c = l; c < d / 8; c += 32)

@@ -16,7 +16,8 @@
 //   warp 1      MMA issuer: per K block 4 x tcgen05.mma kind::f8f6f4 M128
 //               N256 K32 into TMEM partial P[kb & 1].
 //   warps 2-9   promotion + epilogue: warp w reads TMEM lanes 32*(w%4).. and
-//               half (w-2)/4 of the columns:
+//               half (w-2)/4 of the columns (16-column TMEM loads keep the
+//               128 accumulators within the 168 registers a thread gets):
 //                 up/gate: gate cols [64h, 64h+64) and up cols 128+[64h, ..)
 //                 of the same 64 output features, so SwiGLU is local; the h
 //                 row block of 128 features (the tile) gets its 1x128 scale
@@ -232,32 +233,37 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int i = 0; i < 128; ++i) acc[i] = 0.0f;
             bool ok = true;
+            // scales of K block kb+1 are loaded while block kb is promoted
+            auto wscale = [&](const float* base, int kb, int col) {
+                return base[((int64_t)wexp * nkb + kb) * nblk + col];
+            };
+            const int wcol = kMode == 0 ? n : 2 * n + half;
+            float sa_n = arow[0];
+            float sw0_n = wscale(p.w_scale0, 0, wcol);
+            float sw1_n = kMode == 0 ? wscale(p.w_scale1, 0, wcol) : sw0_n;
             for (int kb = 0; kb < nkb; ++kb) {
-                const float sa = arow[kb];
-                float sw0, sw1;
-                if (kMode == 0) {
-                    sw0 = p.w_scale0[((int64_t)wexp * nkb + kb) * nblk + n];
-                    sw1 = p.w_scale1[((int64_t)wexp * nkb + kb) * nblk + n];
-                } else {
-                    sw0 = p.w_scale0[((int64_t)wexp * nkb + kb) * nblk + 2 * n + half];
-                    sw1 = sw0;
+                const float sa = sa_n, sw0 = sw0_n, sw1 = sw1_n;
+                if (kb + 1 < nkb) {
+                    sa_n = arow[kb + 1];
+                    sw0_n = wscale(p.w_scale0, kb + 1, wcol);
+                    sw1_n = kMode == 0 ? wscale(p.w_scale1, kb + 1, wcol) : sw0_n;
                 }
                 if (!mbar_wait(&pfull[pb], pph, p.status, kDevErrTimeout)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + pb * 256;
                 const float sc0 = sa * sw0, sc1 = sa * sw1;
 #pragma unroll
-                for (int piece = 0; piece < 4; ++piece) {
-                    uint32_t r[32];
-                    const int col = kMode == 0 ? (piece < 2 ? 64 * half + 32 * piece : 128 + 64 * half + 32 * (piece - 2))
-                                               : 128 * half + 32 * piece;
-                    tmem_ld_32x32b_x32(tbase + col, r);
+                for (int piece = 0; piece < 8; ++piece) {
+                    uint32_t r[16];
+                    const int col = kMode == 0 ? (piece < 4 ? 64 * half + 16 * piece : 128 + 64 * half + 16 * (piece - 4))
+                                               : 128 * half + 16 * piece;
+                    tmem_ld_32x32b_x16(tbase + col, r);
                     tmem_wait_ld();
-                    if (piece == 3) { tc_fence_before(); mbar_arrive(&pempty[pb]); }
-                    const float sc = (kMode == 0 && piece >= 2) ? sc1 : sc0;
+                    if (piece == 7) { tc_fence_before(); mbar_arrive(&pempty[pb]); }
+                    const float sc = (kMode == 0 && piece >= 4) ? sc1 : sc0;
 #pragma unroll
-                    for (int i = 0; i < 32; i += 2)
-                        ffma2(acc[32 * piece + i], acc[32 * piece + i + 1], __uint_as_float(r[i]),
+                    for (int i = 0; i < 16; i += 2)
+                        ffma2(acc[16 * piece + i], acc[16 * piece + i + 1], __uint_as_float(r[i]),
                               __uint_as_float(r[i + 1]), sc);
                 }
                 pb ^= 1;

@@ -11,6 +11,10 @@ namespace moe {
 // Routes per dispatch chunk: the unit of the deterministic slot scan.
 constexpr int kChunkRoutes = 1024;
 
+// Experts from which the router switches to its register-tiled kernel and
+// the sequential-j logit order (the oracle follows the same rule).
+constexpr int kRouterTiledMinExperts = 64;
+
 // Error codes the kernels write to the device status word.
 constexpr int kDevErrTimeout = 1;
 

@@ -3,12 +3,14 @@
 // Reference semantics: kernels/capacity.cu:13-142 (router GEMM, fp32 result)
 // and :171-238 (top_k_gating).  Differences by design:
 //  * logits use a fixed fp32 order (the reference's WMMA order is
-//    unspecified) that the CPU oracle reproduces bit for bit:
+//    unspecified) that the CPU oracle reproduces bit for bit.  For E < 64:
 //      lane l (0..31) owns the 8-element chunks c = l, l+32, l+64, ... of the
 //      d-dimension (elements 8c..8c+7) and accumulates them in ascending j
 //      with fmaf, starting at 0.0f;  the 32 partial sums are then combined by
 //      an xor butterfly  p[l] = p[l] + p[l ^ off]  for off = 16, 8, 4, 2, 1;
 //      logit = p[0] (+ bias[e], one rounded add);
+//    for E >= 64 (router_tiled_kernel): one sequential fmaf chain over
+//    j = 0..d-1 from 0.0f per (token, expert), then + bias[e];
 //  * top-k is a k-round warp argmax over (value desc, index asc), the same
 //    selection as the reference's insertion sort with strict '>' (ties go to
 //    the lower expert index; values <= -1e20 and NaN are never selected;
@@ -45,6 +47,46 @@ __device__ __forceinline__ void load_wr8(const TW* __restrict__ p, float (&w)[8]
             w[2 * q] = f.x;
             w[2 * q + 1] = f.y;
         }
+    }
+}
+
+
+// k-round warp argmax over (value desc, index asc) -- the reference's
+// insertion top-k with strict '>' -- then the softmax over the k kept values,
+// w_l = exp(v_l - v_0) / (sum + 1e-10).  Lane l owns experts l, l+32, ...
+__device__ __forceinline__ void topk_softmax_warp(const float* row, int E, int k, int64_t t, int* __restrict__ idx,
+                                                  float* __restrict__ wts, int lane) {
+    const int per_lane = (E + 31) / 32;  // <= 8
+    uint32_t taken = 0;
+    float my_v = -1e20f;
+    int my_i = -1;
+    for (int l = 0; l < k; ++l) {
+        float bv = 0.0f;
+        int bi = -1;
+        for (int q = 0; q < per_lane; ++q) {
+            const int e = lane + 32 * q;
+            if (e < E && !(taken & (1u << q))) {
+                const float v = row[e];
+                if (v > -1e20f && (bi < 0 || v > bv)) { bv = v; bi = e; }
+            }
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+            if (oi >= 0 && (bi < 0 || ov > bv || (ov == bv && oi < bi))) { bv = ov; bi = oi; }
+        }
+        if (bi < 0) break;  // fewer than k selectable experts: the rest keep the sentinel
+        if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+        if (lane == l) { my_v = bv; my_i = bi; }
+    }
+    const float mx = __shfl_sync(0xffffffffu, my_v, 0);
+    const float ex = (lane < k) ? expf(my_v - mx) : 0.0f;
+    float sum = 0.0f;
+    for (int l = 0; l < k; ++l) sum += __shfl_sync(0xffffffffu, ex, l);
+    if (lane < k) {
+        idx[t * k + lane] = my_i;
+        wts[t * k + lane] = ex / (sum + 1e-10f);
     }
 }
 
@@ -114,45 +156,106 @@ __global__ void __launch_bounds__(kWarps * 32) router_topk_kernel(
     }
     __syncwarp();
 
-    const int per_lane = (E + 31) / 32;  // <= 8
     for (int tt = 0; tt < kTT; ++tt) {
         const int64_t t = t0 + tt;
         if (t >= T) break;
         const float* row = lg + tt * E;
         if (logits != nullptr)
             for (int e = lane; e < E; e += 32) logits[t * E + e] = row[e];
-        uint32_t taken = 0;
-        float my_v = -1e20f;
-        int my_i = -1;
-        for (int l = 0; l < k; ++l) {
-            float bv = 0.0f;
-            int bi = -1;
-            for (int q = 0; q < per_lane; ++q) {
-                const int e = lane + 32 * q;
-                if (e < E && !(taken & (1u << q))) {
-                    const float v = row[e];
-                    if (v > -1e20f && (bi < 0 || v > bv)) { bv = v; bi = e; }
+        topk_softmax_warp(row, E, k, t, idx, wts, lane);
+    }
+}
+
+// Many experts (E >= kTiledMinExperts): a register-tiled CUDA-core GEMM.  The
+// f32 order is then per (token, expert) one sequential fmaf chain over
+// j = 0..d-1 from 0.0f (+ bias[e]), which the oracle mirrors.  CTA = 16*MT
+// tokens x all E experts, 2E threads; thread (r, c) owns tokens MT*r.. and
+// experts 8c..8c+7 (MT=8: 64 accumulators, 4 vector shared loads per 64 FMAs); x and
+// Wr K-slices of 32 are staged in shared memory as f32 (x transposed).
+constexpr int kTiledKC = 32;
+
+template <typename TX, typename TW, int MT>   // MT tokens per thread (8, or 4 for small grids)
+__global__ void __launch_bounds__(512) router_tiled_kernel(
+    const TX* __restrict__ x, const TW* __restrict__ wr, const float* __restrict__ bias, int64_t T, int d, int E,
+    int k, float* __restrict__ logits, int* __restrict__ idx, float* __restrict__ wts) {
+    constexpr int kTiledTM = 16 * MT;
+    extern __shared__ float sm[];
+    float* xs = sm;                          // [kTiledKC][kTiledTM]
+    float* ws = xs + kTiledKC * kTiledTM;    // [kTiledKC][E]
+    float* lg = ws;                          // after the K loop: [kTiledTM][E]
+    const int nthr = blockDim.x;
+    const int cgroups = E / 8;
+    const int r = threadIdx.x / cgroups, c = threadIdx.x - (threadIdx.x / cgroups) * cgroups;
+    const int64_t t0 = (int64_t)blockIdx.x * kTiledTM;
+    float acc[MT][8];
+#pragma unroll
+    for (int i = 0; i < MT; ++i)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[i][e] = 0.0f;
+    for (int j0 = 0; j0 < d; j0 += kTiledKC) {
+        for (int v = threadIdx.x; v < kTiledTM * (kTiledKC / 8); v += nthr) {
+            const int tt = v / (kTiledKC / 8), jv = v - tt * (kTiledKC / 8);
+            const int64_t t = t0 + tt;
+            float f8[8];
+            if (t < T) {
+                const uint4 raw = __ldg(reinterpret_cast<const uint4*>(x + t * d + j0 + jv * 8));
+                const uint32_t* u = reinterpret_cast<const uint32_t*>(&raw);
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const float2 p = F16Traits<TX>::unpack2(u[q]);
+                    f8[2 * q] = p.x;
+                    f8[2 * q + 1] = p.y;
                 }
+            } else {
+#pragma unroll
+                for (int q = 0; q < 8; ++q) f8[q] = 0.0f;
             }
 #pragma unroll
-            for (int off = 16; off > 0; off >>= 1) {
-                const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
-                const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
-                if (oi >= 0 && (bi < 0 || ov > bv || (ov == bv && oi < bi))) { bv = ov; bi = oi; }
+            for (int q = 0; q < 8; ++q) xs[(jv * 8 + q) * kTiledTM + tt] = f8[q];
+        }
+        for (int v = threadIdx.x; v < kTiledKC * cgroups; v += nthr) {
+            const int jj = v / cgroups, cc = v - jj * cgroups;
+            float w8[8];
+            load_wr8(wr + (int64_t)(j0 + jj) * E + 8 * cc, w8);
+            float4* dst = reinterpret_cast<float4*>(ws + jj * E + 8 * cc);
+            dst[0] = make_float4(w8[0], w8[1], w8[2], w8[3]);
+            dst[1] = make_float4(w8[4], w8[5], w8[6], w8[7]);
+        }
+        __syncthreads();
+#pragma unroll 4
+        for (int jj = 0; jj < kTiledKC; ++jj) {
+            const float4 wa = *reinterpret_cast<const float4*>(ws + jj * E + 8 * c);
+            const float4 wb = *reinterpret_cast<const float4*>(ws + jj * E + 8 * c + 4);
+            const float wv[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+            float xv[MT];
+#pragma unroll
+            for (int i = 0; i < MT; i += 4) {
+                const float4 xa = *reinterpret_cast<const float4*>(xs + jj * kTiledTM + MT * r + i);
+                xv[i] = xa.x; xv[i + 1] = xa.y; xv[i + 2] = xa.z; xv[i + 3] = xa.w;
             }
-            if (bi < 0) break;  // fewer than k selectable experts: the rest keep the sentinel
-            if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
-            if (lane == l) { my_v = bv; my_i = bi; }
+#pragma unroll
+            for (int i = 0; i < MT; ++i)
+#pragma unroll
+                for (int e = 0; e < 8; ++e) acc[i][e] = fmaf(xv[i], wv[e], acc[i][e]);
         }
-        // Softmax over the k kept values: w_l = exp(v_l - v_0) / (sum + 1e-10).
-        const float mx = __shfl_sync(0xffffffffu, my_v, 0);
-        const float ex = (lane < k) ? expf(my_v - mx) : 0.0f;
-        float sum = 0.0f;
-        for (int l = 0; l < k; ++l) sum += __shfl_sync(0xffffffffu, ex, l);
-        if (lane < k) {
-            idx[t * k + lane] = my_i;
-            wts[t * k + lane] = ex / (sum + 1e-10f);
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < MT; ++i)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            const int ee = 8 * c + e;
+            lg[(MT * r + i) * E + ee] = bias ? __fadd_rn(acc[i][e], bias[ee]) : acc[i][e];
         }
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = nthr >> 5;
+    for (int tt = warp; tt < kTiledTM; tt += nwarps) {
+        const int64_t t = t0 + tt;
+        if (t >= T) break;
+        const float* row = lg + tt * E;
+        if (logits != nullptr)
+            for (int e = lane; e < E; e += 32) logits[t * E + e] = row[e];
+        topk_softmax_warp(row, E, k, t, idx, wts, lane);
     }
 }
 
@@ -171,6 +274,30 @@ cudaError_t launch_typed(const void* x, const void* wr, const float* bias, const
     return cudaGetLastError();
 }
 
+template <typename TX, typename TW, int MT>
+cudaError_t launch_tiled(const void* x, const void* wr, const float* bias, const Shape& s, float* logits, int* idx,
+                         float* w, cudaStream_t st) {
+    constexpr int kTiledTM = 16 * MT;
+    const int threads = 2 * s.E;
+    const size_t smem = sizeof(float) * ((size_t)kTiledKC * kTiledTM + (size_t)std::max(kTiledKC, kTiledTM) * s.E);
+    auto kern = router_tiled_kernel<TX, TW, MT>;
+    cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (err != cudaSuccess) return err;
+    const int64_t blocks = (s.T() + kTiledTM - 1) / kTiledTM;
+    kern<<<(unsigned)blocks, threads, smem, st>>>((const TX*)x, (const TW*)wr, bias, s.T(), s.d, s.E, s.k, logits,
+                                                  idx, w);
+    return cudaGetLastError();
+}
+
+template <typename TX, typename TW>
+cudaError_t launch_any(const void* x, const void* wr, const float* bias, const Shape& s, float* logits, int* idx,
+                       float* w, cudaStream_t st) {
+    if (s.E < kRouterTiledMinExperts) return launch_typed<TX, TW>(x, wr, bias, s, logits, idx, w, st);
+    // less than one CTA of 128 tokens per SM: halve the tokens per thread
+    return s.T() >= (int64_t)128 * 148 ? launch_tiled<TX, TW, 8>(x, wr, bias, s, logits, idx, w, st)
+                                       : launch_tiled<TX, TW, 4>(x, wr, bias, s, logits, idx, w, st);
+}
+
 }  // namespace
 
 cudaError_t launch_router_topk(const void* x, const void* wr, const float* bias, const Shape& s,
@@ -178,11 +305,11 @@ cudaError_t launch_router_topk(const void* x, const void* wr, const float* bias,
     if (s.T() == 0) return cudaSuccess;
     const bool bf = s.act_bf16;
     if (s.router_dtype == MOE_ROUTER_F32) {
-        return bf ? launch_typed<__nv_bfloat16, float>(x, wr, bias, s, logits, idx, w, st)
-                  : launch_typed<__half, float>(x, wr, bias, s, logits, idx, w, st);
+        return bf ? launch_any<__nv_bfloat16, float>(x, wr, bias, s, logits, idx, w, st)
+                  : launch_any<__half, float>(x, wr, bias, s, logits, idx, w, st);
     }
-    return bf ? launch_typed<__nv_bfloat16, __nv_bfloat16>(x, wr, bias, s, logits, idx, w, st)
-              : launch_typed<__half, __half>(x, wr, bias, s, logits, idx, w, st);
+    return bf ? launch_any<__nv_bfloat16, __nv_bfloat16>(x, wr, bias, s, logits, idx, w, st)
+              : launch_any<__half, __half>(x, wr, bias, s, logits, idx, w, st);
 }
 
 }  // namespace moe

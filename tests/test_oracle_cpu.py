@@ -141,3 +141,18 @@ def test_e4m3_encoder_matches_product_quantiser():
             assert np.array_equal(enc, q[e, kb * 128:(kb + 1) * 128, :].reshape(-1))
     assert L.oracle_e4m3(1000.0) == 0x7E and L.oracle_e4m3(-1000.0) == 0xFE
     assert L.oracle_e4m3_decode(0x7E) == 448.0 and L.oracle_e4m3_decode(0x01) == 2.0 ** -9
+
+
+def test_logit_order_many_experts_is_sequential():
+    """E >= 64: one sequential fmaf chain over j per (token, expert), then + bias."""
+    cfg = sm.LayerConfig(1, 3, 256, 128, 64, 2, 1.0, zipf_s=1.0)
+    inp = sm.make_inputs(cfg, 2)
+    r = O.route(inp["x"], inp["wr"], inp["bias"], 1, 3, 256, 64, 2, 16, False)
+    x = inp["x"].view(np.float16).astype(np.float64)
+    w = inp["wr"].view(np.float16).astype(np.float64)
+    for t in range(3):
+        for e in (0, 17, 63):
+            acc = np.float32(0)
+            for j in range(256):
+                acc = np.float32(np.float64(acc) + x[t, j] * w[j, e])   # exact product + one rounding
+            assert np.float32(acc + inp["bias"][e]) == r["logits"][t, e]
