@@ -48,6 +48,12 @@ def workload(name: str):
         "int8_cfg3": sm.LayerConfig(1, 16384, 2048, 1408, 64, 6, 1.0, dtype=sm.DTYPE_INT8, zipf_s=1.1),
         # FP8 e4m3, 128x128 weight / 1x128 activation block scales.
         "fp8_cfg4": sm.LayerConfig(1, 32768, 2048, 768, 128, 8, 1.25, dtype=sm.DTYPE_FP8_BLOCK),
+        # BASELINE configs[4], one GPU's share under 8-way expert parallelism: 32 experts, top-8 over them
+        # gives the same per-GPU routes and CAP as the global 256-expert routing (decode 160, prefill 2560).
+        "w4_cfg5_decode": sm.LayerConfig(1, 512, 7168, 2048, 32, 8, 1.25, dtype=sm.DTYPE_W4A16, router_f32=True,
+                                         zipf_s=1.0),
+        "w4_cfg5_prefill": sm.LayerConfig(1, 8192, 7168, 2048, 32, 8, 1.25, dtype=sm.DTYPE_W4A16, router_f32=True,
+                                          zipf_s=1.0),
     }
     return table[name]
 
@@ -61,11 +67,13 @@ def load_peaks():
 
 
 def dtype_name(cfg):
+    if cfg.w4:
+        return "int4_g128_weights_bf16_act"
     return "int8" if cfg.int8 else ("fp8_e4m3_block" if cfg.fp8 else ("bf16" if cfg.bf16 else "f16"))
 
 
 def cfg_json(name, cfg, cap):
-    wb = 1 if (cfg.int8 or cfg.fp8) else 2
+    wb = 0.5 if cfg.w4 else (1 if (cfg.int8 or cfg.fp8) else 2)
     xb = cfg.T * cfg.d_model * 2 / 1e6
     wmb = 3 * cfg.num_experts * cfg.d_model * cfg.d_ff * wb / 1e9
     return {"workload": name, "num_batches": cfg.num_batches, "tokens_per_batch": cfg.tokens,
@@ -158,7 +166,7 @@ def device_inputs(layer, seed: int):
     ~ N(0,0.02), gate/up ~ N(0,1/sqrt(d)), down ~ N(0,1/sqrt(f)))."""
     import torch
     cfg = layer.cfg
-    if cfg.int8 or cfg.fp8 or cfg.zipf_s > 0:
+    if cfg.int8 or cfg.fp8 or cfg.w4 or cfg.zipf_s > 0:
         # quantised formats: seeded host generator + the library's host quantisers
         import sparsemoe_b200 as sm
         layer.host_inputs = sm.make_inputs(cfg, seed)
@@ -186,7 +194,8 @@ def cpu_measure(layer, sample_tokens: int, nthreads: int):
                     cfg.top_k, layer.cap, cfg.act_bf16, cfg.router_f32, nthreads)
         t_route = time.perf_counter() - t0
         S = min(sample_tokens, cfg.T)
-        fn = O.ffn_combine_fp8 if cfg.fp8 else (O.ffn_combine_int8 if cfg.int8 else None)
+        fn = O.ffn_combine_fp8 if cfg.fp8 else (O.ffn_combine_int8 if cfg.int8 else
+                                                (O.ffn_combine_w4 if cfg.w4 else None))
         t0 = time.perf_counter()
         if fn is not None:
             fn(inp["x"], inp, cfg, r["idx"], r["w"], r["route_slot"], 0, S, nthreads)

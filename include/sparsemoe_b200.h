@@ -28,6 +28,9 @@ extern "C" {
 #define MOE_DTYPE_FP8_BLOCK 3  // e4m3 weights with f32 scales per 128x128 block (MoeDims.w_scale_*),
                                // activations and h quantised on the fly per 1x128 block, bf16 x and
                                // router, f32 accumulate; MoEArgs *_fp8 fields
+#define MOE_DTYPE_W4A16 4      // 4-bit weights: INT4 asymmetric, group 128 along K, fp16 scale and
+                               // zero per (group, column) (MoeDims.w4_*), nibble-packed [E, K, N/2]
+                               // in the MoEArgs *_int4 fields; bf16 x, router and h
 
 // ---- router formats --------------------------------------------------------
 #define MOE_ROUTER_SAME 0   // router_weights have the activation dtype
@@ -54,6 +57,13 @@ typedef struct MoeDims {
     const float* w_scale_gate;
     const float* w_scale_up;
     const float* w_scale_down;
+    // MOE_DTYPE_W4A16 group scales and zeros (device fp16): gate/up [E, d/128, f], down [E, f/128, d]
+    const void* w4_scale_gate;
+    const void* w4_scale_up;
+    const void* w4_scale_down;
+    const void* w4_zero_gate;
+    const void* w4_zero_up;
+    const void* w4_zero_down;
 } MoeDims;
 
 // Reference: kernels/launcher.h:21 `extern "C" void solve(MoEArgs args)`.
@@ -142,6 +152,15 @@ float moe_quantize_per_tensor(const uint16_t* src_f16, size_t n, int8_t* dst, fl
 // q = e4m3(x / s) rounded to nearest even, saturating at +-448.
 // Writes q [E, K, N] (e4m3 bytes) and scales [E, K/128, N/128].
 void moe_quantize_fp8_blocks(const uint16_t* src, int E, int K, int N, int bf16, uint8_t* q, float* scales);
+
+// 4-bit asymmetric group quantiser for weights [E, K, N] (16-bit, bf16 != 0:
+// bf16): per expert, column n and group of 128 along K, s = (max - min) / 15
+// (1 if max == min), z = -min / s, both rounded to fp16; q = clamp(rint(w /
+// s + z), 0, 15) with the fp16 values; w is represented as (q - z) * s.
+// Writes packed [E, K, N/2] (even column in the low nibble) and fp16 bit
+// patterns of scales / zeros [E, K/128, N].
+void moe_quantize_int4_g128(const uint16_t* src, int E, int K, int N, int bf16, uint8_t* packed,
+                            uint16_t* scales, uint16_t* zeros);
 
 // ---- seeded input generator (the reference has none: inputs/data.cu:164-177
 //      zero-fills everything).  Counter-based, thread-count independent:

@@ -242,11 +242,13 @@ void oracle_route(const uint16_t* x, const void* wr, int router_f32, const float
 // down GEMM, then combine (capacity.cu:380-423) summing kept routes in
 // l = 0..k-1 order:  out = ((0 + w0*y0) + w1*y1) + ...
 // `out` is [B*N, d]; only rows t_begin..t_end-1 are written.
-void oracle_ffn_combine(const uint16_t* x, const uint16_t* wg, const uint16_t* wu,
-                        const uint16_t* wd, int B, int N, int d, int f, int E, int k,
-                        int bf16, const int* idx, const float* w, const int* route_slot,
-                        int64_t t_begin, int64_t t_end, float* out, int nthreads) {
-    (void)B; (void)N;
+}  // extern "C"
+
+namespace {
+template <class RowG, class RowU, class RowD>
+void ffn_impl(const uint16_t* x, RowG row_g, RowU row_u, RowD row_d, int d, int f, int E, int k, int bf16,
+              const int* idx, const float* w, const int* route_slot, int64_t t_begin, int64_t t_end, float* out,
+              int nthreads) {
     // Group the kept routes of the token range by expert.
     std::vector<std::vector<int64_t>> routes(E);
     for (int64_t t = t_begin; t < t_end; ++t)
@@ -270,16 +272,13 @@ void oracle_ffn_combine(const uint16_t* x, const uint16_t* wg, const uint16_t* w
             const int64_t tok = routes[e][r0 + r] / k;
             cvt_row(x + tok * d, &a[(size_t)r * d], d, bf16);
         }
-        const uint16_t* Wg = wg + (size_t)e * d * f;
-        const uint16_t* Wu = wu + (size_t)e * d * f;
-        const uint16_t* Wd = wd + (size_t)e * f * d;
         for (int c0 = 0; c0 < f; c0 += CT) {
             const int nc = std::min(CT, f - c0);
             std::fill(accg.begin(), accg.end(), 0.0f);
             std::fill(accu.begin(), accu.end(), 0.0f);
             for (int j = 0; j < d; ++j) {
-                cvt_row(Wg + (size_t)j * f + c0, wrow_g.data(), nc, bf16);
-                cvt_row(Wu + (size_t)j * f + c0, wrow_u.data(), nc, bf16);
+                row_g(e, j, c0, nc, wrow_g.data());
+                row_u(e, j, c0, nc, wrow_u.data());
                 for (int r = 0; r < nr; ++r) {
                     const float av = a[(size_t)r * d + j];
                     float* pg = &accg[(size_t)r * CT];
@@ -302,7 +301,7 @@ void oracle_ffn_combine(const uint16_t* x, const uint16_t* wg, const uint16_t* w
             const int nc = std::min(CT, d - c0);
             std::fill(accy.begin(), accy.end(), 0.0f);
             for (int j = 0; j < f; ++j) {
-                cvt_row(Wd + (size_t)j * d + c0, wrow_d.data(), nc, bf16);
+                row_d(e, j, c0, nc, wrow_d.data());
                 for (int r = 0; r < nr; ++r) {
                     const float hv = hbuf[(size_t)r * f + j];
                     float* py = &accy[(size_t)r * CT];
@@ -331,6 +330,49 @@ void oracle_ffn_combine(const uint16_t* x, const uint16_t* wg, const uint16_t* w
             }
         }
     });
+}
+
+}  // namespace
+
+extern "C" {
+
+void oracle_ffn_combine(const uint16_t* x, const uint16_t* wg, const uint16_t* wu,
+                        const uint16_t* wd, int B, int N, int d, int f, int E, int k,
+                        int bf16, const int* idx, const float* w, const int* route_slot,
+                        int64_t t_begin, int64_t t_end, float* out, int nthreads) {
+    (void)B; (void)N;
+    auto loader = [&](const uint16_t* W, int K, int Ncol) {
+        return [=](int e, int j, int c0, int nc, float* dst) {
+            cvt_row(W + ((size_t)e * K + j) * Ncol + c0, dst, nc, bf16);
+        };
+    };
+    ffn_impl(x, loader(wg, d, f), loader(wu, d, f), loader(wd, f, d), d, f, E, k, bf16, idx, w, route_slot, t_begin,
+             t_end, out, nthreads);
+}
+
+// 4-bit path (BASELINE config 5 weight format): weights dequantised exactly,
+// w = (q - z) * s with q the nibble of [E, K, N/2] (even column low) and s, z
+// the fp16 group values [E, K/128, N]; activations bf16; otherwise the 16-bit
+// path (h rounded to bf16, f32 down projection, route-order combine).
+void oracle_ffn_combine_w4(const uint16_t* x, const uint8_t* pg, const uint8_t* pu, const uint8_t* pd,
+                           const uint16_t* sg, const uint16_t* su, const uint16_t* sd, const uint16_t* zg,
+                           const uint16_t* zu, const uint16_t* zd, int d, int f, int E, int k, const int* idx,
+                           const float* w, const int* route_slot, int64_t t_begin, int64_t t_end, float* out,
+                           int nthreads) {
+    auto loader = [&](const uint8_t* P, const uint16_t* S, const uint16_t* Z, int K, int Ncol) {
+        return [=](int e, int j, int c0, int nc, float* dst) {
+            const size_t g = (size_t)e * (K / 128) + j / 128;
+            const uint8_t* row = P + ((size_t)e * K + j) * (Ncol / 2);
+            for (int c = 0; c < nc; ++c) {
+                const int n = c0 + c;
+                const int q = (row[n / 2] >> ((n & 1) * 4)) & 15;
+                const double sv = f16_to_f32(S[g * Ncol + n]), zv = f16_to_f32(Z[g * Ncol + n]);
+                dst[c] = (float)(((double)q - zv) * sv);
+            }
+        };
+    };
+    ffn_impl(x, loader(pg, sg, zg, d, f), loader(pu, su, zu, d, f), loader(pd, sd, zd, f, d), d, f, E, k, 1, idx, w,
+             route_slot, t_begin, t_end, out, nthreads);
 }
 
 // int8 path (reference kernels/capacity_int8_ptx.cu): per-tensor quantised

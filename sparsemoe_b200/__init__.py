@@ -29,6 +29,7 @@ DTYPE_F16 = 0
 DTYPE_BF16 = 1
 DTYPE_INT8 = 2
 DTYPE_FP8_BLOCK = 3
+DTYPE_W4A16 = 4
 ROUTER_SAME = 0
 ROUTER_F32 = 1
 
@@ -78,6 +79,8 @@ class MoeDims(ctypes.Structure):
         ("router_dtype", ctypes.c_int), ("router_bias", _p), ("output_16", _p),
         ("scratch", _p), ("scratch_bytes", ctypes.c_size_t),
         ("w_scale_gate", _p), ("w_scale_up", _p), ("w_scale_down", _p),
+        ("w4_scale_gate", _p), ("w4_scale_up", _p), ("w4_scale_down", _p),
+        ("w4_zero_gate", _p), ("w4_zero_up", _p), ("w4_zero_down", _p),
     ]
 
 
@@ -107,6 +110,7 @@ def _load() -> ctypes.CDLL:
         "moe_fill_normal_16": (None, [_p, ctypes.c_size_t, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_float,
                                       ctypes.c_int]),
         "moe_quantize_per_tensor": (ctypes.c_float, [_p, ctypes.c_size_t, _p, ctypes.c_float]),
+        "moe_quantize_int4_g128": (None, [_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _p, _p, _p]),
         "moe_quantize_fp8_blocks": (None, [_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _p, _p]),
         "moe_fill_normal_f32": (None, [_p, ctypes.c_size_t, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_float]),
         "moe_zipf_bias": (None, [_p, ctypes.c_int, ctypes.c_float, ctypes.c_float, ctypes.c_uint64]),
@@ -185,9 +189,13 @@ class LayerConfig:
         return self.dtype == DTYPE_FP8_BLOCK
 
     @property
+    def w4(self) -> bool:
+        return self.dtype == DTYPE_W4A16
+
+    @property
     def act_bf16(self) -> bool:
         """Activations (x, router, 16-bit output) are bf16."""
-        return self.dtype in (DTYPE_BF16, DTYPE_FP8_BLOCK)
+        return self.dtype in (DTYPE_BF16, DTYPE_FP8_BLOCK, DTYPE_W4A16)
 
     @property
     def int8(self) -> bool:
@@ -201,10 +209,11 @@ class LayerConfig:
         return capacity(self.tokens, self.top_k, self.num_experts, self.capacity_factor)
 
     def dims(self, router_bias_ptr: int | None = None, out16_ptr: int | None = None,
-             scratch_ptr: int | None = None, scratch_bytes: int = 0, w_scales=(None, None, None)) -> MoeDims:
+             scratch_ptr: int | None = None, scratch_bytes: int = 0, w_scales=(None, None, None),
+             w4=(None,) * 6) -> MoeDims:
         return MoeDims(self.num_batches, self.tokens, self.d_model, self.d_ff, self.num_experts, self.top_k,
                        self.capacity_factor, self.cap, self.dtype, ROUTER_F32 if self.router_f32 else ROUTER_SAME,
-                       router_bias_ptr, out16_ptr, scratch_ptr, scratch_bytes, *w_scales)
+                       router_bias_ptr, out16_ptr, scratch_ptr, scratch_bytes, *w_scales, *w4)
 
 
 def make_inputs(cfg: LayerConfig, seed: int = 0) -> dict:
@@ -225,6 +234,10 @@ def make_inputs(cfg: LayerConfig, seed: int = 0) -> dict:
         out["wr"] = normal_f32(d * E, seed, 1, 0.02).reshape(d, E)
     else:
         out["wr"] = normal16(d * E, seed, 1, 0.02, b16).reshape(d, E)
+    if cfg.w4:
+        for n in ("wg", "wu", "wd"):
+            q, sc, zr = quantize_int4_g128(out[n], bf16=True)
+            out[n + "_q"], out[n + "_s"], out[n + "_z"] = q, sc, zr
     if cfg.fp8:
         for n, key in (("wg", "sg"), ("wu", "su"), ("wd", "sd")):
             q, sc = quantize_fp8_blocks(out[n], bf16=True)
@@ -240,6 +253,19 @@ def make_inputs(cfg: LayerConfig, seed: int = 0) -> dict:
         out["s_in"] = float(np.float32(cfg.act_scale))
         out["s_mid"] = float(np.float32(cfg.mid_scale))
     return out
+
+
+def quantize_int4_g128(w16: np.ndarray, bf16: bool = True):
+    """INT4 asymmetric, group 128 along K, fp16 scale and zero per (group,
+    column); returns (packed [E, K, N/2] uint8, scales, zeros [E, K/128, N]
+    as fp16 bit patterns).  w16: [E, K, N] 16-bit bit patterns."""
+    E, K, N = w16.shape
+    w16 = np.ascontiguousarray(w16, np.uint16)
+    q = np.empty((E, K, N // 2), np.uint8)
+    sc = np.empty((E, K // 128, N), np.uint16)
+    zr = np.empty((E, K // 128, N), np.uint16)
+    lib.moe_quantize_int4_g128(w16.ctypes.data, E, K, N, int(bf16), q.ctypes.data, sc.ctypes.data, zr.ctypes.data)
+    return q, sc, zr
 
 
 def quantize_fp8_blocks(w16: np.ndarray, bf16: bool = True):
@@ -265,4 +291,5 @@ from .layer import MoeLayer  # noqa: E402  (needs `lib` above)
 
 __all__ = ["MoEArgs", "MoeDims", "LayerConfig", "MoeLayer", "make_inputs", "capacity", "lib", "check",
            "MoeError", "normal16", "normal_f32", "zipf_bias", "quantize_per_tensor", "DTYPE_F16", "DTYPE_BF16",
-           "DTYPE_INT8", "DTYPE_FP8_BLOCK", "quantize_fp8_blocks"]
+           "DTYPE_INT8", "DTYPE_FP8_BLOCK", "quantize_fp8_blocks",
+           "DTYPE_W4A16", "quantize_int4_g128"]

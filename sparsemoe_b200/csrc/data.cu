@@ -90,6 +90,48 @@ extern "C" void moe_quantize_fp8_blocks(const uint16_t* src, int E, int K, int N
             }
 }
 
+extern "C" void moe_quantize_int4_g128(const uint16_t* src, int E, int K, int N, int bf16, uint8_t* packed,
+                                       uint16_t* scales, uint16_t* zeros) {
+    auto val = [&](size_t i) -> float {
+        if (bf16) {
+            uint32_t u = (uint32_t)src[i] << 16;
+            float f;
+            std::memcpy(&f, &u, 4);
+            return f;
+        }
+        half h;
+        std::memcpy(&h, &src[i], 2);
+        return __half2float(h);
+    };
+    const int G = K / 128;
+    std::memset(packed, 0, (size_t)E * K * (N / 2));
+    for (int e = 0; e < E; ++e)
+        for (int g = 0; g < G; ++g)
+            for (int n = 0; n < N; ++n) {
+                float mn = INFINITY, mx = -INFINITY;
+                for (int i = 0; i < 128; ++i) {
+                    const float v = val(((size_t)e * K + g * 128 + i) * N + n);
+                    mn = std::fmin(mn, v);
+                    mx = std::fmax(mx, v);
+                }
+                float sc = (mx - mn) / 15.0f;
+                if (!(sc > 0.0f)) sc = 1.0f;
+                const half sh = __float2half_rn(sc);
+                const half zh = __float2half_rn(-mn / __half2float(sh));
+                const float sf = __half2float(sh), zf = __half2float(zh);
+                std::memcpy(&scales[((size_t)e * G + g) * N + n], &sh, 2);
+                std::memcpy(&zeros[((size_t)e * G + g) * N + n], &zh, 2);
+                for (int i = 0; i < 128; ++i) {
+                    const size_t k = (size_t)g * 128 + i;
+                    const float v = val(((size_t)e * K + k) * N + n);
+                    int q = (int)rintf(v / sf + zf);
+                    q = q < 0 ? 0 : (q > 15 ? 15 : q);
+                    uint8_t& b = packed[((size_t)e * K + k) * (N / 2) + n / 2];
+                    b |= (n & 1) ? (uint8_t)(q << 4) : (uint8_t)q;
+                }
+            }
+}
+
 namespace {
 
 float quant_symmetric(const std::vector<half>& src, std::vector<int8_t>& dst, float qmax) {

@@ -427,6 +427,26 @@ bool make_map_u8(CUtensorMap* map, const void* base, uint64_t inner, uint64_t ou
     return make_map(map, base, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, inner, outer, box_outer);
 }
 
+// General 2-D row-major map with an explicit box and swizzle mode.
+bool make_map_box(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes, uint64_t inner,
+                  uint64_t outer, uint32_t box_inner, uint32_t box_outer, bool swizzle128) {
+    auto fn = encode_fn();
+    if (!fn) { set_error("cuTensorMapEncodeTiled unavailable"); return false; }
+    cuuint64_t dims[2] = {inner, outer};
+    cuuint64_t strides[1] = {inner * (uint64_t)elem_bytes};
+    cuuint32_t box[2] = {box_inner, box_outer};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        set_error("cuTensorMapEncodeTiled failed (%d) for [%llu, %llu] box [%u, %u]", (int)r,
+                  (unsigned long long)outer, (unsigned long long)inner, box_outer, box_inner);
+        return false;
+    }
+    return true;
+}
+
 cudaError_t launch_expert_up_gate(const void* a_rows, const void* w_gate, const void* w_up, const Shape& s,
                                   const GroupTable& gt, int* status, const GemmScales& sc, void* h_rows,
                                   cudaStream_t st, int num_sms) {

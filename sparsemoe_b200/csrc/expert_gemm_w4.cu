@@ -1,0 +1,401 @@
+// Stage 4 with 4-bit weights (BASELINE config 5 format): INT4 asymmetric,
+// group 128 along K, fp16 scale and zero per (group, output column),
+// nibble-packed along N ([E, K, N/2] bytes, even column in the low nibble);
+// bf16 activations; f32 accumulate.
+//
+//   w(k, n) = (q(k, n) - z(k/128, n)) * s(k/128, n)
+//
+// The weights travel from HBM as nibbles (a quarter of bf16's bytes) and are
+// dequantised in shared memory by a converter warpgroup: each 64-row K stage
+// of packed nibbles becomes bf16 w = fma(q, s, -z*s) (f32, one rounding to
+// bf16) written straight into the 128B-swizzled MN-major layout the MMA
+// reads, so the tensor cores run plain kind::f16 bf16 MMAs into TMEM with no
+// per-group promotion.  (Dequantising to e4m3 instead would round every
+// weight to a 3-bit mantissa -- ~6% relative error per weight -- which the
+// 6e-2 bar of this format cannot absorb; bf16 keeps 2^-9.)
+//
+// Warps (320 threads, persistent, one CTA per SM):
+//   0      TMA: bf16 A tile (128 x 64, K-major SW128), packed B (64 K-rows x
+//          256 columns / 2), the stage's 256 fp16 scales and zeros.
+//   1      MMA: 4 x tcgen05.mma kind::f16 M128 N256 K16 per stage, double-
+//          buffered TMEM accumulators.
+//   2-5    epilogue (SwiGLU -> bf16 h, or f32 y), as the 16-bit kernel.
+//   6-9    converter: nibbles -> bf16 into the stage's B buffer, then
+//          fence.proxy.async and arrive on the stage's converted barrier.
+#include "moe_internal.h"
+#include "common.cuh"
+#include "sm100.cuh"
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+namespace moe {
+
+bool make_map_box(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes, uint64_t inner,
+                  uint64_t outer, uint32_t box_inner, uint32_t box_outer, bool swizzle128);
+
+namespace {
+
+using namespace sm100;
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;
+constexpr int kStages = 3;
+constexpr int kThreads = 320;
+constexpr int kABytes = kBM * 128;        // 16 KB
+constexpr int kBBytes = 64 * 256 * 2;     // 32 KB bf16: 4 chunks of 64 columns x 64 K-rows
+constexpr int kChunkBytes = 64 * 128;     // 8 KB
+constexpr int kPBytes = 64 * 128;         // 8 KB packed nibbles
+constexpr int kSZBytes = 512;             // 256 fp16 scales (and as many zeros)
+constexpr int kStageBytes = kABytes + kBBytes + kPBytes + 2 * kSZBytes;   // 57 KB
+constexpr int kTxBytes = kABytes + kPBytes + 2 * kSZBytes;
+constexpr int kTmemCols = 512;
+constexpr size_t kSmemBytes = 1024 + (size_t)kStages * kStageBytes + 256;
+
+struct W4Params {
+    const int* g_rows;
+    const int* g_start;
+    const int* g_weight;
+    int G;
+    int K;
+    int n_tiles;
+    int out_ld;
+    void* out;          // bf16 h (up/gate) or f32 y (down)
+    int* status;
+    uint32_t idesc;
+};
+
+struct W4Maps {
+    CUtensorMap a;          // bf16 activations [rows, K]
+    CUtensorMap p0, p1;     // packed weights [E*K, N/2] (gate, up; down uses p0)
+    CUtensorMap s0, s1;     // fp16 scales [E*K/128, N]
+    CUtensorMap z0, z1;     // fp16 zeros
+};
+
+__device__ __forceinline__ void decode_tile(int t, const int* pre, const int* mt, int G, int& g, int& m, int& n) {
+    int lo = 0, hi = G - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (pre[mid] <= t) lo = mid; else hi = mid - 1;
+    }
+    g = lo;
+    const int local = t - pre[g];
+    n = local / mt[g];
+    m = local - n * mt[g];
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+template <int kMode>  // 0: up/gate + SwiGLU -> bf16 h;  1: down -> f32 y
+__global__ void __launch_bounds__(kThreads, 1)
+    w4_gemm_kernel(const __grid_constant__ W4Maps mp, const W4Params p) {
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ int s_pre[kMaxGroups + 1];
+    __shared__ int s_mt[kMaxGroups];
+    __shared__ int s_rows[kMaxGroups];
+    __shared__ int s_start[kMaxGroups];
+    __shared__ int s_wt[kMaxGroups];
+
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* stage0 = smem;  // per stage: A | B | packed | scales | zeros
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
+    uint64_t* conv = full + kStages;
+    uint64_t* empty = conv + kStages;
+    uint64_t* tfull = empty + kStages;
+    uint64_t* tempty = tfull + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+    auto sA = [&](int s) { return stage0 + s * kStageBytes; };
+    auto sB = [&](int s) { return stage0 + s * kStageBytes + kABytes; };
+    auto sP = [&](int s) { return stage0 + s * kStageBytes + kABytes + kBBytes; };
+    auto sS = [&](int s) { return stage0 + s * kStageBytes + kABytes + kBBytes + kPBytes; };
+    auto sZ = [&](int s) { return stage0 + s * kStageBytes + kABytes + kBBytes + kPBytes + kSZBytes; };
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&conv[s], 128);
+            mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) { mbar_init(&tfull[a], 1); mbar_init(&tempty[a], 128); }
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, kTmemCols);
+        tmem_relinquish();
+    }
+    for (int g = threadIdx.x; g < p.G; g += kThreads) {
+        const int r = p.g_rows[g];
+        s_rows[g] = r;
+        s_mt[g] = (r + kBM - 1) / kBM;
+        s_start[g] = p.g_start[g];
+        s_wt[g] = p.g_weight ? p.g_weight[g] : g;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int acc = 0;
+        for (int g = 0; g < p.G; ++g) { s_pre[g] = acc; acc += s_mt[g] * p.n_tiles; }
+        s_pre[p.G] = acc;
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const int total = s_pre[p.G];
+    const int kblocks = p.K / kBK;
+    const int groups_k = p.K / 128;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int s = 0;
+            uint32_t ph = 0;
+            for (int t = blockIdx.x; t < total; t += gridDim.x) {
+                int g, m, n;
+                decode_tile(t, s_pre, s_mt, p.G, g, m, n);
+                const int a_row = s_start[g] + m * kBM;
+                const int b_row = s_wt[g] * p.K;
+                const int sz_row0 = s_wt[g] * groups_k;
+                for (int kb = 0; kb < kblocks; ++kb) {
+                    if (!mbar_wait(&empty[s], ph ^ 1u, p.status, kDevErrTimeout)) goto producer_done;
+                    mbar_arrive_expect_tx(&full[s], kTxBytes);
+                    const int k0 = kb * kBK;
+                    tma_load_2d(sA(s), &mp.a, &full[s], k0, a_row);
+                    if (kMode == 0) {
+                        tma_load_2d(sP(s), &mp.p0, &full[s], n * 64, b_row + k0);
+                        tma_load_2d(sP(s) + kPBytes / 2, &mp.p1, &full[s], n * 64, b_row + k0);
+                        tma_load_2d(sS(s), &mp.s0, &full[s], n * 128, sz_row0 + k0 / 128);
+                        tma_load_2d(sS(s) + kSZBytes / 2, &mp.s1, &full[s], n * 128, sz_row0 + k0 / 128);
+                        tma_load_2d(sZ(s), &mp.z0, &full[s], n * 128, sz_row0 + k0 / 128);
+                        tma_load_2d(sZ(s) + kSZBytes / 2, &mp.z1, &full[s], n * 128, sz_row0 + k0 / 128);
+                    } else {
+                        tma_load_2d(sP(s), &mp.p0, &full[s], n * 128, b_row + k0);
+                        tma_load_2d(sS(s), &mp.s0, &full[s], n * 256, sz_row0 + k0 / 128);
+                        tma_load_2d(sZ(s), &mp.z0, &full[s], n * 256, sz_row0 + k0 / 128);
+                    }
+                    if (++s == kStages) { s = 0; ph ^= 1u; }
+                }
+            }
+        producer_done:;
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            int s = 0, acc = 0;
+            uint32_t ph = 0, aph = 0;
+            for (int t = blockIdx.x; t < total; t += gridDim.x) {
+                if (!mbar_wait(&tempty[acc], aph ^ 1u, p.status, kDevErrTimeout)) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + acc * 256;
+                bool ok = true;
+                for (int kb = 0; kb < kblocks; ++kb) {
+                    if (!mbar_wait(&conv[s], ph, p.status, kDevErrTimeout)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t a_base = smem_u32(sA(s));
+                    const uint32_t b_base = smem_u32(sB(s));
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk) {
+                        const uint64_t adesc = smem_desc_sw128(a_base + kk * 32, 16, 1024);
+                        const uint64_t bdesc = smem_desc_sw128(b_base + kk * 16 * 128, kChunkBytes, 1024);
+                        mma_f16_ss(d_tmem, adesc, bdesc, p.idesc, (kb | kk) != 0 ? 1u : 0u);
+                    }
+                    mma_commit(&empty[s]);
+                    if (++s == kStages) { s = 0; ph ^= 1u; }
+                }
+                if (!ok) break;
+                mma_commit(&tfull[acc]);
+                acc ^= 1;
+                if (acc == 0) aph ^= 1u;
+            }
+        }
+    } else if (warp < 6) {
+        // ---------------- epilogue (warps 2..5) ----------------
+        const int q = warp & 3;
+        const int row_in_tile = q * 32 + lane;
+        int acc = 0;
+        uint32_t aph = 0;
+        for (int t = blockIdx.x; t < total; t += gridDim.x) {
+            int g, m, n;
+            decode_tile(t, s_pre, s_mt, p.G, g, m, n);
+            if (!mbar_wait(&tfull[acc], aph, p.status, kDevErrTimeout)) break;
+            tc_fence_after();
+            const int row_local = m * kBM + row_in_tile;
+            const bool valid = row_local < s_rows[g];
+            const int64_t out_row = (int64_t)s_start[g] + row_local;
+            const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + acc * 256;
+            if (kMode == 0) {
+                __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(p.out) + out_row * p.out_ld + n * 128;
+#pragma unroll 1
+                for (int c = 0; c < 128; c += 32) {
+                    uint32_t gr[32], ur[32];
+                    tmem_ld_32x32b_x32(taddr + c, gr);
+                    tmem_ld_32x32b_x32(taddr + 128 + c, ur);
+                    tmem_wait_ld();
+                    if (c == 96) { tc_fence_before(); mbar_arrive(&tempty[acc]); }
+                    uint32_t packed[16];
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        float hv[2];
+#pragma unroll
+                        for (int j = 0; j < 2; ++j) {
+                            const float gv = __uint_as_float(gr[2 * i + j]);
+                            const float uv = __uint_as_float(ur[2 * i + j]);
+                            hv[j] = uv * (gv / (1.0f + __expf(-gv)));
+                        }
+                        packed[i] = F16Traits<__nv_bfloat16>::pack2(hv[0], hv[1]);
+                    }
+                    if (valid) {
+                        uint4* o = reinterpret_cast<uint4*>(h + c);
+#pragma unroll
+                        for (int v = 0; v < 4; ++v)
+                            o[v] = make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
+                    }
+                }
+            } else {
+                float* y = reinterpret_cast<float*>(p.out) + out_row * p.out_ld + n * 256;
+#pragma unroll 1
+                for (int c = 0; c < 256; c += 32) {
+                    uint32_t r[32];
+                    tmem_ld_32x32b_x32(taddr + c, r);
+                    tmem_wait_ld();
+                    if (c == 224) { tc_fence_before(); mbar_arrive(&tempty[acc]); }
+                    if (valid) {
+                        uint4* dst = reinterpret_cast<uint4*>(y + c);
+#pragma unroll
+                        for (int v = 0; v < 8; ++v)
+                            dst[v] = make_uint4(r[4 * v], r[4 * v + 1], r[4 * v + 2], r[4 * v + 3]);
+                    }
+                }
+            }
+            acc ^= 1;
+            if (acc == 0) aph ^= 1u;
+        }
+    } else {
+        // ---------------- converter (warps 6..9) ----------------
+        // thread: 8-column unit u (columns 8u..8u+7) of K-rows rg, rg+4, ...
+        const int ct = threadIdx.x - 192;
+        const int u = ct & 31, rg = ct >> 5;
+        const int chunk = u >> 3, uc = u & 7;
+        int s = 0;
+        uint32_t ph = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+            for (int kb = 0; kb < kblocks; ++kb) {
+                if (!mbar_wait(&full[s], ph, p.status, kDevErrTimeout)) { ok = false; break; }
+                float sc[8], cc[8];
+                {
+                    const uint4 s8 = *reinterpret_cast<const uint4*>(sS(s) + u * 16);
+                    const uint4 z8 = *reinterpret_cast<const uint4*>(sZ(s) + u * 16);
+                    const __half2* sh = reinterpret_cast<const __half2*>(&s8);
+                    const __half2* zh = reinterpret_cast<const __half2*>(&z8);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const float2 sf = __half22float2(sh[i]), zf = __half22float2(zh[i]);
+                        sc[2 * i] = sf.x;
+                        sc[2 * i + 1] = sf.y;
+                        cc[2 * i] = -(zf.x * sf.x);
+                        cc[2 * i + 1] = -(zf.y * sf.y);
+                    }
+                }
+                const uint8_t* src = sP(s);
+                uint8_t* dst = sB(s) + chunk * kChunkBytes;
+#pragma unroll 4
+                for (int j = 0; j < 16; ++j) {
+                    const int k = rg + 4 * j;
+                    const int off = kMode == 0 ? (u < 16 ? k * 64 + u * 4 : kPBytes / 2 + k * 64 + (u - 16) * 4)
+                                               : k * 128 + u * 4;
+                    const uint32_t w = *reinterpret_cast<const uint32_t*>(src + off);
+                    uint32_t o[4];
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const float q0 = __int_as_float(0x4B000000 | ((w >> (8 * i)) & 15u)) - 8388608.0f;
+                        const float q1 = __int_as_float(0x4B000000 | ((w >> (8 * i + 4)) & 15u)) - 8388608.0f;
+                        o[i] = F16Traits<__nv_bfloat16>::pack2(fmaf(q0, sc[2 * i], cc[2 * i]),
+                                                               fmaf(q1, sc[2 * i + 1], cc[2 * i + 1]));
+                    }
+                    *reinterpret_cast<uint4*>(dst + k * 128 + ((uc ^ (k & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+                }
+                fence_proxy_async_smem();
+                mbar_arrive(&conv[s]);
+                if (++s == kStages) { s = 0; ph ^= 1u; }
+            }
+        }
+    }
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, kTmemCols);
+    }
+}
+
+template <int kMode>
+cudaError_t launch(const W4Maps& mp, const W4Params& p, cudaStream_t st, int num_sms) {
+    auto kern = w4_gemm_kernel<kMode>;
+    cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+    if (err != cudaSuccess) return err;
+    kern<<<num_sms, kThreads, kSmemBytes, st>>>(mp, p);
+    return cudaGetLastError();
+}
+
+bool packed_map(CUtensorMap* m, const void* w, uint64_t rows, uint64_t n_cols, uint32_t box_cols) {
+    return make_map_box(m, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, n_cols / 2, rows, box_cols / 2, kBK, false);
+}
+bool sz_map(CUtensorMap* m, const void* sz, uint64_t rows, uint64_t n_cols, uint32_t box_cols) {
+    return make_map_box(m, sz, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, n_cols, rows, box_cols, 1, false);
+}
+
+}  // namespace
+
+cudaError_t launch_w4_up_gate(const void* a_rows, const void* w_gate, const void* w_up, const void* s_gate,
+                              const void* s_up, const void* z_gate, const void* z_up, const Shape& s,
+                              const GroupTable& gt, int* status, void* h_rows, cudaStream_t st, int num_sms) {
+    if (gt.G <= 0 || gt.rows_capacity <= 0) return cudaSuccess;
+    W4Maps mp;
+    const uint64_t wrows = (uint64_t)s.E * s.d, grows = (uint64_t)s.E * (s.d / 128);
+    if (!make_map_box(&mp.a, a_rows, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, s.d, gt.rows_capacity, 64, kBM, true) ||
+        !packed_map(&mp.p0, w_gate, wrows, s.f, 128) || !packed_map(&mp.p1, w_up, wrows, s.f, 128) ||
+        !sz_map(&mp.s0, s_gate, grows, s.f, 128) || !sz_map(&mp.s1, s_up, grows, s.f, 128) ||
+        !sz_map(&mp.z0, z_gate, grows, s.f, 128) || !sz_map(&mp.z1, z_up, grows, s.f, 128))
+        return cudaErrorInvalidValue;
+    W4Params p{};
+    p.g_rows = gt.rows;
+    p.g_start = gt.start;
+    p.g_weight = gt.weight;
+    p.G = gt.G;
+    p.K = s.d;
+    p.n_tiles = s.f / 128;
+    p.out_ld = s.f;
+    p.out = h_rows;
+    p.status = status;
+    p.idesc = idesc_f16(true, kBM, 256, false, true);
+    return launch<0>(mp, p, st, num_sms);
+}
+
+cudaError_t launch_w4_down(const void* h_rows, const void* w_down, const void* s_down, const void* z_down,
+                           const Shape& s, const GroupTable& gt, int* status, float* y_rows, cudaStream_t st,
+                           int num_sms) {
+    if (gt.G <= 0 || gt.rows_capacity <= 0) return cudaSuccess;
+    W4Maps mp;
+    const uint64_t wrows = (uint64_t)s.E * s.f, grows = (uint64_t)s.E * (s.f / 128);
+    if (!make_map_box(&mp.a, h_rows, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, s.f, gt.rows_capacity, 64, kBM, true) ||
+        !packed_map(&mp.p0, w_down, wrows, s.d, 256) || !sz_map(&mp.s0, s_down, grows, s.d, 256) ||
+        !sz_map(&mp.z0, z_down, grows, s.d, 256))
+        return cudaErrorInvalidValue;
+    mp.p1 = mp.p0;
+    mp.s1 = mp.s0;
+    mp.z1 = mp.z0;
+    W4Params p{};
+    p.g_rows = gt.rows;
+    p.g_start = gt.start;
+    p.g_weight = gt.weight;
+    p.G = gt.G;
+    p.K = s.f;
+    p.n_tiles = s.d / 256;
+    p.out_ld = s.d;
+    p.out = y_rows;
+    p.status = status;
+    p.idesc = idesc_f16(true, kBM, 256, false, true);
+    return launch<1>(mp, p, st, num_sms);
+}
+
+}  // namespace moe

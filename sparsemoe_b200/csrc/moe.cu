@@ -126,7 +126,7 @@ int make_shape(const MoeDims* d, Shape* s) {
         return MOE_ERR_UNSUPPORTED;
     }
     if (d->dtype != MOE_DTYPE_F16 && d->dtype != MOE_DTYPE_BF16 && d->dtype != MOE_DTYPE_INT8 &&
-        d->dtype != MOE_DTYPE_FP8_BLOCK) {
+        d->dtype != MOE_DTYPE_FP8_BLOCK && d->dtype != MOE_DTYPE_W4A16) {
         set_error("dtype %d not supported by this entry point", d->dtype);
         return MOE_ERR_UNSUPPORTED;
     }
@@ -142,7 +142,12 @@ int make_shape(const MoeDims* d, Shape* s) {
     s->k = d->top_k;
     s->dtype = d->dtype;
     s->router_dtype = d->router_dtype;
-    s->act_bf16 = d->dtype == MOE_DTYPE_BF16 || d->dtype == MOE_DTYPE_FP8_BLOCK;
+    s->act_bf16 = d->dtype == MOE_DTYPE_BF16 || d->dtype == MOE_DTYPE_FP8_BLOCK || d->dtype == MOE_DTYPE_W4A16;
+    if (d->dtype == MOE_DTYPE_W4A16 && (!d->w4_scale_gate || !d->w4_scale_up || !d->w4_scale_down ||
+                                        !d->w4_zero_gate || !d->w4_zero_up || !d->w4_zero_down)) {
+        set_error("MOE_DTYPE_W4A16 needs MoeDims.w4_scale_* and w4_zero_*");
+        return MOE_ERR_INVALID_ARG;
+    }
     if (d->dtype == MOE_DTYPE_FP8_BLOCK && (!d->w_scale_gate || !d->w_scale_up || !d->w_scale_down)) {
         set_error("MOE_DTYPE_FP8_BLOCK needs MoeDims.w_scale_gate / w_scale_up / w_scale_down");
         return MOE_ERR_INVALID_ARG;
@@ -276,7 +281,10 @@ int check_args(const MoEArgs* a, int dtype) {
                         a->expert_counts && a->expert_token_ids && a->expert_token_weights &&
                         a->hidden_mlp_layer_2_out && a->final_output;
     bool fmt = false;
-    if (dtype == MOE_DTYPE_FP8_BLOCK)
+    if (dtype == MOE_DTYPE_W4A16)
+        fmt = a->expert_up_proj_weights_int4 && a->expert_gate_proj_weights_int4 &&
+              a->expert_down_proj_weights_int4 && a->per_expert_wmma_inputs && a->hidden_mlp_layer_1_out_fp16;
+    else if (dtype == MOE_DTYPE_FP8_BLOCK)
         fmt = a->expert_up_proj_weights_fp8 && a->expert_gate_proj_weights_fp8 && a->expert_down_proj_weights_fp8 &&
               a->per_expert_wmma_inputs_fp8 && a->hidden_mlp_layer_1_out_fp8;
     else if (dtype == MOE_DTYPE_INT8)
@@ -287,7 +295,8 @@ int check_args(const MoEArgs* a, int dtype) {
               a->per_expert_wmma_inputs && a->hidden_mlp_layer_1_out_fp16;
     if (!common || !fmt) {
         set_error("a MoEArgs buffer needed by the %s path is null",
-                  dtype == MOE_DTYPE_INT8 ? "int8" : dtype == MOE_DTYPE_FP8_BLOCK ? "fp8" : "16-bit");
+                  dtype == MOE_DTYPE_INT8 ? "int8" : dtype == MOE_DTYPE_FP8_BLOCK ? "fp8"
+                                                  : dtype == MOE_DTYPE_W4A16  ? "4-bit" : "16-bit");
         return MOE_ERR_INVALID_ARG;
     }
     if (dtype == MOE_DTYPE_INT8 && !(a->scale_input_act > 0.0f && a->scale_mid_act > 0.0f)) {
@@ -329,6 +338,14 @@ struct FfnBuffers {
 FfnBuffers ffn_buffers(const MoEArgs* a, const Shape& s) {
     const bool i8 = s.dtype == MOE_DTYPE_INT8;
     FfnBuffers b;
+    if (s.dtype == MOE_DTYPE_W4A16) {
+        b.a_rows = (void*)a->per_expert_wmma_inputs;
+        b.h_rows = (void*)a->hidden_mlp_layer_1_out_fp16;
+        b.wg = a->expert_gate_proj_weights_int4;
+        b.wu = a->expert_up_proj_weights_int4;
+        b.wd = a->expert_down_proj_weights_int4;
+        return b;
+    }
     if (s.dtype == MOE_DTYPE_FP8_BLOCK) {
         b.a_rows = (void*)a->per_expert_wmma_inputs_fp8;
         b.h_rows = (void*)a->hidden_mlp_layer_1_out_fp8;
@@ -372,6 +389,16 @@ int enqueue_route(const MoEArgs* a, const MoeDims* dims, const Shape& s, const W
 int enqueue_ffn(const MoEArgs* a, const MoeDims* dims, const Shape& s, const GroupTable& gt, int* status,
                 float* a_scale, float* h_scale, int num_sms, cudaStream_t stream) {
     const FfnBuffers fb = ffn_buffers(a, s);
+    if (s.dtype == MOE_DTYPE_W4A16) {
+        MOE_TRY(launch_w4_up_gate(fb.a_rows, fb.wg, fb.wu, dims->w4_scale_gate, dims->w4_scale_up,
+                                  dims->w4_zero_gate, dims->w4_zero_up, s, gt, status, fb.h_rows, stream, num_sms),
+                "4-bit up/gate GEMM");
+        MOE_TRY(mark_stage(3, stream), "cudaEventRecord(stage event)");
+        MOE_TRY(launch_w4_down(fb.h_rows, fb.wd, dims->w4_scale_down, dims->w4_zero_down, s, gt, status,
+                               a->hidden_mlp_layer_2_out, stream, num_sms),
+                "4-bit down GEMM");
+        return MOE_OK;
+    }
     if (s.dtype == MOE_DTYPE_FP8_BLOCK) {
         MOE_TRY(launch_fp8_up_gate(fb.a_rows, a_scale, fb.wg, fb.wu, dims->w_scale_gate, dims->w_scale_up, s, gt,
                                    status, fb.h_rows, h_scale, stream, num_sms),

@@ -92,6 +92,14 @@ cudaError_t launch_fp8_down(const void* h_rows, const float* h_scale, const void
                             const Shape& s, const GroupTable& gt, int* status, float* y_rows, cudaStream_t st,
                             int num_sms);
 
+// expert_gemm_w4.cu: 4-bit weights dequantised to bf16 in shared memory.
+cudaError_t launch_w4_up_gate(const void* a_rows, const void* w_gate, const void* w_up, const void* s_gate,
+                              const void* s_up, const void* z_gate, const void* z_up, const Shape& s,
+                              const GroupTable& gt, int* status, void* h_rows, cudaStream_t st, int num_sms);
+cudaError_t launch_w4_down(const void* h_rows, const void* w_down, const void* s_down, const void* z_down,
+                           const Shape& s, const GroupTable& gt, int* status, float* y_rows, cudaStream_t st,
+                           int num_sms);
+
 // combine.cu: gate-weighted gather-sum into [B, N, d].
 cudaError_t launch_combine(const float* y_rows, const int* idx, const float* w, const Shape& s,
                            const Workspace& ws, float* out, void* out16, cudaStream_t st);

@@ -33,9 +33,14 @@ class MoeLayer:
         self.x = z(max(T, 1), d, dt=t16)
         self.wr = z(d, E, dt=torch.float32 if cfg.router_f32 else t16)
         wt = torch.int8 if cfg.int8 else (torch.uint8 if cfg.fp8 else t16)
-        self.wg = z(E, d, f, dt=wt)
-        self.wu = z(E, d, f, dt=wt)
-        self.wd = z(E, f, d, dt=wt)
+        if cfg.w4:
+            self.wg = z(E, d, f // 2, dt=torch.uint8)
+            self.wu = z(E, d, f // 2, dt=torch.uint8)
+            self.wd = z(E, f, d // 2, dt=torch.uint8)
+        else:
+            self.wg = z(E, d, f, dt=wt)
+            self.wu = z(E, d, f, dt=wt)
+            self.wd = z(E, f, d, dt=wt)
         self.scales = {}
         self.bias = None
         self.logits = z(max(T, 1), E, dt=torch.float32) if want_logits else None
@@ -63,12 +68,15 @@ class MoeLayer:
         if self.cfg.T > 0:
             put(self.x, inputs["x"])
         put(self.wr, inputs["wr"])
-        sfx = "_q" if (self.cfg.int8 or self.cfg.fp8) else ""
+        sfx = "_q" if (self.cfg.int8 or self.cfg.fp8 or self.cfg.w4) else ""
         put(self.wg, inputs["wg" + sfx])
         put(self.wu, inputs["wu" + sfx])
         put(self.wd, inputs["wd" + sfx])
         if self.cfg.int8:
             self.scales = {k: inputs[k] for k in ("s_in", "s_gate", "s_up", "s_mid", "s_down")}
+        if self.cfg.w4:
+            self.w4sz = [torch.from_numpy(np.ascontiguousarray(inputs[k]).view(np.int16)).to(self.device)
+                         for k in ("wg_s", "wu_s", "wd_s", "wg_z", "wu_z", "wd_z")]
         if self.cfg.fp8:
             self.wscale = [torch.from_numpy(np.ascontiguousarray(inputs[k])).to(self.device)
                            for k in ("sg", "su", "sd")]
@@ -82,7 +90,13 @@ class MoeLayer:
         p = lambda t: None if t is None else t.data_ptr()  # noqa: E731
         a.input = p(self.x)
         a.router_weights = p(self.wr)
-        if self.cfg.fp8:
+        if self.cfg.w4:
+            a.expert_up_proj_weights_int4 = p(self.wu)
+            a.expert_gate_proj_weights_int4 = p(self.wg)
+            a.expert_down_proj_weights_int4 = p(self.wd)
+            a.per_expert_wmma_inputs = p(self.a_rows)
+            a.hidden_mlp_layer_1_out_fp16 = p(self.h_rows)
+        elif self.cfg.fp8:
             a.expert_up_proj_weights_fp8 = p(self.wu)
             a.expert_gate_proj_weights_fp8 = p(self.wg)
             a.expert_down_proj_weights_fp8 = p(self.wd)
@@ -118,8 +132,9 @@ class MoeLayer:
 
     def dims(self):
         ws = tuple(t.data_ptr() for t in self.wscale) if self.cfg.fp8 else (None, None, None)
+        w4 = tuple(t.data_ptr() for t in self.w4sz) if self.cfg.w4 else (None,) * 6
         return self.cfg.dims(None if self.bias is None else self.bias.data_ptr(),
-                             None if self.out16 is None else self.out16.data_ptr(), w_scales=ws)
+                             None if self.out16 is None else self.out16.data_ptr(), w_scales=ws, w4=w4)
 
     def forward(self, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
         """Enqueues one layer call on `stream` (default: torch's current stream)."""
