@@ -30,6 +30,7 @@ extern "C" {
                                // router, f32 accumulate; MoEArgs *_fp8 fields
 #define MOE_DTYPE_W4A16 4      // 4-bit weights: INT4 asymmetric, group 128 along K, fp16 scale and
                                // zero per (group, column) (MoeDims.w4_*), nibble-packed [E, K, N/2]
+                               // (pair-interleaved words, see moe_quantize_int4_g128)
                                // in the MoEArgs *_int4 fields; bf16 x, router and h
 
 // ---- router formats --------------------------------------------------------
@@ -157,8 +158,9 @@ void moe_quantize_fp8_blocks(const uint16_t* src, int E, int K, int N, int bf16,
 // bf16): per expert, column n and group of 128 along K, s = (max - min) / 15
 // (1 if max == min), z = -min / s, both rounded to fp16; q = clamp(rint(w /
 // s + z), 0, 15) with the fp16 values; w is represented as (q - z) * s.
-// Writes packed [E, K, N/2] (even column in the low nibble) and fp16 bit
-// patterns of scales / zeros [E, K/128, N].
+// Writes packed [E, K, N/2] -- each little-endian 32-bit word holds 8
+// consecutive columns, column pair (2p, 2p+1) at bits 4p and 16 + 4p -- and
+// fp16 bit patterns of scales / zeros [E, K/128, N].
 void moe_quantize_int4_g128(const uint16_t* src, int E, int K, int N, int bf16, uint8_t* packed,
                             uint16_t* scales, uint16_t* zeros);
 

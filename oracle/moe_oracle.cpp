@@ -351,7 +351,8 @@ void oracle_ffn_combine(const uint16_t* x, const uint16_t* wg, const uint16_t* w
 }
 
 // 4-bit path (BASELINE config 5 weight format): weights dequantised exactly,
-// w = (q - z) * s with q the nibble of [E, K, N/2] (even column low) and s, z
+// w = (q - z) * s with q the nibble of [E, K, N/2] (8 columns per 32-bit
+// word, column pair (2p, 2p+1) at bits 4p and 16+4p) and s, z
 // the fp16 group values [E, K/128, N]; activations bf16; otherwise the 16-bit
 // path (h rounded to bf16, f32 down projection, route-order combine).
 void oracle_ffn_combine_w4(const uint16_t* x, const uint8_t* pg, const uint8_t* pu, const uint8_t* pd,
@@ -365,7 +366,9 @@ void oracle_ffn_combine_w4(const uint16_t* x, const uint8_t* pg, const uint8_t* 
             const uint8_t* row = P + ((size_t)e * K + j) * (Ncol / 2);
             for (int c = 0; c < nc; ++c) {
                 const int n = c0 + c;
-                const int q = (row[n / 2] >> ((n & 1) * 4)) & 15;
+                const uint8_t* word = row + (n >> 3) * 4;
+                const int bit = 4 * ((n & 7) >> 1) + 16 * (n & 1);
+                const int q = (word[bit >> 3] >> (bit & 7)) & 15;
                 const double sv = f16_to_f32(S[g * Ncol + n]), zv = f16_to_f32(Z[g * Ncol + n]);
                 dst[c] = (float)(((double)q - zv) * sv);
             }

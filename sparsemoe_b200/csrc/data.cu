@@ -126,8 +126,10 @@ extern "C" void moe_quantize_int4_g128(const uint16_t* src, int E, int K, int N,
                     const float v = val(((size_t)e * K + k) * N + n);
                     int q = (int)rintf(v / sf + zf);
                     q = q < 0 ? 0 : (q > 15 ? 15 : q);
-                    uint8_t& b = packed[((size_t)e * K + k) * (N / 2) + n / 2];
-                    b |= (n & 1) ? (uint8_t)(q << 4) : (uint8_t)q;
+                    // 8 columns per 32-bit word, pair (2p, 2p+1) at bits 4p and 16 + 4p
+                    const int pcol = n & 7, bit = 4 * (pcol >> 1) + 16 * (pcol & 1);
+                    uint8_t* word = packed + ((size_t)e * K + k) * (N / 2) + (n >> 3) * 4;
+                    word[bit >> 3] |= (uint8_t)(q << (bit & 7));
                 }
             }
 }

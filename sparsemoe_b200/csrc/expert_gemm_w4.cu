@@ -1,26 +1,28 @@
 // Stage 4 with 4-bit weights (BASELINE config 5 format): INT4 asymmetric,
 // group 128 along K, fp16 scale and zero per (group, output column),
-// nibble-packed along N ([E, K, N/2] bytes, even column in the low nibble);
-// bf16 activations; f32 accumulate.
+// nibble-packed along N ([E, K, N/2] bytes; each 32-bit word holds 8
+// consecutive columns interleaved so that column pair (2p, 2p+1) sits at bits
+// 4p and 16+4p); bf16 activations; f32 accumulate.
 //
 //   w(k, n) = (q(k, n) - z(k/128, n)) * s(k/128, n)
 //
 // The weights travel from HBM as nibbles (a quarter of bf16's bytes) and are
 // dequantised in shared memory by a converter warpgroup: each 64-row K stage
-// of packed nibbles becomes bf16 w = fma(q, s, -z*s) (f32, one rounding to
-// bf16) written straight into the 128B-swizzled MN-major layout the MMA
+// of packed nibbles becomes bf16 w = fma(q, s, -z*s) in packed bf16x2 math
+// (q from the magic constant 0x4300|q = 128+q, one shift + LOP3 per column
+// pair) written straight into the 128B-swizzled MN-major layout the MMA
 // reads, so the tensor cores run plain kind::f16 bf16 MMAs into TMEM with no
 // per-group promotion.  (Dequantising to e4m3 instead would round every
 // weight to a 3-bit mantissa -- ~6% relative error per weight -- which the
 // 6e-2 bar of this format cannot absorb; bf16 keeps 2^-9.)
 //
-// Warps (320 threads, persistent, one CTA per SM):
+// Warps (448 threads, persistent, one CTA per SM):
 //   0      TMA: bf16 A tile (128 x 64, K-major SW128), packed B (64 K-rows x
 //          256 columns / 2), the stage's 256 fp16 scales and zeros.
 //   1      MMA: 4 x tcgen05.mma kind::f16 M128 N256 K16 per stage, double-
 //          buffered TMEM accumulators.
 //   2-5    epilogue (SwiGLU -> bf16 h, or f32 y), as the 16-bit kernel.
-//   6-9    converter: nibbles -> bf16 into the stage's B buffer, then
+//   6-13   converter: nibbles -> bf16 into the stage's B buffer, then
 //          fence.proxy.async and arrive on the stage's converted barrier.
 #include "moe_internal.h"
 #include "common.cuh"
@@ -41,7 +43,8 @@ using namespace sm100;
 constexpr int kBM = 128;
 constexpr int kBK = 64;
 constexpr int kStages = 3;
-constexpr int kThreads = 320;
+constexpr int kThreads = 448;   // 2 + 4 epilogue + 8 converter warps
+constexpr int kConvThreads = 256;
 constexpr int kABytes = kBM * 128;        // 16 KB
 constexpr int kBBytes = 64 * 256 * 2;     // 32 KB bf16: 4 chunks of 64 columns x 64 K-rows
 constexpr int kChunkBytes = 64 * 128;     // 8 KB
@@ -116,7 +119,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&conv[s], 128);
+            mbar_init(&conv[s], kConvThreads);
             mbar_init(&empty[s], 1);
         }
         for (int a = 0; a < 2; ++a) { mbar_init(&tfull[a], 1); mbar_init(&tempty[a], 128); }
@@ -271,18 +274,19 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (acc == 0) aph ^= 1u;
         }
     } else {
-        // ---------------- converter (warps 6..9) ----------------
-        // thread: 8-column unit u (columns 8u..8u+7) of K-rows rg, rg+4, ...
+        // ---------------- converter (warps 6..13) ----------------
+        // thread: 8-column unit u (columns 8u..8u+7) of K-rows rg, rg+8, ...
         const int ct = threadIdx.x - 192;
         const int u = ct & 31, rg = ct >> 5;
         const int chunk = u >> 3, uc = u & 7;
+        const __nv_bfloat162 k128 = __floats2bfloat162_rn(128.0f, 128.0f);
         int s = 0;
         uint32_t ph = 0;
         bool ok = true;
         for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
             for (int kb = 0; kb < kblocks; ++kb) {
                 if (!mbar_wait(&full[s], ph, p.status, kDevErrTimeout)) { ok = false; break; }
-                float sc[8], cc[8];
+                __nv_bfloat162 sc[4], cc[4];
                 {
                     const uint4 s8 = *reinterpret_cast<const uint4*>(sS(s) + u * 16);
                     const uint4 z8 = *reinterpret_cast<const uint4*>(sZ(s) + u * 16);
@@ -291,27 +295,25 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int i = 0; i < 4; ++i) {
                         const float2 sf = __half22float2(sh[i]), zf = __half22float2(zh[i]);
-                        sc[2 * i] = sf.x;
-                        sc[2 * i + 1] = sf.y;
-                        cc[2 * i] = -(zf.x * sf.x);
-                        cc[2 * i + 1] = -(zf.y * sf.y);
+                        sc[i] = __floats2bfloat162_rn(sf.x, sf.y);
+                        cc[i] = __floats2bfloat162_rn(-(zf.x * sf.x), -(zf.y * sf.y));
                     }
                 }
                 const uint8_t* src = sP(s);
                 uint8_t* dst = sB(s) + chunk * kChunkBytes;
 #pragma unroll 4
-                for (int j = 0; j < 16; ++j) {
-                    const int k = rg + 4 * j;
+                for (int j = 0; j < 8; ++j) {
+                    const int k = rg + 8 * j;
                     const int off = kMode == 0 ? (u < 16 ? k * 64 + u * 4 : kPBytes / 2 + k * 64 + (u - 16) * 4)
                                                : k * 128 + u * 4;
                     const uint32_t w = *reinterpret_cast<const uint32_t*>(src + off);
                     uint32_t o[4];
 #pragma unroll
                     for (int i = 0; i < 4; ++i) {
-                        const float q0 = __int_as_float(0x4B000000 | ((w >> (8 * i)) & 15u)) - 8388608.0f;
-                        const float q1 = __int_as_float(0x4B000000 | ((w >> (8 * i + 4)) & 15u)) - 8388608.0f;
-                        o[i] = F16Traits<__nv_bfloat16>::pack2(fmaf(q0, sc[2 * i], cc[2 * i]),
-                                                               fmaf(q1, sc[2 * i + 1], cc[2 * i + 1]));
+                        const uint32_t biased = ((w >> (4 * i)) & 0x000F000Fu) | 0x43004300u;   // bf16x2 128+q
+                        const __nv_bfloat162 q = __hsub2(*reinterpret_cast<const __nv_bfloat162*>(&biased), k128);
+                        const __nv_bfloat162 v = __hfma2(q, sc[i], cc[i]);
+                        o[i] = *reinterpret_cast<const uint32_t*>(&v);
                     }
                     *reinterpret_cast<uint4*>(dst + k * 128 + ((uc ^ (k & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
                 }
