@@ -16,11 +16,11 @@
 //    the lower expert index; values <= -1e20 and NaN are never selected;
 //    unfilled slots keep (-1e20, -1)).
 //
-// Layout: 8 warps per CTA, each warp owns TT consecutive tokens and walks the
-// experts in groups of 8.  Lanes read x as 16-byte vectors (one 512-byte
+// Layout: 8 warps per CTA; a work item is TT consecutive tokens x one group
+// of 8 experts.  Lanes read x as 16-byte vectors (one 512-byte
 // coalesced segment per warp load) and the matching 8 router rows x 8
 // experts; all lanes end the butterfly with the same sums.  Logits go to
-// shared memory, then the same warp runs the top-k for its tokens.  The
+// shared memory, then each warp runs the top-k of one token at a time.  The
 // kernel reads x once from HBM (the router weights stay in L1/L2).
 #include "moe_internal.h"
 #include "common.cuh"
@@ -90,28 +90,35 @@ __device__ __forceinline__ void topk_softmax_warp(const float* row, int E, int k
     }
 }
 
-template <typename TX, typename TW>
+// Work item = (TT tokens, one group of 8 experts); a CTA holds CT tokens
+// (CT a multiple of TT) and its warps take the CT/TT x E/8 items in turn, so
+// small token counts still spread over many warps (TT = 1) while large ones
+// reuse each router row for 4 tokens (TT = 4).
+template <typename TX, typename TW, int TT>
 __global__ void __launch_bounds__(kWarps * 32) router_topk_kernel(
     const TX* __restrict__ x, const TW* __restrict__ wr, const float* __restrict__ bias,
-    int64_t T, int d, int E, int k, float* __restrict__ logits, int* __restrict__ idx,
+    int64_t T, int d, int E, int k, int CT, float* __restrict__ logits, int* __restrict__ idx,
     float* __restrict__ wts) {
-    extern __shared__ float lg_all[];  // [kWarps][kTT][E]
+    extern __shared__ float lg_all[];  // [CT][E]
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t t0 = ((int64_t)blockIdx.x * kWarps + warp) * kTT;
-    float* lg = lg_all + warp * kTT * E;
+    const int64_t cta_t0 = (int64_t)blockIdx.x * CT;
     const int nchunks = d / 256;
+    const int G = E / 8;
+    const int items = (CT / TT) * G;
 
-    for (int g = 0; g < E / 8; ++g) {
-        float acc[kTT][8];
+    for (int item = warp; item < items; item += kWarps) {
+        const int quad = item / G, g = item - quad * G;
+        const int64_t t0 = cta_t0 + (int64_t)quad * TT;
+        float acc[TT][8];
 #pragma unroll
-        for (int tt = 0; tt < kTT; ++tt)
+        for (int tt = 0; tt < TT; ++tt)
 #pragma unroll
             for (int e = 0; e < 8; ++e) acc[tt][e] = 0.0f;
         for (int i = 0; i < nchunks; ++i) {
             const int j0 = 8 * (lane + 32 * i);
-            float xv[kTT][8];
+            float xv[TT][8];
 #pragma unroll
-            for (int tt = 0; tt < kTT; ++tt) {
+            for (int tt = 0; tt < TT; ++tt) {
                 const int64_t t = t0 + tt;
                 if (t < T) {
                     const uint4 raw = __ldg(reinterpret_cast<const uint4*>(x + t * d + j0));
@@ -132,13 +139,13 @@ __global__ void __launch_bounds__(kWarps * 32) router_topk_kernel(
                 float wv[8];
                 load_wr8(wr + (int64_t)(j0 + jj) * E + 8 * g, wv);
 #pragma unroll
-                for (int tt = 0; tt < kTT; ++tt)
+                for (int tt = 0; tt < TT; ++tt)
 #pragma unroll
                     for (int e = 0; e < 8; ++e) acc[tt][e] = fmaf(xv[tt][jj], wv[e], acc[tt][e]);
             }
         }
 #pragma unroll
-        for (int tt = 0; tt < kTT; ++tt)
+        for (int tt = 0; tt < TT; ++tt)
 #pragma unroll
             for (int e = 0; e < 8; ++e)
 #pragma unroll
@@ -146,20 +153,20 @@ __global__ void __launch_bounds__(kWarps * 32) router_topk_kernel(
                     acc[tt][e] = acc[tt][e] + __shfl_xor_sync(0xffffffffu, acc[tt][e], off);
         if (lane == 0) {
 #pragma unroll
-            for (int tt = 0; tt < kTT; ++tt)
+            for (int tt = 0; tt < TT; ++tt)
 #pragma unroll
                 for (int e = 0; e < 8; ++e) {
                     const int ee = 8 * g + e;
-                    lg[tt * E + ee] = bias ? __fadd_rn(acc[tt][e], bias[ee]) : acc[tt][e];
+                    lg_all[(quad * TT + tt) * E + ee] = bias ? __fadd_rn(acc[tt][e], bias[ee]) : acc[tt][e];
                 }
         }
     }
-    __syncwarp();
+    __syncthreads();
 
-    for (int tt = 0; tt < kTT; ++tt) {
-        const int64_t t = t0 + tt;
+    for (int tt = warp; tt < CT; tt += kWarps) {
+        const int64_t t = cta_t0 + tt;
         if (t >= T) break;
-        const float* row = lg + tt * E;
+        const float* row = lg_all + tt * E;
         if (logits != nullptr)
             for (int e = lane; e < E; e += 32) logits[t * E + e] = row[e];
         topk_softmax_warp(row, E, k, t, idx, wts, lane);
@@ -262,15 +269,26 @@ __global__ void __launch_bounds__(512) router_tiled_kernel(
 template <typename TX, typename TW>
 cudaError_t launch_typed(const void* x, const void* wr, const float* bias, const Shape& s,
                          float* logits, int* idx, float* w, cudaStream_t st) {
-    const int threads = kWarps * 32;
-    const size_t smem = sizeof(float) * (size_t)kWarps * kTT * s.E;
-    auto kern = router_topk_kernel<TX, TW>;
-    cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (err != cudaSuccess) return err;
-    const int64_t per_cta = (int64_t)kWarps * kTT;
-    const int64_t blocks = (s.T() + per_cta - 1) / per_cta;
-    kern<<<(unsigned)blocks, threads, smem, st>>>((const TX*)x, (const TW*)wr, bias, s.T(), s.d, s.E,
-                                                  s.k, logits, idx, w);
+    // 4 tokens per item and 32 per CTA when that still gives two CTAs per SM;
+    // otherwise one token per item and fewer tokens per CTA.
+    const bool big = s.T() >= (int64_t)kWarps * kTT * 296;
+    const int CT = big ? kWarps * kTT : (int)std::max<int64_t>(1, std::min<int64_t>(32, s.T() / 296));
+    const size_t smem = sizeof(float) * (size_t)CT * s.E;
+    const int64_t blocks = (s.T() + CT - 1) / CT;
+    cudaError_t err;
+    if (big) {
+        auto kern = router_topk_kernel<TX, TW, kTT>;
+        err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (err != cudaSuccess) return err;
+        kern<<<(unsigned)blocks, kWarps * 32, smem, st>>>((const TX*)x, (const TW*)wr, bias, s.T(), s.d, s.E, s.k,
+                                                          CT, logits, idx, w);
+    } else {
+        auto kern = router_topk_kernel<TX, TW, 1>;
+        err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (err != cudaSuccess) return err;
+        kern<<<(unsigned)blocks, kWarps * 32, smem, st>>>((const TX*)x, (const TW*)wr, bias, s.T(), s.d, s.E, s.k,
+                                                          CT, logits, idx, w);
+    }
     return cudaGetLastError();
 }
 
