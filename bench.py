@@ -46,6 +46,9 @@ def workload(name: str):
         # BASELINE configs[2] shape in the reference's int8 format (per-tensor int8 weights and
         # activations, kernels/capacity_int8_ptx.cu), Zipf(1.1) router bias so hot experts drop routes.
         "int8_cfg3": sm.LayerConfig(1, 16384, 2048, 1408, 64, 6, 1.0, dtype=sm.DTYPE_INT8, zipf_s=1.1),
+        # BASELINE configs[2] in its own format: per-output-channel int8 weights, per-token int8 x
+        # (h per token and 128-feature block), same shape and Zipf(1.1) bias.
+        "int8ch_cfg3": sm.LayerConfig(1, 16384, 2048, 1408, 64, 6, 1.0, dtype=sm.DTYPE_INT8_CHANNEL, zipf_s=1.1),
         # FP8 e4m3, 128x128 weight / 1x128 activation block scales.
         "fp8_cfg4": sm.LayerConfig(1, 32768, 2048, 768, 128, 8, 1.25, dtype=sm.DTYPE_FP8_BLOCK),
         # BASELINE configs[4], one GPU's share under 8-way expert parallelism: 32 experts, top-8 over them
@@ -54,6 +57,11 @@ def workload(name: str):
                                          zipf_s=1.0),
         "w4_cfg5_prefill": sm.LayerConfig(1, 8192, 7168, 2048, 32, 8, 1.25, dtype=sm.DTYPE_W4A16, router_f32=True,
                                           zipf_s=1.0),
+        # the same two shapes with config 5's other weight format, NVFP4 (e2m1, e4m3 scale per 16 K-rows)
+        "nvfp4_cfg5_decode": sm.LayerConfig(1, 512, 7168, 2048, 32, 8, 1.25, dtype=sm.DTYPE_NVFP4,
+                                            router_f32=True, zipf_s=1.0),
+        "nvfp4_cfg5_prefill": sm.LayerConfig(1, 8192, 7168, 2048, 32, 8, 1.25, dtype=sm.DTYPE_NVFP4,
+                                             router_f32=True, zipf_s=1.0),
     }
     return table[name]
 
@@ -67,13 +75,17 @@ def load_peaks():
 
 
 def dtype_name(cfg):
+    if cfg.nvfp4:
+        return "nvfp4_g16_weights_bf16_act"
     if cfg.w4:
         return "int4_g128_weights_bf16_act"
+    if cfg.int8ch:
+        return "int8_channel_token"
     return "int8" if cfg.int8 else ("fp8_e4m3_block" if cfg.fp8 else ("bf16" if cfg.bf16 else "f16"))
 
 
 def cfg_json(name, cfg, cap):
-    wb = 0.5 if cfg.w4 else (1 if (cfg.int8 or cfg.fp8) else 2)
+    wb = 0.5 if cfg.w4 else (1 if (cfg.int8 or cfg.int8ch or cfg.fp8) else 2)
     xb = cfg.T * cfg.d_model * 2 / 1e6
     wmb = 3 * cfg.num_experts * cfg.d_model * cfg.d_ff * wb / 1e9
     return {"workload": name, "num_batches": cfg.num_batches, "tokens_per_batch": cfg.tokens,
@@ -166,7 +178,7 @@ def device_inputs(layer, seed: int):
     ~ N(0,0.02), gate/up ~ N(0,1/sqrt(d)), down ~ N(0,1/sqrt(f)))."""
     import torch
     cfg = layer.cfg
-    if cfg.int8 or cfg.fp8 or cfg.w4 or cfg.zipf_s > 0:
+    if cfg.int8 or cfg.int8ch or cfg.fp8 or cfg.w4 or cfg.zipf_s > 0:
         # quantised formats: seeded host generator + the library's host quantisers
         import sparsemoe_b200 as sm
         layer.host_inputs = sm.make_inputs(cfg, seed)
@@ -195,7 +207,9 @@ def cpu_measure(layer, sample_tokens: int, nthreads: int):
         t_route = time.perf_counter() - t0
         S = min(sample_tokens, cfg.T)
         fn = O.ffn_combine_fp8 if cfg.fp8 else (O.ffn_combine_int8 if cfg.int8 else
-                                                (O.ffn_combine_w4 if cfg.w4 else None))
+                                                (O.ffn_combine_nvfp4 if cfg.nvfp4 else
+                                                 O.ffn_combine_w4 if cfg.w4 else
+                                                 (O.ffn_combine_int8ch if cfg.int8ch else None)))
         t0 = time.perf_counter()
         if fn is not None:
             fn(inp["x"], inp, cfg, r["idx"], r["w"], r["route_slot"], 0, S, nthreads)
@@ -335,7 +349,7 @@ def run_ep(args, cfg, ws, rank, local, dev):
     result = {
         "metric": f"MoE-layer tokens/s ({args.config})", "value": ws * cfg.T / (ms * 1e-3), "unit": "tokens/s",
         "n_gpus": ws, "steps": K, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16" if cfg.bf16 else ("int8" if cfg.int8 else "f16"),
+        "scaling": "weak", "vs_baseline": None, "dtype": dtype_name(cfg),
         "data": "synthetic (seeded torch normal: x N(0,1), router N(0,0.02), W N(0,1/sqrt(fan_in)))",
         "config": {**cfg_json(args.config, cfg, layer.cap),
                    "parallelism": f"ep{ws} (expert parallel, {cfg.num_experts // ws} experts per GPU, "
@@ -451,7 +465,7 @@ def main():
     peaks, peak_src = load_peaks()
     peak_tf = float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
     peak_note = f"{peak_src} bf16_tflops_sustained (cuBLAS bf16, power-capped loop)"
-    if cfg.int8 or cfg.fp8:
+    if cfg.int8 or cfg.int8ch or cfg.fp8:
         peak_tf *= 2.0   # dense int8 / fp8 tensor rate is twice bf16 on B200
         peak_note = f"2 x {peak_src} bf16_tflops_sustained (dense 8-bit rate = 2x bf16; no 8-bit peak measured)"
     d, f = cfg.d_model, cfg.d_ff

@@ -32,6 +32,15 @@ extern "C" {
                                // zero per (group, column) (MoeDims.w4_*), nibble-packed [E, K, N/2]
                                // (pair-interleaved words, see moe_quantize_int4_g128)
                                // in the MoEArgs *_int4 fields; bf16 x, router and h
+#define MOE_DTYPE_NVFP4 6   // NVFP4 weights: e2m1 nibbles packed as for MOE_DTYPE_W4A16 in the *_int4
+                            // fields, one e4m3 scale per (16 K-rows, column) (MoeDims.w4_scale_*:
+                            // gate/up [E, d/16, f], down [E, f/16, d]) and one f32 global scale per
+                            // expert matrix (MoeDims.fp4_global_*); w = e2m1 * scale * global;
+                            // bf16 x, router and h
+#define MOE_DTYPE_INT8_CHANNEL 5   // int8 weights with one f32 scale per output channel (MoeDims.w_scale_*:
+                                   // gate/up [E, f], down [E, d]); x quantised per token (amax / 127) on
+                                   // the fly, h per token and 128-feature block; s32 accumulate; bf16 x
+                                   // and router; MoEArgs *_int8 fields
 
 // ---- router formats --------------------------------------------------------
 #define MOE_ROUTER_SAME 0   // router_weights have the activation dtype
@@ -54,17 +63,23 @@ typedef struct MoeDims {
     void* output_16;        // optional device [B, N, d] copy of the output in the 16-bit dtype
     void* scratch;          // optional caller device memory for the library's routing tables
     size_t scratch_bytes;   //   (>= moe_workspace_bytes(dims)); NULL: the library's own block
-    // MOE_DTYPE_FP8_BLOCK weight scales (device f32): gate/up [E, d/128, f/128], down [E, f/128, d/128]
+    // weight scales (device f32).  MOE_DTYPE_FP8_BLOCK: gate/up [E, d/128, f/128], down [E, f/128, d/128];
+    // MOE_DTYPE_INT8_CHANNEL: gate/up [E, f], down [E, d]
     const float* w_scale_gate;
     const float* w_scale_up;
     const float* w_scale_down;
-    // MOE_DTYPE_W4A16 group scales and zeros (device fp16): gate/up [E, d/128, f], down [E, f/128, d]
+    // MOE_DTYPE_W4A16 group scales and zeros (device fp16): gate/up [E, d/128, f], down [E, f/128, d];
+    // MOE_DTYPE_NVFP4 uses w4_scale_* for its e4m3 block scales (see above)
     const void* w4_scale_gate;
     const void* w4_scale_up;
     const void* w4_scale_down;
     const void* w4_zero_gate;
     const void* w4_zero_up;
     const void* w4_zero_down;
+    // MOE_DTYPE_NVFP4 per-expert global scales (device f32 [E] each)
+    const float* fp4_global_gate;
+    const float* fp4_global_up;
+    const float* fp4_global_down;
 } MoeDims;
 
 // Reference: kernels/launcher.h:21 `extern "C" void solve(MoEArgs args)`.
@@ -153,6 +168,22 @@ float moe_quantize_per_tensor(const uint16_t* src_f16, size_t n, int8_t* dst, fl
 // q = e4m3(x / s) rounded to nearest even, saturating at +-448.
 // Writes q [E, K, N] (e4m3 bytes) and scales [E, K/128, N/128].
 void moe_quantize_fp8_blocks(const uint16_t* src, int E, int K, int N, int bf16, uint8_t* q, float* scales);
+
+// Per-output-channel int8 quantiser for weights [E, K, N] (16-bit, bf16 != 0:
+// bf16): per expert and column n, s = max_k |w| / 127 (1 if the column is
+// zero), q = clamp(nearbyint(w / s), -127, 127).  Writes q [E, K, N] and
+// scales [E, N].
+void moe_quantize_int8_channel(const uint16_t* src, int E, int K, int N, int bf16, int8_t* q, float* scales);
+
+// NVFP4 quantiser for weights [E, K, N] (16-bit, bf16 != 0: bf16): per expert
+// g = amax / (448 * 6) (1 if the matrix is zero); per column and group of 16
+// along K, s = e4m3(amax_group / (6 * g)) (round to nearest even, saturating;
+// a zero group gets s = 1.0), and q = e2m1(w / (s * g)) rounded to the nearest
+// of {0, 0.5, 1, 1.5, 2, 3, 4, 6} (ties to the even code), sign in bit 3.
+// Writes packed [E, K, N/2] (same pair-interleaved words as
+// moe_quantize_int4_g128), e4m3 scales [E, K/16, N] and globals [E].
+void moe_quantize_nvfp4(const uint16_t* src, int E, int K, int N, int bf16, uint8_t* packed, uint8_t* scales,
+                        float* globals);
 
 // 4-bit asymmetric group quantiser for weights [E, K, N] (16-bit, bf16 != 0:
 // bf16): per expert, column n and group of 128 along K, s = (max - min) / 15

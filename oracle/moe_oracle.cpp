@@ -378,6 +378,35 @@ void oracle_ffn_combine_w4(const uint16_t* x, const uint8_t* pg, const uint8_t* 
              route_slot, t_begin, t_end, out, nthreads);
 }
 
+// NVFP4 weights (second format): w = e2m1(q) * e4m3(s) * g
+// exactly, q the nibble (same packing as the 4-bit path; sign in bit 3,
+// magnitudes {0, 0.5, 1, 1.5, 2, 3, 4, 6}), s the scale of its 16-row group
+// [E, K/16, N], g the expert matrix's global scale [E]; the rest as the
+// 16-bit path.
+void oracle_ffn_combine_nvfp4(const uint16_t* x, const uint8_t* pg, const uint8_t* pu, const uint8_t* pd,
+                              const uint8_t* sg, const uint8_t* su, const uint8_t* sd, const float* gg,
+                              const float* gu, const float* gd, int d, int f, int E, int k, const int* idx,
+                              const float* w, const int* route_slot, int64_t t_begin, int64_t t_end, float* out,
+                              int nthreads) {
+    static const double kMag[8] = {0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0};
+    auto loader = [&](const uint8_t* P, const uint8_t* S, const float* G, int K, int Ncol) {
+        return [=](int e, int j, int c0, int nc, float* dst) {
+            const size_t grp = (size_t)e * (K / 16) + j / 16;
+            const uint8_t* row = P + ((size_t)e * K + j) * (Ncol / 2);
+            for (int c = 0; c < nc; ++c) {
+                const int n = c0 + c;
+                const uint8_t* word = row + (n >> 3) * 4;
+                const int bit = 4 * ((n & 7) >> 1) + 16 * (n & 1);
+                const int q = (word[bit >> 3] >> (bit & 7)) & 15;
+                const double v = (q & 8 ? -1.0 : 1.0) * kMag[q & 7];
+                dst[c] = (float)(v * (double)e4m3_to_f32(S[grp * Ncol + n]) * (double)G[e]);
+            }
+        };
+    };
+    ffn_impl(x, loader(pg, sg, gg, d, f), loader(pu, su, gu, d, f), loader(pd, sd, gd, f, d), d, f, E, k, 1, idx, w,
+             route_slot, t_begin, t_end, out, nthreads);
+}
+
 // int8 path (reference kernels/capacity_int8_ptx.cu): per-tensor quantised
 // operands, exact integer GEMMs, the reference's dequant / SiLU / requant
 // arithmetic in f32.
@@ -551,6 +580,94 @@ void oracle_ffn_combine_fp8(const uint16_t* x, const uint8_t* wg, const uint8_t*
                 acc[c] = fmaf(pd[c], sh[kb] * sd[((size_t)e * fk + kb) * dk + c / 128], acc[c]);
         }
         std::memcpy(&y[((size_t)(route - t_begin * k)) * d], acc.data(), sizeof(float) * d);
+    });
+    parallel_for(t_end - t_begin, nthreads, [&](int64_t i) {
+        const int64_t t = t_begin + i;
+        float* o = out + t * d;
+        for (int c = 0; c < d; ++c) o[c] = 0.0f;
+        for (int l = 0; l < k; ++l) {
+            const int64_t r = t * k + l;
+            if (route_slot[r] < 0) continue;
+            const float wl = w[r];
+            const float* yr = &y[((size_t)(r - t_begin * k)) * d];
+            for (int c = 0; c < d; ++c) {
+                volatile float pp = wl * yr[c];
+                o[c] = o[c] + pp;
+            }
+        }
+    });
+}
+
+// INT8_CHANNEL path (BASELINE config 3 format): x (bf16) quantised per token,
+// s_x = amax/127 (1 if zero), q = clamp(rn(x/s_x), +-127); weights int8 with
+// one scale per output column; G, U = exact s32 sums over all of K, then
+// g = (float)G * (s_x * s_g[c]) (same for u); h = u * g/(1+exp(-g)) quantised
+// per 128-feature block, s_h = amax/127; the down GEMM promotes each 128-wide K
+// block: acc = fmaf((float)P_kb, s_h[kb], acc), and y = acc * s_d[c]; then the
+// route-order combine.   wq: [E, K, N] int8; ws: [E, N] f32.
+void oracle_ffn_combine_int8ch(const uint16_t* x, const int8_t* wg, const int8_t* wu, const int8_t* wd,
+                               const float* sg, const float* su, const float* sd, int d, int f, int E, int k,
+                               const int* idx, const float* w, const int* route_slot, int64_t t_begin,
+                               int64_t t_end, float* out, int nthreads) {
+    std::vector<std::vector<int64_t>> routes(E);
+    for (int64_t t = t_begin; t < t_end; ++t)
+        for (int l = 0; l < k; ++l) {
+            const int64_t r = t * k + l;
+            if (route_slot[r] >= 0) routes[idx[r]].push_back(r);
+        }
+    std::vector<float> y((size_t)(t_end - t_begin) * k * d, 0.0f);
+    const int fk = f / 128;
+    struct Item { int e; int r; };
+    std::vector<Item> items;
+    for (int e = 0; e < E; ++e)
+        for (int r = 0; r < (int)routes[e].size(); ++r) items.push_back({e, r});
+    auto q8 = [](float v) { return (int32_t)fminf(fmaxf(nearbyintf(v), -127.0f), 127.0f); };
+    parallel_for((int64_t)items.size(), nthreads, [&](int64_t it) {
+        const int e = items[it].e;
+        const int64_t route = routes[e][items[it].r];
+        const int64_t tok = route / k;
+        std::vector<float> h(f), acc(d, 0.0f), sh(fk);
+        std::vector<int32_t> qa(d), G(f, 0), U(f, 0), qh(f), P(d);
+        float m = 0.0f;
+        for (int j = 0; j < d; ++j) m = fmaxf(m, fabsf(bf16_to_f32(x[tok * d + j])));
+        const float sx = m > 0.0f ? m / 127.0f : 1.0f;
+        for (int j = 0; j < d; ++j) qa[j] = q8(bf16_to_f32(x[tok * d + j]) / sx);
+        const int8_t* Wg = wg + (size_t)e * d * f;
+        const int8_t* Wu = wu + (size_t)e * d * f;
+        const int8_t* Wd = wd + (size_t)e * f * d;
+        for (int j = 0; j < d; ++j) {
+            const int32_t av = qa[j];
+            if (av == 0) continue;
+            const int8_t* gr = Wg + (size_t)j * f;
+            const int8_t* ur = Wu + (size_t)j * f;
+            for (int c = 0; c < f; ++c) {
+                G[c] += av * gr[c];
+                U[c] += av * ur[c];
+            }
+        }
+        for (int c = 0; c < f; ++c) {
+            const float gv = (float)G[c] * (sx * sg[(size_t)e * f + c]);
+            const float uv = (float)U[c] * (sx * su[(size_t)e * f + c]);
+            h[c] = uv * (gv / (1.0f + expf(-gv)));
+        }
+        for (int b = 0; b < fk; ++b) {
+            float hm = 0.0f;
+            for (int i = 0; i < 128; ++i) hm = fmaxf(hm, fabsf(h[b * 128 + i]));
+            sh[b] = hm > 0.0f ? hm / 127.0f : 1.0f;
+            for (int i = 0; i < 128; ++i) qh[b * 128 + i] = q8(h[b * 128 + i] / sh[b]);
+        }
+        for (int kb = 0; kb < fk; ++kb) {
+            std::fill(P.begin(), P.end(), 0);
+            for (int j = kb * 128; j < kb * 128 + 128; ++j) {
+                const int32_t hv = qh[j];
+                if (hv == 0) continue;
+                const int8_t* dr = Wd + (size_t)j * d;
+                for (int c = 0; c < d; ++c) P[c] += hv * dr[c];
+            }
+            for (int c = 0; c < d; ++c) acc[c] = fmaf((float)P[c], sh[kb], acc[c]);
+        }
+        float* dst = &y[((size_t)(route - t_begin * k)) * d];
+        for (int c = 0; c < d; ++c) dst[c] = acc[c] * sd[(size_t)e * d + c];
     });
     parallel_for(t_end - t_begin, nthreads, [&](int64_t i) {
         const int64_t t = t_begin + i;

@@ -49,6 +49,11 @@ def lib() -> ctypes.CDLL:
         L.oracle_ffn_combine_fp8.restype = None
         L.oracle_ffn_combine_fp8.argtypes = [P, P, P, P, P, P, P, I, I, I, I, P, P, P, ctypes.c_int64,
                                              ctypes.c_int64, P, I]
+        L.oracle_ffn_combine_int8ch.restype = None
+        L.oracle_ffn_combine_int8ch.argtypes = [P, P, P, P, P, P, P, I, I, I, I, P, P, P, ctypes.c_int64,
+                                                ctypes.c_int64, P, I]
+        L.oracle_ffn_combine_nvfp4.restype = None
+        L.oracle_ffn_combine_nvfp4.argtypes = [P] * 10 + [I, I, I, I, P, P, P, ctypes.c_int64, ctypes.c_int64, P, I]
         L.oracle_e4m3.restype = ctypes.c_uint8
         L.oracle_e4m3.argtypes = [ctypes.c_float]
         L.oracle_e4m3_decode.restype = ctypes.c_float
@@ -137,6 +142,38 @@ def ffn_combine_fp8(x, q, cfg, idx, w, route_slot, t_begin=0, t_end=None, nthrea
     return out[t_begin:t_end]
 
 
+def ffn_combine_int8ch(x, q, cfg, idx, w, route_slot, t_begin=0, t_end=None, nthreads=None):
+    """int8 per-channel / per-token path for tokens [t_begin, t_end); q holds
+    wg_q/wu_q/wd_q (int8) and sg/su/sd (per-output-channel scales)."""
+    T = cfg.T
+    t_end = T if t_end is None else t_end
+    out = np.zeros((T, cfg.d_model), np.float32)
+    ws = [np.ascontiguousarray(q[n], np.int8) for n in ("wg_q", "wu_q", "wd_q")]
+    ss = [np.ascontiguousarray(q[n], np.float32) for n in ("sg", "su", "sd")]
+    lib().oracle_ffn_combine_int8ch(_ptr(np.ascontiguousarray(x, np.uint16)), *(_ptr(a) for a in ws),
+                                    *(_ptr(a) for a in ss), cfg.d_model, cfg.d_ff, cfg.num_experts, cfg.top_k,
+                                    _ptr(np.ascontiguousarray(idx, np.int32)),
+                                    _ptr(np.ascontiguousarray(w, np.float32)),
+                                    _ptr(np.ascontiguousarray(route_slot, np.int32)), t_begin, t_end, _ptr(out),
+                                    nthreads or threads())
+    return out[t_begin:t_end]
+
+
+def ffn_combine_nvfp4(x, q, cfg, idx, w, route_slot, t_begin=0, t_end=None, nthreads=None):
+    """NVFP4 weight path for tokens [t_begin, t_end): exact e2m1 * e4m3 * g weights."""
+    T = cfg.T
+    t_end = T if t_end is None else t_end
+    out = np.zeros((T, cfg.d_model), np.float32)
+    arrs = [np.ascontiguousarray(q[n], np.uint8) for n in ("wg_q", "wu_q", "wd_q", "wg_s", "wu_s", "wd_s")]
+    arrs += [np.ascontiguousarray(q[n], np.float32) for n in ("wg_g", "wu_g", "wd_g")]
+    lib().oracle_ffn_combine_nvfp4(_ptr(np.ascontiguousarray(x, np.uint16)), *(_ptr(a) for a in arrs),
+                                   cfg.d_model, cfg.d_ff, cfg.num_experts, cfg.top_k,
+                                   _ptr(np.ascontiguousarray(idx, np.int32)), _ptr(np.ascontiguousarray(w, np.float32)),
+                                   _ptr(np.ascontiguousarray(route_slot, np.int32)), t_begin, t_end, _ptr(out),
+                                   nthreads or threads())
+    return out[t_begin:t_end]
+
+
 def ffn_combine_w4(x, q, cfg, idx, w, route_slot, t_begin=0, t_end=None, nthreads=None):
     """4-bit weight path for tokens [t_begin, t_end): exact (q - z) * s weights."""
     T = cfg.T
@@ -158,12 +195,18 @@ def forward(inputs: dict, cfg, t_begin=0, t_end=None, nthreads=None):
     act_bf16 = getattr(cfg, "act_bf16", cfg.bf16)
     r = route(inputs["x"], inputs["wr"], inputs.get("bias"), cfg.num_batches, cfg.tokens, cfg.d_model,
               cfg.num_experts, cfg.top_k, cap, act_bf16, cfg.router_f32, nthreads)
-    if getattr(cfg, "w4", False):
+    if getattr(cfg, "nvfp4", False):
+        r["out"] = ffn_combine_nvfp4(inputs["x"], inputs, cfg, r["idx"], r["w"], r["route_slot"], t_begin, t_end,
+                                     nthreads)
+    elif getattr(cfg, "w4", False):
         r["out"] = ffn_combine_w4(inputs["x"], inputs, cfg, r["idx"], r["w"], r["route_slot"], t_begin, t_end,
                                   nthreads)
     elif getattr(cfg, "fp8", False):
         r["out"] = ffn_combine_fp8(inputs["x"], inputs, cfg, r["idx"], r["w"], r["route_slot"], t_begin, t_end,
                                    nthreads)
+    elif getattr(cfg, "int8ch", False):
+        r["out"] = ffn_combine_int8ch(inputs["x"], inputs, cfg, r["idx"], r["w"], r["route_slot"], t_begin, t_end,
+                                      nthreads)
     elif getattr(cfg, "int8", False):
         r["out"] = ffn_combine_int8(inputs["x"], inputs, cfg, r["idx"], r["w"], r["route_slot"], t_begin, t_end,
                                     nthreads)

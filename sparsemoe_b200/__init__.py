@@ -30,6 +30,8 @@ DTYPE_BF16 = 1
 DTYPE_INT8 = 2
 DTYPE_FP8_BLOCK = 3
 DTYPE_W4A16 = 4
+DTYPE_INT8_CHANNEL = 5
+DTYPE_NVFP4 = 6
 ROUTER_SAME = 0
 ROUTER_F32 = 1
 
@@ -81,6 +83,7 @@ class MoeDims(ctypes.Structure):
         ("w_scale_gate", _p), ("w_scale_up", _p), ("w_scale_down", _p),
         ("w4_scale_gate", _p), ("w4_scale_up", _p), ("w4_scale_down", _p),
         ("w4_zero_gate", _p), ("w4_zero_up", _p), ("w4_zero_down", _p),
+        ("fp4_global_gate", _p), ("fp4_global_up", _p), ("fp4_global_down", _p),
     ]
 
 
@@ -112,6 +115,8 @@ def _load() -> ctypes.CDLL:
         "moe_quantize_per_tensor": (ctypes.c_float, [_p, ctypes.c_size_t, _p, ctypes.c_float]),
         "moe_quantize_int4_g128": (None, [_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _p, _p, _p]),
         "moe_quantize_fp8_blocks": (None, [_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _p, _p]),
+        "moe_quantize_int8_channel": (None, [_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _p, _p]),
+        "moe_quantize_nvfp4": (None, [_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _p, _p, _p]),
         "moe_fill_normal_f32": (None, [_p, ctypes.c_size_t, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_float]),
         "moe_zipf_bias": (None, [_p, ctypes.c_int, ctypes.c_float, ctypes.c_float, ctypes.c_uint64]),
     }
@@ -190,16 +195,32 @@ class LayerConfig:
 
     @property
     def w4(self) -> bool:
-        return self.dtype == DTYPE_W4A16
+        """4-bit packed weights (INT4 asymmetric g128 or NVFP4), bf16 activations."""
+        return self.dtype in (DTYPE_W4A16, DTYPE_NVFP4)
+
+    @property
+    def nvfp4(self) -> bool:
+        return self.dtype == DTYPE_NVFP4
 
     @property
     def act_bf16(self) -> bool:
         """Activations (x, router, 16-bit output) are bf16."""
-        return self.dtype in (DTYPE_BF16, DTYPE_FP8_BLOCK, DTYPE_W4A16)
+        return self.dtype in (DTYPE_BF16, DTYPE_FP8_BLOCK, DTYPE_W4A16, DTYPE_INT8_CHANNEL, DTYPE_NVFP4)
 
     @property
     def int8(self) -> bool:
+        """The reference's per-tensor int8 format."""
         return self.dtype == DTYPE_INT8
+
+    @property
+    def int8ch(self) -> bool:
+        """int8 with per-output-channel weight scales and per-token activation scales."""
+        return self.dtype == DTYPE_INT8_CHANNEL
+
+    @property
+    def channel_scaled(self) -> bool:
+        """Weight scales travel in MoeDims.w_scale_* (FP8 blocks or int8 channels)."""
+        return self.dtype in (DTYPE_FP8_BLOCK, DTYPE_INT8_CHANNEL)
 
     def capacity(self) -> int:
         if self.cap > 0:
@@ -210,10 +231,10 @@ class LayerConfig:
 
     def dims(self, router_bias_ptr: int | None = None, out16_ptr: int | None = None,
              scratch_ptr: int | None = None, scratch_bytes: int = 0, w_scales=(None, None, None),
-             w4=(None,) * 6) -> MoeDims:
+             w4=(None,) * 6, fp4_global=(None,) * 3) -> MoeDims:
         return MoeDims(self.num_batches, self.tokens, self.d_model, self.d_ff, self.num_experts, self.top_k,
                        self.capacity_factor, self.cap, self.dtype, ROUTER_F32 if self.router_f32 else ROUTER_SAME,
-                       router_bias_ptr, out16_ptr, scratch_ptr, scratch_bytes, *w_scales, *w4)
+                       router_bias_ptr, out16_ptr, scratch_ptr, scratch_bytes, *w_scales, *w4, *fp4_global)
 
 
 def make_inputs(cfg: LayerConfig, seed: int = 0) -> dict:
@@ -234,13 +255,21 @@ def make_inputs(cfg: LayerConfig, seed: int = 0) -> dict:
         out["wr"] = normal_f32(d * E, seed, 1, 0.02).reshape(d, E)
     else:
         out["wr"] = normal16(d * E, seed, 1, 0.02, b16).reshape(d, E)
-    if cfg.w4:
+    if cfg.nvfp4:
+        for n in ("wg", "wu", "wd"):
+            q, sc, gl = quantize_nvfp4(out[n], bf16=True)
+            out[n + "_q"], out[n + "_s"], out[n + "_g"] = q, sc, gl
+    elif cfg.w4:
         for n in ("wg", "wu", "wd"):
             q, sc, zr = quantize_int4_g128(out[n], bf16=True)
             out[n + "_q"], out[n + "_s"], out[n + "_z"] = q, sc, zr
     if cfg.fp8:
         for n, key in (("wg", "sg"), ("wu", "su"), ("wd", "sd")):
             q, sc = quantize_fp8_blocks(out[n], bf16=True)
+            out[n + "_q"], out[key] = q, sc
+    if cfg.int8ch:
+        for n, key in (("wg", "sg"), ("wu", "su"), ("wd", "sd")):
+            q, sc = quantize_int8_channel(out[n], bf16=True)
             out[n + "_q"], out[key] = q, sc
     out["bias"] = zipf_bias(E, cfg.zipf_s) if cfg.zipf_s > 0 else None
     if cfg.int8:
@@ -268,6 +297,20 @@ def quantize_int4_g128(w16: np.ndarray, bf16: bool = True):
     return q, sc, zr
 
 
+def quantize_nvfp4(w16: np.ndarray, bf16: bool = True):
+    """NVFP4: e2m1 nibbles (packed like quantize_int4_g128), one e4m3 scale per
+    16 K-rows and column, one f32 global scale per expert matrix.  w16: [E, K,
+    N] 16-bit bit patterns.  Returns (packed [E, K, N/2] uint8, scales [E,
+    K/16, N] uint8 e4m3 codes, globals [E] f32)."""
+    E, K, N = w16.shape
+    w16 = np.ascontiguousarray(w16, np.uint16)
+    q = np.empty((E, K, N // 2), np.uint8)
+    sc = np.empty((E, K // 16, N), np.uint8)
+    gl = np.empty(E, np.float32)
+    lib.moe_quantize_nvfp4(w16.ctypes.data, E, K, N, int(bf16), q.ctypes.data, sc.ctypes.data, gl.ctypes.data)
+    return q, sc, gl
+
+
 def quantize_fp8_blocks(w16: np.ndarray, bf16: bool = True):
     """e4m3 weights with f32 scales per 128x128 block of each [K, N] expert
     matrix (s = amax/448).  w16: [E, K, N] 16-bit bit patterns."""
@@ -276,6 +319,18 @@ def quantize_fp8_blocks(w16: np.ndarray, bf16: bool = True):
     q = np.empty((E, K, N), np.uint8)
     sc = np.empty((E, K // 128, N // 128), np.float32)
     lib.moe_quantize_fp8_blocks(w16.ctypes.data, E, K, N, int(bf16), q.ctypes.data, sc.ctypes.data)
+    return q, sc
+
+
+def quantize_int8_channel(w16: np.ndarray, bf16: bool = True):
+    """Symmetric int8 weights with one f32 scale per output column of each
+    [K, N] expert matrix (s = amax/127).  w16: [E, K, N] 16-bit bit patterns.
+    Returns (q [E, K, N] int8, scales [E, N] f32)."""
+    E, K, N = w16.shape
+    w16 = np.ascontiguousarray(w16, np.uint16)
+    q = np.empty((E, K, N), np.int8)
+    sc = np.empty((E, N), np.float32)
+    lib.moe_quantize_int8_channel(w16.ctypes.data, E, K, N, int(bf16), q.ctypes.data, sc.ctypes.data)
     return q, sc
 
 
@@ -292,4 +347,5 @@ from .layer import MoeLayer  # noqa: E402  (needs `lib` above)
 __all__ = ["MoEArgs", "MoeDims", "LayerConfig", "MoeLayer", "make_inputs", "capacity", "lib", "check",
            "MoeError", "normal16", "normal_f32", "zipf_bias", "quantize_per_tensor", "DTYPE_F16", "DTYPE_BF16",
            "DTYPE_INT8", "DTYPE_FP8_BLOCK", "quantize_fp8_blocks",
-           "DTYPE_W4A16", "quantize_int4_g128"]
+           "DTYPE_W4A16", "quantize_int4_g128", "DTYPE_INT8_CHANNEL", "quantize_int8_channel",
+           "DTYPE_NVFP4", "quantize_nvfp4"]

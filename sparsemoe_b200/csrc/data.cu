@@ -90,6 +90,101 @@ extern "C" void moe_quantize_fp8_blocks(const uint16_t* src, int E, int K, int N
             }
 }
 
+extern "C" void moe_quantize_int8_channel(const uint16_t* src, int E, int K, int N, int bf16, int8_t* q,
+                                          float* scales) {
+    auto val = [&](size_t i) -> float {
+        if (bf16) {
+            uint32_t u = (uint32_t)src[i] << 16;
+            float f;
+            std::memcpy(&f, &u, 4);
+            return f;
+        }
+        half h;
+        std::memcpy(&h, &src[i], 2);
+        return __half2float(h);
+    };
+    std::vector<float> m((size_t)N);
+    for (int e = 0; e < E; ++e) {
+        std::fill(m.begin(), m.end(), 0.0f);
+        for (int r = 0; r < K; ++r)
+            for (int c = 0; c < N; ++c) m[c] = std::fmax(m[c], std::fabs(val(((size_t)e * K + r) * N + c)));
+        for (int c = 0; c < N; ++c) scales[(size_t)e * N + c] = m[c] > 0.0f ? m[c] / 127.0f : 1.0f;
+        for (int r = 0; r < K; ++r)
+            for (int c = 0; c < N; ++c) {
+                const size_t i = ((size_t)e * K + r) * N + c;
+                const float v = nearbyintf(val(i) / scales[(size_t)e * N + c]);
+                q[i] = (int8_t)(int)std::fmin(std::fmax(v, -127.0f), 127.0f);
+            }
+    }
+}
+
+namespace {
+// e2m1 magnitudes by code 0..7
+constexpr float kE2m1[8] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f};
+
+// Nearest e2m1 code of v (ties to the even code, saturating at 6), sign in bit 3.
+uint8_t e2m1_code(float v) {
+    const uint8_t sign = v < 0.0f ? 8 : 0;
+    const float a = std::fabs(v);
+    int best = 7;
+    if (a < 6.0f) {
+        best = 0;
+        for (int c = 1; c < 8; ++c) {
+            const float dc = std::fabs(a - kE2m1[c]), db = std::fabs(a - kE2m1[best]);
+            if (dc < db || (dc == db && (c & 1) == 0)) best = c;
+        }
+    }
+    return (uint8_t)(sign | best);
+}
+
+float e4m3_value(uint8_t code) {
+    const __half_raw r = __nv_cvt_fp8_to_halfraw(code, __NV_E4M3);
+    return __half2float(__half(r));
+}
+}  // namespace
+
+extern "C" void moe_quantize_nvfp4(const uint16_t* src, int E, int K, int N, int bf16, uint8_t* packed,
+                                   uint8_t* scales, float* globals) {
+    auto val = [&](size_t i) -> float {
+        if (bf16) {
+            uint32_t u = (uint32_t)src[i] << 16;
+            float f;
+            std::memcpy(&f, &u, 4);
+            return f;
+        }
+        half h;
+        std::memcpy(&h, &src[i], 2);
+        return __half2float(h);
+    };
+    const int G = K / 16;
+    std::memset(packed, 0, (size_t)E * K * (N / 2));
+    for (int e = 0; e < E; ++e) {
+        float amax = 0.0f;
+        for (size_t i = 0; i < (size_t)K * N; ++i) amax = std::fmax(amax, std::fabs(val((size_t)e * K * N + i)));
+        const float g = amax > 0.0f ? amax / (448.0f * 6.0f) : 1.0f;
+        globals[e] = g;
+        for (int gr = 0; gr < G; ++gr)
+            for (int n = 0; n < N; ++n) {
+                float m = 0.0f;
+                for (int i = 0; i < 16; ++i) m = std::fmax(m, std::fabs(val(((size_t)e * K + gr * 16 + i) * N + n)));
+                uint8_t sc = 0x38;   // 1.0
+                if (m > 0.0f) {
+                    sc = (uint8_t)__nv_cvt_float_to_fp8(m / (6.0f * g), __NV_SATFINITE, __NV_E4M3);
+                    if ((sc & 0x7F) == 0) sc = 0x01;   // smallest positive subnormal, never zero
+                }
+                scales[((size_t)e * G + gr) * N + n] = sc;
+                const float div = e4m3_value(sc) * g;
+                for (int i = 0; i < 16; ++i) {
+                    const size_t k = (size_t)gr * 16 + i;
+                    const uint8_t q = e2m1_code(val(((size_t)e * K + k) * N + n) / div);
+                    const int pcol = n & 7, bit = 4 * (pcol >> 1) + 16 * (pcol & 1);
+                    uint8_t* word = packed + ((size_t)e * K + k) * (N / 2) + (n >> 3) * 4;
+                    word[bit >> 3] |= (uint8_t)(q << (bit & 7));
+                }
+            }
+    }
+}
+
 extern "C" void moe_quantize_int4_g128(const uint16_t* src, int E, int K, int N, int bf16, uint8_t* packed,
                                        uint16_t* scales, uint16_t* zeros) {
     auto val = [&](size_t i) -> float {

@@ -237,6 +237,53 @@ __global__ void __launch_bounds__(kThreads) dispatch_gather_fp8_kernel(
     }
 }
 
+// INT8_CHANNEL gather: the row is quantised per token, s = amax / 127 (1 for a
+// zero row), q = clamp(rn(x / s), -127, 127).  Pass 1 reduces amax over the
+// row, pass 2 re-reads it (L1/L2 hits) and writes 8 int8 per 16-byte load.
+__global__ void __launch_bounds__(kThreads) dispatch_gather_q8tok_kernel(
+    const uint4* __restrict__ x, const int* __restrict__ counts, const int* __restrict__ token_ids,
+    const int* __restrict__ row_base, const int* __restrict__ expert_start, int N, int E, int B, int cap, int vecs,
+    uint2* __restrict__ a_rows, float* __restrict__ a_scale) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t slot_lin = (int64_t)blockIdx.x * kWarps + warp;
+    if (slot_lin >= (int64_t)B * E * cap) return;
+    const int be = (int)(slot_lin / cap);
+    const int s = (int)(slot_lin - (int64_t)be * cap);
+    if (s >= counts[be]) return;
+    const int b = be / E, e = be - b * E;
+    const int64_t t = token_ids[slot_lin];
+    const uint4* src = x + ((int64_t)b * N + t) * vecs;
+    const int64_t row = (int64_t)expert_start[e] + row_base[be] + s;
+    float amax = 0.0f;
+    for (int v = lane; v < vecs; v += 32) {
+        const uint4 raw = __ldg(src + v);
+        const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float2 f = __bfloat1622float2(h2[i]);
+            amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
+        }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+    const float sc = amax > 0.0f ? amax / 127.0f : 1.0f;
+    uint2* dst = a_rows + row * vecs;
+    for (int v = lane; v < vecs; v += 32) {
+        const uint4 raw = __ldg(src + v);
+        const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+        uint32_t w[2] = {0u, 0u};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float2 f = __bfloat1622float2(h2[i]);
+            const int q0 = max(-127, min(127, __float2int_rn(f.x / sc)));
+            const int q1 = max(-127, min(127, __float2int_rn(f.y / sc)));
+            w[i >> 1] |= ((uint32_t)(q0 & 0xff) | ((uint32_t)(q1 & 0xff) << 8)) << (16 * (i & 1));
+        }
+        dst[v] = make_uint2(w[0], w[1]);
+    }
+    if (lane == 0) a_scale[row] = sc;
+}
+
 }  // namespace
 
 cudaError_t launch_dispatch(const void* x, const int* idx, const float* w, const Shape& s,
@@ -261,6 +308,10 @@ cudaError_t launch_dispatch(const void* x, const int* idx, const float* w, const
         dispatch_gather_fp8_kernel<<<gblocks, kThreads, 0, st>>>(
             (const __nv_bfloat16*)x, counts, token_ids, ws.row_base, ws.expert_start, s.N, s.E, s.B, s.cap, s.d,
             (uint8_t*)a_rows, ws.a_scale);
+    else if (slots > 0 && s.dtype == MOE_DTYPE_INT8_CHANNEL)
+        dispatch_gather_q8tok_kernel<<<gblocks, kThreads, 0, st>>>((const uint4*)x, counts, token_ids, ws.row_base,
+                                                                   ws.expert_start, s.N, s.E, s.B, s.cap, s.d / 8,
+                                                                   (uint2*)a_rows, ws.a_scale);
     else if (slots > 0 && s.dtype == MOE_DTYPE_INT8)
         dispatch_gather_q8_kernel<<<gblocks, kThreads, 0, st>>>((const uint4*)x, counts, token_ids, ws.row_base,
                                                                 ws.expert_start, s.N, s.E, s.B, s.cap, s.d / 8,

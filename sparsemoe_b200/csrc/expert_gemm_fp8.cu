@@ -26,6 +26,18 @@
 //                 down: cols [128h, 128h+128), written as f32 rows of Y.
 // Quantisation (host weights, device activations and h) rounds x / s to the
 // nearest e4m3, saturating at +-448.
+//
+// The same kernel, kKind = 1, runs the INT8_CHANNEL format (s8 x s8 -> s32,
+// tcgen05.mma kind::i8): per-output-channel weight scales s_w[n] and per-row
+// activation scales (x: one per row; h: one per row and 128-feature block, the
+// up/gate tile), both amax / 127.
+//   up/gate: the row and column scales are constant along K, so all K blocks
+//            accumulate into one s32 TMEM tile and the epilogue reads it once:
+//            g = (float)G_s32 * (s_x[r] * s_g[n]); h = silu(g) * u is
+//            requantised per 128-feature block, q = clamp(rn(h / s_h), +-127).
+//   down:    s_h varies along K, so each K block is promoted as in the FP8 form
+//            (acc += (float)P_kb * s_h[r, kb]) and the epilogue multiplies the
+//            sum by s_d[n].
 #include "moe_internal.h"
 #include "common.cuh"
 #include "sm100.cuh"
@@ -100,7 +112,14 @@ __device__ __forceinline__ uint32_t e4m3x4(float a, float b, float c, float d) {
     return lo | (hi << 16);
 }
 
-template <int kMode>  // 0: up/gate + SwiGLU -> e4m3 h + scales;  1: down -> f32 y
+__device__ __forceinline__ uint32_t s8x4(float a, float b, float c, float d) {
+    auto q = [](float v) { return (uint32_t)(max(-127, min(127, __float2int_rn(v))) & 0xff); };
+    return q(a) | (q(b) << 8) | (q(c) << 16) | (q(d) << 24);
+}
+
+// kMode 0: up/gate + SwiGLU -> 8-bit h + scales;  1: down -> f32 y.
+// kKind 0: e4m3 with block scales;  1: int8 with channel scales.
+template <int kMode, int kKind>
 __global__ void __launch_bounds__(kThreads, 1)
     fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB0,
                     const __grid_constant__ CUtensorMap tmB1, const Fp8Params p) {
@@ -186,9 +205,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             int s = 0, pb = 0;
             uint32_t ph = 0, pph = 0;
             bool ok = true;
+            // kWhole: one TMEM accumulator over all K blocks (int8 up/gate)
+            constexpr bool kWhole = kKind == 1 && kMode == 0;
             for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
                 for (int kb = 0; kb < kblocks; ++kb) {
-                    if (!mbar_wait(&pempty[pb], pph ^ 1u, p.status, kDevErrTimeout) ||
+                    if (((!kWhole || kb == 0) && !mbar_wait(&pempty[pb], pph ^ 1u, p.status, kDevErrTimeout)) ||
                         !mbar_wait(&full[s], ph, p.status, kDevErrTimeout)) {
                         ok = false;
                         break;
@@ -201,13 +222,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int kk = 0; kk < 4; ++kk) {
                         const uint64_t adesc = smem_desc_sw128(a_base + kk * 32, 16, 1024);
                         const uint64_t bdesc = smem_desc_sw128(b_base + kk * 32 * 128, kChunkBytes, 1024);
-                        mma_f8_ss(d_tmem, adesc, bdesc, p.idesc, kk != 0 ? 1u : 0u);
+                        const uint32_t accum = (kk != 0 || (kWhole && kb != 0)) ? 1u : 0u;
+                        if (kKind == 0) mma_f8_ss(d_tmem, adesc, bdesc, p.idesc, accum);
+                        else mma_i8_ss(d_tmem, adesc, bdesc, p.idesc, accum);
                     }
                     mma_commit(&empty[s]);
-                    mma_commit(&pfull[pb]);
                     if (++s == kStages) { s = 0; ph ^= 1u; }
-                    pb ^= 1;
-                    if (pb == 0) pph ^= 1u;
+                    if (!kWhole || kb == kblocks - 1) {
+                        mma_commit(&pfull[pb]);
+                        pb ^= 1;
+                        if (pb == 0) pph ^= 1u;
+                    }
                 }
             }
         }
@@ -238,38 +263,71 @@ __global__ void __launch_bounds__(kThreads, 1)
                 return base[((int64_t)wexp * nkb + kb) * nblk + col];
             };
             const int wcol = kMode == 0 ? n : 2 * n + half;
-            float sa_n = arow[0];
-            float sw0_n = wscale(p.w_scale0, 0, wcol);
-            float sw1_n = kMode == 0 ? wscale(p.w_scale1, 0, wcol) : sw0_n;
-            for (int kb = 0; kb < nkb; ++kb) {
-                const float sa = sa_n, sw0 = sw0_n, sw1 = sw1_n;
-                if (kb + 1 < nkb) {
-                    sa_n = arow[kb + 1];
-                    sw0_n = wscale(p.w_scale0, kb + 1, wcol);
-                    sw1_n = kMode == 0 ? wscale(p.w_scale1, kb + 1, wcol) : sw0_n;
-                }
-                if (!mbar_wait(&pfull[pb], pph, p.status, kDevErrTimeout)) { ok = false; break; }
+            if (kKind == 1 && kMode == 0) {
+                // int8 up/gate: one s32 accumulator, scaled by s_x[r] * s_w[n]
+                const float sx = p.a_scale[valid ? row : (int64_t)s_start[g]];
+                const float* sg = p.w_scale0 + (int64_t)wexp * p.out_ld + n * 128 + 64 * half;
+                const float* su = p.w_scale1 + (int64_t)wexp * p.out_ld + n * 128 + 64 * half;
+                if (!mbar_wait(&pfull[pb], pph, p.status, kDevErrTimeout)) break;
                 tc_fence_after();
                 const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + pb * 256;
-                const float sc0 = sa * sw0, sc1 = sa * sw1;
 #pragma unroll
                 for (int piece = 0; piece < 8; ++piece) {
                     uint32_t r[16];
-                    const int col = kMode == 0 ? (piece < 4 ? 64 * half + 16 * piece : 128 + 64 * half + 16 * (piece - 4))
-                                               : 128 * half + 16 * piece;
+                    const int col = piece < 4 ? 64 * half + 16 * piece : 128 + 64 * half + 16 * (piece - 4);
                     tmem_ld_32x32b_x16(tbase + col, r);
                     tmem_wait_ld();
                     if (piece == 7) { tc_fence_before(); mbar_arrive(&pempty[pb]); }
-                    const float sc = (kMode == 0 && piece >= 4) ? sc1 : sc0;
+                    const float4* ws4 = reinterpret_cast<const float4*>((piece < 4 ? sg : su) + 16 * (piece & 3));
 #pragma unroll
-                    for (int i = 0; i < 16; i += 2)
-                        ffma2(acc[16 * piece + i], acc[16 * piece + i + 1], __uint_as_float(r[i]),
-                              __uint_as_float(r[i + 1]), sc);
+                    for (int v = 0; v < 4; ++v) {
+                        const float4 w4 = __ldg(ws4 + v);
+                        acc[16 * piece + 4 * v + 0] = (float)(int)r[4 * v + 0] * (sx * w4.x);
+                        acc[16 * piece + 4 * v + 1] = (float)(int)r[4 * v + 1] * (sx * w4.y);
+                        acc[16 * piece + 4 * v + 2] = (float)(int)r[4 * v + 2] * (sx * w4.z);
+                        acc[16 * piece + 4 * v + 3] = (float)(int)r[4 * v + 3] * (sx * w4.w);
+                    }
                 }
                 pb ^= 1;
                 if (pb == 0) pph ^= 1u;
+            } else {
+                float sa_n = arow[0];
+                float sw0_n = kKind == 0 ? wscale(p.w_scale0, 0, wcol) : 1.0f;
+                float sw1_n = (kKind == 0 && kMode == 0) ? wscale(p.w_scale1, 0, wcol) : sw0_n;
+                for (int kb = 0; kb < nkb; ++kb) {
+                    const float sa = sa_n, sw0 = sw0_n, sw1 = sw1_n;
+                    if (kb + 1 < nkb) {
+                        sa_n = arow[kb + 1];
+                        if (kKind == 0) {
+                            sw0_n = wscale(p.w_scale0, kb + 1, wcol);
+                            sw1_n = kMode == 0 ? wscale(p.w_scale1, kb + 1, wcol) : sw0_n;
+                        }
+                    }
+                    if (!mbar_wait(&pfull[pb], pph, p.status, kDevErrTimeout)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + pb * 256;
+                    const float sc0 = sa * sw0, sc1 = sa * sw1;
+#pragma unroll
+                    for (int piece = 0; piece < 8; ++piece) {
+                        uint32_t r[16];
+                        const int col = kMode == 0 ? (piece < 4 ? 64 * half + 16 * piece : 128 + 64 * half + 16 * (piece - 4))
+                                                   : 128 * half + 16 * piece;
+                        tmem_ld_32x32b_x16(tbase + col, r);
+                        tmem_wait_ld();
+                        if (piece == 7) { tc_fence_before(); mbar_arrive(&pempty[pb]); }
+                        const float sc = (kMode == 0 && piece >= 4) ? sc1 : sc0;
+#pragma unroll
+                        for (int i = 0; i < 16; i += 2) {
+                            const float p0 = kKind == 0 ? __uint_as_float(r[i]) : (float)(int)r[i];
+                            const float p1 = kKind == 0 ? __uint_as_float(r[i + 1]) : (float)(int)r[i + 1];
+                            ffma2(acc[16 * piece + i], acc[16 * piece + i + 1], p0, p1, sc);
+                        }
+                    }
+                    pb ^= 1;
+                    if (pb == 0) pph ^= 1u;
+                }
+                if (!ok) break;
             }
-            if (!ok) break;
             if (kMode == 0) {
                 float amax = 0.0f;
 #pragma unroll
@@ -284,7 +342,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 s_amax[half][row_in_tile] = amax;
                 asm volatile("bar.sync %0, 64;" ::"r"(1 + q) : "memory");
                 const float bmax = fmaxf(s_amax[0][row_in_tile], s_amax[1][row_in_tile]);
-                const float sh = bmax > 0.0f ? bmax / 448.0f : 1.0f;
+                const float sh = bmax > 0.0f ? bmax / (kKind == 0 ? 448.0f : 127.0f) : 1.0f;
                 if (valid) {
                     uint8_t* h8 = reinterpret_cast<uint8_t*>(p.out) + row * p.out_ld + n * 128 + 64 * half;
                     uint4* o = reinterpret_cast<uint4*>(h8);
@@ -294,13 +352,26 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                         for (int j = 0; j < 4; ++j) {
                             const int i = 16 * v + 4 * j;
-                            w4[j] = e4m3x4(acc[i] / sh, acc[i + 1] / sh, acc[i + 2] / sh, acc[i + 3] / sh);
+                            w4[j] = kKind == 0 ? e4m3x4(acc[i] / sh, acc[i + 1] / sh, acc[i + 2] / sh, acc[i + 3] / sh)
+                                               : s8x4(acc[i] / sh, acc[i + 1] / sh, acc[i + 2] / sh, acc[i + 3] / sh);
                         }
                         o[v] = make_uint4(w4[0], w4[1], w4[2], w4[3]);
                     }
                     if (half == 0) p.out_scale[row * nblk + n] = sh;
                 }
             } else if (valid) {
+                if (kKind == 1) {
+                    const float4* wd = reinterpret_cast<const float4*>(p.w_scale0 + (int64_t)wexp * p.out_ld +
+                                                                       n * 256 + 128 * half);
+#pragma unroll
+                    for (int v = 0; v < 32; ++v) {
+                        const float4 w4 = __ldg(wd + v);
+                        acc[4 * v] *= w4.x;
+                        acc[4 * v + 1] *= w4.y;
+                        acc[4 * v + 2] *= w4.z;
+                        acc[4 * v + 3] *= w4.w;
+                    }
+                }
                 float4* y = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + row * p.out_ld + n * 256 +
                                                       128 * half);
 #pragma unroll
@@ -315,10 +386,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
-template <int kMode>
+template <int kMode, int kKind>
 cudaError_t launch(const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& b1, const Fp8Params& p,
                    cudaStream_t st, int num_sms) {
-    auto kern = fp8_gemm_kernel<kMode>;
+    auto kern = fp8_gemm_kernel<kMode, kKind>;
     cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
     if (err != cudaSuccess) return err;
     kern<<<num_sms, kThreads, kSmemBytes, st>>>(a, b0, b1, p);
@@ -351,7 +422,7 @@ cudaError_t launch_fp8_up_gate(const void* a_rows, const float* a_scale, const v
     p.w_scale1 = s_up;
     p.status = status;
     p.idesc = idesc_e4m3(kBM, 256, true);
-    return launch<0>(ta, tg, tu, p, st, num_sms);
+    return launch<0, 0>(ta, tg, tu, p, st, num_sms);
 }
 
 cudaError_t launch_fp8_down(const void* h_rows, const float* h_scale, const void* w_down, const float* s_down,
@@ -375,7 +446,58 @@ cudaError_t launch_fp8_down(const void* h_rows, const float* h_scale, const void
     p.w_scale0 = s_down;
     p.status = status;
     p.idesc = idesc_e4m3(kBM, 256, true);
-    return launch<1>(th, td, td, p, st, num_sms);
+    return launch<1, 0>(th, td, td, p, st, num_sms);
+}
+
+cudaError_t launch_i8c_up_gate(const void* a_rows, const float* a_scale, const void* w_gate, const void* w_up,
+                               const float* s_gate, const float* s_up, const Shape& s, const GroupTable& gt,
+                               int* status, void* h_rows, float* h_scale, cudaStream_t st, int num_sms) {
+    if (gt.G <= 0 || gt.rows_capacity <= 0) return cudaSuccess;
+    CUtensorMap ta, tg, tu;
+    if (!make_map_u8(&ta, a_rows, s.d, gt.rows_capacity, kBM) ||
+        !make_map_u8(&tg, w_gate, s.f, (uint64_t)s.E * s.d, 128) ||
+        !make_map_u8(&tu, w_up, s.f, (uint64_t)s.E * s.d, 128))
+        return cudaErrorInvalidValue;
+    Fp8Params p{};
+    p.g_rows = gt.rows;
+    p.g_start = gt.start;
+    p.g_weight = gt.weight;
+    p.G = gt.G;
+    p.K = s.d;
+    p.n_tiles = s.f / 128;
+    p.out_ld = s.f;
+    p.out = h_rows;
+    p.out_scale = h_scale;
+    p.a_scale = a_scale;
+    p.w_scale0 = s_gate;
+    p.w_scale1 = s_up;
+    p.status = status;
+    p.idesc = idesc_i8(kBM, 256, true);
+    return launch<0, 1>(ta, tg, tu, p, st, num_sms);
+}
+
+cudaError_t launch_i8c_down(const void* h_rows, const float* h_scale, const void* w_down, const float* s_down,
+                            const Shape& s, const GroupTable& gt, int* status, float* y_rows, cudaStream_t st,
+                            int num_sms) {
+    if (gt.G <= 0 || gt.rows_capacity <= 0) return cudaSuccess;
+    CUtensorMap th, td;
+    if (!make_map_u8(&th, h_rows, s.f, gt.rows_capacity, kBM) ||
+        !make_map_u8(&td, w_down, s.d, (uint64_t)s.E * s.f, 128))
+        return cudaErrorInvalidValue;
+    Fp8Params p{};
+    p.g_rows = gt.rows;
+    p.g_start = gt.start;
+    p.g_weight = gt.weight;
+    p.G = gt.G;
+    p.K = s.f;
+    p.n_tiles = s.d / 256;
+    p.out_ld = s.d;
+    p.out = y_rows;
+    p.a_scale = h_scale;
+    p.w_scale0 = s_down;
+    p.status = status;
+    p.idesc = idesc_i8(kBM, 256, true);
+    return launch<1, 1>(th, td, td, p, st, num_sms);
 }
 
 }  // namespace moe

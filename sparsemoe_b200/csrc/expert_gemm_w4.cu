@@ -16,6 +16,15 @@
 // weight to a 3-bit mantissa -- ~6% relative error per weight -- which the
 // 6e-2 bar of this format cannot absorb; bf16 keeps 2^-9.)
 //
+// kFmt = 1 runs NVFP4 weights through the same pipeline: e2m1 nibbles in the
+// same packing, one e4m3 scale per (16 K-rows, column) and one f32 global
+// scale per expert matrix, w = e2m1 * s * g.  The converter places the nibble's
+// magnitude in bf16 bits 6..8 and its sign in bit 15, which as a bf16 value is
+// exactly e2m1 * 2^-126 (code 1 lands on the subnormal 2^-127), and multiplies
+// by the bf16 s * 2^118, so the staged weight is e2m1 * s * 2^-8 -- exact,
+// since the product has at most 6 significant bits.  The epilogue applies
+// g * 2^8 in f32 (the accumulators of one tile share one expert matrix).
+//
 // Warps (448 threads, persistent, one CTA per SM):
 //   0      TMA: bf16 A tile (128 x 64, K-major SW128), packed B (64 K-rows x
 //          256 columns / 2), the stage's 256 fp16 scales and zeros.
@@ -29,6 +38,7 @@
 #include "sm100.cuh"
 
 #include <cuda.h>
+#include <cuda_fp8.h>
 #include <cudaTypedefs.h>
 
 namespace moe {
@@ -64,6 +74,8 @@ struct W4Params {
     int n_tiles;
     int out_ld;
     void* out;          // bf16 h (up/gate) or f32 y (down)
+    const float* gs0;   // NVFP4: per-expert global scales (gate or down)
+    const float* gs1;   // NVFP4: up
     int* status;
     uint32_t idesc;
 };
@@ -71,8 +83,8 @@ struct W4Params {
 struct W4Maps {
     CUtensorMap a;          // bf16 activations [rows, K]
     CUtensorMap p0, p1;     // packed weights [E*K, N/2] (gate, up; down uses p0)
-    CUtensorMap s0, s1;     // fp16 scales [E*K/128, N]
-    CUtensorMap z0, z1;     // fp16 zeros
+    CUtensorMap s0, s1;     // fp16 scales [E*K/128, N]  (NVFP4: e4m3 scales [E*K/16, N])
+    CUtensorMap z0, z1;     // fp16 zeros (unused by NVFP4)
 };
 
 __device__ __forceinline__ void decode_tile(int t, const int* pre, const int* mt, int G, int& g, int& m, int& n) {
@@ -91,7 +103,9 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-template <int kMode>  // 0: up/gate + SwiGLU -> bf16 h;  1: down -> f32 y
+// kMode 0: up/gate + SwiGLU -> bf16 h;  1: down -> f32 y.
+// kFmt 0: INT4 asymmetric g128;  1: NVFP4.
+template <int kMode, int kFmt>
 __global__ void __launch_bounds__(kThreads, 1)
     w4_gemm_kernel(const __grid_constant__ W4Maps mp, const W4Params p) {
     extern __shared__ uint8_t smem_raw[];
@@ -160,6 +174,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int a_row = s_start[g] + m * kBM;
                 const int b_row = s_wt[g] * p.K;
                 const int sz_row0 = s_wt[g] * groups_k;
+                const int fp4_row0 = s_wt[g] * (p.K / 16);
                 for (int kb = 0; kb < kblocks; ++kb) {
                     if (!mbar_wait(&empty[s], ph ^ 1u, p.status, kDevErrTimeout)) goto producer_done;
                     mbar_arrive_expect_tx(&full[s], kTxBytes);
@@ -168,14 +183,23 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (kMode == 0) {
                         tma_load_2d(sP(s), &mp.p0, &full[s], n * 64, b_row + k0);
                         tma_load_2d(sP(s) + kPBytes / 2, &mp.p1, &full[s], n * 64, b_row + k0);
-                        tma_load_2d(sS(s), &mp.s0, &full[s], n * 128, sz_row0 + k0 / 128);
-                        tma_load_2d(sS(s) + kSZBytes / 2, &mp.s1, &full[s], n * 128, sz_row0 + k0 / 128);
-                        tma_load_2d(sZ(s), &mp.z0, &full[s], n * 128, sz_row0 + k0 / 128);
-                        tma_load_2d(sZ(s) + kSZBytes / 2, &mp.z1, &full[s], n * 128, sz_row0 + k0 / 128);
+                        if (kFmt == 0) {
+                            tma_load_2d(sS(s), &mp.s0, &full[s], n * 128, sz_row0 + k0 / 128);
+                            tma_load_2d(sS(s) + kSZBytes / 2, &mp.s1, &full[s], n * 128, sz_row0 + k0 / 128);
+                            tma_load_2d(sZ(s), &mp.z0, &full[s], n * 128, sz_row0 + k0 / 128);
+                            tma_load_2d(sZ(s) + kSZBytes / 2, &mp.z1, &full[s], n * 128, sz_row0 + k0 / 128);
+                        } else {   // 4 groups of 16 K-rows x 128 columns of e4m3 scales each
+                            tma_load_2d(sS(s), &mp.s0, &full[s], n * 128, fp4_row0 + k0 / 16);
+                            tma_load_2d(sS(s) + kSZBytes, &mp.s1, &full[s], n * 128, fp4_row0 + k0 / 16);
+                        }
                     } else {
                         tma_load_2d(sP(s), &mp.p0, &full[s], n * 128, b_row + k0);
-                        tma_load_2d(sS(s), &mp.s0, &full[s], n * 256, sz_row0 + k0 / 128);
-                        tma_load_2d(sZ(s), &mp.z0, &full[s], n * 256, sz_row0 + k0 / 128);
+                        if (kFmt == 0) {
+                            tma_load_2d(sS(s), &mp.s0, &full[s], n * 256, sz_row0 + k0 / 128);
+                            tma_load_2d(sZ(s), &mp.z0, &full[s], n * 256, sz_row0 + k0 / 128);
+                        } else {   // 4 x 256 e4m3 scales
+                            tma_load_2d(sS(s), &mp.s0, &full[s], n * 256, fp4_row0 + k0 / 16);
+                        }
                     }
                     if (++s == kStages) { s = 0; ph ^= 1u; }
                 }
@@ -226,6 +250,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             const bool valid = row_local < s_rows[g];
             const int64_t out_row = (int64_t)s_start[g] + row_local;
             const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + acc * 256;
+            // NVFP4: the global scale times 2^8 (the staged weights carry 2^-8)
+            const float gsa = kFmt == 1 ? p.gs0[s_wt[g]] * 256.0f : 1.0f;
+            const float gsb = (kFmt == 1 && kMode == 0) ? p.gs1[s_wt[g]] * 256.0f : 1.0f;
             if (kMode == 0) {
                 __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(p.out) + out_row * p.out_ld + n * 128;
 #pragma unroll 1
@@ -241,8 +268,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                         float hv[2];
 #pragma unroll
                         for (int j = 0; j < 2; ++j) {
-                            const float gv = __uint_as_float(gr[2 * i + j]);
-                            const float uv = __uint_as_float(ur[2 * i + j]);
+                            const float gv = __uint_as_float(gr[2 * i + j]) * gsa;
+                            const float uv = __uint_as_float(ur[2 * i + j]) * gsb;
                             hv[j] = uv * (gv / (1.0f + __expf(-gv)));
                         }
                         packed[i] = F16Traits<__nv_bfloat16>::pack2(hv[0], hv[1]);
@@ -263,10 +290,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tmem_wait_ld();
                     if (c == 224) { tc_fence_before(); mbar_arrive(&tempty[acc]); }
                     if (valid) {
-                        uint4* dst = reinterpret_cast<uint4*>(y + c);
+                        float4* dst = reinterpret_cast<float4*>(y + c);
 #pragma unroll
                         for (int v = 0; v < 8; ++v)
-                            dst[v] = make_uint4(r[4 * v], r[4 * v + 1], r[4 * v + 2], r[4 * v + 3]);
+                            dst[v] = make_float4(__uint_as_float(r[4 * v]) * gsa, __uint_as_float(r[4 * v + 1]) * gsa,
+                                                 __uint_as_float(r[4 * v + 2]) * gsa,
+                                                 __uint_as_float(r[4 * v + 3]) * gsa);
                     }
                 }
             }
@@ -286,36 +315,75 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
             for (int kb = 0; kb < kblocks; ++kb) {
                 if (!mbar_wait(&full[s], ph, p.status, kDevErrTimeout)) { ok = false; break; }
-                __nv_bfloat162 sc[4], cc[4];
-                {
-                    const uint4 s8 = *reinterpret_cast<const uint4*>(sS(s) + u * 16);
-                    const uint4 z8 = *reinterpret_cast<const uint4*>(sZ(s) + u * 16);
-                    const __half2* sh = reinterpret_cast<const __half2*>(&s8);
-                    const __half2* zh = reinterpret_cast<const __half2*>(&z8);
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const float2 sf = __half22float2(sh[i]), zf = __half22float2(zh[i]);
-                        sc[i] = __floats2bfloat162_rn(sf.x, sf.y);
-                        cc[i] = __floats2bfloat162_rn(-(zf.x * sf.x), -(zf.y * sf.y));
+                if (kFmt == 0) {
+                    __nv_bfloat162 sc[4], cc[4];
+                    {
+                        const uint4 s8 = *reinterpret_cast<const uint4*>(sS(s) + u * 16);
+                        const uint4 z8 = *reinterpret_cast<const uint4*>(sZ(s) + u * 16);
+                        const __half2* sh = reinterpret_cast<const __half2*>(&s8);
+                        const __half2* zh = reinterpret_cast<const __half2*>(&z8);
+    #pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            const float2 sf = __half22float2(sh[i]), zf = __half22float2(zh[i]);
+                            sc[i] = __floats2bfloat162_rn(sf.x, sf.y);
+                            cc[i] = __floats2bfloat162_rn(-(zf.x * sf.x), -(zf.y * sf.y));
+                        }
                     }
-                }
-                const uint8_t* src = sP(s);
-                uint8_t* dst = sB(s) + chunk * kChunkBytes;
-#pragma unroll 4
-                for (int j = 0; j < 8; ++j) {
-                    const int k = rg + 8 * j;
-                    const int off = kMode == 0 ? (u < 16 ? k * 64 + u * 4 : kPBytes / 2 + k * 64 + (u - 16) * 4)
-                                               : k * 128 + u * 4;
-                    const uint32_t w = *reinterpret_cast<const uint32_t*>(src + off);
-                    uint32_t o[4];
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const uint32_t biased = ((w >> (4 * i)) & 0x000F000Fu) | 0x43004300u;   // bf16x2 128+q
-                        const __nv_bfloat162 q = __hsub2(*reinterpret_cast<const __nv_bfloat162*>(&biased), k128);
-                        const __nv_bfloat162 v = __hfma2(q, sc[i], cc[i]);
-                        o[i] = *reinterpret_cast<const uint32_t*>(&v);
+                    const uint8_t* src = sP(s);
+                    uint8_t* dst = sB(s) + chunk * kChunkBytes;
+    #pragma unroll 4
+                    for (int j = 0; j < 8; ++j) {
+                        const int k = rg + 8 * j;
+                        const int off = kMode == 0 ? (u < 16 ? k * 64 + u * 4 : kPBytes / 2 + k * 64 + (u - 16) * 4)
+                                                   : k * 128 + u * 4;
+                        const uint32_t w = *reinterpret_cast<const uint32_t*>(src + off);
+                        uint32_t o[4];
+    #pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            const uint32_t biased = ((w >> (4 * i)) & 0x000F000Fu) | 0x43004300u;   // bf16x2 128+q
+                            const __nv_bfloat162 q = __hsub2(*reinterpret_cast<const __nv_bfloat162*>(&biased), k128);
+                            const __nv_bfloat162 v = __hfma2(q, sc[i], cc[i]);
+                            o[i] = *reinterpret_cast<const uint32_t*>(&v);
+                        }
+                        *reinterpret_cast<uint4*>(dst + k * 128 + ((uc ^ (k & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
                     }
-                    *reinterpret_cast<uint4*>(dst + k * 128 + ((uc ^ (k & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+                } else {
+                    // e4m3 scales of this thread's 8 columns for the stage's 4 groups, as bf16 s * 2^118
+                    __nv_bfloat162 sc[4][4];
+#pragma unroll
+                    for (int gi = 0; gi < 4; ++gi) {
+                        const uint8_t* sp = kMode == 0 ? (u < 16 ? sS(s) + gi * 128 + 8 * u
+                                                                 : sS(s) + 512 + gi * 128 + 8 * (u - 16))
+                                                       : sS(s) + gi * 256 + 8 * u;
+                        const uint2 raw = *reinterpret_cast<const uint2*>(sp);
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            const uint32_t word = i < 2 ? raw.x : raw.y;
+                            const __nv_fp8x2_storage_t pr = (__nv_fp8x2_storage_t)((word >> (16 * (i & 1))) & 0xFFFFu);
+                            const float2 f = __half22float2(__half2(__nv_cvt_fp8x2_to_halfraw2(pr, __NV_E4M3)));
+                            sc[gi][i] = __floats2bfloat162_rn(f.x * 0x1p118f, f.y * 0x1p118f);
+                        }
+                    }
+                    const uint8_t* src = sP(s);
+                    uint8_t* dst = sB(s) + chunk * kChunkBytes;
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        const int k = rg + 8 * j;   // K-row k of the stage is in group j / 2
+                        const int off = kMode == 0 ? (u < 16 ? k * 64 + u * 4 : kPBytes / 2 + k * 64 + (u - 16) * 4)
+                                                   : k * 128 + u * 4;
+                        const uint32_t w = *reinterpret_cast<const uint32_t*>(src + off);
+                        uint32_t o[4];
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            const uint32_t sh = w >> (4 * i);
+                            const uint32_t bits = ((sh << 6) & 0x01C001C0u) | ((sh << 12) & 0x80008000u);
+                            const __nv_bfloat162 v =
+                                __hmul2(*reinterpret_cast<const __nv_bfloat162*>(&bits), sc[j >> 1][i]);
+                            o[i] = *reinterpret_cast<const uint32_t*>(&v);
+                        }
+                        *reinterpret_cast<uint4*>(dst + k * 128 + ((uc ^ (k & 7)) << 4)) =
+                            make_uint4(o[0], o[1], o[2], o[3]);
+                    }
                 }
                 fence_proxy_async_smem();
                 mbar_arrive(&conv[s]);
@@ -330,9 +398,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
-template <int kMode>
+template <int kMode, int kFmt>
 cudaError_t launch(const W4Maps& mp, const W4Params& p, cudaStream_t st, int num_sms) {
-    auto kern = w4_gemm_kernel<kMode>;
+    auto kern = w4_gemm_kernel<kMode, kFmt>;
     cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
     if (err != cudaSuccess) return err;
     kern<<<num_sms, kThreads, kSmemBytes, st>>>(mp, p);
@@ -344,6 +412,10 @@ bool packed_map(CUtensorMap* m, const void* w, uint64_t rows, uint64_t n_cols, u
 }
 bool sz_map(CUtensorMap* m, const void* sz, uint64_t rows, uint64_t n_cols, uint32_t box_cols) {
     return make_map_box(m, sz, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, n_cols, rows, box_cols, 1, false);
+}
+// NVFP4 e4m3 scales [E*K/16, N]: 4 group rows (one 64-row stage) per box
+bool fp4_scale_map(CUtensorMap* m, const void* sc, uint64_t rows, uint64_t n_cols, uint32_t box_cols) {
+    return make_map_box(m, sc, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, n_cols, rows, box_cols, kBK / 16, false);
 }
 
 }  // namespace
@@ -370,7 +442,7 @@ cudaError_t launch_w4_up_gate(const void* a_rows, const void* w_gate, const void
     p.out = h_rows;
     p.status = status;
     p.idesc = idesc_f16(true, kBM, 256, false, true);
-    return launch<0>(mp, p, st, num_sms);
+    return launch<0, 0>(mp, p, st, num_sms);
 }
 
 cudaError_t launch_w4_down(const void* h_rows, const void* w_down, const void* s_down, const void* z_down,
@@ -397,7 +469,64 @@ cudaError_t launch_w4_down(const void* h_rows, const void* w_down, const void* s
     p.out = y_rows;
     p.status = status;
     p.idesc = idesc_f16(true, kBM, 256, false, true);
-    return launch<1>(mp, p, st, num_sms);
+    return launch<1, 0>(mp, p, st, num_sms);
+}
+
+cudaError_t launch_fp4_up_gate(const void* a_rows, const void* w_gate, const void* w_up, const void* s_gate,
+                               const void* s_up, const float* g_gate, const float* g_up, const Shape& s,
+                               const GroupTable& gt, int* status, void* h_rows, cudaStream_t st, int num_sms) {
+    if (gt.G <= 0 || gt.rows_capacity <= 0) return cudaSuccess;
+    W4Maps mp;
+    const uint64_t wrows = (uint64_t)s.E * s.d, grows = (uint64_t)s.E * (s.d / 16);
+    if (!make_map_box(&mp.a, a_rows, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, s.d, gt.rows_capacity, 64, kBM, true) ||
+        !packed_map(&mp.p0, w_gate, wrows, s.f, 128) || !packed_map(&mp.p1, w_up, wrows, s.f, 128) ||
+        !fp4_scale_map(&mp.s0, s_gate, grows, s.f, 128) || !fp4_scale_map(&mp.s1, s_up, grows, s.f, 128))
+        return cudaErrorInvalidValue;
+    mp.z0 = mp.s0;
+    mp.z1 = mp.s1;
+    W4Params p{};
+    p.g_rows = gt.rows;
+    p.g_start = gt.start;
+    p.g_weight = gt.weight;
+    p.G = gt.G;
+    p.K = s.d;
+    p.n_tiles = s.f / 128;
+    p.out_ld = s.f;
+    p.out = h_rows;
+    p.gs0 = g_gate;
+    p.gs1 = g_up;
+    p.status = status;
+    p.idesc = idesc_f16(true, kBM, 256, false, true);
+    return launch<0, 1>(mp, p, st, num_sms);
+}
+
+cudaError_t launch_fp4_down(const void* h_rows, const void* w_down, const void* s_down, const float* g_down,
+                            const Shape& s, const GroupTable& gt, int* status, float* y_rows, cudaStream_t st,
+                            int num_sms) {
+    if (gt.G <= 0 || gt.rows_capacity <= 0) return cudaSuccess;
+    W4Maps mp;
+    const uint64_t wrows = (uint64_t)s.E * s.f, grows = (uint64_t)s.E * (s.f / 16);
+    if (!make_map_box(&mp.a, h_rows, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, s.f, gt.rows_capacity, 64, kBM, true) ||
+        !packed_map(&mp.p0, w_down, wrows, s.d, 256) || !fp4_scale_map(&mp.s0, s_down, grows, s.d, 256))
+        return cudaErrorInvalidValue;
+    mp.p1 = mp.p0;
+    mp.s1 = mp.s0;
+    mp.z0 = mp.s0;
+    mp.z1 = mp.s0;
+    W4Params p{};
+    p.g_rows = gt.rows;
+    p.g_start = gt.start;
+    p.g_weight = gt.weight;
+    p.G = gt.G;
+    p.K = s.f;
+    p.n_tiles = s.d / 256;
+    p.out_ld = s.d;
+    p.out = y_rows;
+    p.gs0 = g_down;
+    p.gs1 = g_down;
+    p.status = status;
+    p.idesc = idesc_f16(true, kBM, 256, false, true);
+    return launch<1, 1>(mp, p, st, num_sms);
 }
 
 }  // namespace moe

@@ -67,8 +67,13 @@ void set_error(const char* fmt, ...) {
 
 size_t workspace_header_bytes() { return 256 + 3 * align256(sizeof(int) * kMaxGroups); }
 
+// Per-row activation scales: FP8 one per 1x128 block of x / h; INT8_CHANNEL one
+// per row of x and one per 1x128 block of h.
 size_t scale_bytes(const Shape& s, int dim) {
-    return s.dtype == MOE_DTYPE_FP8_BLOCK ? align256(sizeof(float) * (size_t)s.rows_capacity() * (dim / 128)) : 0;
+    if (s.dtype == MOE_DTYPE_FP8_BLOCK || (s.dtype == MOE_DTYPE_INT8_CHANNEL && dim == s.f))
+        return align256(sizeof(float) * (size_t)s.rows_capacity() * (dim / 128));
+    if (s.dtype == MOE_DTYPE_INT8_CHANNEL) return align256(sizeof(float) * (size_t)s.rows_capacity());
+    return 0;
 }
 
 size_t workspace_bytes(const Shape& s) {
@@ -126,7 +131,8 @@ int make_shape(const MoeDims* d, Shape* s) {
         return MOE_ERR_UNSUPPORTED;
     }
     if (d->dtype != MOE_DTYPE_F16 && d->dtype != MOE_DTYPE_BF16 && d->dtype != MOE_DTYPE_INT8 &&
-        d->dtype != MOE_DTYPE_FP8_BLOCK && d->dtype != MOE_DTYPE_W4A16) {
+        d->dtype != MOE_DTYPE_FP8_BLOCK && d->dtype != MOE_DTYPE_W4A16 && d->dtype != MOE_DTYPE_INT8_CHANNEL &&
+        d->dtype != MOE_DTYPE_NVFP4) {
         set_error("dtype %d not supported by this entry point", d->dtype);
         return MOE_ERR_UNSUPPORTED;
     }
@@ -142,14 +148,21 @@ int make_shape(const MoeDims* d, Shape* s) {
     s->k = d->top_k;
     s->dtype = d->dtype;
     s->router_dtype = d->router_dtype;
-    s->act_bf16 = d->dtype == MOE_DTYPE_BF16 || d->dtype == MOE_DTYPE_FP8_BLOCK || d->dtype == MOE_DTYPE_W4A16;
+    s->act_bf16 = d->dtype == MOE_DTYPE_BF16 || d->dtype == MOE_DTYPE_FP8_BLOCK || d->dtype == MOE_DTYPE_W4A16 ||
+                  d->dtype == MOE_DTYPE_INT8_CHANNEL || d->dtype == MOE_DTYPE_NVFP4;
+    if (d->dtype == MOE_DTYPE_NVFP4 && (!d->w4_scale_gate || !d->w4_scale_up || !d->w4_scale_down ||
+                                        !d->fp4_global_gate || !d->fp4_global_up || !d->fp4_global_down)) {
+        set_error("MOE_DTYPE_NVFP4 needs MoeDims.w4_scale_* (e4m3) and fp4_global_*");
+        return MOE_ERR_INVALID_ARG;
+    }
     if (d->dtype == MOE_DTYPE_W4A16 && (!d->w4_scale_gate || !d->w4_scale_up || !d->w4_scale_down ||
                                         !d->w4_zero_gate || !d->w4_zero_up || !d->w4_zero_down)) {
         set_error("MOE_DTYPE_W4A16 needs MoeDims.w4_scale_* and w4_zero_*");
         return MOE_ERR_INVALID_ARG;
     }
-    if (d->dtype == MOE_DTYPE_FP8_BLOCK && (!d->w_scale_gate || !d->w_scale_up || !d->w_scale_down)) {
-        set_error("MOE_DTYPE_FP8_BLOCK needs MoeDims.w_scale_gate / w_scale_up / w_scale_down");
+    if ((d->dtype == MOE_DTYPE_FP8_BLOCK || d->dtype == MOE_DTYPE_INT8_CHANNEL) &&
+        (!d->w_scale_gate || !d->w_scale_up || !d->w_scale_down)) {
+        set_error("dtype %d needs MoeDims.w_scale_gate / w_scale_up / w_scale_down", d->dtype);
         return MOE_ERR_INVALID_ARG;
     }
     if (d->cap > 0) s->cap = d->cap;
@@ -281,13 +294,13 @@ int check_args(const MoEArgs* a, int dtype) {
                         a->expert_counts && a->expert_token_ids && a->expert_token_weights &&
                         a->hidden_mlp_layer_2_out && a->final_output;
     bool fmt = false;
-    if (dtype == MOE_DTYPE_W4A16)
+    if (dtype == MOE_DTYPE_W4A16 || dtype == MOE_DTYPE_NVFP4)
         fmt = a->expert_up_proj_weights_int4 && a->expert_gate_proj_weights_int4 &&
               a->expert_down_proj_weights_int4 && a->per_expert_wmma_inputs && a->hidden_mlp_layer_1_out_fp16;
     else if (dtype == MOE_DTYPE_FP8_BLOCK)
         fmt = a->expert_up_proj_weights_fp8 && a->expert_gate_proj_weights_fp8 && a->expert_down_proj_weights_fp8 &&
               a->per_expert_wmma_inputs_fp8 && a->hidden_mlp_layer_1_out_fp8;
-    else if (dtype == MOE_DTYPE_INT8)
+    else if (dtype == MOE_DTYPE_INT8 || dtype == MOE_DTYPE_INT8_CHANNEL)
         fmt = a->expert_up_proj_weights_int8 && a->expert_gate_proj_weights_int8 &&
               a->expert_down_proj_weights_int8 && a->per_expert_wmma_inputs_int8 && a->hidden_mlp_layer_1_out_int8;
     else
@@ -295,8 +308,8 @@ int check_args(const MoEArgs* a, int dtype) {
               a->per_expert_wmma_inputs && a->hidden_mlp_layer_1_out_fp16;
     if (!common || !fmt) {
         set_error("a MoEArgs buffer needed by the %s path is null",
-                  dtype == MOE_DTYPE_INT8 ? "int8" : dtype == MOE_DTYPE_FP8_BLOCK ? "fp8"
-                                                  : dtype == MOE_DTYPE_W4A16  ? "4-bit" : "16-bit");
+                  dtype == MOE_DTYPE_INT8 || dtype == MOE_DTYPE_INT8_CHANNEL ? "int8" : dtype == MOE_DTYPE_FP8_BLOCK ? "fp8"
+                                                  : dtype == MOE_DTYPE_W4A16 || dtype == MOE_DTYPE_NVFP4 ? "4-bit" : "16-bit");
         return MOE_ERR_INVALID_ARG;
     }
     if (dtype == MOE_DTYPE_INT8 && !(a->scale_input_act > 0.0f && a->scale_mid_act > 0.0f)) {
@@ -336,9 +349,9 @@ struct FfnBuffers {
     const void *wg, *wu, *wd;
 };
 FfnBuffers ffn_buffers(const MoEArgs* a, const Shape& s) {
-    const bool i8 = s.dtype == MOE_DTYPE_INT8;
+    const bool i8 = s.dtype == MOE_DTYPE_INT8 || s.dtype == MOE_DTYPE_INT8_CHANNEL;
     FfnBuffers b;
-    if (s.dtype == MOE_DTYPE_W4A16) {
+    if (s.dtype == MOE_DTYPE_W4A16 || s.dtype == MOE_DTYPE_NVFP4) {
         b.a_rows = (void*)a->per_expert_wmma_inputs;
         b.h_rows = (void*)a->hidden_mlp_layer_1_out_fp16;
         b.wg = a->expert_gate_proj_weights_int4;
@@ -399,6 +412,17 @@ int enqueue_ffn(const MoEArgs* a, const MoeDims* dims, const Shape& s, const Gro
                 "4-bit down GEMM");
         return MOE_OK;
     }
+    if (s.dtype == MOE_DTYPE_NVFP4) {
+        MOE_TRY(launch_fp4_up_gate(fb.a_rows, fb.wg, fb.wu, dims->w4_scale_gate, dims->w4_scale_up,
+                                   dims->fp4_global_gate, dims->fp4_global_up, s, gt, status, fb.h_rows, stream,
+                                   num_sms),
+                "NVFP4 up/gate GEMM");
+        MOE_TRY(mark_stage(3, stream), "cudaEventRecord(stage event)");
+        MOE_TRY(launch_fp4_down(fb.h_rows, fb.wd, dims->w4_scale_down, dims->fp4_global_down, s, gt, status,
+                                a->hidden_mlp_layer_2_out, stream, num_sms),
+                "NVFP4 down GEMM");
+        return MOE_OK;
+    }
     if (s.dtype == MOE_DTYPE_FP8_BLOCK) {
         MOE_TRY(launch_fp8_up_gate(fb.a_rows, a_scale, fb.wg, fb.wu, dims->w_scale_gate, dims->w_scale_up, s, gt,
                                    status, fb.h_rows, h_scale, stream, num_sms),
@@ -407,6 +431,16 @@ int enqueue_ffn(const MoEArgs* a, const MoeDims* dims, const Shape& s, const Gro
         MOE_TRY(launch_fp8_down(fb.h_rows, h_scale, fb.wd, dims->w_scale_down, s, gt, status,
                                 a->hidden_mlp_layer_2_out, stream, num_sms),
                 "fp8 down GEMM");
+        return MOE_OK;
+    }
+    if (s.dtype == MOE_DTYPE_INT8_CHANNEL) {
+        MOE_TRY(launch_i8c_up_gate(fb.a_rows, a_scale, fb.wg, fb.wu, dims->w_scale_gate, dims->w_scale_up, s, gt,
+                                   status, fb.h_rows, h_scale, stream, num_sms),
+                "int8 per-channel up/gate GEMM");
+        MOE_TRY(mark_stage(3, stream), "cudaEventRecord(stage event)");
+        MOE_TRY(launch_i8c_down(fb.h_rows, h_scale, fb.wd, dims->w_scale_down, s, gt, status,
+                                a->hidden_mlp_layer_2_out, stream, num_sms),
+                "int8 per-channel down GEMM");
         return MOE_OK;
     }
     const GemmScales sc = scales_of(a, s);
@@ -535,8 +569,8 @@ extern "C" int moe_stage_expert_ffn(const MoEArgs* a, const MoeDims* dims, const
                 "cudaMemcpyAsync(group experts)");
     const GroupTable gt{ws.grp_rows, ws.grp_start, group_expert ? ws.grp_weight : nullptr, num_groups,
                         rows_capacity};
-    if (s.dtype == MOE_DTYPE_FP8_BLOCK) {
-        set_error("moe_stage_expert_ffn: the FP8 block path runs through moe_solve_v2 only in this build");
+    if (s.dtype == MOE_DTYPE_FP8_BLOCK || s.dtype == MOE_DTYPE_INT8_CHANNEL) {
+        set_error("moe_stage_expert_ffn: the dynamically quantised paths run through moe_solve_v2 only in this build");
         return MOE_ERR_UNSUPPORTED;
     }
     return enqueue_ffn(a, dims, s, gt, ws.status, nullptr, nullptr, st->num_sms, stream);

@@ -46,8 +46,8 @@ struct Workspace {
     int* row_base;      // [B, E]    first row of (b, e) inside expert e's block
     int* expert_rows;   // [E]       kept rows of expert e over all batches
     int* expert_start;  // [E]       first row of expert e: exclusive prefix of expert_rows
-    float* a_scale;     // FP8 path: [E*B*CAP, d/128] activation block scales
-    float* h_scale;     // FP8 path: [E*B*CAP, f/128] h block scales
+    float* a_scale;     // FP8: [E*B*CAP, d/128] activation block scales; INT8_CHANNEL: [E*B*CAP] row scales
+    float* h_scale;     // FP8 / INT8_CHANNEL: [E*B*CAP, f/128] h block scales
 };
 size_t workspace_header_bytes();
 
@@ -91,6 +91,14 @@ cudaError_t launch_fp8_up_gate(const void* a_rows, const float* a_scale, const v
 cudaError_t launch_fp8_down(const void* h_rows, const float* h_scale, const void* w_down, const float* s_down,
                             const Shape& s, const GroupTable& gt, int* status, float* y_rows, cudaStream_t st,
                             int num_sms);
+// expert_gemm_fp8.cu, int8 form: per-output-channel weight scales, per-row x
+// scales, per-(row, 128-feature block) h scales.
+cudaError_t launch_i8c_up_gate(const void* a_rows, const float* a_scale, const void* w_gate, const void* w_up,
+                               const float* s_gate, const float* s_up, const Shape& s, const GroupTable& gt,
+                               int* status, void* h_rows, float* h_scale, cudaStream_t st, int num_sms);
+cudaError_t launch_i8c_down(const void* h_rows, const float* h_scale, const void* w_down, const float* s_down,
+                            const Shape& s, const GroupTable& gt, int* status, float* y_rows, cudaStream_t st,
+                            int num_sms);
 
 // expert_gemm_w4.cu: 4-bit weights dequantised to bf16 in shared memory.
 cudaError_t launch_w4_up_gate(const void* a_rows, const void* w_gate, const void* w_up, const void* s_gate,
@@ -99,6 +107,14 @@ cudaError_t launch_w4_up_gate(const void* a_rows, const void* w_gate, const void
 cudaError_t launch_w4_down(const void* h_rows, const void* w_down, const void* s_down, const void* z_down,
                            const Shape& s, const GroupTable& gt, int* status, float* y_rows, cudaStream_t st,
                            int num_sms);
+// expert_gemm_w4.cu, NVFP4 form: e2m1 nibbles, e4m3 scales per 16 K-rows, f32
+// global scale per expert matrix.
+cudaError_t launch_fp4_up_gate(const void* a_rows, const void* w_gate, const void* w_up, const void* s_gate,
+                               const void* s_up, const float* g_gate, const float* g_up, const Shape& s,
+                               const GroupTable& gt, int* status, void* h_rows, cudaStream_t st, int num_sms);
+cudaError_t launch_fp4_down(const void* h_rows, const void* w_down, const void* s_down, const float* g_down,
+                            const Shape& s, const GroupTable& gt, int* status, float* y_rows, cudaStream_t st,
+                            int num_sms);
 
 // combine.cu: gate-weighted gather-sum into [B, N, d].
 cudaError_t launch_combine(const float* y_rows, const int* idx, const float* w, const Shape& s,

@@ -30,7 +30,6 @@ namespace moe {
 namespace {
 
 constexpr int kWarps = 8;
-constexpr int kTT = 4;  // tokens per warp
 
 template <typename TW>
 __device__ __forceinline__ void load_wr8(const TW* __restrict__ p, float (&w)[8]) {
@@ -93,7 +92,7 @@ __device__ __forceinline__ void topk_softmax_warp(const float* row, int E, int k
 // Work item = (TT tokens, one group of 8 experts); a CTA holds CT tokens
 // (CT a multiple of TT) and its warps take the CT/TT x E/8 items in turn, so
 // small token counts still spread over many warps (TT = 1) while large ones
-// reuse each router row for 4 tokens (TT = 4).
+// reuse each router row for 4 or 8 tokens.
 template <typename TX, typename TW, int TT>
 __global__ void __launch_bounds__(kWarps * 32) router_topk_kernel(
     const TX* __restrict__ x, const TW* __restrict__ wr, const float* __restrict__ bias,
@@ -178,18 +177,22 @@ __global__ void __launch_bounds__(kWarps * 32) router_topk_kernel(
 // j = 0..d-1 from 0.0f (+ bias[e]), which the oracle mirrors.  CTA = 16*MT
 // tokens x all E experts, 2E threads; thread (r, c) owns tokens MT*r.. and
 // experts 8c..8c+7 (MT=8: 64 accumulators, 4 vector shared loads per 64 FMAs); x and
-// Wr K-slices of 32 are staged in shared memory as f32 (x transposed).
+// Wr K-slices of 32 are staged in shared memory as f32 (x transposed),
+// double-buffered: the next slice is loaded into registers during the FMAs.
 constexpr int kTiledKC = 32;
 
-template <typename TX, typename TW, int MT>   // MT tokens per thread (8, or 4 for small grids)
-__global__ void __launch_bounds__(512) router_tiled_kernel(
+// 2E threads: up to 512 (E = 256) with MT = 4; MT = 8 needs ~150 registers,
+// so it runs only for E <= 128 (<= 256 threads).
+template <typename TX, typename TW, int MT>   // MT tokens per thread (8, or 4 for small grids / E > 128)
+__global__ void __launch_bounds__(MT == 8 ? 256 : 512) router_tiled_kernel(
     const TX* __restrict__ x, const TW* __restrict__ wr, const float* __restrict__ bias, int64_t T, int d, int E,
     int k, float* __restrict__ logits, int* __restrict__ idx, float* __restrict__ wts) {
     constexpr int kTiledTM = 16 * MT;
+    constexpr int kXVec = kTiledTM * (kTiledKC / 8) / 128;   // x vectors per thread (>= 128 threads)
     extern __shared__ float sm[];
-    float* xs = sm;                          // [kTiledKC][kTiledTM]
-    float* ws = xs + kTiledKC * kTiledTM;    // [kTiledKC][E]
-    float* lg = ws;                          // after the K loop: [kTiledTM][E]
+    float* xs = sm;                              // [2][kTiledKC][kTiledTM]
+    float* ws = xs + 2 * kTiledKC * kTiledTM;    // [2][kTiledKC][E]
+    float* lg = ws;                              // after the K loop: [kTiledTM][E]
     const int nthr = blockDim.x;
     const int cgroups = E / 8;
     const int r = threadIdx.x / cgroups, c = threadIdx.x - (threadIdx.x / cgroups) * cgroups;
@@ -199,45 +202,73 @@ __global__ void __launch_bounds__(512) router_tiled_kernel(
     for (int i = 0; i < MT; ++i)
 #pragma unroll
         for (int e = 0; e < 8; ++e) acc[i][e] = 0.0f;
-    for (int j0 = 0; j0 < d; j0 += kTiledKC) {
-        for (int v = threadIdx.x; v < kTiledTM * (kTiledKC / 8); v += nthr) {
-            const int tt = v / (kTiledKC / 8), jv = v - tt * (kTiledKC / 8);
-            const int64_t t = t0 + tt;
-            float f8[8];
-            if (t < T) {
-                const uint4 raw = __ldg(reinterpret_cast<const uint4*>(x + t * d + j0 + jv * 8));
-                const uint32_t* u = reinterpret_cast<const uint32_t*>(&raw);
+
+    // The next K slice is loaded into registers while the current one is
+    // multiplied out of shared memory (double-buffered, one barrier per slice).
+    uint4 xr[kXVec];
+    float wreg[2][8];
+    auto load_slice = [&](int j0) {
+#pragma unroll
+        for (int v = 0; v < kXVec; ++v) {
+            const int vi = threadIdx.x + v * nthr;
+            xr[v] = make_uint4(0u, 0u, 0u, 0u);
+            if (vi < kTiledTM * (kTiledKC / 8)) {
+                const int tt = vi / (kTiledKC / 8), jv = vi - tt * (kTiledKC / 8);
+                const int64_t t = t0 + tt;
+                if (t < T) xr[v] = __ldg(reinterpret_cast<const uint4*>(x + t * d + j0 + jv * 8));
+            }
+        }
+#pragma unroll
+        for (int v = 0; v < 2; ++v) {   // kTiledKC * E/8 vectors = 2 per thread
+            const int vi = threadIdx.x + v * nthr;
+            const int jj = vi / cgroups, cc = vi - jj * cgroups;
+            load_wr8(wr + (int64_t)(j0 + jj) * E + 8 * cc, wreg[v]);
+        }
+    };
+    auto store_slice = [&](int buf) {
+        float* xb = xs + buf * kTiledKC * kTiledTM;
+        float* wb = ws + buf * kTiledKC * E;
+#pragma unroll
+        for (int v = 0; v < kXVec; ++v) {
+            const int vi = threadIdx.x + v * nthr;
+            if (vi < kTiledTM * (kTiledKC / 8)) {
+                const int tt = vi / (kTiledKC / 8), jv = vi - tt * (kTiledKC / 8);
+                const uint32_t* u = reinterpret_cast<const uint32_t*>(&xr[v]);
 #pragma unroll
                 for (int q = 0; q < 4; ++q) {
                     const float2 p = F16Traits<TX>::unpack2(u[q]);
-                    f8[2 * q] = p.x;
-                    f8[2 * q + 1] = p.y;
+                    xb[(jv * 8 + 2 * q) * kTiledTM + tt] = p.x;
+                    xb[(jv * 8 + 2 * q + 1) * kTiledTM + tt] = p.y;
                 }
-            } else {
-#pragma unroll
-                for (int q = 0; q < 8; ++q) f8[q] = 0.0f;
             }
+        }
 #pragma unroll
-            for (int q = 0; q < 8; ++q) xs[(jv * 8 + q) * kTiledTM + tt] = f8[q];
+        for (int v = 0; v < 2; ++v) {
+            const int vi = threadIdx.x + v * nthr;
+            const int jj = vi / cgroups, cc = vi - jj * cgroups;
+            float4* dst = reinterpret_cast<float4*>(wb + jj * E + 8 * cc);
+            dst[0] = make_float4(wreg[v][0], wreg[v][1], wreg[v][2], wreg[v][3]);
+            dst[1] = make_float4(wreg[v][4], wreg[v][5], wreg[v][6], wreg[v][7]);
         }
-        for (int v = threadIdx.x; v < kTiledKC * cgroups; v += nthr) {
-            const int jj = v / cgroups, cc = v - jj * cgroups;
-            float w8[8];
-            load_wr8(wr + (int64_t)(j0 + jj) * E + 8 * cc, w8);
-            float4* dst = reinterpret_cast<float4*>(ws + jj * E + 8 * cc);
-            dst[0] = make_float4(w8[0], w8[1], w8[2], w8[3]);
-            dst[1] = make_float4(w8[4], w8[5], w8[6], w8[7]);
-        }
-        __syncthreads();
+    };
+    const int nslices = d / kTiledKC;
+    load_slice(0);
+    store_slice(0);
+    __syncthreads();
+    for (int sl = 0; sl < nslices; ++sl) {
+        const int buf = sl & 1;
+        if (sl + 1 < nslices) load_slice((sl + 1) * kTiledKC);
+        const float* xb = xs + buf * kTiledKC * kTiledTM;
+        const float* wb = ws + buf * kTiledKC * E;
 #pragma unroll 4
         for (int jj = 0; jj < kTiledKC; ++jj) {
-            const float4 wa = *reinterpret_cast<const float4*>(ws + jj * E + 8 * c);
-            const float4 wb = *reinterpret_cast<const float4*>(ws + jj * E + 8 * c + 4);
-            const float wv[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+            const float4 wa = *reinterpret_cast<const float4*>(wb + jj * E + 8 * c);
+            const float4 wc = *reinterpret_cast<const float4*>(wb + jj * E + 8 * c + 4);
+            const float wv[8] = {wa.x, wa.y, wa.z, wa.w, wc.x, wc.y, wc.z, wc.w};
             float xv[MT];
 #pragma unroll
             for (int i = 0; i < MT; i += 4) {
-                const float4 xa = *reinterpret_cast<const float4*>(xs + jj * kTiledTM + MT * r + i);
+                const float4 xa = *reinterpret_cast<const float4*>(xb + jj * kTiledTM + MT * r + i);
                 xv[i] = xa.x; xv[i + 1] = xa.y; xv[i + 2] = xa.z; xv[i + 3] = xa.w;
             }
 #pragma unroll
@@ -245,6 +276,7 @@ __global__ void __launch_bounds__(512) router_tiled_kernel(
 #pragma unroll
                 for (int e = 0; e < 8; ++e) acc[i][e] = fmaf(xv[i], wv[e], acc[i][e]);
         }
+        if (sl + 1 < nslices) store_slice(buf ^ 1);
         __syncthreads();
     }
 #pragma unroll
@@ -266,30 +298,32 @@ __global__ void __launch_bounds__(512) router_tiled_kernel(
     }
 }
 
+template <typename TX, typename TW, int TT>
+cudaError_t launch_items(const void* x, const void* wr, const float* bias, const Shape& s, int CT, float* logits,
+                         int* idx, float* w, cudaStream_t st) {
+    const size_t smem = sizeof(float) * (size_t)CT * s.E;
+    const int64_t blocks = (s.T() + CT - 1) / CT;
+    auto kern = router_topk_kernel<TX, TW, TT>;
+    cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (err != cudaSuccess) return err;
+    kern<<<(unsigned)blocks, kWarps * 32, smem, st>>>((const TX*)x, (const TW*)wr, bias, s.T(), s.d, s.E, s.k, CT,
+                                                      logits, idx, w);
+    return cudaGetLastError();
+}
+
 template <typename TX, typename TW>
 cudaError_t launch_typed(const void* x, const void* wr, const float* bias, const Shape& s,
                          float* logits, int* idx, float* w, cudaStream_t st) {
-    // 4 tokens per item and 32 per CTA when that still gives two CTAs per SM;
-    // otherwise one token per item and fewer tokens per CTA.
-    const bool big = s.T() >= (int64_t)kWarps * kTT * 296;
-    const int CT = big ? kWarps * kTT : (int)std::max<int64_t>(1, std::min<int64_t>(32, s.T() / 296));
-    const size_t smem = sizeof(float) * (size_t)CT * s.E;
-    const int64_t blocks = (s.T() + CT - 1) / CT;
-    cudaError_t err;
-    if (big) {
-        auto kern = router_topk_kernel<TX, TW, kTT>;
-        err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (err != cudaSuccess) return err;
-        kern<<<(unsigned)blocks, kWarps * 32, smem, st>>>((const TX*)x, (const TW*)wr, bias, s.T(), s.d, s.E, s.k,
-                                                          CT, logits, idx, w);
-    } else {
-        auto kern = router_topk_kernel<TX, TW, 1>;
-        err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (err != cudaSuccess) return err;
-        kern<<<(unsigned)blocks, kWarps * 32, smem, st>>>((const TX*)x, (const TW*)wr, bias, s.T(), s.d, s.E, s.k,
-                                                          CT, logits, idx, w);
-    }
-    return cudaGetLastError();
+    // Tokens per item TT: the largest of 8, 4, 1 that still leaves two CTAs of
+    // work items per SM (each router row read from L2 serves TT tokens);
+    // tokens per CTA CT: one item per warp.
+    const int G = s.E / 8;
+    const int64_t want = 2 * 148 * kWarps;
+    const int TT = s.T() * G / 8 >= want ? 8 : (s.T() * G / 4 >= want ? 4 : 1);
+    const int CT = TT * std::max(1, kWarps / G);
+    if (TT == 8) return launch_items<TX, TW, 8>(x, wr, bias, s, CT, logits, idx, w, st);
+    if (TT == 4) return launch_items<TX, TW, 4>(x, wr, bias, s, CT, logits, idx, w, st);
+    return launch_items<TX, TW, 1>(x, wr, bias, s, CT, logits, idx, w, st);
 }
 
 template <typename TX, typename TW, int MT>
@@ -297,7 +331,8 @@ cudaError_t launch_tiled(const void* x, const void* wr, const float* bias, const
                          float* w, cudaStream_t st) {
     constexpr int kTiledTM = 16 * MT;
     const int threads = 2 * s.E;
-    const size_t smem = sizeof(float) * ((size_t)kTiledKC * kTiledTM + (size_t)std::max(kTiledKC, kTiledTM) * s.E);
+    const size_t smem =
+        sizeof(float) * (2 * (size_t)kTiledKC * kTiledTM + (size_t)std::max(2 * kTiledKC, kTiledTM) * s.E);
     auto kern = router_tiled_kernel<TX, TW, MT>;
     cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (err != cudaSuccess) return err;
@@ -312,7 +347,7 @@ cudaError_t launch_any(const void* x, const void* wr, const float* bias, const S
                        float* w, cudaStream_t st) {
     if (s.E < kRouterTiledMinExperts) return launch_typed<TX, TW>(x, wr, bias, s, logits, idx, w, st);
     // less than one CTA of 128 tokens per SM: halve the tokens per thread
-    return s.T() >= (int64_t)128 * 148 ? launch_tiled<TX, TW, 8>(x, wr, bias, s, logits, idx, w, st)
+    return s.T() >= (int64_t)128 * 148 && s.E <= 128 ? launch_tiled<TX, TW, 8>(x, wr, bias, s, logits, idx, w, st)
                                        : launch_tiled<TX, TW, 4>(x, wr, bias, s, logits, idx, w, st);
 }
 

@@ -32,7 +32,7 @@ class MoeLayer:
         z = lambda *s, dt: torch.empty(*s, dtype=dt, device=dev)  # noqa: E731
         self.x = z(max(T, 1), d, dt=t16)
         self.wr = z(d, E, dt=torch.float32 if cfg.router_f32 else t16)
-        wt = torch.int8 if cfg.int8 else (torch.uint8 if cfg.fp8 else t16)
+        wt = torch.int8 if (cfg.int8 or cfg.int8ch) else (torch.uint8 if cfg.fp8 else t16)
         if cfg.w4:
             self.wg = z(E, d, f // 2, dt=torch.uint8)
             self.wu = z(E, d, f // 2, dt=torch.uint8)
@@ -68,16 +68,21 @@ class MoeLayer:
         if self.cfg.T > 0:
             put(self.x, inputs["x"])
         put(self.wr, inputs["wr"])
-        sfx = "_q" if (self.cfg.int8 or self.cfg.fp8 or self.cfg.w4) else ""
+        sfx = "_q" if (self.cfg.int8 or self.cfg.int8ch or self.cfg.fp8 or self.cfg.w4) else ""
         put(self.wg, inputs["wg" + sfx])
         put(self.wu, inputs["wu" + sfx])
         put(self.wd, inputs["wd" + sfx])
         if self.cfg.int8:
             self.scales = {k: inputs[k] for k in ("s_in", "s_gate", "s_up", "s_mid", "s_down")}
-        if self.cfg.w4:
+        if self.cfg.nvfp4:
+            self.w4sz = [torch.from_numpy(np.ascontiguousarray(inputs[k])).to(self.device)
+                         for k in ("wg_s", "wu_s", "wd_s")]
+            self.fp4g = [torch.from_numpy(np.ascontiguousarray(inputs[k], np.float32)).to(self.device)
+                         for k in ("wg_g", "wu_g", "wd_g")]
+        elif self.cfg.w4:
             self.w4sz = [torch.from_numpy(np.ascontiguousarray(inputs[k]).view(np.int16)).to(self.device)
                          for k in ("wg_s", "wu_s", "wd_s", "wg_z", "wu_z", "wd_z")]
-        if self.cfg.fp8:
+        if self.cfg.channel_scaled:
             self.wscale = [torch.from_numpy(np.ascontiguousarray(inputs[k])).to(self.device)
                            for k in ("sg", "su", "sd")]
         if inputs.get("bias") is not None:
@@ -102,6 +107,12 @@ class MoeLayer:
             a.expert_down_proj_weights_fp8 = p(self.wd)
             a.per_expert_wmma_inputs_fp8 = p(self.a_rows)
             a.hidden_mlp_layer_1_out_fp8 = p(self.h_rows)
+        elif self.cfg.int8ch:
+            a.expert_up_proj_weights_int8 = p(self.wu)
+            a.expert_gate_proj_weights_int8 = p(self.wg)
+            a.expert_down_proj_weights_int8 = p(self.wd)
+            a.per_expert_wmma_inputs_int8 = p(self.a_rows)
+            a.hidden_mlp_layer_1_out_int8 = p(self.h_rows)
         elif self.cfg.int8:
             a.expert_up_proj_weights_int8 = p(self.wu)
             a.expert_gate_proj_weights_int8 = p(self.wg)
@@ -131,10 +142,13 @@ class MoeLayer:
         return a
 
     def dims(self):
-        ws = tuple(t.data_ptr() for t in self.wscale) if self.cfg.fp8 else (None, None, None)
-        w4 = tuple(t.data_ptr() for t in self.w4sz) if self.cfg.w4 else (None,) * 6
+        ws = tuple(t.data_ptr() for t in self.wscale) if self.cfg.channel_scaled else (None, None, None)
+        w4 = tuple(t.data_ptr() for t in self.w4sz) if self.cfg.w4 else ()
+        w4 = w4 + (None,) * (6 - len(w4))
+        g4 = tuple(t.data_ptr() for t in self.fp4g) if self.cfg.nvfp4 else (None,) * 3
         return self.cfg.dims(None if self.bias is None else self.bias.data_ptr(),
-                             None if self.out16 is None else self.out16.data_ptr(), w_scales=ws, w4=w4)
+                             None if self.out16 is None else self.out16.data_ptr(), w_scales=ws, w4=w4,
+                             fp4_global=g4)
 
     def forward(self, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
         """Enqueues one layer call on `stream` (default: torch's current stream)."""

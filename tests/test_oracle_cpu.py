@@ -156,3 +156,89 @@ def test_logit_order_many_experts_is_sequential():
             for j in range(256):
                 acc = np.float32(np.float64(acc) + x[t, j] * w[j, e])   # exact product + one rounding
             assert np.float32(acc + inp["bias"][e]) == r["logits"][t, e]
+
+
+def test_int8_channel_quantiser_matches_numpy():
+    """Per-output-channel int8: s = amax over K / 127 (1 for a zero column),
+    q = clamp(rint(w / s), +-127)."""
+    rng = np.random.default_rng(3)
+    w = rng.standard_normal((2, 64, 48)).astype(np.float32)
+    w[1, :, 5] = 0.0
+    b16 = (w.view(np.uint32) >> 16).astype(np.uint16)
+    q, sc = sm.quantize_int8_channel(b16, bf16=True)
+    vals = (b16.astype(np.uint32) << 16).view(np.float32)
+    amax = np.abs(vals).max(axis=1)
+    s = np.where(amax > 0, amax / np.float32(127.0), np.float32(1.0)).astype(np.float32)
+    assert np.array_equal(sc, s)
+    assert np.array_equal(q, np.clip(np.rint(vals / s[:, None, :]), -127, 127).astype(np.int8))
+
+
+def test_int8_channel_oracle_matches_numpy_restatement():
+    """The C oracle's INT8_CHANNEL FFN against an independent numpy restatement
+    (exact integer sums, the same f32 scale products, per-block h scales)."""
+    cfg = sm.LayerConfig(1, 24, 256, 256, 8, 2, 2.0, dtype=sm.DTYPE_INT8_CHANNEL)
+    inp = sm.make_inputs(cfg, 5)
+    ref = O.forward(inp, cfg, nthreads=2)
+    f32 = np.float32
+    x = (inp["x"].astype(np.uint32) << 16).view(np.float32)
+    out = np.zeros((cfg.T, cfg.d_model), np.float32)
+    for t in range(cfg.T):
+        for l in range(cfg.top_k):
+            if ref["route_slot"][t * cfg.top_k + l] < 0:
+                continue
+            e = ref["idx"][t, l]
+            amax = np.abs(x[t]).max()
+            sx = amax / f32(127) if amax > 0 else f32(1)
+            qa = np.clip(np.rint(x[t] / sx), -127, 127).astype(np.int64)
+            G = qa @ inp["wg_q"][e].astype(np.int64)
+            U = qa @ inp["wu_q"][e].astype(np.int64)
+            g = G.astype(np.float32) * (sx * inp["sg"][e])
+            u = U.astype(np.float32) * (sx * inp["su"][e])
+            h = u * (g / (f32(1) + np.exp(-g)))
+            hb = h.reshape(-1, 128)
+            hm = np.abs(hb).max(axis=1)
+            sh = np.where(hm > 0, hm / f32(127), f32(1)).astype(np.float32)
+            qh = np.clip(np.rint(hb / sh[:, None]), -127, 127).astype(np.int64)
+            acc = np.zeros(cfg.d_model, np.float32)
+            for kb in range(qh.shape[0]):
+                P = qh[kb] @ inp["wd_q"][e, kb * 128:(kb + 1) * 128].astype(np.int64)
+                acc = (P.astype(np.float64) * np.float64(sh[kb]) + acc).astype(np.float32)
+            y = acc * inp["sd"][e]
+            out[t] += ref["w"][t, l] * y
+    np.testing.assert_allclose(ref["out"], out, rtol=1e-4, atol=1e-5 * float(np.abs(out).max()))
+
+
+def test_nvfp4_quantiser_matches_numpy():
+    """NVFP4: g = amax/(448*6); per 16 K-rows and column s = e4m3(amax/(6g));
+    q = nearest e2m1 (ties to the even code) of w / (s g), saturating at 6."""
+    rng = np.random.default_rng(4)
+    w = (rng.standard_normal((2, 64, 16)) * 0.1).astype(np.float32)
+    w[0, 16:32, 3] = 0.0
+    b16 = (w.view(np.uint32) >> 16).astype(np.uint16)
+    q, s, g = sm.quantize_nvfp4(b16, bf16=True)
+    vals = (b16.astype(np.uint32) << 16).view(np.float32)
+    L = O.lib()
+    mags = np.array([0, 0.5, 1, 1.5, 2, 3, 4, 6], np.float64)
+    for e in range(2):
+        ge = np.float32(np.abs(vals[e]).max() / np.float32(448.0 * 6.0))
+        assert g[e] == ge
+        for grp in range(4):
+            blk = vals[e, grp * 16:(grp + 1) * 16]
+            for n in range(16):
+                m = np.abs(blk[:, n]).max()
+                sc = s[e, grp, n]
+                if m == 0:
+                    assert sc == 0x38
+                else:
+                    assert sc == L.oracle_e4m3(float(np.float32(m / (np.float32(6.0) * ge))))
+                div = np.float32(np.float32(L.oracle_e4m3_decode(int(sc))) * ge)
+                for i in range(16):
+                    k = grp * 16 + i
+                    byte = q[e, k, (n >> 3) * 4 + ((4 * ((n & 7) >> 1) + 16 * (n & 1)) >> 3)]
+                    code = (byte >> ((4 * ((n & 7) >> 1) + 16 * (n & 1)) & 7)) & 15
+                    a = abs(float(np.float32(blk[i, n] / div)))
+                    d = np.abs(mags - a)
+                    best = 7 if a >= 6 else min((c for c in range(8) if d[c] == d.min()), key=lambda c: c & 1)
+                    assert code & 7 == best, (e, k, n, a, code)
+                    if blk[i, n] < 0:
+                        assert code & 8

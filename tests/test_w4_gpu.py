@@ -45,3 +45,43 @@ def test_w4_deepseek_decode_shape(gpu):
     Zipf(1.0) bias."""
     cfg = sm.LayerConfig(1, 512, 7168, 2048, 32, 8, 1.25, dtype=sm.DTYPE_W4A16, router_f32=True, zipf_s=1.0)
     w4_check(cfg, gpu, seed=3, t_end=64)
+
+
+# ---- NVFP4 (config 5's second weight format) --------------------------------
+def test_nvfp4_small(gpu):
+    _, _, err = w4_check(sm.LayerConfig(1, 512, 512, 384, 8, 2, 1.25, dtype=sm.DTYPE_NVFP4), gpu)
+    assert err < 1e-2   # the staged bf16 weights are exact; only h's bf16 rounding remains
+
+
+def test_nvfp4_drops_many_experts(gpu):
+    cfg = sm.LayerConfig(2, 300, 1024, 256, 64, 6, 1.0, dtype=sm.DTYPE_NVFP4, zipf_s=1.1)
+    L, ref, _ = w4_check(cfg, gpu, seed=2)
+    assert (ref["route_slot"] < 0).any()
+
+
+def test_nvfp4_every_code_and_tiny_scales(gpu):
+    """Weights built so every e2m1 code (the subnormal 0.5 included) and both
+    extreme e4m3 scales occur: the staged weight e2m1 * s * 2^-8 must stay
+    exact, so the output error stays at the bf16 h rounding level."""
+    cfg = sm.LayerConfig(1, 256, 256, 256, 8, 2, 2.0, dtype=sm.DTYPE_NVFP4)
+    inp = sm.make_inputs(cfg, 6)
+    rng = np.random.default_rng(0)
+    mags = np.array([0, 0.5, 1, 1.5, 2, 3, 4, 6], np.float32)
+    for n, K, N in (("wg", 256, 256), ("wu", 256, 256), ("wd", 256, 256)):
+        v = mags[rng.integers(0, 8, (8, K, N))] * np.where(rng.random((8, K, N)) < 0.5, -1, 1)
+        v *= np.float32(2.0) ** rng.integers(-14, 2, (8, K // 16, 1, N)).repeat(16, 1).reshape(8, K, N)
+        v = v.astype(np.float32) * np.float32(0.05)
+        b16 = (v.view(np.uint32) >> 16).astype(np.uint16)
+        q, s, g = sm.quantize_nvfp4(b16, bf16=True)
+        inp[n + "_q"], inp[n + "_s"], inp[n + "_g"] = q, s, g
+        codes = np.concatenate([(q & 15).ravel(), (q >> 4).ravel()])
+        assert len(np.unique(codes & 7)) == 8
+    L = run(cfg, inp, gpu)
+    ref = O.forward(inp, cfg)
+    check_routing(L, ref, cfg)
+    assert max_abs_rel(L.out.cpu().numpy(), ref["out"]) < 1e-2
+
+
+def test_nvfp4_deepseek_decode_shape(gpu):
+    cfg = sm.LayerConfig(1, 512, 7168, 2048, 32, 8, 1.25, dtype=sm.DTYPE_NVFP4, router_f32=True, zipf_s=1.0)
+    w4_check(cfg, gpu, seed=3, t_end=64)
