@@ -33,4 +33,26 @@ template <> struct F16Traits<__nv_bfloat16> {
     }
 };
 
+// Coalesced store of one warp's 32-row x 16-column f32 block: lane l holds
+// row l's 16 values v[0..15] (an epilogue thread owns one TMEM lane = one
+// row).  Storing from that layout directly would make every vector store
+// touch 32 rows; instead the block goes through a 2 KB shared-memory stage
+// (16-byte slots XOR-swizzled by (row >> 1) & 3, conflict-free both ways) and
+// each store instruction then writes 8 rows x 64 contiguous bytes.  Rows
+// >= nrows are not written.  Must be called by all 32 lanes.
+__device__ __forceinline__ void warp_store_rows16(float4* stage, const float* v, float* g, int64_t ld, int nrows,
+                                                  int lane) {
+    const int sw = (lane >> 1) & 3;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) stage[lane * 4 + (j ^ sw)] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int r = 8 * i + (lane >> 2), c = lane & 3;
+        const float4 val = stage[r * 4 + (c ^ ((r >> 1) & 3))];
+        if (r < nrows) *reinterpret_cast<float4*>(g + (int64_t)r * ld + 4 * c) = val;
+    }
+    __syncwarp();
+}
+
 }  // namespace moe

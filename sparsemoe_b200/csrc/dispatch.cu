@@ -221,19 +221,30 @@ __global__ void __launch_bounds__(kThreads) dispatch_gather_fp8_kernel(
     const __nv_bfloat16* src = x + ((int64_t)b * N + t) * d;
     const int64_t row = (int64_t)expert_start[e] + row_base[be] + s;
     uint8_t* dst = a_rows + row * d;
-    const int nblk = d / 128;
-    for (int blk = 0; blk < nblk; ++blk) {
-        const uint2 raw = __ldg(reinterpret_cast<const uint2*>(src + blk * 128) + lane);
-        const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
-        const float2 v0 = __bfloat1622float2(h2[0]), v1 = __bfloat1622float2(h2[1]);
-        float amax = fmaxf(fmaxf(fabsf(v0.x), fabsf(v0.y)), fmaxf(fabsf(v1.x), fabsf(v1.y)));
+    const int nblk = d / 128;   // a multiple of 2 (d % 256 == 0)
+    // 8 blocks' loads in flight per round (lane: 4 elements of each block)
+    for (int b0 = 0; b0 < nblk; b0 += 8) {
+        const int nb = min(8, nblk - b0);
+        uint2 raw[8];
 #pragma unroll
-        for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
-        const float sc = amax > 0.0f ? amax / 448.0f : 1.0f;
-        const uint32_t lo = __nv_cvt_float2_to_fp8x2(make_float2(v0.x / sc, v0.y / sc), __NV_SATFINITE, __NV_E4M3);
-        const uint32_t hi = __nv_cvt_float2_to_fp8x2(make_float2(v1.x / sc, v1.y / sc), __NV_SATFINITE, __NV_E4M3);
-        reinterpret_cast<uint32_t*>(dst + blk * 128)[lane] = lo | (hi << 16);
-        if (lane == 0) a_scale[row * nblk + blk] = sc;
+        for (int i = 0; i < 8; ++i)
+            if (i < nb) raw[i] = __ldg(reinterpret_cast<const uint2*>(src + (b0 + i) * 128) + lane);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            if (i >= nb) break;
+            const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw[i]);
+            const float2 v0 = __bfloat1622float2(h2[0]), v1 = __bfloat1622float2(h2[1]);
+            float amax = fmaxf(fmaxf(fabsf(v0.x), fabsf(v0.y)), fmaxf(fabsf(v1.x), fabsf(v1.y)));
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+            const float sc = amax > 0.0f ? amax / 448.0f : 1.0f;
+            const uint32_t lo =
+                __nv_cvt_float2_to_fp8x2(make_float2(v0.x / sc, v0.y / sc), __NV_SATFINITE, __NV_E4M3);
+            const uint32_t hi =
+                __nv_cvt_float2_to_fp8x2(make_float2(v1.x / sc, v1.y / sc), __NV_SATFINITE, __NV_E4M3);
+            reinterpret_cast<uint32_t*>(dst + (b0 + i) * 128)[lane] = lo | (hi << 16);
+            if (lane == 0) a_scale[row * nblk + b0 + i] = sc;
+        }
     }
 }
 

@@ -56,7 +56,7 @@ constexpr int kBBytes = 128 * kUmmaN;               // 32 KB: 128 bytes of K row
 constexpr int kStageBytes = kABytes + kBBytes;
 constexpr int kAccCols = kUmmaN;
 constexpr int kTmemCols = 2 * kAccCols;
-constexpr size_t kSmemBytes = 1024 + (size_t)kStages * kStageBytes + 256;
+constexpr size_t kSmemBytes = 1024 + (size_t)kStages * kStageBytes + 256 + 4 * 2048;
 
 struct GemmParams {
     const int* g_rows;       // [G] rows of each group
@@ -186,6 +186,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* tfull = empty + kStages;
     uint64_t* tempty = tfull + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+    uint8_t* sStage = sB + kStages * kBBytes + 256;   // 4 epilogue warps x 2 KB
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -303,7 +304,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int t = blockIdx.x; t < total; t += gridDim.x) {
             int e, m, n;
             decode_tile(t, s_pre, s_mt, p.G, e, m, n);
-            if (!mbar_wait(&tfull[acc], aph, p.status, kDevErrTimeout)) break;
+            if (!mbar_wait_warp(&tfull[acc], aph, p.status, kDevErrTimeout)) break;
             tc_fence_after();
             const int row_local = m * kBM + row_in_tile;
             const bool valid = row_local < s_rows[e];
@@ -322,20 +323,23 @@ __global__ void __launch_bounds__(kThreads, 1)
                     Fmt::swiglu_store(g, u, p, h + c * Fmt::kElemBytes, valid);
                 }
             } else {
-                float* y = reinterpret_cast<float*>(p.out) + out_row * p.out_ld + n * kOutN;
+                // rows of this warp's quarter: [warp_row0, warp_row0 + 32), coalesced through smem
+                const int warp_row0 = m * kBM + q * 32;
+                const int nrows = s_rows[e] - warp_row0;
+                float* y = reinterpret_cast<float*>(p.out) + ((int64_t)s_start[e] + warp_row0) * p.out_ld +
+                           n * kOutN;
+                float4* stage = reinterpret_cast<float4*>(sStage) + (warp - 2) * 128;
 #pragma unroll 1
                 for (int c = 0; c < 256; c += 32) {
                     uint32_t r[32];
                     tmem_ld_32x32b_x32(taddr + c, r);
                     tmem_wait_ld();
                     if (c == 224) { tc_fence_before(); mbar_arrive(&tempty[acc]); }
-                    if (valid) {
-                        float4* dst = reinterpret_cast<float4*>(y + c);
+                    float v[32];
 #pragma unroll
-                        for (int v = 0; v < 8; ++v)
-                            dst[v] = make_float4(Fmt::down_value(r[4 * v], p), Fmt::down_value(r[4 * v + 1], p),
-                                                 Fmt::down_value(r[4 * v + 2], p), Fmt::down_value(r[4 * v + 3], p));
-                    }
+                    for (int i = 0; i < 32; ++i) v[i] = Fmt::down_value(r[i], p);
+                    warp_store_rows16(stage, v, y + c, p.out_ld, nrows, lane);
+                    warp_store_rows16(stage, v + 16, y + c + 16, p.out_ld, nrows, lane);
                 }
             }
             acc ^= 1;

@@ -63,7 +63,8 @@ constexpr int kBBytes = 128 * 256;
 constexpr int kStageBytes = kABytes + kBBytes;
 constexpr int kChunkBytes = 128 * 128;   // 128 K-rows x 128 columns (one swizzle span)
 constexpr int kTmemCols = 512;
-constexpr size_t kSmemBytes = 1024 + (size_t)kStages * kStageBytes + 1024;
+constexpr size_t kStageOutBytes = kPromoWarps * 2048;   // per-warp 32x16 f32 staging for coalesced Y stores
+constexpr size_t kSmemBytes = 1024 + (size_t)kStages * kStageBytes + 256 + kStageOutBytes;
 
 struct Fp8Params {
     const int* g_rows;
@@ -82,7 +83,9 @@ struct Fp8Params {
     uint32_t idesc;
 };
 
-__device__ __forceinline__ void decode_tile(int t, const int* pre, const int* mt, int G, int& g, int& m, int& n) {
+// m-tiles of a group come from its row count (no per-group table: shared
+// memory is at its limit in this kernel)
+__device__ __forceinline__ void decode_tile(int t, const int* pre, const int* rows, int G, int& g, int& m, int& n) {
     int lo = 0, hi = G - 1;
     while (lo < hi) {
         const int mid = (lo + hi + 1) >> 1;
@@ -90,8 +93,9 @@ __device__ __forceinline__ void decode_tile(int t, const int* pre, const int* mt
     }
     g = lo;
     const int local = t - pre[g];
-    n = local / mt[g];
-    m = local - n * mt[g];
+    const int mt = (rows[g] + kBM - 1) / kBM;
+    n = local / mt;
+    m = local - n * mt;
 }
 
 __device__ __forceinline__ void ffma2(float& a0, float& a1, float p0, float p1, float s) {
@@ -125,7 +129,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const __grid_constant__ CUtensorMap tmB1, const Fp8Params p) {
     extern __shared__ uint8_t smem_raw[];
     __shared__ int s_pre[kMaxGroups + 1];
-    __shared__ int s_mt[kMaxGroups];
     __shared__ int s_rows[kMaxGroups];
     __shared__ int s_start[kMaxGroups];
     __shared__ int s_wt[kMaxGroups];
@@ -139,6 +142,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* pfull = empty + kStages;
     uint64_t* pempty = pfull + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pempty + 2);
+    float4* sStage = reinterpret_cast<float4*>(sB + kStages * kBBytes + 256);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
@@ -156,14 +160,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int g = threadIdx.x; g < p.G; g += kThreads) {
         const int r = p.g_rows[g];
         s_rows[g] = r;
-        s_mt[g] = (r + kBM - 1) / kBM;
         s_start[g] = p.g_start[g];
         s_wt[g] = p.g_weight ? p.g_weight[g] : g;
     }
     __syncthreads();
     if (threadIdx.x == 0) {
         int acc = 0;
-        for (int g = 0; g < p.G; ++g) { s_pre[g] = acc; acc += s_mt[g] * p.n_tiles; }
+        for (int g = 0; g < p.G; ++g) { s_pre[g] = acc; acc += (s_rows[g] + kBM - 1) / kBM * p.n_tiles; }
         s_pre[p.G] = acc;
     }
     tc_fence_before();
@@ -179,7 +182,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t ph = 0;
             for (int t = blockIdx.x; t < total; t += gridDim.x) {
                 int g, m, n;
-                decode_tile(t, s_pre, s_mt, p.G, g, m, n);
+                decode_tile(t, s_pre, s_rows, p.G, g, m, n);
                 const int a_row = s_start[g] + m * kBM;
                 const int b_row = s_wt[g] * p.K;
                 for (int kb = 0; kb < kblocks; ++kb) {
@@ -247,7 +250,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t pph = 0;
         for (int t = blockIdx.x; t < total; t += gridDim.x) {
             int g, m, n;
-            decode_tile(t, s_pre, s_mt, p.G, g, m, n);
+            decode_tile(t, s_pre, s_rows, p.G, g, m, n);
             const int row_local = m * kBM + row_in_tile;
             const bool valid = row_local < s_rows[g];
             const int64_t row = (int64_t)s_start[g] + row_local;
@@ -268,7 +271,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const float sx = p.a_scale[valid ? row : (int64_t)s_start[g]];
                 const float* sg = p.w_scale0 + (int64_t)wexp * p.out_ld + n * 128 + 64 * half;
                 const float* su = p.w_scale1 + (int64_t)wexp * p.out_ld + n * 128 + 64 * half;
-                if (!mbar_wait(&pfull[pb], pph, p.status, kDevErrTimeout)) break;
+                if (!mbar_wait_warp(&pfull[pb], pph, p.status, kDevErrTimeout)) break;
                 tc_fence_after();
                 const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + pb * 256;
 #pragma unroll
@@ -303,7 +306,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             sw1_n = kMode == 0 ? wscale(p.w_scale1, kb + 1, wcol) : sw0_n;
                         }
                     }
-                    if (!mbar_wait(&pfull[pb], pph, p.status, kDevErrTimeout)) { ok = false; break; }
+                    if (!mbar_wait_warp(&pfull[pb], pph, p.status, kDevErrTimeout)) { ok = false; break; }
                     tc_fence_after();
                     const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + pb * 256;
                     const float sc0 = sa * sw0, sc1 = sa * sw1;
@@ -359,7 +362,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     if (half == 0) p.out_scale[row * nblk + n] = sh;
                 }
-            } else if (valid) {
+            } else {
                 if (kKind == 1) {
                     const float4* wd = reinterpret_cast<const float4*>(p.w_scale0 + (int64_t)wexp * p.out_ld +
                                                                        n * 256 + 128 * half);
@@ -372,10 +375,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                         acc[4 * v + 3] *= w4.w;
                     }
                 }
-                float4* y = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + row * p.out_ld + n * 256 +
-                                                      128 * half);
+                // this warp's 32 rows x 128 columns, coalesced through shared memory
+                const int warp_row0 = m * kBM + q * 32;
+                const int nrows = s_rows[g] - warp_row0;
+                float* y = reinterpret_cast<float*>(p.out) + ((int64_t)s_start[g] + warp_row0) * p.out_ld + n * 256 +
+                           128 * half;
+                float4* stage = sStage + (warp - 2) * 128;
 #pragma unroll
-                for (int v = 0; v < 32; ++v) y[v] = make_float4(acc[4 * v], acc[4 * v + 1], acc[4 * v + 2], acc[4 * v + 3]);
+                for (int c = 0; c < 8; ++c) warp_store_rows16(stage, acc + 16 * c, y + 16 * c, p.out_ld, nrows, lane);
             }
         }
     }

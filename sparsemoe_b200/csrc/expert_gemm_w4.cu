@@ -63,7 +63,7 @@ constexpr int kSZBytes = 512;             // 256 fp16 scales (and as many zeros)
 constexpr int kStageBytes = kABytes + kBBytes + kPBytes + 2 * kSZBytes;   // 57 KB
 constexpr int kTxBytes = kABytes + kPBytes + 2 * kSZBytes;
 constexpr int kTmemCols = 512;
-constexpr size_t kSmemBytes = 1024 + (size_t)kStages * kStageBytes + 256;
+constexpr size_t kSmemBytes = 1024 + (size_t)kStages * kStageBytes + 256 + 4 * 2048;
 
 struct W4Params {
     const int* g_rows;
@@ -123,6 +123,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* tfull = empty + kStages;
     uint64_t* tempty = tfull + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+    float4* sStage = reinterpret_cast<float4*>(smem + kStages * kStageBytes + 256);   // 4 epilogue warps x 2 KB
     auto sA = [&](int s) { return stage0 + s * kStageBytes; };
     auto sB = [&](int s) { return stage0 + s * kStageBytes + kABytes; };
     auto sP = [&](int s) { return stage0 + s * kStageBytes + kABytes + kBBytes; };
@@ -244,7 +245,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int t = blockIdx.x; t < total; t += gridDim.x) {
             int g, m, n;
             decode_tile(t, s_pre, s_mt, p.G, g, m, n);
-            if (!mbar_wait(&tfull[acc], aph, p.status, kDevErrTimeout)) break;
+            if (!mbar_wait_warp(&tfull[acc], aph, p.status, kDevErrTimeout)) break;
             tc_fence_after();
             const int row_local = m * kBM + row_in_tile;
             const bool valid = row_local < s_rows[g];
@@ -282,21 +283,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
             } else {
-                float* y = reinterpret_cast<float*>(p.out) + out_row * p.out_ld + n * 256;
+                const int warp_row0 = m * kBM + q * 32;
+                const int nrows = s_rows[g] - warp_row0;
+                float* y = reinterpret_cast<float*>(p.out) + ((int64_t)s_start[g] + warp_row0) * p.out_ld + n * 256;
+                float4* stage = sStage + (warp - 2) * 128;
 #pragma unroll 1
                 for (int c = 0; c < 256; c += 32) {
                     uint32_t r[32];
                     tmem_ld_32x32b_x32(taddr + c, r);
                     tmem_wait_ld();
                     if (c == 224) { tc_fence_before(); mbar_arrive(&tempty[acc]); }
-                    if (valid) {
-                        float4* dst = reinterpret_cast<float4*>(y + c);
+                    float v[32];
 #pragma unroll
-                        for (int v = 0; v < 8; ++v)
-                            dst[v] = make_float4(__uint_as_float(r[4 * v]) * gsa, __uint_as_float(r[4 * v + 1]) * gsa,
-                                                 __uint_as_float(r[4 * v + 2]) * gsa,
-                                                 __uint_as_float(r[4 * v + 3]) * gsa);
-                    }
+                    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * gsa;
+                    warp_store_rows16(stage, v, y + c, p.out_ld, nrows, lane);
+                    warp_store_rows16(stage, v + 16, y + c + 16, p.out_ld, nrows, lane);
                 }
             }
             acc ^= 1;

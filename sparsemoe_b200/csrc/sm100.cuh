@@ -62,6 +62,12 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
     }
 }
 
+// Warp-uniform wait for roles that follow it with warp-collective operations
+// (shuffles, __syncwarp): every lane gets the same answer.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, int* status, int code) {
+    return __all_sync(0xffffffffu, mbar_wait(bar, parity, status, code));
+}
+
 // ---- TMA --------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
