@@ -25,12 +25,17 @@
 // since the product has at most 6 significant bits.  The epilogue applies
 // g * 2^8 in f32 (the accumulators of one tile share one expert matrix).
 //
+// Tile: 256 rows x 128 columns (up/gate: 64 gate + 64 up columns of the same
+// 64 h features).  Both 128-row halves multiply the same converted B stage,
+// so each dequantised weight serves 256 rows -- the converter's work per
+// FLOP is half that of a 128-row tile.
+//
 // Warps (448 threads, persistent, one CTA per SM):
-//   0      TMA: bf16 A tile (128 x 64, K-major SW128), packed B (64 K-rows x
-//          256 columns / 2), the stage's 256 fp16 scales and zeros.
-//   1      MMA: 4 x tcgen05.mma kind::f16 M128 N256 K16 per stage, double-
-//          buffered TMEM accumulators.
-//   2-5    epilogue (SwiGLU -> bf16 h, or f32 y), as the 16-bit kernel.
+//   0      TMA: bf16 A tile (256 x 64, K-major SW128), packed B (64 K-rows x
+//          128 columns / 2), the stage's scales (and INT4 zeros).
+//   1      MMA: per K16 step 2 x tcgen05.mma kind::f16 M128 N128 (one per row
+//          half) into a 256-column TMEM accumulator, double-buffered.
+//   2-5    epilogue (SwiGLU -> bf16 h, or f32 y rows stored coalesced).
 //   6-13   converter: nibbles -> bf16 into the stage's B buffer, then
 //          fence.proxy.async and arrive on the stage's converted barrier.
 #include "moe_internal.h"
@@ -50,20 +55,33 @@ namespace {
 
 using namespace sm100;
 
-constexpr int kBM = 128;
+// Tile shapes (kBM x kBN = 32768): 256 x 128 when experts hold many rows (each
+// converted B stage then feeds two M128 MMAs), 128 x 256 when they hold few
+// (decode: fewer N tiles, so the activations are re-read fewer times).
+template <int kBM>
+struct Tile {
+    static constexpr int BM = kBM;
+    static constexpr int BN = 32768 / kBM;
+    static constexpr int kHalves = kBM / 128;            // M128 MMAs per K step
+    static constexpr int kABytes = kBM * 128;            // kBM rows x 64 bf16
+    static constexpr int kBBytes = 64 * BN * 2;          // bf16 B: BN/64 chunks of 64 columns x 64 K-rows
+    static constexpr int kPBytes = 64 * BN / 2;          // packed nibbles
+    static constexpr int kSZBytes = 4 * BN;              // INT4: BN fp16 scales + BN zeros; NVFP4: 4 x BN e4m3
+    static constexpr int kData = kABytes + kBBytes + kPBytes + kSZBytes;
+    // every stage's A and B must sit on a 1024-byte boundary (128B swizzle atoms)
+    static constexpr int kStageBytes = (kData + 1023) / 1024 * 1024;
+    static constexpr int kTxBytes = kABytes + kPBytes + kSZBytes;
+    static constexpr size_t kSmemBytes = 1024 + (size_t)3 * kStageBytes + 256 + 4 * 2048;
+    static constexpr int kUnits = BN / 8;                 // converter: 8-column units
+    static constexpr int kRowGroups = 256 / kUnits;       // converter threads per unit
+    static constexpr int kRowsPerThread = 64 / kRowGroups;
+};
 constexpr int kBK = 64;
 constexpr int kStages = 3;
-constexpr int kThreads = 448;   // 2 + 4 epilogue + 8 converter warps
+constexpr int kThreads = 448;             // 2 + 4 epilogue + 8 converter warps
 constexpr int kConvThreads = 256;
-constexpr int kABytes = kBM * 128;        // 16 KB
-constexpr int kBBytes = 64 * 256 * 2;     // 32 KB bf16: 4 chunks of 64 columns x 64 K-rows
 constexpr int kChunkBytes = 64 * 128;     // 8 KB
-constexpr int kPBytes = 64 * 128;         // 8 KB packed nibbles
-constexpr int kSZBytes = 512;             // 256 fp16 scales (and as many zeros)
-constexpr int kStageBytes = kABytes + kBBytes + kPBytes + 2 * kSZBytes;   // 57 KB
-constexpr int kTxBytes = kABytes + kPBytes + 2 * kSZBytes;
-constexpr int kTmemCols = 512;
-constexpr size_t kSmemBytes = 1024 + (size_t)kStages * kStageBytes + 256 + 4 * 2048;
+constexpr int kTmemCols = 512;            // 2 accumulators x 256 columns
 
 struct W4Params {
     const int* g_rows;
@@ -104,10 +122,14 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
 }
 
 // kMode 0: up/gate + SwiGLU -> bf16 h;  1: down -> f32 y.
-// kFmt 0: INT4 asymmetric g128;  1: NVFP4.
-template <int kMode, int kFmt>
+// kFmt 0: INT4 asymmetric g128;  1: NVFP4.  kBM: tile rows (128 or 256).
+template <int kMode, int kFmt, int kBM>
 __global__ void __launch_bounds__(kThreads, 1)
     w4_gemm_kernel(const __grid_constant__ W4Maps mp, const W4Params p) {
+    using TL = Tile<kBM>;
+    constexpr int kBN = TL::BN;
+    constexpr int kABytes = TL::kABytes, kBBytes = TL::kBBytes, kPBytes = TL::kPBytes, kSZBytes = TL::kSZBytes;
+    constexpr int kStageBytes = TL::kStageBytes;
     extern __shared__ uint8_t smem_raw[];
     __shared__ int s_pre[kMaxGroups + 1];
     __shared__ int s_mt[kMaxGroups];
@@ -128,7 +150,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     auto sB = [&](int s) { return stage0 + s * kStageBytes + kABytes; };
     auto sP = [&](int s) { return stage0 + s * kStageBytes + kABytes + kBBytes; };
     auto sS = [&](int s) { return stage0 + s * kStageBytes + kABytes + kBBytes + kPBytes; };
-    auto sZ = [&](int s) { return stage0 + s * kStageBytes + kABytes + kBBytes + kPBytes + kSZBytes; };
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
@@ -178,28 +199,28 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int fp4_row0 = s_wt[g] * (p.K / 16);
                 for (int kb = 0; kb < kblocks; ++kb) {
                     if (!mbar_wait(&empty[s], ph ^ 1u, p.status, kDevErrTimeout)) goto producer_done;
-                    mbar_arrive_expect_tx(&full[s], kTxBytes);
+                    mbar_arrive_expect_tx(&full[s], TL::kTxBytes);
                     const int k0 = kb * kBK;
                     tma_load_2d(sA(s), &mp.a, &full[s], k0, a_row);
-                    if (kMode == 0) {
-                        tma_load_2d(sP(s), &mp.p0, &full[s], n * 64, b_row + k0);
-                        tma_load_2d(sP(s) + kPBytes / 2, &mp.p1, &full[s], n * 64, b_row + k0);
-                        if (kFmt == 0) {
-                            tma_load_2d(sS(s), &mp.s0, &full[s], n * 128, sz_row0 + k0 / 128);
-                            tma_load_2d(sS(s) + kSZBytes / 2, &mp.s1, &full[s], n * 128, sz_row0 + k0 / 128);
-                            tma_load_2d(sZ(s), &mp.z0, &full[s], n * 128, sz_row0 + k0 / 128);
-                            tma_load_2d(sZ(s) + kSZBytes / 2, &mp.z1, &full[s], n * 128, sz_row0 + k0 / 128);
-                        } else {   // 4 groups of 16 K-rows x 128 columns of e4m3 scales each
-                            tma_load_2d(sS(s), &mp.s0, &full[s], n * 128, fp4_row0 + k0 / 16);
-                            tma_load_2d(sS(s) + kSZBytes, &mp.s1, &full[s], n * 128, fp4_row0 + k0 / 16);
+                    if (kMode == 0) {   // kBN/2 gate + kBN/2 up columns = n * kBN/4 bytes of nibbles
+                        tma_load_2d(sP(s), &mp.p0, &full[s], n * (kBN / 4), b_row + k0);
+                        tma_load_2d(sP(s) + kPBytes / 2, &mp.p1, &full[s], n * (kBN / 4), b_row + k0);
+                        if (kFmt == 0) {   // scales [gate | up], then zeros [gate | up], kBN/2 fp16 each
+                            tma_load_2d(sS(s), &mp.s0, &full[s], n * (kBN / 2), sz_row0 + k0 / 128);
+                            tma_load_2d(sS(s) + kBN, &mp.s1, &full[s], n * (kBN / 2), sz_row0 + k0 / 128);
+                            tma_load_2d(sS(s) + 2 * kBN, &mp.z0, &full[s], n * (kBN / 2), sz_row0 + k0 / 128);
+                            tma_load_2d(sS(s) + 3 * kBN, &mp.z1, &full[s], n * (kBN / 2), sz_row0 + k0 / 128);
+                        } else {   // [gate: 4 groups x kBN/2] [up: 4 groups x kBN/2] e4m3
+                            tma_load_2d(sS(s), &mp.s0, &full[s], n * (kBN / 2), fp4_row0 + k0 / 16);
+                            tma_load_2d(sS(s) + 2 * kBN, &mp.s1, &full[s], n * (kBN / 2), fp4_row0 + k0 / 16);
                         }
                     } else {
-                        tma_load_2d(sP(s), &mp.p0, &full[s], n * 128, b_row + k0);
+                        tma_load_2d(sP(s), &mp.p0, &full[s], n * (kBN / 2), b_row + k0);
                         if (kFmt == 0) {
-                            tma_load_2d(sS(s), &mp.s0, &full[s], n * 256, sz_row0 + k0 / 128);
-                            tma_load_2d(sZ(s), &mp.z0, &full[s], n * 256, sz_row0 + k0 / 128);
-                        } else {   // 4 x 256 e4m3 scales
-                            tma_load_2d(sS(s), &mp.s0, &full[s], n * 256, fp4_row0 + k0 / 16);
+                            tma_load_2d(sS(s), &mp.s0, &full[s], n * kBN, sz_row0 + k0 / 128);
+                            tma_load_2d(sS(s) + 2 * kBN, &mp.z0, &full[s], n * kBN, sz_row0 + k0 / 128);
+                        } else {   // 4 groups x kBN e4m3 scales
+                            tma_load_2d(sS(s), &mp.s0, &full[s], n * kBN, fp4_row0 + k0 / 16);
                         }
                     }
                     if (++s == kStages) { s = 0; ph ^= 1u; }
@@ -214,7 +235,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int t = blockIdx.x; t < total; t += gridDim.x) {
                 if (!mbar_wait(&tempty[acc], aph ^ 1u, p.status, kDevErrTimeout)) break;
                 tc_fence_after();
-                const uint32_t d_tmem = tmem_base + acc * 256;
+                const uint32_t d_tmem = tmem_base + acc * 256;   // kHalves x kBN columns
                 bool ok = true;
                 for (int kb = 0; kb < kblocks; ++kb) {
                     if (!mbar_wait(&conv[s], ph, p.status, kDevErrTimeout)) { ok = false; break; }
@@ -223,9 +244,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint32_t b_base = smem_u32(sB(s));
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk) {
-                        const uint64_t adesc = smem_desc_sw128(a_base + kk * 32, 16, 1024);
                         const uint64_t bdesc = smem_desc_sw128(b_base + kk * 16 * 128, kChunkBytes, 1024);
-                        mma_f16_ss(d_tmem, adesc, bdesc, p.idesc, (kb | kk) != 0 ? 1u : 0u);
+                        const uint32_t accum = (kb | kk) != 0 ? 1u : 0u;
+#pragma unroll
+                        for (int hm = 0; hm < TL::kHalves; ++hm) {   // row halves: A rows 128*hm.. at 16 KB * hm
+                            const uint64_t adesc = smem_desc_sw128(a_base + hm * 16384 + kk * 32, 16, 1024);
+                            mma_f16_ss(d_tmem + hm * kBN, adesc, bdesc, p.idesc, accum);
+                        }
                     }
                     mma_commit(&empty[s]);
                     if (++s == kStages) { s = 0; ph ^= 1u; }
@@ -239,65 +264,69 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp < 6) {
         // ---------------- epilogue (warps 2..5) ----------------
         const int q = warp & 3;
-        const int row_in_tile = q * 32 + lane;
         int acc = 0;
         uint32_t aph = 0;
+        float4* stage = sStage + (warp - 2) * 128;
         for (int t = blockIdx.x; t < total; t += gridDim.x) {
             int g, m, n;
             decode_tile(t, s_pre, s_mt, p.G, g, m, n);
             if (!mbar_wait_warp(&tfull[acc], aph, p.status, kDevErrTimeout)) break;
             tc_fence_after();
-            const int row_local = m * kBM + row_in_tile;
-            const bool valid = row_local < s_rows[g];
-            const int64_t out_row = (int64_t)s_start[g] + row_local;
-            const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + acc * 256;
             // NVFP4: the global scale times 2^8 (the staged weights carry 2^-8)
             const float gsa = kFmt == 1 ? p.gs0[s_wt[g]] * 256.0f : 1.0f;
             const float gsb = (kFmt == 1 && kMode == 0) ? p.gs1[s_wt[g]] * 256.0f : 1.0f;
-            if (kMode == 0) {
-                __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(p.out) + out_row * p.out_ld + n * 128;
 #pragma unroll 1
-                for (int c = 0; c < 128; c += 32) {
-                    uint32_t gr[32], ur[32];
-                    tmem_ld_32x32b_x32(taddr + c, gr);
-                    tmem_ld_32x32b_x32(taddr + 128 + c, ur);
-                    tmem_wait_ld();
-                    if (c == 96) { tc_fence_before(); mbar_arrive(&tempty[acc]); }
-                    uint32_t packed[16];
+            for (int hm = 0; hm < TL::kHalves; ++hm) {
+                const int warp_row0 = m * kBM + hm * 128 + q * 32;
+                const int row_local = warp_row0 + lane;
+                const bool valid = row_local < s_rows[g];
+                const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + acc * 256 + hm * kBN;
+                const bool last_half = hm == TL::kHalves - 1;
+                if (kMode == 0) {
+                    __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(p.out) +
+                                       ((int64_t)s_start[g] + row_local) * p.out_ld + n * (kBN / 2);
+#pragma unroll 1
+                    for (int c = 0; c < kBN / 2; c += 32) {
+                        uint32_t gr[32], ur[32];
+                        tmem_ld_32x32b_x32(taddr + c, gr);
+                        tmem_ld_32x32b_x32(taddr + kBN / 2 + c, ur);
+                        tmem_wait_ld();
+                        if (last_half && c == kBN / 2 - 32) { tc_fence_before(); mbar_arrive(&tempty[acc]); }
+                        uint32_t packed[16];
 #pragma unroll
-                    for (int i = 0; i < 16; ++i) {
-                        float hv[2];
+                        for (int i = 0; i < 16; ++i) {
+                            float hv[2];
 #pragma unroll
-                        for (int j = 0; j < 2; ++j) {
-                            const float gv = __uint_as_float(gr[2 * i + j]) * gsa;
-                            const float uv = __uint_as_float(ur[2 * i + j]) * gsb;
-                            hv[j] = uv * (gv / (1.0f + __expf(-gv)));
+                            for (int j = 0; j < 2; ++j) {
+                                const float gv = __uint_as_float(gr[2 * i + j]) * gsa;
+                                const float uv = __uint_as_float(ur[2 * i + j]) * gsb;
+                                hv[j] = uv * (gv / (1.0f + __expf(-gv)));
+                            }
+                            packed[i] = F16Traits<__nv_bfloat16>::pack2(hv[0], hv[1]);
                         }
-                        packed[i] = F16Traits<__nv_bfloat16>::pack2(hv[0], hv[1]);
-                    }
-                    if (valid) {
-                        uint4* o = reinterpret_cast<uint4*>(h + c);
+                        if (valid) {
+                            uint4* o = reinterpret_cast<uint4*>(h + c);
 #pragma unroll
-                        for (int v = 0; v < 4; ++v)
-                            o[v] = make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
+                            for (int v = 0; v < 4; ++v)
+                                o[v] = make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
+                        }
                     }
-                }
-            } else {
-                const int warp_row0 = m * kBM + q * 32;
-                const int nrows = s_rows[g] - warp_row0;
-                float* y = reinterpret_cast<float*>(p.out) + ((int64_t)s_start[g] + warp_row0) * p.out_ld + n * 256;
-                float4* stage = sStage + (warp - 2) * 128;
+                } else {
+                    const int nrows = s_rows[g] - warp_row0;
+                    float* y = reinterpret_cast<float*>(p.out) + ((int64_t)s_start[g] + warp_row0) * p.out_ld +
+                               n * kBN;
 #pragma unroll 1
-                for (int c = 0; c < 256; c += 32) {
-                    uint32_t r[32];
-                    tmem_ld_32x32b_x32(taddr + c, r);
-                    tmem_wait_ld();
-                    if (c == 224) { tc_fence_before(); mbar_arrive(&tempty[acc]); }
-                    float v[32];
+                    for (int c = 0; c < kBN; c += 32) {
+                        uint32_t r[32];
+                        tmem_ld_32x32b_x32(taddr + c, r);
+                        tmem_wait_ld();
+                        if (last_half && c == kBN - 32) { tc_fence_before(); mbar_arrive(&tempty[acc]); }
+                        float v[32];
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * gsa;
-                    warp_store_rows16(stage, v, y + c, p.out_ld, nrows, lane);
-                    warp_store_rows16(stage, v + 16, y + c + 16, p.out_ld, nrows, lane);
+                        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * gsa;
+                        warp_store_rows16(stage, v, y + c, p.out_ld, nrows, lane);
+                        warp_store_rows16(stage, v + 16, y + c + 16, p.out_ld, nrows, lane);
+                    }
                 }
             }
             acc ^= 1;
@@ -305,10 +334,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else {
         // ---------------- converter (warps 6..13) ----------------
-        // thread: 8-column unit u (columns 8u..8u+7) of K-rows rg, rg+8, ...
+        // thread: 8-column unit u of the kBN columns, K rows krow0 + kRowGroups*j.
+        // Up/gate: the first kUnits/2 units are gate columns, the rest up; the
+        // up units take K rows rg ^ (32 / kUnits), so one warp's gate and up
+        // nibble loads land in distinct shared-memory bank ranges.
+        constexpr int kU = TL::kUnits, kRG = TL::kRowGroups;
+        constexpr int kPRow = kMode == 0 ? kBN / 4 : kBN / 2;   // packed bytes per K row (per half)
         const int ct = threadIdx.x - 192;
-        const int u = ct & 31, rg = ct >> 5;
+        const int u = ct % kU, rg = ct / kU;
         const int chunk = u >> 3, uc = u & 7;
+        const bool up_unit = kMode == 0 && u >= kU / 2;
+        const int ul = up_unit ? u - kU / 2 : u;          // unit within its half
+        const int krow0 = up_unit ? (rg ^ (32 / kU)) : rg;
+        const int p_base = up_unit ? kPBytes / 2 : 0;
         const __nv_bfloat162 k128 = __floats2bfloat162_rn(128.0f, 128.0f);
         int s = 0;
         uint32_t ph = 0;
@@ -316,70 +354,69 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
             for (int kb = 0; kb < kblocks; ++kb) {
                 if (!mbar_wait(&full[s], ph, p.status, kDevErrTimeout)) { ok = false; break; }
+                const uint8_t* src = sP(s) + p_base;
+                uint8_t* dst = sB(s) + chunk * kChunkBytes;
                 if (kFmt == 0) {
                     __nv_bfloat162 sc[4], cc[4];
                     {
-                        const uint4 s8 = *reinterpret_cast<const uint4*>(sS(s) + u * 16);
-                        const uint4 z8 = *reinterpret_cast<const uint4*>(sZ(s) + u * 16);
+                        // fp16 scales at [0, 2 kBN) bytes, zeros at [2 kBN, 4 kBN); gate | up halves
+                        const int so = (up_unit ? kBN : 0) + ul * 16;
+                        const uint4 s8 = *reinterpret_cast<const uint4*>(sS(s) + so);
+                        const uint4 z8 = *reinterpret_cast<const uint4*>(sS(s) + 2 * kBN + so);
                         const __half2* sh = reinterpret_cast<const __half2*>(&s8);
                         const __half2* zh = reinterpret_cast<const __half2*>(&z8);
-    #pragma unroll
+#pragma unroll
                         for (int i = 0; i < 4; ++i) {
                             const float2 sf = __half22float2(sh[i]), zf = __half22float2(zh[i]);
                             sc[i] = __floats2bfloat162_rn(sf.x, sf.y);
                             cc[i] = __floats2bfloat162_rn(-(zf.x * sf.x), -(zf.y * sf.y));
                         }
                     }
-                    const uint8_t* src = sP(s);
-                    uint8_t* dst = sB(s) + chunk * kChunkBytes;
-    #pragma unroll 4
-                    for (int j = 0; j < 8; ++j) {
-                        const int k = rg + 8 * j;
-                        const int off = kMode == 0 ? (u < 16 ? k * 64 + u * 4 : kPBytes / 2 + k * 64 + (u - 16) * 4)
-                                                   : k * 128 + u * 4;
-                        const uint32_t w = *reinterpret_cast<const uint32_t*>(src + off);
+#pragma unroll
+                    for (int j = 0; j < TL::kRowsPerThread; ++j) {
+                        const int k = krow0 + kRG * j;
+                        const uint32_t w = *reinterpret_cast<const uint32_t*>(src + k * kPRow + ul * 4);
                         uint32_t o[4];
-    #pragma unroll
+#pragma unroll
                         for (int i = 0; i < 4; ++i) {
                             const uint32_t biased = ((w >> (4 * i)) & 0x000F000Fu) | 0x43004300u;   // bf16x2 128+q
-                            const __nv_bfloat162 q = __hsub2(*reinterpret_cast<const __nv_bfloat162*>(&biased), k128);
-                            const __nv_bfloat162 v = __hfma2(q, sc[i], cc[i]);
+                            const __nv_bfloat162 qv =
+                                __hsub2(*reinterpret_cast<const __nv_bfloat162*>(&biased), k128);
+                            const __nv_bfloat162 v = __hfma2(qv, sc[i], cc[i]);
                             o[i] = *reinterpret_cast<const uint32_t*>(&v);
                         }
-                        *reinterpret_cast<uint4*>(dst + k * 128 + ((uc ^ (k & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+                        *reinterpret_cast<uint4*>(dst + k * 128 + ((uc ^ (k & 7)) << 4)) =
+                            make_uint4(o[0], o[1], o[2], o[3]);
                     }
                 } else {
-                    // e4m3 scales of this thread's 8 columns for the stage's 4 groups, as bf16 s * 2^118
-                    __nv_bfloat162 sc[4][4];
+                    // e4m3 scales: up/gate [gate: 4 x kBN/2 | up: 4 x kBN/2], down 4 x kBN; K row k of
+                    // the stage is in group k / 16; scales become bf16 s * 2^118
+                    constexpr int kSRow = kMode == 0 ? kBN / 2 : kBN;
+                    const uint8_t* sbase = sS(s) + (up_unit ? 2 * kBN : 0) + 8 * ul;
+                    __nv_bfloat162 sc[4][4];   // [group][column pair]
 #pragma unroll
                     for (int gi = 0; gi < 4; ++gi) {
-                        const uint8_t* sp = kMode == 0 ? (u < 16 ? sS(s) + gi * 128 + 8 * u
-                                                                 : sS(s) + 512 + gi * 128 + 8 * (u - 16))
-                                                       : sS(s) + gi * 256 + 8 * u;
-                        const uint2 raw = *reinterpret_cast<const uint2*>(sp);
+                        const uint2 raw = *reinterpret_cast<const uint2*>(sbase + gi * kSRow);
 #pragma unroll
                         for (int i = 0; i < 4; ++i) {
                             const uint32_t word = i < 2 ? raw.x : raw.y;
-                            const __nv_fp8x2_storage_t pr = (__nv_fp8x2_storage_t)((word >> (16 * (i & 1))) & 0xFFFFu);
+                            const __nv_fp8x2_storage_t pr =
+                                (__nv_fp8x2_storage_t)((word >> (16 * (i & 1))) & 0xFFFFu);
                             const float2 f = __half22float2(__half2(__nv_cvt_fp8x2_to_halfraw2(pr, __NV_E4M3)));
                             sc[gi][i] = __floats2bfloat162_rn(f.x * 0x1p118f, f.y * 0x1p118f);
                         }
                     }
-                    const uint8_t* src = sP(s);
-                    uint8_t* dst = sB(s) + chunk * kChunkBytes;
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        const int k = rg + 8 * j;   // K-row k of the stage is in group j / 2
-                        const int off = kMode == 0 ? (u < 16 ? k * 64 + u * 4 : kPBytes / 2 + k * 64 + (u - 16) * 4)
-                                                   : k * 128 + u * 4;
-                        const uint32_t w = *reinterpret_cast<const uint32_t*>(src + off);
+                    for (int j = 0; j < TL::kRowsPerThread; ++j) {
+                        const int k = krow0 + kRG * j;   // krow0 < kRG <= 16: group (kRG * j) / 16
+                        const uint32_t w = *reinterpret_cast<const uint32_t*>(src + k * kPRow + ul * 4);
                         uint32_t o[4];
 #pragma unroll
                         for (int i = 0; i < 4; ++i) {
                             const uint32_t sh = w >> (4 * i);
                             const uint32_t bits = ((sh << 6) & 0x01C001C0u) | ((sh << 12) & 0x80008000u);
-                            const __nv_bfloat162 v =
-                                __hmul2(*reinterpret_cast<const __nv_bfloat162*>(&bits), sc[j >> 1][i]);
+                            const __nv_bfloat162 v = __hmul2(*reinterpret_cast<const __nv_bfloat162*>(&bits),
+                                                             sc[(kRG * j) >> 4][i]);
                             o[i] = *reinterpret_cast<const uint32_t*>(&v);
                         }
                         *reinterpret_cast<uint4*>(dst + k * 128 + ((uc ^ (k & 7)) << 4)) =
@@ -399,14 +436,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
-template <int kMode, int kFmt>
-cudaError_t launch(const W4Maps& mp, const W4Params& p, cudaStream_t st, int num_sms) {
-    auto kern = w4_gemm_kernel<kMode, kFmt>;
-    cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+template <int kMode, int kFmt, int kBM>
+cudaError_t launch_bm(const W4Maps& mp, const W4Params& p, cudaStream_t st, int num_sms) {
+    auto kern = w4_gemm_kernel<kMode, kFmt, kBM>;
+    constexpr size_t smem = Tile<kBM>::kSmemBytes;
+    cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (err != cudaSuccess) return err;
-    kern<<<num_sms, kThreads, kSmemBytes, st>>>(mp, p);
+    kern<<<num_sms, kThreads, smem, st>>>(mp, p);
     return cudaGetLastError();
 }
+
+// 256-row tiles when the groups average at least 256 rows of capacity
+bool tall_tiles(const GroupTable& gt) { return gt.rows_capacity / gt.G >= 256; }
+
+
 
 bool packed_map(CUtensorMap* m, const void* w, uint64_t rows, uint64_t n_cols, uint32_t box_cols) {
     return make_map_box(m, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, n_cols / 2, rows, box_cols / 2, kBK, false);
@@ -419,115 +462,86 @@ bool fp4_scale_map(CUtensorMap* m, const void* sc, uint64_t rows, uint64_t n_col
     return make_map_box(m, sc, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, n_cols, rows, box_cols, kBK / 16, false);
 }
 
+// One GEMM of the 4-bit path.  kMode 0: w0/w1 = gate/up [E, d, f/2], output
+// h [rows, f]; kMode 1: w0 = down [E, f, d/2], output f32 y [rows, d].
+// INT4 (kFmt 0): s/z fp16 [E, K/128, N]; NVFP4: s e4m3 [E, K/16, N], g f32 [E].
+template <int kMode, int kFmt, int kBM>
+cudaError_t launch_fmt(const void* a_rows, const void* w0, const void* w1, const void* s0, const void* s1,
+                       const void* z0, const void* z1, const float* g0, const float* g1, const Shape& s,
+                       const GroupTable& gt, int* status, void* out, cudaStream_t st, int num_sms) {
+    constexpr int kBN = Tile<kBM>::BN;
+    const int K = kMode == 0 ? s.d : s.f, N = kMode == 0 ? s.f : s.d;
+    const uint32_t box = kMode == 0 ? kBN / 2 : kBN;   // weight columns per operand per tile
+    const uint64_t wrows = (uint64_t)s.E * K;
+    const uint64_t srows = (uint64_t)s.E * (kFmt == 0 ? K / 128 : K / 16);
+    W4Maps mp;
+    bool ok = make_map_box(&mp.a, a_rows, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, gt.rows_capacity, 64, kBM, true) &&
+              packed_map(&mp.p0, w0, wrows, N, box) && packed_map(&mp.p1, kMode == 0 ? w1 : w0, wrows, N, box);
+    if (kFmt == 0)
+        ok = ok && sz_map(&mp.s0, s0, srows, N, box) && sz_map(&mp.s1, kMode == 0 ? s1 : s0, srows, N, box) &&
+             sz_map(&mp.z0, z0, srows, N, box) && sz_map(&mp.z1, kMode == 0 ? z1 : z0, srows, N, box);
+    else {
+        ok = ok && fp4_scale_map(&mp.s0, s0, srows, N, box) &&
+             fp4_scale_map(&mp.s1, kMode == 0 ? s1 : s0, srows, N, box);
+        mp.z0 = mp.s0;
+        mp.z1 = mp.s1;
+    }
+    if (!ok) return cudaErrorInvalidValue;
+    W4Params p{};
+    p.g_rows = gt.rows;
+    p.g_start = gt.start;
+    p.g_weight = gt.weight;
+    p.G = gt.G;
+    p.status = status;
+    p.idesc = idesc_f16(true, 128, kBN, false, true);
+    p.K = K;
+    p.n_tiles = kMode == 0 ? N / (kBN / 2) : N / kBN;
+    p.out_ld = N;
+    p.out = out;
+    p.gs0 = g0;
+    p.gs1 = kMode == 0 ? g1 : g0;
+    return launch_bm<kMode, kFmt, kBM>(mp, p, st, num_sms);
+}
+
+template <int kMode, int kFmt>
+cudaError_t launch_any(const void* a_rows, const void* w0, const void* w1, const void* s0, const void* s1,
+                       const void* z0, const void* z1, const float* g0, const float* g1, const Shape& s,
+                       const GroupTable& gt, int* status, void* out, cudaStream_t st, int num_sms) {
+    if (gt.G <= 0 || gt.rows_capacity <= 0) return cudaSuccess;
+    return tall_tiles(gt)
+               ? launch_fmt<kMode, kFmt, 256>(a_rows, w0, w1, s0, s1, z0, z1, g0, g1, s, gt, status, out, st, num_sms)
+               : launch_fmt<kMode, kFmt, 128>(a_rows, w0, w1, s0, s1, z0, z1, g0, g1, s, gt, status, out, st,
+                                              num_sms);
+}
+
 }  // namespace
 
 cudaError_t launch_w4_up_gate(const void* a_rows, const void* w_gate, const void* w_up, const void* s_gate,
                               const void* s_up, const void* z_gate, const void* z_up, const Shape& s,
                               const GroupTable& gt, int* status, void* h_rows, cudaStream_t st, int num_sms) {
-    if (gt.G <= 0 || gt.rows_capacity <= 0) return cudaSuccess;
-    W4Maps mp;
-    const uint64_t wrows = (uint64_t)s.E * s.d, grows = (uint64_t)s.E * (s.d / 128);
-    if (!make_map_box(&mp.a, a_rows, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, s.d, gt.rows_capacity, 64, kBM, true) ||
-        !packed_map(&mp.p0, w_gate, wrows, s.f, 128) || !packed_map(&mp.p1, w_up, wrows, s.f, 128) ||
-        !sz_map(&mp.s0, s_gate, grows, s.f, 128) || !sz_map(&mp.s1, s_up, grows, s.f, 128) ||
-        !sz_map(&mp.z0, z_gate, grows, s.f, 128) || !sz_map(&mp.z1, z_up, grows, s.f, 128))
-        return cudaErrorInvalidValue;
-    W4Params p{};
-    p.g_rows = gt.rows;
-    p.g_start = gt.start;
-    p.g_weight = gt.weight;
-    p.G = gt.G;
-    p.K = s.d;
-    p.n_tiles = s.f / 128;
-    p.out_ld = s.f;
-    p.out = h_rows;
-    p.status = status;
-    p.idesc = idesc_f16(true, kBM, 256, false, true);
-    return launch<0, 0>(mp, p, st, num_sms);
+    return launch_any<0, 0>(a_rows, w_gate, w_up, s_gate, s_up, z_gate, z_up, nullptr, nullptr, s, gt, status, h_rows,
+                            st, num_sms);
 }
 
 cudaError_t launch_w4_down(const void* h_rows, const void* w_down, const void* s_down, const void* z_down,
                            const Shape& s, const GroupTable& gt, int* status, float* y_rows, cudaStream_t st,
                            int num_sms) {
-    if (gt.G <= 0 || gt.rows_capacity <= 0) return cudaSuccess;
-    W4Maps mp;
-    const uint64_t wrows = (uint64_t)s.E * s.f, grows = (uint64_t)s.E * (s.f / 128);
-    if (!make_map_box(&mp.a, h_rows, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, s.f, gt.rows_capacity, 64, kBM, true) ||
-        !packed_map(&mp.p0, w_down, wrows, s.d, 256) || !sz_map(&mp.s0, s_down, grows, s.d, 256) ||
-        !sz_map(&mp.z0, z_down, grows, s.d, 256))
-        return cudaErrorInvalidValue;
-    mp.p1 = mp.p0;
-    mp.s1 = mp.s0;
-    mp.z1 = mp.z0;
-    W4Params p{};
-    p.g_rows = gt.rows;
-    p.g_start = gt.start;
-    p.g_weight = gt.weight;
-    p.G = gt.G;
-    p.K = s.f;
-    p.n_tiles = s.d / 256;
-    p.out_ld = s.d;
-    p.out = y_rows;
-    p.status = status;
-    p.idesc = idesc_f16(true, kBM, 256, false, true);
-    return launch<1, 0>(mp, p, st, num_sms);
+    return launch_any<1, 0>(h_rows, w_down, nullptr, s_down, nullptr, z_down, nullptr, nullptr, nullptr, s, gt,
+                            status, y_rows, st, num_sms);
 }
 
 cudaError_t launch_fp4_up_gate(const void* a_rows, const void* w_gate, const void* w_up, const void* s_gate,
                                const void* s_up, const float* g_gate, const float* g_up, const Shape& s,
                                const GroupTable& gt, int* status, void* h_rows, cudaStream_t st, int num_sms) {
-    if (gt.G <= 0 || gt.rows_capacity <= 0) return cudaSuccess;
-    W4Maps mp;
-    const uint64_t wrows = (uint64_t)s.E * s.d, grows = (uint64_t)s.E * (s.d / 16);
-    if (!make_map_box(&mp.a, a_rows, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, s.d, gt.rows_capacity, 64, kBM, true) ||
-        !packed_map(&mp.p0, w_gate, wrows, s.f, 128) || !packed_map(&mp.p1, w_up, wrows, s.f, 128) ||
-        !fp4_scale_map(&mp.s0, s_gate, grows, s.f, 128) || !fp4_scale_map(&mp.s1, s_up, grows, s.f, 128))
-        return cudaErrorInvalidValue;
-    mp.z0 = mp.s0;
-    mp.z1 = mp.s1;
-    W4Params p{};
-    p.g_rows = gt.rows;
-    p.g_start = gt.start;
-    p.g_weight = gt.weight;
-    p.G = gt.G;
-    p.K = s.d;
-    p.n_tiles = s.f / 128;
-    p.out_ld = s.f;
-    p.out = h_rows;
-    p.gs0 = g_gate;
-    p.gs1 = g_up;
-    p.status = status;
-    p.idesc = idesc_f16(true, kBM, 256, false, true);
-    return launch<0, 1>(mp, p, st, num_sms);
+    return launch_any<0, 1>(a_rows, w_gate, w_up, s_gate, s_up, nullptr, nullptr, g_gate, g_up, s, gt, status,
+                            h_rows, st, num_sms);
 }
 
 cudaError_t launch_fp4_down(const void* h_rows, const void* w_down, const void* s_down, const float* g_down,
                             const Shape& s, const GroupTable& gt, int* status, float* y_rows, cudaStream_t st,
                             int num_sms) {
-    if (gt.G <= 0 || gt.rows_capacity <= 0) return cudaSuccess;
-    W4Maps mp;
-    const uint64_t wrows = (uint64_t)s.E * s.f, grows = (uint64_t)s.E * (s.f / 16);
-    if (!make_map_box(&mp.a, h_rows, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, s.f, gt.rows_capacity, 64, kBM, true) ||
-        !packed_map(&mp.p0, w_down, wrows, s.d, 256) || !fp4_scale_map(&mp.s0, s_down, grows, s.d, 256))
-        return cudaErrorInvalidValue;
-    mp.p1 = mp.p0;
-    mp.s1 = mp.s0;
-    mp.z0 = mp.s0;
-    mp.z1 = mp.s0;
-    W4Params p{};
-    p.g_rows = gt.rows;
-    p.g_start = gt.start;
-    p.g_weight = gt.weight;
-    p.G = gt.G;
-    p.K = s.f;
-    p.n_tiles = s.d / 256;
-    p.out_ld = s.d;
-    p.out = y_rows;
-    p.gs0 = g_down;
-    p.gs1 = g_down;
-    p.status = status;
-    p.idesc = idesc_f16(true, kBM, 256, false, true);
-    return launch<1, 1>(mp, p, st, num_sms);
+    return launch_any<1, 1>(h_rows, w_down, nullptr, s_down, nullptr, nullptr, nullptr, g_down, nullptr, s, gt,
+                            status, y_rows, st, num_sms);
 }
 
 }  // namespace moe

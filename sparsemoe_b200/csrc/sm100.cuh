@@ -52,12 +52,17 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
     const uint32_t a = smem_u32(bar);
     if (mbar_try_wait(a, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
-    while (true) {
+    for (uint32_t it = 1;; ++it) {
         if (mbar_try_wait(a, parity)) return true;
-        if (*(volatile int*)status != 0) return false;  // another role already gave up
-        if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
-            atomicCAS(status, 0, code);
-            return false;
+        // the status word (global memory) and the clock are polled every 16th
+        // try only, so a waiter is not stuck in a global load when its phase
+        // completes
+        if ((it & 15) == 0) {
+            if (*(volatile int*)status != 0) return false;  // another role already gave up
+            if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+                atomicCAS(status, 0, code);
+                return false;
+            }
         }
     }
 }
