@@ -80,6 +80,15 @@ typedef struct MoeDims {
     const float* fp4_global_gate;
     const float* fp4_global_up;
     const float* fp4_global_down;
+    // Expert parallelism over a batch split across ranks (global capacity).
+    // Optional device int32 [B, E]: for each (batch, expert) the slots that the
+    // routes of earlier shards of the same batch already took; this call keeps
+    // a route iff slot_base + its slot within this shard < cap.  NULL: 0.
+    const int* slot_base;
+    // Optional device f32 buffer for the per-row activation scales of the
+    // dynamically quantised formats (FP8_BLOCK [rows, d/128], INT8_CHANNEL
+    // [rows]): written by the gather, read by the up/gate GEMM.  NULL: scratch.
+    float* act_scale;
 } MoeDims;
 
 // Reference: kernels/launcher.h:21 `extern "C" void solve(MoEArgs args)`.
@@ -117,6 +126,14 @@ size_t moe_noalloc_scratch_bytes(void);
 // the dense expert-major layout: expert e's rows start at
 // sum_{e'<e} sum_b expert_counts[b, e'], batch 0's slots first.
 int moe_stage_route(const struct MoEArgs* args, const MoeDims* dims, cudaStream_t stream);
+// The same stage in two phases, for a batch split across ranks: phase 1
+// (router, top-k, per-(batch, expert) route totals of this shard before any
+// drop, written to raw_counts: device int32 [B, E]); the caller exchanges the
+// totals and sets dims.slot_base; phase 2 (slots, drops, gather) on the same
+// dims and scratch.
+int moe_stage_route_counts(const struct MoEArgs* args, const MoeDims* dims, int* raw_counts,
+                           cudaStream_t stream);
+int moe_stage_route_finish(const struct MoEArgs* args, const MoeDims* dims, cudaStream_t stream);
 // SwiGLU FFN over row groups: group g has group_rows[g] rows starting at row
 // group_start[g] of per_expert_wmma_inputs (A), hidden_mlp_layer_1_out_fp16
 // (H) and hidden_mlp_layer_2_out (Y, f32), all with rows_capacity rows, and
@@ -128,6 +145,11 @@ int moe_stage_expert_ffn(const struct MoEArgs* args, const MoeDims* dims, const 
 // Combine: final_output[t] = sum over kept routes in route order of
 // w * Y[row], Y = hidden_mlp_layer_2_out in the layout moe_stage_route made.
 int moe_stage_combine(const struct MoEArgs* args, const MoeDims* dims, cudaStream_t stream);
+// Scratch (MoeDims.scratch) that moe_stage_expert_ffn needs for rows_capacity
+// rows with these dims: the group table, plus the h scales of FP8_BLOCK and
+// INT8_CHANNEL (for which caller scratch is required; the row scales of A
+// come in MoeDims.act_scale).
+size_t moe_ffn_scratch_bytes(const MoeDims* dims, int64_t rows_capacity);
 
 // Synchronises `stream` and reports a device-side failure (MOE_ERR_TIMEOUT) of
 // the last moe_solve_v2 on this device, MOE_OK otherwise.

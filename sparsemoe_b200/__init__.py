@@ -84,6 +84,7 @@ class MoeDims(ctypes.Structure):
         ("w4_scale_gate", _p), ("w4_scale_up", _p), ("w4_scale_down", _p),
         ("w4_zero_gate", _p), ("w4_zero_up", _p), ("w4_zero_down", _p),
         ("fp4_global_gate", _p), ("fp4_global_up", _p), ("fp4_global_down", _p),
+        ("slot_base", _p), ("act_scale", _p),
     ]
 
 
@@ -106,6 +107,9 @@ def _load() -> ctypes.CDLL:
         "moe_stage_expert_ffn": (ctypes.c_int, [ctypes.POINTER(MoEArgs), ctypes.POINTER(MoeDims), _p, _p, _p,
                                                 ctypes.c_int, ctypes.c_int64, _p]),
         "moe_stage_combine": (ctypes.c_int, [ctypes.POINTER(MoEArgs), ctypes.POINTER(MoeDims), _p]),
+        "moe_stage_route_counts": (ctypes.c_int, [ctypes.POINTER(MoEArgs), ctypes.POINTER(MoeDims), _p, _p]),
+        "moe_stage_route_finish": (ctypes.c_int, [ctypes.POINTER(MoEArgs), ctypes.POINTER(MoeDims), _p]),
+        "moe_ffn_scratch_bytes": (ctypes.c_size_t, [ctypes.POINTER(MoeDims), ctypes.c_int64]),
         "moe_solve_v2_noalloc": (ctypes.c_int, [ctypes.POINTER(MoEArgs), ctypes.POINTER(MoeDims), _p]),
         "moe_noalloc_scratch_bytes": (ctypes.c_size_t, []),
         "moe_set_stage_events": (ctypes.c_int, [ctypes.POINTER(ctypes.c_void_p), ctypes.c_int]),

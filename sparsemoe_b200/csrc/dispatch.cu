@@ -56,8 +56,13 @@ __global__ void __launch_bounds__(kThreads) dispatch_count_kernel(const int* __r
     for (int e = threadIdx.x; e < E; e += kThreads) out[e] = hist[e];
 }
 
+// slot_base (optional, [B, E]): slots already taken by earlier shards of the
+// same batch (expert parallelism over a split batch); raw (optional, [B, E]):
+// the shard's route totals before any drop.
 __global__ void __launch_bounds__(256) dispatch_scan_kernel(const int* __restrict__ chunk_count,
                                                             int B, int E, int chunks, int cap,
+                                                            const int* __restrict__ slot_base,
+                                                            int* __restrict__ raw,
                                                             int* __restrict__ chunk_base,
                                                             int* __restrict__ counts,
                                                             int* __restrict__ row_base,
@@ -74,7 +79,9 @@ __global__ void __launch_bounds__(256) dispatch_scan_kernel(const int* __restric
             chunk_base[o] = run;
             run += chunk_count[o];
         }
-        const int kept = run < cap ? run : cap;
+        if (raw) raw[b * E + e] = run;
+        const int room = slot_base ? max(0, cap - slot_base[b * E + e]) : cap;
+        const int kept = run < room ? run : room;
         counts[b * E + e] = kept;
         row_base[b * E + e] = rows;
         rows += kept;
@@ -91,14 +98,16 @@ __global__ void __launch_bounds__(256) dispatch_scan_kernel(const int* __restric
 
 __global__ void __launch_bounds__(kThreads) dispatch_assign_kernel(
     const int* __restrict__ idx, const float* __restrict__ w, int N, int k, int E, int cap, int chunks,
-    const int* __restrict__ chunk_base, int* __restrict__ token_ids, float* __restrict__ token_weights,
-    int* __restrict__ route_slot) {
+    const int* __restrict__ chunk_base, const int* __restrict__ slot_base, int* __restrict__ token_ids,
+    float* __restrict__ token_weights, int* __restrict__ route_slot) {
     __shared__ int base[256];
+    __shared__ int room[256];   // slots this shard may still fill per expert
     __shared__ int wcnt[kWarps][256];
     const int c = blockIdx.x, b = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int e = threadIdx.x; e < E; e += kThreads) {
         base[e] = chunk_base[((int64_t)b * chunks + c) * E + e];
+        room[e] = slot_base ? max(0, cap - slot_base[b * E + e]) : cap;
 #pragma unroll
         for (int q = 0; q < kWarps; ++q) wcnt[q][e] = 0;
     }
@@ -131,7 +140,7 @@ __global__ void __launch_bounds__(kThreads) dispatch_assign_kernel(
             base[ee] += add;
         }
         // Slot tables.
-        const bool kept = e >= 0 && slot < cap;
+        const bool kept = e >= 0 && slot < room[e];
         if (r < routes) {
             route_slot[rb + r] = kept ? slot : -1;
             if (kept) {
@@ -297,9 +306,28 @@ __global__ void __launch_bounds__(kThreads) dispatch_gather_q8tok_kernel(
 
 }  // namespace
 
-cudaError_t launch_dispatch(const void* x, const int* idx, const float* w, const Shape& s,
-                            const Workspace& ws, const GemmScales& sc, int* counts, int* token_ids,
-                            float* token_weights, void* a_rows, cudaStream_t st) {
+// Route totals per (chunk, batch, expert); with `raw` also the shard's
+// per-(batch, expert) totals.
+cudaError_t launch_dispatch_count(const int* idx, const Shape& s, const Workspace& ws, int* counts, int* raw,
+                                  cudaStream_t st) {
+    if (s.T() == 0) {
+        if (raw && s.B > 0) return cudaMemsetAsync(raw, 0, sizeof(int) * s.B * s.E, st);
+        return cudaSuccess;
+    }
+    const dim3 grid(s.chunks(), s.B);
+    dispatch_count_kernel<<<grid, kThreads, 0, st>>>(idx, s.N, s.k, s.E, s.chunks(), ws.chunk_count);
+    if (raw)
+        dispatch_scan_kernel<<<1, 256, 0, st>>>(ws.chunk_count, s.B, s.E, s.chunks(), s.cap, nullptr, raw,
+                                                ws.chunk_base, counts, ws.row_base, ws.expert_rows,
+                                                ws.expert_start);
+    return cudaGetLastError();
+}
+
+// Slots (with the optional slot_base of earlier shards), drops, slot tables
+// and the gather; needs launch_dispatch_count's histogram in ws.
+cudaError_t launch_dispatch_finish(const void* x, const int* idx, const float* w, const Shape& s,
+                                   const Workspace& ws, const GemmScales& sc, const int* slot_base, int* counts,
+                                   int* token_ids, float* token_weights, void* a_rows, cudaStream_t st) {
     if (s.T() == 0) {
         cudaError_t e = cudaMemsetAsync(ws.expert_rows, 0, sizeof(int) * s.E, st);
         if (e == cudaSuccess) e = cudaMemsetAsync(ws.expert_start, 0, sizeof(int) * s.E, st);
@@ -307,11 +335,10 @@ cudaError_t launch_dispatch(const void* x, const int* idx, const float* w, const
         return e;
     }
     const dim3 grid(s.chunks(), s.B);
-    dispatch_count_kernel<<<grid, kThreads, 0, st>>>(idx, s.N, s.k, s.E, s.chunks(), ws.chunk_count);
-    dispatch_scan_kernel<<<1, 256, 0, st>>>(ws.chunk_count, s.B, s.E, s.chunks(), s.cap,
+    dispatch_scan_kernel<<<1, 256, 0, st>>>(ws.chunk_count, s.B, s.E, s.chunks(), s.cap, slot_base, nullptr,
                                             ws.chunk_base, counts, ws.row_base, ws.expert_rows, ws.expert_start);
     dispatch_assign_kernel<<<grid, kThreads, 0, st>>>(idx, w, s.N, s.k, s.E, s.cap, s.chunks(), ws.chunk_base,
-                                                      token_ids, token_weights, ws.route_slot);
+                                                      slot_base, token_ids, token_weights, ws.route_slot);
     // 16-bit activations: rows of d elements = d/8 16-byte vectors.
     const int64_t slots = (int64_t)s.B * s.E * s.cap;
     const unsigned gblocks = (unsigned)((slots + kWarps - 1) / kWarps);
@@ -332,6 +359,14 @@ cudaError_t launch_dispatch(const void* x, const int* idx, const float* w, const
                                                              ws.expert_start, s.N, s.E, s.B, s.cap, s.d / 8,
                                                              (uint4*)a_rows);
     return cudaGetLastError();
+}
+
+cudaError_t launch_dispatch(const void* x, const int* idx, const float* w, const Shape& s,
+                            const Workspace& ws, const GemmScales& sc, int* counts, int* token_ids,
+                            float* token_weights, void* a_rows, cudaStream_t st) {
+    cudaError_t e = launch_dispatch_count(idx, s, ws, counts, nullptr, st);
+    if (e != cudaSuccess) return e;
+    return launch_dispatch_finish(x, idx, w, s, ws, sc, nullptr, counts, token_ids, token_weights, a_rows, st);
 }
 
 }  // namespace moe

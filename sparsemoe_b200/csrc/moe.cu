@@ -110,8 +110,9 @@ int cuda_fail(cudaError_t e, const char* what) {
     return MOE_ERR_CUDA;
 }
 
-// Shape checks shared by every entry point.
-int make_shape(const MoeDims* d, Shape* s) {
+// Shape checks shared by every entry point; with bind_check, also that the
+// format's MoeDims pointers (weight scales) are set.
+int make_shape(const MoeDims* d, Shape* s, bool bind_check = true) {
     if (!d) { set_error("dims is null"); return MOE_ERR_INVALID_ARG; }
     if (d->num_batches < 0 || d->tokens < 0 || d->d_model <= 0 || d->d_ff <= 0 || d->num_experts <= 0 ||
         d->top_k <= 0) {
@@ -150,17 +151,17 @@ int make_shape(const MoeDims* d, Shape* s) {
     s->router_dtype = d->router_dtype;
     s->act_bf16 = d->dtype == MOE_DTYPE_BF16 || d->dtype == MOE_DTYPE_FP8_BLOCK || d->dtype == MOE_DTYPE_W4A16 ||
                   d->dtype == MOE_DTYPE_INT8_CHANNEL || d->dtype == MOE_DTYPE_NVFP4;
-    if (d->dtype == MOE_DTYPE_NVFP4 && (!d->w4_scale_gate || !d->w4_scale_up || !d->w4_scale_down ||
+    if (bind_check && d->dtype == MOE_DTYPE_NVFP4 && (!d->w4_scale_gate || !d->w4_scale_up || !d->w4_scale_down ||
                                         !d->fp4_global_gate || !d->fp4_global_up || !d->fp4_global_down)) {
         set_error("MOE_DTYPE_NVFP4 needs MoeDims.w4_scale_* (e4m3) and fp4_global_*");
         return MOE_ERR_INVALID_ARG;
     }
-    if (d->dtype == MOE_DTYPE_W4A16 && (!d->w4_scale_gate || !d->w4_scale_up || !d->w4_scale_down ||
+    if (bind_check && d->dtype == MOE_DTYPE_W4A16 && (!d->w4_scale_gate || !d->w4_scale_up || !d->w4_scale_down ||
                                         !d->w4_zero_gate || !d->w4_zero_up || !d->w4_zero_down)) {
         set_error("MOE_DTYPE_W4A16 needs MoeDims.w4_scale_* and w4_zero_*");
         return MOE_ERR_INVALID_ARG;
     }
-    if ((d->dtype == MOE_DTYPE_FP8_BLOCK || d->dtype == MOE_DTYPE_INT8_CHANNEL) &&
+    if (bind_check && (d->dtype == MOE_DTYPE_FP8_BLOCK || d->dtype == MOE_DTYPE_INT8_CHANNEL) &&
         (!d->w_scale_gate || !d->w_scale_up || !d->w_scale_down)) {
         set_error("dtype %d needs MoeDims.w_scale_gate / w_scale_up / w_scale_down", d->dtype);
         return MOE_ERR_INVALID_ARG;
@@ -237,11 +238,14 @@ int resolve_workspace(DeviceState& st, int dev, const MoeDims* dims, const Shape
             return MOE_ERR_INVALID_ARG;
         }
         carve_workspace(dims->scratch, s, ws);
+        if (dims->act_scale) ws->a_scale = dims->act_scale;
         note_status_word(dev, ws->status);
         return MOE_OK;
     }
     std::lock_guard<std::mutex> lk(g_mu);
-    return get_workspace(st, s, ws, header_only);
+    const int rc = get_workspace(st, s, ws, header_only);
+    if (rc == MOE_OK && dims->act_scale) ws->a_scale = dims->act_scale;
+    return rc;
 }
 
 }  // namespace
@@ -260,7 +264,7 @@ extern "C" int moe_capacity(int tokens, int top_k, int num_experts, float cf) {
 
 extern "C" size_t moe_workspace_bytes(const MoeDims* dims) {
     Shape s;
-    if (make_shape(dims, &s) != MOE_OK) return 0;
+    if (make_shape(dims, &s, /*bind_check=*/false) != MOE_OK) return 0;
     return workspace_bytes(s);
 }
 
@@ -392,8 +396,11 @@ int enqueue_route(const MoEArgs* a, const MoeDims* dims, const Shape& s, const W
             "router_topk");
     MOE_TRY(mark_stage(1, stream), "cudaEventRecord(stage event)");
     const FfnBuffers fb = ffn_buffers(a, s);
-    MOE_TRY(launch_dispatch(a->input, a->selected_expert_indices, a->selected_expert_weights, s, ws, scales_of(a, s),
-                            a->expert_counts, a->expert_token_ids, a->expert_token_weights, fb.a_rows, stream),
+    MOE_TRY(launch_dispatch_count(a->selected_expert_indices, s, ws, a->expert_counts, nullptr, stream),
+            "dispatch (count)");
+    MOE_TRY(launch_dispatch_finish(a->input, a->selected_expert_indices, a->selected_expert_weights, s, ws,
+                                   scales_of(a, s), dims->slot_base, a->expert_counts, a->expert_token_ids,
+                                   a->expert_token_weights, fb.a_rows, stream),
             "dispatch");
     return MOE_OK;
 }
@@ -494,26 +501,73 @@ extern "C" int moe_solve_v2(const MoEArgs* a, const MoeDims* dims, cudaStream_t 
 }
 
 // ---- expert-parallel building blocks ---------------------------------------
-extern "C" int moe_stage_route(const MoEArgs* a, const MoeDims* dims, cudaStream_t stream) {
-    Shape s;
-    int rc = make_shape(dims, &s);
+namespace {
+int route_stage_setup(const MoEArgs* a, const MoeDims* dims, const char* who, Shape* s, Workspace* ws) {
+    int rc = make_shape(dims, s, /*bind_check=*/false);   // routing needs no weights
     if (rc != MOE_OK) return rc;
-    const bool i8 = s.dtype == MOE_DTYPE_INT8;
     if (!a || !a->input || !a->router_weights || !a->selected_expert_indices || !a->selected_expert_weights ||
-        !a->expert_counts || !a->expert_token_ids || !a->expert_token_weights ||
-        !(i8 ? (const void*)a->per_expert_wmma_inputs_int8 : (const void*)a->per_expert_wmma_inputs)) {
-        set_error("moe_stage_route: a routing buffer of MoEArgs is null");
+        !a->expert_counts || !a->expert_token_ids || !a->expert_token_weights || !ffn_buffers(a, *s).a_rows) {
+        set_error("%s: a routing buffer of MoEArgs is null", who);
         return MOE_ERR_INVALID_ARG;
     }
     DeviceState* st = nullptr;
     int dev = 0;
     rc = device_state(&st, &dev);
     if (rc != MOE_OK) return rc;
+    return resolve_workspace(*st, dev, dims, *s, ws);
+}
+}  // namespace
+
+extern "C" int moe_stage_route(const MoEArgs* a, const MoeDims* dims, cudaStream_t stream) {
+    Shape s;
     Workspace ws;
-    rc = resolve_workspace(*st, dev, dims, s, &ws);
+    const int rc = route_stage_setup(a, dims, "moe_stage_route", &s, &ws);
     if (rc != MOE_OK) return rc;
     MOE_TRY(cudaMemsetAsync(ws.status, 0, sizeof(int), stream), "cudaMemsetAsync(status)");
     return enqueue_route(a, dims, s, ws, stream);
+}
+
+extern "C" int moe_stage_route_counts(const MoEArgs* a, const MoeDims* dims, int* raw_counts, cudaStream_t stream) {
+    Shape s;
+    Workspace ws;
+    const int rc = route_stage_setup(a, dims, "moe_stage_route_counts", &s, &ws);
+    if (rc != MOE_OK) return rc;
+    if (!raw_counts) { set_error("moe_stage_route_counts: raw_counts is null"); return MOE_ERR_INVALID_ARG; }
+    MOE_TRY(cudaMemsetAsync(ws.status, 0, sizeof(int), stream), "cudaMemsetAsync(status)");
+    MOE_TRY(launch_router_topk(a->input, a->router_weights, dims->router_bias, s, a->expert_logits,
+                               a->selected_expert_indices, a->selected_expert_weights, stream),
+            "router_topk");
+    MOE_TRY(launch_dispatch_count(a->selected_expert_indices, s, ws, a->expert_counts, raw_counts, stream),
+            "dispatch (count)");
+    return MOE_OK;
+}
+
+extern "C" int moe_stage_route_finish(const MoEArgs* a, const MoeDims* dims, cudaStream_t stream) {
+    Shape s;
+    Workspace ws;
+    const int rc = route_stage_setup(a, dims, "moe_stage_route_finish", &s, &ws);
+    if (rc != MOE_OK) return rc;
+    const FfnBuffers fb = ffn_buffers(a, s);
+    MOE_TRY(launch_dispatch_finish(a->input, a->selected_expert_indices, a->selected_expert_weights, s, ws,
+                                   scales_of(a, s), dims->slot_base, a->expert_counts, a->expert_token_ids,
+                                   a->expert_token_weights, fb.a_rows, stream),
+            "dispatch");
+    return MOE_OK;
+}
+
+namespace {
+size_t ffn_h_scale_bytes(const Shape& s, int64_t rows_capacity) {
+    if (s.dtype != MOE_DTYPE_FP8_BLOCK && s.dtype != MOE_DTYPE_INT8_CHANNEL) return 0;
+    return align256(sizeof(float) * (size_t)rows_capacity * (s.f / 128));
+}
+}  // namespace
+
+extern "C" size_t moe_ffn_scratch_bytes(const MoeDims* dims, int64_t rows_capacity) {
+    if (!dims || rows_capacity < 0 || dims->d_ff <= 0) return 0;
+    Shape s;   // only the format and d_ff matter (weights need not be bound yet)
+    s.dtype = dims->dtype;
+    s.f = dims->d_ff;
+    return workspace_header_bytes() + ffn_h_scale_bytes(s, rows_capacity);
 }
 
 extern "C" int moe_stage_expert_ffn(const MoEArgs* a, const MoeDims* dims, const int* group_rows,
@@ -569,16 +623,23 @@ extern "C" int moe_stage_expert_ffn(const MoEArgs* a, const MoeDims* dims, const
                 "cudaMemcpyAsync(group experts)");
     const GroupTable gt{ws.grp_rows, ws.grp_start, group_expert ? ws.grp_weight : nullptr, num_groups,
                         rows_capacity};
+    float* h_scale = nullptr;
     if (s.dtype == MOE_DTYPE_FP8_BLOCK || s.dtype == MOE_DTYPE_INT8_CHANNEL) {
-        set_error("moe_stage_expert_ffn: the dynamically quantised paths run through moe_solve_v2 only in this build");
-        return MOE_ERR_UNSUPPORTED;
+        // row scales of A from the caller; h scales in the caller's scratch after the header
+        if (!dims->act_scale || !dims->scratch ||
+            dims->scratch_bytes < workspace_header_bytes() + ffn_h_scale_bytes(s, rows_capacity)) {
+            set_error("moe_stage_expert_ffn: FP8_BLOCK / INT8_CHANNEL need MoeDims.act_scale and a scratch of "
+                      "moe_ffn_scratch_bytes()");
+            return MOE_ERR_INVALID_ARG;
+        }
+        h_scale = reinterpret_cast<float*>(static_cast<uint8_t*>(dims->scratch) + workspace_header_bytes());
     }
-    return enqueue_ffn(a, dims, s, gt, ws.status, nullptr, nullptr, st->num_sms, stream);
+    return enqueue_ffn(a, dims, s, gt, ws.status, dims->act_scale, h_scale, st->num_sms, stream);
 }
 
 extern "C" int moe_stage_combine(const MoEArgs* a, const MoeDims* dims, cudaStream_t stream) {
     Shape s;
-    int rc = make_shape(dims, &s);
+    int rc = make_shape(dims, &s, /*bind_check=*/false);
     if (rc != MOE_OK) return rc;
     if (!a || !a->hidden_mlp_layer_2_out || !a->final_output || !a->selected_expert_indices ||
         !a->selected_expert_weights) {

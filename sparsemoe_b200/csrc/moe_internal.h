@@ -77,6 +77,14 @@ cudaError_t launch_router_topk(const void* x, const void* wr, const float* bias,
 cudaError_t launch_dispatch(const void* x, const int* idx, const float* w, const Shape& s,
                             const Workspace& ws, const GemmScales& sc, int* counts, int* token_ids,
                             float* token_weights, void* a_rows, cudaStream_t st);
+// The same in two phases (expert parallelism over a split batch): route
+// histogram (+ the shard's raw per-(batch, expert) totals), then slots with
+// the earlier shards' slot_base, drops, tables and gather.
+cudaError_t launch_dispatch_count(const int* idx, const Shape& s, const Workspace& ws, int* counts, int* raw,
+                                  cudaStream_t st);
+cudaError_t launch_dispatch_finish(const void* x, const int* idx, const float* w, const Shape& s,
+                                   const Workspace& ws, const GemmScales& sc, const int* slot_base, int* counts,
+                                   int* token_ids, float* token_weights, void* a_rows, cudaStream_t st);
 // expert_gemm.cu: grouped tcgen05 GEMMs.
 cudaError_t launch_expert_up_gate(const void* a_rows, const void* w_gate, const void* w_up,
                                   const Shape& s, const GroupTable& gt, int* status, const GemmScales& sc,

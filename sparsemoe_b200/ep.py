@@ -15,10 +15,23 @@ exchanges, libsparsemoe_b200.so does all the compute:
                             expert-major layout (second stream)
   6. moe_stage_combine      local tokens: gate-weighted sum in route order
 
-Routing and capacity are per batch and every batch lives on one rank (each
-rank routes its own batches), so drops are decided locally exactly as on one
-GPU; the rows travel in f32 on the way back, so the output equals the
-single-GPU layer's on the same tokens.
+Two ways to place the tokens:
+
+* per-rank batches (default): every batch lives on one rank, so capacity and
+  drops are decided locally exactly as on one GPU;
+* global batches (`global_batch=True`): every batch of world*N tokens is split
+  over the ranks in token order (rank r holds tokens [r*N, (r+1)*N)); CAP is
+  that of the whole batch and a route is kept iff its slot in global route-id
+  order is < CAP.  Step 1 then runs in two phases: router + per-(batch,
+  expert) route totals (moe_stage_route_counts), an all_gather of the totals,
+  and the slots with each rank's prefix over the lower ranks' totals as
+  slot_base (moe_stage_route_finish).
+
+The rows travel back in f32, so the output equals the single-GPU layer's on
+the same tokens.  All weight formats run: 16-bit, per-tensor int8, 4-bit
+(INT4 g128, NVFP4) with bf16 rows on the wire, and the dynamically quantised
+FP8-block / int8-per-channel formats, whose 8-bit rows travel with their row
+scales (a second all-to-all of [rows, d/128] or [rows] f32).
 
 The planner functions below are pure (numpy) and shared with the CPU tests.
 """
@@ -28,7 +41,7 @@ import ctypes
 
 import numpy as np
 
-from . import LayerConfig, MoEArgs, MoeDims, check, lib
+from . import LayerConfig, MoEArgs, MoeDims, capacity, check, lib
 
 
 # ---- planner ---------------------------------------------------------------------
@@ -66,9 +79,21 @@ class _Chunk:
     """One group of whole batches routed, exchanged and combined together."""
 
 
+def _fmt(cfg: LayerConfig):
+    """(wire dtype of the A rows, dtype of h, activation scales per row) of a format."""
+    import torch
+    t16 = torch.bfloat16 if cfg.act_bf16 else torch.float16
+    if cfg.int8 or cfg.int8ch:
+        return torch.int8, torch.int8, (1 if cfg.int8ch else 0)
+    if cfg.fp8:
+        return torch.uint8, torch.uint8, cfg.d_model // 128
+    return t16, t16, 0
+
+
 class ExpertParallelLayer:
     """Rank-local part of an expert-parallel layer.  `cfg` is the per-rank
-    workload (its batches and tokens) and the global expert count.
+    workload (its batches and tokens -- with `global_batch`, its shard of
+    every batch) and the global expert count.
 
     The rank's batches can be split into `chunks` groups that pipeline: while
     the owner GEMMs run on chunk c (compute stream), chunk c+1's rows arrive
@@ -80,7 +105,8 @@ class ExpertParallelLayer:
 
     PHASES = ("route", "exchange_and_ffn", "combine")
 
-    def __init__(self, cfg: LayerConfig, device, group=None, chunks: int | None = None):
+    def __init__(self, cfg: LayerConfig, device, group=None, chunks: int | None = None,
+                 global_batch: bool = False):
         import torch
         import torch.distributed as dist
         self.torch, self.dist = torch, dist
@@ -89,16 +115,26 @@ class ExpertParallelLayer:
         self.rank = dist.get_rank(group)
         assert cfg.num_experts % self.world == 0, "experts must divide evenly over the ranks"
         self.cfg = cfg
+        self.global_batch = global_batch
         self.device = torch.device(device)
         self.e_loc = cfg.num_experts // self.world
         B, N, d, f, E, k = cfg.num_batches, cfg.tokens, cfg.d_model, cfg.d_ff, cfg.num_experts, cfg.top_k
-        if chunks is None:
-            chunks = 1
+        chunks = 1 if chunks is None else chunks
         assert B % chunks == 0 or B == 0, "chunks must divide num_batches"
+        assert not (global_batch and chunks > 1), "global batches run as one chunk"
         self.n_chunks = max(chunks, 1)
-        self.cap = cfg.capacity()
-        t16 = torch.bfloat16 if cfg.bf16 else torch.float16
-        wt = torch.int8 if cfg.int8 else t16
+        if global_batch:
+            # CAP of the whole batch (world shards of N tokens); cap < 0: no drop
+            if cfg.cap > 0:
+                self.cap = cfg.cap
+            elif cfg.cap < 0:
+                self.cap = N * self.world
+            else:
+                self.cap = capacity(N * self.world, k, E, cfg.capacity_factor)
+        else:
+            self.cap = cfg.capacity()
+        t16 = torch.bfloat16 if cfg.act_bf16 else torch.float16
+        at, ht, self.n_scale = _fmt(cfg)
         dev = self.device
         z = lambda *s, dt: torch.empty(*s, dtype=dt, device=dev)  # noqa: E731
         T = cfg.T
@@ -113,29 +149,34 @@ class ExpertParallelLayer:
         self.counts = z(max(B, 1), E, dt=torch.int32)
         self.token_ids = z(rows, dt=torch.int32)
         self.token_weights = z(rows, dt=torch.float32)
-        self.send_x = z(rows, d, dt=wt)
+        self.send_x = z(rows, d, dt=at)
+        self.send_scale = z(rows, self.n_scale, dt=torch.float32) if self.n_scale else None
         self.back_y = z(rows, d, dt=torch.float32)
         self.out = z(max(T, 1), d, dt=torch.float32)
         self.out16 = z(max(T, 1), d, dt=t16)
-        # owner side (E/P experts, rows from every rank)
-        self.recv_cap = max(self.world * B * self.e_loc * self.cap, 1)
-        self.wg = z(self.e_loc, d, f, dt=wt)
-        self.wu = z(self.e_loc, d, f, dt=wt)
-        self.wd = z(self.e_loc, f, d, dt=wt)
-        self.recv_x = z(self.recv_cap, d, dt=wt)
-        self.h = z(self.recv_cap, f, dt=wt)
+        self.raw = z(max(B, 1), E, dt=torch.int32) if global_batch else None
+        self.slot_base = z(max(B, 1), E, dt=torch.int32) if global_batch else None
+        # owner side (E/P experts, rows from every rank): per (batch, local
+        # expert) at most CAP rows in all -- per sender with per-rank batches
+        per_owner = B * self.e_loc * self.cap
+        self.recv_cap = max(per_owner if global_batch else self.world * per_owner, 1)
+        self.recv_x = z(self.recv_cap, d, dt=at)
+        self.recv_scale = z(self.recv_cap, self.n_scale, dt=torch.float32) if self.n_scale else None
+        self.h = z(self.recv_cap, f, dt=ht)
         self.recv_y = z(self.recv_cap, d, dt=torch.float32)
+        self.weights = {}
         self.scales = {}
         self.last_plan = None
         # chunk views and scratch
         Bc = B // self.n_chunks if B else 0
         self.chunk_cfg = LayerConfig(Bc, N, d, f, E, k, cfg.capacity_factor, cfg.dtype, cfg.router_f32, cfg.zipf_s,
-                                     cfg.cap, cfg.act_scale, cfg.mid_scale)
+                                     self.cap if global_batch else cfg.cap, cfg.act_scale, cfg.mid_scale)
         sdims = self.chunk_cfg.dims()
-        ws_bytes = int(lib.moe_workspace_bytes(ctypes.byref(sdims)))
-        ws_bytes = max(ws_bytes, 1 << 16)
+        ws_bytes = max(int(lib.moe_workspace_bytes(ctypes.byref(sdims))), 1 << 16)
         self.chunks = []
-        Tc, rc, ocap = Bc * N, Bc * E * self.cap, self.world * Bc * self.e_loc * self.cap
+        Tc, rc, ocap = Bc * N, Bc * E * self.cap, self.recv_cap // self.n_chunks
+        fdims = self._ffn_dims_base()
+        ffn_bytes = max(int(lib.moe_ffn_scratch_bytes(ctypes.byref(fdims), ocap)), 1 << 16)
         for c in range(self.n_chunks):
             ch = _Chunk()
             t0, r0, o0 = c * Tc, c * rc, c * ocap
@@ -144,41 +185,89 @@ class ExpertParallelLayer:
             ch.counts = self.counts[c * Bc:(c + 1) * Bc]
             ch.token_ids, ch.token_weights = self.token_ids[r0:r0 + rc], self.token_weights[r0:r0 + rc]
             ch.send_x, ch.back_y = self.send_x[r0:r0 + rc], self.back_y[r0:r0 + rc]
+            ch.send_scale = self.send_scale[r0:r0 + rc] if self.n_scale else None
             ch.out, ch.out16 = self.out[t0:t0 + Tc], self.out16[t0:t0 + Tc]
             ch.recv_x, ch.h, ch.recv_y = self.recv_x[o0:o0 + ocap], self.h[o0:o0 + ocap], self.recv_y[o0:o0 + ocap]
+            ch.recv_scale = self.recv_scale[o0:o0 + ocap] if self.n_scale else None
             ch.recv_cap = ocap
             ch.scratch = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
-            ch.ffn_scratch = torch.empty(1 << 16, dtype=torch.uint8, device=dev)
+            ch.ffn_scratch = torch.empty(ffn_bytes, dtype=torch.uint8, device=dev)
             self.chunks.append(ch)
         self.comm_stream = torch.cuda.Stream(device=dev)
 
-    def load(self, inputs: dict) -> "ExpertParallelLayer":
-        """inputs from make_inputs() for the FULL expert set; this rank keeps its experts."""
-        torch = self.torch
+    # -- weights ------------------------------------------------------------------
+    def load(self, inputs: dict, local: bool = False) -> "ExpertParallelLayer":
+        """inputs from make_inputs(): x (this rank's tokens), wr, bias and the
+        weights of the FULL expert set (this rank keeps its E/P experts), or
+        with local=True weights that already hold only this rank's experts."""
+        torch, cfg = self.torch, self.cfg
 
-        def put(dst, arr):
+        def dev_t(arr):
             arr = np.ascontiguousarray(arr)
-            src = torch.from_numpy(arr.view(np.int16)).view(dst.dtype) if arr.dtype == np.uint16 \
-                else torch.from_numpy(arr)
-            dst.copy_(src.reshape(dst.shape))
-        lo, hi = self.rank * self.e_loc, (self.rank + 1) * self.e_loc
-        if self.cfg.T > 0:
-            put(self.x, inputs["x"])
-        put(self.wr, inputs["wr"])
-        sfx = "_q" if self.cfg.int8 else ""
-        put(self.wg, inputs["wg" + sfx][lo:hi])
-        put(self.wu, inputs["wu" + sfx][lo:hi])
-        put(self.wd, inputs["wd" + sfx][lo:hi])
-        if self.cfg.int8:
+            t = torch.from_numpy(arr.view(np.int16)) if arr.dtype == np.uint16 else torch.from_numpy(arr)
+            return t.to(self.device)
+
+        def mine(arr):
+            return arr if local else arr[self.rank * self.e_loc:(self.rank + 1) * self.e_loc]
+        if cfg.T > 0:
+            x = dev_t(inputs["x"])
+            self.x[: cfg.T].copy_(x.view(self.x.dtype).reshape(cfg.T, cfg.d_model))
+        wr = dev_t(inputs["wr"])
+        self.wr.copy_(wr.view(self.wr.dtype).reshape(self.wr.shape))
+        quant = cfg.int8 or cfg.int8ch or cfg.fp8 or cfg.w4
+        sfx = "_q" if quant else ""
+        t16 = self.x.dtype
+        for n in ("wg", "wu", "wd"):
+            t = dev_t(mine(inputs[n + sfx]))
+            self.weights[n] = t.view(t16) if not quant else t
+        if cfg.int8:
             self.scales = {k: inputs[k] for k in ("s_in", "s_gate", "s_up", "s_mid", "s_down")}
+        if cfg.channel_scaled:
+            self.weights["w_scale"] = [dev_t(mine(inputs[k])) for k in ("sg", "su", "sd")]
+        if cfg.w4:
+            keys = ("wg_s", "wu_s", "wd_s") + (() if cfg.nvfp4 else ("wg_z", "wu_z", "wd_z"))
+            self.weights["w4"] = [dev_t(mine(inputs[k])) for k in keys]
+            if cfg.nvfp4:
+                self.weights["fp4g"] = [dev_t(mine(np.asarray(inputs[k], np.float32)))
+                                        for k in ("wg_g", "wu_g", "wd_g")]
         if inputs.get("bias") is not None:
             self.bias = torch.from_numpy(inputs["bias"]).to(self.device)
         return self
 
+    @property
+    def wg(self):
+        return self.weights["wg"]
+
+    @property
+    def wu(self):
+        return self.weights["wu"]
+
+    @property
+    def wd(self):
+        return self.weights["wd"]
+
+    # -- call arguments -------------------------------------------------------------
     def _scales_into(self, a):
         sc = self.scales
         a.scale_input_act, a.scale_gate_w, a.scale_up_w = sc["s_in"], sc["s_gate"], sc["s_up"]
         a.scale_mid_act, a.scale_down_w = sc["s_mid"], sc["s_down"]
+
+    def _set_rows(self, a, rows, h=None):
+        cfg, p = self.cfg, (lambda t: t.data_ptr())
+        if cfg.int8 or cfg.int8ch:
+            a.per_expert_wmma_inputs_int8 = p(rows)
+            if h is not None:
+                a.hidden_mlp_layer_1_out_int8 = p(h)
+            if cfg.int8:
+                self._scales_into(a)
+        elif cfg.fp8:
+            a.per_expert_wmma_inputs_fp8 = p(rows)
+            if h is not None:
+                a.hidden_mlp_layer_1_out_fp8 = p(h)
+        else:
+            a.per_expert_wmma_inputs = p(rows)
+            if h is not None:
+                a.hidden_mlp_layer_1_out_fp16 = p(h)
 
     def _route_args(self, ch) -> MoEArgs:
         a = MoEArgs()
@@ -187,11 +276,7 @@ class ExpertParallelLayer:
         a.selected_expert_indices, a.selected_expert_weights = p(ch.idx), p(ch.w)
         a.expert_counts, a.expert_token_ids, a.expert_token_weights = p(ch.counts), p(ch.token_ids), \
             p(ch.token_weights)
-        if self.cfg.int8:
-            a.per_expert_wmma_inputs_int8 = p(ch.send_x)
-            self._scales_into(a)
-        else:
-            a.per_expert_wmma_inputs = p(ch.send_x)
+        self._set_rows(a, ch.send_x)
         a.hidden_mlp_layer_2_out = p(ch.back_y)
         a.final_output = p(ch.out)
         a.num_batches = self.chunk_cfg.num_batches
@@ -200,20 +285,39 @@ class ExpertParallelLayer:
         return a
 
     def _ffn_args(self, ch) -> MoEArgs:
-        a = MoEArgs()
+        cfg, a = self.cfg, MoEArgs()
         p = lambda t: t.data_ptr()  # noqa: E731
-        if self.cfg.int8:
-            a.expert_gate_proj_weights_int8, a.expert_up_proj_weights_int8 = p(self.wg), p(self.wu)
-            a.expert_down_proj_weights_int8 = p(self.wd)
-            a.per_expert_wmma_inputs_int8, a.hidden_mlp_layer_1_out_int8 = p(ch.recv_x), p(ch.h)
-            self._scales_into(a)
+        wg, wu, wd = p(self.wg), p(self.wu), p(self.wd)
+        if cfg.int8 or cfg.int8ch:
+            a.expert_gate_proj_weights_int8, a.expert_up_proj_weights_int8, a.expert_down_proj_weights_int8 = \
+                wg, wu, wd
+        elif cfg.fp8:
+            a.expert_gate_proj_weights_fp8, a.expert_up_proj_weights_fp8, a.expert_down_proj_weights_fp8 = \
+                wg, wu, wd
+        elif cfg.w4:
+            a.expert_gate_proj_weights_int4, a.expert_up_proj_weights_int4, a.expert_down_proj_weights_int4 = \
+                wg, wu, wd
         else:
-            a.expert_gate_proj_weights, a.expert_up_proj_weights = p(self.wg), p(self.wu)
-            a.expert_down_proj_weights = p(self.wd)
-            a.per_expert_wmma_inputs, a.hidden_mlp_layer_1_out_fp16 = p(ch.recv_x), p(ch.h)
+            a.expert_gate_proj_weights, a.expert_up_proj_weights, a.expert_down_proj_weights = wg, wu, wd
+        self._set_rows(a, ch.recv_x, ch.h)
         a.hidden_mlp_layer_2_out = p(ch.recv_y)
         return a
 
+    def _ffn_dims_base(self) -> MoeDims:
+        cfg = self.cfg
+        fd = MoeDims(0, 0, cfg.d_model, cfg.d_ff, self.e_loc, 1, cfg.capacity_factor, 0, cfg.dtype, 0)
+        if self.weights.get("w_scale"):
+            fd.w_scale_gate, fd.w_scale_up, fd.w_scale_down = (t.data_ptr() for t in self.weights["w_scale"])
+        if self.weights.get("w4"):
+            w4 = [t.data_ptr() for t in self.weights["w4"]]
+            fd.w4_scale_gate, fd.w4_scale_up, fd.w4_scale_down = w4[:3]
+            if len(w4) == 6:
+                fd.w4_zero_gate, fd.w4_zero_up, fd.w4_zero_down = w4[3:]
+        if self.weights.get("fp4g"):
+            fd.fp4_global_gate, fd.fp4_global_up, fd.fp4_global_down = (t.data_ptr() for t in self.weights["fp4g"])
+        return fd
+
+    # -- one layer call -------------------------------------------------------------
     def forward(self, stream=None, timing=None):
         """One layer call.  `timing` (optional dict) receives torch.cuda.Event
         lists: 'start', 'routed', 'ffn' (pairs per chunk), 'combine', 'end'."""
@@ -234,8 +338,20 @@ class ExpertParallelLayer:
         bias = None if self.bias is None else self.bias.data_ptr()
         for ch in self.chunks:                                   # 1. route every chunk
             ch.dims = self.chunk_cfg.dims(bias, ch.out16.data_ptr(), ch.scratch.data_ptr(), ch.scratch.numel())
+            if self.n_scale:
+                ch.dims.act_scale = ch.send_scale.data_ptr()
             ch.ra = self._route_args(ch)
-            check(lib.moe_stage_route(ctypes.byref(ch.ra), ctypes.byref(ch.dims), sp))
+            if self.global_batch:
+                # phase 1, then every rank's totals; slot_base = sum over the lower ranks
+                check(lib.moe_stage_route_counts(ctypes.byref(ch.ra), ctypes.byref(ch.dims),
+                                                 self.raw.data_ptr(), sp))
+                allraw = torch.empty(self.world, *self.raw.shape, dtype=torch.int32, device=self.device)
+                dist.all_gather_into_tensor(allraw, self.raw, group=self.group)
+                torch.sum(allraw[: self.rank], dim=0, dtype=torch.int32, out=self.slot_base)
+                ch.dims.slot_base = self.slot_base.data_ptr()
+                check(lib.moe_stage_route_finish(ctypes.byref(ch.ra), ctypes.byref(ch.dims), sp))
+            else:
+                check(lib.moe_stage_route(ctypes.byref(ch.ra), ctypes.byref(ch.dims), sp))
         ev("routed")
         nc = self.n_chunks
         mine = self.counts[: cfg.num_batches].view(nc, -1, cfg.num_experts).sum(dim=1, dtype=torch.int32)
@@ -250,20 +366,26 @@ class ExpertParallelLayer:
             rs, groups = recv_plan(table_h[:, c], self.rank)
             plans.append((ss, rs, groups))
         sends = []
-        with torch.cuda.stream(C):                          # 3. rows to owners, all chunks
+        with torch.cuda.stream(C):                          # 3. rows (and row scales) to owners
             C.wait_event(routed)
             for ch, (ss, rs, _) in zip(self.chunks, plans):
-                sends.append(dist.all_to_all_single(ch.recv_x[:sum(rs)], ch.send_x[:sum(ss)], rs, ss,
-                                                    group=self.group, async_op=True))
+                works = [dist.all_to_all_single(ch.recv_x[:sum(rs)], ch.send_x[:sum(ss)], rs, ss,
+                                                group=self.group, async_op=True)]
+                if self.n_scale:
+                    works.append(dist.all_to_all_single(ch.recv_scale[:sum(rs)], ch.send_scale[:sum(ss)], rs, ss,
+                                                        group=self.group, async_op=True))
+                sends.append(works)
         rets = []
-        fdims = MoeDims(0, 0, cfg.d_model, cfg.d_ff, self.e_loc, 1, cfg.capacity_factor, 0, cfg.dtype, 0, None,
-                        None, None, 0)
-        for ch, (ss, rs, (g_rows, g_start, g_exp)), work in zip(self.chunks, plans, sends):
-            work.wait()                                      # compute stream waits for chunk's rows
+        fdims = self._ffn_dims_base()
+        for ch, (ss, rs, (g_rows, g_start, g_exp)), works in zip(self.chunks, plans, sends):
+            for work in works:
+                work.wait()                                  # compute stream waits for chunk's rows
             ev("ffn")
             fa = self._ffn_args(ch)
             fd = MoeDims(*[getattr(fdims, n) for n, _ in MoeDims._fields_])
             fd.scratch, fd.scratch_bytes = ch.ffn_scratch.data_ptr(), ch.ffn_scratch.numel()
+            if self.n_scale:
+                fd.act_scale = ch.recv_scale.data_ptr()
             check(lib.moe_stage_expert_ffn(ctypes.byref(fa), ctypes.byref(fd), g_rows.ctypes.data,
                                            g_start.ctypes.data, g_exp.ctypes.data, len(g_rows), ch.recv_cap, sp))
             ev("ffn")

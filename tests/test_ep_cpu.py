@@ -114,3 +114,50 @@ def test_ep_exchange_gloo_world2():
         errs = dict(results)
     assert set(errs) == {0, 1}
     assert max(errs.values()) < 1e-2, errs
+
+
+def _global_rank_main(rank, world, port, cfg_args, results):
+    """A batch of world*N tokens split over the ranks: each rank routes its
+    shard, the per-expert totals are all-gathered and a route is kept iff
+    (sum of the lower ranks' totals) + its slot within the shard < CAP of the
+    whole batch.  Must equal the single-process routing of the whole batch."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    B, N, d, f, E, k, cf, zipf = cfg_args
+    full_cfg = sm.LayerConfig(B, N * world, d, f, E, k, cf, zipf_s=zipf)
+    full = sm.make_inputs(full_cfg, 3)
+    cap = full_cfg.capacity()
+    ref = O.route(full["x"], full["wr"], full["bias"], B, N * world, d, E, k, cap, False)
+    x = full["x"].reshape(B, world, N, d)[:, rank].reshape(B * N, d)
+    # local routing with no drop (cap = N) gives the shard's route-order slots
+    loc = O.route(x, full["wr"], full["bias"], B, N, d, E, k, N * k, False)
+    raw = np.zeros((B, E), np.int32)
+    for b in range(B):
+        raw[b] = np.bincount(loc["idx"][b * N:(b + 1) * N].reshape(-1), minlength=E)[:E]
+    gathered = [torch.zeros(B, E, dtype=torch.int32) for _ in range(world)]
+    dist.all_gather(gathered, torch.from_numpy(raw))
+    slot_base = sum(g.numpy() for g in gathered[:rank]) if rank else np.zeros((B, E), np.int32)
+    ok = True
+    for b in range(B):
+        for t in range(N):
+            for l in range(k):
+                r = (b * N + t) * k + l
+                e = loc["idx"][b * N + t, l]
+                kept = loc["route_slot"][r] >= 0 and slot_base[b, e] + loc["route_slot"][r] < cap
+                gr = (b * N * world + rank * N + t) * k + l
+                ok &= bool(ref["idx"][b * N * world + rank * N + t, l] == e)
+                ok &= bool(kept == (ref["route_slot"][gr] >= 0))
+                if kept:
+                    ok &= bool(slot_base[b, e] + loc["route_slot"][r] == ref["route_slot"][gr])
+    results[rank] = ok
+    dist.destroy_process_group()
+
+
+def test_global_batch_drops_gloo_world2():
+    cfg_args = (2, 96, 256, 128, 16, 4, 1.0, 1.2)       # Zipf bias: hot experts overflow CAP
+    port = 29700 + (os.getpid() % 2000)
+    with mp.Manager() as m:
+        results = m.dict()
+        mp.spawn(_global_rank_main, args=(2, port, cfg_args, results), nprocs=2, join=True)
+        res = dict(results)
+    assert res == {0: True, 1: True}

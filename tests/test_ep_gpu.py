@@ -1,61 +1,89 @@
-"""Expert parallelism on real GPUs (NCCL): each rank routes its own batches,
-sends rows to the experts' owners, runs its E/P experts, gets the rows back
-and combines.  Must equal the single-GPU layer on the same tokens.  Needs >= 2
-GPUs; runs as child processes, one per GPU."""
+"""Expert parallelism on real GPUs (NCCL): each rank routes its own tokens,
+sends rows (and, for the dynamically quantised formats, their row scales) to
+the experts' owners, runs its E/P experts, gets the rows back and combines.
+Must equal the single-GPU layer on the same tokens bit for bit.  Needs >= 2
+GPUs; runs as child processes, one per GPU, with NVLS off."""
 import os
 
 import numpy as np
 import pytest
 
+import sparsemoe_b200 as sm
+
 pytestmark = pytest.mark.gpu
 
 
-def _worker(rank, world, port, cfg_args, results):
+def _worker(rank, world, port, case, results):
     import torch
     import torch.distributed as dist
-    import sparsemoe_b200 as sm
     from sparsemoe_b200.ep import ExpertParallelLayer
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     from datetime import timedelta
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
                             device_id=torch.device("cuda", rank))
-    cfg = sm.LayerConfig(*cfg_args[:7], dtype=cfg_args[7], zipf_s=cfg_args[8])
-    full = sm.make_inputs(cfg, 5)
-    mine = sm.make_inputs(cfg, 100 + rank)
-    inputs = {**full, "x": mine["x"]}
-    ep = ExpertParallelLayer(cfg, f"cuda:{rank}", chunks=cfg_args[9] if len(cfg_args) > 9 else 1).load(inputs)
+    B, N, d, f, E, k, cf, dtype, zipf, chunks, glob = case
+    if glob:
+        # one batch of world*N tokens; this rank holds tokens [rank*N, (rank+1)*N) of every batch
+        full_cfg = sm.LayerConfig(B, N * world, d, f, E, k, cf, dtype=dtype, zipf_s=zipf,
+                                  router_f32=dtype in (sm.DTYPE_W4A16, sm.DTYPE_NVFP4))
+        full = sm.make_inputs(full_cfg, 5)
+        x = full["x"].reshape(B, world, N, d)[:, rank].reshape(B * N, d)
+        cfg = sm.LayerConfig(B, N, d, f, E, k, cf, dtype=dtype, zipf_s=zipf, router_f32=full_cfg.router_f32)
+        ep = ExpertParallelLayer(cfg, f"cuda:{rank}", global_batch=True).load({**full, "x": x})
+        single = sm.MoeLayer(full_cfg, f"cuda:{rank}").load(full)
+        rows = np.concatenate([np.arange(b * N * world + rank * N, b * N * world + (rank + 1) * N)
+                               for b in range(B)])
+    else:
+        cfg = sm.LayerConfig(B, N, d, f, E, k, cf, dtype=dtype, zipf_s=zipf)
+        full = sm.make_inputs(cfg, 5)
+        mine = sm.make_inputs(cfg, 100 + rank)
+        inputs = {**full, "x": mine["x"]}
+        ep = ExpertParallelLayer(cfg, f"cuda:{rank}", chunks=chunks).load(inputs)
+        single = sm.MoeLayer(cfg, f"cuda:{rank}").load(inputs)
+        rows = np.arange(cfg.T)
     ep.forward()
     ep.sync_check()
     ep.forward()          # second call: reuses buffers and the library scratch
     ep.sync_check()
-    single = sm.MoeLayer(cfg, f"cuda:{rank}").load(inputs)
     single.forward()
     single.sync_check()
     a = ep.out.cpu().numpy()[: cfg.T]
-    b = single.out.cpu().numpy()[: cfg.T]
+    b = single.out.cpu().numpy()[rows]
+    idx_equal = bool(np.array_equal(ep.idx.cpu().numpy()[: cfg.T], single.idx.cpu().numpy()[rows]))
     results[rank] = (bool(np.array_equal(a, b)), float(np.abs(a - b).max() / max(np.abs(b).max(), 1e-30)),
-                     bool(np.array_equal(ep.idx.cpu().numpy(), single.idx.cpu().numpy())))
+                     idx_equal)
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("cfg_args", [
-    (2, 256, 512, 512, 8, 2, 1.25, 1, 0.0),     # bf16, Mixtral-like routing
-    (1, 384, 256, 256, 16, 4, 1.0, 0, 1.1),     # fp16, Zipf bias -> drops
-    (2, 128, 512, 256, 8, 2, 1.25, 2, 0.0),     # int8 path
-    (4, 128, 256, 256, 8, 2, 1.25, 1, 0.0, 2),  # two pipelined batch chunks
-])
-def test_ep_matches_single_gpu(gpu, cfg_args):
+CASES = {
+    "bf16": (2, 256, 512, 512, 8, 2, 1.25, sm.DTYPE_BF16, 0.0, 1, False),
+    "fp16_zipf_drops": (1, 384, 256, 256, 16, 4, 1.0, sm.DTYPE_F16, 1.1, 1, False),
+    "int8": (2, 128, 512, 256, 8, 2, 1.25, sm.DTYPE_INT8, 0.0, 1, False),
+    "two_chunks": (4, 128, 256, 256, 8, 2, 1.25, sm.DTYPE_BF16, 0.0, 2, False),
+    "int8_channel": (1, 256, 512, 256, 16, 4, 1.0, sm.DTYPE_INT8_CHANNEL, 1.1, 1, False),
+    "fp8_block": (1, 256, 512, 256, 16, 4, 1.25, sm.DTYPE_FP8_BLOCK, 0.0, 1, False),
+    "int4_g128": (1, 256, 512, 256, 16, 4, 1.25, sm.DTYPE_W4A16, 1.0, 1, False),
+    "nvfp4": (1, 256, 512, 256, 16, 4, 1.25, sm.DTYPE_NVFP4, 1.0, 1, False),
+    "global_bf16_drops": (2, 192, 512, 256, 16, 4, 1.0, sm.DTYPE_BF16, 1.2, 1, True),
+    "global_int4_deepseek_like": (1, 256, 512, 256, 32, 8, 1.25, sm.DTYPE_W4A16, 1.0, 1, True),
+    "global_fp8": (1, 256, 512, 256, 16, 4, 1.0, sm.DTYPE_FP8_BLOCK, 1.1, 1, True),
+}
+
+
+@pytest.mark.parametrize("name", list(CASES))
+def test_ep_matches_single_gpu(gpu, name):
     import torch
     import torch.multiprocessing as mp
+    case = CASES[name]
     world = torch.cuda.device_count()
     if world < 2:
         pytest.skip("needs >= 2 GPUs")
-    world = 2 if cfg_args[4] % 4 else min(world, 4)
+    world = 2 if case[4] % 4 else min(world, 4)
     port = 29600 + (os.getpid() % 2000)
     with mp.Manager() as m:
         results = m.dict()
-        mp.spawn(_worker, args=(world, port, cfg_args, results), nprocs=world, join=True)
+        mp.spawn(_worker, args=(world, port, case, results), nprocs=world, join=True)
         res = dict(results)
     assert len(res) == world
     for rank, (equal, err, idx_equal) in res.items():
