@@ -35,6 +35,10 @@ STAGES = ["router_topk", "dispatch", "expert_up_gate_gemm", "expert_down_gemm", 
 KERNELS_PER_STEP = 8   # router_topk, dispatch x4 (count, scan, assign, gather), up/gate GEMM, down GEMM, combine
 
 
+# workloads whose batches are split over the ranks under expert parallelism (global CAP)
+GLOBAL_BATCH = {"ds3_int4_decode", "ds3_int4_prefill", "ds3_nvfp4_decode", "ds3_nvfp4_prefill"}
+
+
 def workload(name: str):
     import sparsemoe_b200 as sm
     table = {
@@ -62,6 +66,17 @@ def workload(name: str):
                                             router_f32=True, zipf_s=1.0),
         "nvfp4_cfg5_prefill": sm.LayerConfig(1, 8192, 7168, 2048, 32, 8, 1.25, dtype=sm.DTYPE_NVFP4,
                                              router_f32=True, zipf_s=1.0),
+        # BASELINE configs[4] as the whole expert-parallel layer: E = 256 over the GPUs, 512 (decode) or
+        # 8192 (prefill) tokens per GPU; under torchrun the batch of N x tokens is split over the ranks
+        # and CAP / drops are global (GLOBAL_BATCH).  On one GPU: all 256 experts, its own tokens.
+        "ds3_int4_decode": sm.LayerConfig(1, 512, 7168, 2048, 256, 8, 1.25, dtype=sm.DTYPE_W4A16,
+                                          router_f32=True, zipf_s=1.0),
+        "ds3_int4_prefill": sm.LayerConfig(1, 8192, 7168, 2048, 256, 8, 1.25, dtype=sm.DTYPE_W4A16,
+                                           router_f32=True, zipf_s=1.0),
+        "ds3_nvfp4_decode": sm.LayerConfig(1, 512, 7168, 2048, 256, 8, 1.25, dtype=sm.DTYPE_NVFP4,
+                                           router_f32=True, zipf_s=1.0),
+        "ds3_nvfp4_prefill": sm.LayerConfig(1, 8192, 7168, 2048, 256, 8, 1.25, dtype=sm.DTYPE_NVFP4,
+                                            router_f32=True, zipf_s=1.0),
     }
     return table[name]
 
@@ -173,22 +188,112 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------------------
-def device_inputs(layer, seed: int):
-    """Seeded synthetic inputs generated on the device (x ~ N(0,1), router
-    ~ N(0,0.02), gate/up ~ N(0,1/sqrt(d)), down ~ N(0,1/sqrt(f)))."""
+def quantise_weights(cfg, dev, g, E, wdict):
+    """Seeded 16-bit weights (gate/up ~ N(0,1/sqrt(d)), down ~ N(0,1/sqrt(f)))
+    generated on the device and quantised there by the library's device
+    quantisers (bit-identical to the host ones).  Fills wdict with the
+    quantised tensors: wg/wu/wd plus w_scale (FP8 / int8 per channel), w4
+    (INT4 scales+zeros, NVFP4 scales) and fp4g (NVFP4 globals)."""
     import torch
+    import sparsemoe_b200 as sm
+    d, f = cfg.d_model, cfg.d_ff
+    t16 = torch.bfloat16 if cfg.act_bf16 else torch.float16
+    st = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+    p = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    ws, w4s, w4z, fp4g = [], [], [], []
+    for name, (K, N) in (("wg", (d, f)), ("wu", (d, f)), ("wd", (f, d))):
+        w16 = torch.empty(E, K, N, dtype=t16, device=dev).normal_(0.0, K ** -0.5, generator=g)
+        bf = int(cfg.act_bf16)
+        if not (cfg.fp8 or cfg.int8ch or cfg.w4):
+            wdict[name] = w16
+            continue
+        if cfg.fp8:
+            q = torch.empty(E, K, N, dtype=torch.uint8, device=dev)
+            sc = torch.empty(E, K // 128, N // 128, dtype=torch.float32, device=dev)
+            rc = sm.lib.moe_quantize_fp8_blocks_device(p(w16), E, K, N, bf, p(q), p(sc), st)
+            ws.append(sc)
+        elif cfg.int8ch:
+            q = torch.empty(E, K, N, dtype=torch.int8, device=dev)
+            sc = torch.empty(E, N, dtype=torch.float32, device=dev)
+            rc = sm.lib.moe_quantize_int8_channel_device(p(w16), E, K, N, bf, p(q), p(sc), st)
+            ws.append(sc)
+        elif cfg.nvfp4:
+            q = torch.empty(E, K, N // 2, dtype=torch.uint8, device=dev)
+            sc = torch.empty(E, K // 16, N, dtype=torch.uint8, device=dev)
+            gl = torch.empty(E, dtype=torch.float32, device=dev)
+            rc = sm.lib.moe_quantize_nvfp4_device(p(w16), E, K, N, bf, p(q), p(sc), p(gl), st)
+            w4s.append(sc)
+            fp4g.append(gl)
+        else:
+            q = torch.empty(E, K, N // 2, dtype=torch.uint8, device=dev)
+            sc = torch.empty(E, K // 128, N, dtype=torch.int16, device=dev)
+            zr = torch.empty_like(sc)
+            rc = sm.lib.moe_quantize_int4_g128_device(p(w16), E, K, N, bf, p(q), p(sc), p(zr), st)
+            w4s.append(sc)
+            w4z.append(zr)
+        sm.check(rc)
+        wdict[name] = q
+        del w16
+    if ws:
+        wdict["w_scale"] = ws
+    if w4s:
+        wdict["w4"] = w4s + w4z
+    if fp4g:
+        wdict["fp4g"] = fp4g
+    torch.cuda.synchronize(dev)
+
+
+def device_inputs(layer, seed: int):
+    """Seeded synthetic inputs generated on the device: x ~ N(0,1), router
+    ~ N(0,0.02) (+ the Zipf popularity bias), weights as quantise_weights."""
+    import torch
+    import sparsemoe_b200 as sm
     cfg = layer.cfg
-    if cfg.int8 or cfg.int8ch or cfg.fp8 or cfg.w4 or cfg.zipf_s > 0:
-        # quantised formats: seeded host generator + the library's host quantisers
-        import sparsemoe_b200 as sm
+    if cfg.int8:
+        # the reference's per-tensor int8 format: host generator + the host quantiser
         layer.host_inputs = sm.make_inputs(cfg, seed)
         layer.load(layer.host_inputs)
         return
     g = torch.Generator(device=layer.device)
     g.manual_seed(seed)
-    for t, std in ((layer.x, 1.0), (layer.wr, 0.02), (layer.wg, cfg.d_model ** -0.5),
-                   (layer.wu, cfg.d_model ** -0.5), (layer.wd, cfg.d_ff ** -0.5)):
-        t.normal_(0.0, std, generator=g)
+    layer.x.normal_(0.0, 1.0, generator=g)
+    layer.wr.normal_(0.0, 0.02, generator=g)
+    if cfg.zipf_s > 0:
+        layer.bias = torch.from_numpy(sm.zipf_bias(cfg.num_experts, cfg.zipf_s)).to(layer.device)
+    wd = {}
+    quantise_weights(cfg, layer.device, g, cfg.num_experts, wd)
+    for n in ("wg", "wu", "wd"):
+        getattr(layer, n).copy_(wd[n].view(getattr(layer, n).dtype))
+    if "w_scale" in wd:
+        layer.wscale = wd["w_scale"]
+    if "w4" in wd:
+        layer.w4sz = wd["w4"]
+    if "fp4g" in wd:
+        layer.fp4g = wd["fp4g"]
+    layer.host_inputs = None
+
+
+def host_inputs_from_device(layer) -> dict:
+    """The layer's device inputs as the host dict the oracle reads."""
+    import numpy as np
+    import torch
+    cfg = layer.cfg
+    u16 = lambda t: t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)  # noqa: E731
+    inp = {"x": u16(layer.x)[: cfg.T], "wr": layer.wr.cpu().numpy() if cfg.router_f32 else u16(layer.wr),
+           "bias": None if layer.bias is None else layer.bias.cpu().numpy()}
+    quant = cfg.fp8 or cfg.int8ch or cfg.w4
+    for n in ("wg", "wu", "wd"):
+        t = getattr(layer, n)
+        inp[n + ("_q" if quant else "")] = t.cpu().numpy() if quant else u16(t)
+    if cfg.channel_scaled:
+        inp["sg"], inp["su"], inp["sd"] = (t.cpu().numpy() for t in layer.wscale)
+    if cfg.nvfp4:
+        inp["wg_s"], inp["wu_s"], inp["wd_s"] = (t.cpu().numpy() for t in layer.w4sz)
+        inp["wg_g"], inp["wu_g"], inp["wd_g"] = (t.cpu().numpy() for t in layer.fp4g)
+    elif cfg.w4:
+        v = [t.cpu().numpy().view(np.uint16) for t in layer.w4sz]
+        inp["wg_s"], inp["wu_s"], inp["wd_s"], inp["wg_z"], inp["wu_z"], inp["wd_z"] = v
+    return inp
 
 
 def cpu_measure(layer, sample_tokens: int, nthreads: int):
@@ -199,6 +304,8 @@ def cpu_measure(layer, sample_tokens: int, nthreads: int):
     import torch
     from oracle import oracle as O
     cfg = layer.cfg
+    if getattr(layer, "host_inputs", None) is None and (cfg.fp8 or cfg.int8ch or cfg.w4 or cfg.zipf_s > 0):
+        layer.host_inputs = host_inputs_from_device(layer)
     if getattr(layer, "host_inputs", None) is not None:
         inp = layer.host_inputs
         t0 = time.perf_counter()
@@ -282,15 +389,24 @@ def run_ep(args, cfg, ws, rank, local, dev):
     import torch
     import torch.distributed as dist
     from sparsemoe_b200.ep import ExpertParallelLayer
-    layer = ExpertParallelLayer(cfg, dev, chunks=args.ep_chunks)
-    g = torch.Generator(device=dev)
-    g.manual_seed(1000 + rank)
-    layer.x.normal_(0.0, 1.0, generator=g)
-    g.manual_seed(7)                                   # router replicated on every rank
-    layer.wr.normal_(0.0, 0.02, generator=g)
-    g.manual_seed(2000 + rank)                         # this rank's experts
-    for t, std in ((layer.wg, cfg.d_model ** -0.5), (layer.wu, cfg.d_model ** -0.5), (layer.wd, cfg.d_ff ** -0.5)):
-        t.normal_(0.0, std, generator=g)
+    import sparsemoe_b200 as sm
+    glob = args.config in GLOBAL_BATCH
+    layer = ExpertParallelLayer(cfg, dev, chunks=args.ep_chunks, global_batch=glob)
+    if cfg.int8:
+        # the reference's per-tensor int8 format: host generator + host quantiser (all experts; each
+        # rank keeps its own), this rank's tokens
+        full = sm.make_inputs(cfg, 5)
+        layer.load({**full, "x": sm.make_inputs(cfg, 100 + rank)["x"]})
+    else:
+        g = torch.Generator(device=dev)
+        g.manual_seed(1000 + rank)
+        layer.x.normal_(0.0, 1.0, generator=g)
+        g.manual_seed(7)                                   # router replicated on every rank
+        layer.wr.normal_(0.0, 0.02, generator=g)
+        if cfg.zipf_s > 0:
+            layer.bias = torch.from_numpy(sm.zipf_bias(cfg.num_experts, cfg.zipf_s)).to(dev)
+        g.manual_seed(2000 + rank)                         # this rank's experts, quantised on the device
+        quantise_weights(cfg, dev, g, layer.e_loc, layer.weights)
     stream = torch.cuda.current_stream(dev)
     for _ in range(args.warmup):
         layer.forward(stream)
@@ -341,6 +457,8 @@ def run_ep(args, cfg, ws, rank, local, dev):
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / K, ws, dev)
     peaks, peak_src = load_peaks()
     peak_tf = float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
+    if cfg.int8 or cfg.int8ch or cfg.fp8:
+        peak_tf *= 2.0   # dense int8 / fp8 tensor rate is twice bf16 on B200
     flop_ffn = 6.0 * cfg.d_model * cfg.d_ff * statistics.mean(owner_rows)
     ach = flop_ffn / (phase_ms["expert_ffn_compute"] * 1e-3) / 1e12
     ach_min = max_over_ranks(-ach, ws, dev) * -1.0      # slowest rank
@@ -354,7 +472,9 @@ def run_ep(args, cfg, ws, rank, local, dev):
         "config": {**cfg_json(args.config, cfg, layer.cap),
                    "parallelism": f"ep{ws} (expert parallel, {cfg.num_experts // ws} experts per GPU, "
                                   f"NCCL all-to-all dispatch/return on a second stream, {layer.n_chunks} "
-                                  f"pipelined batch chunks; {cfg.T} tokens per GPU)"},
+                                  f"pipelined batch chunks; {cfg.T} tokens per GPU"
+                                  + (f"; each batch split over the {ws} ranks, global CAP {layer.cap})"
+                                     if glob else ", per-rank batches)")},
         "roofline": {"bound": "tensor", "achieved": ach_min, "peak": peak_tf, "unit": "TFLOP/s",
                      "frac": ach_min / peak_tf, "traffic": None,
                      "kernel": "expert_ffn phase (up/gate + down tcgen05 GEMMs), slowest rank",

@@ -207,6 +207,20 @@ void moe_quantize_int8_channel(const uint16_t* src, int E, int K, int N, int bf1
 void moe_quantize_nvfp4(const uint16_t* src, int E, int K, int N, int bf16, uint8_t* packed, uint8_t* scales,
                         float* globals);
 
+// Device twins of the four quantisers above (int8 per channel, FP8 blocks,
+// INT4 g128 -- declared below -- and NVFP4): same formats, bit-identical
+// outputs, for weights already in device memory; asynchronous on `stream`.
+// src must be 16-byte aligned; N a multiple of 8 (FP8: K, N multiples of 128;
+// INT4: K of 128; NVFP4: K of 16).  Return MOE_OK or an error code.
+int moe_quantize_int8_channel_device(const void* src, int E, int K, int N, int bf16, int8_t* q, float* scales,
+                                     cudaStream_t stream);
+int moe_quantize_fp8_blocks_device(const void* src, int E, int K, int N, int bf16, uint8_t* q, float* scales,
+                                   cudaStream_t stream);
+int moe_quantize_int4_g128_device(const void* src, int E, int K, int N, int bf16, uint8_t* packed,
+                                  uint16_t* scales, uint16_t* zeros, cudaStream_t stream);
+int moe_quantize_nvfp4_device(const void* src, int E, int K, int N, int bf16, uint8_t* packed, uint8_t* scales,
+                              float* globals, cudaStream_t stream);
+
 // 4-bit asymmetric group quantiser for weights [E, K, N] (16-bit, bf16 != 0:
 // bf16): per expert, column n and group of 128 along K, s = (max - min) / 15
 // (1 if max == min), z = -min / s, both rounded to fp16; q = clamp(rint(w /

@@ -156,8 +156,8 @@ void oracle_route(const uint16_t* x, const void* wr, int router_f32, const float
         for (size_t i = 0; i < (size_t)d * E; ++i) wrf[i] = to_f32(w16[i], bf16);
     }
     // capacity.cu:13-142 (router GEMM) in the fixed order the GPU router uses.
-    // E >= 64: per (token, expert) a sequential fmaf chain over j from 0.0f.
-    // E < 64:
+    // E >= 64 and a multiple of 32: per (token, expert) a sequential fmaf
+    // chain over j from 0.0f.  Otherwise:
     // lane l (0..31) accumulates, with fmaf from 0.0f, the 8-element chunks
     // c = l, l+32, ... (elements 8c..8c+7) in ascending j; the 32 partials
     // are combined by the xor butterfly p[l] = p[l] + p[l^off], off = 16..1;
@@ -168,7 +168,7 @@ void oracle_route(const uint16_t* x, const void* wr, int router_f32, const float
         for (int64_t t = blk * 64; t < std::min<int64_t>(T, blk * 64 + 64); ++t) {
             for (int j = 0; j < d; ++j) xr[j] = to_f32(x[t * d + j], bf16);
             for (int e = 0; e < E; ++e) {
-                if (E >= 64) {   // many experts: one sequential fmaf chain (GPU router_tiled_kernel)
+                if (E >= 64 && E % 32 == 0) {   // many experts: one fmaf chain (GPU router_tiled_kernel)
                     float acc = 0.0f;
                     for (int j = 0; j < d; ++j) acc = fmaf(xr[j], wrf[(size_t)j * E + e], acc);
                     logits[t * E + e] = bias ? acc + bias[e] : acc;

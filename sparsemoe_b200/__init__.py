@@ -121,6 +121,14 @@ def _load() -> ctypes.CDLL:
         "moe_quantize_fp8_blocks": (None, [_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _p, _p]),
         "moe_quantize_int8_channel": (None, [_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _p, _p]),
         "moe_quantize_nvfp4": (None, [_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _p, _p, _p]),
+        "moe_quantize_int8_channel_device": (ctypes.c_int, [_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                                             _p, _p, _p]),
+        "moe_quantize_fp8_blocks_device": (ctypes.c_int, [_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                                           _p, _p, _p]),
+        "moe_quantize_int4_g128_device": (ctypes.c_int, [_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                                          _p, _p, _p, _p]),
+        "moe_quantize_nvfp4_device": (ctypes.c_int, [_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                                      _p, _p, _p, _p]),
         "moe_fill_normal_f32": (None, [_p, ctypes.c_size_t, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_float]),
         "moe_zipf_bias": (None, [_p, ctypes.c_int, ctypes.c_float, ctypes.c_float, ctypes.c_uint64]),
     }

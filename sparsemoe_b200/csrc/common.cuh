@@ -55,4 +55,18 @@ __device__ __forceinline__ void warp_store_rows16(float4* stage, const float* v,
     __syncwarp();
 }
 
+// Packed f32x2 FMA (sm_100): a0 = fma(p0, s, a0), a1 = fma(p1, s, a1), each
+// rounded once exactly as fmaf -- one instruction for two accumulators.
+__device__ __forceinline__ void ffma2(float& a0, float& a1, float p0, float p1, float s) {
+    unsigned long long acc, pp, ss;
+    float2 av = make_float2(a0, a1), pv = make_float2(p0, p1), sv = make_float2(s, s);
+    acc = *reinterpret_cast<unsigned long long*>(&av);
+    pp = *reinterpret_cast<unsigned long long*>(&pv);
+    ss = *reinterpret_cast<unsigned long long*>(&sv);
+    asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc) : "l"(pp), "l"(ss));
+    const float2 r = *reinterpret_cast<float2*>(&acc);
+    a0 = r.x;
+    a1 = r.y;
+}
+
 }  // namespace moe

@@ -98,18 +98,6 @@ __device__ __forceinline__ void decode_tile(int t, const int* pre, const int* ro
     m = local - n * mt;
 }
 
-__device__ __forceinline__ void ffma2(float& a0, float& a1, float p0, float p1, float s) {
-    unsigned long long acc, pp, ss;
-    float2 av = make_float2(a0, a1), pv = make_float2(p0, p1), sv = make_float2(s, s);
-    acc = *reinterpret_cast<unsigned long long*>(&av);
-    pp = *reinterpret_cast<unsigned long long*>(&pv);
-    ss = *reinterpret_cast<unsigned long long*>(&sv);
-    asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc) : "l"(pp), "l"(ss));
-    const float2 r = *reinterpret_cast<float2*>(&acc);
-    a0 = r.x;
-    a1 = r.y;
-}
-
 __device__ __forceinline__ uint32_t e4m3x4(float a, float b, float c, float d) {
     const uint32_t lo = __nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3);
     const uint32_t hi = __nv_cvt_float2_to_fp8x2(make_float2(c, d), __NV_SATFINITE, __NV_E4M3);

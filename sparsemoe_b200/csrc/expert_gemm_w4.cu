@@ -67,17 +67,20 @@ struct Tile {
     static constexpr int kBBytes = 64 * BN * 2;          // bf16 B: BN/64 chunks of 64 columns x 64 K-rows
     static constexpr int kPBytes = 64 * BN / 2;          // packed nibbles
     static constexpr int kSZBytes = 4 * BN;              // INT4: BN fp16 scales + BN zeros; NVFP4: 4 x BN e4m3
-    static constexpr int kData = kABytes + kBBytes + kPBytes + kSZBytes;
-    // every stage's A and B must sit on a 1024-byte boundary (128B swizzle atoms)
-    static constexpr int kStageBytes = (kData + 1023) / 1024 * 1024;
+    // Two rings: kRaw TMA stages (A, packed weights, scales) and kBSt converted
+    // bf16 B stages.  The raw ring is the deeper one, so that small tiles
+    // (decode) keep enough loads in flight; every A and B buffer sits on a
+    // 1024-byte boundary (128B swizzle atoms).
+    static constexpr int kRawBytes = (kABytes + kPBytes + kSZBytes + 1023) / 1024 * 1024;
+    static constexpr int kRaw = kBM == 128 ? 5 : 4;
+    static constexpr int kBSt = 2;
     static constexpr int kTxBytes = kABytes + kPBytes + kSZBytes;
-    static constexpr size_t kSmemBytes = 1024 + (size_t)3 * kStageBytes + 256 + 4 * 2048;
+    static constexpr size_t kSmemBytes = 1024 + (size_t)kRaw * kRawBytes + (size_t)kBSt * kBBytes + 256 + 4 * 2048;
     static constexpr int kUnits = BN / 8;                 // converter: 8-column units
     static constexpr int kRowGroups = 256 / kUnits;       // converter threads per unit
     static constexpr int kRowsPerThread = 64 / kRowGroups;
 };
 constexpr int kBK = 64;
-constexpr int kStages = 3;
 constexpr int kThreads = 448;             // 2 + 4 epilogue + 8 converter warps
 constexpr int kConvThreads = 256;
 constexpr int kChunkBytes = 64 * 128;     // 8 KB
@@ -129,7 +132,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     using TL = Tile<kBM>;
     constexpr int kBN = TL::BN;
     constexpr int kABytes = TL::kABytes, kBBytes = TL::kBBytes, kPBytes = TL::kPBytes, kSZBytes = TL::kSZBytes;
-    constexpr int kStageBytes = TL::kStageBytes;
+    constexpr int kRaw = TL::kRaw, kBSt = TL::kBSt, kRawBytes = TL::kRawBytes;
     extern __shared__ uint8_t smem_raw[];
     __shared__ int s_pre[kMaxGroups + 1];
     __shared__ int s_mt[kMaxGroups];
@@ -138,26 +141,25 @@ __global__ void __launch_bounds__(kThreads, 1)
     __shared__ int s_wt[kMaxGroups];
 
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* stage0 = smem;  // per stage: A | B | packed | scales | zeros
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
-    uint64_t* conv = full + kStages;
-    uint64_t* empty = conv + kStages;
-    uint64_t* tfull = empty + kStages;
+    uint8_t* raw0 = smem;                                  // kRaw x [A | packed | scales (| zeros)]
+    uint8_t* bst0 = smem + kRaw * kRawBytes;               // kBSt x converted bf16 B
+    uint64_t* full = reinterpret_cast<uint64_t*>(bst0 + kBSt * kBBytes);   // raw stage loaded
+    uint64_t* empty = full + kRaw;                         // raw stage consumed (MMA done)
+    uint64_t* conv = empty + kRaw;                         // B stage converted
+    uint64_t* bfree = conv + kBSt;                         // B stage consumed (MMA done)
+    uint64_t* tfull = bfree + kBSt;
     uint64_t* tempty = tfull + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
-    float4* sStage = reinterpret_cast<float4*>(smem + kStages * kStageBytes + 256);   // 4 epilogue warps x 2 KB
-    auto sA = [&](int s) { return stage0 + s * kStageBytes; };
-    auto sB = [&](int s) { return stage0 + s * kStageBytes + kABytes; };
-    auto sP = [&](int s) { return stage0 + s * kStageBytes + kABytes + kBBytes; };
-    auto sS = [&](int s) { return stage0 + s * kStageBytes + kABytes + kBBytes + kPBytes; };
+    float4* sStage = reinterpret_cast<float4*>(bst0 + kBSt * kBBytes + 256);   // 4 epilogue warps x 2 KB
+    auto sA = [&](int s) { return raw0 + s * kRawBytes; };
+    auto sP = [&](int s) { return raw0 + s * kRawBytes + kABytes; };
+    auto sS = [&](int s) { return raw0 + s * kRawBytes + kABytes + kPBytes; };
+    auto sB = [&](int b) { return bst0 + b * kBBytes; };
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kStages; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&conv[s], kConvThreads);
-            mbar_init(&empty[s], 1);
-        }
+        for (int s = 0; s < kRaw; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+        for (int b = 0; b < kBSt; ++b) { mbar_init(&conv[b], kConvThreads); mbar_init(&bfree[b], 1); }
         for (int a = 0; a < 2; ++a) { mbar_init(&tfull[a], 1); mbar_init(&tempty[a], 128); }
         fence_mbar_init();
     }
@@ -223,25 +225,26 @@ __global__ void __launch_bounds__(kThreads, 1)
                             tma_load_2d(sS(s), &mp.s0, &full[s], n * kBN, fp4_row0 + k0 / 16);
                         }
                     }
-                    if (++s == kStages) { s = 0; ph ^= 1u; }
+                    if (++s == kRaw) { s = 0; ph ^= 1u; }
                 }
             }
         producer_done:;
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            int s = 0, acc = 0;
-            uint32_t ph = 0, aph = 0;
+            int s = 0, b = 0, acc = 0;
+            uint32_t ph = 0, bph = 0, aph = 0;
             for (int t = blockIdx.x; t < total; t += gridDim.x) {
                 if (!mbar_wait(&tempty[acc], aph ^ 1u, p.status, kDevErrTimeout)) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + acc * 256;   // kHalves x kBN columns
                 bool ok = true;
                 for (int kb = 0; kb < kblocks; ++kb) {
-                    if (!mbar_wait(&conv[s], ph, p.status, kDevErrTimeout)) { ok = false; break; }
+                    // the converter finished B[b], so raw stage s (same K step) has landed too
+                    if (!mbar_wait(&conv[b], bph, p.status, kDevErrTimeout)) { ok = false; break; }
                     tc_fence_after();
                     const uint32_t a_base = smem_u32(sA(s));
-                    const uint32_t b_base = smem_u32(sB(s));
+                    const uint32_t b_base = smem_u32(sB(b));
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk) {
                         const uint64_t bdesc = smem_desc_sw128(b_base + kk * 16 * 128, kChunkBytes, 1024);
@@ -253,7 +256,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                         }
                     }
                     mma_commit(&empty[s]);
-                    if (++s == kStages) { s = 0; ph ^= 1u; }
+                    mma_commit(&bfree[b]);
+                    if (++s == kRaw) { s = 0; ph ^= 1u; }
+                    if (++b == kBSt) { b = 0; bph ^= 1u; }
                 }
                 if (!ok) break;
                 mma_commit(&tfull[acc]);
@@ -348,14 +353,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int krow0 = up_unit ? (rg ^ (32 / kU)) : rg;
         const int p_base = up_unit ? kPBytes / 2 : 0;
         const __nv_bfloat162 k128 = __floats2bfloat162_rn(128.0f, 128.0f);
-        int s = 0;
-        uint32_t ph = 0;
+        int s = 0, b = 0;
+        uint32_t ph = 0, bph = 0;
         bool ok = true;
         for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
             for (int kb = 0; kb < kblocks; ++kb) {
-                if (!mbar_wait(&full[s], ph, p.status, kDevErrTimeout)) { ok = false; break; }
+                if (!mbar_wait(&full[s], ph, p.status, kDevErrTimeout) ||
+                    !mbar_wait(&bfree[b], bph ^ 1u, p.status, kDevErrTimeout)) {
+                    ok = false;
+                    break;
+                }
                 const uint8_t* src = sP(s) + p_base;
-                uint8_t* dst = sB(s) + chunk * kChunkBytes;
+                uint8_t* dst = sB(b) + chunk * kChunkBytes;
                 if (kFmt == 0) {
                     __nv_bfloat162 sc[4], cc[4];
                     {
@@ -424,8 +433,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
                 fence_proxy_async_smem();
-                mbar_arrive(&conv[s]);
-                if (++s == kStages) { s = 0; ph ^= 1u; }
+                mbar_arrive(&conv[b]);
+                if (++s == kRaw) { s = 0; ph ^= 1u; }
+                if (++b == kBSt) { b = 0; bph ^= 1u; }
             }
         }
     }

@@ -76,12 +76,16 @@ size_t scale_bytes(const Shape& s, int dim) {
     return 0;
 }
 
+size_t router_scratch_bytes(const Shape& s) {
+    return router_sliced(s) ? align256(sizeof(float) * (size_t)s.T() * s.E) : 0;
+}
+
 size_t workspace_bytes(const Shape& s) {
     const size_t routes = (size_t)s.T() * s.k;
     const size_t chunk_tab = (size_t)s.B * s.chunks() * s.E;
     return workspace_header_bytes() + align256(sizeof(int) * routes) + 2 * align256(sizeof(int) * chunk_tab) +
            align256(sizeof(int) * (size_t)s.B * s.E) + 2 * align256(sizeof(int) * s.E) + scale_bytes(s, s.d) +
-           scale_bytes(s, s.f);
+           scale_bytes(s, s.f) + router_scratch_bytes(s);
 }
 
 void carve_workspace(void* base, const Shape& s, Workspace* ws) {
@@ -101,6 +105,8 @@ void carve_workspace(void* base, const Shape& s, Workspace* ws) {
     ws->a_scale = scale_bytes(s, s.d) ? reinterpret_cast<float*>(p) : nullptr;
     p += scale_bytes(s, s.d);
     ws->h_scale = scale_bytes(s, s.f) ? reinterpret_cast<float*>(p) : nullptr;
+    p += scale_bytes(s, s.f);
+    ws->router_logits = router_scratch_bytes(s) ? reinterpret_cast<float*>(p) : nullptr;
 }
 
 namespace {
@@ -391,7 +397,7 @@ cudaError_t mark_stage(int i, cudaStream_t stream) {
 
 // Stages 1-3: router + top-k, slots, gather into the dense expert-major rows.
 int enqueue_route(const MoEArgs* a, const MoeDims* dims, const Shape& s, const Workspace& ws, cudaStream_t stream) {
-    MOE_TRY(launch_router_topk(a->input, a->router_weights, dims->router_bias, s, a->expert_logits,
+    MOE_TRY(launch_router_topk(a->input, a->router_weights, dims->router_bias, s, ws.router_logits, a->expert_logits,
                                a->selected_expert_indices, a->selected_expert_weights, stream),
             "router_topk");
     MOE_TRY(mark_stage(1, stream), "cudaEventRecord(stage event)");
@@ -534,7 +540,7 @@ extern "C" int moe_stage_route_counts(const MoEArgs* a, const MoeDims* dims, int
     if (rc != MOE_OK) return rc;
     if (!raw_counts) { set_error("moe_stage_route_counts: raw_counts is null"); return MOE_ERR_INVALID_ARG; }
     MOE_TRY(cudaMemsetAsync(ws.status, 0, sizeof(int), stream), "cudaMemsetAsync(status)");
-    MOE_TRY(launch_router_topk(a->input, a->router_weights, dims->router_bias, s, a->expert_logits,
+    MOE_TRY(launch_router_topk(a->input, a->router_weights, dims->router_bias, s, ws.router_logits, a->expert_logits,
                                a->selected_expert_indices, a->selected_expert_weights, stream),
             "router_topk");
     MOE_TRY(launch_dispatch_count(a->selected_expert_indices, s, ws, a->expert_counts, raw_counts, stream),

@@ -14,6 +14,9 @@ constexpr int kChunkRoutes = 1024;
 // Experts from which the router switches to its register-tiled kernel and
 // the sequential-j logit order (the oracle follows the same rule).
 constexpr int kRouterTiledMinExperts = 64;
+// Below this many tokens, many-expert routers split the experts over CTAs
+// (logits, then a separate top-k pass) so that small batches fill the GPU.
+constexpr int64_t kRouterSliceMaxT = 2048;
 
 // Error codes the kernels write to the device status word.
 constexpr int kDevErrTimeout = 1;
@@ -48,6 +51,7 @@ struct Workspace {
     int* expert_start;  // [E]       first row of expert e: exclusive prefix of expert_rows
     float* a_scale;     // FP8: [E*B*CAP, d/128] activation block scales; INT8_CHANNEL: [E*B*CAP] row scales
     float* h_scale;     // FP8 / INT8_CHANNEL: [E*B*CAP, f/128] h block scales
+    float* router_logits;  // [T, E] logits of the sliced router (router_sliced) when args carry none
 };
 size_t workspace_header_bytes();
 
@@ -70,7 +74,10 @@ struct GemmScales {
 };
 
 // router.cu: logits (+bias), warp-shuffle top-k, softmax.
+// True when the router runs expert-sliced (E >= 64, E % 32 == 0, T < kRouterSliceMaxT).
+bool router_sliced(const Shape& s);
 cudaError_t launch_router_topk(const void* x, const void* wr, const float* bias, const Shape& s,
+                               float* logits_scratch,
                                float* logits, int* idx, float* w, cudaStream_t st);
 // dispatch.cu: deterministic capacity slots + 16-byte row gather.
 // a_rows receives 16-bit rows, or int8 rows quantised with 1/s_in (int8 path).

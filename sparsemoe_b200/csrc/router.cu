@@ -3,13 +3,14 @@
 // Reference semantics: kernels/capacity.cu:13-142 (router GEMM, fp32 result)
 // and :171-238 (top_k_gating).  Differences by design:
 //  * logits use a fixed fp32 order (the reference's WMMA order is
-//    unspecified) that the CPU oracle reproduces bit for bit.  For E < 64:
+//    unspecified) that the CPU oracle reproduces bit for bit.  For E < 64 (or
+//    E not a multiple of 32):
 //      lane l (0..31) owns the 8-element chunks c = l, l+32, l+64, ... of the
 //      d-dimension (elements 8c..8c+7) and accumulates them in ascending j
 //      with fmaf, starting at 0.0f;  the 32 partial sums are then combined by
 //      an xor butterfly  p[l] = p[l] + p[l ^ off]  for off = 16, 8, 4, 2, 1;
 //      logit = p[0] (+ bias[e], one rounded add);
-//    for E >= 64 (router_tiled_kernel): one sequential fmaf chain over
+//    for E >= 64 and a multiple of 32 (router_tiled_kernel): one sequential fmaf chain over
 //    j = 0..d-1 from 0.0f per (token, expert), then + bias[e];
 //  * top-k is a k-round warp argmax over (value desc, index asc), the same
 //    selection as the reference's insertion sort with strict '>' (ties go to
@@ -172,7 +173,7 @@ __global__ void __launch_bounds__(kWarps * 32) router_topk_kernel(
     }
 }
 
-// Many experts (E >= kTiledMinExperts): a register-tiled CUDA-core GEMM.  The
+// Many experts (E >= kRouterTiledMinExperts, E % 32 == 0): a register-tiled CUDA-core GEMM.  The
 // f32 order is then per (token, expert) one sequential fmaf chain over
 // j = 0..d-1 from 0.0f (+ bias[e]), which the oracle mirrors.  CTA = 16*MT
 // tokens x all E experts, 2E threads; thread (r, c) owns tokens MT*r.. and
@@ -181,9 +182,9 @@ __global__ void __launch_bounds__(kWarps * 32) router_topk_kernel(
 // double-buffered: the next slice is loaded into registers during the FMAs.
 constexpr int kTiledKC = 32;
 
-// 2E threads: up to 512 (E = 256) with MT = 4; MT = 8 needs ~150 registers,
-// so it runs only for E <= 128 (<= 256 threads).
-template <typename TX, typename TW, int MT>   // MT tokens per thread (8, or 4 for small grids / E > 128)
+// 2E threads: up to 512 (E = 256) with MT = 4 tokens per thread (the only
+// size launched: MT = 8 halves the CTAs per SM through its register need).
+template <typename TX, typename TW, int MT>
 __global__ void __launch_bounds__(MT == 8 ? 256 : 512) router_tiled_kernel(
     const TX* __restrict__ x, const TW* __restrict__ wr, const float* __restrict__ bias, int64_t T, int d, int E,
     int k, float* __restrict__ logits, int* __restrict__ idx, float* __restrict__ wts) {
@@ -195,7 +196,11 @@ __global__ void __launch_bounds__(MT == 8 ? 256 : 512) router_tiled_kernel(
     float* lg = ws;                              // after the K loop: [kTiledTM][E]
     const int nthr = blockDim.x;
     const int cgroups = E / 8;
-    const int r = threadIdx.x / cgroups, c = threadIdx.x - (threadIdx.x / cgroups) * cgroups;
+    // a warp covers 8 token rows x 4 expert groups, so its shared-memory
+    // loads touch 8 x-rows (256 B) and 4 router groups (128 B) per K step
+    const int warp_id = threadIdx.x >> 5, lane_id = threadIdx.x & 31;
+    const int wpr = cgroups / 4;   // warps per 8-row block
+    const int r = (warp_id / wpr) * 8 + (lane_id & 7), c = (warp_id % wpr) * 4 + (lane_id >> 3);
     const int64_t t0 = (int64_t)blockIdx.x * kTiledTM;
     float acc[MT][8];
 #pragma unroll
@@ -274,7 +279,7 @@ __global__ void __launch_bounds__(MT == 8 ? 256 : 512) router_tiled_kernel(
 #pragma unroll
             for (int i = 0; i < MT; ++i)
 #pragma unroll
-                for (int e = 0; e < 8; ++e) acc[i][e] = fmaf(xv[i], wv[e], acc[i][e]);
+                for (int e = 0; e < 8; e += 2) ffma2(acc[i][e], acc[i][e + 1], wv[e], wv[e + 1], xv[i]);
         }
         if (sl + 1 < nslices) store_slice(buf ^ 1);
         __syncthreads();
@@ -296,6 +301,122 @@ __global__ void __launch_bounds__(MT == 8 ? 256 : 512) router_tiled_kernel(
             for (int e = lane; e < E; e += 32) logits[t * E + e] = row[e];
         topk_softmax_warp(row, E, k, t, idx, wts, lane);
     }
+}
+
+// Few tokens, many experts (router_sliced): CTA = 16 tokens x 32 experts,
+// 64 threads, thread (r, c) = token r, experts 8c..8c+7 of the slice; x and
+// Wr K-slices of 128 double-buffered in shared memory.  Same per-(token,
+// expert) order as router_tiled_kernel (one fmaf chain over j from 0.0f,
+// then + bias); logits go to global memory and topk_rows_kernel selects.
+constexpr int kSliceTM = 16, kSliceEC = 32, kSliceKC = 128, kSliceThreads = 64;
+constexpr size_t kSliceSmem = sizeof(float) * 2 * kSliceKC * (kSliceTM + kSliceEC);
+
+template <typename TX, typename TW>
+__global__ void __launch_bounds__(kSliceThreads) router_slice_kernel(
+    const TX* __restrict__ x, const TW* __restrict__ wr, const float* __restrict__ bias, int64_t T, int d, int E,
+    float* __restrict__ logits) {
+    extern __shared__ float sm[];
+    float* xs = sm;                               // [2][KC][TM]
+    float* ws = xs + 2 * kSliceKC * kSliceTM;     // [2][KC][EC]
+    const int r = threadIdx.x >> 2, c = threadIdx.x & 3;
+    const int64_t t0 = (int64_t)blockIdx.x * kSliceTM;
+    const int e0 = blockIdx.y * kSliceEC;
+    constexpr int kXV = kSliceTM * (kSliceKC / 8) / kSliceThreads;   // 4 x vectors per thread
+    constexpr int kWV = kSliceKC * (kSliceEC / 8) / kSliceThreads;   // 8 router 8-vectors per thread
+    uint4 xr[kXV];
+    float wreg[kWV][8];
+    auto load_slice = [&](int j0) {
+#pragma unroll
+        for (int v = 0; v < kXV; ++v) {
+            const int vi = threadIdx.x + v * kSliceThreads;
+            const int tt = vi / (kSliceKC / 8), jv = vi - tt * (kSliceKC / 8);
+            const int64_t t = t0 + tt;
+            xr[v] = t < T ? __ldg(reinterpret_cast<const uint4*>(x + t * d + j0 + jv * 8)) : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int v = 0; v < kWV; ++v) {
+            const int vi = threadIdx.x + v * kSliceThreads;
+            const int jj = vi >> 2, cc = vi & 3;
+            load_wr8(wr + (int64_t)(j0 + jj) * E + e0 + 8 * cc, wreg[v]);
+        }
+    };
+    auto store_slice = [&](int buf) {
+        float* xb = xs + buf * kSliceKC * kSliceTM;
+        float* wb = ws + buf * kSliceKC * kSliceEC;
+#pragma unroll
+        for (int v = 0; v < kXV; ++v) {
+            const int vi = threadIdx.x + v * kSliceThreads;
+            const int tt = vi / (kSliceKC / 8), jv = vi - tt * (kSliceKC / 8);
+            const uint32_t* u = reinterpret_cast<const uint32_t*>(&xr[v]);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const float2 p = F16Traits<TX>::unpack2(u[q]);
+                xb[(jv * 8 + 2 * q) * kSliceTM + tt] = p.x;
+                xb[(jv * 8 + 2 * q + 1) * kSliceTM + tt] = p.y;
+            }
+        }
+#pragma unroll
+        for (int v = 0; v < kWV; ++v) {
+            const int vi = threadIdx.x + v * kSliceThreads;
+            const int jj = vi >> 2, cc = vi & 3;
+            float4* dst = reinterpret_cast<float4*>(wb + jj * kSliceEC + 8 * cc);
+            dst[0] = make_float4(wreg[v][0], wreg[v][1], wreg[v][2], wreg[v][3]);
+            dst[1] = make_float4(wreg[v][4], wreg[v][5], wreg[v][6], wreg[v][7]);
+        }
+    };
+    float acc[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] = 0.0f;
+    const int nslices = d / kSliceKC;   // d % 256 == 0
+    load_slice(0);
+    store_slice(0);
+    __syncthreads();
+    for (int sl = 0; sl < nslices; ++sl) {
+        const int buf = sl & 1;
+        if (sl + 1 < nslices) load_slice((sl + 1) * kSliceKC);
+        const float* xb = xs + buf * kSliceKC * kSliceTM;
+        const float* wb = ws + buf * kSliceKC * kSliceEC;
+#pragma unroll 8
+        for (int jj = 0; jj < kSliceKC; ++jj) {
+            const float4 wa = *reinterpret_cast<const float4*>(wb + jj * kSliceEC + 8 * c);
+            const float4 wc = *reinterpret_cast<const float4*>(wb + jj * kSliceEC + 8 * c + 4);
+            const float xv = xb[jj * kSliceTM + r];
+            ffma2(acc[0], acc[1], wa.x, wa.y, xv);
+            ffma2(acc[2], acc[3], wa.z, wa.w, xv);
+            ffma2(acc[4], acc[5], wc.x, wc.y, xv);
+            ffma2(acc[6], acc[7], wc.z, wc.w, xv);
+        }
+        if (sl + 1 < nslices) store_slice(buf ^ 1);
+        __syncthreads();
+    }
+    const int64_t t = t0 + r;
+    if (t < T) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            const int ee = e0 + 8 * c + e;
+            logits[t * E + ee] = bias ? __fadd_rn(acc[e], bias[ee]) : acc[e];
+        }
+    }
+}
+
+// One warp per token: top-k + softmax over a logits row in global memory.
+__global__ void __launch_bounds__(256) topk_rows_kernel(const float* __restrict__ logits, int64_t T, int E, int k,
+                                                       int* __restrict__ idx, float* __restrict__ wts) {
+    const int64_t t = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (t >= T) return;
+    topk_softmax_warp(logits + t * E, E, k, t, idx, wts, threadIdx.x & 31);
+}
+
+template <typename TX, typename TW>
+cudaError_t launch_sliced(const void* x, const void* wr, const float* bias, const Shape& s, float* logits, int* idx,
+                          float* w, cudaStream_t st) {
+    auto kern = router_slice_kernel<TX, TW>;
+    cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSliceSmem);
+    if (err != cudaSuccess) return err;
+    const dim3 grid((unsigned)((s.T() + kSliceTM - 1) / kSliceTM), s.E / kSliceEC);
+    kern<<<grid, kSliceThreads, kSliceSmem, st>>>((const TX*)x, (const TW*)wr, bias, s.T(), s.d, s.E, logits);
+    topk_rows_kernel<<<(unsigned)((s.T() + 7) / 8), 256, 0, st>>>(logits, s.T(), s.E, s.k, idx, w);
+    return cudaGetLastError();
 }
 
 template <typename TX, typename TW, int TT>
@@ -343,26 +464,30 @@ cudaError_t launch_tiled(const void* x, const void* wr, const float* bias, const
 }
 
 template <typename TX, typename TW>
-cudaError_t launch_any(const void* x, const void* wr, const float* bias, const Shape& s, float* logits, int* idx,
-                       float* w, cudaStream_t st) {
-    if (s.E < kRouterTiledMinExperts) return launch_typed<TX, TW>(x, wr, bias, s, logits, idx, w, st);
-    // less than one CTA of 128 tokens per SM: halve the tokens per thread
-    return s.T() >= (int64_t)128 * 148 && s.E <= 128 ? launch_tiled<TX, TW, 8>(x, wr, bias, s, logits, idx, w, st)
-                                       : launch_tiled<TX, TW, 4>(x, wr, bias, s, logits, idx, w, st);
+cudaError_t launch_any(const void* x, const void* wr, const float* bias, const Shape& s, float* logits,
+                       float* logits_scratch, int* idx, float* w, cudaStream_t st) {
+    if (s.E < kRouterTiledMinExperts || s.E % 32 != 0) return launch_typed<TX, TW>(x, wr, bias, s, logits, idx, w, st);
+    if (router_sliced(s))
+        return launch_sliced<TX, TW>(x, wr, bias, s, logits ? logits : logits_scratch, idx, w, st);
+    return launch_tiled<TX, TW, 4>(x, wr, bias, s, logits, idx, w, st);
 }
 
 }  // namespace
 
+bool router_sliced(const Shape& s) {
+    return s.E >= kRouterTiledMinExperts && s.E % 32 == 0 && s.T() < kRouterSliceMaxT;
+}
+
 cudaError_t launch_router_topk(const void* x, const void* wr, const float* bias, const Shape& s,
-                               float* logits, int* idx, float* w, cudaStream_t st) {
+                               float* logits_scratch, float* logits, int* idx, float* w, cudaStream_t st) {
     if (s.T() == 0) return cudaSuccess;
     const bool bf = s.act_bf16;
     if (s.router_dtype == MOE_ROUTER_F32) {
-        return bf ? launch_any<__nv_bfloat16, float>(x, wr, bias, s, logits, idx, w, st)
-                  : launch_any<__half, float>(x, wr, bias, s, logits, idx, w, st);
+        return bf ? launch_any<__nv_bfloat16, float>(x, wr, bias, s, logits, logits_scratch, idx, w, st)
+                  : launch_any<__half, float>(x, wr, bias, s, logits, logits_scratch, idx, w, st);
     }
-    return bf ? launch_any<__nv_bfloat16, __nv_bfloat16>(x, wr, bias, s, logits, idx, w, st)
-              : launch_any<__half, __half>(x, wr, bias, s, logits, idx, w, st);
+    return bf ? launch_any<__nv_bfloat16, __nv_bfloat16>(x, wr, bias, s, logits, logits_scratch, idx, w, st)
+              : launch_any<__half, __half>(x, wr, bias, s, logits, logits_scratch, idx, w, st);
 }
 
 }  // namespace moe
