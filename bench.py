@@ -81,6 +81,22 @@ def workload(name: str):
     return table[name]
 
 
+def profiled_traffic(config: str):
+    """DRAM bytes of one up/gate launch for this workload from the ncu table in
+    profiles/traffic.md (None when no capture exists)."""
+    tf = ROOT / "profiles" / "traffic.md"
+    if not tf.exists():
+        return None
+    for line in tf.read_text().splitlines():
+        cells = [c.strip() for c in line.strip().strip("|").split("|")]
+        if len(cells) >= 3 and cells[0] == config:
+            try:
+                return float(cells[2])
+            except ValueError:
+                return None
+    return None
+
+
 def load_peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -594,14 +610,7 @@ def main():
     flop_router = 2.0 * cfg.T * d * cfg.num_experts
     ach_up = flop_up / (stage_ms["expert_up_gate_gemm"] * 1e-3) / 1e12
     ach_down = flop_down / (stage_ms["expert_down_gemm"] * 1e-3) / 1e12
-    traffic = None
-    tf = ROOT / "profiles" / "traffic.json"
-    if tf.exists():
-        try:
-            t = json.loads(tf.read_text()).get(args.config, {}).get("expert_up_gate_gemm")
-            traffic = None if t is None else float(t)
-        except Exception:
-            traffic = None
+    traffic = profiled_traffic(args.config)
 
     result = {
         "metric": f"MoE-layer tokens/s ({args.config})", "value": ws * cfg.T / (ms * 1e-3),

@@ -328,8 +328,10 @@ __global__ void __launch_bounds__(kSliceThreads) router_slice_kernel(
     auto load_slice = [&](int j0) {
 #pragma unroll
         for (int v = 0; v < kXV; ++v) {
+            // consecutive lanes take consecutive tokens, so the transposed
+            // shared-memory stores below hit distinct banks
             const int vi = threadIdx.x + v * kSliceThreads;
-            const int tt = vi / (kSliceKC / 8), jv = vi - tt * (kSliceKC / 8);
+            const int tt = vi % kSliceTM, jv = vi / kSliceTM;
             const int64_t t = t0 + tt;
             xr[v] = t < T ? __ldg(reinterpret_cast<const uint4*>(x + t * d + j0 + jv * 8)) : make_uint4(0, 0, 0, 0);
         }
@@ -346,7 +348,7 @@ __global__ void __launch_bounds__(kSliceThreads) router_slice_kernel(
 #pragma unroll
         for (int v = 0; v < kXV; ++v) {
             const int vi = threadIdx.x + v * kSliceThreads;
-            const int tt = vi / (kSliceKC / 8), jv = vi - tt * (kSliceKC / 8);
+            const int tt = vi % kSliceTM, jv = vi / kSliceTM;
             const uint32_t* u = reinterpret_cast<const uint32_t*>(&xr[v]);
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
