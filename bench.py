@@ -32,7 +32,12 @@ sys.path.insert(0, str(ROOT))
 
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 STAGES = ["router_topk", "dispatch", "expert_up_gate_gemm", "expert_down_gemm", "combine"]
-KERNELS_PER_STEP = 8   # router_topk, dispatch x4 (count, scan, assign, gather), up/gate GEMM, down GEMM, combine
+def kernels_per_step(cfg) -> int:
+    """Kernels one layer call launches: router (+ a top-k pass when the
+    many-expert router runs expert-sliced, T < 2048), dispatch x4 (count, scan,
+    assign, gather), up/gate GEMM, down GEMM, combine."""
+    sliced = cfg.num_experts >= 64 and cfg.num_experts % 32 == 0 and cfg.T < 2048
+    return 8 + (1 if sliced else 0)
 
 
 # workloads whose batches are split over the ranks under expert parallelism (global CAP)
@@ -499,7 +504,7 @@ def run_ep(args, cfg, ws, rank, local, dev):
         "e2e": {"value": ws * cfg.T / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
                 "path": "ExpertParallelLayer.forward (moe_stage_route / moe_stage_expert_ffn / moe_stage_combine)"},
-        "gpu_launches": KERNELS_PER_STEP * K,
+        "gpu_launches": kernels_per_step(cfg) * K,
         "clocks": clocks.summary(),
     }
     if rank == 0:
@@ -517,6 +522,8 @@ def main():
     ap.add_argument("--cpu-sample-tokens", type=int, default=1024)
     ap.add_argument("--ref-sample-tokens", type=int, default=128)
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline measurement")
+    ap.add_argument("--graph", action="store_true",
+                    help="also time the layer captured as one CUDA graph (the decode path)")
     ap.add_argument("--parallel", default="auto", choices=["auto", "ep", "replicas"],
                     help="N>1: expert parallelism over NCCL (default) or independent replicas")
     ap.add_argument("--ep-chunks", type=int, default=1, help="pipelined batch chunks in EP mode")
@@ -597,6 +604,34 @@ def main():
     barrier(ws)
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / K, ws, dev)
 
+    # ---- optional: the layer as one CUDA graph (decode path) ----------------
+    graph = None
+    if args.graph:
+        gstream = torch.cuda.Stream(dev)
+        layer.capture(gstream)
+        with torch.cuda.stream(gstream):
+            for _ in range(args.warmup):
+                layer.replay()
+            torch.cuda.synchronize(dev)
+            g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            g0.record(gstream)
+            for _ in range(K):
+                layer.replay()
+            g1.record(gstream)
+            torch.cuda.synchronize(dev)
+            gms = max_over_ranks(g0.elapsed_time(g1) / K, ws, dev)
+            t0 = time.perf_counter()
+            for _ in range(K):
+                layer.x.copy_(x_host, non_blocking=True)
+                layer.replay()
+                out_host.copy_(layer.out16, non_blocking=True)
+            torch.cuda.synchronize(dev)
+            gwall = (time.perf_counter() - t0) * 1e3 / K
+        graph = {"ms_per_step": gms, "value": ws * cfg.T / (gms * 1e-3), "unit": "tokens/s",
+                 "e2e_wall_ms_per_step": gwall,
+                 "path": "MoeLayer.capture -> CUDAGraph.replay (one launch per layer)"}
+        layer.sync_check(gstream)
+
     # ---- roofline of the dominant kernel (up/gate GEMM with fused SwiGLU) --
     peaks, peak_src = load_peaks()
     peak_tf = float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
@@ -631,9 +666,11 @@ def main():
         "e2e": {"value": ws * cfg.T / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
                 "path": "MoeLayer.forward -> moe_solve_v2, pinned host x in, 16-bit output out"},
-        "gpu_launches": KERNELS_PER_STEP * K,
+        "gpu_launches": kernels_per_step(cfg) * K,
         "clocks": clocks.summary(),
     }
+    if graph is not None:
+        result["graph"] = graph
     if rank == 0 and ws == 1 and not args.no_cpu:
         nthreads = os.cpu_count() or 1
         v, t_route, t_ffn, S = cpu_measure(layer, args.cpu_sample_tokens, nthreads)

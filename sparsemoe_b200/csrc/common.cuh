@@ -5,6 +5,8 @@
 #include <cuda_bf16.h>
 #include <cstdint>
 
+#include <atomic>
+
 namespace moe {
 
 template <typename T> struct F16Traits;
@@ -67,6 +69,28 @@ __device__ __forceinline__ void ffma2(float& a0, float& a1, float p0, float p1, 
     const float2 r = *reinterpret_cast<float2*>(&acc);
     a0 = r.x;
     a1 = r.y;
+}
+
+// Raises a kernel's dynamic shared-memory limit once per device (again only
+// when a launch needs more), so that launches recorded inside a CUDA-graph
+// capture make no attribute call.  One SmemAttr per kernel instantiation.
+struct SmemAttr {
+    std::atomic<int> bytes[64];
+};
+template <typename Kernel>
+inline cudaError_t ensure_smem(Kernel kern, size_t bytes, SmemAttr& a) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    std::atomic<int>& have = a.bytes[dev & 63];
+    if (have.load(std::memory_order_acquire) >= (int)bytes) return cudaSuccess;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    if (e == cudaSuccess) {
+        int cur = have.load();
+        while (cur < (int)bytes && !have.compare_exchange_weak(cur, (int)bytes)) {
+        }
+    }
+    return e;
 }
 
 }  // namespace moe

@@ -391,7 +391,8 @@ template <int kMode, class Fmt>
 cudaError_t launch_gemm(const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& b1,
                         const GemmParams& p, cudaStream_t st, int num_sms) {
     auto kern = expert_gemm_kernel<kMode, Fmt>;
-    cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+    static SmemAttr attr;
+    cudaError_t err = ensure_smem(kern, kSmemBytes, attr);
     if (err != cudaSuccess) return err;
     kern<<<num_sms, kThreads, kSmemBytes, st>>>(a, b0, b1, p);
     return cudaGetLastError();

@@ -385,7 +385,8 @@ template <int kMode, int kKind>
 cudaError_t launch(const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& b1, const Fp8Params& p,
                    cudaStream_t st, int num_sms) {
     auto kern = fp8_gemm_kernel<kMode, kKind>;
-    cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+    static SmemAttr attr;
+    cudaError_t err = ensure_smem(kern, kSmemBytes, attr);
     if (err != cudaSuccess) return err;
     kern<<<num_sms, kThreads, kSmemBytes, st>>>(a, b0, b1, p);
     return cudaGetLastError();

@@ -450,7 +450,8 @@ template <int kMode, int kFmt, int kBM>
 cudaError_t launch_bm(const W4Maps& mp, const W4Params& p, cudaStream_t st, int num_sms) {
     auto kern = w4_gemm_kernel<kMode, kFmt, kBM>;
     constexpr size_t smem = Tile<kBM>::kSmemBytes;
-    cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    static SmemAttr attr;
+    cudaError_t err = ensure_smem(kern, smem, attr);
     if (err != cudaSuccess) return err;
     kern<<<num_sms, kThreads, smem, st>>>(mp, p);
     return cudaGetLastError();

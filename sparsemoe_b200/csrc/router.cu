@@ -413,7 +413,8 @@ template <typename TX, typename TW>
 cudaError_t launch_sliced(const void* x, const void* wr, const float* bias, const Shape& s, float* logits, int* idx,
                           float* w, cudaStream_t st) {
     auto kern = router_slice_kernel<TX, TW>;
-    cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSliceSmem);
+    static SmemAttr attr;
+    cudaError_t err = ensure_smem(kern, kSliceSmem, attr);
     if (err != cudaSuccess) return err;
     const dim3 grid((unsigned)((s.T() + kSliceTM - 1) / kSliceTM), s.E / kSliceEC);
     kern<<<grid, kSliceThreads, kSliceSmem, st>>>((const TX*)x, (const TW*)wr, bias, s.T(), s.d, s.E, logits);
@@ -427,7 +428,8 @@ cudaError_t launch_items(const void* x, const void* wr, const float* bias, const
     const size_t smem = sizeof(float) * (size_t)CT * s.E;
     const int64_t blocks = (s.T() + CT - 1) / CT;
     auto kern = router_topk_kernel<TX, TW, TT>;
-    cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    static SmemAttr attr;
+    cudaError_t err = ensure_smem(kern, smem, attr);
     if (err != cudaSuccess) return err;
     kern<<<(unsigned)blocks, kWarps * 32, smem, st>>>((const TX*)x, (const TW*)wr, bias, s.T(), s.d, s.E, s.k, CT,
                                                       logits, idx, w);
@@ -457,7 +459,8 @@ cudaError_t launch_tiled(const void* x, const void* wr, const float* bias, const
     const size_t smem =
         sizeof(float) * (2 * (size_t)kTiledKC * kTiledTM + (size_t)std::max(2 * kTiledKC, kTiledTM) * s.E);
     auto kern = router_tiled_kernel<TX, TW, MT>;
-    cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    static SmemAttr attr;
+    cudaError_t err = ensure_smem(kern, smem, attr);
     if (err != cudaSuccess) return err;
     const int64_t blocks = (s.T() + kTiledTM - 1) / kTiledTM;
     kern<<<(unsigned)blocks, threads, smem, st>>>((const TX*)x, (const TW*)wr, bias, s.T(), s.d, s.E, s.k, logits,

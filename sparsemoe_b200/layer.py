@@ -158,6 +158,28 @@ class MoeLayer:
         check(lib.moe_solve_v2(ctypes.byref(a), ctypes.byref(dm), ctypes.c_void_p(s.cuda_stream)))
         return self.out
 
+    def capture(self, stream: torch.cuda.Stream | None = None) -> "torch.cuda.CUDAGraph":
+        """Records one forward() into a CUDA graph (the decode path: a replay
+        costs one launch instead of the layer's ~10 kernel launches, tensor-map
+        encodes and ctypes calls).  One eager call first sets up the library
+        scratch and the kernels' attributes outside the capture.  The graph
+        reads x and the weights from this layer's buffers, so new tokens are
+        copied into `self.x` before each replay()."""
+        s = stream if stream is not None else torch.cuda.Stream(self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        self.forward(s)
+        s.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            self.forward(s)
+        self.graph = g
+        return g
+
+    def replay(self) -> torch.Tensor:
+        """Replays the captured layer on the stream it was captured on."""
+        self.graph.replay()
+        return self.out
+
     def sync_check(self, stream: torch.cuda.Stream | None = None) -> None:
         s = stream if stream is not None else torch.cuda.current_stream(self.device)
         check(lib.moe_check_device_status(ctypes.c_void_p(s.cuda_stream)))
