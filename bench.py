@@ -412,7 +412,7 @@ def run_ep(args, cfg, ws, rank, local, dev):
     from sparsemoe_b200.ep import ExpertParallelLayer
     import sparsemoe_b200 as sm
     glob = args.config in GLOBAL_BATCH
-    layer = ExpertParallelLayer(cfg, dev, chunks=args.ep_chunks, global_batch=glob)
+    layer = ExpertParallelLayer(cfg, dev, chunks=args.ep_chunks, global_batch=glob, transport=args.ep_transport)
     if cfg.int8:
         # the reference's per-tensor int8 format: host generator + host quantiser (all experts; each
         # rank keeps its own), this rank's tokens
@@ -492,14 +492,18 @@ def run_ep(args, cfg, ws, rank, local, dev):
         "data": "synthetic (seeded torch normal: x N(0,1), router N(0,0.02), W N(0,1/sqrt(fan_in)))",
         "config": {**cfg_json(args.config, cfg, layer.cap),
                    "parallelism": f"ep{ws} (expert parallel, {cfg.num_experts // ws} experts per GPU, "
-                                  f"NCCL all-to-all dispatch/return on a second stream, {layer.n_chunks} "
-                                  f"pipelined batch chunks; {cfg.T} tokens per GPU"
+                                  + ("rows over NVLink peer memory: copy-engine dispatch, down-GEMM epilogue "
+                                     "stores the results into the senders' buffers; "
+                                     if layer.transport == "peer" else
+                                     f"NCCL all-to-all dispatch/return on a second stream, {layer.n_chunks} "
+                                     f"pipelined batch chunks; ")
+                                  + f"{cfg.T} tokens per GPU"
                                   + (f"; each batch split over the {ws} ranks, global CAP {layer.cap})"
                                      if glob else ", per-rank batches)")},
         "roofline": {"bound": "tensor", "achieved": ach_min, "peak": peak_tf, "unit": "TFLOP/s",
                      "frac": ach_min / peak_tf, "traffic": None,
                      "kernel": "expert_ffn phase (up/gate + down tcgen05 GEMMs), slowest rank",
-                     "peak_source": f"{peak_src} bf16_tflops_sustained"},
+                     "peak_source": f"{peak_src} bf16_tflops_sustained" + (" x 2 (8-bit)" if cfg.int8 or cfg.int8ch or cfg.fp8 else "")},
         "phases_ms": phase_ms,
         "e2e": {"value": ws * cfg.T / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
@@ -509,6 +513,7 @@ def run_ep(args, cfg, ws, rank, local, dev):
     }
     if rank == 0:
         print(json.dumps(result))
+    layer.close()
     dist.destroy_process_group()
 
 
@@ -527,6 +532,8 @@ def main():
     ap.add_argument("--parallel", default="auto", choices=["auto", "ep", "replicas"],
                     help="N>1: expert parallelism over NCCL (default) or independent replicas")
     ap.add_argument("--ep-chunks", type=int, default=1, help="pipelined batch chunks in EP mode")
+    ap.add_argument("--ep-transport", default="peer", choices=["peer", "nccl"],
+                    help="EP rows over NVLink peer memory (copy engines + down-GEMM epilogue stores) or NCCL all-to-all")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 

@@ -142,6 +142,16 @@ int moe_stage_route_finish(const struct MoEArgs* args, const MoeDims* dims, cuda
 int moe_stage_expert_ffn(const struct MoEArgs* args, const MoeDims* dims, const int* group_rows,
                          const int* group_start, const int* group_expert, int num_groups,
                          int64_t rows_capacity, cudaStream_t stream);
+// The FFN stage with its output rows sent to peers: group g's rows of Y go to
+// out_bases[group_out_rank[g]] from row group_out_row[g] on (f32 rows of
+// d_model), written by the down GEMM's epilogue (NVLink stores from inside the
+// GEMM, so the return transfer overlaps it) instead of hidden_mlp_layer_2_out.
+// out_bases are device pointers valid in this process (moe_peer_open), at most
+// 8.  The caller orders the peers' later reads after this stage (a barrier).
+int moe_stage_expert_ffn_peer(const struct MoEArgs* args, const MoeDims* dims, const int* group_rows,
+                              const int* group_start, const int* group_expert, const int* group_out_rank,
+                              const int* group_out_row, int num_groups, int64_t rows_capacity,
+                              float* const* out_bases, int num_bases, cudaStream_t stream);
 // Combine: final_output[t] = sum over kept routes in route order of
 // w * Y[row], Y = hidden_mlp_layer_2_out in the layout moe_stage_route made.
 int moe_stage_combine(const struct MoEArgs* args, const MoeDims* dims, cudaStream_t stream);
@@ -150,6 +160,16 @@ int moe_stage_combine(const struct MoEArgs* args, const MoeDims* dims, cudaStrea
 // INT8_CHANNEL (for which caller scratch is required; the row scales of A
 // come in MoeDims.act_scale).
 size_t moe_ffn_scratch_bytes(const MoeDims* dims, int64_t rows_capacity);
+
+// Peer memory for expert parallelism (CUDA IPC within a node): allocate a
+// device buffer and its 64-byte handle; map a peer's handle in this process;
+// unmap; free.  moe_memcpy_async copies between any device pointers
+// (a peer's included) on `stream` with the copy engines.
+int moe_peer_alloc(size_t bytes, void** ptr, void* handle64);
+int moe_peer_open(const void* handle64, void** ptr);
+int moe_peer_close(void* ptr);
+int moe_peer_free(void* ptr);
+int moe_memcpy_async(void* dst, const void* src, size_t bytes, cudaStream_t stream);
 
 // Synchronises `stream` and reports a device-side failure (MOE_ERR_TIMEOUT) of
 // the last moe_solve_v2 on this device, MOE_OK otherwise.

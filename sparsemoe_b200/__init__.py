@@ -110,6 +110,13 @@ def _load() -> ctypes.CDLL:
         "moe_stage_route_counts": (ctypes.c_int, [ctypes.POINTER(MoEArgs), ctypes.POINTER(MoeDims), _p, _p]),
         "moe_stage_route_finish": (ctypes.c_int, [ctypes.POINTER(MoEArgs), ctypes.POINTER(MoeDims), _p]),
         "moe_ffn_scratch_bytes": (ctypes.c_size_t, [ctypes.POINTER(MoeDims), ctypes.c_int64]),
+        "moe_stage_expert_ffn_peer": (ctypes.c_int, [ctypes.POINTER(MoEArgs), ctypes.POINTER(MoeDims), _p, _p, _p,
+                                                      _p, _p, ctypes.c_int, ctypes.c_int64, _p, ctypes.c_int, _p]),
+        "moe_peer_alloc": (ctypes.c_int, [ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p), _p]),
+        "moe_peer_open": (ctypes.c_int, [_p, ctypes.POINTER(ctypes.c_void_p)]),
+        "moe_peer_close": (ctypes.c_int, [_p]),
+        "moe_peer_free": (ctypes.c_int, [_p]),
+        "moe_memcpy_async": (ctypes.c_int, [_p, _p, ctypes.c_size_t, _p]),
         "moe_solve_v2_noalloc": (ctypes.c_int, [ctypes.POINTER(MoEArgs), ctypes.POINTER(MoeDims), _p]),
         "moe_noalloc_scratch_bytes": (ctypes.c_size_t, []),
         "moe_set_stage_events": (ctypes.c_int, [ctypes.POINTER(ctypes.c_void_p), ctypes.c_int]),

@@ -7,7 +7,16 @@
 
 #include <atomic>
 
+#include "moe_internal.h"
+
 namespace moe {
+
+// First output row of group g of a down GEMM: the local Y at the group's
+// start row, or the redirected peer rows (expert parallelism).
+__device__ __forceinline__ float* down_rows(const OutRedirect& r, float* local, int g, int start, int ld) {
+    if (r.rank) return r.bases[__ldg(r.rank + g)] + (int64_t)__ldg(r.row0 + g) * ld;
+    return local + (int64_t)start * ld;
+}
 
 template <typename T> struct F16Traits;
 template <> struct F16Traits<__half> {

@@ -73,6 +73,7 @@ struct GemmParams {
     float deq_gate, deq_up;  // s_in*s_gate, s_in*s_up
     float inv_mid;           // 1 / s_mid
     float deq_down;          // s_mid*s_down
+    OutRedirect red;         // down: optional peer destination of each group's rows
 };
 
 // ---- operand formats -----------------------------------------------------------
@@ -326,8 +327,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // rows of this warp's quarter: [warp_row0, warp_row0 + 32), coalesced through smem
                 const int warp_row0 = m * kBM + q * 32;
                 const int nrows = s_rows[e] - warp_row0;
-                float* y = reinterpret_cast<float*>(p.out) + ((int64_t)s_start[e] + warp_row0) * p.out_ld +
-                           n * kOutN;
+                float* y = down_rows(p.red, reinterpret_cast<float*>(p.out), e, s_start[e], p.out_ld) +
+                           (int64_t)warp_row0 * p.out_ld + n * kOutN;
                 float4* stage = reinterpret_cast<float4*>(sStage) + (warp - 2) * 128;
 #pragma unroll 1
                 for (int c = 0; c < 256; c += 32) {
@@ -345,6 +346,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             acc ^= 1;
             if (acc == 0) aph ^= 1u;
         }
+        if (kMode == 1 && p.red.rank) __threadfence_system();   // peer rows visible before the kernel ends
     }
     __syncthreads();
     if (warp == 1) {
@@ -423,6 +425,7 @@ GemmParams base_params(const GroupTable& gt, int* status, const GemmScales& sc) 
     p.deq_up = sc.s_in * sc.s_up;
     p.inv_mid = 1.0f / sc.s_mid;
     p.deq_down = sc.s_mid * sc.s_down;
+    p.red = gt.redirect;   // used by the down GEMM only
     return p;
 }
 

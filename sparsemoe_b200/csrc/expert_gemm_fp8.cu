@@ -81,6 +81,7 @@ struct Fp8Params {
     const float* w_scale1;   // up/gate: up scales
     int* status;
     uint32_t idesc;
+    OutRedirect red;         // down: optional peer destination of each group's rows
 };
 
 // m-tiles of a group come from its row count (no per-group table: shared
@@ -366,13 +367,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // this warp's 32 rows x 128 columns, coalesced through shared memory
                 const int warp_row0 = m * kBM + q * 32;
                 const int nrows = s_rows[g] - warp_row0;
-                float* y = reinterpret_cast<float*>(p.out) + ((int64_t)s_start[g] + warp_row0) * p.out_ld + n * 256 +
-                           128 * half;
+                float* y = down_rows(p.red, reinterpret_cast<float*>(p.out), g, s_start[g], p.out_ld) +
+                           (int64_t)warp_row0 * p.out_ld + n * 256 + 128 * half;
                 float4* stage = sStage + (warp - 2) * 128;
 #pragma unroll
                 for (int c = 0; c < 8; ++c) warp_store_rows16(stage, acc + 16 * c, y + 16 * c, p.out_ld, nrows, lane);
             }
         }
+        if (kMode == 1 && p.red.rank) __threadfence_system();   // peer rows visible before the kernel ends
     }
     __syncthreads();
     if (warp == 1) {
@@ -442,6 +444,7 @@ cudaError_t launch_fp8_down(const void* h_rows, const float* h_scale, const void
     p.w_scale0 = s_down;
     p.status = status;
     p.idesc = idesc_e4m3(kBM, 256, true);
+    p.red = gt.redirect;
     return launch<1, 0>(th, td, td, p, st, num_sms);
 }
 
@@ -493,6 +496,7 @@ cudaError_t launch_i8c_down(const void* h_rows, const float* h_scale, const void
     p.w_scale0 = s_down;
     p.status = status;
     p.idesc = idesc_i8(kBM, 256, true);
+    p.red = gt.redirect;
     return launch<1, 1>(th, td, td, p, st, num_sms);
 }
 

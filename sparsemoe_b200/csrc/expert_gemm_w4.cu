@@ -99,6 +99,7 @@ struct W4Params {
     const float* gs1;   // NVFP4: up
     int* status;
     uint32_t idesc;
+    OutRedirect red;    // down: optional peer destination of each group's rows
 };
 
 struct W4Maps {
@@ -318,8 +319,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 } else {
                     const int nrows = s_rows[g] - warp_row0;
-                    float* y = reinterpret_cast<float*>(p.out) + ((int64_t)s_start[g] + warp_row0) * p.out_ld +
-                               n * kBN;
+                    float* y = down_rows(p.red, reinterpret_cast<float*>(p.out), g, s_start[g], p.out_ld) +
+                               (int64_t)warp_row0 * p.out_ld + n * kBN;
 #pragma unroll 1
                     for (int c = 0; c < kBN; c += 32) {
                         uint32_t r[32];
@@ -337,6 +338,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             acc ^= 1;
             if (acc == 0) aph ^= 1u;
         }
+        if (kMode == 1 && p.red.rank) __threadfence_system();   // peer rows visible before the kernel ends
     } else {
         // ---------------- converter (warps 6..13) ----------------
         // thread: 8-column unit u of the kBN columns, K rows krow0 + kRowGroups*j.
@@ -511,6 +513,7 @@ cudaError_t launch_fmt(const void* a_rows, const void* w0, const void* w1, const
     p.out = out;
     p.gs0 = g0;
     p.gs1 = kMode == 0 ? g1 : g0;
+    if (kMode == 1) p.red = gt.redirect;
     return launch_bm<kMode, kFmt, kBM>(mp, p, st, num_sms);
 }
 

@@ -65,7 +65,7 @@ void set_error(const char* fmt, ...) {
     g_error = buf;
 }
 
-size_t workspace_header_bytes() { return 256 + 3 * align256(sizeof(int) * kMaxGroups); }
+size_t workspace_header_bytes() { return 256 + 5 * align256(sizeof(int) * kMaxGroups); }
 
 // Per-row activation scales: FP8 one per 1x128 block of x / h; INT8_CHANNEL one
 // per row of x and one per 1x128 block of h.
@@ -96,6 +96,8 @@ void carve_workspace(void* base, const Shape& s, Workspace* ws) {
     ws->grp_rows = reinterpret_cast<int*>(p);     p += align256(sizeof(int) * kMaxGroups);
     ws->grp_start = reinterpret_cast<int*>(p);    p += align256(sizeof(int) * kMaxGroups);
     ws->grp_weight = reinterpret_cast<int*>(p);   p += align256(sizeof(int) * kMaxGroups);
+    ws->grp_out_rank = reinterpret_cast<int*>(p); p += align256(sizeof(int) * kMaxGroups);
+    ws->grp_out_row = reinterpret_cast<int*>(p);  p += align256(sizeof(int) * kMaxGroups);
     ws->route_slot = reinterpret_cast<int*>(p);   p += align256(sizeof(int) * routes);
     ws->chunk_count = reinterpret_cast<int*>(p);  p += align256(sizeof(int) * chunk_tab);
     ws->chunk_base = reinterpret_cast<int*>(p);   p += align256(sizeof(int) * chunk_tab);
@@ -576,9 +578,10 @@ extern "C" size_t moe_ffn_scratch_bytes(const MoeDims* dims, int64_t rows_capaci
     return workspace_header_bytes() + ffn_h_scale_bytes(s, rows_capacity);
 }
 
-extern "C" int moe_stage_expert_ffn(const MoEArgs* a, const MoeDims* dims, const int* group_rows,
-                                    const int* group_start, const int* group_expert, int num_groups,
-                                    int64_t rows_capacity, cudaStream_t stream) {
+namespace {
+int stage_ffn(const MoEArgs* a, const MoeDims* dims, const int* group_rows, const int* group_start,
+              const int* group_expert, const int* group_out_rank, const int* group_out_row, int num_groups,
+              int64_t rows_capacity, float* const* out_bases, int num_bases, cudaStream_t stream) {
     // Only the FFN shape matters here: an owner may hold a single expert.
     if (!dims) { set_error("dims is null"); return MOE_ERR_INVALID_ARG; }
     MoeDims fd = *dims;
@@ -603,7 +606,16 @@ extern "C" int moe_stage_expert_ffn(const MoEArgs* a, const MoeDims* dims, const
         set_error("moe_stage_expert_ffn: bad group table (num_groups %d, max %d)", num_groups, kMaxGroups);
         return MOE_ERR_INVALID_ARG;
     }
+    if (group_out_rank && (!group_out_row || !out_bases || num_bases < 1 || num_bases > kMaxPeers)) {
+        set_error("moe_stage_expert_ffn_peer: out rows / bases missing or more than %d peers", kMaxPeers);
+        return MOE_ERR_INVALID_ARG;
+    }
     for (int g = 0; g < num_groups; ++g) {
+        if (group_out_rank && (group_out_rank[g] < 0 || group_out_rank[g] >= num_bases || group_out_row[g] < 0 ||
+                               !out_bases[group_out_rank[g]])) {
+            set_error("moe_stage_expert_ffn_peer: group %d has a bad output rank / row", g);
+            return MOE_ERR_INVALID_ARG;
+        }
         const int w = group_expert ? group_expert[g] : g;
         if (group_rows[g] < 0 || group_start[g] < 0 || (int64_t)group_start[g] + group_rows[g] > rows_capacity ||
             w < 0 || w >= s.E) {
@@ -627,8 +639,18 @@ extern "C" int moe_stage_expert_ffn(const MoEArgs* a, const MoeDims* dims, const
         MOE_TRY(cudaMemcpyAsync(ws.grp_weight, group_expert, sizeof(int) * num_groups, cudaMemcpyHostToDevice,
                                 stream),
                 "cudaMemcpyAsync(group experts)");
-    const GroupTable gt{ws.grp_rows, ws.grp_start, group_expert ? ws.grp_weight : nullptr, num_groups,
-                        rows_capacity};
+    GroupTable gt{ws.grp_rows, ws.grp_start, group_expert ? ws.grp_weight : nullptr, num_groups, rows_capacity};
+    if (group_out_rank) {
+        MOE_TRY(cudaMemcpyAsync(ws.grp_out_rank, group_out_rank, sizeof(int) * num_groups, cudaMemcpyHostToDevice,
+                                stream),
+                "cudaMemcpyAsync(group output ranks)");
+        MOE_TRY(cudaMemcpyAsync(ws.grp_out_row, group_out_row, sizeof(int) * num_groups, cudaMemcpyHostToDevice,
+                                stream),
+                "cudaMemcpyAsync(group output rows)");
+        gt.redirect.rank = ws.grp_out_rank;
+        gt.redirect.row0 = ws.grp_out_row;
+        for (int r = 0; r < num_bases; ++r) gt.redirect.bases[r] = out_bases[r];
+    }
     float* h_scale = nullptr;
     if (s.dtype == MOE_DTYPE_FP8_BLOCK || s.dtype == MOE_DTYPE_INT8_CHANNEL) {
         // row scales of A from the caller; h scales in the caller's scratch after the header
@@ -641,6 +663,23 @@ extern "C" int moe_stage_expert_ffn(const MoEArgs* a, const MoeDims* dims, const
         h_scale = reinterpret_cast<float*>(static_cast<uint8_t*>(dims->scratch) + workspace_header_bytes());
     }
     return enqueue_ffn(a, dims, s, gt, ws.status, dims->act_scale, h_scale, st->num_sms, stream);
+}
+}  // namespace
+
+extern "C" int moe_stage_expert_ffn(const MoEArgs* a, const MoeDims* dims, const int* group_rows,
+                                    const int* group_start, const int* group_expert, int num_groups,
+                                    int64_t rows_capacity, cudaStream_t stream) {
+    return stage_ffn(a, dims, group_rows, group_start, group_expert, nullptr, nullptr, num_groups, rows_capacity,
+                     nullptr, 0, stream);
+}
+
+extern "C" int moe_stage_expert_ffn_peer(const MoEArgs* a, const MoeDims* dims, const int* group_rows,
+                                         const int* group_start, const int* group_expert, const int* group_out_rank,
+                                         const int* group_out_row, int num_groups, int64_t rows_capacity,
+                                         float* const* out_bases, int num_bases, cudaStream_t stream) {
+    if (!group_out_rank) { set_error("moe_stage_expert_ffn_peer: group_out_rank is null"); return MOE_ERR_INVALID_ARG; }
+    return stage_ffn(a, dims, group_rows, group_start, group_expert, group_out_rank, group_out_row, num_groups,
+                     rows_capacity, out_bases, num_bases, stream);
 }
 
 extern "C" int moe_stage_combine(const MoEArgs* a, const MoeDims* dims, cudaStream_t stream) {

@@ -43,6 +43,8 @@ struct Workspace {
     int* grp_rows;      // [kMaxGroups] rows of each GEMM group (expert-parallel calls)
     int* grp_start;     // [kMaxGroups] first row of each group
     int* grp_weight;    // [kMaxGroups] expert weight index of each group
+    int* grp_out_rank;  // [kMaxGroups] peer that receives each group's output rows
+    int* grp_out_row;   // [kMaxGroups] first output row of each group there
     int* route_slot;    // [B*N*k]   slot of each route, -1 if dropped / no expert
     int* chunk_count;   // [B, chunks, E] routes per (batch, chunk, expert)
     int* chunk_base;    // [B, chunks, E] exclusive prefix over chunks
@@ -58,12 +60,24 @@ size_t workspace_header_bytes();
 // Row groups of one grouped GEMM: group g has rows[g] rows starting at row
 // start[g] of the A/H/Y buffers (capacity rows_capacity) and multiplies expert
 // weight[g] (weight == nullptr: group g uses expert g).  Device arrays.
+constexpr int kMaxPeers = 8;
+// Optional redirect of the down GEMM's output rows (expert parallelism over
+// peer memory): group g's rows go to bases[rank[g]] from row row0[g] on (rows
+// of out_ld f32), instead of the local Y at the group's start row.  The
+// epilogue then ends with a system-scope fence.
+struct OutRedirect {
+    const int* rank = nullptr;   // [G] device
+    const int* row0 = nullptr;   // [G] device
+    float* bases[kMaxPeers] = {};
+};
+
 struct GroupTable {
     const int* rows;
     const int* start;
     const int* weight;
     int G;
     int64_t rows_capacity;
+    OutRedirect redirect = {};
 };
 size_t workspace_bytes(const Shape& s);
 void carve_workspace(void* base, const Shape& s, Workspace* ws);

@@ -75,6 +75,16 @@ def recv_plan(table: np.ndarray, rank: int):
 
 
 # ---- runner ----------------------------------------------------------------------
+class _Ptr:
+    """A raw device address with the data_ptr() of a tensor."""
+
+    def __init__(self, addr: int):
+        self.addr = addr
+
+    def data_ptr(self) -> int:
+        return self.addr
+
+
 class _Chunk:
     """One group of whole batches routed, exchanged and combined together."""
 
@@ -106,7 +116,7 @@ class ExpertParallelLayer:
     PHASES = ("route", "exchange_and_ffn", "combine")
 
     def __init__(self, cfg: LayerConfig, device, group=None, chunks: int | None = None,
-                 global_batch: bool = False):
+                 global_batch: bool = False, transport: str = "nccl"):
         import torch
         import torch.distributed as dist
         self.torch, self.dist = torch, dist
@@ -122,6 +132,9 @@ class ExpertParallelLayer:
         chunks = 1 if chunks is None else chunks
         assert B % chunks == 0 or B == 0, "chunks must divide num_batches"
         assert not (global_batch and chunks > 1), "global batches run as one chunk"
+        assert transport in ("nccl", "peer"), transport
+        assert not (transport == "peer" and chunks > 1), "the peer transport runs as one chunk"
+        self.transport = transport
         self.n_chunks = max(chunks, 1)
         if global_batch:
             # CAP of the whole batch (world shards of N tokens); cap < 0: no drop
@@ -194,6 +207,60 @@ class ExpertParallelLayer:
             ch.ffn_scratch = torch.empty(ffn_bytes, dtype=torch.uint8, device=dev)
             self.chunks.append(ch)
         self.comm_stream = torch.cuda.Stream(device=dev)
+        if transport == "peer":
+            self._setup_peer()
+
+    # -- peer memory (transport="peer") ---------------------------------------------
+    def _setup_peer(self):
+        """Receive buffers (rows, row scales) and return buffers (f32 rows)
+        that the other ranks map through CUDA IPC: senders copy their rows
+        straight into the owners' receive buffers, and owners' down-GEMM
+        epilogues store result rows straight into the senders' return
+        buffers."""
+        torch, dist = self.torch, self.dist
+        cfg, d = self.cfg, self.cfg.d_model
+        ch = self.chunks[0]
+        self._row_bytes = d * self.recv_x.element_size()
+        self._scale_bytes = 4 * self.n_scale
+        sizes = {"recv_x": self.recv_cap * self._row_bytes, "back_y": ch.send_x.shape[0] * d * 4}
+        if self.n_scale:
+            sizes["recv_scale"] = self.recv_cap * self._scale_bytes
+        self.peer_local, self.peer_maps = {}, {}
+        for name, nbytes in sizes.items():
+            ptr, handle = ctypes.c_void_p(), (ctypes.c_ubyte * 64)()
+            check(lib.moe_peer_alloc(max(nbytes, 256), ctypes.byref(ptr), handle))
+            self.peer_local[name] = ptr.value
+            mine = torch.tensor(list(bytes(handle)), dtype=torch.uint8, device=self.device)
+            every = torch.empty(self.world, 64, dtype=torch.uint8, device=self.device)
+            dist.all_gather_into_tensor(every, mine, group=self.group)
+            every = every.cpu().numpy()
+            maps = []
+            for r in range(self.world):
+                if r == self.rank:
+                    maps.append(ptr.value)
+                    continue
+                h = (ctypes.c_ubyte * 64)(*every[r].tolist())
+                q = ctypes.c_void_p()
+                check(lib.moe_peer_open(h, ctypes.byref(q)))
+                maps.append(q.value)
+            self.peer_maps[name] = maps
+        self._bar = torch.zeros(1, dtype=torch.int32, device=self.device)
+
+    def close(self):
+        """Unmaps the peers' buffers and frees this rank's (peer transport)."""
+        if getattr(self, "peer_maps", None):
+            self.torch.cuda.synchronize(self.device)
+            for maps in self.peer_maps.values():
+                for r, ptr in enumerate(maps):
+                    if r != self.rank:
+                        lib.moe_peer_close(ctypes.c_void_p(ptr))
+            for ptr in self.peer_local.values():
+                lib.moe_peer_free(ctypes.c_void_p(ptr))
+            self.peer_maps, self.peer_local = {}, {}
+
+    def _barrier(self, S):
+        with self.torch.cuda.stream(S):
+            self.dist.all_reduce(self._bar, group=self.group)
 
     # -- weights ------------------------------------------------------------------
     def load(self, inputs: dict, local: bool = False) -> "ExpertParallelLayer":
@@ -318,6 +385,66 @@ class ExpertParallelLayer:
         return fd
 
     # -- one layer call -------------------------------------------------------------
+    def _forward_peer(self, S, ev):
+        """Steps 3-5 over peer memory: copy-engine row copies into the owners'
+        receive buffers, a barrier, the owner FFN whose epilogue stores the
+        result rows into the senders' return buffers, a barrier."""
+        torch, cfg = self.torch, self.cfg
+        ch = self.chunks[0]
+        sp = ctypes.c_void_p(S.cuda_stream)
+        P, E, e_loc, me = self.world, cfg.num_experts, self.e_loc, self.rank
+        mine = self.counts[: cfg.num_batches].sum(dim=0, dtype=torch.int32)
+        table = torch.empty(P, E, dtype=torch.int32, device=self.device)
+        with torch.cuda.stream(S):
+            self.dist.all_gather_into_tensor(table, mine, group=self.group)
+        t = table.cpu().numpy().astype(np.int64)                      # [sender, expert]
+        own = t.reshape(P, P, e_loc)                                 # [sender, owner, local expert]
+        to_owner = own.sum(axis=2)                                   # rows sender -> owner
+        block_start = np.concatenate([np.zeros((P, 1), np.int64), np.cumsum(to_owner, axis=1)[:, :-1]], axis=1)
+        recv_off = np.concatenate([np.zeros((1, P), np.int64), np.cumsum(to_owner, axis=0)[:-1]], axis=0)
+        # 3. my rows for owner q -> q's receive buffer after the blocks of senders < me
+        for q in range(P):
+            n = int(to_owner[me, q])
+            if n == 0:
+                continue
+            src_row, dst_row = int(block_start[me, q]), int(recv_off[me, q])
+            check(lib.moe_memcpy_async(ctypes.c_void_p(self.peer_maps["recv_x"][q] + dst_row * self._row_bytes),
+                                       ctypes.c_void_p(ch.send_x.data_ptr() + src_row * self._row_bytes),
+                                       n * self._row_bytes, sp))
+            if self.n_scale:
+                check(lib.moe_memcpy_async(
+                    ctypes.c_void_p(self.peer_maps["recv_scale"][q] + dst_row * self._scale_bytes),
+                    ctypes.c_void_p(ch.send_scale.data_ptr() + src_row * self._scale_bytes),
+                    n * self._scale_bytes, sp))
+        self._barrier(S)
+        ev("ffn")
+        # 4. owner FFN: groups (local expert j, sender s), results to s's return buffer
+        within = np.concatenate([np.zeros((P, 1), np.int64), np.cumsum(own[:, me, :], axis=1)[:, :-1]], axis=1)
+        rows, start, expert, orank, orow = [], [], [], [], []
+        for j in range(e_loc):
+            for snd in range(P):
+                rows.append(int(own[snd, me, j]))
+                start.append(int(recv_off[snd, me] + within[snd, j]))
+                expert.append(j)
+                orank.append(snd)
+                orow.append(int(block_start[snd, me] + within[snd, j]))
+        arr = [np.array(v, np.int32) for v in (rows, start, expert, orank, orow)]
+        fa = self._ffn_args(ch)
+        fa.per_expert_wmma_inputs = fa.per_expert_wmma_inputs_int8 = fa.per_expert_wmma_inputs_fp8 = None
+        self._set_rows(fa, _Ptr(self.peer_local["recv_x"]), ch.h)
+        fd = self._ffn_dims_base()
+        fd.scratch, fd.scratch_bytes = ch.ffn_scratch.data_ptr(), ch.ffn_scratch.numel()
+        if self.n_scale:
+            fd.act_scale = self.peer_local["recv_scale"]
+        bases = (ctypes.c_void_p * P)(*self.peer_maps["back_y"])
+        check(lib.moe_stage_expert_ffn_peer(ctypes.byref(fa), ctypes.byref(fd), *(a.ctypes.data for a in arr[:3]),
+                                            arr[3].ctypes.data, arr[4].ctypes.data, len(rows), self.recv_cap, bases,
+                                            P, sp))
+        ev("ffn")
+        self._barrier(S)
+        self._keep = (fa, fd, arr, bases)
+        return t, int(to_owner[:, me].sum())
+
     def forward(self, stream=None, timing=None):
         """One layer call.  `timing` (optional dict) receives torch.cuda.Event
         lists: 'start', 'routed', 'ffn' (pairs per chunk), 'combine', 'end'."""
@@ -353,6 +480,15 @@ class ExpertParallelLayer:
             else:
                 check(lib.moe_stage_route(ctypes.byref(ch.ra), ctypes.byref(ch.dims), sp))
         ev("routed")
+        if self.transport == "peer":
+            ch = self.chunks[0]
+            ch.ra.hidden_mlp_layer_2_out = self.peer_local["back_y"]   # combine reads the peer-written rows
+            table_h, owner_rows = self._forward_peer(S, ev)
+            ev("combine")
+            check(lib.moe_stage_combine(ctypes.byref(ch.ra), ctypes.byref(ch.dims), sp))
+            ev("end")
+            self.last_plan = {"table": table_h, "owner_rows": owner_rows}
+            return self.out
         nc = self.n_chunks
         mine = self.counts[: cfg.num_batches].view(nc, -1, cfg.num_experts).sum(dim=1, dtype=torch.int32)
         table = torch.empty(self.world, nc, cfg.num_experts, dtype=torch.int32, device=self.device)

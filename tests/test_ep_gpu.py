@@ -22,7 +22,8 @@ def _worker(rank, world, port, case, results):
     from datetime import timedelta
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
                             device_id=torch.device("cuda", rank))
-    B, N, d, f, E, k, cf, dtype, zipf, chunks, glob = case
+    B, N, d, f, E, k, cf, dtype, zipf, chunks, glob = case[:11]
+    transport = case[11] if len(case) > 11 else "nccl"
     if glob:
         # one batch of world*N tokens; this rank holds tokens [rank*N, (rank+1)*N) of every batch
         full_cfg = sm.LayerConfig(B, N * world, d, f, E, k, cf, dtype=dtype, zipf_s=zipf,
@@ -30,7 +31,7 @@ def _worker(rank, world, port, case, results):
         full = sm.make_inputs(full_cfg, 5)
         x = full["x"].reshape(B, world, N, d)[:, rank].reshape(B * N, d)
         cfg = sm.LayerConfig(B, N, d, f, E, k, cf, dtype=dtype, zipf_s=zipf, router_f32=full_cfg.router_f32)
-        ep = ExpertParallelLayer(cfg, f"cuda:{rank}", global_batch=True).load({**full, "x": x})
+        ep = ExpertParallelLayer(cfg, f"cuda:{rank}", global_batch=True, transport=transport).load({**full, "x": x})
         single = sm.MoeLayer(full_cfg, f"cuda:{rank}").load(full)
         rows = np.concatenate([np.arange(b * N * world + rank * N, b * N * world + (rank + 1) * N)
                                for b in range(B)])
@@ -39,7 +40,7 @@ def _worker(rank, world, port, case, results):
         full = sm.make_inputs(cfg, 5)
         mine = sm.make_inputs(cfg, 100 + rank)
         inputs = {**full, "x": mine["x"]}
-        ep = ExpertParallelLayer(cfg, f"cuda:{rank}", chunks=chunks).load(inputs)
+        ep = ExpertParallelLayer(cfg, f"cuda:{rank}", chunks=chunks, transport=transport).load(inputs)
         single = sm.MoeLayer(cfg, f"cuda:{rank}").load(inputs)
         rows = np.arange(cfg.T)
     ep.forward()
@@ -53,6 +54,7 @@ def _worker(rank, world, port, case, results):
     idx_equal = bool(np.array_equal(ep.idx.cpu().numpy()[: cfg.T], single.idx.cpu().numpy()[rows]))
     results[rank] = (bool(np.array_equal(a, b)), float(np.abs(a - b).max() / max(np.abs(b).max(), 1e-30)),
                      idx_equal)
+    ep.close()
     dist.destroy_process_group()
 
 
@@ -68,6 +70,11 @@ CASES = {
     "global_bf16_drops": (2, 192, 512, 256, 16, 4, 1.0, sm.DTYPE_BF16, 1.2, 1, True),
     "global_int4_deepseek_like": (1, 256, 512, 256, 32, 8, 1.25, sm.DTYPE_W4A16, 1.0, 1, True),
     "global_fp8": (1, 256, 512, 256, 16, 4, 1.0, sm.DTYPE_FP8_BLOCK, 1.1, 1, True),
+    # rows over NVLink peer memory: copy-engine dispatch, down-GEMM epilogue stores into the senders
+    "peer_bf16": (2, 256, 512, 512, 8, 2, 1.25, sm.DTYPE_BF16, 0.0, 1, False, "peer"),
+    "peer_fp8_block_scales": (1, 256, 512, 256, 16, 4, 1.25, sm.DTYPE_FP8_BLOCK, 0.0, 1, False, "peer"),
+    "peer_global_int4": (1, 256, 512, 256, 32, 8, 1.25, sm.DTYPE_W4A16, 1.0, 1, True, "peer"),
+    "peer_global_nvfp4_drops": (1, 192, 512, 256, 16, 4, 1.0, sm.DTYPE_NVFP4, 1.2, 1, True, "peer"),
 }
 
 
