@@ -441,7 +441,6 @@ def run_ep(args, cfg, ws, rank, local, dev):
     with ClockSampler(local) as clocks:
         for i in range(K):
             layer.forward(stream, timing=timings[i])
-            owner_rows.append(layer.last_plan["owner_rows"])
         torch.cuda.synchronize(dev)
     barrier(ws)
 
@@ -480,6 +479,7 @@ def run_ep(args, cfg, ws, rank, local, dev):
     peak_tf = float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
     if cfg.int8 or cfg.int8ch or cfg.fp8:
         peak_tf *= 2.0   # dense int8 / fp8 tensor rate is twice bf16 on B200
+    owner_rows.append(layer.owner_rows())   # the same tokens every step
     flop_ffn = 6.0 * cfg.d_model * cfg.d_ff * statistics.mean(owner_rows)
     ach = flop_ffn / (phase_ms["expert_ffn_compute"] * 1e-3) / 1e12
     ach_min = max_over_ranks(-ach, ws, dev) * -1.0      # slowest rank

@@ -89,6 +89,9 @@ typedef struct MoeDims {
     // dynamically quantised formats (FP8_BLOCK [rows, d/128], INT8_CHANNEL
     // [rows]): written by the gather, read by the up/gate GEMM.  NULL: scratch.
     float* act_scale;
+    // Non-zero: the routing stages stop before the gather (expert parallelism
+    // over peer memory, where moe_stage_dispatch_peer gathers into the owners).
+    int skip_gather;
 } MoeDims;
 
 // Reference: kernels/launcher.h:21 `extern "C" void solve(MoEArgs args)`.
@@ -160,6 +163,28 @@ int moe_stage_combine(const struct MoEArgs* args, const MoeDims* dims, cudaStrea
 // INT8_CHANNEL (for which caller scratch is required; the row scales of A
 // come in MoeDims.act_scale).
 size_t moe_ffn_scratch_bytes(const MoeDims* dims, int64_t rows_capacity);
+
+// Expert parallelism over peer memory without host synchronisation.
+// moe_ep_plan: from the all-gathered kept-row table [world, E] (device int32,
+// rows each rank routes to each expert), writes the device plan of this rank
+// (7*E int32): per expert e the owner rank and the first row of this rank's
+// block in the owner's receive buffer, then the owner-side row groups
+// (local expert j x sender s, g = j*world + s): rows, start row in the
+// receive buffer, local expert, sender, and the first row of the group's
+// results in the sender's return buffer.
+int moe_ep_plan(const int* table, int world, int rank, int num_experts, int* plan, cudaStream_t stream);
+// Gathers this rank's kept rows (quantised for the 8-bit formats, with their
+// row scales) straight into the owners' receive buffers row_bases[owner]
+// (scale_bases[owner]) as the plan places them; the routing tables come from
+// moe_stage_route / _finish with dims.skip_gather on the same dims and scratch.
+int moe_stage_dispatch_peer(const struct MoEArgs* args, const MoeDims* dims, const int* plan,
+                            void* const* row_bases, float* const* scale_bases, int num_bases, cudaStream_t stream);
+// The owner FFN over the plan's row groups (device arrays; num_groups =
+// E_global), result rows stored into out_bases[sender] by the down GEMM.
+// dims.num_experts is the owner's local expert count.
+int moe_stage_expert_ffn_planned(const struct MoEArgs* args, const MoeDims* dims, const int* plan,
+                                 int num_groups, int64_t rows_capacity, float* const* out_bases, int num_bases,
+                                 cudaStream_t stream);
 
 // Peer memory for expert parallelism (CUDA IPC within a node): allocate a
 // device buffer and its 64-byte handle; map a peer's handle in this process;

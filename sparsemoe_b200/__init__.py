@@ -84,7 +84,7 @@ class MoeDims(ctypes.Structure):
         ("w4_scale_gate", _p), ("w4_scale_up", _p), ("w4_scale_down", _p),
         ("w4_zero_gate", _p), ("w4_zero_up", _p), ("w4_zero_down", _p),
         ("fp4_global_gate", _p), ("fp4_global_up", _p), ("fp4_global_down", _p),
-        ("slot_base", _p), ("act_scale", _p),
+        ("slot_base", _p), ("act_scale", _p), ("skip_gather", ctypes.c_int),
     ]
 
 
@@ -112,6 +112,11 @@ def _load() -> ctypes.CDLL:
         "moe_ffn_scratch_bytes": (ctypes.c_size_t, [ctypes.POINTER(MoeDims), ctypes.c_int64]),
         "moe_stage_expert_ffn_peer": (ctypes.c_int, [ctypes.POINTER(MoEArgs), ctypes.POINTER(MoeDims), _p, _p, _p,
                                                       _p, _p, ctypes.c_int, ctypes.c_int64, _p, ctypes.c_int, _p]),
+        "moe_ep_plan": (ctypes.c_int, [_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, _p, _p]),
+        "moe_stage_dispatch_peer": (ctypes.c_int, [ctypes.POINTER(MoEArgs), ctypes.POINTER(MoeDims), _p, _p, _p,
+                                                    ctypes.c_int, _p]),
+        "moe_stage_expert_ffn_planned": (ctypes.c_int, [ctypes.POINTER(MoEArgs), ctypes.POINTER(MoeDims), _p,
+                                                         ctypes.c_int, ctypes.c_int64, _p, ctypes.c_int, _p]),
         "moe_peer_alloc": (ctypes.c_int, [ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p), _p]),
         "moe_peer_open": (ctypes.c_int, [_p, ctypes.POINTER(ctypes.c_void_p)]),
         "moe_peer_close": (ctypes.c_int, [_p]),

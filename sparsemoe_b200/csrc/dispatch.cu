@@ -33,6 +33,17 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
+
+// Row of slot (b, e, s) and the peer (0: local) that receives it.
+__device__ __forceinline__ int64_t gather_row(const GatherDst& g, const int* expert_start, const int* row_base,
+                                              int e, int be, int s, int& q) {
+    if (g.rank) {
+        q = g.rank[e];
+        return (int64_t)g.row0[e] + row_base[be] + s;
+    }
+    q = 0;
+    return (int64_t)expert_start[e] + row_base[be] + s;
+}
 constexpr int kRounds = kChunkRoutes / kThreads;
 
 __global__ void __launch_bounds__(kThreads) dispatch_count_kernel(const int* __restrict__ idx, int N,
@@ -158,7 +169,7 @@ __global__ void __launch_bounds__(kThreads) dispatch_assign_kernel(
 __global__ void __launch_bounds__(kThreads) dispatch_gather_kernel(
     const uint4* __restrict__ x, const int* __restrict__ counts, const int* __restrict__ token_ids,
     const int* __restrict__ row_base, const int* __restrict__ expert_start, int N, int E, int B, int cap,
-    int vec_per_row, uint4* __restrict__ a_rows) {
+    int vec_per_row, const GatherDst gd) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t slot_lin = (int64_t)blockIdx.x * kWarps + warp;
     if (slot_lin >= (int64_t)B * E * cap) return;
@@ -168,7 +179,9 @@ __global__ void __launch_bounds__(kThreads) dispatch_gather_kernel(
     const int b = be / E, e = be - b * E;
     const int64_t t = token_ids[slot_lin];
     const uint4* src = x + ((int64_t)b * N + t) * vec_per_row;
-    uint4* dst = a_rows + ((int64_t)expert_start[e] + row_base[be] + s) * vec_per_row;
+    int q;
+    const int64_t row = gather_row(gd, expert_start, row_base, e, be, s, q);
+    uint4* dst = static_cast<uint4*>(gd.rows[q]) + row * vec_per_row;
     int v = lane;
     for (; v + 96 < vec_per_row; v += 128) {
         const uint4 a0 = __ldg(src + v), a1 = __ldg(src + v + 32), a2 = __ldg(src + v + 64),
@@ -186,7 +199,7 @@ __global__ void __launch_bounds__(kThreads) dispatch_gather_kernel(
 __global__ void __launch_bounds__(kThreads) dispatch_gather_q8_kernel(
     const uint4* __restrict__ x, const int* __restrict__ counts, const int* __restrict__ token_ids,
     const int* __restrict__ row_base, const int* __restrict__ expert_start, int N, int E, int B, int cap,
-    int vec_per_row, float s_in, uint2* __restrict__ a_rows) {
+    int vec_per_row, float s_in, const GatherDst gd) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t slot_lin = (int64_t)blockIdx.x * kWarps + warp;
     if (slot_lin >= (int64_t)B * E * cap) return;
@@ -196,7 +209,9 @@ __global__ void __launch_bounds__(kThreads) dispatch_gather_q8_kernel(
     const int b = be / E, e = be - b * E;
     const int64_t t = token_ids[slot_lin];
     const uint4* src = x + ((int64_t)b * N + t) * vec_per_row;
-    uint2* dst = a_rows + ((int64_t)expert_start[e] + row_base[be] + s) * vec_per_row;
+    int q;
+    const int64_t row = gather_row(gd, expert_start, row_base, e, be, s, q);
+    uint2* dst = static_cast<uint2*>(gd.rows[q]) + row * vec_per_row;
     for (int v = lane; v < vec_per_row; v += 32) {
         const uint4 raw = __ldg(src + v);
         const __half2* h2 = reinterpret_cast<const __half2*>(&raw);
@@ -218,7 +233,7 @@ __global__ void __launch_bounds__(kThreads) dispatch_gather_q8_kernel(
 __global__ void __launch_bounds__(kThreads) dispatch_gather_fp8_kernel(
     const __nv_bfloat16* __restrict__ x, const int* __restrict__ counts, const int* __restrict__ token_ids,
     const int* __restrict__ row_base, const int* __restrict__ expert_start, int N, int E, int B, int cap, int d,
-    uint8_t* __restrict__ a_rows, float* __restrict__ a_scale) {
+    const GatherDst gd) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t slot_lin = (int64_t)blockIdx.x * kWarps + warp;
     if (slot_lin >= (int64_t)B * E * cap) return;
@@ -228,8 +243,10 @@ __global__ void __launch_bounds__(kThreads) dispatch_gather_fp8_kernel(
     const int b = be / E, e = be - b * E;
     const int64_t t = token_ids[slot_lin];
     const __nv_bfloat16* src = x + ((int64_t)b * N + t) * d;
-    const int64_t row = (int64_t)expert_start[e] + row_base[be] + s;
-    uint8_t* dst = a_rows + row * d;
+    int q;
+    const int64_t row = gather_row(gd, expert_start, row_base, e, be, s, q);
+    uint8_t* dst = static_cast<uint8_t*>(gd.rows[q]) + row * d;
+    float* a_scale = gd.scales[q];
     const int nblk = d / 128;   // a multiple of 2 (d % 256 == 0)
     // 8 blocks' loads in flight per round (lane: 4 elements of each block)
     for (int b0 = 0; b0 < nblk; b0 += 8) {
@@ -263,7 +280,7 @@ __global__ void __launch_bounds__(kThreads) dispatch_gather_fp8_kernel(
 __global__ void __launch_bounds__(kThreads) dispatch_gather_q8tok_kernel(
     const uint4* __restrict__ x, const int* __restrict__ counts, const int* __restrict__ token_ids,
     const int* __restrict__ row_base, const int* __restrict__ expert_start, int N, int E, int B, int cap, int vecs,
-    uint2* __restrict__ a_rows, float* __restrict__ a_scale) {
+    const GatherDst gd) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t slot_lin = (int64_t)blockIdx.x * kWarps + warp;
     if (slot_lin >= (int64_t)B * E * cap) return;
@@ -273,7 +290,8 @@ __global__ void __launch_bounds__(kThreads) dispatch_gather_q8tok_kernel(
     const int b = be / E, e = be - b * E;
     const int64_t t = token_ids[slot_lin];
     const uint4* src = x + ((int64_t)b * N + t) * vecs;
-    const int64_t row = (int64_t)expert_start[e] + row_base[be] + s;
+    int q;
+    const int64_t row = gather_row(gd, expert_start, row_base, e, be, s, q);
     float amax = 0.0f;
     for (int v = lane; v < vecs; v += 32) {
         const uint4 raw = __ldg(src + v);
@@ -287,7 +305,7 @@ __global__ void __launch_bounds__(kThreads) dispatch_gather_q8tok_kernel(
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
     const float sc = amax > 0.0f ? amax / 127.0f : 1.0f;
-    uint2* dst = a_rows + row * vecs;
+    uint2* dst = static_cast<uint2*>(gd.rows[q]) + row * vecs;
     for (int v = lane; v < vecs; v += 32) {
         const uint4 raw = __ldg(src + v);
         const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
@@ -301,10 +319,52 @@ __global__ void __launch_bounds__(kThreads) dispatch_gather_q8tok_kernel(
         }
         dst[v] = make_uint2(w[0], w[1]);
     }
-    if (lane == 0) a_scale[row] = sc;
+    if (lane == 0) gd.scales[q][row] = sc;
+}
+
+// Expert-parallel plan of rank `me` from the kept-row table [P, E] (one CTA).
+// Layout (7E ints): owner[E] | row0[E] | g_rows[G] | g_start[G] | g_expert[G] |
+// g_sender[G] | g_out_row[G], G = E, g = j * P + s.
+__global__ void __launch_bounds__(256) ep_plan_kernel(const int* __restrict__ table, int P, int E, int me,
+                                                      int* __restrict__ plan) {
+    const int el = E / P;
+    auto to_owner = [&](int s, int q) {
+        int n = 0;
+        for (int j = 0; j < el; ++j) n += table[s * E + q * el + j];
+        return n;
+    };
+    auto recv_off = [&](int s, int q) {   // rows of senders < s in q's receive buffer
+        int n = 0;
+        for (int s2 = 0; s2 < s; ++s2) n += to_owner(s2, q);
+        return n;
+    };
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+        const int q = e / el;
+        int within = 0;
+        for (int e2 = q * el; e2 < e; ++e2) within += table[me * E + e2];
+        plan[e] = q;
+        plan[E + e] = recv_off(me, q) + within;
+    }
+    for (int g = threadIdx.x; g < E; g += blockDim.x) {
+        const int j = g / P, s = g - j * P;
+        int within = 0;
+        for (int j2 = 0; j2 < j; ++j2) within += table[s * E + me * el + j2];
+        int block_start = 0;   // first row of owner me's experts in sender s's dense layout
+        for (int e2 = 0; e2 < me * el; ++e2) block_start += table[s * E + e2];
+        plan[2 * E + g] = table[s * E + me * el + j];
+        plan[3 * E + g] = recv_off(s, me) + within;
+        plan[4 * E + g] = j;
+        plan[5 * E + g] = s;
+        plan[6 * E + g] = block_start + within;
+    }
 }
 
 }  // namespace
+
+cudaError_t launch_ep_plan(const int* table, int P, int E, int me, int* plan, cudaStream_t st) {
+    ep_plan_kernel<<<1, 256, 0, st>>>(table, P, E, me, plan);
+    return cudaGetLastError();
+}
 
 // Route totals per (chunk, batch, expert); with `raw` also the shard's
 // per-(batch, expert) totals.
@@ -327,7 +387,8 @@ cudaError_t launch_dispatch_count(const int* idx, const Shape& s, const Workspac
 // and the gather; needs launch_dispatch_count's histogram in ws.
 cudaError_t launch_dispatch_finish(const void* x, const int* idx, const float* w, const Shape& s,
                                    const Workspace& ws, const GemmScales& sc, const int* slot_base, int* counts,
-                                   int* token_ids, float* token_weights, void* a_rows, cudaStream_t st) {
+                                   int* token_ids, float* token_weights, void* a_rows, cudaStream_t st,
+                                   bool skip_gather) {
     if (s.T() == 0) {
         cudaError_t e = cudaMemsetAsync(ws.expert_rows, 0, sizeof(int) * s.E, st);
         if (e == cudaSuccess) e = cudaMemsetAsync(ws.expert_start, 0, sizeof(int) * s.E, st);
@@ -339,25 +400,30 @@ cudaError_t launch_dispatch_finish(const void* x, const int* idx, const float* w
                                             ws.chunk_base, counts, ws.row_base, ws.expert_rows, ws.expert_start);
     dispatch_assign_kernel<<<grid, kThreads, 0, st>>>(idx, w, s.N, s.k, s.E, s.cap, s.chunks(), ws.chunk_base,
                                                       slot_base, token_ids, token_weights, ws.route_slot);
+    return skip_gather ? cudaGetLastError()
+                       : launch_dispatch_gather(x, s, ws, sc, counts, token_ids, GatherDst{{a_rows}, {ws.a_scale}}, st);
+}
+
+// The gather alone: every kept slot's token row (quantised for the 8-bit
+// formats) into its destination row.
+cudaError_t launch_dispatch_gather(const void* x, const Shape& s, const Workspace& ws, const GemmScales& sc,
+                                   const int* counts, const int* token_ids, const GatherDst& gd, cudaStream_t st) {
     // 16-bit activations: rows of d elements = d/8 16-byte vectors.
     const int64_t slots = (int64_t)s.B * s.E * s.cap;
     const unsigned gblocks = (unsigned)((slots + kWarps - 1) / kWarps);
     if (slots > 0 && s.dtype == MOE_DTYPE_FP8_BLOCK)
         dispatch_gather_fp8_kernel<<<gblocks, kThreads, 0, st>>>(
-            (const __nv_bfloat16*)x, counts, token_ids, ws.row_base, ws.expert_start, s.N, s.E, s.B, s.cap, s.d,
-            (uint8_t*)a_rows, ws.a_scale);
+            (const __nv_bfloat16*)x, counts, token_ids, ws.row_base, ws.expert_start, s.N, s.E, s.B, s.cap, s.d, gd);
     else if (slots > 0 && s.dtype == MOE_DTYPE_INT8_CHANNEL)
         dispatch_gather_q8tok_kernel<<<gblocks, kThreads, 0, st>>>((const uint4*)x, counts, token_ids, ws.row_base,
-                                                                   ws.expert_start, s.N, s.E, s.B, s.cap, s.d / 8,
-                                                                   (uint2*)a_rows, ws.a_scale);
+                                                                   ws.expert_start, s.N, s.E, s.B, s.cap, s.d / 8, gd);
     else if (slots > 0 && s.dtype == MOE_DTYPE_INT8)
         dispatch_gather_q8_kernel<<<gblocks, kThreads, 0, st>>>((const uint4*)x, counts, token_ids, ws.row_base,
                                                                 ws.expert_start, s.N, s.E, s.B, s.cap, s.d / 8,
-                                                                sc.s_in, (uint2*)a_rows);
+                                                                sc.s_in, gd);
     else if (slots > 0)
         dispatch_gather_kernel<<<gblocks, kThreads, 0, st>>>((const uint4*)x, counts, token_ids, ws.row_base,
-                                                             ws.expert_start, s.N, s.E, s.B, s.cap, s.d / 8,
-                                                             (uint4*)a_rows);
+                                                             ws.expert_start, s.N, s.E, s.B, s.cap, s.d / 8, gd);
     return cudaGetLastError();
 }
 
@@ -366,7 +432,7 @@ cudaError_t launch_dispatch(const void* x, const int* idx, const float* w, const
                             float* token_weights, void* a_rows, cudaStream_t st) {
     cudaError_t e = launch_dispatch_count(idx, s, ws, counts, nullptr, st);
     if (e != cudaSuccess) return e;
-    return launch_dispatch_finish(x, idx, w, s, ws, sc, nullptr, counts, token_ids, token_weights, a_rows, st);
+    return launch_dispatch_finish(x, idx, w, s, ws, sc, nullptr, counts, token_ids, token_weights, a_rows, st, false);
 }
 
 }  // namespace moe

@@ -408,7 +408,7 @@ int enqueue_route(const MoEArgs* a, const MoeDims* dims, const Shape& s, const W
             "dispatch (count)");
     MOE_TRY(launch_dispatch_finish(a->input, a->selected_expert_indices, a->selected_expert_weights, s, ws,
                                    scales_of(a, s), dims->slot_base, a->expert_counts, a->expert_token_ids,
-                                   a->expert_token_weights, fb.a_rows, stream),
+                                   a->expert_token_weights, fb.a_rows, stream, dims->skip_gather != 0),
             "dispatch");
     return MOE_OK;
 }
@@ -558,7 +558,7 @@ extern "C" int moe_stage_route_finish(const MoEArgs* a, const MoeDims* dims, cud
     const FfnBuffers fb = ffn_buffers(a, s);
     MOE_TRY(launch_dispatch_finish(a->input, a->selected_expert_indices, a->selected_expert_weights, s, ws,
                                    scales_of(a, s), dims->slot_base, a->expert_counts, a->expert_token_ids,
-                                   a->expert_token_weights, fb.a_rows, stream),
+                                   a->expert_token_weights, fb.a_rows, stream, dims->skip_gather != 0),
             "dispatch");
     return MOE_OK;
 }
@@ -680,6 +680,88 @@ extern "C" int moe_stage_expert_ffn_peer(const MoEArgs* a, const MoeDims* dims, 
     if (!group_out_rank) { set_error("moe_stage_expert_ffn_peer: group_out_rank is null"); return MOE_ERR_INVALID_ARG; }
     return stage_ffn(a, dims, group_rows, group_start, group_expert, group_out_rank, group_out_row, num_groups,
                      rows_capacity, out_bases, num_bases, stream);
+}
+
+extern "C" int moe_ep_plan(const int* table, int world, int rank, int num_experts, int* plan, cudaStream_t stream) {
+    if (!table || !plan || world < 1 || world > kMaxPeers || rank < 0 || rank >= world || num_experts < 1 ||
+        num_experts % world != 0 || num_experts > kMaxGroups) {
+        set_error("moe_ep_plan: bad arguments (world %d, rank %d, experts %d)", world, rank, num_experts);
+        return MOE_ERR_INVALID_ARG;
+    }
+    MOE_TRY(launch_ep_plan(table, world, num_experts, rank, plan, stream), "ep plan");
+    return MOE_OK;
+}
+
+extern "C" int moe_stage_dispatch_peer(const MoEArgs* a, const MoeDims* dims, const int* plan,
+                                       void* const* row_bases, float* const* scale_bases, int num_bases,
+                                       cudaStream_t stream) {
+    Shape s;
+    Workspace ws;
+    const int rc = route_stage_setup(a, dims, "moe_stage_dispatch_peer", &s, &ws);
+    if (rc != MOE_OK) return rc;
+    const bool scaled = s.dtype == MOE_DTYPE_FP8_BLOCK || s.dtype == MOE_DTYPE_INT8_CHANNEL;
+    if (!plan || !row_bases || num_bases < 1 || num_bases > kMaxPeers || (scaled && !scale_bases)) {
+        set_error("moe_stage_dispatch_peer: plan / bases missing or more than %d peers", kMaxPeers);
+        return MOE_ERR_INVALID_ARG;
+    }
+    GatherDst gd;
+    for (int r = 0; r < num_bases; ++r) {
+        gd.rows[r] = row_bases[r];
+        gd.scales[r] = scaled ? scale_bases[r] : nullptr;
+    }
+    gd.rank = plan;
+    gd.row0 = plan + s.E;
+    MOE_TRY(launch_dispatch_gather(a->input, s, ws, scales_of(a, s), a->expert_counts, a->expert_token_ids, gd,
+                                   stream),
+            "dispatch (peer gather)");
+    return MOE_OK;
+}
+
+extern "C" int moe_stage_expert_ffn_planned(const MoEArgs* a, const MoeDims* dims, const int* plan, int num_groups,
+                                            int64_t rows_capacity, float* const* out_bases, int num_bases,
+                                            cudaStream_t stream) {
+    if (!dims || !a || !plan || !out_bases || num_bases < 1 || num_bases > kMaxPeers || num_groups < 0 ||
+        num_groups > kMaxGroups || rows_capacity < 0 || rows_capacity >= ((int64_t)1 << 31)) {
+        set_error("moe_stage_expert_ffn_planned: bad arguments");
+        return MOE_ERR_INVALID_ARG;
+    }
+    MoeDims fd = *dims;
+    fd.num_experts = 8;
+    fd.top_k = 1;
+    fd.num_batches = 0;
+    Shape s;
+    int rc = make_shape(&fd, &s);
+    if (rc != MOE_OK) return rc;
+    s.E = dims->num_experts;
+    const FfnBuffers fb = ffn_buffers(a, s);
+    if (!fb.a_rows || !fb.h_rows || !fb.wg || !fb.wu || !fb.wd || !a->hidden_mlp_layer_2_out) {
+        set_error("moe_stage_expert_ffn_planned: a weight or row buffer of MoEArgs is null");
+        return MOE_ERR_INVALID_ARG;
+    }
+    DeviceState* st = nullptr;
+    int dev = 0;
+    rc = device_state(&st, &dev);
+    if (rc != MOE_OK) return rc;
+    Workspace ws;
+    rc = resolve_workspace(*st, dev, dims, s, &ws, /*header_only=*/true);
+    if (rc != MOE_OK) return rc;
+    if (num_groups == 0 || rows_capacity == 0) return MOE_OK;
+    const int E = num_groups;   // plan arrays are E long
+    GroupTable gt{plan + 2 * E, plan + 3 * E, plan + 4 * E, num_groups, rows_capacity};
+    gt.redirect.rank = plan + 5 * E;
+    gt.redirect.row0 = plan + 6 * E;
+    for (int r = 0; r < num_bases; ++r) gt.redirect.bases[r] = out_bases[r];
+    float* h_scale = nullptr;
+    if (s.dtype == MOE_DTYPE_FP8_BLOCK || s.dtype == MOE_DTYPE_INT8_CHANNEL) {
+        if (!dims->act_scale || !dims->scratch ||
+            dims->scratch_bytes < workspace_header_bytes() + ffn_h_scale_bytes(s, rows_capacity)) {
+            set_error("moe_stage_expert_ffn_planned: FP8_BLOCK / INT8_CHANNEL need MoeDims.act_scale and a scratch "
+                      "of moe_ffn_scratch_bytes()");
+            return MOE_ERR_INVALID_ARG;
+        }
+        h_scale = reinterpret_cast<float*>(static_cast<uint8_t*>(dims->scratch) + workspace_header_bytes());
+    }
+    return enqueue_ffn(a, dims, s, gt, ws.status, dims->act_scale, h_scale, st->num_sms, stream);
 }
 
 extern "C" int moe_stage_combine(const MoEArgs* a, const MoeDims* dims, cudaStream_t stream) {

@@ -71,6 +71,17 @@ struct OutRedirect {
     float* bases[kMaxPeers] = {};
 };
 
+// Destination of the gathered rows: the local buffers (rows[0], scales[0],
+// row = expert_start[e] + ...) or, under expert parallelism over peer memory,
+// expert e's owner: rows[rank[e]] / scales[rank[e]] from row row0[e] + the
+// (batch, slot) offset on.  rank / row0 are device arrays of E.
+struct GatherDst {
+    void* rows[kMaxPeers] = {};
+    float* scales[kMaxPeers] = {};
+    const int* rank = nullptr;
+    const int* row0 = nullptr;
+};
+
 struct GroupTable {
     const int* rows;
     const int* start;
@@ -105,7 +116,11 @@ cudaError_t launch_dispatch_count(const int* idx, const Shape& s, const Workspac
                                   cudaStream_t st);
 cudaError_t launch_dispatch_finish(const void* x, const int* idx, const float* w, const Shape& s,
                                    const Workspace& ws, const GemmScales& sc, const int* slot_base, int* counts,
-                                   int* token_ids, float* token_weights, void* a_rows, cudaStream_t st);
+                                   int* token_ids, float* token_weights, void* a_rows, cudaStream_t st,
+                                   bool skip_gather);
+cudaError_t launch_ep_plan(const int* table, int P, int E, int me, int* plan, cudaStream_t st);
+cudaError_t launch_dispatch_gather(const void* x, const Shape& s, const Workspace& ws, const GemmScales& sc,
+                                   const int* counts, const int* token_ids, const GatherDst& gd, cudaStream_t st);
 // expert_gemm.cu: grouped tcgen05 GEMMs.
 cudaError_t launch_expert_up_gate(const void* a_rows, const void* w_gate, const void* w_up,
                                   const Shape& s, const GroupTable& gt, int* status, const GemmScales& sc,

@@ -245,6 +245,8 @@ class ExpertParallelLayer:
                 maps.append(q.value)
             self.peer_maps[name] = maps
         self._bar = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.table = torch.zeros(self.world, cfg.num_experts, dtype=torch.int32, device=self.device)
+        self.plan = torch.zeros(7 * cfg.num_experts, dtype=torch.int32, device=self.device)
 
     def close(self):
         """Unmaps the peers' buffers and frees this rank's (peer transport)."""
@@ -386,49 +388,27 @@ class ExpertParallelLayer:
 
     # -- one layer call -------------------------------------------------------------
     def _forward_peer(self, S, ev):
-        """Steps 3-5 over peer memory: copy-engine row copies into the owners'
-        receive buffers, a barrier, the owner FFN whose epilogue stores the
-        result rows into the senders' return buffers, a barrier."""
+        """Steps 2-5 over peer memory with no host synchronisation: the
+        kept-row table is all-gathered on the device, moe_ep_plan turns it into
+        this rank's destinations and owner row groups, the gather writes each
+        row straight into its owner's receive buffer, and after a barrier the
+        owner FFN's down-GEMM epilogue stores the results into the senders'
+        return buffers; a second barrier orders the combine."""
         torch, cfg = self.torch, self.cfg
         ch = self.chunks[0]
         sp = ctypes.c_void_p(S.cuda_stream)
-        P, E, e_loc, me = self.world, cfg.num_experts, self.e_loc, self.rank
+        P, E = self.world, cfg.num_experts
         mine = self.counts[: cfg.num_batches].sum(dim=0, dtype=torch.int32)
-        table = torch.empty(P, E, dtype=torch.int32, device=self.device)
         with torch.cuda.stream(S):
-            self.dist.all_gather_into_tensor(table, mine, group=self.group)
-        t = table.cpu().numpy().astype(np.int64)                      # [sender, expert]
-        own = t.reshape(P, P, e_loc)                                 # [sender, owner, local expert]
-        to_owner = own.sum(axis=2)                                   # rows sender -> owner
-        block_start = np.concatenate([np.zeros((P, 1), np.int64), np.cumsum(to_owner, axis=1)[:, :-1]], axis=1)
-        recv_off = np.concatenate([np.zeros((1, P), np.int64), np.cumsum(to_owner, axis=0)[:-1]], axis=0)
-        # 3. my rows for owner q -> q's receive buffer after the blocks of senders < me
-        for q in range(P):
-            n = int(to_owner[me, q])
-            if n == 0:
-                continue
-            src_row, dst_row = int(block_start[me, q]), int(recv_off[me, q])
-            check(lib.moe_memcpy_async(ctypes.c_void_p(self.peer_maps["recv_x"][q] + dst_row * self._row_bytes),
-                                       ctypes.c_void_p(ch.send_x.data_ptr() + src_row * self._row_bytes),
-                                       n * self._row_bytes, sp))
-            if self.n_scale:
-                check(lib.moe_memcpy_async(
-                    ctypes.c_void_p(self.peer_maps["recv_scale"][q] + dst_row * self._scale_bytes),
-                    ctypes.c_void_p(ch.send_scale.data_ptr() + src_row * self._scale_bytes),
-                    n * self._scale_bytes, sp))
+            self.dist.all_gather_into_tensor(self.table, mine, group=self.group)
+        check(lib.moe_ep_plan(ctypes.c_void_p(self.table.data_ptr()), P, self.rank, E,
+                              ctypes.c_void_p(self.plan.data_ptr()), sp))
+        rows = (ctypes.c_void_p * P)(*self.peer_maps["recv_x"])
+        scales = (ctypes.c_void_p * P)(*self.peer_maps["recv_scale"]) if self.n_scale else None
+        check(lib.moe_stage_dispatch_peer(ctypes.byref(ch.ra), ctypes.byref(ch.dims),
+                                          ctypes.c_void_p(self.plan.data_ptr()), rows, scales, P, sp))
         self._barrier(S)
         ev("ffn")
-        # 4. owner FFN: groups (local expert j, sender s), results to s's return buffer
-        within = np.concatenate([np.zeros((P, 1), np.int64), np.cumsum(own[:, me, :], axis=1)[:, :-1]], axis=1)
-        rows, start, expert, orank, orow = [], [], [], [], []
-        for j in range(e_loc):
-            for snd in range(P):
-                rows.append(int(own[snd, me, j]))
-                start.append(int(recv_off[snd, me] + within[snd, j]))
-                expert.append(j)
-                orank.append(snd)
-                orow.append(int(block_start[snd, me] + within[snd, j]))
-        arr = [np.array(v, np.int32) for v in (rows, start, expert, orank, orow)]
         fa = self._ffn_args(ch)
         fa.per_expert_wmma_inputs = fa.per_expert_wmma_inputs_int8 = fa.per_expert_wmma_inputs_fp8 = None
         self._set_rows(fa, _Ptr(self.peer_local["recv_x"]), ch.h)
@@ -437,13 +417,18 @@ class ExpertParallelLayer:
         if self.n_scale:
             fd.act_scale = self.peer_local["recv_scale"]
         bases = (ctypes.c_void_p * P)(*self.peer_maps["back_y"])
-        check(lib.moe_stage_expert_ffn_peer(ctypes.byref(fa), ctypes.byref(fd), *(a.ctypes.data for a in arr[:3]),
-                                            arr[3].ctypes.data, arr[4].ctypes.data, len(rows), self.recv_cap, bases,
-                                            P, sp))
+        check(lib.moe_stage_expert_ffn_planned(ctypes.byref(fa), ctypes.byref(fd),
+                                               ctypes.c_void_p(self.plan.data_ptr()), E, self.recv_cap, bases, P, sp))
         ev("ffn")
         self._barrier(S)
-        self._keep = (fa, fd, arr, bases)
-        return t, int(to_owner[:, me].sum())
+        self._keep = (fa, fd, rows, scales, bases)
+
+    def owner_rows(self) -> int:
+        """Rows this rank's experts processed in the last call (synchronises)."""
+        if self.transport == "peer":
+            t = self.table.cpu().numpy()
+            return int(t[:, self.rank * self.e_loc:(self.rank + 1) * self.e_loc].sum())
+        return self.last_plan["owner_rows"]
 
     def forward(self, stream=None, timing=None):
         """One layer call.  `timing` (optional dict) receives torch.cuda.Event
@@ -467,6 +452,7 @@ class ExpertParallelLayer:
             ch.dims = self.chunk_cfg.dims(bias, ch.out16.data_ptr(), ch.scratch.data_ptr(), ch.scratch.numel())
             if self.n_scale:
                 ch.dims.act_scale = ch.send_scale.data_ptr()
+            ch.dims.skip_gather = 1 if self.transport == "peer" else 0
             ch.ra = self._route_args(ch)
             if self.global_batch:
                 # phase 1, then every rank's totals; slot_base = sum over the lower ranks
@@ -483,11 +469,10 @@ class ExpertParallelLayer:
         if self.transport == "peer":
             ch = self.chunks[0]
             ch.ra.hidden_mlp_layer_2_out = self.peer_local["back_y"]   # combine reads the peer-written rows
-            table_h, owner_rows = self._forward_peer(S, ev)
+            self._forward_peer(S, ev)
             ev("combine")
             check(lib.moe_stage_combine(ctypes.byref(ch.ra), ctypes.byref(ch.dims), sp))
             ev("end")
-            self.last_plan = {"table": table_h, "owner_rows": owner_rows}
             return self.out
         nc = self.n_chunks
         mine = self.counts[: cfg.num_batches].view(nc, -1, cfg.num_experts).sum(dim=1, dtype=torch.int32)
