@@ -16,7 +16,9 @@ from pathlib import Path
 import numpy as np
 
 _PKG = Path(__file__).resolve().parent
-LIB_PATH = _PKG / "libsparsemoe_b200.so"
+# the in-tree build; SPARSEMOE_B200_LIB may name another build of the same library
+LIB_PATH = Path(os.environ["SPARSEMOE_B200_LIB"]) if os.environ.get("SPARSEMOE_B200_LIB") else \
+    _PKG / "libsparsemoe_b200.so"
 
 MOE_OK = 0
 MOE_ERR_INVALID_ARG = -1

@@ -9,15 +9,18 @@
 // the epilogue warps into register accumulators with one packed f32x2 FMA per
 // two columns: acc += P_kb * (s_a * s_w).
 //
-// Warp roles (320 threads, one persistent CTA per SM):
+// Warp roles (384 threads = 3 warpgroups, one persistent CTA per SM):
 //   warp 0      TMA producer: A 128 rows x 128 B (one K block, K-major, 128B
 //               swizzle) + B 128 K-rows x 256 columns from the row-major
 //               [K, N] e4m3 weights (MN-major, 128B swizzle); 4-stage ring.
 //   warp 1      MMA issuer: per K block 4 x tcgen05.mma kind::f8f6f4 M128
 //               N256 K32 into TMEM partial P[kb & 1].
-//   warps 2-9   promotion + epilogue: warp w reads TMEM lanes 32*(w%4).. and
-//               half (w-2)/4 of the columns (16-column TMEM loads keep the
-//               128 accumulators within the 168 registers a thread gets):
+//   warps 2-3   idle (they complete warpgroup 0, which hands its registers
+//               to the promotion warpgroups through setmaxnreg).
+//   warps 4-11  promotion + epilogue: warp w reads TMEM lanes 32*(w%4).. and
+//               half (w-4)/4 of the columns, four 16-column TMEM loads in
+//               flight per wait (232 registers per thread: 128 accumulators
+//               plus 64 loaded values):
 //                 up/gate: gate cols [64h, 64h+64) and up cols 128+[64h, ..)
 //                 of the same 64 output features, so SwiGLU is local; the h
 //                 row block of 128 features (the tile) gets its 1x128 scale
@@ -56,8 +59,15 @@ using namespace sm100;
 
 constexpr int kBM = 128;
 constexpr int kStages = 4;
-constexpr int kThreads = 320;
+// 12 warps = 3 warpgroups: warpgroup 0 (TMA, MMA, two idle warps) gives up
+// registers with setmaxnreg, the promotion warpgroups 1-2 take them (40 + 2 x
+// 232 = 3 x 168 registers per thread, the launch's total), so that a
+// promotion thread holds its 128 accumulators plus 4 TMEM loads in flight.
+constexpr int kThreads = 384;
 constexpr int kPromoWarps = 8;
+constexpr int kPromoWarp0 = 4;
+constexpr int kRegsCtrl = 40, kRegsPromo = 232;
+static_assert(kRegsCtrl + 2 * kRegsPromo == 3 * 168, "register split must match the launch total");
 constexpr int kABytes = kBM * 128;
 constexpr int kBBytes = 128 * 256;
 constexpr int kStageBytes = kABytes + kBBytes;
@@ -164,74 +174,80 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tmem_base = *tmem_slot;
     const int total = s_pre[p.G];
     const int kblocks = p.K / 128;
+    // warp-uniform warpgroup index (the shuffle makes the uniformity explicit)
+    const int wgroup = __shfl_sync(0xffffffffu, (int)(threadIdx.x >> 7), 0);
 
-    if (warp == 0) {
-        if (lane == 0) {
-            int s = 0;
-            uint32_t ph = 0;
-            for (int t = blockIdx.x; t < total; t += gridDim.x) {
-                int g, m, n;
-                decode_tile(t, s_pre, s_rows, p.G, g, m, n);
-                const int a_row = s_start[g] + m * kBM;
-                const int b_row = s_wt[g] * p.K;
-                for (int kb = 0; kb < kblocks; ++kb) {
-                    if (!mbar_wait(&empty[s], ph ^ 1u, p.status, kDevErrTimeout)) goto producer_done;
-                    mbar_arrive_expect_tx(&full[s], kStageBytes);
-                    uint8_t* a_dst = sA + s * kABytes;
-                    uint8_t* b_dst = sB + s * kBBytes;
-                    tma_load_2d(a_dst, &tmA, &full[s], kb * 128, a_row);
-                    if (kMode == 0) {
-                        tma_load_2d(b_dst, &tmB0, &full[s], n * 128, b_row + kb * 128);
-                        tma_load_2d(b_dst + kChunkBytes, &tmB1, &full[s], n * 128, b_row + kb * 128);
-                    } else {
-                        tma_load_2d(b_dst, &tmB0, &full[s], n * 256, b_row + kb * 128);
-                        tma_load_2d(b_dst + kChunkBytes, &tmB0, &full[s], n * 256 + 128, b_row + kb * 128);
+    if (wgroup == 0) {
+        asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsCtrl));
+        if (warp == 0) {
+            if (lane == 0) {
+                int s = 0;
+                uint32_t ph = 0;
+                for (int t = blockIdx.x; t < total; t += gridDim.x) {
+                    int g, m, n;
+                    decode_tile(t, s_pre, s_rows, p.G, g, m, n);
+                    const int a_row = s_start[g] + m * kBM;
+                    const int b_row = s_wt[g] * p.K;
+                    for (int kb = 0; kb < kblocks; ++kb) {
+                        if (!mbar_wait(&empty[s], ph ^ 1u, p.status, kDevErrTimeout)) goto producer_done;
+                        mbar_arrive_expect_tx(&full[s], kStageBytes);
+                        uint8_t* a_dst = sA + s * kABytes;
+                        uint8_t* b_dst = sB + s * kBBytes;
+                        tma_load_2d(a_dst, &tmA, &full[s], kb * 128, a_row);
+                        if (kMode == 0) {
+                            tma_load_2d(b_dst, &tmB0, &full[s], n * 128, b_row + kb * 128);
+                            tma_load_2d(b_dst + kChunkBytes, &tmB1, &full[s], n * 128, b_row + kb * 128);
+                        } else {
+                            tma_load_2d(b_dst, &tmB0, &full[s], n * 256, b_row + kb * 128);
+                            tma_load_2d(b_dst + kChunkBytes, &tmB0, &full[s], n * 256 + 128, b_row + kb * 128);
+                        }
+                        if (++s == kStages) { s = 0; ph ^= 1u; }
                     }
-                    if (++s == kStages) { s = 0; ph ^= 1u; }
                 }
+            producer_done:;
             }
-        producer_done:;
-        }
-    } else if (warp == 1) {
-        if (lane == 0) {
-            int s = 0, pb = 0;
-            uint32_t ph = 0, pph = 0;
-            bool ok = true;
-            // kWhole: one TMEM accumulator over all K blocks (int8 up/gate)
-            constexpr bool kWhole = kKind == 1 && kMode == 0;
-            for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-                for (int kb = 0; kb < kblocks; ++kb) {
-                    if (((!kWhole || kb == 0) && !mbar_wait(&pempty[pb], pph ^ 1u, p.status, kDevErrTimeout)) ||
-                        !mbar_wait(&full[s], ph, p.status, kDevErrTimeout)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-                    const uint32_t a_base = smem_u32(sA + s * kABytes);
-                    const uint32_t b_base = smem_u32(sB + s * kBBytes);
-                    const uint32_t d_tmem = tmem_base + pb * 256;
+        } else if (warp == 1) {
+            if (lane == 0) {
+                int s = 0, pb = 0;
+                uint32_t ph = 0, pph = 0;
+                bool ok = true;
+                // kWhole: one TMEM accumulator over all K blocks (int8 up/gate)
+                constexpr bool kWhole = kKind == 1 && kMode == 0;
+                for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+                    for (int kb = 0; kb < kblocks; ++kb) {
+                        if (((!kWhole || kb == 0) && !mbar_wait(&pempty[pb], pph ^ 1u, p.status, kDevErrTimeout)) ||
+                            !mbar_wait(&full[s], ph, p.status, kDevErrTimeout)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint32_t a_base = smem_u32(sA + s * kABytes);
+                        const uint32_t b_base = smem_u32(sB + s * kBBytes);
+                        const uint32_t d_tmem = tmem_base + pb * 256;
 #pragma unroll
-                    for (int kk = 0; kk < 4; ++kk) {
-                        const uint64_t adesc = smem_desc_sw128(a_base + kk * 32, 16, 1024);
-                        const uint64_t bdesc = smem_desc_sw128(b_base + kk * 32 * 128, kChunkBytes, 1024);
-                        const uint32_t accum = (kk != 0 || (kWhole && kb != 0)) ? 1u : 0u;
-                        if (kKind == 0) mma_f8_ss(d_tmem, adesc, bdesc, p.idesc, accum);
-                        else mma_i8_ss(d_tmem, adesc, bdesc, p.idesc, accum);
-                    }
-                    mma_commit(&empty[s]);
-                    if (++s == kStages) { s = 0; ph ^= 1u; }
-                    if (!kWhole || kb == kblocks - 1) {
-                        mma_commit(&pfull[pb]);
-                        pb ^= 1;
-                        if (pb == 0) pph ^= 1u;
+                        for (int kk = 0; kk < 4; ++kk) {
+                            const uint64_t adesc = smem_desc_sw128(a_base + kk * 32, 16, 1024);
+                            const uint64_t bdesc = smem_desc_sw128(b_base + kk * 32 * 128, kChunkBytes, 1024);
+                            const uint32_t accum = (kk != 0 || (kWhole && kb != 0)) ? 1u : 0u;
+                            if (kKind == 0) mma_f8_ss(d_tmem, adesc, bdesc, p.idesc, accum);
+                            else mma_i8_ss(d_tmem, adesc, bdesc, p.idesc, accum);
+                        }
+                        mma_commit(&empty[s]);
+                        if (++s == kStages) { s = 0; ph ^= 1u; }
+                        if (!kWhole || kb == kblocks - 1) {
+                            mma_commit(&pfull[pb]);
+                            pb ^= 1;
+                            if (pb == 0) pph ^= 1u;
+                        }
                     }
                 }
             }
-        }
+        }   // warps 2, 3: idle
     } else {
-        // ---------------- promotion + epilogue (warps 2..9) ----------------
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsPromo));
+        // ---------------- promotion + epilogue (warps 4..11) ----------------
         const int q = warp & 3;
-        const int half = (warp - 2) >> 2;
+        const int half = (warp - kPromoWarp0) >> 2;
         const int row_in_tile = q * 32 + lane;
         const int nkb = kblocks;
         const int nblk = p.out_ld / 128;
@@ -299,20 +315,28 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tc_fence_after();
                     const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + pb * 256;
                     const float sc0 = sa * sw0, sc1 = sa * sw1;
+                    // two rounds of four 16-column TMEM loads in flight, one wait each
+                    auto pcol = [&](int piece) {
+                        return kMode == 0 ? (piece < 4 ? 64 * half + 16 * piece : 128 + 64 * half + 16 * (piece - 4))
+                                          : 128 * half + 16 * piece;
+                    };
 #pragma unroll
-                    for (int piece = 0; piece < 8; ++piece) {
-                        uint32_t r[16];
-                        const int col = kMode == 0 ? (piece < 4 ? 64 * half + 16 * piece : 128 + 64 * half + 16 * (piece - 4))
-                                                   : 128 * half + 16 * piece;
-                        tmem_ld_32x32b_x16(tbase + col, r);
+                    for (int rnd = 0; rnd < 2; ++rnd) {
+                        uint32_t r4[4][16];
+#pragma unroll
+                        for (int k4 = 0; k4 < 4; ++k4) tmem_ld_32x32b_x16(tbase + pcol(4 * rnd + k4), r4[k4]);
                         tmem_wait_ld();
-                        if (piece == 7) { tc_fence_before(); mbar_arrive(&pempty[pb]); }
-                        const float sc = (kMode == 0 && piece >= 4) ? sc1 : sc0;
+                        if (rnd == 1) { tc_fence_before(); mbar_arrive(&pempty[pb]); }
+                        const float sc = (kMode == 0 && rnd == 1) ? sc1 : sc0;
 #pragma unroll
-                        for (int i = 0; i < 16; i += 2) {
-                            const float p0 = kKind == 0 ? __uint_as_float(r[i]) : (float)(int)r[i];
-                            const float p1 = kKind == 0 ? __uint_as_float(r[i + 1]) : (float)(int)r[i + 1];
-                            ffma2(acc[16 * piece + i], acc[16 * piece + i + 1], p0, p1, sc);
+                        for (int k4 = 0; k4 < 4; ++k4) {
+                            const int piece = 4 * rnd + k4;
+#pragma unroll
+                            for (int i = 0; i < 16; i += 2) {
+                                const float p0 = kKind == 0 ? __uint_as_float(r4[k4][i]) : (float)(int)r4[k4][i];
+                                const float p1 = kKind == 0 ? __uint_as_float(r4[k4][i + 1]) : (float)(int)r4[k4][i + 1];
+                                ffma2(acc[16 * piece + i], acc[16 * piece + i + 1], p0, p1, sc);
+                            }
                         }
                     }
                     pb ^= 1;
@@ -369,7 +393,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int nrows = s_rows[g] - warp_row0;
                 float* y = down_rows(p.red, reinterpret_cast<float*>(p.out), g, s_start[g], p.out_ld) +
                            (int64_t)warp_row0 * p.out_ld + n * 256 + 128 * half;
-                float4* stage = sStage + (warp - 2) * 128;
+                float4* stage = sStage + (warp - kPromoWarp0) * 128;
 #pragma unroll
                 for (int c = 0; c < 8; ++c) warp_store_rows16(stage, acc + 16 * c, y + 16 * c, p.out_ld, nrows, lane);
             }

@@ -132,7 +132,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     w4_gemm_kernel(const __grid_constant__ W4Maps mp, const W4Params p) {
     using TL = Tile<kBM>;
     constexpr int kBN = TL::BN;
-    constexpr int kABytes = TL::kABytes, kBBytes = TL::kBBytes, kPBytes = TL::kPBytes, kSZBytes = TL::kSZBytes;
+    constexpr int kABytes = TL::kABytes, kBBytes = TL::kBBytes, kPBytes = TL::kPBytes;
     constexpr int kRaw = TL::kRaw, kBSt = TL::kBSt, kRawBytes = TL::kRawBytes;
     extern __shared__ uint8_t smem_raw[];
     __shared__ int s_pre[kMaxGroups + 1];
