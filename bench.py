@@ -412,7 +412,10 @@ def run_ep(args, cfg, ws, rank, local, dev):
     from sparsemoe_b200.ep import ExpertParallelLayer
     import sparsemoe_b200 as sm
     glob = args.config in GLOBAL_BATCH
-    layer = ExpertParallelLayer(cfg, dev, chunks=args.ep_chunks, global_batch=glob, transport=args.ep_transport)
+    # the DeepSeek-V3 workloads own experts strided, so the Zipf-popular low-index experts spread over the ranks
+    placement = "strided" if glob and args.ep_transport == "peer" else "contiguous"
+    layer = ExpertParallelLayer(cfg, dev, chunks=args.ep_chunks, global_batch=glob, transport=args.ep_transport,
+                                placement=placement)
     if cfg.int8:
         # the reference's per-tensor int8 format: host generator + host quantiser (all experts; each
         # rank keeps its own), this rank's tokens
@@ -498,7 +501,8 @@ def run_ep(args, cfg, ws, rank, local, dev):
                                      f"NCCL all-to-all dispatch/return on a second stream, {layer.n_chunks} "
                                      f"pipelined batch chunks; ")
                                   + f"{cfg.T} tokens per GPU"
-                                  + (f"; each batch split over the {ws} ranks, global CAP {layer.cap})"
+                                  + (f"; each batch split over the {ws} ranks, global CAP {layer.cap}, "
+                                     f"{layer.placement} expert ownership)"
                                      if glob else ", per-rank batches)")},
         "roofline": {"bound": "tensor", "achieved": ach_min, "peak": peak_tf, "unit": "TFLOP/s",
                      "frac": ach_min / peak_tf, "traffic": None,

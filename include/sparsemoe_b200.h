@@ -167,12 +167,16 @@ size_t moe_ffn_scratch_bytes(const MoeDims* dims, int64_t rows_capacity);
 // Expert parallelism over peer memory without host synchronisation.
 // moe_ep_plan: from the all-gathered kept-row table [world, E] (device int32,
 // rows each rank routes to each expert), writes the device plan of this rank
-// (7*E int32): per expert e the owner rank and the first row of this rank's
+// (7*E int32) for contiguous ownership (strided == 0: rank q holds experts
+// q*E/world .. (q+1)*E/world - 1) or strided ownership (rank q holds experts
+// q, q + world, q + 2*world, ...; local index e / world): per expert e the
+// owner rank and the first row of this rank's
 // block in the owner's receive buffer, then the owner-side row groups
 // (local expert j x sender s, g = j*world + s): rows, start row in the
 // receive buffer, local expert, sender, and the first row of the group's
 // results in the sender's return buffer.
-int moe_ep_plan(const int* table, int world, int rank, int num_experts, int* plan, cudaStream_t stream);
+int moe_ep_plan(const int* table, int world, int rank, int num_experts, int strided, int* plan,
+                cudaStream_t stream);
 // Gathers this rank's kept rows (quantised for the 8-bit formats, with their
 // row scales) straight into the owners' receive buffers row_bases[owner]
 // (scale_bases[owner]) as the plan places them; the routing tables come from

@@ -114,7 +114,7 @@ def _load() -> ctypes.CDLL:
         "moe_ffn_scratch_bytes": (ctypes.c_size_t, [ctypes.POINTER(MoeDims), ctypes.c_int64]),
         "moe_stage_expert_ffn_peer": (ctypes.c_int, [ctypes.POINTER(MoEArgs), ctypes.POINTER(MoeDims), _p, _p, _p,
                                                       _p, _p, ctypes.c_int, ctypes.c_int64, _p, ctypes.c_int, _p]),
-        "moe_ep_plan": (ctypes.c_int, [_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, _p, _p]),
+        "moe_ep_plan": (ctypes.c_int, [_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _p, _p]),
         "moe_stage_dispatch_peer": (ctypes.c_int, [ctypes.POINTER(MoEArgs), ctypes.POINTER(MoeDims), _p, _p, _p,
                                                     ctypes.c_int, _p]),
         "moe_stage_expert_ffn_planned": (ctypes.c_int, [ctypes.POINTER(MoEArgs), ctypes.POINTER(MoeDims), _p,

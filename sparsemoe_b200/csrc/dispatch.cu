@@ -323,14 +323,17 @@ __global__ void __launch_bounds__(kThreads) dispatch_gather_q8tok_kernel(
 }
 
 // Expert-parallel plan of rank `me` from the kept-row table [P, E] (one CTA).
-// Layout (7E ints): owner[E] | row0[E] | g_rows[G] | g_start[G] | g_expert[G] |
-// g_sender[G] | g_out_row[G], G = E, g = j * P + s.
+// Ownership: contiguous (expert e on rank e / (E/P), local index e % (E/P)) or
+// strided (rank e % P, local index e / P -- spreads popular low-index experts
+// over the ranks).  Layout (7E ints): owner[E] | row0[E] | g_rows[G] |
+// g_start[G] | g_expert[G] | g_sender[G] | g_out_row[G], G = E, g = j * P + s.
 __global__ void __launch_bounds__(256) ep_plan_kernel(const int* __restrict__ table, int P, int E, int me,
-                                                      int* __restrict__ plan) {
+                                                      int strided, int* __restrict__ plan) {
     const int el = E / P;
+    auto gexp = [&](int q, int j) { return strided ? j * P + q : q * el + j; };   // owner q's j-th expert
     auto to_owner = [&](int s, int q) {
         int n = 0;
-        for (int j = 0; j < el; ++j) n += table[s * E + q * el + j];
+        for (int j = 0; j < el; ++j) n += table[s * E + gexp(q, j)];
         return n;
     };
     auto recv_off = [&](int s, int q) {   // rows of senders < s in q's receive buffer
@@ -339,30 +342,31 @@ __global__ void __launch_bounds__(256) ep_plan_kernel(const int* __restrict__ ta
         return n;
     };
     for (int e = threadIdx.x; e < E; e += blockDim.x) {
-        const int q = e / el;
+        const int q = strided ? e % P : e / el, lj = strided ? e / P : e % el;
         int within = 0;
-        for (int e2 = q * el; e2 < e; ++e2) within += table[me * E + e2];
+        for (int j2 = 0; j2 < lj; ++j2) within += table[me * E + gexp(q, j2)];
         plan[e] = q;
         plan[E + e] = recv_off(me, q) + within;
     }
     for (int g = threadIdx.x; g < E; g += blockDim.x) {
         const int j = g / P, s = g - j * P;
+        const int ge = gexp(me, j);
         int within = 0;
-        for (int j2 = 0; j2 < j; ++j2) within += table[s * E + me * el + j2];
-        int block_start = 0;   // first row of owner me's experts in sender s's dense layout
-        for (int e2 = 0; e2 < me * el; ++e2) block_start += table[s * E + e2];
-        plan[2 * E + g] = table[s * E + me * el + j];
+        for (int j2 = 0; j2 < j; ++j2) within += table[s * E + gexp(me, j2)];
+        int start_in_sender = 0;   // first row of expert ge in sender s's dense expert-major layout
+        for (int e2 = 0; e2 < ge; ++e2) start_in_sender += table[s * E + e2];
+        plan[2 * E + g] = table[s * E + ge];
         plan[3 * E + g] = recv_off(s, me) + within;
         plan[4 * E + g] = j;
         plan[5 * E + g] = s;
-        plan[6 * E + g] = block_start + within;
+        plan[6 * E + g] = start_in_sender;
     }
 }
 
 }  // namespace
 
-cudaError_t launch_ep_plan(const int* table, int P, int E, int me, int* plan, cudaStream_t st) {
-    ep_plan_kernel<<<1, 256, 0, st>>>(table, P, E, me, plan);
+cudaError_t launch_ep_plan(const int* table, int P, int E, int me, int strided, int* plan, cudaStream_t st) {
+    ep_plan_kernel<<<1, 256, 0, st>>>(table, P, E, me, strided, plan);
     return cudaGetLastError();
 }
 

@@ -682,13 +682,14 @@ extern "C" int moe_stage_expert_ffn_peer(const MoEArgs* a, const MoeDims* dims, 
                      rows_capacity, out_bases, num_bases, stream);
 }
 
-extern "C" int moe_ep_plan(const int* table, int world, int rank, int num_experts, int* plan, cudaStream_t stream) {
+extern "C" int moe_ep_plan(const int* table, int world, int rank, int num_experts, int strided, int* plan,
+                           cudaStream_t stream) {
     if (!table || !plan || world < 1 || world > kMaxPeers || rank < 0 || rank >= world || num_experts < 1 ||
         num_experts % world != 0 || num_experts > kMaxGroups) {
         set_error("moe_ep_plan: bad arguments (world %d, rank %d, experts %d)", world, rank, num_experts);
         return MOE_ERR_INVALID_ARG;
     }
-    MOE_TRY(launch_ep_plan(table, world, num_experts, rank, plan, stream), "ep plan");
+    MOE_TRY(launch_ep_plan(table, world, num_experts, rank, strided != 0, plan, stream), "ep plan");
     return MOE_OK;
 }
 

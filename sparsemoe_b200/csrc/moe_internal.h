@@ -118,7 +118,7 @@ cudaError_t launch_dispatch_finish(const void* x, const int* idx, const float* w
                                    const Workspace& ws, const GemmScales& sc, const int* slot_base, int* counts,
                                    int* token_ids, float* token_weights, void* a_rows, cudaStream_t st,
                                    bool skip_gather);
-cudaError_t launch_ep_plan(const int* table, int P, int E, int me, int* plan, cudaStream_t st);
+cudaError_t launch_ep_plan(const int* table, int P, int E, int me, int strided, int* plan, cudaStream_t st);
 cudaError_t launch_dispatch_gather(const void* x, const Shape& s, const Workspace& ws, const GemmScales& sc,
                                    const int* counts, const int* token_ids, const GatherDst& gd, cudaStream_t st);
 // expert_gemm.cu: grouped tcgen05 GEMMs.

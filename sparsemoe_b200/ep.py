@@ -28,7 +28,16 @@ Two ways to place the tokens:
   slot_base (moe_stage_route_finish).
 
 The rows travel back in f32, so the output equals the single-GPU layer's on
-the same tokens.  All weight formats run: 16-bit, per-tensor int8, 4-bit
+the same tokens.
+
+Transport: NCCL all-to-all (rows and results on a second stream), or
+(transport="peer") NVLink peer memory with no host synchronisation -- the
+kept-row table is all-gathered on the device, moe_ep_plan places every row,
+the gather writes each row into its owner's receive buffer, and the owner's
+down-GEMM epilogue stores each result row into its sender's buffer.  With the
+peer transport the experts can be owned strided (placement="strided": rank q
+holds experts q, q+P, ...), which spreads a popularity skew over low expert
+indices (the Zipf-biased routers) across the ranks.  All weight formats run: 16-bit, per-tensor int8, 4-bit
 (INT4 g128, NVFP4) with bf16 rows on the wire, and the dynamically quantised
 FP8-block / int8-per-channel formats, whose 8-bit rows travel with their row
 scales (a second all-to-all of [rows, d/128] or [rows] f32).
@@ -116,7 +125,7 @@ class ExpertParallelLayer:
     PHASES = ("route", "exchange_and_ffn", "combine")
 
     def __init__(self, cfg: LayerConfig, device, group=None, chunks: int | None = None,
-                 global_batch: bool = False, transport: str = "nccl"):
+                 global_batch: bool = False, transport: str = "nccl", placement: str = "contiguous"):
         import torch
         import torch.distributed as dist
         self.torch, self.dist = torch, dist
@@ -135,6 +144,9 @@ class ExpertParallelLayer:
         assert transport in ("nccl", "peer"), transport
         assert not (transport == "peer" and chunks > 1), "the peer transport runs as one chunk"
         self.transport = transport
+        assert placement in ("contiguous", "strided"), placement
+        assert not (placement == "strided" and transport != "peer"), "strided placement needs the peer transport"
+        self.placement = placement
         self.n_chunks = max(chunks, 1)
         if global_batch:
             # CAP of the whole batch (world shards of N tokens); cap < 0: no drop
@@ -277,7 +289,11 @@ class ExpertParallelLayer:
             return t.to(self.device)
 
         def mine(arr):
-            return arr if local else arr[self.rank * self.e_loc:(self.rank + 1) * self.e_loc]
+            if local:
+                return arr
+            if self.placement == "strided":
+                return np.ascontiguousarray(arr[self.rank::self.world])
+            return arr[self.rank * self.e_loc:(self.rank + 1) * self.e_loc]
         if cfg.T > 0:
             x = dev_t(inputs["x"])
             self.x[: cfg.T].copy_(x.view(self.x.dtype).reshape(cfg.T, cfg.d_model))
@@ -402,7 +418,7 @@ class ExpertParallelLayer:
         with torch.cuda.stream(S):
             self.dist.all_gather_into_tensor(self.table, mine, group=self.group)
         check(lib.moe_ep_plan(ctypes.c_void_p(self.table.data_ptr()), P, self.rank, E,
-                              ctypes.c_void_p(self.plan.data_ptr()), sp))
+                              int(self.placement == "strided"), ctypes.c_void_p(self.plan.data_ptr()), sp))
         rows = (ctypes.c_void_p * P)(*self.peer_maps["recv_x"])
         scales = (ctypes.c_void_p * P)(*self.peer_maps["recv_scale"]) if self.n_scale else None
         check(lib.moe_stage_dispatch_peer(ctypes.byref(ch.ra), ctypes.byref(ch.dims),
@@ -427,6 +443,8 @@ class ExpertParallelLayer:
         """Rows this rank's experts processed in the last call (synchronises)."""
         if self.transport == "peer":
             t = self.table.cpu().numpy()
+            if self.placement == "strided":
+                return int(t[:, self.rank::self.world].sum())
             return int(t[:, self.rank * self.e_loc:(self.rank + 1) * self.e_loc].sum())
         return self.last_plan["owner_rows"]
 

@@ -24,6 +24,7 @@ def _worker(rank, world, port, case, results):
                             device_id=torch.device("cuda", rank))
     B, N, d, f, E, k, cf, dtype, zipf, chunks, glob = case[:11]
     transport = case[11] if len(case) > 11 else "nccl"
+    placement = case[12] if len(case) > 12 else "contiguous"
     if glob:
         # one batch of world*N tokens; this rank holds tokens [rank*N, (rank+1)*N) of every batch
         full_cfg = sm.LayerConfig(B, N * world, d, f, E, k, cf, dtype=dtype, zipf_s=zipf,
@@ -31,7 +32,8 @@ def _worker(rank, world, port, case, results):
         full = sm.make_inputs(full_cfg, 5)
         x = full["x"].reshape(B, world, N, d)[:, rank].reshape(B * N, d)
         cfg = sm.LayerConfig(B, N, d, f, E, k, cf, dtype=dtype, zipf_s=zipf, router_f32=full_cfg.router_f32)
-        ep = ExpertParallelLayer(cfg, f"cuda:{rank}", global_batch=True, transport=transport).load({**full, "x": x})
+        ep = ExpertParallelLayer(cfg, f"cuda:{rank}", global_batch=True, transport=transport,
+                                 placement=placement).load({**full, "x": x})
         single = sm.MoeLayer(full_cfg, f"cuda:{rank}").load(full)
         rows = np.concatenate([np.arange(b * N * world + rank * N, b * N * world + (rank + 1) * N)
                                for b in range(B)])
@@ -40,7 +42,8 @@ def _worker(rank, world, port, case, results):
         full = sm.make_inputs(cfg, 5)
         mine = sm.make_inputs(cfg, 100 + rank)
         inputs = {**full, "x": mine["x"]}
-        ep = ExpertParallelLayer(cfg, f"cuda:{rank}", chunks=chunks, transport=transport).load(inputs)
+        ep = ExpertParallelLayer(cfg, f"cuda:{rank}", chunks=chunks, transport=transport,
+                                 placement=placement).load(inputs)
         single = sm.MoeLayer(cfg, f"cuda:{rank}").load(inputs)
         rows = np.arange(cfg.T)
     ep.forward()
@@ -75,6 +78,10 @@ CASES = {
     "peer_fp8_block_scales": (1, 256, 512, 256, 16, 4, 1.25, sm.DTYPE_FP8_BLOCK, 0.0, 1, False, "peer"),
     "peer_global_int4": (1, 256, 512, 256, 32, 8, 1.25, sm.DTYPE_W4A16, 1.0, 1, True, "peer"),
     "peer_global_nvfp4_drops": (1, 192, 512, 256, 16, 4, 1.0, sm.DTYPE_NVFP4, 1.2, 1, True, "peer"),
+    # strided expert ownership (rank q holds experts q, q+P, ...)
+    "peer_strided_bf16": (2, 256, 512, 512, 8, 2, 1.25, sm.DTYPE_BF16, 0.0, 1, False, "peer", "strided"),
+    "peer_strided_global_int8ch_zipf": (1, 256, 512, 256, 32, 8, 1.0, sm.DTYPE_INT8_CHANNEL, 1.0, 1, True, "peer",
+                                        "strided"),
 }
 
 
