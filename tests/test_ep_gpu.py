@@ -103,3 +103,4 @@ def test_ep_matches_single_gpu(gpu, name):
     for rank, (equal, err, idx_equal) in res.items():
         assert idx_equal, f"rank {rank}: routing differs"
         assert err < 1e-6, f"rank {rank}: max-abs-rel {err}"
+
