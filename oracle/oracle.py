@@ -8,7 +8,6 @@ from __future__ import annotations
 import ctypes
 import os
 import subprocess
-import time
 from pathlib import Path
 
 import numpy as np

@@ -431,12 +431,5 @@ cudaError_t launch_dispatch_gather(const void* x, const Shape& s, const Workspac
     return cudaGetLastError();
 }
 
-cudaError_t launch_dispatch(const void* x, const int* idx, const float* w, const Shape& s,
-                            const Workspace& ws, const GemmScales& sc, int* counts, int* token_ids,
-                            float* token_weights, void* a_rows, cudaStream_t st) {
-    cudaError_t e = launch_dispatch_count(idx, s, ws, counts, nullptr, st);
-    if (e != cudaSuccess) return e;
-    return launch_dispatch_finish(x, idx, w, s, ws, sc, nullptr, counts, token_ids, token_weights, a_rows, st, false);
-}
 
 }  // namespace moe

@@ -106,12 +106,10 @@ cudaError_t launch_router_topk(const void* x, const void* wr, const float* bias,
                                float* logits, int* idx, float* w, cudaStream_t st);
 // dispatch.cu: deterministic capacity slots + 16-byte row gather.
 // a_rows receives 16-bit rows, or int8 rows quantised with 1/s_in (int8 path).
-cudaError_t launch_dispatch(const void* x, const int* idx, const float* w, const Shape& s,
-                            const Workspace& ws, const GemmScales& sc, int* counts, int* token_ids,
-                            float* token_weights, void* a_rows, cudaStream_t st);
-// The same in two phases (expert parallelism over a split batch): route
-// histogram (+ the shard's raw per-(batch, expert) totals), then slots with
-// the earlier shards' slot_base, drops, tables and gather.
+// Two phases (a batch split over expert-parallel ranks needs the totals of
+// every shard in between): route histogram (+ the shard's raw per-(batch,
+// expert) totals), then slots with the earlier shards' slot_base, drops,
+// tables and (unless skipped) the gather.
 cudaError_t launch_dispatch_count(const int* idx, const Shape& s, const Workspace& ws, int* counts, int* raw,
                                   cudaStream_t st);
 cudaError_t launch_dispatch_finish(const void* x, const int* idx, const float* w, const Shape& s,

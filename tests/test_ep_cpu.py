@@ -5,7 +5,6 @@ stages.  The exchanged result must equal the single-process layer."""
 import os
 
 import numpy as np
-import pytest
 import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp

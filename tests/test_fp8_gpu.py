@@ -2,7 +2,6 @@
 weights with f32 scales per 128x128 block, activations and h quantised per
 1x128 block on the device, f32 accumulation with per-K-block promotion.
 Bar: routing bit-exact, output max-abs-rel 3e-2 vs the oracle's restatement."""
-import numpy as np
 import pytest
 
 import sparsemoe_b200 as sm

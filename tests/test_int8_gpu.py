@@ -5,7 +5,6 @@ Bar: routing bit-exact, output max-abs-rel 3e-2 (BASELINE tolerance for
 INT8); in practice only SiLU's exp differs, flipping rare requant roundings."""
 import ctypes
 
-import numpy as np
 import pytest
 
 import sparsemoe_b200 as sm
