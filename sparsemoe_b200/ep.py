@@ -83,6 +83,36 @@ def recv_plan(table: np.ndarray, rank: int):
                                       np.array(expert, np.int32))
 
 
+def ep_plan_host(table: np.ndarray, rank: int, strided: bool = False) -> np.ndarray:
+    """Host restatement of moe_ep_plan (the device plan of the peer transport)
+    for one rank: table [P, E] kept rows per (sender, expert).  Returns the
+    7*E int32 plan: owner[E] | row0[E] | g_rows | g_start | g_expert |
+    g_sender | g_out_row (G = E groups, g = j * P + s)."""
+    P, E = table.shape
+    el = E // P
+    t = table.astype(np.int64)
+
+    def gexp(q, j):
+        return j * P + q if strided else q * el + j
+    to_owner = np.array([[sum(t[s, gexp(q, j)] for j in range(el)) for q in range(P)] for s in range(P)])
+    recv_off = np.concatenate([np.zeros((1, P), np.int64), np.cumsum(to_owner, axis=0)[:-1]], axis=0)
+    plan = np.zeros(7 * E, np.int64)
+    for e in range(E):
+        q, lj = (e % P, e // P) if strided else (e // el, e % el)
+        plan[e] = q
+        plan[E + e] = recv_off[rank, q] + sum(t[rank, gexp(q, j2)] for j2 in range(lj))
+    for g in range(E):
+        j, s = divmod(g, P)
+        ge = gexp(rank, j)
+        within = sum(t[s, gexp(rank, j2)] for j2 in range(j))
+        plan[2 * E + g] = t[s, ge]
+        plan[3 * E + g] = recv_off[s, rank] + within
+        plan[4 * E + g] = j
+        plan[5 * E + g] = s
+        plan[6 * E + g] = t[s, :ge].sum()
+    return plan.astype(np.int32)
+
+
 # ---- runner ----------------------------------------------------------------------
 class _Ptr:
     """A raw device address with the data_ptr() of a tensor."""

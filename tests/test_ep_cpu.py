@@ -160,3 +160,29 @@ def test_global_batch_drops_gloo_world2():
         mp.spawn(_global_rank_main, args=(2, port, cfg_args, results), nprocs=2, join=True)
         res = dict(results)
     assert res == {0: True, 1: True}
+
+
+def test_ep_plan_host_matches_recv_plan():
+    """The peer transport's plan (host restatement of moe_ep_plan) agrees with
+    the NCCL transport's planner for contiguous ownership: same owner-side
+    groups, and each sender's rows land after the blocks of lower senders."""
+    from sparsemoe_b200.ep import ep_plan_host
+    rng = np.random.default_rng(0)
+    P, E = 4, 16
+    table = rng.integers(0, 50, (P, E)).astype(np.int32)
+    for rank in range(P):
+        plan = ep_plan_host(table, rank)
+        _, (rows, start, exp) = recv_plan(table, rank)
+        assert np.array_equal(plan[2 * E:3 * E], rows)
+        assert np.array_equal(plan[3 * E:4 * E], start)
+        assert np.array_equal(plan[4 * E:5 * E], exp)
+        # group (j, s) results go to expert rank*E/P + j's first row in sender s's dense layout
+        el = E // P
+        for g in range(E):
+            j, s = divmod(g, P)
+            assert plan[6 * E + g] == table[s, :rank * el + j].sum()
+    # strided ownership: every expert has exactly one owner and each owner's groups cover its experts
+    for rank in range(P):
+        plan = ep_plan_host(table, rank, strided=True)
+        assert np.array_equal(plan[:E], np.arange(E) % P)
+        assert np.array_equal(plan[2 * E:3 * E].reshape(E // P, P), table[:, rank::P].T)

@@ -104,3 +104,23 @@ def test_ep_matches_single_gpu(gpu, name):
         assert idx_equal, f"rank {rank}: routing differs"
         assert err < 1e-6, f"rank {rank}: max-abs-rel {err}"
 
+
+
+@pytest.mark.parametrize("strided", [False, True])
+def test_ep_plan_kernel_matches_host(gpu, strided):
+    """moe_ep_plan (one-CTA kernel) against its host restatement on random
+    kept-row tables, every rank of an 8-way layout (runs on one GPU)."""
+    import ctypes
+    import torch
+    from sparsemoe_b200.ep import ep_plan_host
+    rng = np.random.default_rng(1)
+    P, E = 8, 64
+    table = rng.integers(0, 300, (P, E)).astype(np.int32)
+    t = torch.from_numpy(table).to(gpu)
+    plan = torch.empty(7 * E, dtype=torch.int32, device=gpu)
+    for rank in range(P):
+        rc = sm.lib.moe_ep_plan(ctypes.c_void_p(t.data_ptr()), P, rank, E, int(strided),
+                                ctypes.c_void_p(plan.data_ptr()), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+        assert rc == 0
+        torch.cuda.synchronize()
+        assert np.array_equal(plan.cpu().numpy(), ep_plan_host(table, rank, strided)), f"rank {rank}"
