@@ -68,14 +68,16 @@ struct Tile {
     static constexpr int kPBytes = 64 * BN / 2;          // packed nibbles
     static constexpr int kSZBytes = 4 * BN;              // INT4: BN fp16 scales + BN zeros; NVFP4: 4 x BN e4m3
     // Two rings: kRaw TMA stages (A, packed weights, scales) and kBSt converted
-    // bf16 B stages.  The raw ring is the deeper one, so that small tiles
-    // (decode) keep enough loads in flight; every A and B buffer sits on a
-    // 1024-byte boundary (128B swizzle atoms).
+    // bf16 B stages, so loads, conversion and MMAs overlap across stages;
+    // every A and B buffer sits on a 1024-byte boundary (128B swizzle atoms).
+    // 4 + 3 stages fill 230.7 KB of the 232 KB a CTA may use for both tiles.
     static constexpr int kRawBytes = (kABytes + kPBytes + kSZBytes + 1023) / 1024 * 1024;
-    static constexpr int kRaw = kBM == 128 ? 5 : 4;
-    static constexpr int kBSt = 2;
+    static constexpr int kRaw = 4;
+    static constexpr int kBSt = 3;   // the converter runs up to two stages ahead of the MMA
     static constexpr int kTxBytes = kABytes + kPBytes + kSZBytes;
     static constexpr size_t kSmemBytes = 1024 + (size_t)kRaw * kRawBytes + (size_t)kBSt * kBBytes + 256 + 4 * 2048;
+    // dynamic + the kernel's static group tables (5 x kMaxGroups ints + 1) within a CTA's 227 KB
+    static_assert(kSmemBytes + sizeof(int) * (5 * kMaxGroups + 1) <= 232448, "shared memory per CTA");
     static constexpr int kUnits = BN / 8;                 // converter: 8-column units
     static constexpr int kRowGroups = 256 / kUnits;       // converter threads per unit
     static constexpr int kRowsPerThread = 64 / kRowGroups;
