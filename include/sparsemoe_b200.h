@@ -190,6 +190,38 @@ int moe_stage_expert_ffn_planned(const struct MoEArgs* args, const MoeDims* dims
                                  int num_groups, int64_t rows_capacity, float* const* out_bases, int num_bases,
                                  cudaStream_t stream);
 
+// ---- expert weight files (.bin): a layer's router and expert weights in the
+//      formats the kernels read (no repacking on load).  The reference's
+//      driver names a cache file it never writes (drivers/main.cu:27-31).
+#define MOE_WFILE_MAX_ARRAYS 16
+typedef struct MoeWeightArray {
+    char name[24];          // "wr", "bias", "wg", "wu", "wd", "wg_q", "sg", "wg_s", "wg_z", "wg_g", ...
+    int32_t elem_bytes;     // 1, 2 or 4
+    int32_t kind;           // 0 unsigned integer (or 16-bit float bit patterns), 1 signed integer, 2 float
+    int32_t ndim;           // 1..4
+    int32_t reserved;
+    int64_t shape[4];
+    uint64_t offset;        // byte offset in the file (256-aligned); set by moe_weights_write
+    uint64_t bytes;         // elements x elem_bytes; set by moe_weights_write
+} MoeWeightArray;
+typedef struct MoeWeightFile {
+    char magic[8];          // "SMOEW001"
+    int32_t dtype;          // MOE_DTYPE_* of the expert weights
+    int32_t router_dtype;   // MOE_ROUTER_*
+    int32_t num_experts, d_model, d_ff;
+    int32_t num_arrays;
+    int32_t reserved;
+    MoeWeightArray arrays[MOE_WFILE_MAX_ARRAYS];
+} MoeWeightFile;
+// Writes the header (magic, offsets and sizes filled in) and data[i] (host
+// memory) for each of header->num_arrays arrays.
+int moe_weights_write(const char* path, const MoeWeightFile* header, const void* const* data);
+// Reads and checks the header (magic, descriptors, sizes within the file).
+int moe_weights_read_header(const char* path, MoeWeightFile* header);
+// Copies array `index` into dst (host memory of at least its bytes).
+int moe_weights_read_array(const char* path, const MoeWeightFile* header, int index, void* dst,
+                           size_t dst_bytes);
+
 // Peer memory for expert parallelism (CUDA IPC within a node): allocate a
 // device buffer and its 64-byte handle; map a peer's handle in this process;
 // unmap; free.  moe_memcpy_async copies between any device pointers

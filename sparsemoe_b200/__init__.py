@@ -90,6 +90,22 @@ class MoeDims(ctypes.Structure):
     ]
 
 
+class MoeWeightArray(ctypes.Structure):
+    """ctypes image of `MoeWeightArray` (include/sparsemoe_b200.h)."""
+
+    _fields_ = [("name", ctypes.c_char * 24), ("elem_bytes", ctypes.c_int32), ("kind", ctypes.c_int32),
+                ("ndim", ctypes.c_int32), ("reserved", ctypes.c_int32), ("shape", ctypes.c_int64 * 4),
+                ("offset", ctypes.c_uint64), ("bytes", ctypes.c_uint64)]
+
+
+class MoeWeightFile(ctypes.Structure):
+    """ctypes image of `MoeWeightFile` (include/sparsemoe_b200.h)."""
+
+    _fields_ = [("magic", ctypes.c_char * 8), ("dtype", ctypes.c_int32), ("router_dtype", ctypes.c_int32),
+                ("num_experts", ctypes.c_int32), ("d_model", ctypes.c_int32), ("d_ff", ctypes.c_int32),
+                ("num_arrays", ctypes.c_int32), ("reserved", ctypes.c_int32), ("arrays", MoeWeightArray * 16)]
+
+
 def _load() -> ctypes.CDLL:
     if not LIB_PATH.exists():
         raise ImportError(
@@ -114,6 +130,10 @@ def _load() -> ctypes.CDLL:
         "moe_ffn_scratch_bytes": (ctypes.c_size_t, [ctypes.POINTER(MoeDims), ctypes.c_int64]),
         "moe_stage_expert_ffn_peer": (ctypes.c_int, [ctypes.POINTER(MoEArgs), ctypes.POINTER(MoeDims), _p, _p, _p,
                                                       _p, _p, ctypes.c_int, ctypes.c_int64, _p, ctypes.c_int, _p]),
+        "moe_weights_write": (ctypes.c_int, [ctypes.c_char_p, ctypes.POINTER(MoeWeightFile), _p]),
+        "moe_weights_read_header": (ctypes.c_int, [ctypes.c_char_p, ctypes.POINTER(MoeWeightFile)]),
+        "moe_weights_read_array": (ctypes.c_int, [ctypes.c_char_p, ctypes.POINTER(MoeWeightFile), ctypes.c_int,
+                                                   _p, ctypes.c_size_t]),
         "moe_ep_plan": (ctypes.c_int, [_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _p, _p]),
         "moe_stage_dispatch_peer": (ctypes.c_int, [ctypes.POINTER(MoEArgs), ctypes.POINTER(MoeDims), _p, _p, _p,
                                                     ctypes.c_int, _p]),
@@ -310,6 +330,54 @@ def make_inputs(cfg: LayerConfig, seed: int = 0) -> dict:
     return out
 
 
+_KIND = {"u": 0, "i": 1, "f": 2}
+_INT8_SCALES = ("s_in", "s_gate", "s_up", "s_mid", "s_down")
+
+
+def save_weights(path: str, cfg: LayerConfig, inputs: dict) -> None:
+    """Writes the router and expert weights of `inputs` (a make_inputs() dict,
+    or one with the same keys) in the library's .bin format: every array but
+    the tokens `x`, the per-tensor int8 scales as one f32 array."""
+    arrays = {k: np.ascontiguousarray(v) for k, v in inputs.items()
+              if k not in ("x",) + _INT8_SCALES and v is not None and isinstance(v, np.ndarray)}
+    if cfg.int8:
+        arrays["int8_scales"] = np.array([inputs[k] for k in _INT8_SCALES], np.float32)
+    if len(arrays) > 16:
+        raise ValueError("more than 16 arrays")
+    h = MoeWeightFile()
+    h.dtype, h.router_dtype = cfg.dtype, ROUTER_F32 if cfg.router_f32 else ROUTER_SAME
+    h.num_experts, h.d_model, h.d_ff, h.num_arrays = cfg.num_experts, cfg.d_model, cfg.d_ff, len(arrays)
+    ptrs = (ctypes.c_void_p * len(arrays))()
+    for i, (name, a) in enumerate(arrays.items()):
+        d = h.arrays[i]
+        d.name = name.encode()
+        d.elem_bytes, d.kind, d.ndim = a.dtype.itemsize, _KIND[a.dtype.kind], a.ndim
+        for j, n in enumerate(a.shape):
+            d.shape[j] = n
+        ptrs[i] = a.ctypes.data
+    check(lib.moe_weights_write(str(path).encode(), ctypes.byref(h), ptrs))
+
+
+def load_weights(path: str) -> tuple[dict, dict]:
+    """Reads a .bin weight file: (info: dtype, router_dtype, num_experts,
+    d_model, d_ff; arrays by name, with the int8 scales back as floats)."""
+    h = MoeWeightFile()
+    check(lib.moe_weights_read_header(str(path).encode(), ctypes.byref(h)))
+    out = {}
+    for i in range(h.num_arrays):
+        d = h.arrays[i]
+        dt = np.dtype(f"{'uif'[d.kind]}{d.elem_bytes}")
+        a = np.empty(tuple(d.shape[j] for j in range(d.ndim)), dt)
+        check(lib.moe_weights_read_array(str(path).encode(), ctypes.byref(h), i, a.ctypes.data, a.nbytes))
+        out[d.name.decode()] = a
+    if "int8_scales" in out:
+        for k, v in zip(_INT8_SCALES, out.pop("int8_scales")):
+            out[k] = float(v)
+    info = {"dtype": h.dtype, "router_dtype": h.router_dtype, "num_experts": h.num_experts,
+            "d_model": h.d_model, "d_ff": h.d_ff}
+    return info, out
+
+
 def quantize_int4_g128(w16: np.ndarray, bf16: bool = True):
     """INT4 asymmetric, group 128 along K, fp16 scale and zero per (group,
     column); returns (packed [E, K, N/2] uint8, scales, zeros [E, K/128, N]
@@ -374,4 +442,4 @@ __all__ = ["MoEArgs", "MoeDims", "LayerConfig", "MoeLayer", "make_inputs", "capa
            "MoeError", "normal16", "normal_f32", "zipf_bias", "quantize_per_tensor", "DTYPE_F16", "DTYPE_BF16",
            "DTYPE_INT8", "DTYPE_FP8_BLOCK", "quantize_fp8_blocks",
            "DTYPE_W4A16", "quantize_int4_g128", "DTYPE_INT8_CHANNEL", "quantize_int8_channel",
-           "DTYPE_NVFP4", "quantize_nvfp4"]
+           "DTYPE_NVFP4", "quantize_nvfp4", "save_weights", "load_weights", "MoeWeightFile", "MoeWeightArray"]

@@ -85,3 +85,16 @@ def test_nvfp4_every_code_and_tiny_scales(gpu):
 def test_nvfp4_deepseek_decode_shape(gpu):
     cfg = sm.LayerConfig(1, 512, 7168, 2048, 32, 8, 1.25, dtype=sm.DTYPE_NVFP4, router_f32=True, zipf_s=1.0)
     w4_check(cfg, gpu, seed=3, t_end=64)
+
+
+def test_layer_from_weight_file(gpu, tmp_path):
+    """A layer loaded from a .bin weight file computes exactly what the same
+    weights loaded from memory compute."""
+    import torch
+    cfg = sm.LayerConfig(1, 256, 512, 256, 16, 4, 1.25, dtype=sm.DTYPE_NVFP4, router_f32=True, zipf_s=1.0)
+    inp = sm.make_inputs(cfg, 4)
+    sm.save_weights(tmp_path / "w.bin", cfg, inp)
+    _, back = sm.load_weights(tmp_path / "w.bin")
+    a = run(cfg, inp, gpu)
+    b = run(cfg, {**back, "x": inp["x"]}, gpu)
+    assert torch.equal(a.out, b.out)
