@@ -242,3 +242,168 @@ def test_nvfp4_quantiser_matches_numpy():
                     assert code & 7 == best, (e, k, n, a, code)
                     if blk[i, n] < 0:
                         assert code & 8
+
+
+# ---- numpy restatements of the oracle's FFN for the quantised formats -----------
+def _bf16_to_f32(u16):
+    return (np.asarray(u16, np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def _round_bf16(v):
+    """f32 -> nearest-even bf16 -> f32."""
+    u = np.asarray(v, np.float32).view(np.uint32).astype(np.uint64)
+    u = (u + 0x7FFF + ((u >> 16) & 1)) >> 16
+    return (u.astype(np.uint32) << 16).view(np.float32)
+
+
+def _nibbles(packed, N):
+    """[E, K, N/2] pair-interleaved 4-bit words -> [E, K, N] codes."""
+    n = np.arange(N)
+    bit = 4 * ((n & 7) >> 1) + 16 * (n & 1)
+    byte = (n >> 3) * 4 + (bit >> 3)
+    return (packed[:, :, byte] >> (bit & 7)) & 15
+
+
+def _np_ffn(x, wg, wu, wd, r, k, round_h, T):
+    """Route-by-route f32 FFN of dequantised weights (h rounded by round_h),
+    combined in route order."""
+    out = np.zeros((T, x.shape[1]), np.float32)
+    for t in range(T):
+        for l in range(k):
+            if r["route_slot"][t * k + l] < 0:
+                continue
+            e = r["idx"][t, l]
+            g = (x[t].astype(np.float64) @ wg[e].astype(np.float64)).astype(np.float32)
+            u = (x[t].astype(np.float64) @ wu[e].astype(np.float64)).astype(np.float32)
+            h = round_h(u * (g / (np.float32(1) + np.exp(-g))))
+            y = (h.astype(np.float64) @ wd[e].astype(np.float64)).astype(np.float32)
+            out[t] = out[t] + np.float32(r["w"][t, l]) * y
+    return out
+
+
+def _check_close(ref_out, np_out):
+    np.testing.assert_allclose(ref_out, np_out, rtol=2e-3, atol=2e-3 * float(np.abs(np_out).max()))
+
+
+def test_int4_g128_quantiser_matches_numpy():
+    rng = np.random.default_rng(6)
+    w = (rng.standard_normal((2, 256, 16)) * 0.05).astype(np.float32)
+    w[1, :128, 3] = 0.25                               # a constant group: s = 1 (fp16), z = -min
+    b16 = (w.view(np.uint32) >> 16).astype(np.uint16)
+    q, s, z = sm.quantize_int4_g128(b16, bf16=True)
+    vals = _bf16_to_f32(b16)
+    codes = _nibbles(q, 16)
+    for e in range(2):
+        for g in range(2):
+            blk = vals[e, g * 128:(g + 1) * 128]
+            mn, mx = blk.min(axis=0), blk.max(axis=0)
+            sc = ((mx - mn) / np.float32(15)).astype(np.float32)
+            sc = np.where(sc > 0, sc, np.float32(1)).astype(np.float32)
+            sh = sc.astype(np.float16)
+            zh = (-mn / sh.astype(np.float32)).astype(np.float16)
+            assert np.array_equal(s[e, g], sh.view(np.uint16)) and np.array_equal(z[e, g], zh.view(np.uint16))
+            qq = np.clip(np.rint(blk / sh.astype(np.float32) + zh.astype(np.float32)), 0, 15)
+            assert np.array_equal(codes[e, g * 128:(g + 1) * 128], qq)
+
+
+def test_w4_oracle_matches_numpy_restatement():
+    cfg = sm.LayerConfig(1, 16, 256, 256, 8, 2, 1.0, dtype=sm.DTYPE_W4A16, cap=-1)
+    inp = sm.make_inputs(cfg, 2)
+    ref = O.forward(inp, cfg, nthreads=2)
+    x = _bf16_to_f32(inp["x"])
+
+    def deq(n):
+        q = _nibbles(inp[n + "_q"], inp[n].shape[2]).astype(np.float64)
+        s = inp[n + "_s"].view(np.float16).astype(np.float64).repeat(128, axis=1)
+        z = inp[n + "_z"].view(np.float16).astype(np.float64).repeat(128, axis=1)
+        return ((q - z) * s).astype(np.float32)
+    out = _np_ffn(x, deq("wg"), deq("wu"), deq("wd"), ref, cfg.top_k, _round_bf16, cfg.T)
+    _check_close(ref["out"], out)
+
+
+def test_nvfp4_oracle_matches_numpy_restatement():
+    cfg = sm.LayerConfig(1, 16, 256, 256, 8, 2, 1.0, dtype=sm.DTYPE_NVFP4, cap=-1)
+    inp = sm.make_inputs(cfg, 2)
+    ref = O.forward(inp, cfg, nthreads=2)
+    x = _bf16_to_f32(inp["x"])
+    L = O.lib()
+    e4m3 = np.array([L.oracle_e4m3_decode(i) for i in range(256)], np.float64)
+    mag = np.array([0, 0.5, 1, 1.5, 2, 3, 4, 6], np.float64)
+
+    def deq(n):
+        c = _nibbles(inp[n + "_q"], inp[n].shape[2])
+        v = np.where(c & 8, -1.0, 1.0) * mag[c & 7]
+        s = e4m3[inp[n + "_s"]].repeat(16, axis=1)
+        return (v * s * inp[n + "_g"].astype(np.float64)[:, None, None]).astype(np.float32)
+    out = _np_ffn(x, deq("wg"), deq("wu"), deq("wd"), ref, cfg.top_k, _round_bf16, cfg.T)
+    _check_close(ref["out"], out)
+
+
+def test_fp8_oracle_matches_numpy_restatement():
+    """FP8 block path: x and h quantised per 1x128 block (amax/448, e4m3),
+    weights e4m3 with 128x128 scales, per-K-block promotion."""
+    cfg = sm.LayerConfig(1, 12, 256, 256, 8, 2, 1.0, dtype=sm.DTYPE_FP8_BLOCK, cap=-1)
+    inp = sm.make_inputs(cfg, 3)
+    ref = O.forward(inp, cfg, nthreads=2)
+    L = O.lib()
+    dec = np.array([L.oracle_e4m3_decode(i) for i in range(256)], np.float32)
+
+    def q_row(v):
+        qv, sc = np.empty_like(v), np.empty(v.size // 128, np.float32)
+        for b in range(v.size // 128):
+            blk = v[b * 128:(b + 1) * 128]
+            m = np.abs(blk).max()
+            s = np.float32(m / np.float32(448)) if m > 0 else np.float32(1)
+            sc[b] = s
+            qv[b * 128:(b + 1) * 128] = dec[[L.oracle_e4m3(float(np.float32(t / s))) for t in blk]]
+        return qv, sc
+    x = _bf16_to_f32(inp["x"])
+    out = np.zeros((cfg.T, cfg.d_model), np.float32)
+    for t in range(cfg.T):
+        for l in range(cfg.top_k):
+            if ref["route_slot"][t * cfg.top_k + l] < 0:
+                continue
+            e = ref["idx"][t, l]
+            qa, sa = q_row(x[t])
+
+            def gemm(qv, sv, wq, ws):
+                K, N = wq.shape
+                acc = np.zeros(N, np.float32)
+                for kb in range(K // 128):
+                    p = (qv[kb * 128:(kb + 1) * 128].astype(np.float64) @
+                         dec[wq[kb * 128:(kb + 1) * 128]].astype(np.float64)).astype(np.float32)
+                    acc = (p.astype(np.float64) * (sv[kb] * ws[kb].repeat(128)).astype(np.float32) + acc).astype(np.float32)
+                return acc
+            g = gemm(qa, sa, inp["wg_q"][e], inp["sg"][e])
+            u = gemm(qa, sa, inp["wu_q"][e], inp["su"][e])
+            h = u * (g / (np.float32(1) + np.exp(-g)))
+            qh, sh = q_row(h.astype(np.float32))
+            y = gemm(qh, sh, inp["wd_q"][e], inp["sd"][e])
+            out[t] = out[t] + np.float32(ref["w"][t, l]) * y
+    _check_close(ref["out"], out)
+
+
+def test_int8_per_tensor_oracle_matches_numpy_restatement():
+    """The reference's int8 format (capacity_int8_ptx.cu): per-tensor x / h
+    quantisation with the MoEArgs scales, exact s32 GEMMs, f32 dequant."""
+    cfg = sm.LayerConfig(1, 16, 256, 256, 8, 2, 1.0, dtype=sm.DTYPE_INT8, cap=-1, act_scale=0.03, mid_scale=0.02)
+    inp = sm.make_inputs(cfg, 4)
+    ref = O.forward(inp, cfg, nthreads=2)
+    f32 = np.float32
+    x = inp["x"].view(np.float16).astype(np.float32)
+    s_in, s_mid = f32(inp["s_in"]), f32(inp["s_mid"])
+    out = np.zeros((cfg.T, cfg.d_model), np.float32)
+    for t in range(cfg.T):
+        for l in range(cfg.top_k):
+            if ref["route_slot"][t * cfg.top_k + l] < 0:
+                continue
+            e = ref["idx"][t, l]
+            a = np.rint(np.clip(x[t] / s_in, -128, 127)).astype(np.int64)
+            G = a @ inp["wg_q"][e].astype(np.int64)
+            U = a @ inp["wu_q"][e].astype(np.int64)
+            gf = G.astype(np.float32) * f32(s_in * f32(inp["s_gate"]))
+            uf = U.astype(np.float32) * f32(s_in * f32(inp["s_up"]))
+            h = np.rint(np.clip(uf * (gf / (f32(1) + np.exp(-gf))) * (f32(1) / s_mid), -128, 127)).astype(np.int64)
+            y = (h @ inp["wd_q"][e].astype(np.int64)).astype(np.float32) * f32(s_mid * f32(inp["s_down"]))
+            out[t] = out[t] + f32(ref["w"][t, l]) * y
+    _check_close(ref["out"], out)
