@@ -186,3 +186,91 @@ def test_ep_plan_host_matches_recv_plan():
         plan = ep_plan_host(table, rank, strided=True)
         assert np.array_equal(plan[:E], np.arange(E) % P)
         assert np.array_equal(plan[2 * E:3 * E].reshape(E // P, P), table[:, rank::P].T)
+
+
+def _peer_rank_main(rank, world, port, strided, results):
+    """The peer transport's data movement on CPU: each rank routes its shard of
+    one global batch (global CAP via the slot_base prefix), places its kept
+    rows with the device plan's host restatement (ep_plan_host), the owners
+    run the FFN over the plan's row groups and send each result row to the
+    row the plan names in the sender's layout, and the sender combines.  Must
+    equal the single-process layer on the whole batch, for contiguous and
+    strided expert ownership."""
+    from sparsemoe_b200.ep import ep_plan_host
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    N, d, f, E, k = 48, 256, 128, 8, 2
+    full_cfg = sm.LayerConfig(1, N * world, d, f, E, k, 1.0, zipf_s=1.0)
+    full = sm.make_inputs(full_cfg, 9)
+    cap = full_cfg.capacity()
+    ref = O.forward(full, full_cfg, nthreads=2)
+    x = full["x"][rank * N:(rank + 1) * N]
+    loc = O.route(x, full["wr"], full["bias"], 1, N, d, E, k, N * k, False)      # shard slots, no drop yet
+    raw = np.bincount(loc["idx"].reshape(-1), minlength=E).astype(np.int32)
+    every = [torch.zeros(E, dtype=torch.int32) for _ in range(world)]
+    dist.all_gather(every, torch.from_numpy(raw))
+    base = sum(t.numpy() for t in every[:rank]) if rank else np.zeros(E, np.int32)
+    # kept routes of this shard, dense expert-major (expert, slot) order
+    kept = {}
+    for r in range(N * k):
+        e, s = loc["idx"].reshape(-1)[r], loc["route_slot"][r]
+        if s >= 0 and base[e] + s < cap:
+            kept.setdefault(e, []).append((s, r))
+    table_mine = np.array([len(kept.get(e, [])) for e in range(E)], np.int32)
+    every = [torch.zeros(E, dtype=torch.int32) for _ in range(world)]
+    dist.all_gather(every, torch.from_numpy(table_mine))
+    table = np.stack([t.numpy() for t in every])
+    plan = ep_plan_host(table, rank, strided)
+    start = np.concatenate([[0], np.cumsum(table_mine)])          # my dense layout
+    # dispatch: (owner, receive row, token row) for every kept route of mine
+    msgs = []
+    for e, lst in kept.items():
+        for i, (_, r) in enumerate(sorted(lst)):
+            msgs.append((int(plan[e]), int(plan[E + e]) + i, r // k))
+    got = [None] * world
+    dist.all_gather_object(got, [(q, row, x[t].tolist()) for q, row, t in msgs])
+    recv = {}
+    for lst in got:
+        for q, row, vals in lst:
+            if q == rank:
+                recv[row] = np.array(vals, np.uint16)
+    # owner FFN over the plan's groups; results to (sender, row in its layout)
+    outs = []
+    P = world
+    for g in range(E):
+        n, st, j, snd, orow = (int(plan[c * E + g]) for c in range(2, 7))
+        ge = j * P + rank if strided else rank * (E // P) + j
+        for i in range(n):
+            y = _ffn_rows(recv[st + i][None, :], full["wg"][ge], full["wu"][ge], full["wd"][ge])[0]
+            outs.append((snd, orow + i, y.tolist()))
+    got = [None] * world
+    dist.all_gather_object(got, outs)
+    back = np.zeros((int(start[-1]), d), np.float32)
+    for lst in got:
+        for snd, row, vals in lst:
+            if snd == rank:
+                back[row] = vals
+    # combine in route order
+    out = np.zeros((N, d), np.float32)
+    for t in range(N):
+        for l in range(k):
+            r = t * k + l
+            e = loc["idx"][t, l]
+            lst = sorted(kept.get(e, []))
+            pos = [rr for _, rr in lst]
+            if r in pos:
+                out[t] += loc["w"][t, l] * back[start[e] + pos.index(r)]
+    err = float(np.abs(out - ref["out"][rank * N:(rank + 1) * N]).max() / np.abs(ref["out"]).max())
+    results[rank] = err
+    dist.destroy_process_group()
+
+
+def test_peer_transport_plan_gloo_world2():
+    for strided in (False, True):
+        port = 29900 + (os.getpid() % 1000) + (7 if strided else 0)
+        with mp.Manager() as m:
+            results = m.dict()
+            mp.spawn(_peer_rank_main, args=(2, port, strided, results), nprocs=2, join=True)
+            errs = dict(results)
+        assert set(errs) == {0, 1}
+        assert max(errs.values()) < 1e-2, (strided, errs)
