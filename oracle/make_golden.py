@@ -69,6 +69,6 @@ def run(name: str, out_dir: Path) -> Path:
 
 
 if __name__ == "__main__":
-    od = Path(sys.argv[1] if len(sys.argv) > 1 else "gpurun_out/golden")
+    od = Path(sys.argv[1] if len(sys.argv) > 1 else "golden_out")
     for n in CONFIGS:
         print(run(n, od))
