@@ -274,3 +274,92 @@ def test_peer_transport_plan_gloo_world2():
             errs = dict(results)
         assert set(errs) == {0, 1}
         assert max(errs.values()) < 1e-2, (strided, errs)
+
+
+def _simulate_ranks(P, strided, B=2, N=32, d=256, E=32, k=4, cf=1.0, zipf=1.2, seed=11):
+    """P expert-parallel ranks in one process, at the level of row indices:
+    each rank routes its shard of every global batch, the global drop rule
+    keeps a route iff (lower ranks' totals) + its shard slot < CAP, every kept
+    row is placed with the sender's plan and found again through the owner's
+    plan, and the owner's result row goes back to the sender's dense slot."""
+    from sparsemoe_b200.ep import ep_plan_host
+    full_cfg = sm.LayerConfig(B, N * P, d, 128, E, k, cf, zipf_s=zipf)
+    full = sm.make_inputs(full_cfg, seed)
+    cap = full_cfg.capacity()
+    ref = O.route(full["x"], full["wr"], full["bias"], B, N * P, d, E, k, cap, False)
+    xs = full["x"].reshape(B, P, N, d)
+    loc = [O.route(np.ascontiguousarray(xs[:, q]).reshape(B * N, d), full["wr"], full["bias"],
+                   B, N, d, E, k, N * k, False) for q in range(P)]
+    raw = np.zeros((P, B, E), np.int64)
+    for q in range(P):
+        for b in range(B):
+            raw[q, b] = np.bincount(loc[q]["idx"][b * N:(b + 1) * N].reshape(-1), minlength=E)[:E]
+    # (1) global drops, bit-exact against the single-rank routing of the whole batch
+    kept = [dict() for _ in range(P)]          # kept[q][(b, e)] = route ids in slot order
+    for q in range(P):
+        base = raw[:q].sum(axis=0)
+        idx, slot = loc[q]["idx"], loc[q]["route_slot"]
+        for b in range(B):
+            for t in range(N):
+                for l in range(k):
+                    r = (b * N + t) * k + l
+                    gt = b * N * P + q * N + t
+                    e = int(idx[b * N + t, l])
+                    assert e == ref["idx"][gt, l]
+                    keep = slot[r] >= 0 and base[b, e] + slot[r] < cap
+                    assert keep == (ref["route_slot"][gt * k + l] >= 0)
+                    if keep:
+                        assert base[b, e] + slot[r] == ref["route_slot"][gt * k + l]
+                        kept[q].setdefault((b, e), []).append((int(slot[r]), r))
+    for q in range(P):
+        for key in kept[q]:
+            kept[q][key].sort()
+    # each sender's dense layout: expert-major, then batch, then slot
+    dense = []
+    for q in range(P):
+        order = [(e, r) for e in range(E) for b in range(B) for _, r in kept[q].get((b, e), [])]
+        dense.append(order)
+    table = np.array([[sum(1 for ee, _ in dense[q] if ee == e) for e in range(E)] for q in range(P)], np.int32)
+    plans = [ep_plan_host(table, q, strided).astype(np.int64) for q in range(P)]
+    # (2) dispatch: (owner, receive row) of every kept row, unique and dense per owner
+    where = {}
+    for q in range(P):
+        seen = {}
+        for pos, (e, r) in enumerate(dense[q]):
+            i = seen.get(e, 0)
+            seen[e] = i + 1
+            dst = (int(plans[q][e]), int(plans[q][E + e]) + i)
+            assert dst not in where
+            where[dst] = (q, e, pos)
+    for o in range(P):
+        rows = sorted(row for (own, row) in where if own == o)
+        assert rows == list(range(len(rows)))
+    # (3) the owner's groups find every row and send its result to the sender's dense slot
+    back = set()
+    el = E // P
+    for o in range(P):
+        pl = plans[o]
+        for g in range(E):
+            n, st, j, snd, orow = (int(pl[c * E + g]) for c in range(2, 7))
+            ge = j * P + o if strided else o * el + j
+            assert (ge % P == o) if strided else (ge // el == o)
+            for i in range(n):
+                q, e, pos = where[(o, st + i)]
+                assert (q, e) == (snd, ge)
+                assert orow + i == pos
+                back.add((q, pos))
+    assert back == {(q, pos) for q in range(P) for pos in range(len(dense[q]))}
+    return int(table.sum()), int(ref["counts"].sum())
+
+
+def test_ep_simulated_ranks_up_to_8():
+    """Partition, global drops and the peer plan as 2, 4 and 8 ranks in one
+    process, for contiguous and strided expert ownership: the kept set and
+    slots equal the single-rank routing bit for bit and every kept row makes
+    the round trip sender -> owner -> sender to its own slot."""
+    for P in (2, 4, 8):
+        for strided in (False, True):
+            kept_rows, ref_rows = _simulate_ranks(P, strided)
+            assert kept_rows == ref_rows and kept_rows < 2 * 32 * P * 4     # Zipf bias: drops happen
+            kept_rows, ref_rows = _simulate_ranks(P, strided, cf=2.0, zipf=0.0)
+            assert kept_rows == ref_rows
