@@ -100,7 +100,7 @@ def ffn_combine(x, wg, wu, wd, B, N, d, f, E, k, bf16, idx, w, route_slot, t_beg
     """Stages 4-5 for tokens [t_begin, t_end); returns the [t_end - t_begin, d] f32 output rows."""
     T = B * N
     t_end = T if t_end is None else t_end
-    out = np.zeros((T, d), np.float32) if t_end - t_begin == T else np.zeros((T, d), np.float32)
+    out = np.zeros((T, d), np.float32)
     args = [np.ascontiguousarray(a, dtype=np.uint16) for a in (x, wg, wu, wd)]
     lib().oracle_ffn_combine(*(_ptr(a) for a in args), B, N, d, f, E, k, int(bf16),
                              _ptr(np.ascontiguousarray(idx, np.int32)), _ptr(np.ascontiguousarray(w, np.float32)),

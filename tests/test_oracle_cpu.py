@@ -407,3 +407,43 @@ def test_int8_per_tensor_oracle_matches_numpy_restatement():
             y = (h @ inp["wd_q"][e].astype(np.int64)).astype(np.float32) * f32(s_mid * f32(inp["s_down"]))
             out[t] = out[t] + f32(ref["w"][t, l]) * y
     _check_close(ref["out"], out)
+
+
+@pytest.mark.parametrize("B,N,E,k,cf,zipf", [(2, 64, 8, 2, 1.0, 1.5), (1, 96, 16, 16, 1.0, 0.0),
+                                             (3, 40, 32, 4, 0.5, 1.0), (1, 1, 8, 8, 1.0, 0.0)])
+def test_capacity_drop_invariants(B, N, E, k, cf, zipf):
+    """Stage 3 (capacity.cu:245-309 in route-id order): per (batch, expert) the
+    kept routes are exactly the first CAP routes in route-id order, slots are
+    0..count-1 in that order, counts = min(routes, CAP), token_ids / weights
+    hold the kept routes' tokens and gate weights, and slots past the count
+    stay empty.  Includes k = E (every expert selected) and a single token."""
+    cfg = sm.LayerConfig(B, N, 256, 128, E, k, cf, zipf_s=zipf)
+    inp = sm.make_inputs(cfg, 4)
+    cap = cfg.capacity()
+    r = O.route(inp["x"], inp["wr"], inp["bias"], B, N, 256, E, k, cap, False)
+    if k == E:
+        assert (np.sort(r["idx"], axis=1) == np.arange(E)).all()
+    for b in range(B):
+        seen = np.zeros(E, np.int64)
+        for t in range(N):
+            for l in range(k):
+                rid = (b * N + t) * k + l
+                e = r["idx"][b * N + t, l]
+                s = r["route_slot"][rid]
+                if seen[e] < cap:
+                    assert s == seen[e]
+                    assert r["token_ids"][b, e, s] == t
+                    assert r["token_weights"][b, e, s] == r["w"][b * N + t, l]
+                else:
+                    assert s == -1
+                seen[e] += 1
+        assert np.array_equal(r["counts"][b], np.minimum(seen, cap))
+        for e in range(E):
+            assert (r["token_ids"][b, e, r["counts"][b, e]:] == -1).all()
+            assert (r["token_weights"][b, e, r["counts"][b, e]:] == 0).all()
+
+
+def test_empty_batch_routes_nothing():
+    """T = 0: no routes, zero counts, nothing written."""
+    r = O.route(np.zeros((0, 256), np.uint16), np.zeros((256, 8), np.uint16), None, 1, 0, 256, 8, 2, 16, False)
+    assert r["idx"].shape == (0, 2) and (r["counts"] == 0).all() and (r["token_ids"] == -1).all()
