@@ -44,8 +44,24 @@ def kernels_per_step(cfg) -> int:
 GLOBAL_BATCH = {"ds3_int4_decode", "ds3_int4_prefill", "ds3_nvfp4_decode", "ds3_nvfp4_prefill"}
 
 
-def workload(name: str):
-    import sparsemoe_b200 as sm
+def load_config_module():
+    """sparsemoe_b200/config.py loaded by path: LayerConfig and the format
+    codes without importing the package (which loads libsparsemoe_b200.so).
+    CAP comes from the CPU oracle's restatement of the reference formula."""
+    import importlib.util
+    from oracle import oracle as O
+    spec = importlib.util.spec_from_file_location("_smoe_config", ROOT / "sparsemoe_b200" / "config.py")
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[spec.name] = mod            # dataclasses resolve annotations through sys.modules
+    spec.loader.exec_module(mod)
+    mod.set_capacity_fn(O.capacity)
+    return mod
+
+
+def workload(name: str, sm=None):
+    """The named workload as a LayerConfig of `sm` (default: the package)."""
+    if sm is None:
+        import sparsemoe_b200 as sm
     table = {
         "mixtral_bf16": sm.LayerConfig(8, 2048, 4096, 14336, 8, 2, 1.25, dtype=sm.DTYPE_BF16),
         "mixtral_fp16": sm.LayerConfig(8, 2048, 4096, 14336, 8, 2, 1.25, dtype=sm.DTYPE_F16),
@@ -127,7 +143,35 @@ def cfg_json(name, cfg, cap):
     return {"workload": name, "num_batches": cfg.num_batches, "tokens_per_batch": cfg.tokens,
             "tokens": cfg.T, "d_model": cfg.d_model, "d_ff": cfg.d_ff, "experts": cfg.num_experts,
             "top_k": cfg.top_k, "capacity_factor": cfg.capacity_factor, "cap": cap, "zipf_s": cfg.zipf_s,
-            "l2": f"inputs larger than L2 (x {xb:.0f} MB, weights {wmb:.2f} GB; no flush needed)"}
+            "l2": (f"inputs larger than L2 (x {xb:.0f} MB, weights {wmb:.2f} GB; no flush needed)"
+                   if xb + wmb * 1e3 > 126 else
+                   f"inputs smaller than L2 (x {xb:.0f} MB, weights {wmb * 1e3:.0f} MB): L2-resident between "
+                   f"steps, not flushed")}
+
+
+def parallelism_desc(args, cfg, ws, cap, mode) -> str:
+    """config.parallelism of a run (the same text on both arms)."""
+    if ws == 1:
+        return "single GPU"
+    if mode != "ep":
+        return f"{ws} independent replicas (no data-path collective)"
+    glob = args.config in GLOBAL_BATCH
+    placement = "strided" if glob and args.ep_transport == "peer" else "contiguous"
+    return (f"ep{ws} (expert parallel, {cfg.num_experts // ws} experts per GPU, "
+            + ("rows over NVLink peer memory: gather kernels store the rows into the owners, down-GEMM "
+               "epilogue stores the results into the senders' buffers; " if args.ep_transport == "peer" else
+               f"NCCL all-to-all dispatch/return on a second stream, {args.ep_chunks} pipelined batch chunks; ")
+            + f"{cfg.T} tokens per GPU"
+            + (f"; each batch split over the {ws} ranks, global CAP {cap}, {placement} expert ownership)"
+               if glob else ", per-rank batches)"))
+
+
+def run_cap(args, cfg, ws, mode) -> int:
+    """CAP of the run: per batch, or of the whole split batch under EP with global batches."""
+    if ws > 1 and mode == "ep" and args.config in GLOBAL_BATCH and cfg.cap == 0:
+        from oracle import oracle as O
+        return O.capacity(cfg.tokens * ws, cfg.top_k, cfg.num_experts, cfg.capacity_factor)
+    return cfg.capacity()
 
 
 # ---------------------------------------------------------------------------
@@ -317,7 +361,7 @@ def host_inputs_from_device(layer) -> dict:
     return inp
 
 
-def pipelined_e2e(layer, stream, x_host, out_host, K, warmup, dev) -> float:
+def pipelined_e2e(layer, stream, x_host, out_host, K, warmup, dev, set_io=None) -> float:
     """ms per step of K layer calls with every step's tokens copied in from
     pinned host memory and its 16-bit output copied back, the copies on a
     second stream with two device buffers each, so that step i's compute
@@ -330,6 +374,9 @@ def pipelined_e2e(layer, stream, x_host, out_host, K, warmup, dev) -> float:
     outs = [layer.out16, torch.empty_like(layer.out16)]
     hosts = [out_host, torch.empty_like(out_host).pin_memory()]
     x0, o0 = layer.x, layer.out16
+    if set_io is None:
+        def set_io(xb, ob):
+            layer.x, layer.out16 = xb, ob
 
     def run(n, e_start=None, e_end=None):
         h2d_done = [torch.cuda.Event(), torch.cuda.Event()]
@@ -344,7 +391,7 @@ def pipelined_e2e(layer, stream, x_host, out_host, K, warmup, dev) -> float:
         for i in range(n):
             b = i & 1
             stream.wait_event(h2d_done[b])
-            layer.x, layer.out16 = xs[b], outs[b]
+            set_io(xs[b], outs[b])
             layer.forward(stream)
             fwd_done[b].record(stream)
             copy.wait_event(fwd_done[b])
@@ -362,79 +409,65 @@ def pipelined_e2e(layer, stream, x_host, out_host, K, warmup, dev) -> float:
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     run(K, e0, e1)
     torch.cuda.synchronize(dev)
-    layer.x, layer.out16 = x0, o0
+    set_io(x0, o0)
     return e0.elapsed_time(e1) / K
 
 
-def cpu_measure(layer, sample_tokens: int, nthreads: int):
+def oracle_measure(inp: dict, cfg, cap: int, sample_tokens: int, nthreads: int):
     """The oracle (CPU transcription of the reference's five stages) on a
-    bounded sample: routing of all T tokens, expert FFN + combine of the first
-    `sample_tokens` tokens.  tokens/s = S / (t_ffn(S) + t_route(T) * S / T)."""
-    import numpy as np
-    import torch
+    bounded sample of host inputs: routing of all T tokens, expert FFN +
+    combine of the first S tokens.  tokens/s = S / (t_ffn(S) + t_route(T) * S / T).
+    Returns (tokens/s, t_route, t_ffn, S)."""
     from oracle import oracle as O
-    cfg = layer.cfg
-    if getattr(layer, "host_inputs", None) is None and (cfg.fp8 or cfg.int8ch or cfg.w4 or cfg.zipf_s > 0):
-        layer.host_inputs = host_inputs_from_device(layer)
-    if getattr(layer, "host_inputs", None) is not None:
-        inp = layer.host_inputs
-        t0 = time.perf_counter()
-        r = O.route(inp["x"], inp["wr"], inp["bias"], cfg.num_batches, cfg.tokens, cfg.d_model, cfg.num_experts,
-                    cfg.top_k, layer.cap, cfg.act_bf16, cfg.router_f32, nthreads)
-        t_route = time.perf_counter() - t0
-        S = min(sample_tokens, cfg.T)
-        fn = O.ffn_combine_fp8 if cfg.fp8 else (O.ffn_combine_int8 if cfg.int8 else
-                                                (O.ffn_combine_nvfp4 if cfg.nvfp4 else
-                                                 O.ffn_combine_w4 if cfg.w4 else
-                                                 (O.ffn_combine_int8ch if cfg.int8ch else None)))
-        t0 = time.perf_counter()
-        if fn is not None:
-            fn(inp["x"], inp, cfg, r["idx"], r["w"], r["route_slot"], 0, S, nthreads)
-        else:
-            O.ffn_combine(inp["x"], inp["wg"], inp["wu"], inp["wd"], cfg.num_batches, cfg.tokens, cfg.d_model,
-                          cfg.d_ff, cfg.num_experts, cfg.top_k, cfg.bf16, r["idx"], r["w"], r["route_slot"], 0, S,
-                          nthreads)
-        t_ffn = time.perf_counter() - t0
-        return S / (t_ffn + t_route * S / cfg.T), t_route, t_ffn, S
-    u16 = lambda t: t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)  # noqa: E731
-    x, wg, wu, wd = u16(layer.x), u16(layer.wg), u16(layer.wu), u16(layer.wd)
-    wr = layer.wr.cpu().numpy() if cfg.router_f32 else u16(layer.wr)
-    cap = layer.cap
     t0 = time.perf_counter()
-    r = O.route(x, wr, None, cfg.num_batches, cfg.tokens, cfg.d_model, cfg.num_experts, cfg.top_k, cap,
-                cfg.bf16, cfg.router_f32, nthreads)
+    r = O.route(inp["x"], inp["wr"], inp.get("bias"), cfg.num_batches, cfg.tokens, cfg.d_model, cfg.num_experts,
+                cfg.top_k, cap, cfg.act_bf16, cfg.router_f32, nthreads)
     t_route = time.perf_counter() - t0
     S = min(sample_tokens, cfg.T)
+    fn = O.ffn_combine_fp8 if cfg.fp8 else (O.ffn_combine_int8 if cfg.int8 else
+                                            (O.ffn_combine_nvfp4 if cfg.nvfp4 else
+                                             O.ffn_combine_w4 if cfg.w4 else
+                                             (O.ffn_combine_int8ch if cfg.int8ch else None)))
     t0 = time.perf_counter()
-    O.ffn_combine(x, wg, wu, wd, cfg.num_batches, cfg.tokens, cfg.d_model, cfg.d_ff, cfg.num_experts,
-                  cfg.top_k, cfg.bf16, r["idx"], r["w"], r["route_slot"], 0, S, nthreads)
+    if fn is not None:
+        fn(inp["x"], inp, cfg, r["idx"], r["w"], r["route_slot"], 0, S, nthreads)
+    else:
+        O.ffn_combine(inp["x"], inp["wg"], inp["wu"], inp["wd"], cfg.num_batches, cfg.tokens, cfg.d_model,
+                      cfg.d_ff, cfg.num_experts, cfg.top_k, cfg.bf16, r["idx"], r["w"], r["route_slot"], 0, S,
+                      nthreads)
     t_ffn = time.perf_counter() - t0
-    return S / (t_ffn + t_route * S / cfg.T), t_route, t_ffn, S
+    return S / (t_ffn + t_route * S / max(cfg.T, 1)), t_route, t_ffn, S
+
+
+def cpu_measure(layer, sample_tokens: int, nthreads: int):
+    """cpu_baseline of our own line: the oracle on this layer's own inputs."""
+    if getattr(layer, "host_inputs", None) is None:
+        layer.host_inputs = host_inputs_from_device(layer)
+    return oracle_measure(layer.host_inputs, layer.cfg, layer.cap, sample_tokens, nthreads)
 
 
 def run_reference_arm(args, ws, rank, local):
     """`--impl reference`: the reference has no CPU implementation and its GPU
     kernels are not this arm; the CPU transcription of its five stages (oracle/)
-    is timed on the host cores, rank 0 only."""
+    is timed on the host cores, rank 0 only.  Nothing of the product is loaded:
+    the workload is described by sparsemoe_b200/config.py (loaded by path),
+    drawn and quantised on the host by oracle/inputs.py, and CAP comes from the
+    oracle."""
     if rank != 0:
         return
-    import torch
-    import sparsemoe_b200 as sm
-    cfg = workload(args.config)
+    from oracle import inputs as OI
+    cm = load_config_module()
+    cfg = workload(args.config, cm)
+    mode = args.parallel if args.parallel != "auto" else ("ep" if ws > 1 else "single")
     nthreads = os.cpu_count() or 1
-    layer = sm.MoeLayer(cfg, f"cuda:{local}" if torch.cuda.is_available() else "cpu", want_logits=False,
-                        want_out16=False) if torch.cuda.is_available() else None
-    if layer is None:
-        print(json.dumps({"impl": "reference", "unavailable": "no GPU to hold the synthetic workload"}))
-        return
-    device_inputs(layer, 0)
-    torch.cuda.synchronize()
+    cap = cfg.capacity()
+    inp = OI.make_inputs(cfg, 0)
     for _ in range(args.warmup):
-        cpu_measure(layer, args.ref_sample_tokens, nthreads)
+        oracle_measure(inp, cfg, cap, args.ref_sample_tokens, nthreads)
     vals = []
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        v, _, _, S = cpu_measure(layer, args.ref_sample_tokens, nthreads)
+        v, _, _, S = oracle_measure(inp, cfg, cap, args.ref_sample_tokens, nthreads)
         vals.append(v)
     wall = time.perf_counter() - t0
     value = statistics.mean(vals)
@@ -444,12 +477,83 @@ def run_reference_arm(args, ws, rank, local):
         "impl": "reference", "metric": f"MoE-layer tokens/s ({args.config})", "value": value,
         "unit": "tokens/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1000.0 * wall / args.steps, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": dtype_name(cfg), "data": "synthetic",
-        "config": cfg_json(args.config, cfg, layer.cap),
+        "vs_baseline": None, "dtype": dtype_name(cfg),
+        "data": "synthetic (seeded normal: x N(0,1), router N(0,0.02), W N(0,1/sqrt(fan_in)); host-drawn)",
+        "config": {**cfg_json(args.config, cfg, run_cap(args, cfg, ws, mode)),
+                   "parallelism": parallelism_desc(args, cfg, ws, run_cap(args, cfg, ws, mode), mode)},
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": nthreads, "kind": "port",
                          "sample": sample},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }))
+
+
+# ---------------------------------------------------------------------------
+def ep_parity(layer, cfg, ws, rank, dev, glob, int8_full=None):
+    """Checks the expert-parallel layer's last call against the single-GPU
+    layer on the same tokens and weights: every rank's tokens, router and
+    experts are all-gathered, rank 0 runs one MoeLayer over all of them
+    (all E experts, all ranks' tokens, the same batches and CAP) and compares
+    each rank's expert indices and f32 output rows.  Runs after the timed
+    region.  Returns {"idx_equal", "out_equal", "max_abs_rel", ...} on rank 0."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    import sparsemoe_b200 as sm
+
+    def gather(t):
+        t = t.contiguous()
+        out = torch.empty((ws,) + tuple(t.shape), dtype=t.dtype, device=dev)
+        dist.all_gather_into_tensor(out, t)
+        return out
+
+    def experts(t):
+        """[e_loc, ...] per rank -> [E, ...] in global expert order."""
+        g = gather(t)
+        if layer.placement == "strided":        # rank q holds experts q, q + P, ...
+            g = g.transpose(0, 1)
+        return g.reshape((cfg.num_experts,) + tuple(t.shape[1:]))
+
+    B, N = cfg.num_batches, cfg.tokens
+    xs, outs, idxs = gather(layer.x[: cfg.T]), gather(layer.out[: cfg.T]), gather(layer.idx[: cfg.T])
+    wts = {n: experts(getattr(layer, n)) for n in ("wg", "wu", "wd")}
+    extra = {k: [experts(t) for t in layer.weights[k]] for k in ("w_scale", "w4", "fp4g") if layer.weights.get(k)}
+    if rank != 0:
+        torch.cuda.synchronize(dev)
+        return None
+    if glob:     # every batch of P*N tokens split over the ranks in token order
+        full = sm.LayerConfig(B, N * ws, cfg.d_model, cfg.d_ff, cfg.num_experts, cfg.top_k, cfg.capacity_factor,
+                              cfg.dtype, cfg.router_f32, cfg.zipf_s, layer.cap, cfg.act_scale, cfg.mid_scale)
+        order = lambda t: t.reshape(ws, B, N, -1).transpose(0, 1).reshape(B * ws * N, -1)  # noqa: E731
+    else:        # per-rank batches, rank-major
+        full = sm.LayerConfig(B * ws, N, cfg.d_model, cfg.d_ff, cfg.num_experts, cfg.top_k, cfg.capacity_factor,
+                              cfg.dtype, cfg.router_f32, cfg.zipf_s, cfg.cap, cfg.act_scale, cfg.mid_scale)
+        order = lambda t: t.reshape(ws * B * N, -1)  # noqa: E731
+    single = sm.MoeLayer(full, dev, want_logits=False, want_out16=False)
+    if cfg.int8:
+        single.load({**int8_full, "x": np.zeros((0, cfg.d_model), np.uint16)} if full.T == 0 else
+                    {**int8_full, "x": order(xs).view(torch.int16).cpu().numpy().view(np.uint16)})
+    else:
+        single.x.copy_(order(xs))
+        single.wr.copy_(layer.wr)
+        for n in ("wg", "wu", "wd"):
+            getattr(single, n).copy_(wts[n])
+        single.bias = layer.bias
+        if "w_scale" in extra:
+            single.wscale = extra["w_scale"]
+        if "w4" in extra:
+            single.w4sz = extra["w4"]
+        if "fp4g" in extra:
+            single.fp4g = extra["fp4g"]
+    single.forward()
+    single.sync_check()
+    a, b = order(outs), single.out[: full.T]
+    idx_equal = bool(torch.equal(order(idxs), single.idx[: full.T]))
+    out_equal = bool(torch.equal(a, b))
+    err = float((a - b).abs().max() / b.abs().max().clamp_min(1e-30))
+    return {"idx_equal": idx_equal, "out_equal": out_equal, "max_abs_rel": err, "ranks_checked": ws,
+            "tokens_checked": full.T,
+            "how": "all ranks' tokens and experts gathered; one single-GPU MoeLayer over them on rank 0; "
+                   "expert indices and f32 output rows of every rank compared"}
 
 
 # ---------------------------------------------------------------------------
@@ -465,6 +569,7 @@ def run_ep(args, cfg, ws, rank, local, dev):
     placement = "strided" if glob and args.ep_transport == "peer" else "contiguous"
     layer = ExpertParallelLayer(cfg, dev, chunks=args.ep_chunks, global_batch=glob, transport=args.ep_transport,
                                 placement=placement)
+    full = None
     if cfg.int8:
         # the reference's per-tensor int8 format: host generator + host quantiser (all experts; each
         # rank keeps its own), this rank's tokens
@@ -526,7 +631,21 @@ def run_ep(args, cfg, ws, rank, local, dev):
     e1.record(stream)
     torch.cuda.synchronize(dev)
     barrier(ws)
-    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / K, ws, dev)
+    serial_ms = max_over_ranks(e0.elapsed_time(e1) / K, ws, dev)
+
+    # the same double-buffered copy stream as the one-GPU line: step i+1's
+    # tokens arrive and step i-1's output leaves while step i computes
+    def ep_set_io(xb, ob):
+        layer.x, layer.out16 = xb, ob
+        if layer.n_chunks == 1:
+            layer.chunks[0].x, layer.chunks[0].out16 = xb[: cfg.T], ob[: cfg.T]
+    barrier(ws)
+    pipe_ms = pipelined_e2e(layer, stream, x_host, out_host, K, args.warmup, dev, set_io=ep_set_io)
+    e2e_ms = max_over_ranks(pipe_ms, ws, dev)
+    barrier(ws)
+    # the last call's output against one GPU running all experts on all ranks' tokens (untimed)
+    parity = ep_parity(layer, cfg, ws, rank, dev, glob, full)
+    barrier(ws)
     peaks, peak_src = load_peaks()
     peak_tf = float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
     if cfg.int8 or cfg.int8ch or cfg.fp8:
@@ -543,26 +662,20 @@ def run_ep(args, cfg, ws, rank, local, dev):
         "scaling": "weak", "vs_baseline": None, "dtype": dtype_name(cfg),
         "data": "synthetic (seeded torch normal: x N(0,1), router N(0,0.02), W N(0,1/sqrt(fan_in)))",
         "config": {**cfg_json(args.config, cfg, layer.cap),
-                   "parallelism": f"ep{ws} (expert parallel, {cfg.num_experts // ws} experts per GPU, "
-                                  + ("rows over NVLink peer memory: copy-engine dispatch, down-GEMM epilogue "
-                                     "stores the results into the senders' buffers; "
-                                     if layer.transport == "peer" else
-                                     f"NCCL all-to-all dispatch/return on a second stream, {layer.n_chunks} "
-                                     f"pipelined batch chunks; ")
-                                  + f"{cfg.T} tokens per GPU"
-                                  + (f"; each batch split over the {ws} ranks, global CAP {layer.cap}, "
-                                     f"{layer.placement} expert ownership)"
-                                     if glob else ", per-rank batches)")},
+                   "parallelism": parallelism_desc(args, cfg, ws, layer.cap, "ep")},
         "roofline": {"bound": "tensor", "achieved": ach_min, "peak": peak_tf, "unit": "TFLOP/s",
                      "frac": ach_min / peak_tf, "traffic": None,
                      "kernel": "expert_ffn phase (up/gate + down tcgen05 GEMMs), slowest rank",
                      "peak_source": f"{peak_src} bf16_tflops_sustained" + (" x 2 (8-bit)" if cfg.int8 or cfg.int8ch or cfg.fp8 else "")},
         "phases_ms": phase_ms,
         "e2e": {"value": ws * cfg.T / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
-                "path": "ExpertParallelLayer.forward (moe_stage_route / moe_stage_expert_ffn / moe_stage_combine)"},
+                "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms, "serial_ms_per_step": serial_ms,
+                "path": "ExpertParallelLayer.forward (moe_stage_route / moe_stage_expert_ffn / moe_stage_combine) "
+                        "each step, pinned host x in and 16-bit output out every step on a copy stream, "
+                        "double-buffered (serial_ms_per_step: copy in, layer, copy out on one stream)"},
         "gpu_launches": kernels_per_step(cfg) * K,
         "clocks": clocks.summary(),
+        "ep_parity": parity,
     }
     if rank == 0:
         print(json.dumps(result))
@@ -719,7 +832,7 @@ def main():
         "dtype": dtype_name(cfg),
         "data": "synthetic (seeded normal: x N(0,1), router N(0,0.02), W N(0,1/sqrt(fan_in)))",
         "config": {**cfg_json(args.config, cfg, layer.cap),
-                   "parallelism": "single GPU" if ws == 1 else f"{ws} independent replicas (no data-path collective)"},
+                   "parallelism": parallelism_desc(args, cfg, ws, layer.cap, mode)},
         "roofline": {"bound": "tensor", "achieved": ach_up, "peak": peak_tf, "unit": "TFLOP/s",
                      "frac": ach_up / peak_tf, "traffic": traffic,
                      "kernel": "expert_up_gate_gemm (tcgen05, fused SwiGLU)",

@@ -114,8 +114,10 @@ int moe_solve_v2(const struct MoEArgs* args, const MoeDims* dims, cudaStream_t s
 // the device synchronisation of cudaMalloc/cudaFree).  Calls needing more
 // scratch than the array (moe_workspace_bytes) fail with MOE_ERR_UNSUPPORTED.
 // All calls on a device share the array: calls that overlap on the GPU race.
-// The first call on a device resolves the array's address (cudaGetSymbolAddress);
-// make it before any stream capture.
+// The first call on a device resolves the array's address (cudaGetSymbolAddress)
+// and caches it for the life of the CUDA context (stale after cudaDeviceReset);
+// make it before any stream capture.  dims->act_scale is honoured as in
+// moe_solve_v2; dims->scratch must be null (MOE_ERR_INVALID_ARG otherwise).
 int moe_solve_v2_noalloc(const struct MoEArgs* args, const MoeDims* dims, cudaStream_t stream);
 size_t moe_noalloc_scratch_bytes(void);
 

@@ -23,7 +23,14 @@
 //    race on the array; order them on one stream or with events.
 //  * The first call on each device looks up the array's device address with
 //    cudaGetSymbolAddress (with that device current) and caches it; make that
-//    first call before any stream capture.
+//    first call before any stream capture.  The cache lives as long as the
+//    process's CUDA context: after cudaDeviceReset the cached address is
+//    stale, so a process that resets a device must not call this entry point
+//    on that device again.
+//  * MoeDims.act_scale is honoured as in moe_solve_v2 (the dynamic formats'
+//    per-row activation scales go to the caller's buffer instead of the
+//    array; the size check still counts them).  MoeDims.scratch must be
+//    null: a caller that has scratch of its own calls moe_solve_v2 with it.
 #include "moe_internal.h"
 
 #include <mutex>
@@ -69,6 +76,10 @@ extern "C" int moe_solve_v2_noalloc(const MoEArgs* a, const MoeDims* dims, cudaS
     if (rc != MOE_OK) return rc;
     rc = check_args(a, s.dtype);
     if (rc != MOE_OK) return rc;
+    if (dims->scratch) {
+        set_error("moe_solve_v2_noalloc: MoeDims.scratch must be null (pass caller scratch to moe_solve_v2)");
+        return MOE_ERR_INVALID_ARG;
+    }
     const size_t need = workspace_bytes(s);
     if (need > kNoAllocScratchBytes) {
         set_error("moe_solve_v2_noalloc: this call needs %zu bytes of scratch, the static array holds %zu "
@@ -88,6 +99,7 @@ extern "C" int moe_solve_v2_noalloc(const MoEArgs* a, const MoeDims* dims, cudaS
     if (rc != MOE_OK) return rc;
     Workspace ws;
     carve_workspace(base, s, &ws);
+    if (dims->act_scale) ws.a_scale = dims->act_scale;
     note_status_word(dev, ws.status);
     return enqueue_layer(a, dims, s, ws, num_sms, stream);
 }

@@ -481,9 +481,17 @@ class ExpertParallelLayer:
     def forward(self, stream=None, timing=None):
         """One layer call.  `timing` (optional dict) receives torch.cuda.Event
         lists: 'start', 'routed', 'ffn' (pairs per chunk), 'combine', 'end'."""
+        torch = self.torch
+        S = stream if stream is not None else torch.cuda.current_stream(self.device)
+        # every torch op and collective below (all_gather of the route totals
+        # and kept-row table, the slot-base and count sums) then runs on S, in
+        # order with the library kernels enqueued on S
+        with torch.cuda.stream(S):
+            return self._forward(S, timing)
+
+    def _forward(self, S, timing):
         torch, dist = self.torch, self.dist
         cfg = self.cfg
-        S = stream if stream is not None else torch.cuda.current_stream(self.device)
         C = self.comm_stream
         sp = ctypes.c_void_p(S.cuda_stream)
 

@@ -240,3 +240,24 @@ def test_nan_token_selects_nothing(gpu):
     L, ref, _ = full_check(cfg, gpu, inputs=inp)
     assert (L.idx.cpu().numpy()[5] == -1).all()
     assert float(L.out[5].abs().max()) == 0.0
+
+
+def test_config2_mixtral_shape_token_sample(gpu):
+    """BASELINE config 2, the shape bench.py times (8 batches x 2048 tokens,
+    d=4096, f=14336, E=8, k=2, cf=1.25, bf16): logits, indices, slots, drops
+    and counts of all 16384 tokens bit-exact vs the oracle; the output checked
+    on a sample of 256 tokens (the first 128 of batch 0 and of batch 7) within
+    the 1e-2 bar."""
+    cfg = sm.LayerConfig(8, 2048, 4096, 14336, 8, 2, 1.25, dtype=sm.DTYPE_BF16)
+    inp = sm.make_inputs(cfg, 0)
+    L = run(cfg, inp, gpu)
+    assert L.cap == 640
+    r0 = O.forward(inp, cfg, 0, 128)
+    check_routing(L, r0, cfg)
+    r7 = O.ffn_combine(inp["x"], inp["wg"], inp["wu"], inp["wd"], cfg.num_batches, cfg.tokens, cfg.d_model,
+                       cfg.d_ff, cfg.num_experts, cfg.top_k, True, r0["idx"], r0["w"], r0["route_slot"],
+                       cfg.T - 128, cfg.T)
+    out = L.out.cpu().numpy()
+    assert max_abs_rel(out[:128], r0["out"]) <= TOL_16
+    assert max_abs_rel(out[cfg.T - 128:], r7) <= TOL_16
+    assert max_abs_rel(L.out16.float().cpu().numpy()[:128], r0["out"]) <= TOL_16
