@@ -691,7 +691,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="mixtral_bf16")
     ap.add_argument("--cpu-sample-tokens", type=int, default=1024)
-    ap.add_argument("--ref-sample-tokens", type=int, default=128)
+    ap.add_argument("--ref-sample-tokens", type=int, default=512)
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline measurement")
     ap.add_argument("--graph", action="store_true",
                     help="also time the layer captured as one CUDA graph (the decode path)")

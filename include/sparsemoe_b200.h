@@ -37,6 +37,18 @@ extern "C" {
                             // gate/up [E, d/16, f], down [E, f/16, d]) and one f32 global scale per
                             // expert matrix (MoeDims.fp4_global_*); w = e2m1 * scale * global;
                             // bf16 x, router and h
+#define MOE_DTYPE_INT4_PTX 7   // the reference's int4 format (kernels/capacity_int4_ptx.cu:166-307,396-486,
+                               // 586-675; inputs/data.cu:89-140): per-tensor int4 weights (max/7) packed
+                               // transposed, per expert [N/2][K] bytes, columns 2p (low nibble) and 2p+1
+                               // (high) of row k at byte (p, k), in the MoEArgs *_int4 fields; f16 x and
+                               // router; x and h quantised per tensor to int4 values rn(clamp(v/s, -7, 7)),
+                               // kept one per byte in per_expert_wmma_inputs_int8 and
+                               // hidden_mlp_layer_1_out_int8; s32 accumulate; the MoEArgs scales.
+                               // The library unpacks the weights into its scratch every call.
+#define MOE_DTYPE_FP8 8        // the reference's fp8 format (kernels/capacity_fp8_ptx.cu:98-220,330-395,
+                               // 566-670; inputs/data.cu:142-150): e4m3 weights in the MoEArgs *_fp8
+                               // fields with per-tensor scales (the builder's are 1.0); f16 x and router;
+                               // x and h quantised as e4m3(clamp(v/s, -448, 448)); f32 accumulate
 #define MOE_DTYPE_INT8_CHANNEL 5   // int8 weights with one f32 scale per output channel (MoeDims.w_scale_*:
                                    // gate/up [E, f], down [E, d]); x quantised per token (amax / 127) on
                                    // the fly, h per token and 128-feature block; s32 accumulate; bf16 x
@@ -99,7 +111,12 @@ typedef struct MoeDims {
 // reference's include/config.h), synchronises the device, prints
 // "Total duration via cudaEventRecord: %.3f ms" and exits(1) on any error,
 // exactly as the reference launcher does.  The format path is chosen from the
-// non-null weight fields (fp16 weights -> the `capacity` semantics).
+// non-null weight fields, as the reference's allocators fill them
+// (drivers/main.cu:84-106): fp16 weights -> `capacity` (or the bf16 / other
+// 16-bit-field formats set by moe_set_solve_dims); *_int4 weights ->
+// `capacity_int4_ptx` (MOE_DTYPE_INT4_PTX); *_int8 weights alone ->
+// `capacity_int8_ptx` (MOE_DTYPE_INT8); *_fp8 weights -> `capacity_fp8_ptx`
+// (MOE_DTYPE_FP8).
 void solve(struct MoEArgs args);
 
 // Status-returning, stream-ordered form of solve() with runtime dims.
@@ -267,6 +284,15 @@ const char* moe_last_error(void);
 // values, scale = max|x| / qmax (1 if all zero), q = nearbyint(clamp(x/scale,
 // -qmax, qmax)).  qmax = 127 (int8) or 7 (int4 values).  Returns the scale.
 float moe_quantize_per_tensor(const uint16_t* src_f16, size_t n, int8_t* dst, float qmax);
+
+// Reference inputs/data.cu:89-140 (quantize_symmetric_per_tensor_int4_packed_transposed,
+// its packing step): int4 values of E row-major [K, N] matrices -> per expert
+// [N/2][K] bytes, column 2p in the low and 2p+1 in the high nibble of byte (p, k).
+void moe_pack_int4_transposed(const int8_t* q, int E, int K, int N, uint8_t* out);
+
+// Reference inputs/data.cu:142-150 (quantize_per_tensor_fp8_e4m3): n fp16
+// values cast to e4m3 (nearest even, saturating to +-448).
+void moe_cast_e4m3(const uint16_t* src_f16, size_t n, uint8_t* dst);
 
 // FP8 block quantiser for weights [E, K, N] (16-bit, bf16 != 0: bf16):
 // per expert and 128x128 block, s = amax / 448 (1 if the block is zero),

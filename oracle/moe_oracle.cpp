@@ -407,6 +407,17 @@ void oracle_ffn_combine_nvfp4(const uint16_t* x, const uint8_t* pg, const uint8_
              route_slot, t_begin, t_end, out, nthreads);
 }
 
+}  // extern "C"
+
+namespace {
+void int_per_tensor_impl(const uint16_t* x, const int8_t* wg, const int8_t* wu, const int8_t* wd,
+                         float s_in, float s_gate, float s_up, float s_mid, float s_down, int d, int f,
+                         int E, int k, const int* idx, const float* w, const int* route_slot,
+                         int64_t t_begin, int64_t t_end, float* out, int nthreads, float qlo, float qhi);
+}  // namespace
+
+extern "C" {
+
 // int8 path (reference kernels/capacity_int8_ptx.cu): per-tensor quantised
 // operands, exact integer GEMMs, the reference's dequant / SiLU / requant
 // arithmetic in f32.
@@ -419,6 +430,117 @@ void oracle_ffn_combine_int8(const uint16_t* x, const int8_t* wg, const int8_t* 
                              float s_in, float s_gate, float s_up, float s_mid, float s_down, int d, int f,
                              int E, int k, const int* idx, const float* w, const int* route_slot,
                              int64_t t_begin, int64_t t_end, float* out, int nthreads) {
+    int_per_tensor_impl(x, wg, wu, wd, s_in, s_gate, s_up, s_mid, s_down, d, f, E, k, idx, w, route_slot, t_begin,
+                        t_end, out, nthreads, -128.f, 127.f);
+}
+
+// The reference's int4 format (kernels/capacity_int4_ptx.cu): the int8 path
+// with every activation clamp at [-7, 7] (:396-441 the gather, :446-486 the
+// requant) on int4 weights stored packed transposed (inputs/data.cu:89-140:
+// per expert [N/2][K] bytes, column 2p in the low nibble of byte (p, k),
+// 2p+1 in the high nibble), unpacked here by that definition; the s4 x s4
+// products are summed exactly (mma.m16n8k64.s4 accumulates in s32).
+void oracle_ffn_combine_int4ptx(const uint16_t* x, const uint8_t* pg, const uint8_t* pu, const uint8_t* pd,
+                                float s_in, float s_gate, float s_up, float s_mid, float s_down, int d, int f,
+                                int E, int k, const int* idx, const float* w, const int* route_slot,
+                                int64_t t_begin, int64_t t_end, float* out, int nthreads) {
+    auto unpack = [&](const uint8_t* P, int K, int N) {
+        std::vector<int8_t> q((size_t)E * K * N);
+        for (int e = 0; e < E; ++e)
+            for (int n = 0; n < N; ++n)
+                for (int kk = 0; kk < K; ++kk) {
+                    const uint8_t b = P[(size_t)e * (N / 2) * K + (size_t)(n / 2) * K + kk];
+                    const int nib = (n & 1) ? (b >> 4) : (b & 15);
+                    q[(size_t)e * K * N + (size_t)kk * N + n] = (int8_t)(nib >= 8 ? nib - 16 : nib);
+                }
+        return q;
+    };
+    const std::vector<int8_t> g = unpack(pg, d, f), u = unpack(pu, d, f), dn = unpack(pd, f, d);
+    int_per_tensor_impl(x, g.data(), u.data(), dn.data(), s_in, s_gate, s_up, s_mid, s_down, d, f, E, k, idx, w,
+                        route_slot, t_begin, t_end, out, nthreads, -7.f, 7.f);
+}
+
+// The reference's fp8 format (kernels/capacity_fp8_ptx.cu): per-tensor e4m3
+// operands with f32 accumulation and the int8 path's scale arithmetic.
+//   a = e4m3(clamp(x / s_in, -448, 448))                          :330-352
+//   U, G = sums of e4m3 products (exact in double, rounded once to f32)
+//   uf = U*(s_in*s_up), gf = G*(s_in*s_gate)
+//   h = e4m3(clamp(uf * gf/(1+exp(-gf)) * (1/s_mid), -448, 448))   :362-395
+//   y = Y * (s_mid*s_down)                                         :566-600
+//   out = sum_l w_l * y_l in route order
+void oracle_ffn_combine_fp8pt(const uint16_t* x, const uint8_t* wg, const uint8_t* wu, const uint8_t* wd,
+                              float s_in, float s_gate, float s_up, float s_mid, float s_down, int d, int f,
+                              int E, int k, const int* idx, const float* w, const int* route_slot,
+                              int64_t t_begin, int64_t t_end, float* out, int nthreads) {
+    std::vector<std::vector<int64_t>> routes(E);
+    for (int64_t t = t_begin; t < t_end; ++t)
+        for (int l = 0; l < k; ++l) {
+            const int64_t r = t * k + l;
+            if (route_slot[r] >= 0) routes[idx[r]].push_back(r);
+        }
+    const float deq_up = s_in * s_up, deq_gate = s_in * s_gate, inv_mid = 1.0f / s_mid, deq_down = s_mid * s_down;
+    float lut[256];
+    for (int i = 0; i < 256; ++i) lut[i] = e4m3_to_f32((uint8_t)i);
+    std::vector<float> y((size_t)(t_end - t_begin) * k * d, 0.0f);
+    parallel_for((int64_t)E, nthreads, [&](int64_t e) {
+        const uint8_t* Wg = wg + (size_t)e * d * f;
+        const uint8_t* Wu = wu + (size_t)e * d * f;
+        const uint8_t* Wd = wd + (size_t)e * f * d;
+        std::vector<double> ag(f), au(f), ay(d);
+        std::vector<float> a(d), h(f);
+        for (const int64_t route : routes[e]) {
+            const int64_t tok = route / k;
+            for (int j = 0; j < d; ++j)
+                a[j] = lut[f32_to_e4m3(fminf(fmaxf(f16_to_f32(x[tok * d + j]) / s_in, -448.f), 448.f))];
+            std::fill(ag.begin(), ag.end(), 0.0);
+            std::fill(au.begin(), au.end(), 0.0);
+            for (int j = 0; j < d; ++j) {
+                if (a[j] == 0.0f) continue;
+                const double av = a[j];
+                for (int c = 0; c < f; ++c) {
+                    ag[c] += av * lut[Wg[(size_t)j * f + c]];
+                    au[c] += av * lut[Wu[(size_t)j * f + c]];
+                }
+            }
+            for (int c = 0; c < f; ++c) {
+                const float uf = (float)au[c] * deq_up, gf = (float)ag[c] * deq_gate;
+                const float silu = gf / (1.0f + expf(-gf));
+                h[c] = lut[f32_to_e4m3(fminf(fmaxf(uf * silu * inv_mid, -448.f), 448.f))];
+            }
+            std::fill(ay.begin(), ay.end(), 0.0);
+            for (int j = 0; j < f; ++j) {
+                if (h[j] == 0.0f) continue;
+                const double hv = h[j];
+                for (int c = 0; c < d; ++c) ay[c] += hv * lut[Wd[(size_t)j * d + c]];
+            }
+            float* dst = &y[((size_t)(route - t_begin * k)) * d];
+            for (int c = 0; c < d; ++c) dst[c] = (float)ay[c] * deq_down;
+        }
+    });
+    parallel_for(t_end - t_begin, nthreads, [&](int64_t i) {
+        const int64_t t = t_begin + i;
+        float* o = out + t * d;
+        for (int c = 0; c < d; ++c) o[c] = 0.0f;
+        for (int l = 0; l < k; ++l) {
+            const int64_t r = t * k + l;
+            if (route_slot[r] < 0) continue;
+            const float wl = w[r];
+            const float* yr = &y[((size_t)(r - t_begin * k)) * d];
+            for (int c = 0; c < d; ++c) {
+                volatile float p = wl * yr[c];
+                o[c] = o[c] + p;
+            }
+        }
+    });
+}
+
+}  // extern "C"
+
+namespace {
+void int_per_tensor_impl(const uint16_t* x, const int8_t* wg, const int8_t* wu, const int8_t* wd,
+                         float s_in, float s_gate, float s_up, float s_mid, float s_down, int d, int f,
+                         int E, int k, const int* idx, const float* w, const int* route_slot,
+                         int64_t t_begin, int64_t t_end, float* out, int nthreads, float qlo, float qhi) {
     std::vector<std::vector<int64_t>> routes(E);
     for (int64_t t = t_begin; t < t_end; ++t)
         for (int l = 0; l < k; ++l) {
@@ -442,7 +564,7 @@ void oracle_ffn_combine_int8(const uint16_t* x, const int8_t* wg, const int8_t* 
             const int64_t tok = routes[e][r0 + r] / k;
             for (int j = 0; j < d; ++j) {
                 const float v = f16_to_f32(x[tok * d + j]) / s_in;
-                a[(size_t)r * d + j] = (int32_t)nearbyintf(fminf(fmaxf(v, -128.f), 127.f));
+                a[(size_t)r * d + j] = (int32_t)nearbyintf(fminf(fmaxf(v, qlo), qhi));
             }
         }
         std::fill(accg.begin(), accg.end(), 0);
@@ -470,7 +592,7 @@ void oracle_ffn_combine_int8(const uint16_t* x, const int8_t* wg, const int8_t* 
                 const float gf = (float)accg[(size_t)r * f + c] * deq_gate;
                 const float silu = gf / (1.0f + expf(-gf));
                 const float fused = uf * silu;
-                h[(size_t)r * f + c] = (int32_t)nearbyintf(fminf(fmaxf(fused * inv_mid, -128.f), 127.f));
+                h[(size_t)r * f + c] = (int32_t)nearbyintf(fminf(fmaxf(fused * inv_mid, qlo), qhi));
             }
         std::fill(accy.begin(), accy.end(), 0);
         for (int j = 0; j < f; ++j) {
@@ -504,6 +626,9 @@ void oracle_ffn_combine_int8(const uint16_t* x, const int8_t* wg, const int8_t* 
         }
     });
 }
+}  // namespace
+
+extern "C" {
 
 // FP8 block-scaled path: x (bf16) quantised per 1x128
 // block (s = amax/448, 1 if zero), weights e4m3 with scales per 128x128 block;

@@ -45,6 +45,10 @@ def lib() -> ctypes.CDLL:
         F = ctypes.c_float
         L.oracle_ffn_combine_int8.argtypes = [P, P, P, P, F, F, F, F, F, I, I, I, I, P, P, P, ctypes.c_int64,
                                               ctypes.c_int64, P, I]
+        for name in ("oracle_ffn_combine_int4ptx", "oracle_ffn_combine_fp8pt"):
+            fn = getattr(L, name)
+            fn.restype = None
+            fn.argtypes = [P, P, P, P, F, F, F, F, F, I, I, I, I, P, P, P, ctypes.c_int64, ctypes.c_int64, P, I]
         L.oracle_ffn_combine_fp8.restype = None
         L.oracle_ffn_combine_fp8.argtypes = [P, P, P, P, P, P, P, I, I, I, I, P, P, P, ctypes.c_int64,
                                              ctypes.c_int64, P, I]
@@ -122,6 +126,22 @@ def ffn_combine_int8(x, q, cfg, idx, w, route_slot, t_begin=0, t_end=None, nthre
                                   _ptr(np.ascontiguousarray(idx, np.int32)), _ptr(np.ascontiguousarray(w, np.float32)),
                                   _ptr(np.ascontiguousarray(route_slot, np.int32)), t_begin, t_end, _ptr(out),
                                   nthreads or threads())
+    return out[t_begin:t_end]
+
+
+def ffn_combine_per_tensor(x, q, cfg, idx, w, route_slot, t_begin=0, t_end=None, nthreads=None):
+    """The reference's int4 (capacity_int4_ptx.cu: packed-transposed weights,
+    clamps at +-7) or fp8 (capacity_fp8_ptx.cu: e4m3 operands) format for
+    tokens [t_begin, t_end).  `q` holds wg_q/wu_q/wd_q and the five scales."""
+    T = cfg.T
+    t_end = T if t_end is None else t_end
+    out = np.zeros((T, cfg.d_model), np.float32)
+    ws = [np.ascontiguousarray(q[n], np.uint8) for n in ("wg_q", "wu_q", "wd_q")]
+    fn = lib().oracle_ffn_combine_int4ptx if cfg.int4ptx else lib().oracle_ffn_combine_fp8pt
+    fn(_ptr(np.ascontiguousarray(x, np.uint16)), *(_ptr(a) for a in ws), q["s_in"], q["s_gate"], q["s_up"],
+       q["s_mid"], q["s_down"], cfg.d_model, cfg.d_ff, cfg.num_experts, cfg.top_k,
+       _ptr(np.ascontiguousarray(idx, np.int32)), _ptr(np.ascontiguousarray(w, np.float32)),
+       _ptr(np.ascontiguousarray(route_slot, np.int32)), t_begin, t_end, _ptr(out), nthreads or threads())
     return out[t_begin:t_end]
 
 
@@ -206,6 +226,9 @@ def forward(inputs: dict, cfg, t_begin=0, t_end=None, nthreads=None):
     elif getattr(cfg, "int8ch", False):
         r["out"] = ffn_combine_int8ch(inputs["x"], inputs, cfg, r["idx"], r["w"], r["route_slot"], t_begin, t_end,
                                       nthreads)
+    elif getattr(cfg, "int4ptx", False) or getattr(cfg, "fp8pt", False):
+        r["out"] = ffn_combine_per_tensor(inputs["x"], inputs, cfg, r["idx"], r["w"], r["route_slot"], t_begin,
+                                          t_end, nthreads)
     elif getattr(cfg, "int8", False):
         r["out"] = ffn_combine_int8(inputs["x"], inputs, cfg, r["idx"], r["w"], r["route_slot"], t_begin, t_end,
                                     nthreads)

@@ -20,8 +20,12 @@ LIB_PATH = Path(os.environ["SPARSEMOE_B200_LIB"]) if os.environ.get("SPARSEMOE_B
     _PKG / "libsparsemoe_b200.so"
 
 from .config import (  # noqa: F401  (re-exported)
-    MOE_OK, MOE_ERR_INVALID_ARG, MOE_ERR_UNSUPPORTED, MOE_ERR_CUDA, MOE_ERR_TIMEOUT, MOE_ERR_NO_KERNEL, DTYPE_F16, DTYPE_BF16, DTYPE_INT8, DTYPE_FP8_BLOCK, DTYPE_W4A16, DTYPE_INT8_CHANNEL, DTYPE_NVFP4, ROUTER_SAME, ROUTER_F32, MoeError, MoEArgs, MoeDims, MoeWeightArray, MoeWeightFile, LayerConfig, _p)
+    MOE_OK, MOE_ERR_INVALID_ARG, MOE_ERR_UNSUPPORTED, MOE_ERR_CUDA, MOE_ERR_TIMEOUT, MOE_ERR_NO_KERNEL,
+    DTYPE_F16, DTYPE_BF16, DTYPE_INT8, DTYPE_FP8_BLOCK, DTYPE_W4A16, DTYPE_INT8_CHANNEL, DTYPE_NVFP4,
+    DTYPE_INT4_PTX, DTYPE_FP8, ROUTER_SAME, ROUTER_F32, MoeError, MoEArgs, MoeDims, MoeWeightArray,
+    MoeWeightFile, LayerConfig, _p)
 from . import config as _config
+
 
 def _load() -> ctypes.CDLL:
     if not LIB_PATH.exists():
@@ -68,6 +72,8 @@ def _load() -> ctypes.CDLL:
         "moe_fill_normal_16": (None, [_p, ctypes.c_size_t, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_float,
                                       ctypes.c_int]),
         "moe_quantize_per_tensor": (ctypes.c_float, [_p, ctypes.c_size_t, _p, ctypes.c_float]),
+        "moe_pack_int4_transposed": (None, [_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, _p]),
+        "moe_cast_e4m3": (None, [_p, ctypes.c_size_t, _p]),
         "moe_quantize_int4_g128": (None, [_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _p, _p, _p]),
         "moe_quantize_fp8_blocks": (None, [_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _p, _p]),
         "moe_quantize_int8_channel": (None, [_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _p, _p]),
@@ -164,13 +170,29 @@ def make_inputs(cfg: LayerConfig, seed: int = 0) -> dict:
             q, sc = quantize_int8_channel(out[n], bf16=True)
             out[n + "_q"], out[key] = q, sc
     out["bias"] = zipf_bias(E, cfg.zipf_s) if cfg.zipf_s > 0 else None
-    if cfg.int8:
-        # reference inputs/data.cu:315-322: per-tensor int8 weights, placeholder activation scales
+    if cfg.per_tensor:
+        # reference inputs/data.cu:275-390: per-tensor int8 (max/127) or int4 (max/7, packed
+        # transposed) weights, or a direct e4m3 cast with unit scales; activation scales from cfg
+        # (the reference's placeholders are 1.0)
         for n in ("wg", "wu", "wd"):
+            name = "s_" + {"wg": "gate", "wu": "up", "wd": "down"}[n]
+            if cfg.fp8pt:
+                q = np.empty(out[n].size, np.uint8)
+                lib.moe_cast_e4m3(out[n].ctypes.data, out[n].size, q.ctypes.data)
+                out[n + "_q"], out[name] = q.reshape(out[n].shape), 1.0
+                continue
             q = np.empty(out[n].size, np.int8)
-            scale = lib.moe_quantize_per_tensor(out[n].ctypes.data, out[n].size, q.ctypes.data, 127.0)
-            out[n + "_q"] = q.reshape(out[n].shape)
-            out["s_" + {"wg": "gate", "wu": "up", "wd": "down"}[n]] = float(scale)
+            scale = lib.moe_quantize_per_tensor(out[n].ctypes.data, out[n].size, q.ctypes.data,
+                                                7.0 if cfg.int4ptx else 127.0)
+            q = q.reshape(out[n].shape)
+            out[name] = float(scale)
+            if cfg.int4ptx:
+                E_, K_, N_ = q.shape
+                packed = np.empty((E_, N_ // 2, K_), np.uint8)
+                lib.moe_pack_int4_transposed(q.ctypes.data, E_, K_, N_, packed.ctypes.data)
+                out[n + "_i4"] = q                  # the unpacked int4 values (for checks)
+                q = packed
+            out[n + "_q"] = q
         out["s_in"] = float(np.float32(cfg.act_scale))
         out["s_mid"] = float(np.float32(cfg.mid_scale))
     return out
@@ -186,7 +208,7 @@ def save_weights(path: str, cfg: LayerConfig, inputs: dict) -> None:
     the tokens `x`, the per-tensor int8 scales as one f32 array."""
     arrays = {k: np.ascontiguousarray(v) for k, v in inputs.items()
               if k not in ("x",) + _INT8_SCALES and v is not None and isinstance(v, np.ndarray)}
-    if cfg.int8:
+    if cfg.per_tensor:
         arrays["int8_scales"] = np.array([inputs[k] for k in _INT8_SCALES], np.float32)
     if len(arrays) > 16:
         raise ValueError("more than 16 arrays")
@@ -288,4 +310,4 @@ __all__ = ["MoEArgs", "MoeDims", "LayerConfig", "MoeLayer", "make_inputs", "capa
            "MoeError", "normal16", "normal_f32", "zipf_bias", "quantize_per_tensor", "DTYPE_F16", "DTYPE_BF16",
            "DTYPE_INT8", "DTYPE_FP8_BLOCK", "quantize_fp8_blocks",
            "DTYPE_W4A16", "quantize_int4_g128", "DTYPE_INT8_CHANNEL", "quantize_int8_channel",
-           "DTYPE_NVFP4", "quantize_nvfp4", "save_weights", "load_weights", "MoeWeightFile", "MoeWeightArray"]
+           "DTYPE_NVFP4", "quantize_nvfp4", "DTYPE_INT4_PTX", "DTYPE_FP8", "save_weights", "load_weights", "MoeWeightFile", "MoeWeightArray"]

@@ -36,6 +36,8 @@ DTYPE_FP8_BLOCK = 3
 DTYPE_W4A16 = 4
 DTYPE_INT8_CHANNEL = 5
 DTYPE_NVFP4 = 6
+DTYPE_INT4_PTX = 7   # the reference's capacity_int4_ptx format (packed-transposed per-tensor int4)
+DTYPE_FP8 = 8        # the reference's capacity_fp8_ptx format (per-tensor e4m3)
 ROUTER_SAME = 0
 ROUTER_F32 = 1
 
@@ -123,8 +125,8 @@ class LayerConfig:
     router_f32: bool = False
     zipf_s: float = 0.0          # > 0: add a Zipf(s) popularity bias to the logits
     cap: int = 0                 # 0: computed; > 0: override; -1: no drop
-    act_scale: float = 1.0       # int8 path: s_in (the reference's placeholder is 1.0)
-    mid_scale: float = 1.0       # int8 path: s_mid
+    act_scale: float = 1.0       # per-tensor formats: s_in (the reference's placeholder is 1.0)
+    mid_scale: float = 1.0       # per-tensor formats: s_mid
 
     @property
     def T(self) -> int:
@@ -161,6 +163,22 @@ class LayerConfig:
     def int8ch(self) -> bool:
         """int8 with per-output-channel weight scales and per-token activation scales."""
         return self.dtype == DTYPE_INT8_CHANNEL
+
+    @property
+    def int4ptx(self) -> bool:
+        """The reference's int4 format: per-tensor int4 weights packed
+        transposed ([E, N/2, K] bytes), int4 activations (one per byte)."""
+        return self.dtype == DTYPE_INT4_PTX
+
+    @property
+    def fp8pt(self) -> bool:
+        """The reference's fp8 format: per-tensor e4m3 weights and activations."""
+        return self.dtype == DTYPE_FP8
+
+    @property
+    def per_tensor(self) -> bool:
+        """A format with the reference's five per-tensor MoEArgs scales."""
+        return self.dtype in (DTYPE_INT8, DTYPE_INT4_PTX, DTYPE_FP8)
 
     @property
     def channel_scaled(self) -> bool:

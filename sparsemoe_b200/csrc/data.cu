@@ -229,6 +229,30 @@ extern "C" void moe_quantize_int4_g128(const uint16_t* src, int E, int K, int N,
             }
 }
 
+// inputs/data.cu:89-140: int4 values (int8 in [-8, 7]) of E row-major [K, N]
+// matrices -> per expert [N/2][K] bytes, column 2p in the low nibble and 2p+1
+// in the high nibble of byte (p, k).
+extern "C" void moe_pack_int4_transposed(const int8_t* q, int E, int K, int N, uint8_t* out) {
+    const size_t per = (size_t)K * N, bytes_per = (size_t)(N / 2) * K;
+    std::memset(out, 0, (size_t)E * bytes_per);
+    for (int e = 0; e < E; ++e)
+        for (int kk = 0; kk < K; ++kk)
+            for (int n = 0; n < N; ++n) {
+                const uint8_t nib = (uint8_t)(q[(size_t)e * per + (size_t)kk * N + n] & 0xF);
+                out[(size_t)e * bytes_per + (size_t)(n / 2) * K + kk] |= (n & 1) ? (uint8_t)(nib << 4) : nib;
+            }
+}
+
+// inputs/data.cu:142-150: fp16 -> e4m3 by direct conversion (nearest even,
+// saturating to +-448).
+extern "C" void moe_cast_e4m3(const uint16_t* src, size_t n, uint8_t* dst) {
+    for (size_t i = 0; i < n; ++i) {
+        half h;
+        std::memcpy(&h, &src[i], 2);
+        dst[i] = (uint8_t)__nv_cvt_float_to_fp8(__half2float(h), __NV_SATFINITE, __NV_E4M3);
+    }
+}
+
 namespace {
 
 float quant_symmetric(const std::vector<half>& src, std::vector<int8_t>& dst, float qmax) {

@@ -194,8 +194,25 @@ __global__ void __launch_bounds__(kThreads) dispatch_gather_kernel(
     for (; v < vec_per_row; v += 32) dst[v] = __ldg(src + v);
 }
 
-// int8 path (reference capacity_int8_ptx.cu:391-432): the slot's f16 token row
-// quantised as rn(clamp(x / s_in, -128, 127)), 8 values per 16-byte load.
+// The per-tensor formats: the slot's f16 token row quantised with the MoEArgs
+// scale s_in, 8 values per 16-byte load, one byte each:
+//   kQ = 0  int8  rn(clamp(x / s_in, -128, 127))  (reference capacity_int8_ptx.cu:391-432)
+//   kQ = 1  int4  rn(clamp(x / s_in, -7, 7))      (capacity_int4_ptx.cu:396-441; kept one value per
+//                                                  byte, not nibble-packed: the GEMM reads int8)
+//   kQ = 2  e4m3  e4m3(clamp(x / s_in, -448, 448)) (capacity_fp8_ptx.cu:330-352, nearest even)
+template <int kQ>
+__device__ __forceinline__ uint32_t quant_pair(float a, float b, float s_in) {
+    if (kQ == 2) {
+        const float qa = fminf(fmaxf(a / s_in, -448.f), 448.f), qb = fminf(fmaxf(b / s_in, -448.f), 448.f);
+        return (uint32_t)__nv_cvt_float2_to_fp8x2(make_float2(qa, qb), __NV_SATFINITE, __NV_E4M3);
+    }
+    constexpr float lo = kQ == 0 ? -128.f : -7.f, hi = kQ == 0 ? 127.f : 7.f;
+    const int q0 = __float2int_rn(fminf(fmaxf(a / s_in, lo), hi));
+    const int q1 = __float2int_rn(fminf(fmaxf(b / s_in, lo), hi));
+    return (uint32_t)(q0 & 0xFF) | ((uint32_t)(q1 & 0xFF) << 8);
+}
+
+template <int kQ>
 __global__ void __launch_bounds__(kThreads) dispatch_gather_q8_kernel(
     const uint4* __restrict__ x, const int* __restrict__ counts, const int* __restrict__ token_ids,
     const int* __restrict__ row_base, const int* __restrict__ expert_start, int N, int E, int B, int cap,
@@ -219,9 +236,7 @@ __global__ void __launch_bounds__(kThreads) dispatch_gather_q8_kernel(
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
             const float2 f = __half22float2(h2[q]);
-            const int q0 = __float2int_rn(fminf(fmaxf(f.x / s_in, -128.f), 127.f));
-            const int q1 = __float2int_rn(fminf(fmaxf(f.y / s_in, -128.f), 127.f));
-            w[q >> 1] |= ((uint32_t)(q0 & 0xFF) | ((uint32_t)(q1 & 0xFF) << 8)) << (16 * (q & 1));
+            w[q >> 1] |= quant_pair<kQ>(f.x, f.y, s_in) << (16 * (q & 1));
         }
         dst[v] = make_uint2(w[0], w[1]);
     }
@@ -422,9 +437,17 @@ cudaError_t launch_dispatch_gather(const void* x, const Shape& s, const Workspac
         dispatch_gather_q8tok_kernel<<<gblocks, kThreads, 0, st>>>((const uint4*)x, counts, token_ids, ws.row_base,
                                                                    ws.expert_start, s.N, s.E, s.B, s.cap, s.d / 8, gd);
     else if (slots > 0 && s.dtype == MOE_DTYPE_INT8)
-        dispatch_gather_q8_kernel<<<gblocks, kThreads, 0, st>>>((const uint4*)x, counts, token_ids, ws.row_base,
-                                                                ws.expert_start, s.N, s.E, s.B, s.cap, s.d / 8,
-                                                                sc.s_in, gd);
+        dispatch_gather_q8_kernel<0><<<gblocks, kThreads, 0, st>>>((const uint4*)x, counts, token_ids, ws.row_base,
+                                                                   ws.expert_start, s.N, s.E, s.B, s.cap, s.d / 8,
+                                                                   sc.s_in, gd);
+    else if (slots > 0 && s.dtype == MOE_DTYPE_INT4_PTX)
+        dispatch_gather_q8_kernel<1><<<gblocks, kThreads, 0, st>>>((const uint4*)x, counts, token_ids, ws.row_base,
+                                                                   ws.expert_start, s.N, s.E, s.B, s.cap, s.d / 8,
+                                                                   sc.s_in, gd);
+    else if (slots > 0 && s.dtype == MOE_DTYPE_FP8)
+        dispatch_gather_q8_kernel<2><<<gblocks, kThreads, 0, st>>>((const uint4*)x, counts, token_ids, ws.row_base,
+                                                                   ws.expert_start, s.N, s.E, s.B, s.cap, s.d / 8,
+                                                                   sc.s_in, gd);
     else if (slots > 0)
         dispatch_gather_kernel<<<gblocks, kThreads, 0, st>>>((const uint4*)x, counts, token_ids, ws.row_base,
                                                              ws.expert_start, s.N, s.E, s.B, s.cap, s.d / 8, gd);

@@ -111,7 +111,11 @@ struct Fmt16 {
     static __device__ __forceinline__ float down_value(uint32_t r, const GemmParams&) { return __uint_as_float(r); }
 };
 
-struct FmtI8 {
+// Per-tensor int8 (kQMax 127, lower clamp -128: capacity_int8_ptx.cu) and the
+// reference's int4 format (kQMax 7, clamp [-7, 7]: capacity_int4_ptx.cu:446-486,
+// int4 values held one per byte so the same kind::i8 MMA is exact).
+template <int kQMax>
+struct FmtI8T {
     static constexpr int kElemBytes = 1;
     static constexpr int kBK = 128;
     static constexpr int kChunkN = 128;
@@ -119,7 +123,7 @@ struct FmtI8 {
     static __device__ __forceinline__ void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t id, uint32_t acc) {
         mma_i8_ss(d, a, b, id, acc);
     }
-    // capacity_int8_ptx.cu:465-474: dequant, SiLU(gate)*up, requant to int8.
+    // capacity_int8_ptx.cu:465-474 / capacity_int4_ptx.cu:470-477: dequant, SiLU(gate)*up, requant.
     static __device__ __forceinline__ void swiglu_store(const uint32_t (&g)[32], const uint32_t (&u)[32],
                                                         const GemmParams& p, void* dst, bool valid) {
         uint32_t packed[8];
@@ -132,7 +136,8 @@ struct FmtI8 {
                 const float gf = (float)(int)g[4 * i + j] * p.deq_gate;
                 const float silu = gf / (1.0f + __expf(-gf));
                 const float fused = uf * silu;
-                const int q = __float2int_rn(fminf(fmaxf(fused * p.inv_mid, -128.f), 127.f));
+                constexpr float lo = kQMax == 127 ? -128.f : -(float)kQMax;
+                const int q = __float2int_rn(fminf(fmaxf(fused * p.inv_mid, lo), (float)kQMax));
                 word |= (uint32_t)(q & 0xFF) << (8 * j);
             }
             packed[i] = word;
@@ -146,6 +151,48 @@ struct FmtI8 {
     // capacity_int8_ptx.cu:615: (float)int32 * (s_mid * s_down)
     static __device__ __forceinline__ float down_value(uint32_t r, const GemmParams& p) {
         return (float)(int)r * p.deq_down;
+    }
+};
+using FmtI8 = FmtI8T<127>;
+using FmtI4 = FmtI8T<7>;
+
+// The reference's per-tensor fp8 format (capacity_fp8_ptx.cu:362-395, :566-600):
+// e4m3 x e4m3 with f32 accumulation (kind::f8f6f4); up*s_in*s_up and
+// gate*s_in*s_gate, SiLU*mul, h = e4m3(clamp(fused / s_mid, -448, 448));
+// the down result is dequantised by s_mid*s_down.
+struct FmtE4 {
+    static constexpr int kElemBytes = 1;
+    static constexpr int kBK = 128;
+    static constexpr int kChunkN = 128;
+    static constexpr int kUmmaK = 32;
+    static __device__ __forceinline__ void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t id, uint32_t acc) {
+        mma_f8_ss(d, a, b, id, acc);
+    }
+    static __device__ __forceinline__ void swiglu_store(const uint32_t (&g)[32], const uint32_t (&u)[32],
+                                                        const GemmParams& p, void* dst, bool valid) {
+        uint32_t packed[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            float v[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float uf = __uint_as_float(u[4 * i + j]) * p.deq_up;
+                const float gf = __uint_as_float(g[4 * i + j]) * p.deq_gate;
+                const float silu = gf / (1.0f + __expf(-gf));
+                v[j] = fminf(fmaxf(uf * silu * p.inv_mid, -448.f), 448.f);
+            }
+            packed[i] = (uint32_t)__nv_cvt_float2_to_fp8x2(make_float2(v[0], v[1]), __NV_SATFINITE, __NV_E4M3) |
+                        ((uint32_t)__nv_cvt_float2_to_fp8x2(make_float2(v[2], v[3]), __NV_SATFINITE, __NV_E4M3)
+                         << 16);
+        }
+        if (valid) {
+            uint4* o = reinterpret_cast<uint4*>(dst);
+            o[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+            o[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+        }
+    }
+    static __device__ __forceinline__ float down_value(uint32_t r, const GemmParams& p) {
+        return __uint_as_float(r) * p.deq_down;
     }
 };
 
@@ -409,7 +456,9 @@ struct FmtDesc {
 FmtDesc fmt_desc(int dtype) {
     switch (dtype) {
         case MOE_DTYPE_BF16: return {CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 64, 64};
-        case MOE_DTYPE_INT8: return {CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, 128, 128};
+        case MOE_DTYPE_INT8:
+        case MOE_DTYPE_INT4_PTX:
+        case MOE_DTYPE_FP8: return {CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, 128, 128};
         default: return {CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, 64, 64};
     }
 }
@@ -475,6 +524,12 @@ cudaError_t launch_expert_up_gate(const void* a_rows, const void* w_gate, const 
         case MOE_DTYPE_INT8:
             p.idesc = idesc_i8(kBM, kUmmaN, true);
             return launch_gemm<0, FmtI8>(ta, tg, tu, p, st, num_sms);
+        case MOE_DTYPE_INT4_PTX:
+            p.idesc = idesc_i8(kBM, kUmmaN, true);
+            return launch_gemm<0, FmtI4>(ta, tg, tu, p, st, num_sms);
+        case MOE_DTYPE_FP8:
+            p.idesc = idesc_e4m3(kBM, kUmmaN, true);
+            return launch_gemm<0, FmtE4>(ta, tg, tu, p, st, num_sms);
         case MOE_DTYPE_BF16:
             p.idesc = idesc_f16(true, kBM, kUmmaN, false, true);
             return launch_gemm<0, Fmt16<__nv_bfloat16>>(ta, tg, tu, p, st, num_sms);
@@ -500,8 +555,12 @@ cudaError_t launch_expert_down(const void* h_rows, const void* w_down, const Sha
     p.out = y_rows;
     switch (s.dtype) {
         case MOE_DTYPE_INT8:
+        case MOE_DTYPE_INT4_PTX:   // the down epilogue of the two is the same
             p.idesc = idesc_i8(kBM, kUmmaN, true);
             return launch_gemm<1, FmtI8>(th, td, td, p, st, num_sms);
+        case MOE_DTYPE_FP8:
+            p.idesc = idesc_e4m3(kBM, kUmmaN, true);
+            return launch_gemm<1, FmtE4>(th, td, td, p, st, num_sms);
         case MOE_DTYPE_BF16:
             p.idesc = idesc_f16(true, kBM, kUmmaN, false, true);
             return launch_gemm<1, Fmt16<__nv_bfloat16>>(th, td, td, p, st, num_sms);

@@ -80,12 +80,17 @@ size_t router_scratch_bytes(const Shape& s) {
     return router_sliced(s) ? align256(sizeof(float) * (size_t)s.T() * s.E) : 0;
 }
 
+// INT4_PTX: int8 copies of the three packed weight matrices.
+size_t unpacked_weight_bytes(const Shape& s) {
+    return s.dtype == MOE_DTYPE_INT4_PTX ? 3 * align256((size_t)s.E * s.d * s.f) : 0;
+}
+
 size_t workspace_bytes(const Shape& s) {
     const size_t routes = (size_t)s.T() * s.k;
     const size_t chunk_tab = (size_t)s.B * s.chunks() * s.E;
     return workspace_header_bytes() + align256(sizeof(int) * routes) + 2 * align256(sizeof(int) * chunk_tab) +
            align256(sizeof(int) * (size_t)s.B * s.E) + 2 * align256(sizeof(int) * s.E) + scale_bytes(s, s.d) +
-           scale_bytes(s, s.f) + router_scratch_bytes(s);
+           scale_bytes(s, s.f) + router_scratch_bytes(s) + unpacked_weight_bytes(s);
 }
 
 void carve_workspace(void* base, const Shape& s, Workspace* ws) {
@@ -109,6 +114,8 @@ void carve_workspace(void* base, const Shape& s, Workspace* ws) {
     ws->h_scale = scale_bytes(s, s.f) ? reinterpret_cast<float*>(p) : nullptr;
     p += scale_bytes(s, s.f);
     ws->router_logits = router_scratch_bytes(s) ? reinterpret_cast<float*>(p) : nullptr;
+    p += router_scratch_bytes(s);
+    ws->w_unpacked = unpacked_weight_bytes(s) ? reinterpret_cast<int8_t*>(p) : nullptr;
 }
 
 namespace {
@@ -141,7 +148,7 @@ int make_shape(const MoeDims* d, Shape* s, bool bind_check = true) {
     }
     if (d->dtype != MOE_DTYPE_F16 && d->dtype != MOE_DTYPE_BF16 && d->dtype != MOE_DTYPE_INT8 &&
         d->dtype != MOE_DTYPE_FP8_BLOCK && d->dtype != MOE_DTYPE_W4A16 && d->dtype != MOE_DTYPE_INT8_CHANNEL &&
-        d->dtype != MOE_DTYPE_NVFP4) {
+        d->dtype != MOE_DTYPE_NVFP4 && d->dtype != MOE_DTYPE_INT4_PTX && d->dtype != MOE_DTYPE_FP8) {
         set_error("dtype %d not supported by this entry point", d->dtype);
         return MOE_ERR_UNSUPPORTED;
     }
@@ -309,7 +316,10 @@ int check_args(const MoEArgs* a, int dtype) {
     if (dtype == MOE_DTYPE_W4A16 || dtype == MOE_DTYPE_NVFP4)
         fmt = a->expert_up_proj_weights_int4 && a->expert_gate_proj_weights_int4 &&
               a->expert_down_proj_weights_int4 && a->per_expert_wmma_inputs && a->hidden_mlp_layer_1_out_fp16;
-    else if (dtype == MOE_DTYPE_FP8_BLOCK)
+    else if (dtype == MOE_DTYPE_INT4_PTX)
+        fmt = a->expert_up_proj_weights_int4 && a->expert_gate_proj_weights_int4 &&
+              a->expert_down_proj_weights_int4 && a->per_expert_wmma_inputs_int8 && a->hidden_mlp_layer_1_out_int8;
+    else if (dtype == MOE_DTYPE_FP8_BLOCK || dtype == MOE_DTYPE_FP8)
         fmt = a->expert_up_proj_weights_fp8 && a->expert_gate_proj_weights_fp8 && a->expert_down_proj_weights_fp8 &&
               a->per_expert_wmma_inputs_fp8 && a->hidden_mlp_layer_1_out_fp8;
     else if (dtype == MOE_DTYPE_INT8 || dtype == MOE_DTYPE_INT8_CHANNEL)
@@ -320,12 +330,16 @@ int check_args(const MoEArgs* a, int dtype) {
               a->per_expert_wmma_inputs && a->hidden_mlp_layer_1_out_fp16;
     if (!common || !fmt) {
         set_error("a MoEArgs buffer needed by the %s path is null",
-                  dtype == MOE_DTYPE_INT8 || dtype == MOE_DTYPE_INT8_CHANNEL ? "int8" : dtype == MOE_DTYPE_FP8_BLOCK ? "fp8"
-                                                  : dtype == MOE_DTYPE_W4A16 || dtype == MOE_DTYPE_NVFP4 ? "4-bit" : "16-bit");
+                  dtype == MOE_DTYPE_INT8 || dtype == MOE_DTYPE_INT8_CHANNEL ? "int8"
+                  : dtype == MOE_DTYPE_FP8_BLOCK || dtype == MOE_DTYPE_FP8  ? "fp8"
+                  : dtype == MOE_DTYPE_INT4_PTX                             ? "int4 (packed-transposed)"
+                  : dtype == MOE_DTYPE_W4A16 || dtype == MOE_DTYPE_NVFP4    ? "4-bit"
+                                                                            : "16-bit");
         return MOE_ERR_INVALID_ARG;
     }
-    if (dtype == MOE_DTYPE_INT8 && !(a->scale_input_act > 0.0f && a->scale_mid_act > 0.0f)) {
-        set_error("int8 path needs positive scale_input_act and scale_mid_act");
+    if ((dtype == MOE_DTYPE_INT8 || dtype == MOE_DTYPE_INT4_PTX || dtype == MOE_DTYPE_FP8) &&
+        !(a->scale_input_act > 0.0f && a->scale_mid_act > 0.0f)) {
+        set_error("the per-tensor formats need positive scale_input_act and scale_mid_act");
         return MOE_ERR_INVALID_ARG;
     }
     return MOE_OK;
@@ -345,7 +359,7 @@ void note_status_word(int dev, int* status) {
 
 GemmScales scales_of(const MoEArgs* a, const Shape& s) {
     GemmScales sc;
-    if (s.dtype == MOE_DTYPE_INT8) {
+    if (s.dtype == MOE_DTYPE_INT8 || s.dtype == MOE_DTYPE_INT4_PTX || s.dtype == MOE_DTYPE_FP8) {
         sc.s_in = a->scale_input_act;
         sc.s_gate = a->scale_gate_w;
         sc.s_up = a->scale_up_w;
@@ -371,7 +385,16 @@ FfnBuffers ffn_buffers(const MoEArgs* a, const Shape& s) {
         b.wd = a->expert_down_proj_weights_int4;
         return b;
     }
-    if (s.dtype == MOE_DTYPE_FP8_BLOCK) {
+    if (s.dtype == MOE_DTYPE_INT4_PTX) {
+        // int4 values one per byte; the weights are unpacked into the scratch by enqueue_ffn
+        b.a_rows = (void*)a->per_expert_wmma_inputs_int8;
+        b.h_rows = (void*)a->hidden_mlp_layer_1_out_int8;
+        b.wg = a->expert_gate_proj_weights_int4;
+        b.wu = a->expert_up_proj_weights_int4;
+        b.wd = a->expert_down_proj_weights_int4;
+        return b;
+    }
+    if (s.dtype == MOE_DTYPE_FP8_BLOCK || s.dtype == MOE_DTYPE_FP8) {
         b.a_rows = (void*)a->per_expert_wmma_inputs_fp8;
         b.h_rows = (void*)a->hidden_mlp_layer_1_out_fp8;
         b.wg = a->expert_gate_proj_weights_fp8;
@@ -415,8 +438,27 @@ int enqueue_route(const MoEArgs* a, const MoeDims* dims, const Shape& s, const W
 
 // Stage 4: the two grouped GEMMs over the row groups `gt`.
 int enqueue_ffn(const MoEArgs* a, const MoeDims* dims, const Shape& s, const GroupTable& gt, int* status,
-                float* a_scale, float* h_scale, int num_sms, cudaStream_t stream) {
-    const FfnBuffers fb = ffn_buffers(a, s);
+                float* a_scale, float* h_scale, int num_sms, cudaStream_t stream, int8_t* w_unpacked = nullptr) {
+    FfnBuffers fb = ffn_buffers(a, s);
+    if (s.dtype == MOE_DTYPE_INT4_PTX) {
+        if (!w_unpacked) {
+            set_error("the int4 (packed-transposed) format runs through moe_solve_v2 / solve only");
+            return MOE_ERR_UNSUPPORTED;
+        }
+        const size_t per = align256((size_t)s.E * s.d * s.f);
+        int8_t* ug = w_unpacked;
+        int8_t* uu = w_unpacked + per;
+        int8_t* ud = w_unpacked + 2 * per;
+        MOE_TRY(launch_unpack_int4_ptx(static_cast<const uint8_t*>(fb.wg), s.E, s.d, s.f, ug, stream),
+                "int4 weight unpack (gate)");
+        MOE_TRY(launch_unpack_int4_ptx(static_cast<const uint8_t*>(fb.wu), s.E, s.d, s.f, uu, stream),
+                "int4 weight unpack (up)");
+        MOE_TRY(launch_unpack_int4_ptx(static_cast<const uint8_t*>(fb.wd), s.E, s.f, s.d, ud, stream),
+                "int4 weight unpack (down)");
+        fb.wg = ug;
+        fb.wu = uu;
+        fb.wd = ud;
+    }
     if (s.dtype == MOE_DTYPE_W4A16) {
         MOE_TRY(launch_w4_up_gate(fb.a_rows, fb.wg, fb.wu, dims->w4_scale_gate, dims->w4_scale_up,
                                   dims->w4_zero_gate, dims->w4_zero_up, s, gt, status, fb.h_rows, stream, num_sms),
@@ -477,7 +519,7 @@ int enqueue_layer(const MoEArgs* a, const MoeDims* dims, const Shape& s, const W
     MOE_TRY(mark_stage(2, stream), "cudaEventRecord(stage event)");
     if (s.T() > 0 && s.cap > 0) {
         const GroupTable gt{ws.expert_rows, ws.expert_start, nullptr, s.E, s.rows_capacity()};
-        rc = enqueue_ffn(a, dims, s, gt, ws.status, ws.a_scale, ws.h_scale, num_sms, stream);
+        rc = enqueue_ffn(a, dims, s, gt, ws.status, ws.a_scale, ws.h_scale, num_sms, stream, ws.w_unpacked);
         if (rc != MOE_OK) return rc;
     } else {
         MOE_TRY(mark_stage(3, stream), "cudaEventRecord(stage event)");
@@ -846,14 +888,23 @@ extern "C" void solve(MoEArgs args) {
         fprintf(stderr, "CUDA Error at: %s: %s \n", what, moe_last_error());
         exit(1);
     };
-    // The reference picks the kernel at build time (Makefile KERNEL=); here the
-    // weight format the builder filled in picks the path.
+    // The reference picks the kernel at build time (Makefile KERNEL=) and the
+    // allocator at run time (drivers/main.cu:84-106); here the weight fields
+    // that allocator filled in pick the path: fp16 -> capacity, int4 (its
+    // int4_ptx allocator also fills the int8 fields) -> capacity_int4_ptx,
+    // int8 alone -> capacity_int8_ptx, fp8 -> capacity_fp8_ptx.
+    const bool per_tensor = dims.dtype == MOE_DTYPE_INT8 || dims.dtype == MOE_DTYPE_INT4_PTX ||
+                            dims.dtype == MOE_DTYPE_FP8;
     if (args.expert_up_proj_weights) {
-        if (dims.dtype == MOE_DTYPE_INT8) dims.dtype = MOE_DTYPE_F16;
-    } else if (args.expert_up_proj_weights_int8 && !args.expert_up_proj_weights_int4) {
+        if (per_tensor) dims.dtype = MOE_DTYPE_F16;
+    } else if (args.expert_up_proj_weights_int4) {
+        dims.dtype = MOE_DTYPE_INT4_PTX;
+    } else if (args.expert_up_proj_weights_int8) {
         dims.dtype = MOE_DTYPE_INT8;
+    } else if (args.expert_up_proj_weights_fp8) {
+        dims.dtype = MOE_DTYPE_FP8;
     } else {
-        set_error("solve(): no kernel for this weight format (int4 / fp8 MoEArgs fields)");
+        set_error("solve(): no expert weights in MoEArgs");
         die("solve");
     }
     cudaEvent_t start, stop;

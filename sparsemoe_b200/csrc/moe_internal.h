@@ -54,6 +54,8 @@ struct Workspace {
     float* a_scale;     // FP8: [E*B*CAP, d/128] activation block scales; INT8_CHANNEL: [E*B*CAP] row scales
     float* h_scale;     // FP8 / INT8_CHANNEL: [E*B*CAP, f/128] h block scales
     float* router_logits;  // [T, E] logits of the sliced router (router_sliced) when args carry none
+    int8_t* w_unpacked;    // INT4_PTX: the three weight matrices unpacked to int8, gate/up [E, d, f],
+                           // down [E, f, d] (row-major, the layout the int8 GEMM reads)
 };
 size_t workspace_header_bytes();
 
@@ -141,6 +143,11 @@ cudaError_t launch_i8c_up_gate(const void* a_rows, const float* a_scale, const v
 cudaError_t launch_i8c_down(const void* h_rows, const float* h_scale, const void* w_down, const float* s_down,
                             const Shape& s, const GroupTable& gt, int* status, float* y_rows, cudaStream_t st,
                             int num_sms);
+
+// repack.cu: the reference's packed-transposed int4 weights (per expert
+// [N/2][K] bytes, columns 2p / 2p+1 in the low / high nibble of byte (p, k),
+// inputs/data.cu:89-140) -> int8 row-major [E, K, N].
+cudaError_t launch_unpack_int4_ptx(const uint8_t* packed, int E, int K, int N, int8_t* out, cudaStream_t st);
 
 // expert_gemm_w4.cu: 4-bit weights dequantised to bf16 in shared memory.
 cudaError_t launch_w4_up_gate(const void* a_rows, const void* w_gate, const void* w_up, const void* s_gate,

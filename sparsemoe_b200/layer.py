@@ -32,8 +32,14 @@ class MoeLayer:
         z = lambda *s, dt: torch.empty(*s, dtype=dt, device=dev)  # noqa: E731
         self.x = z(max(T, 1), d, dt=t16)
         self.wr = z(d, E, dt=torch.float32 if cfg.router_f32 else t16)
-        wt = torch.int8 if (cfg.int8 or cfg.int8ch) else (torch.uint8 if cfg.fp8 else t16)
-        if cfg.w4:
+        wt = torch.int8 if (cfg.int8 or cfg.int8ch or cfg.int4ptx) else \
+            (torch.uint8 if (cfg.fp8 or cfg.fp8pt) else t16)
+        if cfg.int4ptx:
+            # the reference's packed-transposed int4: per expert [N/2][K] bytes
+            self.wg = z(E, f // 2, d, dt=torch.uint8)
+            self.wu = z(E, f // 2, d, dt=torch.uint8)
+            self.wd = z(E, d // 2, f, dt=torch.uint8)
+        elif cfg.w4:
             self.wg = z(E, d, f // 2, dt=torch.uint8)
             self.wu = z(E, d, f // 2, dt=torch.uint8)
             self.wd = z(E, f, d // 2, dt=torch.uint8)
@@ -68,11 +74,11 @@ class MoeLayer:
         if self.cfg.T > 0:
             put(self.x, inputs["x"])
         put(self.wr, inputs["wr"])
-        sfx = "_q" if (self.cfg.int8 or self.cfg.int8ch or self.cfg.fp8 or self.cfg.w4) else ""
+        sfx = "_q" if (self.cfg.per_tensor or self.cfg.int8ch or self.cfg.fp8 or self.cfg.w4) else ""
         put(self.wg, inputs["wg" + sfx])
         put(self.wu, inputs["wu" + sfx])
         put(self.wd, inputs["wd" + sfx])
-        if self.cfg.int8:
+        if self.cfg.per_tensor:
             self.scales = {k: inputs[k] for k in ("s_in", "s_gate", "s_up", "s_mid", "s_down")}
         if self.cfg.nvfp4:
             self.w4sz = [torch.from_numpy(np.ascontiguousarray(inputs[k])).to(self.device)
@@ -113,12 +119,25 @@ class MoeLayer:
             a.expert_down_proj_weights_int8 = p(self.wd)
             a.per_expert_wmma_inputs_int8 = p(self.a_rows)
             a.hidden_mlp_layer_1_out_int8 = p(self.h_rows)
-        elif self.cfg.int8:
-            a.expert_up_proj_weights_int8 = p(self.wu)
-            a.expert_gate_proj_weights_int8 = p(self.wg)
-            a.expert_down_proj_weights_int8 = p(self.wd)
-            a.per_expert_wmma_inputs_int8 = p(self.a_rows)
-            a.hidden_mlp_layer_1_out_int8 = p(self.h_rows)
+        elif self.cfg.per_tensor:
+            if self.cfg.int4ptx:
+                a.expert_up_proj_weights_int4 = p(self.wu)
+                a.expert_gate_proj_weights_int4 = p(self.wg)
+                a.expert_down_proj_weights_int4 = p(self.wd)
+            elif self.cfg.fp8pt:
+                a.expert_up_proj_weights_fp8 = p(self.wu)
+                a.expert_gate_proj_weights_fp8 = p(self.wg)
+                a.expert_down_proj_weights_fp8 = p(self.wd)
+            else:
+                a.expert_up_proj_weights_int8 = p(self.wu)
+                a.expert_gate_proj_weights_int8 = p(self.wg)
+                a.expert_down_proj_weights_int8 = p(self.wd)
+            if self.cfg.fp8pt:
+                a.per_expert_wmma_inputs_fp8 = p(self.a_rows)
+                a.hidden_mlp_layer_1_out_fp8 = p(self.h_rows)
+            else:
+                a.per_expert_wmma_inputs_int8 = p(self.a_rows)
+                a.hidden_mlp_layer_1_out_int8 = p(self.h_rows)
             sc = self.scales
             a.scale_input_act, a.scale_gate_w, a.scale_up_w = sc["s_in"], sc["s_gate"], sc["s_up"]
             a.scale_mid_act, a.scale_down_w = sc["s_mid"], sc["s_down"]

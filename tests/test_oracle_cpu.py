@@ -447,3 +447,82 @@ def test_empty_batch_routes_nothing():
     """T = 0: no routes, zero counts, nothing written."""
     r = O.route(np.zeros((0, 256), np.uint16), np.zeros((256, 8), np.uint16), None, 1, 0, 256, 8, 2, 16, False)
     assert r["idx"].shape == (0, 2) and (r["counts"] == 0).all() and (r["token_ids"] == -1).all()
+
+
+def _np_per_tensor_ffn(inp, ref, cfg, wq, quant, deq):
+    """Route-by-route restatement of the reference's per-tensor paths: a =
+    quant(x / s_in), exact / f64 GEMMs, uf = U s_in s_up, gf = G s_in s_gate,
+    h = quant(uf * silu(gf) / s_mid), y = Y s_mid s_down, route-order combine."""
+    f32 = np.float32
+    x = inp["x"].view(np.float16).astype(np.float32)
+    s_in, s_mid = f32(inp["s_in"]), f32(inp["s_mid"])
+    out = np.zeros((cfg.T, cfg.d_model), np.float32)
+    for t in range(cfg.T):
+        for l in range(cfg.top_k):
+            if ref["route_slot"][t * cfg.top_k + l] < 0:
+                continue
+            e = ref["idx"][t, l]
+            a = deq(quant(x[t] / s_in))
+            G = (a @ wq["wg"][e]).astype(np.float32)
+            U = (a @ wq["wu"][e]).astype(np.float32)
+            gf = G * f32(s_in * f32(inp["s_gate"]))
+            uf = U * f32(s_in * f32(inp["s_up"]))
+            h = deq(quant(uf * (gf / (f32(1) + np.exp(-gf))) * (f32(1) / s_mid)))
+            y = (h @ wq["wd"][e]).astype(np.float32) * f32(s_mid * f32(inp["s_down"]))
+            out[t] = out[t] + f32(ref["w"][t, l]) * y
+    return out
+
+
+def test_int4ptx_packing_matches_reference_layout():
+    """inputs/data.cu:89-140: byte (n/2, k) of each expert holds column n in
+    its low nibble (even n) or high nibble (odd n)."""
+    cfg = sm.LayerConfig(1, 4, 256, 128, 8, 2, 1.0, dtype=sm.DTYPE_INT4_PTX)
+    inp = sm.make_inputs(cfg, 1)
+    q, P = inp["wg_i4"], inp["wg_q"]                   # [E, K, N] values, [E, N/2, K] bytes
+    assert P.shape == (8, 64, 256) and q.min() >= -7 and q.max() <= 7
+    lo = (P & 15).astype(np.int8)
+    hi = (P >> 4).astype(np.int8)
+    lo = np.where(lo >= 8, lo - 16, lo)
+    hi = np.where(hi >= 8, hi - 16, hi)
+    assert np.array_equal(lo.transpose(0, 2, 1), q[:, :, 0::2])
+    assert np.array_equal(hi.transpose(0, 2, 1), q[:, :, 1::2])
+
+
+def test_int4ptx_oracle_matches_numpy_restatement():
+    """The reference's int4 format (capacity_int4_ptx.cu): clamps at +-7."""
+    cfg = sm.LayerConfig(1, 16, 256, 256, 8, 2, 1.0, dtype=sm.DTYPE_INT4_PTX, cap=-1, act_scale=0.3,
+                         mid_scale=0.05)
+    inp = sm.make_inputs(cfg, 4)
+    ref = O.forward(inp, cfg, nthreads=2)
+    wq = {n: inp[n + "_i4"].astype(np.float64) for n in ("wg", "wu", "wd")}
+    out = _np_per_tensor_ffn(inp, ref, cfg, wq, lambda v: np.rint(np.clip(v, -7, 7)), lambda q: q.astype(np.float64))
+    _check_close(ref["out"], out)
+    assert np.abs(out).max() > 0
+
+
+def test_fp8pt_oracle_matches_numpy_restatement():
+    """The reference's fp8 format (capacity_fp8_ptx.cu): e4m3 operands with
+    unit weight scales, clamps at +-448."""
+    cfg = sm.LayerConfig(1, 12, 256, 256, 8, 2, 1.0, dtype=sm.DTYPE_FP8, cap=-1, act_scale=0.02, mid_scale=0.001)
+    inp = sm.make_inputs(cfg, 3)
+    ref = O.forward(inp, cfg, nthreads=2)
+    L = O.lib()
+    dec = np.array([L.oracle_e4m3_decode(i) for i in range(256)], np.float64)
+    wq = {n: dec[inp[n + "_q"]] for n in ("wg", "wu", "wd")}
+
+    def quant(v):
+        v = np.clip(v, -448, 448)
+        return np.array([L.oracle_e4m3(float(t)) for t in v.reshape(-1)], np.uint8).reshape(v.shape)
+    out = _np_per_tensor_ffn(inp, ref, cfg, wq, quant, lambda q: dec[q])
+    _check_close(ref["out"], out)
+    assert np.abs(out).max() > 0
+
+
+def test_fp8pt_weight_cast_is_the_reference_cast():
+    """inputs/data.cu:142-150: e4m3 = nearest-even cast of the fp16 weight."""
+    cfg = sm.LayerConfig(1, 4, 256, 128, 8, 2, 1.0, dtype=sm.DTYPE_FP8)
+    inp = sm.make_inputs(cfg, 2)
+    L = O.lib()
+    v = inp["wu"].view(np.float16).astype(np.float32).reshape(-1)[:4096]
+    enc = np.array([L.oracle_e4m3(float(t)) for t in v], np.uint8)
+    assert np.array_equal(enc, inp["wu_q"].reshape(-1)[:4096])
