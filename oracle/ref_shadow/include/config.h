@@ -1,5 +1,6 @@
-// Compile-time shape for building the reference's kernels/unfused.cu as a
-// golden-vector generator (test infrastructure).  It shadows the reference's
+// Compile-time shape for building the reference's kernels (kernels/unfused.cu
+// as a golden-vector generator, the fused kernels for the pin harness) as test
+// infrastructure.  It shadows the reference's
 // own include/config.h through the include path: same names (the reference
 // sources use them), values chosen by -D at build time.
 #include <math.h>
@@ -25,6 +26,9 @@
 #ifndef REF_UP
 #define REF_UP 2
 #endif
+#ifndef REF_CF
+#define REF_CF 0.8f
+#endif
 
 constexpr int N = REF_N;
 constexpr int d_model = REF_D;
@@ -45,7 +49,7 @@ constexpr int THREADS_PER_WARP = 32;
 #define WARPS_PER_BLOCK (WARP_TILES_X * WARP_TILES_Y)
 
 constexpr int up_proj_dim = REF_UP;
-constexpr float capacity_factor = 0.8f;
+constexpr float capacity_factor = REF_CF;
 constexpr int NSTREAMS = 4;
 
 #endif  // CONFIG_H

@@ -449,11 +449,11 @@ int enqueue_ffn(const MoEArgs* a, const MoeDims* dims, const Shape& s, const Gro
         int8_t* ug = w_unpacked;
         int8_t* uu = w_unpacked + per;
         int8_t* ud = w_unpacked + 2 * per;
-        MOE_TRY(launch_unpack_int4_ptx(static_cast<const uint8_t*>(fb.wg), s.E, s.d, s.f, ug, stream),
+        MOE_TRY(launch_unpack_int4_ptx(static_cast<const uint8_t*>(fb.wg), s.E, s.d, s.f, gt.rows, ug, stream),
                 "int4 weight unpack (gate)");
-        MOE_TRY(launch_unpack_int4_ptx(static_cast<const uint8_t*>(fb.wu), s.E, s.d, s.f, uu, stream),
+        MOE_TRY(launch_unpack_int4_ptx(static_cast<const uint8_t*>(fb.wu), s.E, s.d, s.f, gt.rows, uu, stream),
                 "int4 weight unpack (up)");
-        MOE_TRY(launch_unpack_int4_ptx(static_cast<const uint8_t*>(fb.wd), s.E, s.f, s.d, ud, stream),
+        MOE_TRY(launch_unpack_int4_ptx(static_cast<const uint8_t*>(fb.wd), s.E, s.f, s.d, gt.rows, ud, stream),
                 "int4 weight unpack (down)");
         fb.wg = ug;
         fb.wu = uu;

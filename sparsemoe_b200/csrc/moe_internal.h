@@ -146,8 +146,10 @@ cudaError_t launch_i8c_down(const void* h_rows, const float* h_scale, const void
 
 // repack.cu: the reference's packed-transposed int4 weights (per expert
 // [N/2][K] bytes, columns 2p / 2p+1 in the low / high nibble of byte (p, k),
-// inputs/data.cu:89-140) -> int8 row-major [E, K, N].
-cudaError_t launch_unpack_int4_ptx(const uint8_t* packed, int E, int K, int N, int8_t* out, cudaStream_t st);
+// inputs/data.cu:89-140) -> int8 row-major [E, K, N]; experts whose
+// expert_rows entry (device [E], optional) is 0 are skipped.
+cudaError_t launch_unpack_int4_ptx(const uint8_t* packed, int E, int K, int N, const int* expert_rows, int8_t* out,
+                                   cudaStream_t st);
 
 // expert_gemm_w4.cu: 4-bit weights dequantised to bf16 in shared memory.
 cudaError_t launch_w4_up_gate(const void* a_rows, const void* w_gate, const void* w_up, const void* s_gate,

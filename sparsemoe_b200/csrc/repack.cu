@@ -11,7 +11,8 @@
 //
 // One CTA transposes a tile of 64 byte-rows (128 columns) x 32 K: coalesced
 // 4-byte loads along K into shared memory, coalesced 4-byte stores along N.
-// HBM-bound: E*K*N/2 bytes read, E*K*N written per matrix.
+// Experts that kept no rows in this call are skipped.  HBM-bound: per expert
+// used, K*N/2 bytes read and K*N written per matrix.
 #include "moe_internal.h"
 
 namespace moe {
@@ -23,9 +24,11 @@ constexpr int kTileK = 32;   // K rows per tile
 __device__ __forceinline__ uint32_t sext_nibble(uint32_t v) { return (uint32_t)(((int32_t)(v << 28)) >> 28) & 0xFFu; }
 
 __global__ void __launch_bounds__(256) unpack_int4_ptx_kernel(const uint8_t* __restrict__ packed, int K, int N,
+                                                             const int* __restrict__ expert_rows,
                                                              int8_t* __restrict__ out) {
     __shared__ uint32_t tile[kTileP][kTileK / 4 + 1];   // [p][k/4] words of 4 K-bytes (+1: no bank conflicts)
     const int e = blockIdx.z;
+    if (expert_rows && expert_rows[e] == 0) return;     // no kept rows: the GEMM never reads this expert
     const int p0 = blockIdx.x * kTileP, k0 = blockIdx.y * kTileK;
     const uint8_t* src = packed + (size_t)e * (N / 2) * K;
     int8_t* dst = out + (size_t)e * K * N;
@@ -49,11 +52,12 @@ __global__ void __launch_bounds__(256) unpack_int4_ptx_kernel(const uint8_t* __r
 
 }  // namespace
 
-cudaError_t launch_unpack_int4_ptx(const uint8_t* packed, int E, int K, int N, int8_t* out, cudaStream_t st) {
+cudaError_t launch_unpack_int4_ptx(const uint8_t* packed, int E, int K, int N, const int* expert_rows, int8_t* out,
+                                   cudaStream_t st) {
     if (E <= 0 || K <= 0 || N <= 0) return cudaSuccess;
     if (K % kTileK != 0 || N % (2 * kTileP) != 0) return cudaErrorInvalidValue;
     const dim3 grid(N / (2 * kTileP), K / kTileK, E);
-    unpack_int4_ptx_kernel<<<grid, 256, 0, st>>>(packed, K, N, out);
+    unpack_int4_ptx_kernel<<<grid, 256, 0, st>>>(packed, K, N, expert_rows, out);
     return cudaGetLastError();
 }
 
