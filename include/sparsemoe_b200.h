@@ -277,6 +277,15 @@ int moe_set_stage_events(void* const* events, int count);
 // Frees the library's cached device scratch on the current device.
 void moe_release(void);
 
+// No reference counterpart (the reference has no failure detection).
+// Self-test of the bounded device waits every kernel here uses: enqueues one
+// CTA that waits on an mbarrier nothing arrives on, for at most timeout_ns
+// (0 < timeout_ns <= 10 s); the wait gives up, records a timeout in this
+// device's status word and the kernel returns, so the context stays usable.
+// A following moe_check_device_status(stream) returns MOE_ERR_TIMEOUT; the
+// next layer call clears the word.
+int moe_selftest_wait_timeout(int64_t timeout_ns, cudaStream_t stream);
+
 // Text of the last error recorded on this host thread ("" if none).
 const char* moe_last_error(void);
 

@@ -37,6 +37,7 @@ def _load() -> ctypes.CDLL:
         "solve": (None, [MoEArgs]),
         "moe_solve_v2": (ctypes.c_int, [ctypes.POINTER(MoEArgs), ctypes.POINTER(MoeDims), _p]),
         "moe_check_device_status": (ctypes.c_int, [_p]),
+        "moe_selftest_wait_timeout": (ctypes.c_int, [ctypes.c_int64, _p]),
         "moe_set_solve_dims": (ctypes.c_int, [ctypes.POINTER(MoeDims)]),
         "moe_get_solve_dims": (ctypes.c_int, [ctypes.POINTER(MoeDims)]),
         "moe_capacity": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float]),

@@ -866,6 +866,27 @@ extern "C" int moe_check_device_status(cudaStream_t stream) {
     return MOE_OK;
 }
 
+extern "C" int moe_selftest_wait_timeout(int64_t timeout_ns, cudaStream_t stream) {
+    if (timeout_ns <= 0 || timeout_ns > 10000000000ll) {
+        set_error("timeout_ns must be in (0, 10 s]");
+        return MOE_ERR_INVALID_ARG;
+    }
+    DeviceState* st = nullptr;
+    int dev = 0;
+    int rc = device_state(&st, &dev);
+    if (rc != MOE_OK) return rc;
+    Workspace ws;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        rc = get_workspace(*st, Shape{}, &ws, /*header_only=*/true);
+    }
+    if (rc != MOE_OK) return rc;
+    MOE_TRY(cudaMemsetAsync(ws.status, 0, sizeof(int), stream), "cudaMemsetAsync(status)");
+    MOE_TRY(launch_wait_selftest(ws.status, (uint64_t)timeout_ns, stream), "wait self-test");
+    note_status_word(dev, ws.status);
+    return MOE_OK;
+}
+
 extern "C" void moe_release(void) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev >= kMaxDevices) return;

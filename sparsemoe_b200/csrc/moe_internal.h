@@ -144,6 +144,10 @@ cudaError_t launch_i8c_down(const void* h_rows, const float* h_scale, const void
                             const Shape& s, const GroupTable& gt, int* status, float* y_rows, cudaStream_t st,
                             int num_sms);
 
+// selftest.cu: one CTA whose bounded mbarrier wait runs out after timeout_ns
+// (nothing arrives) and records kDevErrTimeout in *status.
+cudaError_t launch_wait_selftest(int* status, uint64_t timeout_ns, cudaStream_t st);
+
 // repack.cu: the reference's packed-transposed int4 weights (per expert
 // [N/2][K] bytes, columns 2p / 2p+1 in the low / high nibble of byte (p, k),
 // inputs/data.cu:89-140) -> int8 row-major [E, K, N]; experts whose

@@ -48,7 +48,8 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t parity) {
 // Bounded wait: gives up after `timeout_ns`, records `code` in *status and
 // returns false.  Nothing in this library spins without such a limit.
 constexpr uint64_t kWaitTimeoutNs = 2000000000ull;  // 2 s
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code) {
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, int* status, int code,
+                                              uint64_t timeout_ns) {
     const uint32_t a = smem_u32(bar);
     if (mbar_try_wait(a, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
@@ -59,12 +60,15 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
         // completes
         if ((it & 15) == 0) {
             if (*(volatile int*)status != 0) return false;  // another role already gave up
-            if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+            if (globaltimer_ns() - t0 > timeout_ns) {
                 atomicCAS(status, 0, code);
                 return false;
             }
         }
     }
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code) {
+    return mbar_wait_for(bar, parity, status, code, kWaitTimeoutNs);
 }
 
 // Warp-uniform wait for roles that follow it with warp-collective operations

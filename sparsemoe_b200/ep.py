@@ -150,12 +150,18 @@ class ExpertParallelLayer:
     chunk has its own routing-table scratch (MoeDims.scratch).  Default 1:
     measured on 2 B200s (Mixtral shape), 2 chunks were slower (11.4 vs 10.6
     ms) because NCCL's kernels take SMs from the persistent GEMM and the
-    weights are streamed once per chunk."""
+    weights are streamed once per chunk.
+
+    With `health_timeout` (seconds) every forward() first runs a host-side
+    liveness barrier (health.PeerWatch over the process group's store): a
+    peer that left between steps raises health.PeerLost on the survivors
+    before any kernel or collective of the step is enqueued."""
 
     PHASES = ("route", "exchange_and_ffn", "combine")
 
     def __init__(self, cfg: LayerConfig, device, group=None, chunks: int | None = None,
-                 global_batch: bool = False, transport: str = "nccl", placement: str = "contiguous"):
+                 global_batch: bool = False, transport: str = "nccl", placement: str = "contiguous",
+                 health_timeout: float | None = None, store=None):
         import torch
         import torch.distributed as dist
         self.torch, self.dist = torch, dist
@@ -249,6 +255,12 @@ class ExpertParallelLayer:
             ch.ffn_scratch = torch.empty(ffn_bytes, dtype=torch.uint8, device=dev)
             self.chunks.append(ch)
         self.comm_stream = torch.cuda.Stream(device=dev)
+        # host-side liveness check before every call (health_timeout seconds per step)
+        self.watch = None
+        if health_timeout is not None:
+            from .health import PeerWatch
+            self.watch = PeerWatch(store if store is not None else PeerWatch.default_store(), self.rank,
+                                   self.world, health_timeout)
         if transport == "peer":
             self._setup_peer()
 
@@ -482,6 +494,8 @@ class ExpertParallelLayer:
         """One layer call.  `timing` (optional dict) receives torch.cuda.Event
         lists: 'start', 'routed', 'ffn' (pairs per chunk), 'combine', 'end'."""
         torch = self.torch
+        if self.watch is not None:
+            self.watch.step()      # raises PeerLost before anything of this call is enqueued
         S = stream if stream is not None else torch.cuda.current_stream(self.device)
         # every torch op and collective below (all_gather of the route totals
         # and kept-row table, the slot-base and count sums) then runs on S, in
