@@ -502,9 +502,10 @@ def ep_parity(layer, cfg, ws, rank, dev, glob, int8_full=None):
 
     def gather(t):
         t = t.contiguous()
-        out = torch.empty((ws,) + tuple(t.shape), dtype=t.dtype, device=dev)
-        dist.all_gather_into_tensor(out, t)
-        return out
+        b = t.view(torch.uint8)                 # as bytes: NCCL has no int16 (the INT4 scales / zeros)
+        out = torch.empty((ws,) + tuple(b.shape), dtype=torch.uint8, device=dev)
+        dist.all_gather_into_tensor(out, b)
+        return out.view(t.dtype)
 
     def experts(t):
         """[e_loc, ...] per rank -> [E, ...] in global expert order."""
