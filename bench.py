@@ -33,11 +33,12 @@ sys.path.insert(0, str(ROOT))
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 STAGES = ["router_topk", "dispatch", "expert_up_gate_gemm", "expert_down_gemm", "combine"]
 def kernels_per_step(cfg) -> int:
-    """Kernels one layer call launches: router (+ a top-k pass when the
-    many-expert router runs expert-sliced, T < 2048), dispatch x4 (count, scan,
-    assign, gather), up/gate GEMM, down GEMM, combine."""
-    sliced = cfg.num_experts >= 64 and cfg.num_experts % 32 == 0 and cfg.T < 2048
-    return 8 + (1 if sliced else 0)
+    """Kernels one layer call launches: router (+ the block fold / top-k pass of
+    the many-expert routers, E >= 64), dispatch x4 (count, scan, assign,
+    gather), up/gate GEMM, down GEMM, combine (+ three weight unpacks for the
+    reference's packed-transposed int4 format)."""
+    blocked = cfg.num_experts >= 64 and cfg.num_experts % 32 == 0
+    return 8 + (1 if blocked else 0) + (3 if getattr(cfg, "int4ptx", False) else 0)
 
 
 # workloads whose batches are split over the ranks under expert parallelism (global CAP)

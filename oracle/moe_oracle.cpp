@@ -122,6 +122,17 @@ inline uint8_t f32_to_e4m3(float x) {
     return sgn | (uint8_t)(((e + 7) << 3) | mq);
 }
 
+// The router's block tree for many experts (E >= 64): blocks of 512 j's,
+// tree(a, n) = tree(a, h) + tree(a + h, n - h) with h the largest power of
+// two below n.
+constexpr int kRouterBlockJ = 512;
+float block_tree(const float* b, int a, int n) {
+    if (n == 1) return b[a];
+    int h = 1;
+    while (2 * h < n) h *= 2;
+    return block_tree(b, a, h) + block_tree(b, a + h, n - h);
+}
+
 }  // namespace
 
 extern "C" {
@@ -156,22 +167,33 @@ void oracle_route(const uint16_t* x, const void* wr, int router_f32, const float
         for (size_t i = 0; i < (size_t)d * E; ++i) wrf[i] = to_f32(w16[i], bf16);
     }
     // capacity.cu:13-142 (router GEMM) in the fixed order the GPU router uses.
-    // E >= 64 and a multiple of 32: per (token, expert) a sequential fmaf
-    // chain over j from 0.0f.  Otherwise:
+    // E >= 64 and a multiple of 32: per (token, expert), d is cut into blocks
+    // of 512 j's; block i's value is one fmaf chain over its j's in ascending
+    // order from 0.0f; the blocks are summed by the tree
+    //   tree(a, 1) = b_a,  tree(a, n) = tree(a, h) + tree(a + h, n - h),
+    //   h = the largest power of two below n,
+    // over all nb = ceil(d / 512) blocks, then + bias[e].  Otherwise:
     // lane l (0..31) accumulates, with fmaf from 0.0f, the 8-element chunks
     // c = l, l+32, ... (elements 8c..8c+7) in ascending j; the 32 partials
     // are combined by the xor butterfly p[l] = p[l] + p[l^off], off = 16..1;
     // logit = p[0], then + bias[e].
-    parallel_for((T + 63) / 64, nthreads, [&](int64_t blk) {
-        std::vector<float> xr(d);
+    parallel_for((T + 63) / 64, nthreads, [&](int64_t tb) {
+        const int64_t blk_t0 = tb * 64;
+        std::vector<float> xr(d), blk((d + kRouterBlockJ - 1) / kRouterBlockJ);
         float p[32], q[32];
-        for (int64_t t = blk * 64; t < std::min<int64_t>(T, blk * 64 + 64); ++t) {
+        for (int64_t t = blk_t0; t < std::min<int64_t>(T, blk_t0 + 64); ++t) {
             for (int j = 0; j < d; ++j) xr[j] = to_f32(x[t * d + j], bf16);
             for (int e = 0; e < E; ++e) {
-                if (E >= 64 && E % 32 == 0) {   // many experts: one fmaf chain (GPU router_tiled_kernel)
-                    float acc = 0.0f;
-                    for (int j = 0; j < d; ++j) acc = fmaf(xr[j], wrf[(size_t)j * E + e], acc);
-                    logits[t * E + e] = bias ? acc + bias[e] : acc;
+                if (E >= 64 && E % 32 == 0) {   // many experts (GPU router_tiled / router_slice + fold)
+                    const int nb = (d + kRouterBlockJ - 1) / kRouterBlockJ;
+                    for (int b = 0; b < nb; ++b) {
+                        float acc = 0.0f;
+                        for (int j = b * kRouterBlockJ; j < std::min(d, (b + 1) * kRouterBlockJ); ++j)
+                            acc = fmaf(xr[j], wrf[(size_t)j * E + e], acc);
+                        blk[b] = acc;
+                    }
+                    const float v = block_tree(blk.data(), 0, nb);
+                    logits[t * E + e] = bias ? v + bias[e] : v;
                     continue;
                 }
                 for (int l = 0; l < 32; ++l) {

@@ -77,7 +77,8 @@ size_t scale_bytes(const Shape& s, int dim) {
 }
 
 size_t router_scratch_bytes(const Shape& s) {
-    return router_sliced(s) ? align256(sizeof(float) * (size_t)s.T() * s.E) : 0;
+    const size_t nb = (size_t)(s.d + kRouterBlockJ - 1) / kRouterBlockJ;
+    return router_blocked(s) ? align256(sizeof(float) * nb * (size_t)s.T() * s.E) : 0;
 }
 
 // INT4_PTX: int8 copies of the three packed weight matrices.

@@ -15,8 +15,12 @@ constexpr int kChunkRoutes = 1024;
 // the sequential-j logit order (the oracle follows the same rule).
 constexpr int kRouterTiledMinExperts = 64;
 // Below this many tokens, many-expert routers split the experts over CTAs
-// (logits, then a separate top-k pass) so that small batches fill the GPU.
+// so that small batches fill the GPU.
 constexpr int64_t kRouterSliceMaxT = 2048;
+// Many-expert routers cut d into blocks of this many j's: each block is one
+// fmaf chain (a CTA's work), and the blocks are summed by a fixed tree in a
+// separate fold + top-k pass (the oracle follows the same order).
+constexpr int kRouterBlockJ = 512;
 
 // Error codes the kernels write to the device status word.
 constexpr int kDevErrTimeout = 1;
@@ -53,7 +57,7 @@ struct Workspace {
     int* expert_start;  // [E]       first row of expert e: exclusive prefix of expert_rows
     float* a_scale;     // FP8: [E*B*CAP, d/128] activation block scales; INT8_CHANNEL: [E*B*CAP] row scales
     float* h_scale;     // FP8 / INT8_CHANNEL: [E*B*CAP, f/128] h block scales
-    float* router_logits;  // [T, E] logits of the sliced router (router_sliced) when args carry none
+    float* router_logits;  // [ceil(d/512), T, E] per-block partial logits of the many-expert routers
     int8_t* w_unpacked;    // INT4_PTX: the three weight matrices unpacked to int8, gate/up [E, d, f],
                            // down [E, f, d] (row-major, the layout the int8 GEMM reads)
 };
@@ -103,6 +107,8 @@ struct GemmScales {
 // router.cu: logits (+bias), warp-shuffle top-k, softmax.
 // True when the router runs expert-sliced (E >= 64, E % 32 == 0, T < kRouterSliceMaxT).
 bool router_sliced(const Shape& s);
+// True for the many-expert routers (E >= 64, E % 32 == 0): per-block partials + fold.
+bool router_blocked(const Shape& s);
 cudaError_t launch_router_topk(const void* x, const void* wr, const float* bias, const Shape& s,
                                float* logits_scratch,
                                float* logits, int* idx, float* w, cudaStream_t st);

@@ -14,8 +14,11 @@
 //    and stays allocated until the process exits.  A call whose scratch
 //    (moe_workspace_bytes(dims)) exceeds it is rejected with
 //    MOE_ERR_UNSUPPORTED and a message naming both sizes.  4 MiB covers, for
-//    example, 65536 tokens at top-8 over 256 experts (about 3.2 MiB) or the
-//    Mixtral-shape call of 16384 tokens at top-2 (about 0.14 MiB).
+//    example, the Mixtral-shape call of 16384 tokens at top-2 over 8 experts
+//    (about 0.14 MiB) or a decode call of 512 tokens at top-8 over 256
+//    experts with d_model = 1024 (about 1 MiB); routers over 64 or more
+//    experts add 4 * tokens * experts * ceil(d_model / 512) bytes of partial
+//    logits, so large many-expert calls need moe_solve_v2.
 //  * Every call on a device shares the one array and leaves its contents
 //    behind.  The kernels rewrite every table entry they read in each call;
 //    the status word is cleared at the start of each call.  Two calls whose

@@ -10,8 +10,13 @@
 //      with fmaf, starting at 0.0f;  the 32 partial sums are then combined by
 //      an xor butterfly  p[l] = p[l] + p[l ^ off]  for off = 16, 8, 4, 2, 1;
 //      logit = p[0] (+ bias[e], one rounded add);
-//    for E >= 64 and a multiple of 32 (router_tiled_kernel): one sequential fmaf chain over
-//    j = 0..d-1 from 0.0f per (token, expert), then + bias[e];
+//    for E >= 64 and a multiple of 32 (router_tiled_kernel / router_slice_kernel, then
+//    fold_topk_kernel): d is cut into blocks of kRouterBlockJ = 512 j's; per (token, expert)
+//    each block is one sequential fmaf chain over its j's from 0.0f (one CTA's work, written
+//    as a partial logit), and fold_topk_kernel sums the nb blocks by the fixed tree
+//      tree(a, 1) = b_a,  tree(a, n) = tree(a, h) + tree(a + h, n - h),  h = largest power of
+//      two below n,
+//    then + bias[e];
 //  * top-k is a k-round warp argmax over (value desc, index asc), the same
 //    selection as the reference's insertion sort with strict '>' (ties go to
 //    the lower expert index; values <= -1e20 and NaN are never selected;
@@ -173,27 +178,25 @@ __global__ void __launch_bounds__(kWarps * 32) router_topk_kernel(
     }
 }
 
-// Many experts (E >= kRouterTiledMinExperts, E % 32 == 0): a register-tiled CUDA-core GEMM.  The
-// f32 order is then per (token, expert) one sequential fmaf chain over
-// j = 0..d-1 from 0.0f (+ bias[e]), which the oracle mirrors.  CTA = 16*MT
+// Many experts (E >= kRouterTiledMinExperts, E % 32 == 0): a register-tiled
+// CUDA-core GEMM over one 512-j block of d per CTA (grid.y = block), written
+// as partial logits part[block][t][e] for fold_topk_kernel.  CTA = 16*MT
 // tokens x all E experts, 2E threads; thread (r, c) owns tokens MT*r.. and
-// experts 8c..8c+7 (MT=8: 64 accumulators, 4 vector shared loads per 64 FMAs); x and
-// Wr K-slices of 32 are staged in shared memory as f32 (x transposed),
-// double-buffered: the next slice is loaded into registers during the FMAs.
+// experts 8c..8c+7 (4 vector shared loads per MT*8 FMAs); x and Wr K-slices
+// of 32 are staged in shared memory as f32 (x transposed), double-buffered:
+// the next slice is loaded into registers during the FMAs.  Splitting d into
+// blocks multiplies the CTAs by ceil(d/512), so even 64-expert routers keep
+// every SM busy.
 constexpr int kTiledKC = 32;
 
-// 2E threads: up to 512 (E = 256) with MT = 4 tokens per thread (the only
-// size launched: MT = 8 halves the CTAs per SM through its register need).
 template <typename TX, typename TW, int MT>
 __global__ void __launch_bounds__(MT == 8 ? 256 : 512) router_tiled_kernel(
-    const TX* __restrict__ x, const TW* __restrict__ wr, const float* __restrict__ bias, int64_t T, int d, int E,
-    int k, float* __restrict__ logits, int* __restrict__ idx, float* __restrict__ wts) {
+    const TX* __restrict__ x, const TW* __restrict__ wr, int64_t T, int d, int E, float* __restrict__ part) {
     constexpr int kTiledTM = 16 * MT;
     constexpr int kXVec = kTiledTM * (kTiledKC / 8) / 128;   // x vectors per thread (>= 128 threads)
     extern __shared__ float sm[];
     float* xs = sm;                              // [2][kTiledKC][kTiledTM]
     float* ws = xs + 2 * kTiledKC * kTiledTM;    // [2][kTiledKC][E]
-    float* lg = ws;                              // after the K loop: [kTiledTM][E]
     const int nthr = blockDim.x;
     const int cgroups = E / 8;
     // a warp covers 8 token rows x 4 expert groups, so its shared-memory
@@ -202,6 +205,7 @@ __global__ void __launch_bounds__(MT == 8 ? 256 : 512) router_tiled_kernel(
     const int wpr = cgroups / 4;   // warps per 8-row block
     const int r = (warp_id / wpr) * 8 + (lane_id & 7), c = (warp_id % wpr) * 4 + (lane_id >> 3);
     const int64_t t0 = (int64_t)blockIdx.x * kTiledTM;
+    const int jbeg = blockIdx.y * kRouterBlockJ, jend = min(d, jbeg + kRouterBlockJ);
     float acc[MT][8];
 #pragma unroll
     for (int i = 0; i < MT; ++i)
@@ -256,13 +260,13 @@ __global__ void __launch_bounds__(MT == 8 ? 256 : 512) router_tiled_kernel(
             dst[1] = make_float4(wreg[v][4], wreg[v][5], wreg[v][6], wreg[v][7]);
         }
     };
-    const int nslices = d / kTiledKC;
-    load_slice(0);
+    const int nslices = (jend - jbeg) / kTiledKC;
+    load_slice(jbeg);
     store_slice(0);
     __syncthreads();
     for (int sl = 0; sl < nslices; ++sl) {
         const int buf = sl & 1;
-        if (sl + 1 < nslices) load_slice((sl + 1) * kTiledKC);
+        if (sl + 1 < nslices) load_slice(jbeg + (sl + 1) * kTiledKC);
         const float* xb = xs + buf * kTiledKC * kTiledTM;
         const float* wb = ws + buf * kTiledKC * E;
 #pragma unroll 4
@@ -284,43 +288,36 @@ __global__ void __launch_bounds__(MT == 8 ? 256 : 512) router_tiled_kernel(
         if (sl + 1 < nslices) store_slice(buf ^ 1);
         __syncthreads();
     }
+    float* pb = part + (int64_t)blockIdx.y * T * E;
 #pragma unroll
-    for (int i = 0; i < MT; ++i)
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-            const int ee = 8 * c + e;
-            lg[(MT * r + i) * E + ee] = bias ? __fadd_rn(acc[i][e], bias[ee]) : acc[i][e];
+    for (int i = 0; i < MT; ++i) {
+        const int64_t t = t0 + MT * r + i;
+        if (t < T) {
+            float4* dst = reinterpret_cast<float4*>(pb + t * E + 8 * c);
+            dst[0] = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+            dst[1] = make_float4(acc[i][4], acc[i][5], acc[i][6], acc[i][7]);
         }
-    __syncthreads();
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = nthr >> 5;
-    for (int tt = warp; tt < kTiledTM; tt += nwarps) {
-        const int64_t t = t0 + tt;
-        if (t >= T) break;
-        const float* row = lg + tt * E;
-        if (logits != nullptr)
-            for (int e = lane; e < E; e += 32) logits[t * E + e] = row[e];
-        topk_softmax_warp(row, E, k, t, idx, wts, lane);
     }
 }
 
-// Few tokens, many experts (router_sliced): CTA = 16 tokens x 32 experts,
-// 64 threads, thread (r, c) = token r, experts 8c..8c+7 of the slice; x and
-// Wr K-slices of 128 double-buffered in shared memory.  Same per-(token,
-// expert) order as router_tiled_kernel (one fmaf chain over j from 0.0f,
-// then + bias); logits go to global memory and topk_rows_kernel selects.
+// Few tokens, many experts (router_sliced): CTA = 16 tokens x 32 experts x
+// one 512-j block of d (grid.z = block), 64 threads, thread (r, c) = token r,
+// experts 8c..8c+7 of the slice; x and Wr K-slices of 128 double-buffered in
+// shared memory.  Same per-(token, expert, block) chain as
+// router_tiled_kernel; partial logits go to part[block][t][e].
 constexpr int kSliceTM = 16, kSliceEC = 32, kSliceKC = 128, kSliceThreads = 64;
 constexpr size_t kSliceSmem = sizeof(float) * 2 * kSliceKC * (kSliceTM + kSliceEC);
 
 template <typename TX, typename TW>
 __global__ void __launch_bounds__(kSliceThreads) router_slice_kernel(
-    const TX* __restrict__ x, const TW* __restrict__ wr, const float* __restrict__ bias, int64_t T, int d, int E,
-    float* __restrict__ logits) {
+    const TX* __restrict__ x, const TW* __restrict__ wr, int64_t T, int d, int E, float* __restrict__ part) {
     extern __shared__ float sm[];
     float* xs = sm;                               // [2][KC][TM]
     float* ws = xs + 2 * kSliceKC * kSliceTM;     // [2][KC][EC]
     const int r = threadIdx.x >> 2, c = threadIdx.x & 3;
     const int64_t t0 = (int64_t)blockIdx.x * kSliceTM;
     const int e0 = blockIdx.y * kSliceEC;
+    const int jbeg = blockIdx.z * kRouterBlockJ, jend = min(d, jbeg + kRouterBlockJ);
     constexpr int kXV = kSliceTM * (kSliceKC / 8) / kSliceThreads;   // 4 x vectors per thread
     constexpr int kWV = kSliceKC * (kSliceEC / 8) / kSliceThreads;   // 8 router 8-vectors per thread
     uint4 xr[kXV];
@@ -369,13 +366,13 @@ __global__ void __launch_bounds__(kSliceThreads) router_slice_kernel(
     float acc[8];
 #pragma unroll
     for (int e = 0; e < 8; ++e) acc[e] = 0.0f;
-    const int nslices = d / kSliceKC;   // d % 256 == 0
-    load_slice(0);
+    const int nslices = (jend - jbeg) / kSliceKC;   // 512 or 256 j's (d % 256 == 0)
+    load_slice(jbeg);
     store_slice(0);
     __syncthreads();
     for (int sl = 0; sl < nslices; ++sl) {
         const int buf = sl & 1;
-        if (sl + 1 < nslices) load_slice((sl + 1) * kSliceKC);
+        if (sl + 1 < nslices) load_slice(jbeg + (sl + 1) * kSliceKC);
         const float* xb = xs + buf * kSliceKC * kSliceTM;
         const float* wb = ws + buf * kSliceKC * kSliceEC;
 #pragma unroll 8
@@ -393,32 +390,66 @@ __global__ void __launch_bounds__(kSliceThreads) router_slice_kernel(
     }
     const int64_t t = t0 + r;
     if (t < T) {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-            const int ee = e0 + 8 * c + e;
-            logits[t * E + ee] = bias ? __fadd_rn(acc[e], bias[ee]) : acc[e];
-        }
+        float4* dst = reinterpret_cast<float4*>(part + ((int64_t)blockIdx.z * T + t) * E + e0 + 8 * c);
+        dst[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        dst[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
     }
 }
 
-// One warp per token: top-k + softmax over a logits row in global memory.
-__global__ void __launch_bounds__(256) topk_rows_kernel(const float* __restrict__ logits, int64_t T, int E, int k,
-                                                       int* __restrict__ idx, float* __restrict__ wts) {
-    const int64_t t = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+// One warp per token: the nb partial logits of each expert summed by the
+// block tree (a binary-counter stack: leaf b closes one pair per trailing 1
+// bit of b, the left operand first; the remaining stack is folded from the
+// top, each entry added on the left), + bias, then top-k + softmax.
+constexpr int kFoldMaxLevels = 8;   // nb <= 255 blocks (d <= 130560)
+__global__ void __launch_bounds__(256) fold_topk_kernel(const float* __restrict__ part, int nb, int64_t T, int E,
+                                                       int k, const float* __restrict__ bias,
+                                                       float* __restrict__ logits, int* __restrict__ idx,
+                                                       float* __restrict__ wts) {
+    __shared__ float rows[8][256];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t t = (int64_t)blockIdx.x * 8 + warp;
     if (t >= T) return;
-    topk_softmax_warp(logits + t * E, E, k, t, idx, wts, threadIdx.x & 31);
+    float* row = rows[warp];
+    for (int e = lane; e < E; e += 32) {
+        float st[kFoldMaxLevels];
+        int top = 0;
+        for (int b = 0; b < nb; ++b) {
+            float v = part[((int64_t)b * T + t) * E + e];
+            for (int i = b; i & 1; i >>= 1) v = st[--top] + v;
+            st[top++] = v;
+        }
+        float v = st[--top];
+        while (top > 0) v = st[--top] + v;
+        if (bias) v = __fadd_rn(v, bias[e]);
+        row[e] = v;
+        if (logits != nullptr) logits[t * E + e] = v;
+    }
+    __syncwarp();
+    topk_softmax_warp(row, E, k, t, idx, wts, lane);
 }
 
 template <typename TX, typename TW>
-cudaError_t launch_sliced(const void* x, const void* wr, const float* bias, const Shape& s, float* logits, int* idx,
-                          float* w, cudaStream_t st) {
-    auto kern = router_slice_kernel<TX, TW>;
-    static SmemAttr attr;
-    cudaError_t err = ensure_smem(kern, kSliceSmem, attr);
-    if (err != cudaSuccess) return err;
-    const dim3 grid((unsigned)((s.T() + kSliceTM - 1) / kSliceTM), s.E / kSliceEC);
-    kern<<<grid, kSliceThreads, kSliceSmem, st>>>((const TX*)x, (const TW*)wr, bias, s.T(), s.d, s.E, logits);
-    topk_rows_kernel<<<(unsigned)((s.T() + 7) / 8), 256, 0, st>>>(logits, s.T(), s.E, s.k, idx, w);
+cudaError_t launch_blocked(const void* x, const void* wr, const float* bias, const Shape& s, float* logits,
+                           float* part, int* idx, float* w, cudaStream_t st) {
+    const int nb = (s.d + kRouterBlockJ - 1) / kRouterBlockJ;
+    if (router_sliced(s)) {
+        auto kern = router_slice_kernel<TX, TW>;
+        static SmemAttr attr;
+        cudaError_t err = ensure_smem(kern, kSliceSmem, attr);
+        if (err != cudaSuccess) return err;
+        const dim3 grid((unsigned)((s.T() + kSliceTM - 1) / kSliceTM), s.E / kSliceEC, nb);
+        kern<<<grid, kSliceThreads, kSliceSmem, st>>>((const TX*)x, (const TW*)wr, s.T(), s.d, s.E, part);
+    } else {
+        constexpr int MT = 4, kTiledTM = 16 * MT;
+        const size_t smem = sizeof(float) * 2 * (size_t)kTiledKC * (kTiledTM + (size_t)s.E);
+        auto kern = router_tiled_kernel<TX, TW, MT>;
+        static SmemAttr attr;
+        cudaError_t err = ensure_smem(kern, smem, attr);
+        if (err != cudaSuccess) return err;
+        const dim3 grid((unsigned)((s.T() + kTiledTM - 1) / kTiledTM), nb);
+        kern<<<grid, 2 * s.E, smem, st>>>((const TX*)x, (const TW*)wr, s.T(), s.d, s.E, part);
+    }
+    fold_topk_kernel<<<(unsigned)((s.T() + 7) / 8), 256, 0, st>>>(part, nb, s.T(), s.E, s.k, bias, logits, idx, w);
     return cudaGetLastError();
 }
 
@@ -451,37 +482,18 @@ cudaError_t launch_typed(const void* x, const void* wr, const float* bias, const
     return launch_items<TX, TW, 1>(x, wr, bias, s, CT, logits, idx, w, st);
 }
 
-template <typename TX, typename TW, int MT>
-cudaError_t launch_tiled(const void* x, const void* wr, const float* bias, const Shape& s, float* logits, int* idx,
-                         float* w, cudaStream_t st) {
-    constexpr int kTiledTM = 16 * MT;
-    const int threads = 2 * s.E;
-    const size_t smem =
-        sizeof(float) * (2 * (size_t)kTiledKC * kTiledTM + (size_t)std::max(2 * kTiledKC, kTiledTM) * s.E);
-    auto kern = router_tiled_kernel<TX, TW, MT>;
-    static SmemAttr attr;
-    cudaError_t err = ensure_smem(kern, smem, attr);
-    if (err != cudaSuccess) return err;
-    const int64_t blocks = (s.T() + kTiledTM - 1) / kTiledTM;
-    kern<<<(unsigned)blocks, threads, smem, st>>>((const TX*)x, (const TW*)wr, bias, s.T(), s.d, s.E, s.k, logits,
-                                                  idx, w);
-    return cudaGetLastError();
-}
-
 template <typename TX, typename TW>
 cudaError_t launch_any(const void* x, const void* wr, const float* bias, const Shape& s, float* logits,
                        float* logits_scratch, int* idx, float* w, cudaStream_t st) {
-    if (s.E < kRouterTiledMinExperts || s.E % 32 != 0) return launch_typed<TX, TW>(x, wr, bias, s, logits, idx, w, st);
-    if (router_sliced(s))
-        return launch_sliced<TX, TW>(x, wr, bias, s, logits ? logits : logits_scratch, idx, w, st);
-    return launch_tiled<TX, TW, 4>(x, wr, bias, s, logits, idx, w, st);
+    if (!router_blocked(s)) return launch_typed<TX, TW>(x, wr, bias, s, logits, idx, w, st);
+    return launch_blocked<TX, TW>(x, wr, bias, s, logits, logits_scratch, idx, w, st);
 }
 
 }  // namespace
 
-bool router_sliced(const Shape& s) {
-    return s.E >= kRouterTiledMinExperts && s.E % 32 == 0 && s.T() < kRouterSliceMaxT;
-}
+bool router_blocked(const Shape& s) { return s.E >= kRouterTiledMinExperts && s.E % 32 == 0; }
+
+bool router_sliced(const Shape& s) { return router_blocked(s) && s.T() < kRouterSliceMaxT; }
 
 cudaError_t launch_router_topk(const void* x, const void* wr, const float* bias, const Shape& s,
                                float* logits_scratch, float* logits, int* idx, float* w, cudaStream_t st) {

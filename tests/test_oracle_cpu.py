@@ -143,19 +143,35 @@ def test_e4m3_encoder_matches_product_quantiser():
     assert L.oracle_e4m3_decode(0x7E) == 448.0 and L.oracle_e4m3_decode(0x01) == 2.0 ** -9
 
 
-def test_logit_order_many_experts_is_sequential():
-    """E >= 64: one sequential fmaf chain over j per (token, expert), then + bias."""
-    cfg = sm.LayerConfig(1, 3, 256, 128, 64, 2, 1.0, zipf_s=1.0)
+def _block_tree(b, a, n):
+    if n == 1:
+        return b[a]
+    h = 1
+    while 2 * h < n:
+        h *= 2
+    return np.float32(_block_tree(b, a, h) + _block_tree(b, a + h, n - h))
+
+
+@pytest.mark.parametrize("d", [256, 1536, 3584])
+def test_logit_order_many_experts_is_blocked_tree(d):
+    """E >= 64: per (token, expert) one fmaf chain per 512-j block from 0.0f,
+    the blocks summed by the tree tree(a, n) = tree(a, h) + tree(a + h, n - h)
+    (h the largest power of two below n), then + bias."""
+    cfg = sm.LayerConfig(1, 2, d, 128, 64, 2, 1.0, zipf_s=1.0)
     inp = sm.make_inputs(cfg, 2)
-    r = O.route(inp["x"], inp["wr"], inp["bias"], 1, 3, 256, 64, 2, 16, False)
+    r = O.route(inp["x"], inp["wr"], inp["bias"], 1, 2, d, 64, 2, 16, False)
     x = inp["x"].view(np.float16).astype(np.float64)
     w = inp["wr"].view(np.float16).astype(np.float64)
-    for t in range(3):
+    nb = (d + 511) // 512
+    for t in range(2):
         for e in (0, 17, 63):
-            acc = np.float32(0)
-            for j in range(256):
-                acc = np.float32(np.float64(acc) + x[t, j] * w[j, e])   # exact product + one rounding
-            assert np.float32(acc + inp["bias"][e]) == r["logits"][t, e]
+            blocks = []
+            for b in range(nb):
+                acc = np.float32(0)
+                for j in range(512 * b, min(d, 512 * b + 512)):
+                    acc = np.float32(np.float64(acc) + x[t, j] * w[j, e])   # exact product + one rounding
+                blocks.append(acc)
+            assert np.float32(_block_tree(blocks, 0, nb) + inp["bias"][e]) == r["logits"][t, e]
 
 
 def test_int8_channel_quantiser_matches_numpy():
