@@ -10,7 +10,7 @@
 //      with fmaf, starting at 0.0f;  the 32 partial sums are then combined by
 //      an xor butterfly  p[l] = p[l] + p[l ^ off]  for off = 16, 8, 4, 2, 1;
 //      logit = p[0] (+ bias[e], one rounded add);
-//    for E >= 64 and a multiple of 32 (router_tiled_kernel / router_slice_kernel, then
+//    for E >= 64 and a multiple of 32 (router_tiled_kernel, then
 //    fold_topk_kernel): d is cut into blocks of kRouterBlockJ = 512 j's; per (token, expert)
 //    each block is one sequential fmaf chain over its j's from 0.0f (one CTA's work, written
 //    as a partial logit), and fold_topk_kernel sums the nb blocks by the fixed tree
@@ -181,7 +181,8 @@ __global__ void __launch_bounds__(kWarps * 32) router_topk_kernel(
 // Many experts (E >= kRouterTiledMinExperts, E % 32 == 0): a register-tiled
 // CUDA-core GEMM over one 512-j block of d per CTA (grid.y = block), written
 // as partial logits part[block][t][e] for fold_topk_kernel.  CTA = 16*MT
-// tokens x all E experts, 2E threads; thread (r, c) owns tokens MT*r.. and
+// tokens x an expert slice of EC experts (grid.z; EC = E, or 32 for small
+// batches), 2EC threads; thread (r, c) owns tokens MT*r.. and
 // experts 8c..8c+7 (4 vector shared loads per MT*8 FMAs); x and Wr K-slices
 // of 32 are staged in shared memory as f32 (x transposed), double-buffered:
 // the next slice is loaded into registers during the FMAs.  Splitting d into
@@ -193,12 +194,14 @@ template <typename TX, typename TW, int MT>
 __global__ void __launch_bounds__(MT == 8 ? 256 : 512) router_tiled_kernel(
     const TX* __restrict__ x, const TW* __restrict__ wr, int64_t T, int d, int E, float* __restrict__ part) {
     constexpr int kTiledTM = 16 * MT;
-    constexpr int kXVec = kTiledTM * (kTiledKC / 8) / 128;   // x vectors per thread (>= 128 threads)
     extern __shared__ float sm[];
-    float* xs = sm;                              // [2][kTiledKC][kTiledTM]
-    float* ws = xs + 2 * kTiledKC * kTiledTM;    // [2][kTiledKC][E]
     const int nthr = blockDim.x;
-    const int cgroups = E / 8;
+    const int EC = nthr / 2;                     // experts of this CTA's slice (a multiple of 32)
+    const int e0 = blockIdx.z * EC;
+    float* xs = sm;                              // [2][kTiledKC][kTiledTM]
+    float* ws = xs + 2 * kTiledKC * kTiledTM;    // [2][kTiledKC][EC]
+    const int cgroups = EC / 8;
+    const int xvecs = kTiledTM * (kTiledKC / 8);   // x vectors per slice (8 tokens of 16 B each per j-row)
     // a warp covers 8 token rows x 4 expert groups, so its shared-memory
     // loads touch 8 x-rows (256 B) and 4 router groups (128 B) per K step
     const int warp_id = threadIdx.x >> 5, lane_id = threadIdx.x & 31;
@@ -214,6 +217,7 @@ __global__ void __launch_bounds__(MT == 8 ? 256 : 512) router_tiled_kernel(
 
     // The next K slice is loaded into registers while the current one is
     // multiplied out of shared memory (double-buffered, one barrier per slice).
+    constexpr int kXVec = kTiledTM * (kTiledKC / 8) / 64;   // x vectors per thread (>= 64 threads)
     uint4 xr[kXVec];
     float wreg[2][8];
     auto load_slice = [&](int j0) {
@@ -221,26 +225,26 @@ __global__ void __launch_bounds__(MT == 8 ? 256 : 512) router_tiled_kernel(
         for (int v = 0; v < kXVec; ++v) {
             const int vi = threadIdx.x + v * nthr;
             xr[v] = make_uint4(0u, 0u, 0u, 0u);
-            if (vi < kTiledTM * (kTiledKC / 8)) {
+            if (vi < xvecs) {
                 const int tt = vi / (kTiledKC / 8), jv = vi - tt * (kTiledKC / 8);
                 const int64_t t = t0 + tt;
                 if (t < T) xr[v] = __ldg(reinterpret_cast<const uint4*>(x + t * d + j0 + jv * 8));
             }
         }
 #pragma unroll
-        for (int v = 0; v < 2; ++v) {   // kTiledKC * E/8 vectors = 2 per thread
+        for (int v = 0; v < 2; ++v) {   // kTiledKC * EC/8 vectors = 2 per thread
             const int vi = threadIdx.x + v * nthr;
             const int jj = vi / cgroups, cc = vi - jj * cgroups;
-            load_wr8(wr + (int64_t)(j0 + jj) * E + 8 * cc, wreg[v]);
+            load_wr8(wr + (int64_t)(j0 + jj) * E + e0 + 8 * cc, wreg[v]);
         }
     };
     auto store_slice = [&](int buf) {
         float* xb = xs + buf * kTiledKC * kTiledTM;
-        float* wb = ws + buf * kTiledKC * E;
+        float* wb = ws + buf * kTiledKC * EC;
 #pragma unroll
         for (int v = 0; v < kXVec; ++v) {
             const int vi = threadIdx.x + v * nthr;
-            if (vi < kTiledTM * (kTiledKC / 8)) {
+            if (vi < xvecs) {
                 const int tt = vi / (kTiledKC / 8), jv = vi - tt * (kTiledKC / 8);
                 const uint32_t* u = reinterpret_cast<const uint32_t*>(&xr[v]);
 #pragma unroll
@@ -255,7 +259,7 @@ __global__ void __launch_bounds__(MT == 8 ? 256 : 512) router_tiled_kernel(
         for (int v = 0; v < 2; ++v) {
             const int vi = threadIdx.x + v * nthr;
             const int jj = vi / cgroups, cc = vi - jj * cgroups;
-            float4* dst = reinterpret_cast<float4*>(wb + jj * E + 8 * cc);
+            float4* dst = reinterpret_cast<float4*>(wb + jj * EC + 8 * cc);
             dst[0] = make_float4(wreg[v][0], wreg[v][1], wreg[v][2], wreg[v][3]);
             dst[1] = make_float4(wreg[v][4], wreg[v][5], wreg[v][6], wreg[v][7]);
         }
@@ -268,11 +272,11 @@ __global__ void __launch_bounds__(MT == 8 ? 256 : 512) router_tiled_kernel(
         const int buf = sl & 1;
         if (sl + 1 < nslices) load_slice(jbeg + (sl + 1) * kTiledKC);
         const float* xb = xs + buf * kTiledKC * kTiledTM;
-        const float* wb = ws + buf * kTiledKC * E;
+        const float* wb = ws + buf * kTiledKC * EC;
 #pragma unroll 4
         for (int jj = 0; jj < kTiledKC; ++jj) {
-            const float4 wa = *reinterpret_cast<const float4*>(wb + jj * E + 8 * c);
-            const float4 wc = *reinterpret_cast<const float4*>(wb + jj * E + 8 * c + 4);
+            const float4 wa = *reinterpret_cast<const float4*>(wb + jj * EC + 8 * c);
+            const float4 wc = *reinterpret_cast<const float4*>(wb + jj * EC + 8 * c + 4);
             const float wv[8] = {wa.x, wa.y, wa.z, wa.w, wc.x, wc.y, wc.z, wc.w};
             float xv[MT];
 #pragma unroll
@@ -293,106 +297,10 @@ __global__ void __launch_bounds__(MT == 8 ? 256 : 512) router_tiled_kernel(
     for (int i = 0; i < MT; ++i) {
         const int64_t t = t0 + MT * r + i;
         if (t < T) {
-            float4* dst = reinterpret_cast<float4*>(pb + t * E + 8 * c);
+            float4* dst = reinterpret_cast<float4*>(pb + t * E + e0 + 8 * c);
             dst[0] = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
             dst[1] = make_float4(acc[i][4], acc[i][5], acc[i][6], acc[i][7]);
         }
-    }
-}
-
-// Few tokens, many experts (router_sliced): CTA = 16 tokens x 32 experts x
-// one 512-j block of d (grid.z = block), 64 threads, thread (r, c) = token r,
-// experts 8c..8c+7 of the slice; x and Wr K-slices of 128 double-buffered in
-// shared memory.  Same per-(token, expert, block) chain as
-// router_tiled_kernel; partial logits go to part[block][t][e].
-constexpr int kSliceTM = 16, kSliceEC = 32, kSliceKC = 128, kSliceThreads = 64;
-constexpr size_t kSliceSmem = sizeof(float) * 2 * kSliceKC * (kSliceTM + kSliceEC);
-
-template <typename TX, typename TW>
-__global__ void __launch_bounds__(kSliceThreads) router_slice_kernel(
-    const TX* __restrict__ x, const TW* __restrict__ wr, int64_t T, int d, int E, float* __restrict__ part) {
-    extern __shared__ float sm[];
-    float* xs = sm;                               // [2][KC][TM]
-    float* ws = xs + 2 * kSliceKC * kSliceTM;     // [2][KC][EC]
-    const int r = threadIdx.x >> 2, c = threadIdx.x & 3;
-    const int64_t t0 = (int64_t)blockIdx.x * kSliceTM;
-    const int e0 = blockIdx.y * kSliceEC;
-    const int jbeg = blockIdx.z * kRouterBlockJ, jend = min(d, jbeg + kRouterBlockJ);
-    constexpr int kXV = kSliceTM * (kSliceKC / 8) / kSliceThreads;   // 4 x vectors per thread
-    constexpr int kWV = kSliceKC * (kSliceEC / 8) / kSliceThreads;   // 8 router 8-vectors per thread
-    uint4 xr[kXV];
-    float wreg[kWV][8];
-    auto load_slice = [&](int j0) {
-#pragma unroll
-        for (int v = 0; v < kXV; ++v) {
-            // consecutive lanes take consecutive tokens, so the transposed
-            // shared-memory stores below hit distinct banks
-            const int vi = threadIdx.x + v * kSliceThreads;
-            const int tt = vi % kSliceTM, jv = vi / kSliceTM;
-            const int64_t t = t0 + tt;
-            xr[v] = t < T ? __ldg(reinterpret_cast<const uint4*>(x + t * d + j0 + jv * 8)) : make_uint4(0, 0, 0, 0);
-        }
-#pragma unroll
-        for (int v = 0; v < kWV; ++v) {
-            const int vi = threadIdx.x + v * kSliceThreads;
-            const int jj = vi >> 2, cc = vi & 3;
-            load_wr8(wr + (int64_t)(j0 + jj) * E + e0 + 8 * cc, wreg[v]);
-        }
-    };
-    auto store_slice = [&](int buf) {
-        float* xb = xs + buf * kSliceKC * kSliceTM;
-        float* wb = ws + buf * kSliceKC * kSliceEC;
-#pragma unroll
-        for (int v = 0; v < kXV; ++v) {
-            const int vi = threadIdx.x + v * kSliceThreads;
-            const int tt = vi % kSliceTM, jv = vi / kSliceTM;
-            const uint32_t* u = reinterpret_cast<const uint32_t*>(&xr[v]);
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const float2 p = F16Traits<TX>::unpack2(u[q]);
-                xb[(jv * 8 + 2 * q) * kSliceTM + tt] = p.x;
-                xb[(jv * 8 + 2 * q + 1) * kSliceTM + tt] = p.y;
-            }
-        }
-#pragma unroll
-        for (int v = 0; v < kWV; ++v) {
-            const int vi = threadIdx.x + v * kSliceThreads;
-            const int jj = vi >> 2, cc = vi & 3;
-            float4* dst = reinterpret_cast<float4*>(wb + jj * kSliceEC + 8 * cc);
-            dst[0] = make_float4(wreg[v][0], wreg[v][1], wreg[v][2], wreg[v][3]);
-            dst[1] = make_float4(wreg[v][4], wreg[v][5], wreg[v][6], wreg[v][7]);
-        }
-    };
-    float acc[8];
-#pragma unroll
-    for (int e = 0; e < 8; ++e) acc[e] = 0.0f;
-    const int nslices = (jend - jbeg) / kSliceKC;   // 512 or 256 j's (d % 256 == 0)
-    load_slice(jbeg);
-    store_slice(0);
-    __syncthreads();
-    for (int sl = 0; sl < nslices; ++sl) {
-        const int buf = sl & 1;
-        if (sl + 1 < nslices) load_slice(jbeg + (sl + 1) * kSliceKC);
-        const float* xb = xs + buf * kSliceKC * kSliceTM;
-        const float* wb = ws + buf * kSliceKC * kSliceEC;
-#pragma unroll 8
-        for (int jj = 0; jj < kSliceKC; ++jj) {
-            const float4 wa = *reinterpret_cast<const float4*>(wb + jj * kSliceEC + 8 * c);
-            const float4 wc = *reinterpret_cast<const float4*>(wb + jj * kSliceEC + 8 * c + 4);
-            const float xv = xb[jj * kSliceTM + r];
-            ffma2(acc[0], acc[1], wa.x, wa.y, xv);
-            ffma2(acc[2], acc[3], wa.z, wa.w, xv);
-            ffma2(acc[4], acc[5], wc.x, wc.y, xv);
-            ffma2(acc[6], acc[7], wc.z, wc.w, xv);
-        }
-        if (sl + 1 < nslices) store_slice(buf ^ 1);
-        __syncthreads();
-    }
-    const int64_t t = t0 + r;
-    if (t < T) {
-        float4* dst = reinterpret_cast<float4*>(part + ((int64_t)blockIdx.z * T + t) * E + e0 + 8 * c);
-        dst[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
-        dst[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
     }
 }
 
@@ -432,23 +340,18 @@ template <typename TX, typename TW>
 cudaError_t launch_blocked(const void* x, const void* wr, const float* bias, const Shape& s, float* logits,
                            float* part, int* idx, float* w, cudaStream_t st) {
     const int nb = (s.d + kRouterBlockJ - 1) / kRouterBlockJ;
-    if (router_sliced(s)) {
-        auto kern = router_slice_kernel<TX, TW>;
-        static SmemAttr attr;
-        cudaError_t err = ensure_smem(kern, kSliceSmem, attr);
-        if (err != cudaSuccess) return err;
-        const dim3 grid((unsigned)((s.T() + kSliceTM - 1) / kSliceTM), s.E / kSliceEC, nb);
-        kern<<<grid, kSliceThreads, kSliceSmem, st>>>((const TX*)x, (const TW*)wr, s.T(), s.d, s.E, part);
-    } else {
-        constexpr int MT = 4, kTiledTM = 16 * MT;
-        const size_t smem = sizeof(float) * 2 * (size_t)kTiledKC * (kTiledTM + (size_t)s.E);
-        auto kern = router_tiled_kernel<TX, TW, MT>;
-        static SmemAttr attr;
-        cudaError_t err = ensure_smem(kern, smem, attr);
-        if (err != cudaSuccess) return err;
-        const dim3 grid((unsigned)((s.T() + kTiledTM - 1) / kTiledTM), nb);
-        kern<<<grid, 2 * s.E, smem, st>>>((const TX*)x, (const TW*)wr, s.T(), s.d, s.E, part);
-    }
+    // Tokens x experts x blocks: every expert in one CTA when the tokens alone
+    // fill the GPU (x read once per block), else 32-expert slices so that
+    // decode-sized batches still spread over every SM.
+    constexpr int MT = 4, kTiledTM = 16 * MT;
+    const int EC = router_sliced(s) ? 32 : s.E;
+    const size_t smem = sizeof(float) * 2 * (size_t)kTiledKC * (kTiledTM + (size_t)EC);
+    auto kern = router_tiled_kernel<TX, TW, MT>;
+    static SmemAttr attr;
+    cudaError_t err = ensure_smem(kern, 2 * (size_t)kTiledKC * (kTiledTM + 256) * sizeof(float), attr);
+    if (err != cudaSuccess) return err;
+    const dim3 grid((unsigned)((s.T() + kTiledTM - 1) / kTiledTM), nb, s.E / EC);
+    kern<<<grid, 2 * EC, smem, st>>>((const TX*)x, (const TW*)wr, s.T(), s.d, s.E, part);
     fold_topk_kernel<<<(unsigned)((s.T() + 7) / 8), 256, 0, st>>>(part, nb, s.T(), s.E, s.k, bias, logits, idx, w);
     return cudaGetLastError();
 }
