@@ -95,6 +95,12 @@ def workload(name: str, sm=None):
                                           router_f32=True, zipf_s=1.0),
         "ds3_int4_prefill": sm.LayerConfig(1, 8192, 7168, 2048, 256, 8, 1.25, dtype=sm.DTYPE_W4A16,
                                            router_f32=True, zipf_s=1.0),
+        # the reference's own include/config.h shape (4 batches x 256 tokens, d=4096, d_ff=16384, E=32,
+        # top-4, cf=0.8, CAP=32) in its four kernels' formats, with seeded data and the builder's scales
+        "refcfg_fp16": sm.LayerConfig(4, 256, 4096, 16384, 32, 4, 0.8, dtype=sm.DTYPE_F16),
+        "refcfg_int8": sm.LayerConfig(4, 256, 4096, 16384, 32, 4, 0.8, dtype=sm.DTYPE_INT8),
+        "refcfg_int4": sm.LayerConfig(4, 256, 4096, 16384, 32, 4, 0.8, dtype=sm.DTYPE_INT4_PTX),
+        "refcfg_fp8": sm.LayerConfig(4, 256, 4096, 16384, 32, 4, 0.8, dtype=sm.DTYPE_FP8),
         "ds3_nvfp4_decode": sm.LayerConfig(1, 512, 7168, 2048, 256, 8, 1.25, dtype=sm.DTYPE_NVFP4,
                                            router_f32=True, zipf_s=1.0),
         "ds3_nvfp4_prefill": sm.LayerConfig(1, 8192, 7168, 2048, 256, 8, 1.25, dtype=sm.DTYPE_NVFP4,
@@ -127,6 +133,15 @@ def load_peaks():
     return FALLBACK_PEAKS, "fallback"
 
 
+def tensor_peaks(peaks, eight_bit: bool):
+    """(burst, sustained) dense tensor TFLOP/s for the roofline: the measured
+    bf16 figures, doubled for the 8-bit kinds."""
+    burst = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+    sus = float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
+    f = 2.0 if eight_bit else 1.0   # dense int8 / fp8 tensor rate is twice bf16 on B200
+    return burst * f, sus * f
+
+
 def dtype_name(cfg):
     if cfg.nvfp4:
         return "nvfp4_g16_weights_bf16_act"
@@ -134,11 +149,15 @@ def dtype_name(cfg):
         return "int4_g128_weights_bf16_act"
     if cfg.int8ch:
         return "int8_channel_token"
+    if cfg.int4ptx:
+        return "int4_per_tensor"
+    if cfg.fp8pt:
+        return "fp8_e4m3_per_tensor"
     return "int8" if cfg.int8 else ("fp8_e4m3_block" if cfg.fp8 else ("bf16" if cfg.bf16 else "f16"))
 
 
 def cfg_json(name, cfg, cap):
-    wb = 0.5 if cfg.w4 else (1 if (cfg.int8 or cfg.int8ch or cfg.fp8) else 2)
+    wb = 0.5 if (cfg.w4 or cfg.int4ptx) else (1 if (cfg.int8 or cfg.int8ch or cfg.fp8 or cfg.fp8pt) else 2)
     xb = cfg.T * cfg.d_model * 2 / 1e6
     wmb = 3 * cfg.num_experts * cfg.d_model * cfg.d_ff * wb / 1e9
     return {"workload": name, "num_batches": cfg.num_batches, "tokens_per_batch": cfg.tokens,
@@ -315,8 +334,8 @@ def device_inputs(layer, seed: int):
     import torch
     import sparsemoe_b200 as sm
     cfg = layer.cfg
-    if cfg.int8:
-        # the reference's per-tensor int8 format: host generator + the host quantiser
+    if cfg.per_tensor:
+        # the reference's per-tensor formats (int8, packed int4, e4m3): host generator + host quantisers
         layer.host_inputs = sm.make_inputs(cfg, seed)
         layer.load(layer.host_inputs)
         return
@@ -428,7 +447,8 @@ def oracle_measure(inp: dict, cfg, cap: int, sample_tokens: int, nthreads: int):
     fn = O.ffn_combine_fp8 if cfg.fp8 else (O.ffn_combine_int8 if cfg.int8 else
                                             (O.ffn_combine_nvfp4 if cfg.nvfp4 else
                                              O.ffn_combine_w4 if cfg.w4 else
-                                             (O.ffn_combine_int8ch if cfg.int8ch else None)))
+                                             (O.ffn_combine_int8ch if cfg.int8ch else
+                                              (O.ffn_combine_per_tensor if (cfg.int4ptx or cfg.fp8pt) else None))))
     t0 = time.perf_counter()
     if fn is not None:
         fn(inp["x"], inp, cfg, r["idx"], r["w"], r["route_slot"], 0, S, nthreads)
@@ -531,7 +551,7 @@ def ep_parity(layer, cfg, ws, rank, dev, glob, int8_full=None):
                               cfg.dtype, cfg.router_f32, cfg.zipf_s, cfg.cap, cfg.act_scale, cfg.mid_scale)
         order = lambda t: t.reshape(ws * B * N, -1)  # noqa: E731
     single = sm.MoeLayer(full, dev, want_logits=False, want_out16=False)
-    if cfg.int8:
+    if cfg.per_tensor:
         single.load({**int8_full, "x": np.zeros((0, cfg.d_model), np.uint16)} if full.T == 0 else
                     {**int8_full, "x": order(xs).view(torch.int16).cpu().numpy().view(np.uint16)})
     else:
@@ -572,8 +592,8 @@ def run_ep(args, cfg, ws, rank, local, dev):
     layer = ExpertParallelLayer(cfg, dev, chunks=args.ep_chunks, global_batch=glob, transport=args.ep_transport,
                                 placement=placement)
     full = None
-    if cfg.int8:
-        # the reference's per-tensor int8 format: host generator + host quantiser (all experts; each
+    if cfg.per_tensor:
+        # the reference's per-tensor formats: host generator + host quantiser (all experts; each
         # rank keeps its own), this rank's tokens
         full = sm.make_inputs(cfg, 5)
         layer.load({**full, "x": sm.make_inputs(cfg, 100 + rank)["x"]})
@@ -649,9 +669,8 @@ def run_ep(args, cfg, ws, rank, local, dev):
     parity = ep_parity(layer, cfg, ws, rank, dev, glob, full)
     barrier(ws)
     peaks, peak_src = load_peaks()
-    peak_tf = float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
-    if cfg.int8 or cfg.int8ch or cfg.fp8:
-        peak_tf *= 2.0   # dense int8 / fp8 tensor rate is twice bf16 on B200
+    eight_bit = cfg.int8 or cfg.int8ch or cfg.fp8 or cfg.int4ptx or cfg.fp8pt
+    peak_tf, peak_sus = tensor_peaks(peaks, eight_bit)
     owner_rows.append(layer.owner_rows())   # the same tokens every step
     flop_ffn = 6.0 * cfg.d_model * cfg.d_ff * statistics.mean(owner_rows)
     ach = flop_ffn / (phase_ms["expert_ffn_compute"] * 1e-3) / 1e12
@@ -666,9 +685,9 @@ def run_ep(args, cfg, ws, rank, local, dev):
         "config": {**cfg_json(args.config, cfg, layer.cap),
                    "parallelism": parallelism_desc(args, cfg, ws, layer.cap, "ep")},
         "roofline": {"bound": "tensor", "achieved": ach_min, "peak": peak_tf, "unit": "TFLOP/s",
-                     "frac": ach_min / peak_tf, "traffic": None,
+                     "frac": ach_min / peak_tf, "frac_of_sustained": ach_min / peak_sus, "traffic": None,
                      "kernel": "expert_ffn phase (up/gate + down tcgen05 GEMMs), slowest rank",
-                     "peak_source": f"{peak_src} bf16_tflops_sustained" + (" x 2 (8-bit)" if cfg.int8 or cfg.int8ch or cfg.fp8 else "")},
+                     "peak_source": f"{peak_src} bf16_tflops (burst)" + (" x 2 (8-bit)" if eight_bit else "")},
         "phases_ms": phase_ms,
         "e2e": {"value": ws * cfg.T / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms, "serial_ms_per_step": serial_ms,
@@ -814,11 +833,11 @@ def main():
 
     # ---- roofline of the dominant kernel (up/gate GEMM with fused SwiGLU) --
     peaks, peak_src = load_peaks()
-    peak_tf = float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
-    peak_note = f"{peak_src} bf16_tflops_sustained (cuBLAS bf16, power-capped loop)"
-    if cfg.int8 or cfg.int8ch or cfg.fp8:
-        peak_tf *= 2.0   # dense int8 / fp8 tensor rate is twice bf16 on B200
-        peak_note = f"2 x {peak_src} bf16_tflops_sustained (dense 8-bit rate = 2x bf16; no 8-bit peak measured)"
+    eight_bit = cfg.int8 or cfg.int8ch or cfg.fp8 or cfg.int4ptx or cfg.fp8pt
+    peak_tf, peak_sus = tensor_peaks(peaks, eight_bit)
+    peak_note = (f"{peak_src} bf16_tflops (cuBLAS bf16 burst; the timed region is ~20 steps, not a seconds-long "
+                 f"loop)" if not eight_bit else
+                 f"2 x {peak_src} bf16_tflops burst (dense 8-bit rate = 2x bf16; no 8-bit peak measured)")
     d, f = cfg.d_model, cfg.d_ff
     flop_up = 4.0 * d * f * kept            # gate + up, kept routes only
     flop_down = 2.0 * d * f * kept
@@ -836,7 +855,7 @@ def main():
         "config": {**cfg_json(args.config, cfg, layer.cap),
                    "parallelism": parallelism_desc(args, cfg, ws, layer.cap, mode)},
         "roofline": {"bound": "tensor", "achieved": ach_up, "peak": peak_tf, "unit": "TFLOP/s",
-                     "frac": ach_up / peak_tf, "traffic": traffic,
+                     "frac": ach_up / peak_tf, "frac_of_sustained": ach_up / peak_sus, "traffic": traffic,
                      "kernel": "expert_up_gate_gemm (tcgen05, fused SwiGLU)",
                      "peak_source": peak_note},
         "stages_ms": stage_ms,

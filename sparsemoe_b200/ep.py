@@ -169,6 +169,8 @@ class ExpertParallelLayer:
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         assert cfg.num_experts % self.world == 0, "experts must divide evenly over the ranks"
+        assert not (cfg.int4ptx or cfg.fp8pt), \
+            "the reference's packed int4 and per-tensor fp8 formats run on one GPU (solve / moe_solve_v2)"
         self.cfg = cfg
         self.global_batch = global_batch
         self.device = torch.device(device)
