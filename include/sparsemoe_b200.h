@@ -104,6 +104,19 @@ typedef struct MoeDims {
     // Non-zero: the routing stages stop before the gather (expert parallelism
     // over peer memory, where moe_stage_dispatch_peer gathers into the owners).
     int skip_gather;
+    // The stages either side of the layer (no reference counterpart; a
+    // transformer block's pre-MoE norm and residual connection).  Optional:
+    // norm_weight (device [d], the activation dtype) turns on an RMSNorm of
+    // the input rows before the router, written to norm_out (device [B, N, d],
+    // the activation dtype; required with norm_weight), which the router and
+    // the gather then read:  xn = round16((x * g) / sqrt(sum(x^2) / d + eps)).
+    // residual (device [B, N, d], the activation dtype) is added to every
+    // output row in the combine (out = residual + sum_l w_l y_l, the sum in
+    // route order), usually the un-normalised input.
+    const void* norm_weight;
+    float norm_eps;
+    void* norm_out;
+    const void* residual;
 } MoeDims;
 
 // Reference: kernels/launcher.h:21 `extern "C" void solve(MoEArgs args)`.

@@ -122,6 +122,11 @@ inline uint8_t f32_to_e4m3(float x) {
     return sgn | (uint8_t)(((e + 7) << 3) | mq);
 }
 
+// Optional residual rows [T, d] (16-bit) every combine starts from
+// (oracle_set_residual): out = ((r + w0*y0) + w1*y1) + ... instead of from 0.
+const uint16_t* g_residual = nullptr;
+int g_residual_bf16 = 0;
+
 // The router's block tree for many experts (E >= 64): blocks of 512 j's,
 // tree(a, n) = tree(a, h) + tree(a + h, n - h) with h the largest power of
 // two below n.
@@ -138,6 +143,40 @@ float block_tree(const float* b, int a, int n) {
 extern "C" {
 
 uint8_t oracle_e4m3(float x) { return f32_to_e4m3(x); }
+
+void oracle_set_residual(const uint16_t* residual, int bf16) {
+    g_residual = residual;
+    g_residual_bf16 = bf16;
+}
+
+// Pre-MoE RMSNorm in the GPU kernel's order (norm.cu): ss over j with fmaf
+// from 0.0f, lane l owning the 8-element chunks l, l+32, ... in ascending j,
+// the 32 lane sums combined by the xor butterfly; r = sqrt(ss / d + eps);
+// xn_j = round16((x_j * g_j) / r).
+void oracle_rmsnorm(const uint16_t* x, const uint16_t* g, int64_t T, int d, float eps, int bf16, uint16_t* out) {
+    for (int64_t t = 0; t < T; ++t) {
+        const uint16_t* xr = x + t * d;
+        float p[32], q[32];
+        for (int l = 0; l < 32; ++l) {
+            float acc = 0.0f;
+            for (int c = l; c < d / 8; c += 32)
+                for (int jj = 0; jj < 8; ++jj) {
+                    const float v = to_f32(xr[8 * c + jj], bf16);
+                    acc = fmaf(v, v, acc);
+                }
+            p[l] = acc;
+        }
+        for (int off = 16; off > 0; off >>= 1) {
+            for (int l = 0; l < 32; ++l) q[l] = p[l] + p[l ^ off];
+            for (int l = 0; l < 32; ++l) p[l] = q[l];
+        }
+        const float r = std::sqrt(p[0] / (float)d + eps);
+        for (int j = 0; j < d; ++j) {
+            const float prod = to_f32(xr[j], bf16) * to_f32(g[j], bf16);
+            out[t * d + j] = bf16 ? f32_to_bf16_rn(prod / r) : f32_to_f16_rn(prod / r);
+        }
+    }
+}
 float oracle_e4m3_decode(uint8_t v) { return e4m3_to_f32(v); }
 
 // inputs/data.cu:392-398 (same float expression, rounded up to 16).
@@ -340,7 +379,7 @@ void ffn_impl(const uint16_t* x, RowG row_g, RowU row_u, RowD row_d, int d, int 
     parallel_for(t_end - t_begin, nthreads, [&](int64_t i) {
         const int64_t t = t_begin + i;
         float* o = out + t * d;
-        for (int c = 0; c < d; ++c) o[c] = 0.0f;
+        for (int c = 0; c < d; ++c) o[c] = g_residual ? to_f32(g_residual[t * d + c], g_residual_bf16) : 0.0f;
         for (int l = 0; l < k; ++l) {
             const int64_t r = t * k + l;
             if (route_slot[r] < 0) continue;
@@ -542,7 +581,7 @@ void oracle_ffn_combine_fp8pt(const uint16_t* x, const uint8_t* wg, const uint8_
     parallel_for(t_end - t_begin, nthreads, [&](int64_t i) {
         const int64_t t = t_begin + i;
         float* o = out + t * d;
-        for (int c = 0; c < d; ++c) o[c] = 0.0f;
+        for (int c = 0; c < d; ++c) o[c] = g_residual ? to_f32(g_residual[t * d + c], g_residual_bf16) : 0.0f;
         for (int l = 0; l < k; ++l) {
             const int64_t r = t * k + l;
             if (route_slot[r] < 0) continue;
@@ -635,7 +674,7 @@ void int_per_tensor_impl(const uint16_t* x, const int8_t* wg, const int8_t* wu, 
     parallel_for(t_end - t_begin, nthreads, [&](int64_t i) {
         const int64_t t = t_begin + i;
         float* o = out + t * d;
-        for (int c = 0; c < d; ++c) o[c] = 0.0f;
+        for (int c = 0; c < d; ++c) o[c] = g_residual ? to_f32(g_residual[t * d + c], g_residual_bf16) : 0.0f;
         for (int l = 0; l < k; ++l) {
             const int64_t r = t * k + l;
             if (route_slot[r] < 0) continue;
@@ -731,7 +770,7 @@ void oracle_ffn_combine_fp8(const uint16_t* x, const uint8_t* wg, const uint8_t*
     parallel_for(t_end - t_begin, nthreads, [&](int64_t i) {
         const int64_t t = t_begin + i;
         float* o = out + t * d;
-        for (int c = 0; c < d; ++c) o[c] = 0.0f;
+        for (int c = 0; c < d; ++c) o[c] = g_residual ? to_f32(g_residual[t * d + c], g_residual_bf16) : 0.0f;
         for (int l = 0; l < k; ++l) {
             const int64_t r = t * k + l;
             if (route_slot[r] < 0) continue;
@@ -819,7 +858,7 @@ void oracle_ffn_combine_int8ch(const uint16_t* x, const int8_t* wg, const int8_t
     parallel_for(t_end - t_begin, nthreads, [&](int64_t i) {
         const int64_t t = t_begin + i;
         float* o = out + t * d;
-        for (int c = 0; c < d; ++c) o[c] = 0.0f;
+        for (int c = 0; c < d; ++c) o[c] = g_residual ? to_f32(g_residual[t * d + c], g_residual_bf16) : 0.0f;
         for (int l = 0; l < k; ++l) {
             const int64_t r = t * k + l;
             if (route_slot[r] < 0) continue;

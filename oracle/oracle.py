@@ -61,6 +61,10 @@ def lib() -> ctypes.CDLL:
         L.oracle_e4m3.argtypes = [ctypes.c_float]
         L.oracle_e4m3_decode.restype = ctypes.c_float
         L.oracle_e4m3_decode.argtypes = [ctypes.c_uint8]
+        L.oracle_set_residual.restype = None
+        L.oracle_set_residual.argtypes = [P, I]
+        L.oracle_rmsnorm.restype = None
+        L.oracle_rmsnorm.argtypes = [P, P, ctypes.c_int64, I, F, I, P]
         L.oracle_ffn_combine_w4.restype = None
         L.oracle_ffn_combine_w4.argtypes = [P] * 10 + [I, I, I, I, P, P, P, ctypes.c_int64, ctypes.c_int64, P, I]
         _lib = L
@@ -208,10 +212,33 @@ def ffn_combine_w4(x, q, cfg, idx, w, route_slot, t_begin=0, t_end=None, nthread
     return out[t_begin:t_end]
 
 
+def rmsnorm(x, g, eps: float, bf16: bool) -> np.ndarray:
+    """Pre-MoE RMSNorm in the GPU kernel's order: [T, d] 16-bit rows -> 16-bit rows."""
+    x = np.ascontiguousarray(x, np.uint16)
+    out = np.empty_like(x)
+    lib().oracle_rmsnorm(_ptr(x), _ptr(np.ascontiguousarray(g, np.uint16)), x.shape[0], x.shape[1],
+                         ctypes.c_float(eps), int(bf16), _ptr(out))
+    return out
+
+
 def forward(inputs: dict, cfg, t_begin=0, t_end=None, nthreads=None):
-    """Whole layer on the CPU for a sparsemoe_b200.LayerConfig and make_inputs() dict."""
+    """Whole layer on the CPU for a sparsemoe_b200.LayerConfig and make_inputs() dict.
+    Optional keys: "norm_w" ([d] 16-bit gamma; "norm_eps") runs the pre-MoE
+    RMSNorm on x first; "residual" ([T, d] 16-bit) is added in the combine."""
     cap = cfg.capacity()
     act_bf16 = getattr(cfg, "act_bf16", cfg.bf16)
+    if inputs.get("norm_w") is not None:
+        inputs = {**inputs, "x": rmsnorm(inputs["x"], inputs["norm_w"], inputs.get("norm_eps", 1e-6), act_bf16)}
+    res = inputs.get("residual")
+    res = None if res is None else np.ascontiguousarray(res, np.uint16)
+    lib().oracle_set_residual(_ptr(res), int(act_bf16))
+    try:
+        return _forward(inputs, cfg, cap, act_bf16, t_begin, t_end, nthreads)
+    finally:
+        lib().oracle_set_residual(None, 0)
+
+
+def _forward(inputs, cfg, cap, act_bf16, t_begin, t_end, nthreads):
     r = route(inputs["x"], inputs["wr"], inputs.get("bias"), cfg.num_batches, cfg.tokens, cfg.d_model,
               cfg.num_experts, cfg.top_k, cap, act_bf16, cfg.router_f32, nthreads)
     if getattr(cfg, "nvfp4", False):

@@ -91,6 +91,7 @@ class MoeDims(ctypes.Structure):
         ("w4_zero_gate", _p), ("w4_zero_up", _p), ("w4_zero_down", _p),
         ("fp4_global_gate", _p), ("fp4_global_up", _p), ("fp4_global_down", _p),
         ("slot_base", _p), ("act_scale", _p), ("skip_gather", ctypes.c_int),
+        ("norm_weight", _p), ("norm_eps", ctypes.c_float), ("norm_out", _p), ("residual", _p),
     ]
 
 

@@ -421,8 +421,38 @@ cudaError_t mark_stage(int i, cudaStream_t stream) {
     return g_stage_on ? cudaEventRecord(g_stage_ev[i], stream) : cudaSuccess;
 }
 
+// The input rows the router and the gather read: MoeDims.norm_out when the
+// pre-MoE RMSNorm is on (the stage that writes it: enqueue_norm).
+MoEArgs routed_args(const MoEArgs* a, const MoeDims* dims) {
+    MoEArgs r = *a;
+    if (dims->norm_weight) r.input = static_cast<const half*>(dims->norm_out);
+    return r;
+}
+
+int check_norm(const MoeDims* dims) {
+    if (dims->norm_weight && !dims->norm_out) {
+        set_error("MoeDims.norm_weight needs MoeDims.norm_out (device [B, N, d] for the normalised rows)");
+        return MOE_ERR_INVALID_ARG;
+    }
+    if (dims->norm_weight && !(dims->norm_eps >= 0.0f)) {
+        set_error("MoeDims.norm_eps must be >= 0");
+        return MOE_ERR_INVALID_ARG;
+    }
+    return MOE_OK;
+}
+
+int enqueue_norm(const MoEArgs* a, const MoeDims* dims, const Shape& s, cudaStream_t stream) {
+    if (!dims->norm_weight) return MOE_OK;
+    MOE_TRY(launch_rmsnorm(a->input, dims->norm_weight, s, dims->norm_eps, dims->norm_out, stream), "rmsnorm");
+    return MOE_OK;
+}
+
 // Stages 1-3: router + top-k, slots, gather into the dense expert-major rows.
-int enqueue_route(const MoEArgs* a, const MoeDims* dims, const Shape& s, const Workspace& ws, cudaStream_t stream) {
+int enqueue_route(const MoEArgs* a_in, const MoeDims* dims, const Shape& s, const Workspace& ws, cudaStream_t stream) {
+    int rc = enqueue_norm(a_in, dims, s, stream);
+    if (rc != MOE_OK) return rc;
+    const MoEArgs ra = routed_args(a_in, dims);
+    const MoEArgs* a = &ra;
     MOE_TRY(launch_router_topk(a->input, a->router_weights, dims->router_bias, s, ws.router_logits, a->expert_logits,
                                a->selected_expert_indices, a->selected_expert_weights, stream),
             "router_topk");
@@ -527,7 +557,7 @@ int enqueue_layer(const MoEArgs* a, const MoeDims* dims, const Shape& s, const W
     }
     MOE_TRY(mark_stage(4, stream), "cudaEventRecord(stage event)");
     MOE_TRY(launch_combine(a->hidden_mlp_layer_2_out, a->selected_expert_indices, a->selected_expert_weights, s, ws,
-                           a->final_output, dims->output_16, stream),
+                           a->final_output, dims->output_16, stream, dims->residual),
             "combine");
     MOE_TRY(mark_stage(5, stream), "cudaEventRecord(stage event)");
     return MOE_OK;
@@ -540,6 +570,8 @@ extern "C" int moe_solve_v2(const MoEArgs* a, const MoeDims* dims, cudaStream_t 
     int rc = make_shape(dims, &s);
     if (rc != MOE_OK) return rc;
     rc = check_args(a, s.dtype);
+    if (rc != MOE_OK) return rc;
+    rc = check_norm(dims);
     if (rc != MOE_OK) return rc;
     DeviceState* st = nullptr;
     int dev = 0;
@@ -561,6 +593,8 @@ int route_stage_setup(const MoEArgs* a, const MoeDims* dims, const char* who, Sh
         set_error("%s: a routing buffer of MoEArgs is null", who);
         return MOE_ERR_INVALID_ARG;
     }
+    rc = check_norm(dims);
+    if (rc != MOE_OK) return rc;
     DeviceState* st = nullptr;
     int dev = 0;
     rc = device_state(&st, &dev);
@@ -585,7 +619,10 @@ extern "C" int moe_stage_route_counts(const MoEArgs* a, const MoeDims* dims, int
     if (rc != MOE_OK) return rc;
     if (!raw_counts) { set_error("moe_stage_route_counts: raw_counts is null"); return MOE_ERR_INVALID_ARG; }
     MOE_TRY(cudaMemsetAsync(ws.status, 0, sizeof(int), stream), "cudaMemsetAsync(status)");
-    MOE_TRY(launch_router_topk(a->input, a->router_weights, dims->router_bias, s, ws.router_logits, a->expert_logits,
+    const int nrc = enqueue_norm(a, dims, s, stream);
+    if (nrc != MOE_OK) return nrc;
+    const MoEArgs ra = routed_args(a, dims);
+    MOE_TRY(launch_router_topk(ra.input, a->router_weights, dims->router_bias, s, ws.router_logits, a->expert_logits,
                                a->selected_expert_indices, a->selected_expert_weights, stream),
             "router_topk");
     MOE_TRY(launch_dispatch_count(a->selected_expert_indices, s, ws, a->expert_counts, raw_counts, stream),
@@ -599,7 +636,8 @@ extern "C" int moe_stage_route_finish(const MoEArgs* a, const MoeDims* dims, cud
     const int rc = route_stage_setup(a, dims, "moe_stage_route_finish", &s, &ws);
     if (rc != MOE_OK) return rc;
     const FfnBuffers fb = ffn_buffers(a, s);
-    MOE_TRY(launch_dispatch_finish(a->input, a->selected_expert_indices, a->selected_expert_weights, s, ws,
+    MOE_TRY(launch_dispatch_finish(routed_args(a, dims).input, a->selected_expert_indices, a->selected_expert_weights,
+                                   s, ws,
                                    scales_of(a, s), dims->slot_base, a->expert_counts, a->expert_token_ids,
                                    a->expert_token_weights, fb.a_rows, stream, dims->skip_gather != 0),
             "dispatch");
@@ -755,8 +793,8 @@ extern "C" int moe_stage_dispatch_peer(const MoEArgs* a, const MoeDims* dims, co
     }
     gd.rank = plan;
     gd.row0 = plan + s.E;
-    MOE_TRY(launch_dispatch_gather(a->input, s, ws, scales_of(a, s), a->expert_counts, a->expert_token_ids, gd,
-                                   stream),
+    MOE_TRY(launch_dispatch_gather(routed_args(a, dims).input, s, ws, scales_of(a, s), a->expert_counts,
+                                   a->expert_token_ids, gd, stream),
             "dispatch (peer gather)");
     return MOE_OK;
 }
@@ -834,7 +872,7 @@ extern "C" int moe_stage_combine(const MoEArgs* a, const MoeDims* dims, cudaStre
         carve_workspace(st->ws, s, &ws);
     }
     MOE_TRY(launch_combine(a->hidden_mlp_layer_2_out, a->selected_expert_indices, a->selected_expert_weights, s, ws,
-                           a->final_output, dims->output_16, stream),
+                           a->final_output, dims->output_16, stream, dims->residual),
             "combine");
     return MOE_OK;
 }

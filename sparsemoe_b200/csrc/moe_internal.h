@@ -179,7 +179,10 @@ cudaError_t launch_fp4_down(const void* h_rows, const void* w_down, const void* 
 
 // combine.cu: gate-weighted gather-sum into [B, N, d].
 cudaError_t launch_combine(const float* y_rows, const int* idx, const float* w, const Shape& s,
-                           const Workspace& ws, float* out, void* out16, cudaStream_t st);
+                           const Workspace& ws, float* out, void* out16, cudaStream_t st,
+                           const void* residual = nullptr);
+// norm.cu: RMSNorm of the [T, d] input rows into out (MoeDims.norm_* semantics).
+cudaError_t launch_rmsnorm(const void* x, const void* g, const Shape& s, float eps, void* out, cudaStream_t st);
 
 void set_error(const char* fmt, ...);
 
@@ -187,6 +190,7 @@ void set_error(const char* fmt, ...);
 int make_shape_checked(const MoeDims* dims, Shape* s);
 int check_args_16(const MoEArgs* a);
 int check_args(const MoEArgs* a, int dtype);
+int check_norm(const MoeDims* dims);
 int current_device(int* dev, int* num_sms);           // sm_100 check, cached SM count
 void note_status_word(int dev, int* status);            // read by moe_check_device_status
 int enqueue_layer(const MoEArgs* a, const MoeDims* dims, const Shape& s, const Workspace& ws, int num_sms,

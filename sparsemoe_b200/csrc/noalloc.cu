@@ -79,6 +79,8 @@ extern "C" int moe_solve_v2_noalloc(const MoEArgs* a, const MoeDims* dims, cudaS
     if (rc != MOE_OK) return rc;
     rc = check_args(a, s.dtype);
     if (rc != MOE_OK) return rc;
+    rc = check_norm(dims);
+    if (rc != MOE_OK) return rc;
     if (dims->scratch) {
         set_error("moe_solve_v2_noalloc: MoeDims.scratch must be null (pass caller scratch to moe_solve_v2)");
         return MOE_ERR_INVALID_ARG;

@@ -60,6 +60,9 @@ class MoeLayer:
         self.y_rows = z(rows, d, dt=torch.float32)
         self.out = z(max(T, 1), d, dt=torch.float32)
         self.out16 = z(max(T, 1), d, dt=t16) if want_out16 else None
+        # the stages either side (MoeDims.norm_* / residual): set by load() when the inputs carry them
+        self.norm_w = self.xn = self.residual = None
+        self.norm_eps = 0.0
 
     # -- inputs ---------------------------------------------------------------
     def load(self, inputs: dict) -> "MoeLayer":
@@ -93,6 +96,15 @@ class MoeLayer:
                            for k in ("sg", "su", "sd")]
         if inputs.get("bias") is not None:
             self.bias = torch.from_numpy(inputs["bias"]).to(self.device)
+        if inputs.get("norm_w") is not None:       # pre-MoE RMSNorm of x (gamma [d], 16-bit)
+            self.norm_w = torch.empty(self.cfg.d_model, dtype=self.x.dtype, device=self.device)
+            put(self.norm_w, inputs["norm_w"])
+            self.norm_eps = float(inputs.get("norm_eps", 1e-6))
+            self.xn = torch.empty_like(self.x)
+        if inputs.get("residual") is not None:     # added to every output row in the combine
+            self.residual = torch.empty_like(self.x)
+            if self.cfg.T > 0:
+                put(self.residual, inputs["residual"])
         return self
 
     # -- call -----------------------------------------------------------------
@@ -165,9 +177,14 @@ class MoeLayer:
         w4 = tuple(t.data_ptr() for t in self.w4sz) if self.cfg.w4 else ()
         w4 = w4 + (None,) * (6 - len(w4))
         g4 = tuple(t.data_ptr() for t in self.fp4g) if self.cfg.nvfp4 else (None,) * 3
-        return self.cfg.dims(None if self.bias is None else self.bias.data_ptr(),
-                             None if self.out16 is None else self.out16.data_ptr(), w_scales=ws, w4=w4,
-                             fp4_global=g4)
+        dm = self.cfg.dims(None if self.bias is None else self.bias.data_ptr(),
+                           None if self.out16 is None else self.out16.data_ptr(), w_scales=ws, w4=w4,
+                           fp4_global=g4)
+        if self.norm_w is not None:
+            dm.norm_weight, dm.norm_eps, dm.norm_out = self.norm_w.data_ptr(), self.norm_eps, self.xn.data_ptr()
+        if self.residual is not None:
+            dm.residual = self.residual.data_ptr()
+        return dm
 
     def forward(self, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
         """Enqueues one layer call on `stream` (default: torch's current stream)."""

@@ -542,3 +542,55 @@ def test_fp8pt_weight_cast_is_the_reference_cast():
     v = inp["wu"].view(np.float16).astype(np.float32).reshape(-1)[:4096]
     enc = np.array([L.oracle_e4m3(float(t)) for t in v], np.uint8)
     assert np.array_equal(enc, inp["wu_q"].reshape(-1)[:4096])
+
+
+@pytest.mark.parametrize("bf16", [False, True])
+def test_rmsnorm_oracle_matches_numpy_restatement(bf16):
+    """Pre-MoE RMSNorm order: lane-strided 8-element chunks with fmaf, xor
+    butterfly, r = sqrt(ss / d + eps), xn = round16((x * g) / r)."""
+    rng = np.random.default_rng(5)
+    d, T = 512, 3
+    v = rng.standard_normal((T, d)).astype(np.float32)
+    gv = (1 + 0.1 * rng.standard_normal(d)).astype(np.float32)
+    to16 = (lambda a: (a.view(np.uint32) >> 16).astype(np.uint16)) if bf16 else \
+        (lambda a: a.astype(np.float16).view(np.uint16))
+    x, g = to16(v), to16(gv)
+    out = O.rmsnorm(x, g, 1e-5, bf16)
+    f = (lambda u: (u.astype(np.uint32) << 16).view(np.float32)) if bf16 else \
+        (lambda u: u.view(np.float16).astype(np.float32))
+    xf, gf = f(x), f(g)
+    for t in range(T):
+        p = []
+        for lane in range(32):
+            acc = np.float32(0)
+            for c in range(lane, d // 8, 32):
+                for j in range(8 * c, 8 * c + 8):
+                    acc = np.float32(np.float64(acc) + np.float64(xf[t, j]) * np.float64(xf[t, j]))
+            p.append(acc)
+        for off in (16, 8, 4, 2, 1):
+            p = [np.float32(p[i] + p[i ^ off]) for i in range(32)]
+        r = np.float32(np.sqrt(np.float32(np.float32(p[0] / np.float32(d)) + np.float32(1e-5))))
+        q = ((xf[t] * gf) / r).astype(np.float32)
+        if bf16:   # round to nearest even
+            u = q.view(np.uint32).astype(np.uint64)
+            ref = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+        else:
+            ref = q.astype(np.float16).view(np.uint16)
+        assert np.array_equal(out[t], ref)
+
+
+def test_residual_starts_the_combine():
+    """With a residual the combine is ((r + w0*y0) + w1*y1) ...; a zero
+    residual leaves the output unchanged and a residual without kept routes
+    is copied through."""
+    cfg = sm.LayerConfig(1, 16, 256, 256, 8, 2, 0.5)
+    inp = sm.make_inputs(cfg, 2)
+    base = O.forward(inp, cfg, nthreads=2)["out"]
+    zero = O.forward({**inp, "residual": np.zeros_like(inp["x"])}, cfg, nthreads=2)["out"]
+    assert np.array_equal(base, zero)
+    with_r = O.forward({**inp, "residual": inp["x"]}, cfg, nthreads=2)
+    xr = inp["x"].view(np.float16).astype(np.float32)
+    dropped = [t for t in range(cfg.T) if (with_r["route_slot"][t * 2:(t + 1) * 2] < 0).all()]
+    for t in dropped:
+        assert np.array_equal(with_r["out"][t], xr[t])
+    np.testing.assert_allclose(with_r["out"], base + xr, rtol=1e-6, atol=1e-6)
