@@ -633,6 +633,10 @@ def run_ep(args, cfg, ws, rank, local, dev):
                 "expert_ffn_compute": ffn_ms,
                 "combine_tail": statistics.mean(tm["combine"][-1].elapsed_time(tm["end"][0]) for tm in timings)}
     phase_ms["exposed_exchange"] = ms_local - phase_ms["route"] - ffn_ms - phase_ms["combine_tail"]
+    phase_ms["expert_ffn_compute_slowest_rank"] = max_over_ranks(ffn_ms, ws, dev)
+    if timings[0].get("dispatch"):    # peer transport: the gather into the owners, part of the exchange
+        phase_ms["dispatch_gather"] = statistics.mean(tm["dispatch"][0].elapsed_time(tm["dispatch"][1])
+                                                      for tm in timings)
     layer.sync_check(stream)
     # end-to-end: host x in, 16-bit output out, per step
     x_host = torch.empty_like(layer.x, device="cpu").pin_memory()

@@ -465,8 +465,10 @@ class ExpertParallelLayer:
                               int(self.placement == "strided"), ctypes.c_void_p(self.plan.data_ptr()), sp))
         rows = (ctypes.c_void_p * P)(*self.peer_maps["recv_x"])
         scales = (ctypes.c_void_p * P)(*self.peer_maps["recv_scale"]) if self.n_scale else None
+        ev("dispatch")
         check(lib.moe_stage_dispatch_peer(ctypes.byref(ch.ra), ctypes.byref(ch.dims),
                                           ctypes.c_void_p(self.plan.data_ptr()), rows, scales, P, sp))
+        ev("dispatch")
         self._barrier(S)
         ev("ffn")
         fa = self._ffn_args(ch)
@@ -494,7 +496,8 @@ class ExpertParallelLayer:
 
     def forward(self, stream=None, timing=None):
         """One layer call.  `timing` (optional dict) receives torch.cuda.Event
-        lists: 'start', 'routed', 'ffn' (pairs per chunk), 'combine', 'end'."""
+        lists: 'start', 'routed', 'ffn' (pairs per chunk), 'combine', 'end'
+        (and, peer transport, 'dispatch': the peer gather's start and end)."""
         torch = self.torch
         if self.watch is not None:
             self.watch.step()      # raises PeerLost before anything of this call is enqueued
