@@ -35,10 +35,9 @@ STAGES = ["router_topk", "dispatch", "expert_up_gate_gemm", "expert_down_gemm", 
 def kernels_per_step(cfg) -> int:
     """Kernels one layer call launches: router (+ the block fold / top-k pass of
     the many-expert routers, E >= 64), dispatch x4 (count, scan, assign,
-    gather), up/gate GEMM, down GEMM, combine (+ three weight unpacks for the
-    reference's packed-transposed int4 format)."""
+    gather), up/gate GEMM, down GEMM, combine."""
     blocked = cfg.num_experts >= 64 and cfg.num_experts % 32 == 0
-    return 8 + (1 if blocked else 0) + (3 if getattr(cfg, "int4ptx", False) else 0)
+    return 8 + (1 if blocked else 0)
 
 
 # workloads whose batches are split over the ranks under expert parallelism (global CAP)

@@ -44,7 +44,8 @@ extern "C" {
                                // router; x and h quantised per tensor to int4 values rn(clamp(v/s, -7, 7)),
                                // kept one per byte in per_expert_wmma_inputs_int8 and
                                // hidden_mlp_layer_1_out_int8; s32 accumulate; the MoEArgs scales.
-                               // The library unpacks the weights into its scratch every call.
+                               // The GEMMs read the packed weights as they are (nibbles are
+                               // sign-extended in shared memory).
 #define MOE_DTYPE_FP8 8        // the reference's fp8 format (kernels/capacity_fp8_ptx.cu:98-220,330-395,
                                // 566-670; inputs/data.cu:142-150): e4m3 weights in the MoEArgs *_fp8
                                // fields with per-tensor scales (the builder's are 1.0); f16 x and router;

@@ -111,9 +111,7 @@ struct Fmt16 {
     static __device__ __forceinline__ float down_value(uint32_t r, const GemmParams&) { return __uint_as_float(r); }
 };
 
-// Per-tensor int8 (kQMax 127, lower clamp -128: capacity_int8_ptx.cu) and the
-// reference's int4 format (kQMax 7, clamp [-7, 7]: capacity_int4_ptx.cu:446-486,
-// int4 values held one per byte so the same kind::i8 MMA is exact).
+// Per-tensor int8 (capacity_int8_ptx.cu): clamp [-128, 127].
 template <int kQMax>
 struct FmtI8T {
     static constexpr int kElemBytes = 1;
@@ -123,7 +121,7 @@ struct FmtI8T {
     static __device__ __forceinline__ void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t id, uint32_t acc) {
         mma_i8_ss(d, a, b, id, acc);
     }
-    // capacity_int8_ptx.cu:465-474 / capacity_int4_ptx.cu:470-477: dequant, SiLU(gate)*up, requant.
+    // capacity_int8_ptx.cu:465-474: dequant, SiLU(gate)*up, requant.
     static __device__ __forceinline__ void swiglu_store(const uint32_t (&g)[32], const uint32_t (&u)[32],
                                                         const GemmParams& p, void* dst, bool valid) {
         uint32_t packed[8];
@@ -154,7 +152,6 @@ struct FmtI8T {
     }
 };
 using FmtI8 = FmtI8T<127>;
-using FmtI4 = FmtI8T<7>;
 
 // The reference's per-tensor fp8 format (capacity_fp8_ptx.cu:362-395, :566-600):
 // e4m3 x e4m3 with f32 accumulation (kind::f8f6f4); up*s_in*s_up and
@@ -457,7 +454,6 @@ FmtDesc fmt_desc(int dtype) {
     switch (dtype) {
         case MOE_DTYPE_BF16: return {CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 64, 64};
         case MOE_DTYPE_INT8:
-        case MOE_DTYPE_INT4_PTX:
         case MOE_DTYPE_FP8: return {CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, 128, 128};
         default: return {CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, 64, 64};
     }
@@ -524,9 +520,6 @@ cudaError_t launch_expert_up_gate(const void* a_rows, const void* w_gate, const 
         case MOE_DTYPE_INT8:
             p.idesc = idesc_i8(kBM, kUmmaN, true);
             return launch_gemm<0, FmtI8>(ta, tg, tu, p, st, num_sms);
-        case MOE_DTYPE_INT4_PTX:
-            p.idesc = idesc_i8(kBM, kUmmaN, true);
-            return launch_gemm<0, FmtI4>(ta, tg, tu, p, st, num_sms);
         case MOE_DTYPE_FP8:
             p.idesc = idesc_e4m3(kBM, kUmmaN, true);
             return launch_gemm<0, FmtE4>(ta, tg, tu, p, st, num_sms);
@@ -555,7 +548,6 @@ cudaError_t launch_expert_down(const void* h_rows, const void* w_down, const Sha
     p.out = y_rows;
     switch (s.dtype) {
         case MOE_DTYPE_INT8:
-        case MOE_DTYPE_INT4_PTX:   // the down epilogue of the two is the same
             p.idesc = idesc_i8(kBM, kUmmaN, true);
             return launch_gemm<1, FmtI8>(th, td, td, p, st, num_sms);
         case MOE_DTYPE_FP8:

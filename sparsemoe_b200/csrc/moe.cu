@@ -81,17 +81,12 @@ size_t router_scratch_bytes(const Shape& s) {
     return router_blocked(s) ? align256(sizeof(float) * nb * (size_t)s.T() * s.E) : 0;
 }
 
-// INT4_PTX: int8 copies of the three packed weight matrices.
-size_t unpacked_weight_bytes(const Shape& s) {
-    return s.dtype == MOE_DTYPE_INT4_PTX ? 3 * align256((size_t)s.E * s.d * s.f) : 0;
-}
-
 size_t workspace_bytes(const Shape& s) {
     const size_t routes = (size_t)s.T() * s.k;
     const size_t chunk_tab = (size_t)s.B * s.chunks() * s.E;
     return workspace_header_bytes() + align256(sizeof(int) * routes) + 2 * align256(sizeof(int) * chunk_tab) +
            align256(sizeof(int) * (size_t)s.B * s.E) + 2 * align256(sizeof(int) * s.E) + scale_bytes(s, s.d) +
-           scale_bytes(s, s.f) + router_scratch_bytes(s) + unpacked_weight_bytes(s);
+           scale_bytes(s, s.f) + router_scratch_bytes(s);
 }
 
 void carve_workspace(void* base, const Shape& s, Workspace* ws) {
@@ -115,8 +110,6 @@ void carve_workspace(void* base, const Shape& s, Workspace* ws) {
     ws->h_scale = scale_bytes(s, s.f) ? reinterpret_cast<float*>(p) : nullptr;
     p += scale_bytes(s, s.f);
     ws->router_logits = router_scratch_bytes(s) ? reinterpret_cast<float*>(p) : nullptr;
-    p += router_scratch_bytes(s);
-    ws->w_unpacked = unpacked_weight_bytes(s) ? reinterpret_cast<int8_t*>(p) : nullptr;
 }
 
 namespace {
@@ -387,7 +380,7 @@ FfnBuffers ffn_buffers(const MoEArgs* a, const Shape& s) {
         return b;
     }
     if (s.dtype == MOE_DTYPE_INT4_PTX) {
-        // int4 values one per byte; the weights are unpacked into the scratch by enqueue_ffn
+        // int4 values one per byte; the packed weights go to the GEMM as they are
         b.a_rows = (void*)a->per_expert_wmma_inputs_int8;
         b.h_rows = (void*)a->hidden_mlp_layer_1_out_int8;
         b.wg = a->expert_gate_proj_weights_int4;
@@ -469,26 +462,17 @@ int enqueue_route(const MoEArgs* a_in, const MoeDims* dims, const Shape& s, cons
 
 // Stage 4: the two grouped GEMMs over the row groups `gt`.
 int enqueue_ffn(const MoEArgs* a, const MoeDims* dims, const Shape& s, const GroupTable& gt, int* status,
-                float* a_scale, float* h_scale, int num_sms, cudaStream_t stream, int8_t* w_unpacked = nullptr) {
-    FfnBuffers fb = ffn_buffers(a, s);
+                float* a_scale, float* h_scale, int num_sms, cudaStream_t stream) {
+    const FfnBuffers fb = ffn_buffers(a, s);
     if (s.dtype == MOE_DTYPE_INT4_PTX) {
-        if (!w_unpacked) {
-            set_error("the int4 (packed-transposed) format runs through moe_solve_v2 / solve only");
-            return MOE_ERR_UNSUPPORTED;
-        }
-        const size_t per = align256((size_t)s.E * s.d * s.f);
-        int8_t* ug = w_unpacked;
-        int8_t* uu = w_unpacked + per;
-        int8_t* ud = w_unpacked + 2 * per;
-        MOE_TRY(launch_unpack_int4_ptx(static_cast<const uint8_t*>(fb.wg), s.E, s.d, s.f, gt.rows, ug, stream),
-                "int4 weight unpack (gate)");
-        MOE_TRY(launch_unpack_int4_ptx(static_cast<const uint8_t*>(fb.wu), s.E, s.d, s.f, gt.rows, uu, stream),
-                "int4 weight unpack (up)");
-        MOE_TRY(launch_unpack_int4_ptx(static_cast<const uint8_t*>(fb.wd), s.E, s.f, s.d, gt.rows, ud, stream),
-                "int4 weight unpack (down)");
-        fb.wg = ug;
-        fb.wu = uu;
-        fb.wd = ud;
+        // the packed-transposed nibbles are unpacked inside the GEMM (expert_gemm_i4.cu)
+        const GemmScales sc = scales_of(a, s);
+        MOE_TRY(launch_i4_up_gate(fb.a_rows, fb.wg, fb.wu, s, gt, status, sc, fb.h_rows, stream, num_sms),
+                "int4 up/gate GEMM");
+        MOE_TRY(mark_stage(3, stream), "cudaEventRecord(stage event)");
+        MOE_TRY(launch_i4_down(fb.h_rows, fb.wd, s, gt, status, sc, a->hidden_mlp_layer_2_out, stream, num_sms),
+                "int4 down GEMM");
+        return MOE_OK;
     }
     if (s.dtype == MOE_DTYPE_W4A16) {
         MOE_TRY(launch_w4_up_gate(fb.a_rows, fb.wg, fb.wu, dims->w4_scale_gate, dims->w4_scale_up,
@@ -550,7 +534,7 @@ int enqueue_layer(const MoEArgs* a, const MoeDims* dims, const Shape& s, const W
     MOE_TRY(mark_stage(2, stream), "cudaEventRecord(stage event)");
     if (s.T() > 0 && s.cap > 0) {
         const GroupTable gt{ws.expert_rows, ws.expert_start, nullptr, s.E, s.rows_capacity()};
-        rc = enqueue_ffn(a, dims, s, gt, ws.status, ws.a_scale, ws.h_scale, num_sms, stream, ws.w_unpacked);
+        rc = enqueue_ffn(a, dims, s, gt, ws.status, ws.a_scale, ws.h_scale, num_sms, stream);
         if (rc != MOE_OK) return rc;
     } else {
         MOE_TRY(mark_stage(3, stream), "cudaEventRecord(stage event)");

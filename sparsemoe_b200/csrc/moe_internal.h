@@ -58,8 +58,6 @@ struct Workspace {
     float* a_scale;     // FP8: [E*B*CAP, d/128] activation block scales; INT8_CHANNEL: [E*B*CAP] row scales
     float* h_scale;     // FP8 / INT8_CHANNEL: [E*B*CAP, f/128] h block scales
     float* router_logits;  // [ceil(d/512), T, E] per-block partial logits of the many-expert routers
-    int8_t* w_unpacked;    // INT4_PTX: the three weight matrices unpacked to int8, gate/up [E, d, f],
-                           // down [E, f, d] (row-major, the layout the int8 GEMM reads)
 };
 size_t workspace_header_bytes();
 
@@ -154,12 +152,14 @@ cudaError_t launch_i8c_down(const void* h_rows, const float* h_scale, const void
 // (nothing arrives) and records kDevErrTimeout in *status.
 cudaError_t launch_wait_selftest(int* status, uint64_t timeout_ns, cudaStream_t st);
 
-// repack.cu: the reference's packed-transposed int4 weights (per expert
-// [N/2][K] bytes, columns 2p / 2p+1 in the low / high nibble of byte (p, k),
-// inputs/data.cu:89-140) -> int8 row-major [E, K, N]; experts whose
-// expert_rows entry (device [E], optional) is 0 are skipped.
-cudaError_t launch_unpack_int4_ptx(const uint8_t* packed, int E, int K, int N, const int* expert_rows, int8_t* out,
-                                   cudaStream_t st);
+// expert_gemm_i4.cu: the reference's packed-transposed int4 format (int4
+// values in int8 A rows, weights as packed pairs [E * N/2, K] bytes), exact
+// kind::i8 MMAs on nibbles sign-extended in shared memory.
+cudaError_t launch_i4_up_gate(const void* a_rows, const void* w_gate, const void* w_up, const Shape& s,
+                              const GroupTable& gt, int* status, const GemmScales& sc, void* h_rows, cudaStream_t st,
+                              int num_sms);
+cudaError_t launch_i4_down(const void* h_rows, const void* w_down, const Shape& s, const GroupTable& gt, int* status,
+                           const GemmScales& sc, float* y_rows, cudaStream_t st, int num_sms);
 
 // expert_gemm_w4.cu: 4-bit weights dequantised to bf16 in shared memory.
 cudaError_t launch_w4_up_gate(const void* a_rows, const void* w_gate, const void* w_up, const void* s_gate,
