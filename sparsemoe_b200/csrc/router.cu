@@ -309,22 +309,38 @@ __global__ void __launch_bounds__(MT == 8 ? 256 : 512) router_tiled_kernel(
 // bit of b, the left operand first; the remaining stack is folded from the
 // top, each entry added on the left), + bias, then top-k + softmax.
 constexpr int kFoldMaxLevels = 8;   // nb <= 255 blocks (d <= 130560)
-__global__ void __launch_bounds__(256) fold_topk_kernel(const float* __restrict__ part, int nb, int64_t T, int E,
+constexpr int kFoldUnrolled = 32;   // d <= 16384: every partial of an expert loaded before the fold
+__global__ void __launch_bounds__(128) fold_topk_kernel(const float* __restrict__ part, int nb, int64_t T, int E,
                                                        int k, const float* __restrict__ bias,
                                                        float* __restrict__ logits, int* __restrict__ idx,
                                                        float* __restrict__ wts) {
-    __shared__ float rows[8][256];
+    __shared__ float rows[4][256];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t t = (int64_t)blockIdx.x * 8 + warp;
+    const int64_t t = (int64_t)blockIdx.x * 4 + warp;
     if (t >= T) return;
     float* row = rows[warp];
     for (int e = lane; e < E; e += 32) {
         float st[kFoldMaxLevels];
         int top = 0;
-        for (int b = 0; b < nb; ++b) {
-            float v = part[((int64_t)b * T + t) * E + e];
-            for (int i = b; i & 1; i >>= 1) v = st[--top] + v;
-            st[top++] = v;
+        if (nb <= kFoldUnrolled) {
+            // all of this expert's partials in flight at once, then the fold
+            float pv[kFoldUnrolled];
+#pragma unroll
+            for (int b = 0; b < kFoldUnrolled; ++b)
+                if (b < nb) pv[b] = __ldg(part + ((int64_t)b * T + t) * E + e);
+#pragma unroll
+            for (int b = 0; b < kFoldUnrolled; ++b) {
+                if (b >= nb) break;
+                float v = pv[b];
+                for (int i = b; i & 1; i >>= 1) v = st[--top] + v;
+                st[top++] = v;
+            }
+        } else {
+            for (int b = 0; b < nb; ++b) {
+                float v = part[((int64_t)b * T + t) * E + e];
+                for (int i = b; i & 1; i >>= 1) v = st[--top] + v;
+                st[top++] = v;
+            }
         }
         float v = st[--top];
         while (top > 0) v = st[--top] + v;
@@ -352,7 +368,7 @@ cudaError_t launch_blocked(const void* x, const void* wr, const float* bias, con
     if (err != cudaSuccess) return err;
     const dim3 grid((unsigned)((s.T() + kTiledTM - 1) / kTiledTM), nb, s.E / EC);
     kern<<<grid, 2 * EC, smem, st>>>((const TX*)x, (const TW*)wr, s.T(), s.d, s.E, part);
-    fold_topk_kernel<<<(unsigned)((s.T() + 7) / 8), 256, 0, st>>>(part, nb, s.T(), s.E, s.k, bias, logits, idx, w);
+    fold_topk_kernel<<<(unsigned)((s.T() + 3) / 4), 128, 0, st>>>(part, nb, s.T(), s.E, s.k, bias, logits, idx, w);
     return cudaGetLastError();
 }
 
