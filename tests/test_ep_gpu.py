@@ -1,8 +1,9 @@
 """Expert parallelism on real GPUs (NCCL): each rank routes its own tokens,
 sends rows (and, for the dynamically quantised formats, their row scales) to
 the experts' owners, runs its E/P experts, gets the rows back and combines.
-Must equal the single-GPU layer on the same tokens bit for bit.  Needs >= 2
-GPUs; runs as child processes, one per GPU, with NVLS off."""
+Must equal the single-GPU layer on the same tokens bit for bit, and match the
+CPU oracle (routing bit-exact, the format's bar).  Needs >= 2 GPUs; runs as
+child processes, one per GPU, with NVLS off."""
 import os
 
 import numpy as np
@@ -35,6 +36,7 @@ def _worker(rank, world, port, case, results):
         ep = ExpertParallelLayer(cfg, f"cuda:{rank}", global_batch=True, transport=transport,
                                  placement=placement).load({**full, "x": x})
         single = sm.MoeLayer(full_cfg, f"cuda:{rank}").load(full)
+        single_inputs = full
         rows = np.concatenate([np.arange(b * N * world + rank * N, b * N * world + (rank + 1) * N)
                                for b in range(B)])
     else:
@@ -45,6 +47,7 @@ def _worker(rank, world, port, case, results):
         ep = ExpertParallelLayer(cfg, f"cuda:{rank}", chunks=chunks, transport=transport,
                                  placement=placement).load(inputs)
         single = sm.MoeLayer(cfg, f"cuda:{rank}").load(inputs)
+        single_inputs = inputs
         rows = np.arange(cfg.T)
     ep.forward()
     ep.sync_check()
@@ -55,8 +58,15 @@ def _worker(rank, world, port, case, results):
     a = ep.out.cpu().numpy()[: cfg.T]
     b = single.out.cpu().numpy()[rows]
     idx_equal = bool(np.array_equal(ep.idx.cpu().numpy()[: cfg.T], single.idx.cpu().numpy()[rows]))
+    # and against the CPU oracle on the same tokens (this rank's rows of the single-GPU problem)
+    from oracle import oracle as O
+    sc = single.cfg
+    ref = O.forward(single_inputs, sc)
+    oracle_idx = bool(np.array_equal(ep.idx.cpu().numpy()[: cfg.T], ref["idx"][rows]))
+    tol = {sm.DTYPE_F16: 1e-2, sm.DTYPE_BF16: 1e-2, sm.DTYPE_W4A16: 6e-2, sm.DTYPE_NVFP4: 6e-2}.get(dtype, 3e-2)
+    oracle_err = float(np.abs(a - ref["out"][rows]).max() / max(np.abs(ref["out"][rows]).max(), 1e-30))
     results[rank] = (bool(np.array_equal(a, b)), float(np.abs(a - b).max() / max(np.abs(b).max(), 1e-30)),
-                     idx_equal)
+                     idx_equal, oracle_idx and oracle_err <= tol)
     ep.close()
     dist.destroy_process_group()
 
@@ -100,9 +110,10 @@ def test_ep_matches_single_gpu(gpu, name):
         mp.spawn(_worker, args=(world, port, case, results), nprocs=world, join=True)
         res = dict(results)
     assert len(res) == world
-    for rank, (equal, err, idx_equal) in res.items():
+    for rank, (equal, err, idx_equal, oracle_ok) in res.items():
         assert idx_equal, f"rank {rank}: routing differs"
         assert err < 1e-6, f"rank {rank}: max-abs-rel {err}"
+        assert oracle_ok, f"rank {rank}: differs from the CPU oracle"
 
 
 
