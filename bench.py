@@ -466,6 +466,61 @@ def cpu_measure(layer, sample_tokens: int, nthreads: int):
     return oracle_measure(layer.host_inputs, layer.cfg, layer.cap, sample_tokens, nthreads)
 
 
+# other BASELINE configs measured after the headline line (one GPU, device time)
+OTHER_CONFIGS = ("small_fp16,int8_cfg3,int8ch_cfg3,fp8_cfg4,w4_cfg5_prefill,nvfp4_cfg5_prefill,w4_cfg5_decode,"
+                 "ds3_int4_decode")
+
+
+def measure_other_configs(names, dev, stream, steps: int = 5, warmup: int = 3) -> dict:
+    """Device-time of one layer call for each named workload (seeded inputs as
+    the headline line; warm-up calls, then `steps` timed calls bracketed by
+    CUDA events on the launching stream), with the per-stage split and the
+    dominant GEMM's fraction of the measured tensor peak.  A config that fails
+    is reported with its error instead of a time."""
+    import torch
+    import sparsemoe_b200 as sm
+    peaks, _ = load_peaks()
+    out = {}
+    for name in names:
+        try:
+            cfg = workload(name)
+            layer = sm.MoeLayer(cfg, dev, want_logits=True, want_out16=True)
+            device_inputs(layer, seed=1000)
+            for _ in range(warmup):
+                layer.forward(stream)
+            layer.sync_check(stream)
+            kept = int(layer.counts.sum().item())
+            evs = [[torch.cuda.Event(enable_timing=True) for _ in range(6)] for _ in range(steps)]
+            for row in evs:
+                for e in row:
+                    e.record(stream)
+            torch.cuda.synchronize(dev)
+            t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            t0.record(stream)
+            for i in range(steps):
+                arr = (ctypes.c_void_p * 6)(*[e.cuda_event for e in evs[i]])
+                sm.lib.moe_set_stage_events(arr, 6)
+                layer.forward(stream)
+            t1.record(stream)
+            sm.lib.moe_set_stage_events(None, 0)
+            torch.cuda.synchronize(dev)
+            layer.sync_check(stream)
+            ms = t0.elapsed_time(t1) / steps
+            stages = {st: statistics.mean(evs[i][j].elapsed_time(evs[i][j + 1]) for i in range(steps))
+                      for j, st in enumerate(STAGES)}
+            eight = cfg.int8 or cfg.int8ch or cfg.fp8 or cfg.int4ptx or cfg.fp8pt
+            burst, _sus = tensor_peaks(peaks, eight)
+            flop_up = 4.0 * cfg.d_model * cfg.d_ff * kept
+            out[name] = {"ms_per_step": ms, "tokens_per_s": cfg.T / (ms * 1e-3), "stages_ms": stages,
+                         "dtype": dtype_name(cfg), "kept_routes": kept,
+                         "up_gate_frac_of_tensor_burst": flop_up / (stages["expert_up_gate_gemm"] * 1e-3) / 1e12 / burst}
+            del layer
+            torch.cuda.empty_cache()
+        except Exception as e:   # noqa: BLE001 (report and go on to the next config)
+            out[name] = {"error": f"{type(e).__name__}: {e}"}
+    return out
+
+
 def run_reference_arm(args, ws, rank, local):
     """`--impl reference`: the reference has no CPU implementation and its GPU
     kernels are not this arm; the CPU transcription of its five stages (oracle/)
@@ -717,6 +772,9 @@ def main():
     ap.add_argument("--cpu-sample-tokens", type=int, default=1024)
     ap.add_argument("--ref-sample-tokens", type=int, default=512)
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline measurement")
+    ap.add_argument("--also", default=None,
+                    help="comma-separated workloads measured after the headline (one GPU); default: the other "
+                         "BASELINE configs for the default workload, none otherwise ('' for none)")
     ap.add_argument("--graph", action="store_true",
                     help="also time the layer captured as one CUDA graph (the decode path)")
     ap.add_argument("--parallel", default="auto", choices=["auto", "ep", "replicas"],
@@ -726,6 +784,8 @@ def main():
                     help="EP rows over NVLink peer memory (copy engines + down-GEMM epilogue stores) or NCCL all-to-all")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.also is None:
+        args.also = OTHER_CONFIGS if args.config == "mixtral_bf16" else ""
 
     ws, rank, local = init_dist()
     if args.impl == "reference":
@@ -882,6 +942,10 @@ def main():
             "value": v, "unit": "tokens/s", "cores": nthreads, "kind": "port",
             "sample": f"oracle: routing of all {cfg.T} tokens ({t_route:.2f} s, scaled by S/T) + expert "
                       f"FFN/combine of S={S} tokens ({t_ffn:.2f} s)"}
+    if ws == 1 and args.also:
+        del layer
+        torch.cuda.empty_cache()
+        result["other_configs"] = measure_other_configs(args.also.split(","), dev, stream)
     if rank == 0:
         print(json.dumps(result))
     if ws > 1:
