@@ -694,7 +694,7 @@ extern "C" {
 // FP8 block-scaled path: x (bf16) quantised per 1x128
 // block (s = amax/448, 1 if zero), weights e4m3 with scales per 128x128 block;
 // per K block: P = sum of e4m3 products (f32), acc = fmaf(P, s_a*s_w, acc);
-// h = u * g/(1+exp(-g)), quantised per 1x128 block of f the same way; the down
+// h = u * g/(1+exp(-g)), quantised per 1x128 block of f as e4m3(h * (1/s)); the down
 // GEMM likewise with the h scales; then the route-order combine.
 //   wq: [E, K, N] e4m3 codes; ws: [E, K/128, N/128] f32 scales.
 void oracle_ffn_combine_fp8(const uint16_t* x, const uint8_t* wg, const uint8_t* wu, const uint8_t* wd,
@@ -715,13 +715,17 @@ void oracle_ffn_combine_fp8(const uint16_t* x, const uint8_t* wg, const uint8_t*
     std::vector<Item> items;
     for (int e = 0; e < E; ++e)
         for (int r = 0; r < (int)routes[e].size(); ++r) items.push_back({e, r});
-    auto quant_row = [&](const float* v, int n, float* qv, float* sc) {
+    // x blocks are quantised as v / s (the dispatch gather), h blocks as
+    // v * (1 / s) (the up/gate epilogue: one division per block)
+    auto quant_row = [&](const float* v, int n, float* qv, float* sc, bool by_reciprocal) {
         for (int b = 0; b < n / 128; ++b) {
             float m = 0.0f;
             for (int i = 0; i < 128; ++i) m = fmaxf(m, fabsf(v[b * 128 + i]));
             const float s = m > 0.0f ? m / 448.0f : 1.0f;
+            const float inv = 1.0f / s;
             sc[b] = s;
-            for (int i = 0; i < 128; ++i) qv[b * 128 + i] = dec[f32_to_e4m3(v[b * 128 + i] / s)];
+            for (int i = 0; i < 128; ++i)
+                qv[b * 128 + i] = dec[f32_to_e4m3(by_reciprocal ? v[b * 128 + i] * inv : v[b * 128 + i] / s)];
         }
     };
     parallel_for((int64_t)items.size(), nthreads, [&](int64_t it) {
@@ -731,7 +735,7 @@ void oracle_ffn_combine_fp8(const uint16_t* x, const uint8_t* wg, const uint8_t*
         std::vector<float> xv(d), qa(d), sa(dk), g(f, 0.0f), u(f, 0.0f), p(f), pu(f), h(f), qh(f), sh(fk),
             acc(d, 0.0f), pd(d);
         for (int j = 0; j < d; ++j) xv[j] = bf16_to_f32(x[tok * d + j]);
-        quant_row(xv.data(), d, qa.data(), sa.data());
+        quant_row(xv.data(), d, qa.data(), sa.data(), false);
         const uint8_t* Wg = wg + (size_t)e * d * f;
         const uint8_t* Wu = wu + (size_t)e * d * f;
         const uint8_t* Wd = wd + (size_t)e * f * d;
@@ -754,7 +758,7 @@ void oracle_ffn_combine_fp8(const uint16_t* x, const uint8_t* wg, const uint8_t*
             }
         }
         for (int c = 0; c < f; ++c) h[c] = u[c] * (g[c] / (1.0f + expf(-g[c])));
-        quant_row(h.data(), f, qh.data(), sh.data());
+        quant_row(h.data(), f, qh.data(), sh.data(), true);
         for (int kb = 0; kb < fk; ++kb) {
             std::fill(pd.begin(), pd.end(), 0.0f);
             for (int j = kb * 128; j < kb * 128 + 128; ++j) {
@@ -788,7 +792,7 @@ void oracle_ffn_combine_fp8(const uint16_t* x, const uint8_t* wg, const uint8_t*
 // s_x = amax/127 (1 if zero), q = clamp(rn(x/s_x), +-127); weights int8 with
 // one scale per output column; G, U = exact s32 sums over all of K, then
 // g = (float)G * (s_x * s_g[c]) (same for u); h = u * g/(1+exp(-g)) quantised
-// per 128-feature block, s_h = amax/127; the down GEMM promotes each 128-wide K
+// per 128-feature block, s_h = amax/127, q = clamp(rn(h * (1/s_h)), +-127); the down GEMM promotes each 128-wide K
 // block: acc = fmaf((float)P_kb, s_h[kb], acc), and y = acc * s_d[c]; then the
 // route-order combine.   wq: [E, K, N] int8; ws: [E, N] f32.
 void oracle_ffn_combine_int8ch(const uint16_t* x, const int8_t* wg, const int8_t* wu, const int8_t* wd,
@@ -840,7 +844,8 @@ void oracle_ffn_combine_int8ch(const uint16_t* x, const int8_t* wg, const int8_t
             float hm = 0.0f;
             for (int i = 0; i < 128; ++i) hm = fmaxf(hm, fabsf(h[b * 128 + i]));
             sh[b] = hm > 0.0f ? hm / 127.0f : 1.0f;
-            for (int i = 0; i < 128; ++i) qh[b * 128 + i] = q8(h[b * 128 + i] / sh[b]);
+            const float inv = 1.0f / sh[b];   // h * (1/s), as the up/gate epilogue
+            for (int i = 0; i < 128; ++i) qh[b * 128 + i] = q8(h[b * 128 + i] * inv);
         }
         for (int kb = 0; kb < fk; ++kb) {
             std::fill(P.begin(), P.end(), 0);

@@ -9,24 +9,26 @@
 // the epilogue warps into register accumulators with one packed f32x2 FMA per
 // two columns: acc += P_kb * (s_a * s_w).
 //
-// Warp roles (384 threads = 3 warpgroups, one persistent CTA per SM):
+// Warp roles (640 threads = 5 warpgroups, one persistent CTA per SM):
 //   warp 0      TMA producer: A 128 rows x 128 B (one K block, K-major, 128B
 //               swizzle) + B 128 K-rows x 256 columns from the row-major
-//               [K, N] e4m3 weights (MN-major, 128B swizzle); 4-stage ring.
+//               [K, N] e4m3 weights (MN-major, 128B swizzle); 3-stage ring.
 //   warp 1      MMA issuer: per K block 4 x tcgen05.mma kind::f8f6f4 M128
 //               N256 K32 into TMEM partial P[kb & 1].
 //   warps 2-3   idle (they complete warpgroup 0, which hands its registers
 //               to the promotion warpgroups through setmaxnreg).
-//   warps 4-11  promotion + epilogue: warp w reads TMEM lanes 32*(w%4).. and
-//               half (w-4)/4 of the columns, four 16-column TMEM loads in
-//               flight per wait (232 registers per thread: 128 accumulators
-//               plus 64 loaded values):
-//                 up/gate: gate cols [64h, 64h+64) and up cols 128+[64h, ..)
-//                 of the same 64 output features, so SwiGLU is local; the h
+//   warps 4-19  promotion + epilogue, four per SM sub-partition so that one
+//               warp's TMEM-load latency hides behind the others' FMAs: warp
+//               w reads TMEM lanes 32*(w%4).. and quarter (w-4)/4 of the
+//               columns, one 32-column TMEM load in flight per wait (112
+//               registers per thread: 64 accumulators plus 32 loaded values):
+//                 up/gate: gate cols [32qt, 32qt+32) and up cols 128+[32qt, ..)
+//                 of the same 32 output features, so SwiGLU is local; the
 //                 row block of 128 features (the tile) gets its 1x128 scale
-//                 from the two halves' amax (exchanged through shared
-//                 memory) and is written as e4m3 plus its f32 scale;
-//                 down: cols [128h, 128h+128), written as f32 rows of Y.
+//                 from the four quarters' amax (exchanged through shared
+//                 memory) and is written as e4m3(h * (1/s)) plus its f32
+//                 scale s (SiLU as g * fast-reciprocal(1 + e^-g));
+//                 down: cols [64qt, 64qt+64), written as f32 rows of Y.
 // Quantisation (host weights, device activations and h) rounds x / s to the
 // nearest e4m3, saturating at +-448.
 //
@@ -58,16 +60,20 @@ namespace {
 using namespace sm100;
 
 constexpr int kBM = 128;
-constexpr int kStages = 4;
-// 12 warps = 3 warpgroups: warpgroup 0 (TMA, MMA, two idle warps) gives up
-// registers with setmaxnreg, the promotion warpgroups 1-2 take them (40 + 2 x
-// 232 = 3 x 168 registers per thread, the launch's total), so that a
-// promotion thread holds its 128 accumulators plus 4 TMEM loads in flight.
-constexpr int kThreads = 384;
-constexpr int kPromoWarps = 8;
+constexpr int kStages = 3;
+// 20 warps = 5 warpgroups: warpgroup 0 (TMA, MMA, two idle warps) gives up
+// registers with setmaxnreg, the four promotion warpgroups take them.  The
+// launch holds 96 registers per thread (65536 / 640 rounded down to the
+// allocation unit of 8); the split must not exceed that total, or the
+// setmaxnreg.inc would wait forever -- the host checks the compiled count
+// before the first launch.
+constexpr int kThreads = 640;
+constexpr int kPromoWarps = 16;
 constexpr int kPromoWarp0 = 4;
-constexpr int kRegsCtrl = 40, kRegsPromo = 232;
-static_assert(kRegsCtrl + 2 * kRegsPromo == 3 * 168, "register split must match the launch total");
+constexpr int kRegsLaunch = 96;
+constexpr int kRegsCtrl = 32, kRegsPromo = 112;
+static_assert(kRegsCtrl * 128 + kRegsPromo * 128 * (kPromoWarps / 4) <= kRegsLaunch * kThreads,
+              "register split must fit the launch total");
 constexpr int kABytes = kBM * 128;
 constexpr int kBBytes = 128 * 256;
 constexpr int kStageBytes = kABytes + kBBytes;
@@ -131,7 +137,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __shared__ int s_rows[kMaxGroups];
     __shared__ int s_start[kMaxGroups];
     __shared__ int s_wt[kMaxGroups];
-    __shared__ float s_amax[2][kBM];
+    __shared__ float s_amax[4][kBM];
 
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sA = smem;
@@ -245,12 +251,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         }   // warps 2, 3: idle
     } else {
         asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsPromo));
-        // ---------------- promotion + epilogue (warps 4..11) ----------------
+        // ---------------- promotion + epilogue (warps 4..19) ----------------
         const int q = warp & 3;
-        const int half = (warp - kPromoWarp0) >> 2;
+        const int qt = (warp - kPromoWarp0) >> 2;   // column quarter
         const int row_in_tile = q * 32 + lane;
         const int nkb = kblocks;
         const int nblk = p.out_ld / 128;
+        // TMEM column of round rnd (32 columns each): up/gate reads 32 gate
+        // then the same 32 features' up columns; down reads 64 adjacent columns
+        auto rcol = [&](int rnd) { return kMode == 0 ? 128 * rnd + 32 * qt : 64 * qt + 32 * rnd; };
         int pb = 0;
         uint32_t pph = 0;
         for (int t = blockIdx.x; t < total; t += gridDim.x) {
@@ -262,38 +271,37 @@ __global__ void __launch_bounds__(kThreads, 1)
             // rows past the group's end read the group's first row's (finite) scales; never stored
             const float* arow = p.a_scale + (valid ? row : (int64_t)s_start[g]) * nkb;
             const int wexp = s_wt[g];
-            float acc[128];
+            float acc[64];
 #pragma unroll
-            for (int i = 0; i < 128; ++i) acc[i] = 0.0f;
+            for (int i = 0; i < 64; ++i) acc[i] = 0.0f;
             bool ok = true;
             // scales of K block kb+1 are loaded while block kb is promoted
             auto wscale = [&](const float* base, int kb, int col) {
                 return base[((int64_t)wexp * nkb + kb) * nblk + col];
             };
-            const int wcol = kMode == 0 ? n : 2 * n + half;
+            const int wcol = kMode == 0 ? n : 2 * n + (qt >> 1);
             if (kKind == 1 && kMode == 0) {
                 // int8 up/gate: one s32 accumulator, scaled by s_x[r] * s_w[n]
                 const float sx = p.a_scale[valid ? row : (int64_t)s_start[g]];
-                const float* sg = p.w_scale0 + (int64_t)wexp * p.out_ld + n * 128 + 64 * half;
-                const float* su = p.w_scale1 + (int64_t)wexp * p.out_ld + n * 128 + 64 * half;
+                const float* sg = p.w_scale0 + (int64_t)wexp * p.out_ld + n * 128 + 32 * qt;
+                const float* su = p.w_scale1 + (int64_t)wexp * p.out_ld + n * 128 + 32 * qt;
                 if (!mbar_wait_warp(&pfull[pb], pph, p.status, kDevErrTimeout)) break;
                 tc_fence_after();
                 const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + pb * 256;
 #pragma unroll
-                for (int piece = 0; piece < 8; ++piece) {
-                    uint32_t r[16];
-                    const int col = piece < 4 ? 64 * half + 16 * piece : 128 + 64 * half + 16 * (piece - 4);
-                    tmem_ld_32x32b_x16(tbase + col, r);
+                for (int rnd = 0; rnd < 2; ++rnd) {
+                    uint32_t r[32];
+                    tmem_ld_32x32b_x32(tbase + rcol(rnd), r);
                     tmem_wait_ld();
-                    if (piece == 7) { tc_fence_before(); mbar_arrive(&pempty[pb]); }
-                    const float4* ws4 = reinterpret_cast<const float4*>((piece < 4 ? sg : su) + 16 * (piece & 3));
+                    if (rnd == 1) { tc_fence_before(); mbar_arrive(&pempty[pb]); }
+                    const float4* ws4 = reinterpret_cast<const float4*>(rnd == 0 ? sg : su);
 #pragma unroll
-                    for (int v = 0; v < 4; ++v) {
+                    for (int v = 0; v < 8; ++v) {
                         const float4 w4 = __ldg(ws4 + v);
-                        acc[16 * piece + 4 * v + 0] = (float)(int)r[4 * v + 0] * (sx * w4.x);
-                        acc[16 * piece + 4 * v + 1] = (float)(int)r[4 * v + 1] * (sx * w4.y);
-                        acc[16 * piece + 4 * v + 2] = (float)(int)r[4 * v + 2] * (sx * w4.z);
-                        acc[16 * piece + 4 * v + 3] = (float)(int)r[4 * v + 3] * (sx * w4.w);
+                        acc[32 * rnd + 4 * v + 0] = (float)(int)r[4 * v + 0] * (sx * w4.x);
+                        acc[32 * rnd + 4 * v + 1] = (float)(int)r[4 * v + 1] * (sx * w4.y);
+                        acc[32 * rnd + 4 * v + 2] = (float)(int)r[4 * v + 2] * (sx * w4.z);
+                        acc[32 * rnd + 4 * v + 3] = (float)(int)r[4 * v + 3] * (sx * w4.w);
                     }
                 }
                 pb ^= 1;
@@ -315,28 +323,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tc_fence_after();
                     const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + pb * 256;
                     const float sc0 = sa * sw0, sc1 = sa * sw1;
-                    // two rounds of four 16-column TMEM loads in flight, one wait each
-                    auto pcol = [&](int piece) {
-                        return kMode == 0 ? (piece < 4 ? 64 * half + 16 * piece : 128 + 64 * half + 16 * (piece - 4))
-                                          : 128 * half + 16 * piece;
-                    };
 #pragma unroll
                     for (int rnd = 0; rnd < 2; ++rnd) {
-                        uint32_t r4[4][16];
-#pragma unroll
-                        for (int k4 = 0; k4 < 4; ++k4) tmem_ld_32x32b_x16(tbase + pcol(4 * rnd + k4), r4[k4]);
+                        uint32_t r[32];
+                        tmem_ld_32x32b_x32(tbase + rcol(rnd), r);
                         tmem_wait_ld();
                         if (rnd == 1) { tc_fence_before(); mbar_arrive(&pempty[pb]); }
                         const float sc = (kMode == 0 && rnd == 1) ? sc1 : sc0;
 #pragma unroll
-                        for (int k4 = 0; k4 < 4; ++k4) {
-                            const int piece = 4 * rnd + k4;
-#pragma unroll
-                            for (int i = 0; i < 16; i += 2) {
-                                const float p0 = kKind == 0 ? __uint_as_float(r4[k4][i]) : (float)(int)r4[k4][i];
-                                const float p1 = kKind == 0 ? __uint_as_float(r4[k4][i + 1]) : (float)(int)r4[k4][i + 1];
-                                ffma2(acc[16 * piece + i], acc[16 * piece + i + 1], p0, p1, sc);
-                            }
+                        for (int i = 0; i < 32; i += 2) {
+                            const float p0 = kKind == 0 ? __uint_as_float(r[i]) : (float)(int)r[i];
+                            const float p1 = kKind == 0 ? __uint_as_float(r[i + 1]) : (float)(int)r[i + 1];
+                            ffma2(acc[32 * rnd + i], acc[32 * rnd + i + 1], p0, p1, sc);
                         }
                     }
                     pb ^= 1;
@@ -347,40 +345,42 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (kMode == 0) {
                 float amax = 0.0f;
 #pragma unroll
-                for (int i = 0; i < 64; ++i) {
-                    const float gv = acc[i], uv = acc[64 + i];
-                    const float h = uv * (gv / (1.0f + __expf(-gv)));
+                for (int i = 0; i < 32; ++i) {
+                    const float gv = acc[i], uv = acc[32 + i];
+                    const float h = uv * __fdividef(gv, 1.0f + __expf(-gv));
                     acc[i] = h;
                     amax = fmaxf(amax, fabsf(h));
                 }
-                // the 1x128 block of h = both halves of this row
-                asm volatile("bar.sync %0, 64;" ::"r"(1 + q) : "memory");
-                s_amax[half][row_in_tile] = amax;
-                asm volatile("bar.sync %0, 64;" ::"r"(1 + q) : "memory");
-                const float bmax = fmaxf(s_amax[0][row_in_tile], s_amax[1][row_in_tile]);
+                // the 1x128 block of h = the four quarters of this row
+                asm volatile("bar.sync %0, 128;" ::"r"(1 + q) : "memory");
+                s_amax[qt][row_in_tile] = amax;
+                asm volatile("bar.sync %0, 128;" ::"r"(1 + q) : "memory");
+                const float bmax = fmaxf(fmaxf(s_amax[0][row_in_tile], s_amax[1][row_in_tile]),
+                                         fmaxf(s_amax[2][row_in_tile], s_amax[3][row_in_tile]));
                 const float sh = bmax > 0.0f ? bmax / (kKind == 0 ? 448.0f : 127.0f) : 1.0f;
+                const float inv = 1.0f / sh;   // q = rn(h * (1/s)): one division per row, not per element
                 if (valid) {
-                    uint8_t* h8 = reinterpret_cast<uint8_t*>(p.out) + row * p.out_ld + n * 128 + 64 * half;
+                    uint8_t* h8 = reinterpret_cast<uint8_t*>(p.out) + row * p.out_ld + n * 128 + 32 * qt;
                     uint4* o = reinterpret_cast<uint4*>(h8);
 #pragma unroll
-                    for (int v = 0; v < 4; ++v) {
+                    for (int v = 0; v < 2; ++v) {
                         uint32_t w4[4];
 #pragma unroll
                         for (int j = 0; j < 4; ++j) {
                             const int i = 16 * v + 4 * j;
-                            w4[j] = kKind == 0 ? e4m3x4(acc[i] / sh, acc[i + 1] / sh, acc[i + 2] / sh, acc[i + 3] / sh)
-                                               : s8x4(acc[i] / sh, acc[i + 1] / sh, acc[i + 2] / sh, acc[i + 3] / sh);
+                            w4[j] = kKind == 0 ? e4m3x4(acc[i] * inv, acc[i + 1] * inv, acc[i + 2] * inv, acc[i + 3] * inv)
+                                               : s8x4(acc[i] * inv, acc[i + 1] * inv, acc[i + 2] * inv, acc[i + 3] * inv);
                         }
                         o[v] = make_uint4(w4[0], w4[1], w4[2], w4[3]);
                     }
-                    if (half == 0) p.out_scale[row * nblk + n] = sh;
+                    if (qt == 0) p.out_scale[row * nblk + n] = sh;
                 }
             } else {
                 if (kKind == 1) {
                     const float4* wd = reinterpret_cast<const float4*>(p.w_scale0 + (int64_t)wexp * p.out_ld +
-                                                                       n * 256 + 128 * half);
+                                                                       n * 256 + 64 * qt);
 #pragma unroll
-                    for (int v = 0; v < 32; ++v) {
+                    for (int v = 0; v < 16; ++v) {
                         const float4 w4 = __ldg(wd + v);
                         acc[4 * v] *= w4.x;
                         acc[4 * v + 1] *= w4.y;
@@ -388,14 +388,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                         acc[4 * v + 3] *= w4.w;
                     }
                 }
-                // this warp's 32 rows x 128 columns, coalesced through shared memory
+                // this warp's 32 rows x 64 columns, coalesced through shared memory
                 const int warp_row0 = m * kBM + q * 32;
                 const int nrows = s_rows[g] - warp_row0;
                 float* y = down_rows(p.red, reinterpret_cast<float*>(p.out), g, s_start[g], p.out_ld) +
-                           (int64_t)warp_row0 * p.out_ld + n * 256 + 128 * half;
+                           (int64_t)warp_row0 * p.out_ld + n * 256 + 64 * qt;
                 float4* stage = sStage + (warp - kPromoWarp0) * 128;
 #pragma unroll
-                for (int c = 0; c < 8; ++c) warp_store_rows16(stage, acc + 16 * c, y + 16 * c, p.out_ld, nrows, lane);
+                for (int c = 0; c < 4; ++c) warp_store_rows16(stage, acc + 16 * c, y + 16 * c, p.out_ld, nrows, lane);
             }
         }
         if (kMode == 1 && p.red.rank) __threadfence_system();   // peer rows visible before the kernel ends
@@ -414,6 +414,16 @@ cudaError_t launch(const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMa
     static SmemAttr attr;
     cudaError_t err = ensure_smem(kern, kSmemBytes, attr);
     if (err != cudaSuccess) return err;
+    // the setmaxnreg split draws on the registers the launch holds; a build
+    // that compiled to fewer would make the promotion warps wait forever
+    static int regs = -1;
+    if (regs < 0) {
+        cudaFuncAttributes fa{};
+        err = cudaFuncGetAttributes(&fa, kern);
+        if (err != cudaSuccess) return err;
+        regs = fa.numRegs;
+    }
+    if (regs < kRegsLaunch) return cudaErrorInvalidConfiguration;
     kern<<<num_sms, kThreads, kSmemBytes, st>>>(a, b0, b1, p);
     return cudaGetLastError();
 }
