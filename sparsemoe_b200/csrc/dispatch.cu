@@ -14,15 +14,17 @@
 //   assign  grid (chunks, B): warp-aggregated ranking (__match_any_sync +
 //                             popc), in-order prefix across warps, writes the
 //                             slot tables (token ids / weights / route slots)
-//   gather  one warp per capacity slot: copies the slot's token row into the
-//                             expert's compact block with 16-byte vector
-//                             loads/stores (HBM-bound: R_kept*d*2 B read and
-//                             written).
+//   scatter one warp per token: reads the token's row once (quantising it
+//                             for the 8-bit formats) and writes it to the
+//                             compact-block row of each kept route with
+//                             16-byte vector stores (HBM-bound: T*d*2 B read,
+//                             R_kept*d*s_a B written).
 // Dense expert-major row layout: expert e's kept rows start at
 // expert_start[e] = sum of the kept rows of experts < e; within it batch b's
 // slots start at row_base[b,e].  Row of (b, e, slot) = expert_start[e] +
 // row_base[b,e] + slot.
 #include "moe_internal.h"
+#include <algorithm>
 #include <cstdint>
 #include <cuda_fp16.h>
 #include <cuda_bf16.h>
@@ -164,37 +166,81 @@ __global__ void __launch_bounds__(kThreads) dispatch_assign_kernel(
     }
 }
 
-// One warp per capacity slot (b, e, s) in [B, E, CAP] order; slots past the
-// expert's count are skipped.
-__global__ void __launch_bounds__(kThreads) dispatch_gather_kernel(
-    const uint4* __restrict__ x, const int* __restrict__ counts, const int* __restrict__ token_ids,
-    const int* __restrict__ row_base, const int* __restrict__ expert_start, int N, int E, int B, int cap,
-    int vec_per_row, const GatherDst gd) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t slot_lin = (int64_t)blockIdx.x * kWarps + warp;
-    if (slot_lin >= (int64_t)B * E * cap) return;
-    const int be = (int)(slot_lin / cap);
-    const int s = (int)(slot_lin - (int64_t)be * cap);
-    if (s >= counts[be]) return;
-    const int b = be / E, e = be - b * E;
-    const int64_t t = token_ids[slot_lin];
-    const uint4* src = x + ((int64_t)b * N + t) * vec_per_row;
+// The row copy ("gather" of the reference, assign_per_expert_wmma_inputs)
+// runs token-major: one warp per token (b, t) reads the token's row once,
+// quantises it once (every format's row quantisation depends on the token
+// alone) and writes it to the destination row of each of its kept routes, so
+// x is read once instead of once per route (k times).  Lane l < k holds
+// route l's destination (row, peer); -1 = dropped.
+struct RouteDst {
+    int64_t row;
     int q;
-    const int64_t row = gather_row(gd, expert_start, row_base, e, be, s, q);
-    uint4* dst = static_cast<uint4*>(gd.rows[q]) + row * vec_per_row;
-    int v = lane;
-    for (; v + 96 < vec_per_row; v += 128) {
-        const uint4 a0 = __ldg(src + v), a1 = __ldg(src + v + 32), a2 = __ldg(src + v + 64),
-                    a3 = __ldg(src + v + 96);
-        dst[v] = a0;
-        dst[v + 32] = a1;
-        dst[v + 64] = a2;
-        dst[v + 96] = a3;
+};
+__device__ __forceinline__ RouteDst route_dst(const int* __restrict__ idx, const int* __restrict__ route_slot,
+                                              const int* row_base, const int* expert_start, const GatherDst& gd,
+                                              int E, int k, int64_t r0, int b, int lane) {
+    RouteDst d{-1, 0};
+    if (lane < k) {
+        const int slot = route_slot[r0 + lane];
+        if (slot >= 0) {
+            const int e = idx[r0 + lane];
+            d.row = gather_row(gd, expert_start, row_base, e, b * E + e, slot, d.q);
+        }
     }
-    for (; v < vec_per_row; v += 32) dst[v] = __ldg(src + v);
+    return d;
 }
 
-// The per-tensor formats: the slot's f16 token row quantised with the MoEArgs
+// Warp w handles part w % split of token w / split's row (split > 1 only when
+// there are too few tokens to fill the GPU, e.g. decode batches).
+__device__ __forceinline__ bool token_of_warp(int N, int B, int split, int64_t& bt, int& b, int& part) {
+    const int64_t w = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
+    if (w >= (int64_t)B * N * split) return false;
+    bt = w / split;
+    part = (int)(w - bt * split);
+    b = (int)(bt / N);
+    return true;
+}
+// [begin, end) of part `part` of n units, cut in multiples of `unit`.
+__device__ __forceinline__ void part_range(int n, int unit, int split, int part, int& begin, int& end) {
+    const int per = (n + split * unit - 1) / (split * unit) * unit;
+    begin = min(n, part * per);
+    end = min(n, begin + per);
+}
+
+// 16-bit rows: a plain copy, 4 x 16 B per lane in flight.
+__global__ void __launch_bounds__(kThreads) dispatch_scatter_kernel(
+    const uint4* __restrict__ x, const int* __restrict__ idx, const int* __restrict__ route_slot,
+    const int* __restrict__ row_base, const int* __restrict__ expert_start, int N, int E, int B, int k,
+    int vec_per_row, int split, const GatherDst gd) {
+    const int lane = threadIdx.x & 31;
+    int64_t bt;
+    int b, part, vb, ve;
+    if (!token_of_warp(N, B, split, bt, b, part)) return;
+    const RouteDst my = route_dst(idx, route_slot, row_base, expert_start, gd, E, k, bt * k, b, lane);
+    if (!__any_sync(0xffffffffu, my.row >= 0)) return;
+    part_range(vec_per_row, 128, split, part, vb, ve);
+    const uint4* src = x + bt * vec_per_row;
+    for (int v0 = vb; v0 < ve; v0 += 128) {
+        uint4 a[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int v = v0 + 32 * i + lane;
+            if (v < ve) a[i] = __ldg(src + v);
+        }
+        for (int l = 0; l < k; ++l) {
+            const int64_t row = __shfl_sync(0xffffffffu, my.row, l);
+            if (row < 0) continue;
+            uint4* dst = static_cast<uint4*>(gd.rows[__shfl_sync(0xffffffffu, my.q, l)]) + row * vec_per_row;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int v = v0 + 32 * i + lane;
+                if (v < ve) dst[v] = a[i];
+            }
+        }
+    }
+}
+
+// The per-tensor formats: the token's f16 row quantised with the MoEArgs
 // scale s_in, 8 values per 16-byte load, one byte each:
 //   kQ = 0  int8  rn(clamp(x / s_in, -128, 127))  (reference capacity_int8_ptx.cu:391-432)
 //   kQ = 1  int4  rn(clamp(x / s_in, -7, 7))      (capacity_int4_ptx.cu:396-441; kept one value per
@@ -213,63 +259,74 @@ __device__ __forceinline__ uint32_t quant_pair(float a, float b, float s_in) {
 }
 
 template <int kQ>
-__global__ void __launch_bounds__(kThreads) dispatch_gather_q8_kernel(
-    const uint4* __restrict__ x, const int* __restrict__ counts, const int* __restrict__ token_ids,
-    const int* __restrict__ row_base, const int* __restrict__ expert_start, int N, int E, int B, int cap,
-    int vec_per_row, float s_in, const GatherDst gd) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t slot_lin = (int64_t)blockIdx.x * kWarps + warp;
-    if (slot_lin >= (int64_t)B * E * cap) return;
-    const int be = (int)(slot_lin / cap);
-    const int s = (int)(slot_lin - (int64_t)be * cap);
-    if (s >= counts[be]) return;
-    const int b = be / E, e = be - b * E;
-    const int64_t t = token_ids[slot_lin];
-    const uint4* src = x + ((int64_t)b * N + t) * vec_per_row;
-    int q;
-    const int64_t row = gather_row(gd, expert_start, row_base, e, be, s, q);
-    uint2* dst = static_cast<uint2*>(gd.rows[q]) + row * vec_per_row;
-    for (int v = lane; v < vec_per_row; v += 32) {
-        const uint4 raw = __ldg(src + v);
-        const __half2* h2 = reinterpret_cast<const __half2*>(&raw);
-        uint32_t w[2] = {0u, 0u};
+__global__ void __launch_bounds__(kThreads) dispatch_scatter_q8_kernel(
+    const uint4* __restrict__ x, const int* __restrict__ idx, const int* __restrict__ route_slot,
+    const int* __restrict__ row_base, const int* __restrict__ expert_start, int N, int E, int B, int k,
+    int vec_per_row, int split, float s_in, const GatherDst gd) {
+    const int lane = threadIdx.x & 31;
+    int64_t bt;
+    int b, part, vb, ve;
+    if (!token_of_warp(N, B, split, bt, b, part)) return;
+    const RouteDst my = route_dst(idx, route_slot, row_base, expert_start, gd, E, k, bt * k, b, lane);
+    if (!__any_sync(0xffffffffu, my.row >= 0)) return;
+    part_range(vec_per_row, 64, split, part, vb, ve);
+    const uint4* src = x + bt * vec_per_row;
+    for (int v0 = vb; v0 < ve; v0 += 64) {
+        uint2 w[2];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            const float2 f = __half22float2(h2[q]);
-            w[q >> 1] |= quant_pair<kQ>(f.x, f.y, s_in) << (16 * (q & 1));
+        for (int i = 0; i < 2; ++i) {
+            const int v = v0 + 32 * i + lane;
+            w[i] = make_uint2(0u, 0u);
+            if (v < ve) {
+                const uint4 raw = __ldg(src + v);
+                const __half2* h2 = reinterpret_cast<const __half2*>(&raw);
+                uint32_t p[2] = {0u, 0u};
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const float2 f = __half22float2(h2[j]);
+                    p[j >> 1] |= quant_pair<kQ>(f.x, f.y, s_in) << (16 * (j & 1));
+                }
+                w[i] = make_uint2(p[0], p[1]);
+            }
         }
-        dst[v] = make_uint2(w[0], w[1]);
+        for (int l = 0; l < k; ++l) {
+            const int64_t row = __shfl_sync(0xffffffffu, my.row, l);
+            if (row < 0) continue;
+            uint2* dst = static_cast<uint2*>(gd.rows[__shfl_sync(0xffffffffu, my.q, l)]) + row * vec_per_row;
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+                const int v = v0 + 32 * i + lane;
+                if (v < ve) dst[v] = w[i];
+            }
+        }
     }
 }
 
-// FP8 block path: the slot's bf16 token row quantised per 1x128 block,
+// FP8 block path: the token's bf16 row quantised per 1x128 block,
 // s = amax / 448 (1 for an all-zero block), q = e4m3(x / s) (nearest even,
 // saturating); lane l handles elements 4l..4l+3 of each block.
-__global__ void __launch_bounds__(kThreads) dispatch_gather_fp8_kernel(
-    const __nv_bfloat16* __restrict__ x, const int* __restrict__ counts, const int* __restrict__ token_ids,
-    const int* __restrict__ row_base, const int* __restrict__ expert_start, int N, int E, int B, int cap, int d,
-    const GatherDst gd) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t slot_lin = (int64_t)blockIdx.x * kWarps + warp;
-    if (slot_lin >= (int64_t)B * E * cap) return;
-    const int be = (int)(slot_lin / cap);
-    const int s = (int)(slot_lin - (int64_t)be * cap);
-    if (s >= counts[be]) return;
-    const int b = be / E, e = be - b * E;
-    const int64_t t = token_ids[slot_lin];
-    const __nv_bfloat16* src = x + ((int64_t)b * N + t) * d;
-    int q;
-    const int64_t row = gather_row(gd, expert_start, row_base, e, be, s, q);
-    uint8_t* dst = static_cast<uint8_t*>(gd.rows[q]) + row * d;
-    float* a_scale = gd.scales[q];
+__global__ void __launch_bounds__(kThreads) dispatch_scatter_fp8_kernel(
+    const __nv_bfloat16* __restrict__ x, const int* __restrict__ idx, const int* __restrict__ route_slot,
+    const int* __restrict__ row_base, const int* __restrict__ expert_start, int N, int E, int B, int k, int d,
+    int split, const GatherDst gd) {
+    const int lane = threadIdx.x & 31;
+    int64_t bt;
+    int b, part, kb0, kb1;
+    if (!token_of_warp(N, B, split, bt, b, part)) return;
+    const RouteDst my = route_dst(idx, route_slot, row_base, expert_start, gd, E, k, bt * k, b, lane);
+    if (!__any_sync(0xffffffffu, my.row >= 0)) return;
+    const __nv_bfloat16* src = x + bt * d;
     const int nblk = d / 128;   // a multiple of 2 (d % 256 == 0)
+    part_range(nblk, 8, split, part, kb0, kb1);
     // 8 blocks' loads in flight per round (lane: 4 elements of each block)
-    for (int b0 = 0; b0 < nblk; b0 += 8) {
-        const int nb = min(8, nblk - b0);
+    for (int b0 = kb0; b0 < kb1; b0 += 8) {
+        const int nb = min(8, kb1 - b0);
         uint2 raw[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i)
             if (i < nb) raw[i] = __ldg(reinterpret_cast<const uint2*>(src + (b0 + i) * 128) + lane);
+        uint32_t code[8];
+        float scale[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             if (i >= nb) break;
@@ -283,30 +340,46 @@ __global__ void __launch_bounds__(kThreads) dispatch_gather_fp8_kernel(
                 __nv_cvt_float2_to_fp8x2(make_float2(v0.x / sc, v0.y / sc), __NV_SATFINITE, __NV_E4M3);
             const uint32_t hi =
                 __nv_cvt_float2_to_fp8x2(make_float2(v1.x / sc, v1.y / sc), __NV_SATFINITE, __NV_E4M3);
-            reinterpret_cast<uint32_t*>(dst + (b0 + i) * 128)[lane] = lo | (hi << 16);
-            if (lane == 0) a_scale[row * nblk + b0 + i] = sc;
+            code[i] = lo | (hi << 16);
+            scale[i] = sc;
+        }
+        for (int l = 0; l < k; ++l) {
+            const int64_t row = __shfl_sync(0xffffffffu, my.row, l);
+            if (row < 0) continue;
+            const int q = __shfl_sync(0xffffffffu, my.q, l);
+            uint8_t* dst = static_cast<uint8_t*>(gd.rows[q]) + row * d;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                if (i >= nb) break;
+                reinterpret_cast<uint32_t*>(dst + (b0 + i) * 128)[lane] = code[i];
+            }
+            // lane i writes block b0+i's scale
+            if (lane < nb) {
+                float sc = scale[0];
+#pragma unroll
+                for (int i = 1; i < 8; ++i)
+                    if (lane == i) sc = scale[i];
+                gd.scales[q][row * nblk + b0 + lane] = sc;
+            }
         }
     }
 }
 
-// INT8_CHANNEL gather: the row is quantised per token, s = amax / 127 (1 for a
-// zero row), q = clamp(rn(x / s), -127, 127).  Pass 1 reduces amax over the
-// row, pass 2 re-reads it (L1/L2 hits) and writes 8 int8 per 16-byte load.
-__global__ void __launch_bounds__(kThreads) dispatch_gather_q8tok_kernel(
-    const uint4* __restrict__ x, const int* __restrict__ counts, const int* __restrict__ token_ids,
-    const int* __restrict__ row_base, const int* __restrict__ expert_start, int N, int E, int B, int cap, int vecs,
+// INT8_CHANNEL: the row is quantised per token, s = amax / 127 (1 for a zero
+// row), q = clamp(rn(x / s), -127, 127).  Pass 1 reduces amax over the row,
+// pass 2 re-reads it (L1/L2 hits) and writes 8 int8 per 16-byte load to
+// every kept route's row.
+__global__ void __launch_bounds__(kThreads) dispatch_scatter_q8tok_kernel(
+    const uint4* __restrict__ x, const int* __restrict__ idx, const int* __restrict__ route_slot,
+    const int* __restrict__ row_base, const int* __restrict__ expert_start, int N, int E, int B, int k, int vecs,
     const GatherDst gd) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t slot_lin = (int64_t)blockIdx.x * kWarps + warp;
-    if (slot_lin >= (int64_t)B * E * cap) return;
-    const int be = (int)(slot_lin / cap);
-    const int s = (int)(slot_lin - (int64_t)be * cap);
-    if (s >= counts[be]) return;
-    const int b = be / E, e = be - b * E;
-    const int64_t t = token_ids[slot_lin];
-    const uint4* src = x + ((int64_t)b * N + t) * vecs;
-    int q;
-    const int64_t row = gather_row(gd, expert_start, row_base, e, be, s, q);
+    const int lane = threadIdx.x & 31;
+    int64_t bt;
+    int b, part;
+    if (!token_of_warp(N, B, 1, bt, b, part)) return;
+    const RouteDst my = route_dst(idx, route_slot, row_base, expert_start, gd, E, k, bt * k, b, lane);
+    if (!__any_sync(0xffffffffu, my.row >= 0)) return;
+    const uint4* src = x + bt * vecs;
     float amax = 0.0f;
     for (int v = lane; v < vecs; v += 32) {
         const uint4 raw = __ldg(src + v);
@@ -320,7 +393,6 @@ __global__ void __launch_bounds__(kThreads) dispatch_gather_q8tok_kernel(
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
     const float sc = amax > 0.0f ? amax / 127.0f : 1.0f;
-    uint2* dst = static_cast<uint2*>(gd.rows[q]) + row * vecs;
     for (int v = lane; v < vecs; v += 32) {
         const uint4 raw = __ldg(src + v);
         const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
@@ -332,9 +404,14 @@ __global__ void __launch_bounds__(kThreads) dispatch_gather_q8tok_kernel(
             const int q1 = max(-127, min(127, __float2int_rn(f.y / sc)));
             w[i >> 1] |= ((uint32_t)(q0 & 0xff) | ((uint32_t)(q1 & 0xff) << 8)) << (16 * (i & 1));
         }
-        dst[v] = make_uint2(w[0], w[1]);
+        for (int l = 0; l < k; ++l) {
+            const int64_t row = __shfl_sync(0xffffffffu, my.row, l);
+            if (row < 0) continue;
+            uint2* dst = static_cast<uint2*>(gd.rows[__shfl_sync(0xffffffffu, my.q, l)]) + row * vecs;
+            dst[v] = make_uint2(w[0], w[1]);
+        }
     }
-    if (lane == 0) gd.scales[q][row] = sc;
+    if (lane < k && my.row >= 0) gd.scales[my.q][my.row] = sc;
 }
 
 // Expert-parallel plan of rank `me` from the kept-row table [P, E] (one CTA).
@@ -420,37 +497,52 @@ cudaError_t launch_dispatch_finish(const void* x, const int* idx, const float* w
     dispatch_assign_kernel<<<grid, kThreads, 0, st>>>(idx, w, s.N, s.k, s.E, s.cap, s.chunks(), ws.chunk_base,
                                                       slot_base, token_ids, token_weights, ws.route_slot);
     return skip_gather ? cudaGetLastError()
-                       : launch_dispatch_gather(x, s, ws, sc, counts, token_ids, GatherDst{{a_rows}, {ws.a_scale}}, st);
+                       : launch_dispatch_gather(x, idx, s, ws, sc, GatherDst{{a_rows}, {ws.a_scale}}, st);
 }
 
-// The gather alone: every kept slot's token row (quantised for the 8-bit
-// formats) into its destination row.
-cudaError_t launch_dispatch_gather(const void* x, const Shape& s, const Workspace& ws, const GemmScales& sc,
-                                   const int* counts, const int* token_ids, const GatherDst& gd, cudaStream_t st) {
+// The row copy alone: every kept route's token row (quantised for the 8-bit
+// formats) into its destination row; needs the route slots of the assign.
+cudaError_t launch_dispatch_gather(const void* x, const int* idx, const Shape& s, const Workspace& ws,
+                                   const GemmScales& sc, const GatherDst& gd, cudaStream_t st) {
     // 16-bit activations: rows of d elements = d/8 16-byte vectors.
-    const int64_t slots = (int64_t)s.B * s.E * s.cap;
-    const unsigned gblocks = (unsigned)((slots + kWarps - 1) / kWarps);
-    if (slots > 0 && s.dtype == MOE_DTYPE_FP8_BLOCK)
-        dispatch_gather_fp8_kernel<<<gblocks, kThreads, 0, st>>>(
-            (const __nv_bfloat16*)x, counts, token_ids, ws.row_base, ws.expert_start, s.N, s.E, s.B, s.cap, s.d, gd);
-    else if (slots > 0 && s.dtype == MOE_DTYPE_INT8_CHANNEL)
-        dispatch_gather_q8tok_kernel<<<gblocks, kThreads, 0, st>>>((const uint4*)x, counts, token_ids, ws.row_base,
-                                                                   ws.expert_start, s.N, s.E, s.B, s.cap, s.d / 8, gd);
-    else if (slots > 0 && s.dtype == MOE_DTYPE_INT8)
-        dispatch_gather_q8_kernel<0><<<gblocks, kThreads, 0, st>>>((const uint4*)x, counts, token_ids, ws.row_base,
-                                                                   ws.expert_start, s.N, s.E, s.B, s.cap, s.d / 8,
-                                                                   sc.s_in, gd);
-    else if (slots > 0 && s.dtype == MOE_DTYPE_INT4_PTX)
-        dispatch_gather_q8_kernel<1><<<gblocks, kThreads, 0, st>>>((const uint4*)x, counts, token_ids, ws.row_base,
-                                                                   ws.expert_start, s.N, s.E, s.B, s.cap, s.d / 8,
-                                                                   sc.s_in, gd);
-    else if (slots > 0 && s.dtype == MOE_DTYPE_FP8)
-        dispatch_gather_q8_kernel<2><<<gblocks, kThreads, 0, st>>>((const uint4*)x, counts, token_ids, ws.row_base,
-                                                                   ws.expert_start, s.N, s.E, s.B, s.cap, s.d / 8,
-                                                                   sc.s_in, gd);
-    else if (slots > 0)
-        dispatch_gather_kernel<<<gblocks, kThreads, 0, st>>>((const uint4*)x, counts, token_ids, ws.row_base,
-                                                             ws.expert_start, s.N, s.E, s.B, s.cap, s.d / 8, gd);
+    const int64_t tokens = (int64_t)s.B * s.N;
+    if (tokens <= 0) return cudaSuccess;
+    // split rows over several warps when the tokens alone leave the GPU
+    // under-filled (32 warps per SM wanted); the per-token INT8 form needs
+    // the whole row in one warp for its amax
+    constexpr int64_t kWantWarps = 148 * 32;
+    auto split_for = [&](int units) {
+        const int64_t want = (kWantWarps + tokens - 1) / tokens;
+        return (int)std::max<int64_t>(1, std::min<int64_t>(want, units));
+    };
+    const int split = s.dtype == MOE_DTYPE_INT8_CHANNEL ? 1
+                      : s.dtype == MOE_DTYPE_FP8_BLOCK  ? split_for((s.d / 128 + 7) / 8)
+                      : (s.dtype == MOE_DTYPE_INT8 || s.dtype == MOE_DTYPE_INT4_PTX || s.dtype == MOE_DTYPE_FP8)
+                          ? split_for((s.d / 8 + 63) / 64)
+                          : split_for((s.d / 8 + 127) / 128);
+    const unsigned blocks = (unsigned)((tokens * split + kWarps - 1) / kWarps);
+    const int* rs = ws.route_slot;
+    if (s.dtype == MOE_DTYPE_FP8_BLOCK)
+        dispatch_scatter_fp8_kernel<<<blocks, kThreads, 0, st>>>((const __nv_bfloat16*)x, idx, rs, ws.row_base,
+                                                                 ws.expert_start, s.N, s.E, s.B, s.k, s.d, split, gd);
+    else if (s.dtype == MOE_DTYPE_INT8_CHANNEL)
+        dispatch_scatter_q8tok_kernel<<<blocks, kThreads, 0, st>>>((const uint4*)x, idx, rs, ws.row_base,
+                                                                   ws.expert_start, s.N, s.E, s.B, s.k, s.d / 8, gd);
+    else if (s.dtype == MOE_DTYPE_INT8)
+        dispatch_scatter_q8_kernel<0><<<blocks, kThreads, 0, st>>>((const uint4*)x, idx, rs, ws.row_base,
+                                                                   ws.expert_start, s.N, s.E, s.B, s.k, s.d / 8,
+                                                                   split, sc.s_in, gd);
+    else if (s.dtype == MOE_DTYPE_INT4_PTX)
+        dispatch_scatter_q8_kernel<1><<<blocks, kThreads, 0, st>>>((const uint4*)x, idx, rs, ws.row_base,
+                                                                   ws.expert_start, s.N, s.E, s.B, s.k, s.d / 8,
+                                                                   split, sc.s_in, gd);
+    else if (s.dtype == MOE_DTYPE_FP8)
+        dispatch_scatter_q8_kernel<2><<<blocks, kThreads, 0, st>>>((const uint4*)x, idx, rs, ws.row_base,
+                                                                   ws.expert_start, s.N, s.E, s.B, s.k, s.d / 8,
+                                                                   split, sc.s_in, gd);
+    else
+        dispatch_scatter_kernel<<<blocks, kThreads, 0, st>>>((const uint4*)x, idx, rs, ws.row_base, ws.expert_start,
+                                                             s.N, s.E, s.B, s.k, s.d / 8, split, gd);
     return cudaGetLastError();
 }
 

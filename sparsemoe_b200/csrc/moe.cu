@@ -777,8 +777,8 @@ extern "C" int moe_stage_dispatch_peer(const MoEArgs* a, const MoeDims* dims, co
     }
     gd.rank = plan;
     gd.row0 = plan + s.E;
-    MOE_TRY(launch_dispatch_gather(routed_args(a, dims).input, s, ws, scales_of(a, s), a->expert_counts,
-                                   a->expert_token_ids, gd, stream),
+    MOE_TRY(launch_dispatch_gather(routed_args(a, dims).input, a->selected_expert_indices, s, ws, scales_of(a, s), gd,
+                                   stream),
             "dispatch (peer gather)");
     return MOE_OK;
 }

@@ -123,8 +123,8 @@ cudaError_t launch_dispatch_finish(const void* x, const int* idx, const float* w
                                    int* token_ids, float* token_weights, void* a_rows, cudaStream_t st,
                                    bool skip_gather);
 cudaError_t launch_ep_plan(const int* table, int P, int E, int me, int strided, int* plan, cudaStream_t st);
-cudaError_t launch_dispatch_gather(const void* x, const Shape& s, const Workspace& ws, const GemmScales& sc,
-                                   const int* counts, const int* token_ids, const GatherDst& gd, cudaStream_t st);
+cudaError_t launch_dispatch_gather(const void* x, const int* idx, const Shape& s, const Workspace& ws,
+                                   const GemmScales& sc, const GatherDst& gd, cudaStream_t st);
 // expert_gemm.cu: grouped tcgen05 GEMMs.
 cudaError_t launch_expert_up_gate(const void* a_rows, const void* w_gate, const void* w_up,
                                   const Shape& s, const GroupTable& gt, int* status, const GemmScales& sc,
