@@ -132,13 +132,88 @@ def load_peaks():
     return FALLBACK_PEAKS, "fallback"
 
 
-def tensor_peaks(peaks, eight_bit: bool):
-    """(burst, sustained) dense tensor TFLOP/s for the roofline: the measured
-    bf16 figures, doubled for the 8-bit kinds."""
+_PEAK8_CACHE: dict = {}
+
+
+def measure_8bit_peak(kind: str, dev=None):
+    """Dense 8-bit tensor TFLOP/s measured here the way the bf16 figures are
+    (a cuBLAS GEMM, M = N = K = 8192): `kind` "e4m3" runs torch._scaled_mm on
+    e4m3 operands, "int8" torch._int_mm.  Returns (burst, sustained, note):
+    burst = best of 10 trials of 10 back-to-back GEMMs, sustained = one ~1 s
+    loop.  Measured once per process; None figures if the library refuses
+    the shape."""
+    if kind in _PEAK8_CACHE:
+        return _PEAK8_CACHE[kind]
+    import torch
+    dev = dev or torch.device("cuda", torch.cuda.current_device())
+    n = 8192
+    g = torch.Generator(device=dev).manual_seed(0)
+    try:
+        if kind == "e4m3":
+            a = torch.randn(n, n, device=dev, generator=g).to(torch.float8_e4m3fn)
+            b = torch.randn(n, n, device=dev, generator=g).to(torch.float8_e4m3fn).t()   # column-major
+            one = torch.ones((), device=dev)
+            op = lambda: torch._scaled_mm(a, b, scale_a=one, scale_b=one, out_dtype=torch.bfloat16)  # noqa: E731
+            what = "cuBLAS e4m3 GEMM (torch._scaled_mm, bf16 out)"
+        else:
+            a = torch.randint(-127, 128, (n, n), device=dev, dtype=torch.int8, generator=g)
+            b = torch.randint(-127, 128, (n, n), device=dev, dtype=torch.int8, generator=g).t()
+            op = lambda: torch._int_mm(a, b)  # noqa: E731
+            what = "cuBLAS int8 GEMM (torch._int_mm, s32 out)"
+        for _ in range(3):
+            op()
+        torch.cuda.synchronize(dev)
+        flop = 2.0 * n ** 3
+        best = 0.0
+        for _ in range(10):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(10):
+                op()
+            e1.record()
+            e1.synchronize()
+            best = max(best, 10 * flop / (e0.elapsed_time(e1) * 1e-3) / 1e12)
+        reps = max(10, int(1.0 / (flop / (best * 1e12))))
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            op()
+        e1.record()
+        e1.synchronize()
+        sus = reps * flop / (e0.elapsed_time(e1) * 1e-3) / 1e12
+        res = (best, sus, f"measured in this process: {what} at {n}^3, burst best of 10 x 10 launches, "
+                          f"sustained one {reps}-launch loop")
+        del a, b
+    except Exception as e:   # noqa: BLE001 (no 8-bit GEMM in this build of the library)
+        res = (None, None, f"8-bit GEMM not measurable here ({type(e).__name__}: {str(e)[:80]})")
+    _PEAK8_CACHE[kind] = res
+    return res
+
+
+def eight_bit_kind(cfg):
+    """The tensor-core kind an 8-bit format runs on: "e4m3" (kind::f8f6f4) or
+    "int8" (kind::i8); None for the 16-bit MMAs."""
+    if cfg.fp8 or cfg.fp8pt:
+        return "e4m3"
+    if cfg.int8 or cfg.int8ch or cfg.int4ptx:
+        return "int8"
+    return None
+
+
+def tensor_peaks(peaks, eight_bit, dev=None):
+    """(burst, sustained, note) dense tensor TFLOP/s for the roofline: the
+    driver-measured bf16 figures for the 16-bit MMAs; for an 8-bit kind
+    ("e4m3" / "int8") the cuBLAS 8-bit GEMM measured here, or twice the bf16
+    figures if that cannot run."""
     burst = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
     sus = float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
-    f = 2.0 if eight_bit else 1.0   # dense int8 / fp8 tensor rate is twice bf16 on B200
-    return burst * f, sus * f
+    if not eight_bit:
+        return burst, sus, "bf16_tflops (cuBLAS bf16 burst)"
+    kind = eight_bit if isinstance(eight_bit, str) else "e4m3"
+    b8, s8, note = measure_8bit_peak(kind, dev)
+    if b8:
+        return b8, s8, note
+    return 2 * burst, 2 * sus, f"2 x bf16_tflops burst ({note})"
 
 
 def dtype_name(cfg):
@@ -508,8 +583,7 @@ def measure_other_configs(names, dev, stream, steps: int = 5, warmup: int = 3) -
             ms = t0.elapsed_time(t1) / steps
             stages = {st: statistics.mean(evs[i][j].elapsed_time(evs[i][j + 1]) for i in range(steps))
                       for j, st in enumerate(STAGES)}
-            eight = cfg.int8 or cfg.int8ch or cfg.fp8 or cfg.int4ptx or cfg.fp8pt
-            burst, _sus = tensor_peaks(peaks, eight)
+            burst, _sus, _note = tensor_peaks(peaks, eight_bit_kind(cfg), dev)
             flop_up = 4.0 * cfg.d_model * cfg.d_ff * kept
             out[name] = {"ms_per_step": ms, "tokens_per_s": cfg.T / (ms * 1e-3), "stages_ms": stages,
                          "dtype": dtype_name(cfg), "kept_routes": kept,
@@ -727,8 +801,8 @@ def run_ep(args, cfg, ws, rank, local, dev):
     parity = ep_parity(layer, cfg, ws, rank, dev, glob, full)
     barrier(ws)
     peaks, peak_src = load_peaks()
-    eight_bit = cfg.int8 or cfg.int8ch or cfg.fp8 or cfg.int4ptx or cfg.fp8pt
-    peak_tf, peak_sus = tensor_peaks(peaks, eight_bit)
+    eight_bit = eight_bit_kind(cfg)
+    peak_tf, peak_sus, peak_what = tensor_peaks(peaks, eight_bit, dev)
     owner_rows.append(layer.owner_rows())   # the same tokens every step
     flop_ffn = 6.0 * cfg.d_model * cfg.d_ff * statistics.mean(owner_rows)
     ach = flop_ffn / (phase_ms["expert_ffn_compute"] * 1e-3) / 1e12
@@ -745,7 +819,7 @@ def run_ep(args, cfg, ws, rank, local, dev):
         "roofline": {"bound": "tensor", "achieved": ach_min, "peak": peak_tf, "unit": "TFLOP/s",
                      "frac": ach_min / peak_tf, "frac_of_sustained": ach_min / peak_sus, "traffic": None,
                      "kernel": "expert_ffn phase (up/gate + down tcgen05 GEMMs), slowest rank",
-                     "peak_source": f"{peak_src} bf16_tflops (burst)" + (" x 2 (8-bit)" if eight_bit else "")},
+                     "peak_source": peak_what if eight_bit else f"{peak_src} {peak_what}"},
         "phases_ms": phase_ms,
         "e2e": {"value": ws * cfg.T / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms, "serial_ms_per_step": serial_ms,
@@ -896,11 +970,10 @@ def main():
 
     # ---- roofline of the dominant kernel (up/gate GEMM with fused SwiGLU) --
     peaks, peak_src = load_peaks()
-    eight_bit = cfg.int8 or cfg.int8ch or cfg.fp8 or cfg.int4ptx or cfg.fp8pt
-    peak_tf, peak_sus = tensor_peaks(peaks, eight_bit)
+    eight_bit = eight_bit_kind(cfg)
+    peak_tf, peak_sus, peak_what = tensor_peaks(peaks, eight_bit, dev)
     peak_note = (f"{peak_src} bf16_tflops (cuBLAS bf16 burst; the timed region is ~20 steps, not a seconds-long "
-                 f"loop)" if not eight_bit else
-                 f"2 x {peak_src} bf16_tflops burst (dense 8-bit rate = 2x bf16; no 8-bit peak measured)")
+                 f"loop)" if not eight_bit else peak_what)
     d, f = cfg.d_model, cfg.d_ff
     flop_up = 4.0 * d * f * kept            # gate + up, kept routes only
     flop_down = 2.0 * d * f * kept
