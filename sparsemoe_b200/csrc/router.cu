@@ -56,34 +56,53 @@ __device__ __forceinline__ void load_wr8(const TW* __restrict__ p, float (&w)[8]
 }
 
 
+// Order-preserving key of a float: a larger key is a larger value, -0 maps
+// to +0's key (the two compare equal, so the lower index must win the tie).
+__device__ __forceinline__ uint32_t order_key(float v) {
+    const uint32_t u = __float_as_uint(v + 0.0f);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float key_value(uint32_t key) {
+    return __uint_as_float((key & 0x80000000u) ? (key & 0x7FFFFFFFu) : ~key);
+}
+
 // k-round warp argmax over (value desc, index asc) -- the reference's
 // insertion top-k with strict '>' -- then the softmax over the k kept values,
-// w_l = exp(v_l - v_0) / (sum + 1e-10).  Lane l owns experts l, l+32, ...
-__device__ __forceinline__ void topk_softmax_warp(const float* row, int E, int k, int64_t t, int* __restrict__ idx,
-                                                  float* __restrict__ wts, int lane) {
-    const int per_lane = (E + 31) / 32;  // <= 8
-    uint32_t taken = 0;
+// w_l = exp(v_l - v_0) / (sum + 1e-10).  Lane l holds the logits of experts
+// l, l+32, ... in v[0..8).  A round is two warp reductions (redux.sync): the
+// largest key, then the lowest expert index among the lanes holding it; only
+// the winning lane rescans its candidates.
+__device__ __forceinline__ void topk_softmax_regs(const float (&v)[8], int E, int k, int64_t t,
+                                                  int* __restrict__ idx, float* __restrict__ wts, int lane) {
+    uint32_t avail = 0;
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+        if (lane + 32 * q < E && v[q] > -1e20f) avail |= 1u << q;   // NaN and the sentinel never selectable
+    uint32_t bk = 0;
+    int be = -1;
+    auto lane_best = [&]() {
+        bk = 0;
+        be = -1;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            if (avail & (1u << q)) {
+                const uint32_t kq = order_key(v[q]);
+                if (kq > bk) { bk = kq; be = lane + 32 * q; }   // strict: the lower index keeps a tie
+            }
+        }
+    };
+    lane_best();
     float my_v = -1e20f;
     int my_i = -1;
     for (int l = 0; l < k; ++l) {
-        float bv = 0.0f;
-        int bi = -1;
-        for (int q = 0; q < per_lane; ++q) {
-            const int e = lane + 32 * q;
-            if (e < E && !(taken & (1u << q))) {
-                const float v = row[e];
-                if (v > -1e20f && (bi < 0 || v > bv)) { bv = v; bi = e; }
-            }
+        const uint32_t m = __reduce_max_sync(0xffffffffu, bk);
+        if (m == 0) break;  // fewer than k selectable experts: the rest keep the sentinel
+        const int bi = (int)__reduce_min_sync(0xffffffffu, bk == m ? (uint32_t)be : 0xFFFFFFFFu);
+        if (lane == l) { my_v = key_value(m); my_i = bi; }
+        if ((bi & 31) == lane) {
+            avail &= ~(1u << (bi >> 5));
+            lane_best();
         }
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
-            if (oi >= 0 && (bi < 0 || ov > bv || (ov == bv && oi < bi))) { bv = ov; bi = oi; }
-        }
-        if (bi < 0) break;  // fewer than k selectable experts: the rest keep the sentinel
-        if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
-        if (lane == l) { my_v = bv; my_i = bi; }
     }
     const float mx = __shfl_sync(0xffffffffu, my_v, 0);
     const float ex = (lane < k) ? expf(my_v - mx) : 0.0f;
@@ -93,6 +112,15 @@ __device__ __forceinline__ void topk_softmax_warp(const float* row, int E, int k
         idx[t * k + lane] = my_i;
         wts[t * k + lane] = ex / (sum + 1e-10f);
     }
+}
+
+// The same over a row of E logits in shared memory.
+__device__ __forceinline__ void topk_softmax_warp(const float* row, int E, int k, int64_t t, int* __restrict__ idx,
+                                                  float* __restrict__ wts, int lane) {
+    float v[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) v[q] = lane + 32 * q < E ? row[lane + 32 * q] : -1e20f;
+    topk_softmax_regs(v, E, k, t, idx, wts, lane);
 }
 
 // Work item = (TT tokens, one group of 8 experts); a CTA holds CT tokens
@@ -307,19 +335,23 @@ __global__ void __launch_bounds__(MT == 8 ? 256 : 512) router_tiled_kernel(
 // One warp per token: the nb partial logits of each expert summed by the
 // block tree (a binary-counter stack: leaf b closes one pair per trailing 1
 // bit of b, the left operand first; the remaining stack is folded from the
-// top, each entry added on the left), + bias, then top-k + softmax.
+// top, each entry added on the left), + bias, then top-k + softmax on the
+// lane's logits in registers.
 constexpr int kFoldMaxLevels = 8;   // nb <= 255 blocks (d <= 130560)
-constexpr int kFoldUnrolled = 32;   // d <= 16384: every partial of an expert loaded before the fold
+constexpr int kFoldUnrolled = 16;   // d <= 8192: every partial of an expert loaded before the fold
 __global__ void __launch_bounds__(128) fold_topk_kernel(const float* __restrict__ part, int nb, int64_t T, int E,
                                                        int k, const float* __restrict__ bias,
                                                        float* __restrict__ logits, int* __restrict__ idx,
                                                        float* __restrict__ wts) {
-    __shared__ float rows[4][256];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t t = (int64_t)blockIdx.x * 4 + warp;
     if (t >= T) return;
-    float* row = rows[warp];
-    for (int e = lane; e < E; e += 32) {
+    float vals[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+        const int e = lane + 32 * q;
+        vals[q] = -1e20f;
+        if (e >= E) continue;
         float st[kFoldMaxLevels];
         int top = 0;
         if (nb <= kFoldUnrolled) {
@@ -345,11 +377,10 @@ __global__ void __launch_bounds__(128) fold_topk_kernel(const float* __restrict_
         float v = st[--top];
         while (top > 0) v = st[--top] + v;
         if (bias) v = __fadd_rn(v, bias[e]);
-        row[e] = v;
+        vals[q] = v;
         if (logits != nullptr) logits[t * E + e] = v;
     }
-    __syncwarp();
-    topk_softmax_warp(row, E, k, t, idx, wts, lane);
+    topk_softmax_regs(vals, E, k, t, idx, wts, lane);
 }
 
 template <typename TX, typename TW>
