@@ -269,7 +269,7 @@ class ExpertParallelLayer:
     # -- peer memory (transport="peer") ---------------------------------------------
     def _setup_peer(self):
         """Receive buffers (rows, row scales) and return buffers (f32 rows)
-        that the other ranks map through CUDA IPC: the senders' gather kernels
+        that the other ranks map through CUDA IPC: the senders' dispatch (row scatter) kernels
         store their rows straight into the owners' receive buffers, and owners' down-GEMM
         epilogues store result rows straight into the senders' return
         buffers."""
